@@ -1,0 +1,147 @@
+/*
+ * slang_b200 -- C ABI of the B200 (sm_100a) int4 quantized-matmul path.
+ *
+ * Plain pointers and sizes only.  Every pointer argument named "device" is a
+ * CUDA device address owned by the caller; the library never allocates device
+ * memory.  Every call is stream-ordered on `stream` (a cudaStream_t; NULL =
+ * the legacy default stream) and returns SB_OK or an SB_ERR_* code after
+ * validating its arguments on the host; nothing is launched when validation
+ * fails.  sb_last_error() gives a human-readable message for the calling
+ * thread's last failure.
+ *
+ * Packing (the reference's on-disk format, gemma4_150/export.py:59-61 and
+ * gemma4_150/loader.py:75-86): a weight [n_out, n_in] at `bits` bits is
+ * row-major bytes [n_out, n_in*bits/8]; value i of a row sits at bit bits*i of
+ * the row's little-endian byte stream (low bits first); code q means the
+ * integer q - 2^(bits-1).  Scales are [n_out, n_in/group] in f16 (SB_SCALE_F16,
+ * the per-group-32 format) or f32 (SB_SCALE_F32; group == n_in is the
+ * reference checkpoint's per-row scale, gemma4/qat_loader.py:95-102).
+ * Dequantised weight: w = scale[n, k/group] * (q - 2^(bits-1)).
+ */
+#ifndef SLANG_B200_H
+#define SLANG_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define SB_OK 0
+#define SB_ERR_ARG 1          /* bad shape, null pointer, unsupported combination */
+#define SB_ERR_ALIGN 2        /* a pointer or leading dimension violates an alignment rule */
+#define SB_ERR_CUDA 3         /* a CUDA runtime call failed (message has the CUDA error) */
+#define SB_ERR_TIMEOUT 4      /* a bounded device-side wait expired (see sb_device_status) */
+#define SB_ERR_WORKSPACE 5    /* the caller's workspace is too small */
+
+/* element types */
+#define SB_F16 1
+#define SB_F32 2
+#define SB_SCALE_F16 SB_F16
+#define SB_SCALE_F32 SB_F32
+
+/* Library version and the calling thread's last error message. */
+const char* sb_version(void);
+const char* sb_last_error(void);
+
+/*
+ * Device-side error word: bounded spin-waits inside kernels set it instead of
+ * hanging.  Synchronises `stream`, returns SB_OK if no kernel has reported a
+ * timeout since the last call, else SB_ERR_TIMEOUT (and clears the word).
+ */
+int sb_device_status(void* stream);
+
+/*
+ * Dequantise a packed weight to f16: out[n, k] = f16(scale * (q - ZP)),
+ * the product formed in f32 and rounded once.
+ * Replaces PrefillGPU._dq (gemma4_150/prefill_gpu.py:186-200) and the dq_f16
+ * kernel (gemma4_150/kernels_dsl.py:2101-2138).  bits in {2,4,8};
+ * n_in % (32/bits) == 0; group % 32 == 0 (or group == n_in); n_in % group == 0.
+ *   packed  device [n_out, n_in*bits/8] u8 (4-byte aligned)
+ *   scales  device [n_out, n_in/group] f16 or f32
+ *   out     device [n_out, n_in] f16 (row stride n_in)
+ */
+int sb_dequant_f16(const void* packed, int bits, const void* scales, int scale_dtype,
+                   int group, void* out, int n_out, int n_in, void* stream);
+
+/*
+ * Decode GEMV over an int4 weight: y[m, n] = sum_k w[n, k] * x[m, k], fp32
+ * accumulate, exact dequant (no f16 rounding of the weight).
+ * Replaces matvec_dq4 (gemma4/qat_kernels.py:33-77) and the GEMV cores of the
+ * decode kernels qkv_70 / oproj_73 / gateup_74 / down_75
+ * (gemma4_150/kernels_dsl.py:1384-1480, 872-996, 1232-1300, 322-429), bound by
+ * the runner through Batch.dg (gemma4_150/metal_runner.py:53-67).
+ *   w       device [n, k/2] u8, 16-byte aligned rows (k % 32 == 0)
+ *   scales  device [n, k/group] f16 or f32 (group % 32 == 0, k % group == 0)
+ *   x       device [m, k] f16 or f32 (x_dtype), row stride k
+ *   y       device [m, n] f32, row stride ldy (>= n)
+ *   m       1..8 decode rows
+ */
+int sb_gemv_q4(const void* w, const void* scales, int scale_dtype, int group,
+               const void* x, int x_dtype, float* y, int ldy, int m, int n, int k,
+               void* stream);
+
+/*
+ * Tied lm_head GEMV fused with greedy argmax (ties -> lowest index).
+ * Replaces logits_33 + argmax1_34 + argmax2_35 (gemma4_150/kernels_dsl.py:
+ * 1483-1534, 481-570; dispatch gemma4_150/metal_runner.py:392-396) and the
+ * oracle's `embed @ x` + softcap + argmax (gemma4/reference.py:178-179; the
+ * softcap is monotonic and is not applied).
+ * The table may be a vocabulary shard: its row r is global token
+ * row_offset + r.  For each decode row the result is a 64-bit key
+ *   key = (orderable_u32(max logit) << 32) | (0xFFFFFFFF - global index)
+ * so the maximum key over shards (an integer MAX all-reduce) is the global
+ * greedy token with the lowest-index tie rule; orderable_u32(f) = ~bits(f)
+ * for negative f, bits(f) | 0x80000000 otherwise; NaN counts as -inf.
+ *   emb     device [v, k/2] u8;  scales device [v, k/group]
+ *   h       device [m, k] f16/f32
+ *   keys    device [m] u64 (written; no initialisation needed)
+ *   tokens  device [m] i32 or NULL: global token ids decoded from `keys`
+ *   logits  device [m, v] f32 or NULL: raw logits of this shard
+ */
+int sb_lmhead_argmax(const void* emb, const void* scales, int scale_dtype, int group,
+                     const void* h, int h_dtype, int m, int v, int k, int64_t row_offset,
+                     uint64_t* keys, int32_t* tokens, float* logits, void* stream);
+
+/* tokens[i] = global index held in keys[i] (after a cross-shard MAX). */
+int sb_keys_to_tokens(const uint64_t* keys, int32_t* tokens, int m, void* stream);
+
+/*
+ * f16 GEMM on the tcgen05 tensor cores, f32 accumulate:
+ *   C[M, N] = f16(alpha * A[M, K] @ (B[N, K]^T if tr else B[K, N]))
+ * Replaces PrefillGPU._gemm (gemma4_150/prefill_gpu.py:151-184) and the
+ * gemm_tiled kernel (gemma4_150/kernels_dsl.py:34-141): same (M, N, K, alpha,
+ * tr, lda, ldb, ldc) meaning; the reference's byte offsets aoff/boff/coff are
+ * folded into the pointers.  Row strides are in elements; A, B, C 16-byte
+ * aligned and lda, ldb multiples of 8.
+ */
+int sb_gemm_f16(const void* a, const void* b, void* c, int m, int n, int k, float alpha,
+                int tr, int lda, int ldb, int ldc, void* stream);
+
+/*
+ * Fused prefill projection: dequantise packed int4 tiles into shared memory
+ * and feed them to tcgen05 MMAs, f32 accumulate in tensor memory:
+ *   C[M, N] = f16(alpha * A[M, K] @ dq_f16(W)[N, K]^T)
+ * where dq_f16 is the bit-exact sb_dequant_f16 rounding.  Replaces the
+ * reference's per-layer `_dq` + `_gemm` pair (gemma4_150/prefill_gpu.py:
+ * 331-373) in one launch.
+ *   a       device [M, K] f16, row stride lda (multiple of 8), 16-byte aligned
+ *   w       device [N, K/2] u8 (K % 64 == 0), 16-byte aligned
+ *   scales  device [N, K/group] f16 or f32
+ *   c       device [M, N] f16, row stride ldc
+ *   workspace / workspace_bytes: device f32 scratch for split-K partial sums,
+ *           or NULL/0.  sb_gemm_q4_workspace_size() gives the bytes this call
+ *           wants; with too little (or none) the call runs without split-K.
+ */
+int sb_gemm_q4(const void* a, const void* w, const void* scales, int scale_dtype, int group,
+               void* c, int m, int n, int k, float alpha, int lda, int ldc,
+               void* workspace, size_t workspace_bytes, void* stream);
+size_t sb_gemm_q4_workspace_size(int m, int n, int k);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SLANG_B200_H */

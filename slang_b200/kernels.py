@@ -1,0 +1,174 @@
+"""torch-facing wrappers of the C ABI, named after the reference's operator calls.
+
+Each wrapper validates dtypes/devices, passes raw device pointers and the
+current CUDA stream to ``libslang_b200.so`` and raises ``SlangError`` on a
+non-zero status.  Buffers are owned by the caller (as the reference runners own
+theirs); wrappers only allocate an output when none is given.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import SB_F16, SB_F32
+
+_DT = {torch.float16: SB_F16, torch.float32: SB_F32}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _need(t: torch.Tensor, name: str, dtypes=None, cuda=True):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if cuda and not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if dtypes is not None and t.dtype not in dtypes:
+        raise TypeError(f"{name} has dtype {t.dtype}, expected one of {dtypes}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def group_of(scales: torch.Tensor, n_in: int) -> int:
+    """Values per scale along K, read off the scale tensor's shape."""
+    groups = 1 if scales.dim() == 1 else scales.shape[-1]
+    if n_in % groups:
+        raise ValueError(f"{groups} scale groups do not tile n_in={n_in}")
+    return n_in // groups
+
+
+def dequant_f16(packed: torch.Tensor, scales: torch.Tensor, n_in: int, n_out: int,
+                out: torch.Tensor | None = None, bits: int | None = None) -> torch.Tensor:
+    """``PrefillGPU._dq`` (gemma4_150/prefill_gpu.py:186-200): packed -> f16 [n_out, n_in].
+
+    As in the reference, the bit width is read off the packed buffer's size
+    unless given.
+    """
+    _need(packed, "packed", (torch.uint8, torch.int32, torch.uint32))
+    _need(scales, "scales", (torch.float16, torch.float32))
+    nbytes = packed.numel() * packed.element_size()
+    if bits is None:
+        bits = nbytes * 8 // (n_in * n_out)
+    if bits not in (2, 4, 8) or nbytes * 8 != bits * n_in * n_out:
+        raise ValueError(f"odd width for [{n_out}x{n_in}] from {nbytes} packed bytes")
+    if out is None:
+        out = torch.empty((n_out, n_in), dtype=torch.float16, device=packed.device)
+    _need(out, "out", (torch.float16,))
+    _lib.call("sb_dequant_f16", _ptr(packed), bits, _ptr(scales), _DT[scales.dtype],
+              group_of(scales, n_in), _ptr(out), n_out, n_in, _stream())
+    return out
+
+
+def gemv_q4(w: torch.Tensor, scales: torch.Tensor, x: torch.Tensor,
+            y: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode GEMV ``y[m, n] = x[m] . W[n]`` (matvec_dq4, gemma4/qat_kernels.py:33-77)."""
+    _need(w, "w", (torch.uint8,))
+    _need(scales, "scales", (torch.float16, torch.float32))
+    _need(x, "x", (torch.float16, torch.float32))
+    n, k = w.shape[0], w.shape[1] * 2
+    x2 = x.reshape(-1, k)
+    m = x2.shape[0]
+    if y is None:
+        y = torch.empty((m, n), dtype=torch.float32, device=w.device)
+    _need(y, "y", (torch.float32,))
+    _lib.call("sb_gemv_q4", _ptr(w), _ptr(scales), _DT[scales.dtype], group_of(scales, k),
+              _ptr(x2), _DT[x.dtype], _ptr(y), y.shape[-1], m, n, k, _stream())
+    return y
+
+
+def lmhead_argmax(emb: torch.Tensor, scales: torch.Tensor, h: torch.Tensor, row_offset: int = 0,
+                  keys: torch.Tensor | None = None, tokens: torch.Tensor | None = None,
+                  logits: torch.Tensor | None = None, want_tokens: bool = True):
+    """Fused ``logits_33`` + ``argmax1_34``/``argmax2_35``; returns (keys, tokens)."""
+    _need(emb, "emb", (torch.uint8,))
+    _need(scales, "scales", (torch.float16, torch.float32))
+    _need(h, "h", (torch.float16, torch.float32))
+    v, k = emb.shape[0], emb.shape[1] * 2
+    h2 = h.reshape(-1, k)
+    m = h2.shape[0]
+    dev = emb.device
+    if keys is None:
+        keys = torch.empty(m, dtype=torch.int64, device=dev)
+    if want_tokens and tokens is None:
+        tokens = torch.empty(m, dtype=torch.int32, device=dev)
+    _lib.call("sb_lmhead_argmax", _ptr(emb), _ptr(scales), _DT[scales.dtype], group_of(scales, k),
+              _ptr(h2), _DT[h.dtype], m, v, k, int(row_offset), _ptr(keys),
+              _ptr(tokens) if want_tokens else None, _ptr(logits), _stream())
+    return keys, tokens
+
+
+def keys_to_tokens(keys: torch.Tensor, tokens: torch.Tensor | None = None) -> torch.Tensor:
+    if tokens is None:
+        tokens = torch.empty(keys.numel(), dtype=torch.int32, device=keys.device)
+    _lib.call("sb_keys_to_tokens", _ptr(keys), _ptr(tokens), keys.numel(), _stream())
+    return tokens
+
+
+def gemm(A: torch.Tensor, W: torch.Tensor, C: torch.Tensor, M: int, N: int, K: int, alpha: float = 1.0,
+         tr: bool = True, acols: int | None = None, ccols: int | None = None, aoff: int = 0,
+         boff: int = 0, coff: int = 0, bcols: int | None = None) -> torch.Tensor:
+    """``PrefillGPU._gemm`` (gemma4_150/prefill_gpu.py:151-184) on tcgen05.
+
+    ``C[M,N] = alpha * A[M,K] @ (W[N,K]^T if tr else W[K,N])``, all f16; acols,
+    ccols are row strides wider than the operation and aoff/boff/coff are BYTE
+    offsets into the buffers, exactly as in the reference.
+    """
+    for t, nm in ((A, "A"), (W, "W"), (C, "C")):
+        _need(t, nm, (torch.float16,))
+    lda = acols or K
+    ldb = bcols or (K if tr else N)
+    ldc = ccols or N
+    _lib.call("sb_gemm_f16", A.data_ptr() + aoff, W.data_ptr() + boff, C.data_ptr() + coff, M, N, K,
+              float(alpha), 1 if tr else 0, lda, ldb, ldc, _stream())
+    return C
+
+
+def gemm_q4(A: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, C: torch.Tensor | None = None,
+            alpha: float = 1.0, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused ``_dq`` + ``_gemm``: ``C = f16(alpha * A @ dq_f16(W)^T)``."""
+    _need(A, "A", (torch.float16,))
+    _need(w, "w", (torch.uint8,))
+    _need(scales, "scales", (torch.float16, torch.float32))
+    M, K = A.shape
+    N = w.shape[0]
+    if w.shape[1] * 2 != K:
+        raise ValueError("packed weight does not match A's K")
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.float16, device=A.device)
+    _need(C, "C", (torch.float16,))
+    if workspace is None:
+        need = gemm_q4_workspace_size(M, N, K)
+        workspace = _workspace(A.device, need)
+    _lib.call("sb_gemm_q4", _ptr(A), _ptr(w), _ptr(scales), _DT[scales.dtype], group_of(scales, K),
+              _ptr(C), M, N, K, float(alpha), K, C.shape[1], _ptr(workspace) if workspace is not None else None,
+              0 if workspace is None else workspace.numel() * workspace.element_size(), _stream())
+    return C
+
+
+def gemm_q4_workspace_size(M: int, N: int, K: int) -> int:
+    return int(_lib.load().sb_gemm_q4_workspace_size(M, N, K))
+
+
+_WS: dict = {}
+
+
+def _workspace(device, nbytes: int):
+    """A per-device split-K scratch buffer, grown on demand and reused."""
+    if nbytes == 0:
+        return None
+    key = str(device)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() * 4 < nbytes:
+        buf = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device=device)
+        _WS[key] = buf
+    return buf
+
+
+def device_status() -> None:
+    """Raise if a bounded device-side wait has timed out since the last check."""
+    _lib.call("sb_device_status", _stream())

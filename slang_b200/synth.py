@@ -1,0 +1,106 @@
+"""Seeded synthetic inputs and random-init models for the benchmark configurations.
+
+There is no checkpoint on this machine, so every workload is generated from a
+seed with ``numpy.random.default_rng``:
+
+* packed int4 weights: uniform random bytes, i.e. two independent nibbles
+  uniform in ``[0, 15]`` -> values uniform in ``[-8, 7]``, low nibble first;
+* per-group-32 scales: ``|N(0, 0.02)|`` rounded to f16, shape ``[n_out, n_in/32]``;
+* activations: ``N(0, 1)`` rounded to f16 (or kept f32 for decode);
+* norm weights: ``1 + 0.1 * N(0, 1)`` in f32.
+
+The Gemma-4-E2B-shaped decoder is uniform: 35 layers, hidden 1536, FFN 6144,
+8 query heads and 1 KV head at head_dim 256, full RoPE (theta 1e4), full causal
+attention, tied 262144-row lm_head, final logit softcap 30.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+GROUP = 32
+
+# Gemma-4-E2B-shaped projection matrices: name -> (n_out, n_in)
+E2B_SHAPES = {
+    "q": (2048, 1536), "k": (256, 1536), "v": (256, 1536), "o": (1536, 2048),
+    "gate": (6144, 1536), "up": (6144, 1536), "down": (1536, 6144),
+}
+
+
+def e2b_config(**over) -> dict:
+    cfg = dict(hidden=1536, n_layers=35, n_heads=8, head_dim=256, inter=6144,
+               vocab=262144, eps=1e-6, rope_theta=10000.0, rope_cutoff=128,
+               softcap=30.0, sliding_window=0, group=GROUP)
+    cfg.update(over)
+    cfg["q_dim"] = cfg["n_heads"] * cfg["head_dim"]
+    cfg["embed_scale"] = math.sqrt(cfg["hidden"])
+    return cfg
+
+
+def q4_weight(rng: np.random.Generator, n_out: int, n_in: int,
+              group: int = GROUP) -> tuple[np.ndarray, np.ndarray]:
+    """Packed int4 ``[n_out, n_in/2]`` u8 and f16 scales ``[n_out, n_in/group]``."""
+    packed = rng.integers(0, 256, (n_out, n_in // 2), dtype=np.uint8)
+    scales = np.abs(rng.normal(0.0, 0.02, (n_out, n_in // group))).astype(np.float16)
+    return packed, scales
+
+
+def activations(rng: np.random.Generator, m: int, k: int, dtype=np.float16) -> np.ndarray:
+    return rng.standard_normal((m, k), dtype=np.float32).astype(dtype)
+
+
+def config1(seed: int = 0):
+    """GEMV config: x f16 [1,1536], W int4 [6144,1536], group-32 f16 scales."""
+    rng = np.random.default_rng(seed)
+    packed, scales = q4_weight(rng, 6144, 1536)
+    x = activations(rng, 1, 1536)
+    return packed, scales, x
+
+
+def config2(m: int = 1024, seed: int = 1):
+    """Prefill GEMM config: A f16 [m, K] and the seven E2B projections (seeds 1..7)."""
+    mats = {}
+    for i, (name, (n, k)) in enumerate(E2B_SHAPES.items()):
+        rng = np.random.default_rng(seed + i)
+        packed, scales = q4_weight(rng, n, k)
+        mats[name] = (packed, scales, activations(rng, m, k))
+    return mats
+
+
+def config3(vocab: int = 262144, hidden: int = 1536, seed: int = 3):
+    """Tied lm_head config: int4 embedding [vocab, hidden] + f16 hidden [1, hidden]."""
+    rng = np.random.default_rng(seed)
+    packed, scales = q4_weight(rng, vocab, hidden)
+    h = activations(rng, 1, hidden)
+    return packed, scales, h
+
+
+def random_model(cfg: dict | None = None, seed: int = 1234) -> dict:
+    """Random-init Gemma-4-E2B-architecture int4 decoder (layer ``L`` uses seed+1+L)."""
+    cfg = dict(cfg or e2b_config())
+    H, qd, hd, F = cfg["hidden"], cfg["q_dim"], cfg["head_dim"], cfg["inter"]
+    shapes = {"q": (qd, H), "k": (hd, H), "v": (hd, H), "o": (H, qd),
+              "gate": (F, H), "up": (F, H), "down": (H, F)}
+    rng = np.random.default_rng(seed)
+    embed_q, embed_scale = q4_weight(rng, cfg["vocab"], H, cfg["group"])
+
+    def norm(r, n):
+        return (1.0 + 0.1 * r.standard_normal(n, dtype=np.float32)).astype(np.float32)
+
+    final_norm = norm(rng, H)
+    layers = []
+    for li in range(cfg["n_layers"]):
+        r = np.random.default_rng(seed + 1 + li)
+        layer = {name: q4_weight(r, n, k, cfg["group"]) for name, (n, k) in shapes.items()}
+        for name, n in (("in_norm", H), ("q_norm", hd), ("k_norm", hd), ("post_attn_norm", H),
+                        ("pre_ffn_norm", H), ("post_ffn_norm", H)):
+            layer[name] = norm(r, n)
+        layers.append(layer)
+    return {"config": cfg, "embed_q": embed_q, "embed_scale": embed_scale,
+            "final_norm": final_norm, "layers": layers}
+
+
+def prompt_tokens(n: int, vocab: int, seed: int = 99) -> list[int]:
+    """Uniform random token ids (the synthetic stand-in for a text prompt)."""
+    return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, n)]

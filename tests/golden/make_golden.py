@@ -1,0 +1,273 @@
+"""Generate the golden fixtures in this directory by running the REFERENCE's code.
+
+    python tests/golden/make_golden.py --reference <path to a wakoan/slang checkout> [--full]
+
+What runs from the reference (imported in place, nothing copied):
+
+* ``gemma4.qat_loader.unpack_int4`` / ``unpack_int2`` / ``unpack_bits`` on the
+  reference tests' known-answer bytes and on random packed rows;
+* ``QATIndex.dequant_embedding_full`` (the per-block ``np.repeat`` dequant,
+  gemma4/qat_loader.py:115-121) on synthetic packed tables, through a minimal
+  stand-in for its safetensors index;
+* ``tests/test_gemm_dsl.py``'s float64 ``reference`` and ``_inputs`` for the GEMM shapes;
+* ``gemma4.reference.ReferenceGemma4`` (``ple=False``) for the decoder, with a
+  ``_w``/``_embed_row`` override in the style of ``QATReference``
+  (gemma4/qat_reference.py:24-37) that serves the synthetic int4 weights.
+
+``--full`` additionally runs the full-size cases (config-1 GEMV, the 262144-row
+lm_head, and the 35-layer decoder: 1024-token prompt + 256 greedy steps; the
+decoder alone takes several minutes of CPU).  Outputs are small ``.npz`` files;
+inputs are regenerated from the same seeds by ``slang_b200.synth`` where they
+are large, and stored verbatim where they are small.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+import time
+from types import SimpleNamespace
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+from slang_b200 import synth  # noqa: E402
+
+
+class _StubIndex:
+    """Just enough of ``SafetensorsIndex`` for ``QATIndex.dequant_embedding_*``."""
+
+    def __init__(self, tensors: dict):
+        self.t = tensors
+
+    def raw(self, name):
+        return self.t[name]
+
+    def tensor(self, name, dtype="f32"):
+        return np.asarray(self.t[name]).astype(np.float32)
+
+
+def ref_dequant(packed, scales, bits):
+    """Run the reference's per-block dequant on a synthetic table."""
+    from gemma4.qat_loader import QATIndex
+    q = QATIndex.__new__(QATIndex)
+    q.idx = _StubIndex({"model.t.embedding_quantized": packed,
+                        "model.t.embedding_scale": scales})
+    n_cols = packed.shape[-1] * 8 // bits
+    return q.dequant_embedding_full("t", bits, n_cols)
+
+
+def kats(out):
+    from gemma4.qat_loader import unpack_int2, unpack_int4
+    # tests/test_gemma4_qat_loader.py:18-30
+    b4 = np.array([0x80, 0xF0, 0x08, 0x7F], np.uint8)
+    b2 = np.array([0xE4], np.uint8)
+    out["kat_int4_in"], out["kat_int4_out"] = b4, unpack_int4(b4)
+    out["kat_int2_in"], out["kat_int2_out"] = b2, unpack_int2(b2)
+    rng = np.random.default_rng(5)
+    rows = rng.integers(0, 256, (7, 48), dtype=np.uint8)
+    out["rand_bytes"] = rows
+    out["rand_int4"] = unpack_int4(rows)
+    out["rand_int2"] = unpack_int2(rows)
+
+
+def dequant_cases(out):
+    rng = np.random.default_rng(131)
+    for bits in (2, 4, 8):
+        n_out, n_in = 64, 256
+        packed = rng.integers(0, 256, (n_out, n_in * bits // 8), dtype=np.uint8)
+        gs = np.abs(rng.normal(0, 0.02, (n_out, n_in // 32))).astype(np.float16)
+        rs = (rng.random((n_out, 1)).astype(np.float32) * 0.01 + 0.001)
+        if bits == 8:
+            # the reference's unpack_bits(., 8) reads a byte as signed int8;
+            # our biased code is byte+128 (gemma4_150/export.py:155-157)
+            signed = packed.view(np.int8)
+            biased = (signed.astype(np.int16) + 128).astype(np.uint8)
+            out[f"dq{bits}_packed"] = biased
+            ref_in = packed
+        else:
+            out[f"dq{bits}_packed"] = packed
+            ref_in = packed
+        out[f"dq{bits}_gscale"], out[f"dq{bits}_rscale"] = gs, rs
+        out[f"dq{bits}_f32_group"] = ref_dequant(ref_in, gs, bits)
+        out[f"dq{bits}_f32_row"] = ref_dequant(ref_in, rs, bits)
+
+
+def gemv_cases(out, full):
+    # reference test shapes (tests/test_gemma4_qat_kernels_gpu.py:42) with group scales
+    # inputs: synth.q4_weight + synth.activations from default_rng(700 + case)
+    for i, (n, k) in enumerate([(512, 1536), (2048, 1536), (256, 256)]):
+        rng = np.random.default_rng(700 + i)
+        packed, scales = synth.q4_weight(rng, n, k)
+        x = synth.activations(rng, 1, k)
+        w = ref_dequant(packed, scales, 4)
+        out[f"gemv_{n}x{k}_y"] = w @ x[0].astype(np.float32)
+    if full:
+        packed, scales, x = synth.config1(0)
+        out["cfg1_y"] = ref_dequant(packed, scales, 4) @ x[0].astype(np.float32)
+
+
+def gemm_cases(out):
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "ref_test_gemm_dsl", os.path.join(REF, "tests", "test_gemm_dsl.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    for (M, N, K) in mod.SHAPES:
+        # inputs regenerate as the reference test's _inputs(M, N, K, seed=0)
+        a, b = mod._inputs(M, N, K)
+        out[f"gemm_{M}x{N}x{K}_c64"] = mod.reference(a, b, 1.0)
+    a, b = mod._inputs(32, 32, 16)
+    out["gemm_alpha_c64"] = mod.reference(a, b, 0.375)
+
+
+def lmhead_case(out):
+    packed, scales, h = synth.config3()
+    w = ref_dequant(packed, scales, 4)
+    logits = w @ h[0].astype(np.float32)
+    del w
+    order = np.argsort(-logits, kind="stable")[:8]
+    out["cfg3_token"] = np.int64(np.argmax(logits))
+    out["cfg3_top8_idx"] = order
+    out["cfg3_top8_val"] = logits[order]
+    out["cfg3_logits_head"] = logits[:4096]
+
+
+class _RefModel:
+    """Build a ``ReferenceGemma4(ple=False)`` serving a ``synth.random_model``."""
+
+    def __init__(self, model, max_seq):
+        from gemma4.reference import ReferenceGemma4
+        from gemma4.loader import PREFIX
+        cfg = model["config"]
+        spec = lambda i: SimpleNamespace(  # noqa: E731
+            index=i, sliding=bool(cfg["sliding_window"]), head_dim=cfg["head_dim"],
+            q_dim=cfg["q_dim"], intermediate=cfg["inter"], rope_theta=cfg["rope_theta"],
+            rope_cutoff=cfg["rope_cutoff"], kv_source=i, kv_shared=False)
+        config = SimpleNamespace(
+            hidden_size=cfg["hidden"], num_layers=cfg["n_layers"], num_heads=cfg["n_heads"],
+            num_kv_heads=1, vocab_size=cfg["vocab"], rms_norm_eps=cfg["eps"],
+            sliding_window=cfg["sliding_window"] or 1 << 30,
+            final_logit_softcapping=cfg["softcap"], embed_scale=cfg["embed_scale"],
+            layers=[spec(i) for i in range(cfg["n_layers"])])
+        names = {"self_attn.q_proj": "q", "self_attn.k_proj": "k", "self_attn.v_proj": "v",
+                 "self_attn.o_proj": "o", "mlp.gate_proj": "gate", "mlp.up_proj": "up",
+                 "mlp.down_proj": "down", "input_layernorm": "in_norm",
+                 "self_attn.q_norm": "q_norm", "self_attn.k_norm": "k_norm",
+                 "post_attention_layernorm": "post_attn_norm",
+                 "pre_feedforward_layernorm": "pre_ffn_norm",
+                 "post_feedforward_layernorm": "post_ffn_norm"}
+        cache = {}
+
+        class Ref(ReferenceGemma4):
+            def _w(self, name):
+                if name in cache:
+                    return cache[name]
+                if name == PREFIX + "embed_tokens.weight":
+                    v = ref_dequant(model["embed_q"], model["embed_scale"], 4)
+                elif name == PREFIX + "norm.weight":
+                    v = model["final_norm"]
+                else:
+                    rest = name[len(PREFIX) + len("layers."):-len(".weight")]
+                    li, mod = rest.split(".", 1)
+                    item = model["layers"][int(li)][names[mod]]
+                    v = ref_dequant(item[0], item[1], 4) if isinstance(item, tuple) else item
+                cache[name] = v
+                return v
+
+            def _embed_row(self, token_id):
+                return ref_dequant(model["embed_q"][token_id:token_id + 1],
+                                   model["embed_scale"][token_id:token_id + 1], 4)[0]
+
+        self.ref = Ref(config, None, max_seq=max_seq, ple=False)
+
+    def generate(self, prompt, steps, log_every=0):
+        logits = None
+        t0 = time.time()
+        for pos, t in enumerate(prompt):
+            logits = self.ref.forward(int(t), pos)
+            if log_every and pos % log_every == 0:
+                print(f"  prefill pos {pos} {time.time() - t0:.0f}s", flush=True)
+        toks, margins, top = [], [], []
+        pos = len(prompt)
+        for s in range(steps):
+            part = np.partition(logits, -2)[-2:]
+            margins.append(float(part[1] - part[0]))
+            nxt = int(np.argmax(logits))
+            toks.append(nxt)
+            top.append(float(logits[nxt]))
+            if s + 1 < steps:
+                logits = self.ref.forward(nxt, pos)
+                pos += 1
+            if log_every and s % 32 == 0:
+                print(f"  decode step {s} {time.time() - t0:.0f}s", flush=True)
+        return np.array(toks, np.int64), np.array(margins, np.float32), np.array(top, np.float32)
+
+
+def decoder_small(out):
+    cfg = synth.e2b_config(hidden=256, n_layers=2, n_heads=2, head_dim=64, inter=512,
+                           vocab=2048, rope_cutoff=32)
+    model = synth.random_model(cfg, seed=77)
+    prompt = synth.prompt_tokens(12, cfg["vocab"], seed=78)
+    toks, margins, top = _RefModel(model, 64).generate(prompt, 16)
+    out["dec_small_prompt"] = np.array(prompt, np.int64)
+    out["dec_small_tokens"], out["dec_small_margins"], out["dec_small_top"] = toks, margins, top
+
+
+def decoder_full(out, prompt_len, steps):
+    cfg = synth.e2b_config()
+    model = synth.random_model(cfg, seed=1234)
+    prompt = synth.prompt_tokens(prompt_len, cfg["vocab"], seed=99)
+    toks, margins, top = _RefModel(model, prompt_len + steps).generate(prompt, steps, log_every=64)
+    out["cfg4_prompt_len"] = np.int64(prompt_len)
+    out["cfg4_tokens"], out["cfg4_margins"], out["cfg4_top"] = toks, margins, top
+
+
+def main():
+    global REF
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True)
+    ap.add_argument("--full", action="store_true")
+    ap.add_argument("--only", default="")
+    args = ap.parse_args()
+    REF = os.path.abspath(args.reference)
+    sys.path.insert(0, REF)
+    only = set(filter(None, args.only.split(",")))
+
+    def want(n):
+        return not only or n in only
+
+    if want("small"):
+        out = {}
+        kats(out)
+        dequant_cases(out)
+        gemv_cases(out, full=False)
+        gemm_cases(out)
+        decoder_small(out)
+        np.savez_compressed(os.path.join(HERE, "golden_small.npz"), **out)
+        print("wrote golden_small.npz", len(out))
+    if args.full and want("cfg1"):
+        out = {}
+        gemv_cases({}, full=False)
+        packed, scales, x = synth.config1(0)
+        out["cfg1_y"] = ref_dequant(packed, scales, 4) @ x[0].astype(np.float32)
+        np.savez_compressed(os.path.join(HERE, "golden_cfg1.npz"), **out)
+        print("wrote golden_cfg1.npz")
+    if args.full and want("cfg3"):
+        out = {}
+        lmhead_case(out)
+        np.savez_compressed(os.path.join(HERE, "golden_cfg3.npz"), **out)
+        print("wrote golden_cfg3.npz")
+    if args.full and want("cfg4"):
+        out = {}
+        decoder_full(out, 1024, 256)
+        np.savez_compressed(os.path.join(HERE, "golden_cfg4.npz"), **out)
+        print("wrote golden_cfg4.npz")
+
+
+REF = None
+
+if __name__ == "__main__":
+    main()

@@ -86,14 +86,14 @@ __device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // f16(scale * (q - 8)) for the 8 nibbles of `w`, as 4 half2 in k order.
-// byte_perm gathers nibble pairs (q0,q1), (q2,q3), ... into the low nibbles of
-// the two 16-bit halves; OR-ing 0x6400 makes each half the f16 1024 + q, and
+// byte_perm puts byte j of w in byte 0 and byte j of (w >> 4) in byte 2, so the
+// low nibbles of the two 16-bit halves hold the pair (q_2j, q_2j+1); OR-ing 0x6400 makes each half the f16 1024 + q, and
 // subtracting 1032 gives q - 8 exactly.  The product with an f16 scale is the
 // correctly rounded f16 of the exact product, i.e. f16(float(s) * (q - 8)).
 __device__ __forceinline__ void dq8_half(uint32_t w, __half2 s2, uint32_t (&out)[4]) {
   const uint32_t t = w >> 4;
   const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1032
-  const uint32_t sel[4] = {0x4040u, 0x5151u, 0x6262u, 0x7373u};
+  const uint32_t sel[4] = {0x0400u, 0x0501u, 0x0602u, 0x0703u};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     uint32_t r = (__byte_perm(w, t, sel[j]) & 0x000F000Fu) | 0x64006400u;
@@ -106,7 +106,7 @@ __device__ __forceinline__ void dq8_half(uint32_t w, __half2 s2, uint32_t (&out)
 __device__ __forceinline__ void dq8_float(uint32_t w, float s, uint32_t (&out)[4]) {
   const uint32_t t = w >> 4;
   const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
-  const uint32_t sel[4] = {0x4040u, 0x5151u, 0x6262u, 0x7373u};
+  const uint32_t sel[4] = {0x0400u, 0x0501u, 0x0602u, 0x0703u};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     uint32_t r = (__byte_perm(w, t, sel[j]) & 0x000F000Fu) | 0x64006400u;

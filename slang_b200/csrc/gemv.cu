@@ -293,7 +293,7 @@ Plan plan(int mtile, int n, int k, int sms) {
   const long long tiles4 = (n + nrl * 4 - 1) / (nrl * 4);
   const long long tiles2 = (n + nrl * 2 - 1) / (nrl * 2);
   best.r = tiles4 >= 2LL * sms ? 4 : (tiles2 >= sms ? 2 : 1);
-  if (mtile == 4 && best.r == 4) best.r = 2;
+  if (mtile >= 2 && best.r == 4) best.r = 2;
   return best;
 }
 

@@ -140,6 +140,25 @@ int sb_gemm_q4(const void* a, const void* w, const void* scales, int scale_dtype
                void* workspace, size_t workspace_bytes, void* stream);
 size_t sb_gemm_q4_workspace_size(int m, int n, int k);
 
+/*
+ * sb_gemm_q4 without a caller workspace; it allocates nothing.  No counterpart
+ * in the reference: it is for callers that cannot allocate device memory --
+ * a host reaching the GPU only through this C ABI, with no CUDA allocator of
+ * its own, or a process whose device memory is reserved up front by its own
+ * pool, where a cudaMalloc on this path fails or stalls.
+ * Its split-K scratch is a static 32 MiB device array that every GPU loading
+ * this library holds until the process exits.  Shapes whose split-K scratch
+ * (sb_gemm_q4_workspace_size) exceeds 32 MiB are rejected with
+ * SB_ERR_WORKSPACE.  The first call on each device looks up the array's device
+ * address with that device current; make that first call before any stream
+ * capture.  Every call shares the array and it keeps the last call's partial
+ * sums (nothing in it needs to start at zero), so calls that overlap on the
+ * GPU -- other streams, other host threads -- race: order them on one stream.
+ * Arguments mean what they mean for sb_gemm_q4.
+ */
+int sb_gemm_q4_noalloc(const void* a, const void* w, const void* scales, int scale_dtype, int group,
+                       void* c, int m, int n, int k, float alpha, int lda, int ldc, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

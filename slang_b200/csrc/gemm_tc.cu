@@ -494,3 +494,59 @@ extern "C" int sb_gemm_q4(const void* a, const void* w, const void* scales, int 
   if (rc != SB_OK || splits == 1) return rc;
   return finalize(p, splits, s);
 }
+
+// ------------------------------------------------------------------------
+// Allocation-free variant of sb_gemm_q4.
+//
+// Some callers cannot allocate device memory on the path that calls us: a host
+// that reaches the GPU only through this C ABI (an FFI binding with no CUDA
+// allocator of its own), or a process whose device memory is reserved up front
+// by its own pool, where a cudaMalloc in the hot path fails or stalls.  For them
+// the split-K partial sums live in the array below, which every GPU that loads
+// this library holds until the process exits.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB per device
+static __device__ __align__(256) float g_noalloc_splitk[kNoAllocScratchBytes / sizeof(float)];
+
+// Device address of g_noalloc_splitk on the current device.  The host-side
+// symbol is only a stand-in: a kernel must be given this address instead.
+// Looked up once per device, with that device current, on its first call.
+int noalloc_scratch(float** out) {
+  static float* addr[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "sb_gemm_q4_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= 64) return sb::fail(SB_ERR_ARG, "sb_gemm_q4_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_splitk);
+    if (e != cudaSuccess) return sb::cuda_fail(e, "sb_gemm_q4_noalloc: cudaGetSymbolAddress");
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return SB_OK;
+}
+
+}  // namespace
+
+extern "C" int sb_gemm_q4_noalloc(const void* a, const void* w, const void* scales, int scale_dtype, int group,
+                                  void* c, int m, int n, int k, float alpha, int lda, int ldc, void* stream) {
+  const size_t need = sb_gemm_q4_workspace_size(m, n, k);
+  if (need > kNoAllocScratchBytes)
+    return sb::fail(SB_ERR_WORKSPACE,
+                    "sb_gemm_q4_noalloc: m=%d n=%d k=%d needs %zu bytes of split-K scratch, more than the "
+                    "%zu-byte static scratch; use sb_gemm_q4 with a caller workspace",
+                    m, n, k, need, kNoAllocScratchBytes);
+  float* ws = nullptr;
+  if (need > 0) {
+    int rc = noalloc_scratch(&ws);
+    if (rc != SB_OK) return rc;
+  }
+  // Each split writes every element of its partial plane before the finalize
+  // kernel reads it, so nothing in the scratch has to start at zero.
+  return sb_gemm_q4(a, w, scales, scale_dtype, group, c, m, n, k, alpha, lda, ldc, ws, need > 0 ? kNoAllocScratchBytes : 0,
+                    stream);
+}

@@ -48,7 +48,68 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", default="", choices=["", "gemm_q4", "gemm_f16", "gemv", "lmhead"],
+                    help="run one kernel --iters times on a single shape and exit (for ncu captures)")
+    ap.add_argument("--shape", default="6144,1536", help="N,K of the weight for --kernel")
+    ap.add_argument("--m", type=int, default=1024, help="rows of the activation for --kernel")
+    ap.add_argument("--iters", type=int, default=3)
     return ap.parse_args()
+
+
+def run_kernel_case(args):
+    """One kernel on one shape, --iters launches after one warm-up (ncu target)."""
+    import torch
+
+    from slang_b200 import kernels as kern
+    dev = torch.device("cuda", 0)
+    n, k = (int(v) for v in args.shape.split(","))
+    m = args.m
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    w = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g)
+    s = (torch.randn((n, k // 32), device=dev, generator=g) * 0.02).abs().half()
+    if args.kernel in ("gemm_q4", "gemm_f16"):
+        a = torch.randn((m, k), device=dev, generator=g).half()
+        c = torch.empty((m, n), dtype=torch.float16, device=dev)
+        wf = kern.dequant_f16(w, s, k, n) if args.kernel == "gemm_f16" else None
+
+        def op():
+            if wf is None:
+                kern.gemm_q4(a, w, s, C=c)
+            else:
+                kern.gemm(a, wf, c, m, n, k)
+    else:
+        x = torch.randn((m, k), device=dev, generator=g)
+        y = torch.empty((m, n), device=dev)
+
+        def op():
+            if args.kernel == "gemv":
+                kern.gemv_q4(w, s, x, y=y)
+            else:
+                kern.lmhead_argmax(w, s, x)
+    op()
+    torch.cuda.synchronize()
+    # replay a CUDA graph of --iters launches so host overhead is not timed
+    stream = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(args.iters):
+            op()
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    graph.replay()
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.iters
+    kern.device_status()
+    if args.kernel in ("gemm_q4", "gemm_f16"):
+        rate = f"{2 * m * n * k / us / 1e6:.1f} TFLOP/s"
+    else:
+        rate = f"{(n * k // 2 + n * (k // 32) * 2 + m * k * 4 + m * n * 4) / us / 1e3:.1f} GB/s"
+    print(f"ran {args.kernel} m={m} n={n} k={k} x{args.iters + 1}: {us:.2f} us/launch, {rate} "
+          f"(graph of back-to-back launches; operands L2-warm when they fit in L2)")
 
 
 # ------------------------------------------------------------------ helpers
@@ -180,6 +241,8 @@ def run_reference(args):
 # ------------------------------------------------------------------ GPU arm
 def main():
     args = parse()
+    if args.kernel:
+        return run_kernel_case(args)
     if args.impl == "reference":
         return run_reference(args)
 

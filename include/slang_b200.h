@@ -67,8 +67,11 @@ int sb_dequant_f16(const void* packed, int bits, const void* scales, int scale_d
                    int group, void* out, int n_out, int n_in, void* stream);
 
 /*
- * Decode GEMV over an int4 weight: y[m, n] = sum_k w[n, k] * x[m, k], fp32
- * accumulate, exact dequant (no f16 rounding of the weight).
+ * Decode GEMV over an int4 weight: y[m, n] = sum_k w[n, k] * x[m, k].
+ * The weight is used exactly (no f16 rounding); x is rounded to 16-bit
+ * integers per group of 32 (error <= 2^-16 of the group's max |x|), the
+ * int4 x int16 products are summed exactly in 32-bit integers and each
+ * group's sum is scaled in f32 (max-rel error vs an fp32 oracle ~1e-5).
  * Replaces matvec_dq4 (gemma4/qat_kernels.py:33-77) and the GEMV cores of the
  * decode kernels qkv_70 / oproj_73 / gateup_74 / down_75
  * (gemma4_150/kernels_dsl.py:1384-1480, 872-996, 1232-1300, 322-429), bound by

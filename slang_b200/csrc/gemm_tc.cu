@@ -1,24 +1,33 @@
 // tcgen05 GEMMs for prefill: sb_gemm_f16 (f16 x f16, both orientations of B)
 // and sb_gemm_q4 (A f16 x dequantised int4 W, fused).
 //
-// One CTA computes a 128 x 256 tile of C (BM tokens x BN output features) on
-// one SM with 128x256x16 UMMAs accumulating f32 in 256 TMEM columns.  The K
-// loop runs over 64-wide k-blocks (one 128-byte swizzle row of f16):
+// f16 kernel (gemm_tc_kernel): one CTA computes a 128 x 256 tile of C with
+// 128x256x16 UMMAs (A and B from shared memory) accumulating f32 in 256 TMEM
+// columns over 64-wide k-blocks:
+//   warp 0      TMA producer: A tile [128 x 64] f16 (128B swizzle) and the B
+//               tile [256 x 64] (K-major, tr=1) or four [64 k x 64 n] boxes
+//               (MN-major, tr=0) into a ring of stages.
+//   warp 1      TMEM allocation and the single MMA-issuing thread; completion
+//               is signalled back with tcgen05.commit.
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
+//               lanes 32*(w%4)...), alpha, f16 rounding, stores.
 //
-//   warp 0      TMA producer: A tile [128 x 64] f16 (128B swizzle) and, per
-//               mode, the B tile [256 x 64] f16 (K-major, tr=1), four
-//               [64 k x 64 n] boxes (MN-major, tr=0), or the packed int4 tile
-//               [256 rows x 32 bytes] (no swizzle) into a ring of stages.
-//   warp 1      TMEM allocation and the single MMA-issuing thread; MMA
-//               completion is signalled back with tcgen05.commit.
-//   warps 2..9  (int4 mode only) dequant producers: read the packed stage from
-//               shared memory, form f16(scale * (q - 8)) with exact f16 math,
-//               and store it in the UMMA K-major 128B-swizzled layout of a
-//               second ring; fence.proxy.async then an mbarrier arrive hands it
-//               to the tensor core.
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
-//               32*(w%4)...), scale by alpha, round to f16 and store to C (or
-//               store f32 partials to the split-K workspace).
+// int4 kernel (gemm_q4_kernel): the WEIGHT is the MMA's A operand and lives in
+// tensor memory.  A CTA owns 128 weight rows x 256 tokens; per k-block:
+//   warp 0      TMA: activation tile [256 tokens x 64] f16 (128B swizzle, the
+//               MMA's B operand) and the packed tile [128 rows x 32 bytes].
+//   warps 2..9  dequant: thread = one weight row (TMEM lane) and one 32-value
+//               group; f16(scale * (q - 8)) with exact f16 math, written with
+//               tcgen05.st into a 4-stage ring of 32-column A slots in TMEM.
+//               The tile's group scales are loaded into shared memory once.
+//   warp 1      tcgen05.mma.cta_group::1.kind::f16 with A from TMEM (M=128
+//               weight rows, N=256 tokens, K=16), accumulating D^T in 256
+//               TMEM columns.
+//   warps 2..9  epilogue: lane = output feature, column = token, so a warp's
+//               stores to C[token][feature] are contiguous.
+// Putting the dequantised weight in TMEM keeps it out of shared memory (no
+// 32 KB store + reload per k-block) and halves the dequant work per FLOP
+// compared with dequantising a 256-row B tile.
 //
 // Every mbarrier wait is bounded (2 s of %globaltimer): a stuck pipeline
 // raises a shared abort flag, writes SB_ERR_TIMEOUT to the device error word,
@@ -32,29 +41,38 @@
 
 namespace {
 
+// ---- f16 kernel tile: BM rows of A x BN rows of B (columns of C)
 constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int UMMA_K = 16;
-constexpr int A_BYTES = BM * BK * 2;   // 16 KB
-constexpr int B_BYTES = BN * BK * 2;   // 32 KB
-constexpr int P_BYTES = BN * BK / 2;   // 8 KB packed int4
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KB
 constexpr int TMEM_COLS = 256;
 
-enum Mode { MODE_F16_KMAJOR = 0, MODE_F16_MNMAJOR = 1, MODE_Q4 = 2 };
+// ---- int4 kernel tile: QW weight rows (MMA M, TMEM lanes) x QT tokens (MMA N)
+constexpr int QW = 128, QT = 256;
+constexpr int Q_ACT_BYTES = QT * BK * 2;     // 32 KB activation stage
+constexpr int Q_PACK_BYTES = QW * BK / 2;    // 4 KB packed stage
+constexpr int Q_STAGES = 4;                  // shared-memory load stages
+constexpr int Q_ASLOTS = 4;                  // TMEM A slots, 32 columns (64 k) each
+constexpr int Q_SCALE_BYTES = 48 * 1024;     // the tile's group scales
+constexpr int Q_WARPS = 10;                  // TMA, MMA, 8 dequant/epilogue
+constexpr int Q_TMEM_COLS = 512;             // 256 accumulator + 4 x 32 A slots
+constexpr int Q_OFF_PACK = Q_STAGES * Q_ACT_BYTES;
+constexpr int Q_OFF_SCALE = Q_OFF_PACK + Q_STAGES * Q_PACK_BYTES;
+constexpr int Q_OFF_BAR = Q_OFF_SCALE + Q_SCALE_BYTES;
+constexpr int Q_SMEM = Q_OFF_BAR + 256 + 1024;
+
+enum Mode { MODE_F16_KMAJOR = 0, MODE_F16_MNMAJOR = 1 };
 
 template <int MODE>
 struct Cfg {
-  static constexpr int kLoadStages = 4;
-  static constexpr int kDeqStages = MODE == MODE_Q4 ? 3 : 0;
-  static constexpr int kDqWarps = MODE == MODE_Q4 ? 8 : 0;
-  static constexpr int kWarps = MODE == MODE_Q4 ? 10 : 6;
+  static constexpr int kStages = 4;
+  static constexpr int kWarps = 6;
   static constexpr int kThreads = kWarps * 32;
-  static constexpr int kLoadBytes = A_BYTES + (MODE == MODE_Q4 ? P_BYTES : B_BYTES);
-  // layout: [A stages][B or packed stages][dequant B stages][barriers]
-  static constexpr int kOffB = kLoadStages * A_BYTES;
-  static constexpr int kOffD = kOffB + kLoadStages * (MODE == MODE_Q4 ? P_BYTES : B_BYTES);
-  static constexpr int kOffBar = kOffD + kDeqStages * B_BYTES;
-  static constexpr int kBarBytes = 256;
-  static constexpr int kSmem = kOffBar + kBarBytes + 1024;  // + alignment slack
+  static constexpr int kLoadBytes = A_BYTES + B_BYTES;
+  static constexpr int kOffB = kStages * A_BYTES;
+  static constexpr int kOffBar = kOffB + kStages * B_BYTES;
+  static constexpr int kSmem = kOffBar + 256 + 1024;  // + alignment slack
 };
 
 struct GemmParams {
@@ -87,10 +105,11 @@ __device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity) {
 
 // f16(scale * (q - 8)) for the 8 nibbles of `w`, as 4 half2 in k order.
 // byte_perm puts byte j of w in byte 0 and byte j of (w >> 4) in byte 2, so the
-// low nibbles of the two 16-bit halves hold the pair (q_2j, q_2j+1); OR-ing 0x6400 makes each half the f16 1024 + q, and
-// subtracting 1032 gives q - 8 exactly.  The product with an f16 scale is the
-// correctly rounded f16 of the exact product, i.e. f16(float(s) * (q - 8)).
-__device__ __forceinline__ void dq8_half(uint32_t w, __half2 s2, uint32_t (&out)[4]) {
+// low nibbles of the two 16-bit halves hold the pair (q_2j, q_2j+1); OR-ing
+// 0x6400 makes each half the f16 1024 + q, and subtracting 1032 gives q - 8
+// exactly.  The product with an f16 scale is the correctly rounded f16 of the
+// exact product, i.e. f16(float(s) * (q - 8)), the reference's dq_f16 value.
+__device__ __forceinline__ void dq8_half(uint32_t w, __half2 s2, uint32_t* out) {
   const uint32_t t = w >> 4;
   const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1032
   const uint32_t sel[4] = {0x0400u, 0x0501u, 0x0602u, 0x0703u};
@@ -103,7 +122,8 @@ __device__ __forceinline__ void dq8_half(uint32_t w, __half2 s2, uint32_t (&out)
   }
 }
 
-__device__ __forceinline__ void dq8_float(uint32_t w, float s, uint32_t (&out)[4]) {
+// Same with an f32 scale: the product is formed in f32 and rounded once.
+__device__ __forceinline__ void dq8_float(uint32_t w, float s, uint32_t* out) {
   const uint32_t t = w >> 4;
   const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
   const uint32_t sel[4] = {0x0400u, 0x0501u, 0x0602u, 0x0703u};
@@ -116,13 +136,15 @@ __device__ __forceinline__ void dq8_float(uint32_t w, float s, uint32_t (&out)[4
   }
 }
 
+// =====================================================================
+// f16 x f16 kernel (A and B from shared memory)
+// =====================================================================
 template <int MODE>
 __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmParams p) {
   using C = Cfg<MODE>;
-  constexpr int S = C::kLoadStages;
-  constexpr int S2 = C::kDeqStages > 0 ? C::kDeqStages : 1;
+  constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + C::kOffBar);
@@ -136,11 +158,7 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       sbd::mbar_init(&bars->full[i], 1);
-      sbd::mbar_init(&bars->empty[i], 1 + C::kDqWarps);
-    }
-    for (int i = 0; i < C::kDeqStages; ++i) {
-      sbd::mbar_init(&bars->dfull[i], C::kDqWarps);
-      sbd::mbar_init(&bars->dempty[i], 1);
+      sbd::mbar_init(&bars->empty[i], 1);
     }
     sbd::mbar_init(&bars->accum, 1);
     bars->abort = 0;
@@ -171,14 +189,12 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
         sbd::mbar_arrive_expect_tx(&bars->full[s], C::kLoadBytes);
         const int k0 = (kb0 + kb) * BK;
         sbd::tma_load_2d(&tmA, &bars->full[s], smem + s * A_BYTES, k0, m0);
-        uint8_t* bdst = smem + C::kOffB + s * (MODE == MODE_Q4 ? P_BYTES : B_BYTES);
+        uint8_t* bdst = smem + C::kOffB + s * B_BYTES;
         if (MODE == MODE_F16_KMAJOR) {
           sbd::tma_load_2d(&tmB, &bars->full[s], bdst, k0, n0);
-        } else if (MODE == MODE_F16_MNMAJOR) {
+        } else {
 #pragma unroll
           for (int j = 0; j < BN / 64; ++j) sbd::tma_load_2d(&tmB, &bars->full[s], bdst + j * 8192, n0 + 64 * j, k0);
-        } else {
-          sbd::tma_load_2d(&tmB, &bars->full[s], bdst, k0 / 2, n0);
         }
         issued = kb + 1;
       }
@@ -191,22 +207,12 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = sbd::umma_idesc_f16(BM, BN, 0, MODE == MODE_F16_MNMAJOR ? 1 : 0);
-      bool ok = true;
-      for (int kb = 0; kb < nkb && ok; ++kb) {
+      for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % S;
-        const uint32_t ph = (kb / S) & 1;
-        ok = sbd::mbar_wait(&bars->full[s], ph, abort, p.err);
-        int t2 = 0;
-        if (ok && MODE == MODE_Q4) {
-          t2 = kb % S2;
-          ok = sbd::mbar_wait(&bars->dfull[t2], (kb / S2) & 1, abort, p.err);
-        }
-        if (!ok) break;
+        if (!sbd::mbar_wait(&bars->full[s], (kb / S) & 1, abort, p.err)) break;
         sbd::tc_fence_after();
         const uint32_t a_base = sbd::smem_u32(smem + s * A_BYTES);
-        uint32_t b_base;
-        if (MODE == MODE_Q4) b_base = sbd::smem_u32(smem + C::kOffD + t2 * B_BYTES);
-        else b_base = sbd::smem_u32(smem + C::kOffB + s * B_BYTES);
+        const uint32_t b_base = sbd::smem_u32(smem + C::kOffB + s * B_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BK / UMMA_K; ++kk) {
           const uint64_t adesc = sbd::umma_desc(a_base + kk * 32, 16, 1024, sbd::kLayoutSwizzle128B);
@@ -216,111 +222,42 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
           sbd::umma_f16(tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
         }
         sbd::umma_commit(&bars->empty[s]);
-        if (MODE == MODE_Q4) sbd::umma_commit(&bars->dempty[t2]);
       }
       sbd::umma_commit(&bars->accum);  // fires once every MMA above has completed
     }
   } else {
-    // ------------------------------------------------------------ dequant producers
-    if (MODE == MODE_Q4) {
-      const int dt = threadIdx.x - 64;  // 0..255
-      const int gps = p.k / p.group;
-      bool ok = true;
-      for (int kb = 0; kb < nkb && ok; ++kb) {
-        const int s = kb % S;
-        const int t2 = kb % S2;
-        // scales for this thread's two 32-value chunks (issued before the waits)
-        float sc[2];
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    // tcgen05.ld is warp-collective: agree on the outcome of the wait first
+    const bool ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait(&bars->accum, 0, abort, p.err));
+    if (ok) {
+      sbd::tc_fence_after();
+      const int quad = warp & 3;
+      const int row = m0 + quad * 32 + lane;
+      const bool row_ok = row < p.m;
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        const int col0 = n0 + cc * 32;
+        if (col0 >= p.n) break;  // warp-uniform
+        uint32_t r[32];
+        sbd::tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + cc * 32, r);
+        sbd::tmem_wait_ld();
+        if (!row_ok) continue;
+        __half* dst = static_cast<__half*>(p.c) + static_cast<size_t>(row) * p.ldc + col0;
+        if (col0 + 32 <= p.n && (p.ldc % 8) == 0) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int c = dt + 256 * h;
-          const int row = n0 + (c >> 1);
-          const int kv = (kb0 + kb) * BK + (c & 1) * 32;
-          float v = 0.f;
-          if (row < p.n && kv < p.k) {
-            const size_t si = static_cast<size_t>(row) * gps + kv / p.group;
-            v = p.scale_f16 ? __half2float(static_cast<const __half*>(p.scales)[si])
-                            : static_cast<const float*>(p.scales)[si];
-          }
-          sc[h] = v;
-        }
-        ok = sbd::mbar_wait(&bars->full[s], (kb / S) & 1, abort, p.err);
-        if (ok) ok = sbd::mbar_wait(&bars->dempty[t2], ((kb / S2) & 1) ^ 1, abort, p.err);
-        if (!ok) break;
-        const uint8_t* pk = smem + C::kOffB + s * P_BYTES;
-        uint8_t* bt = smem + C::kOffD + t2 * B_BYTES;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int c = dt + 256 * h;
-          const int row = c >> 1, half = c & 1;
-          const uint4 q = *reinterpret_cast<const uint4*>(pk + c * 16);
-          const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-          const __half2 s2 = __float2half2_rn(sc[h]);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
+          for (int j = 0; j < 32; j += 8) {
             uint32_t o[4];
-            if (p.scale_f16) dq8_half(words[j], s2, o);
-            else dq8_float(words[j], sc[h], o);
-            const int chunk = (half * 4 + j) ^ (row & 7);
-            *reinterpret_cast<uint4*>(bt + row * 128 + chunk * 16) = make_uint4(o[0], o[1], o[2], o[3]);
-          }
-        }
-        sbd::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          sbd::mbar_arrive(&bars->dfull[t2]);
-          sbd::mbar_arrive(&bars->empty[s]);
-        }
-      }
-    }
-    // ------------------------------------------------------------ epilogue
-    if (warp >= 2 && warp < 6) {
-      // tcgen05.ld is warp-collective: agree on the outcome of the wait first
-      const bool ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait(&bars->accum, 0, abort, p.err));
-      if (ok) {
-        sbd::tc_fence_after();
-        const int quad = warp & 3;
-        const int row = m0 + quad * 32 + lane;
-        const bool row_ok = row < p.m;
-        for (int cc = 0; cc < BN / 32; ++cc) {
-          const int col0 = n0 + cc * 32;
-          if (col0 >= p.n) break;  // warp-uniform
-          uint32_t r[32];
-          sbd::tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + cc * 32, r);
-          sbd::tmem_wait_ld();
-          if (!row_ok) continue;
-          if (p.ws) {
-            float* dst = p.ws + (static_cast<size_t>(blockIdx.z) * p.m + row) * p.n + col0;
-            if (col0 + 32 <= p.n && (p.n % 4) == 0) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                                  __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < p.n) dst[j] = __uint_as_float(r[j]);
+            for (int e = 0; e < 4; ++e) {
+              __half2 h = __floats2half2_rn(p.alpha * __uint_as_float(r[j + 2 * e]),
+                                            p.alpha * __uint_as_float(r[j + 2 * e + 1]));
+              o[e] = *reinterpret_cast<uint32_t*>(&h);
             }
-          } else {
-            __half* dst = static_cast<__half*>(p.c) + static_cast<size_t>(row) * p.ldc + col0;
-            if (col0 + 32 <= p.n && (p.ldc % 8) == 0) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                uint32_t o[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  __half2 h = __floats2half2_rn(p.alpha * __uint_as_float(r[j + 2 * e]),
-                                                p.alpha * __uint_as_float(r[j + 2 * e + 1]));
-                  o[e] = *reinterpret_cast<uint32_t*>(&h);
-                }
-                *reinterpret_cast<uint4*>(dst + j) = make_uint4(o[0], o[1], o[2], o[3]);
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < p.n) dst[j] = __float2half_rn(p.alpha * __uint_as_float(r[j]));
-            }
+            *reinterpret_cast<uint4*>(dst + j) = make_uint4(o[0], o[1], o[2], o[3]);
           }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < p.n) dst[j] = __float2half_rn(p.alpha * __uint_as_float(r[j]));
         }
       }
     }
@@ -331,6 +268,182 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
   if (warp == 1) {
     sbd::tc_fence_after();
     sbd::tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// =====================================================================
+// int4 kernel: dequantised weight as the A operand in tensor memory
+// =====================================================================
+// p.m = tokens (MMA N side), p.n = weight rows (MMA M side).
+__global__ void __launch_bounds__(Q_WARPS * 32, 1)
+    gemm_q4_kernel(const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ CUtensorMap tmW,
+                   const GemmParams p) {
+  constexpr int S = Q_STAGES, T = Q_ASLOTS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + Q_OFF_BAR);
+  volatile int* abort = &bars->abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int w0 = blockIdx.x * QW;  // first weight row
+  const int t0 = blockIdx.y * QT;  // first token
+  const int kb0 = blockIdx.z * p.kb_per_split;
+  const int nkb = min(p.kb_per_split, p.kb_total - kb0);
+  // group scales of this split's K range: [g_lo, g_hi)
+  const int g_lo = (kb0 * BK) / p.group;
+  const int g_hi = ((kb0 + nkb) * BK + p.group - 1) / p.group;
+  const int gs = g_hi - g_lo;
+  const int gps = p.k / p.group;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      sbd::mbar_init(&bars->full[i], 1);
+      sbd::mbar_init(&bars->empty[i], 1 + 8);
+    }
+    for (int i = 0; i < T; ++i) {
+      sbd::mbar_init(&bars->dfull[i], 8);
+      sbd::mbar_init(&bars->dempty[i], 1);
+    }
+    sbd::mbar_init(&bars->accum, 1);
+    bars->abort = 0;
+    sbd::fence_mbar_init();
+    sbd::fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    sbd::prefetch_tmap(&tmAct);
+    sbd::prefetch_tmap(&tmW);
+  }
+  if (warp == 1) {
+    sbd::tmem_alloc(&bars->tmem_slot, Q_TMEM_COLS);
+    sbd::tmem_relinquish();
+  }
+  sbd::tc_fence_before();
+  __syncthreads();
+  sbd::tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % S;
+        if (!sbd::mbar_wait(&bars->empty[s], ((kb / S) & 1) ^ 1, abort, p.err)) break;
+        sbd::mbar_arrive_expect_tx(&bars->full[s], Q_ACT_BYTES + Q_PACK_BYTES);
+        const int k0 = (kb0 + kb) * BK;
+        sbd::tma_load_2d(&tmAct, &bars->full[s], smem + s * Q_ACT_BYTES, k0, t0);
+        sbd::tma_load_2d(&tmW, &bars->full[s], smem + Q_OFF_PACK + s * Q_PACK_BYTES, k0 / 2, w0);
+        issued = kb + 1;
+      }
+      if (*abort) {
+        for (int kb = max(0, issued - S); kb < issued; ++kb) drain_wait(&bars->full[kb % S], (kb / S) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = sbd::umma_idesc_f16(QW, QT, 0, 0);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % S, slot = kb % T;
+        if (!sbd::mbar_wait(&bars->full[s], (kb / S) & 1, abort, p.err)) break;
+        if (!sbd::mbar_wait(&bars->dfull[slot], (kb / T) & 1, abort, p.err)) break;
+        sbd::tc_fence_after();
+        const uint32_t b_base = sbd::smem_u32(smem + s * Q_ACT_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+          const uint32_t a_tmem = tmem + 256 + slot * 32 + kk * 8;
+          const uint64_t bdesc = sbd::umma_desc(b_base + kk * 32, 16, 1024, sbd::kLayoutSwizzle128B);
+          sbd::umma_f16_ts(tmem, a_tmem, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+        }
+        sbd::umma_commit(&bars->empty[s]);
+        sbd::umma_commit(&bars->dempty[slot]);
+      }
+      sbd::umma_commit(&bars->accum);
+    }
+  } else {
+    // ------------------------------------------------------------ dequant producers (warps 2..9)
+    const int quad = warp & 3;          // TMEM lane quadrant this warp may access
+    const int khalf = (warp - 2) >> 2;  // which 32-value group of the k-block
+    const int r = quad * 32 + lane;     // weight row within the tile
+    const int dt = threadIdx.x - 64;    // 0..255
+    // the tile's scales -> shared memory, in their storage type
+    const int esz = p.scale_f16 ? 2 : 4;
+    uint8_t* sct = smem + Q_OFF_SCALE;
+    for (int i = dt; i < QW * gs; i += 256) {
+      const int rr = i / gs, g = i - rr * gs;
+      const int row = w0 + rr;
+      const size_t si = static_cast<size_t>(row) * gps + g_lo + g;
+      if (esz == 2) {
+        reinterpret_cast<__half*>(sct)[i] = row < p.n ? static_cast<const __half*>(p.scales)[si] : __float2half(0.f);
+      } else {
+        reinterpret_cast<float*>(sct)[i] = row < p.n ? static_cast<const float*>(p.scales)[si] : 0.f;
+      }
+    }
+    sbd::named_bar_sync(1, 256);
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % S, slot = kb % T;
+      const int kv = (kb0 + kb) * BK + khalf * 32;
+      const int gi = kv / p.group - g_lo;
+      bool ok = sbd::mbar_wait(&bars->full[s], (kb / S) & 1, abort, p.err);
+      if (ok) ok = sbd::mbar_wait(&bars->dempty[slot], ((kb / T) & 1) ^ 1, abort, p.err);
+      if (!__all_sync(0xFFFFFFFFu, ok)) break;
+      sbd::tc_fence_after();
+      const uint4 q = *reinterpret_cast<const uint4*>(smem + Q_OFF_PACK + s * Q_PACK_BYTES + r * 32 + khalf * 16);
+      const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+      uint32_t o[16];
+      if (p.scale_f16) {
+        const __half2 s2 = __half2half2(reinterpret_cast<const __half*>(sct)[r * gs + gi]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dq8_half(words[j], s2, o + 4 * j);
+      } else {
+        const float sf = reinterpret_cast<const float*>(sct)[r * gs + gi];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dq8_float(words[j], sf, o + 4 * j);
+      }
+      sbd::tmem_st_32x32b_x16(lane_addr + 256 + slot * 32 + khalf * 16, o);
+      sbd::tmem_wait_st();
+      sbd::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        sbd::mbar_arrive(&bars->dfull[slot]);
+        sbd::mbar_arrive(&bars->empty[s]);
+      }
+    }
+    // ------------------------------------------------------------ epilogue
+    // D^T: TMEM lane = weight row (output feature), column = token.
+    const bool ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait(&bars->accum, 0, abort, p.err));
+    if (ok) {
+      sbd::tc_fence_after();
+      const int feat = w0 + r;
+      const bool feat_ok = feat < p.n;
+      for (int cc = 0; cc < 4; ++cc) {
+        const int col = khalf * 128 + cc * 32;  // token offset within the tile
+        if (t0 + col >= p.m) break;             // warp-uniform
+        uint32_t v[32];
+        sbd::tmem_ld_32x32b_x32(lane_addr + col, v);
+        sbd::tmem_wait_ld();
+        if (!feat_ok) continue;
+        if (p.ws) {
+          float* dst = p.ws + (static_cast<size_t>(blockIdx.z) * p.m + t0 + col) * p.n + feat;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (t0 + col + j < p.m) dst[static_cast<size_t>(j) * p.n] = __uint_as_float(v[j]);
+        } else {
+          __half* dst = static_cast<__half*>(p.c) + static_cast<size_t>(t0 + col) * p.ldc + feat;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (t0 + col + j < p.m) dst[static_cast<size_t>(j) * p.ldc] = __float2half_rn(p.alpha * __uint_as_float(v[j]));
+        }
+      }
+    }
+  }
+
+  sbd::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sbd::tc_fence_after();
+    sbd::tmem_dealloc(tmem, Q_TMEM_COLS);
   }
 }
 
@@ -375,30 +488,49 @@ int make_map(CUtensorMap* map, CUtensorMapDataType dt, int elt, const void* base
   return SB_OK;
 }
 
-template <int MODE>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int splits, cudaStream_t s) {
-  using C = Cfg<MODE>;
-  static bool attr_set[64] = {false};
+template <typename K>
+int set_smem(K kernel, int bytes, bool (&done)[64]) {
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    if (e != cudaSuccess) return sb::cuda_fail(e, "gemm_tc_kernel: smem attribute");
-    attr_set[dev] = true;
+  if (dev >= 0 && dev < 64 && !done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return sb::cuda_fail(e, "gemm: shared-memory attribute");
+    done[dev] = true;
   }
-  dim3 grid((p.n + BN - 1) / BN, (p.m + BM - 1) / BM, splits);
+  return SB_OK;
+}
+
+template <int MODE>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s) {
+  using C = Cfg<MODE>;
+  static bool done[64] = {false};
+  int rc = set_smem(gemm_tc_kernel<MODE>, C::kSmem, done);
+  if (rc) return rc;
+  dim3 grid((p.n + BN - 1) / BN, (p.m + BM - 1) / BM, 1);
   gemm_tc_kernel<MODE><<<grid, C::kThreads, C::kSmem, s>>>(ta, tb, p);
   return sb::launch_status("gemm_tc_kernel");
 }
 
-int choose_splits(int m, int n, int k) {
-  const int tiles = ((n + BN - 1) / BN) * ((m + BM - 1) / BM);
-  const int kb = (k + BK - 1) / BK;
+// Scale groups one split of `kbs` k-blocks can touch per row: groups of 32 or 64
+// tile a k-block exactly; larger groups may straddle the split's first k-block.
+int q4_scale_groups(int kbs, int group) {
+  return group <= BK ? kbs * (BK / group) : (kbs * BK + group - 1) / group + 1;
+}
+
+// Split-K for the int4 kernel: enough CTAs to fill the SMs when the tile count
+// is small, and enough splits that a split's group scales fit in shared memory.
+int q4_splits(int m, int n, int k, int group, int scale_bytes) {
+  const int tiles = ((n + QW - 1) / QW) * ((m + QT - 1) / QT);
+  const int kb = k / BK;
   const int sms = sb::num_sms();
-  if (tiles * 4 >= sms * 3) return 1;
-  int splits = std::max(1, sms / tiles);
-  splits = std::min(splits, std::max(1, kb / 4));
-  splits = std::min(splits, 16);
+  int splits = 1;
+  if (tiles * 4 < sms * 3) {
+    splits = std::max(1, sms / tiles);
+    splits = std::min(splits, std::max(1, kb / 4));
+    splits = std::min(splits, 16);
+  }
+  while (splits < kb && QW * q4_scale_groups((kb + splits - 1) / splits, group) * scale_bytes > Q_SCALE_BYTES)
+    ++splits;
   return splits;
 }
 
@@ -411,10 +543,15 @@ int finalize(const GemmParams& p, int splits, cudaStream_t s) {
 
 }  // namespace
 
-extern "C" size_t sb_gemm_q4_workspace_size(int m, int n, int k) {
-  if (m <= 0 || n <= 0 || k <= 0) return 0;
-  const int splits = choose_splits(m, n, k);
+static size_t q4_workspace(int m, int n, int k, int group, int scale_bytes) {
+  if (m <= 0 || n <= 0 || k <= 0 || k % BK || group <= 0) return 0;
+  const int splits = q4_splits(m, n, k, group, scale_bytes);
   return splits > 1 ? static_cast<size_t>(splits) * m * n * sizeof(float) : 0;
+}
+
+extern "C" size_t sb_gemm_q4_workspace_size(int m, int n, int k) {
+  // for the group-32 f16 scales of the benchmark format
+  return q4_workspace(m, n, k, 32, 2);
 }
 
 extern "C" int sb_gemm_f16(const void* a, const void* b, void* c, int m, int n, int k, float alpha, int tr, int lda,
@@ -450,7 +587,7 @@ extern "C" int sb_gemm_f16(const void* a, const void* b, void* c, int m, int n, 
   p.alpha = alpha;
   p.kb_total = (k + BK - 1) / BK;
   p.kb_per_split = p.kb_total;
-  return tr ? launch<MODE_F16_KMAJOR>(ta, tb, p, 1, s) : launch<MODE_F16_MNMAJOR>(ta, tb, p, 1, s);
+  return tr ? launch<MODE_F16_KMAJOR>(ta, tb, p, s) : launch<MODE_F16_MNMAJOR>(ta, tb, p, s);
 }
 
 extern "C" int sb_gemm_q4(const void* a, const void* w, const void* scales, int scale_dtype, int group, void* c, int m,
@@ -467,10 +604,11 @@ extern "C" int sb_gemm_q4(const void* a, const void* w, const void* scales, int 
   if (!sb::aligned(a, 16) || !sb::aligned(w, 16) || !sb::aligned(c, 2) || lda % 8)
     return sb::fail(SB_ERR_ALIGN, "sb_gemm_q4: A and W must be 16-byte aligned with lda a multiple of 8");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  CUtensorMap ta, tb;
-  int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, k, m, lda, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  const int esz = scale_dtype == SB_SCALE_F16 ? 2 : 4;
+  CUtensorMap tact, tw;
+  int rc = make_map(&tact, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, k, m, lda, BK, QT, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, k / 2, n, k / 2, BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+  rc = make_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, k / 2, n, k / 2, BK / 2, QW, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   GemmParams p{};
   p.scales = scales;
@@ -481,16 +619,26 @@ extern "C" int sb_gemm_q4(const void* a, const void* w, const void* scales, int 
   p.k = k;
   p.ldc = ldc;
   p.group = group;
-  p.scale_f16 = scale_dtype == SB_SCALE_F16;
+  p.scale_f16 = esz == 2;
   p.alpha = alpha;
   p.kb_total = k / BK;
-  int splits = choose_splits(m, n, k);
+  int splits = q4_splits(m, n, k, group, esz);
   const size_t need = splits > 1 ? static_cast<size_t>(splits) * m * n * sizeof(float) : 0;
-  if (splits > 1 && (!workspace || workspace_bytes < need)) splits = 1;
+  if (splits > 1 && (!workspace || workspace_bytes < need)) {
+    // without room for partial sums run unsplit, if the scales still fit
+    if (QW * q4_scale_groups(k / BK, group) * esz > Q_SCALE_BYTES)
+      return sb::fail(SB_ERR_WORKSPACE, "sb_gemm_q4: k=%d needs split-K (%zu workspace bytes) for its scales", k, need);
+    splits = 1;
+  }
   p.kb_per_split = (p.kb_total + splits - 1) / splits;
   splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
   if (splits > 1) p.ws = static_cast<float*>(workspace);
-  rc = launch<MODE_Q4>(ta, tb, p, splits, s);
+  static bool done[64] = {false};
+  rc = set_smem(gemm_q4_kernel, Q_SMEM, done);
+  if (rc) return rc;
+  dim3 grid((n + QW - 1) / QW, (m + QT - 1) / QT, splits);
+  gemm_q4_kernel<<<grid, Q_WARPS * 32, Q_SMEM, s>>>(tact, tw, p);
+  rc = sb::launch_status("gemm_q4_kernel");
   if (rc != SB_OK || splits == 1) return rc;
   return finalize(p, splits, s);
 }

@@ -1,28 +1,43 @@
 // Decode GEMV over packed int4 weights (sb_gemv_q4) and the tied lm_head GEMV
 // fused with greedy argmax (sb_lmhead_argmax).
 //
-// Work split.  A CTA is 16 half-warps.  The K range is cut into `ks` slices
-// (1..16, a power of two) and each half-warp owns one slice for a run of R
-// rows; lane l of a half-warp owns the groups slice_begin + l + 16*u,
-// u < GPL, of every row it visits.  Because a lane's groups never change, its
-// slice of x (32 f32 values per group and decode row) is loaded into
-// registers once per CTA and reused for every row: the inner loop touches only
-// the weight stream.  Each (row, group) is one 16-byte load of 32 nibbles; a
-// half-warp reads 256 contiguous bytes per group index, so loads are fully
-// coalesced.  Partial sums are reduced with half-warp shuffles and, across
-// K slices, through shared memory, in a fixed order (deterministic results).
+// Streaming.  Rows are cut into stages of `rs` consecutive rows; a stage is one
+// contiguous span of the packed matrix (and of its scales), moved by a single
+// cp.async.bulk (TMA bulk copy) into a 4-deep shared-memory ring whose slots
+// complete on mbarriers.  Lane 0 of warp 0 issues the first four stages at
+// entry and refills a slot right after the per-stage CTA barrier that already
+// proves every warp is done with it, so there is no producer warp and no
+// "empty" barrier.  CTAs (8 warps) take stages round robin, two per SM, so up
+// to 8 x 24 KB per SM is in flight.  Kernels are launched with programmatic
+// dependent launch: weights (which no earlier kernel writes) start streaming
+// at once, and the warps wait for the previous kernel (griddepcontrol.wait)
+// only before they read x.
 //
-// Exact dequant without an int->float conversion: for a nibble q at bit p of
-// a word (p <= 16), the f32 with exponent 150-p and mantissa (q << p) equals
-// 2^(23-p) + q, so subtracting 2^(23-p) + 8 gives q - 8 exactly.  One LOP3 and
-// one FADD per value; nibbles 5..7 are first shifted down by 12 bits.
+// Arithmetic.  16 consumer half-warps; K is split into `ks` slices and each
+// half-warp owns one slice of some rows of a stage; lane l owns the 32-value
+// groups slice_begin + l + 16*u (u < GPL) of every row it visits.  Its slice
+// of x is quantised once per CTA to 16-bit integers per group (scale = the
+// group's max |x| / 32767, error <= 2^-16 of that max) and split into a
+// signed high byte and an unsigned low byte, packed to match the packed
+// nibbles.  A 16-byte chunk (32 nibbles) then costs 2 LOP3, 1 SHF and 4 DP4A
+// per 8 values, and the int4 x int16 products are summed exactly in int32:
+//   sum_k (q_k - 8) x_k = 256*dot(q, x_hi) + dot(q, x_lo) - 8*sum(x_int).
+// Per (row, group) the integer dot is scaled by s_w * s_x in f32.  Partial
+// sums are reduced with half-warp shuffles and, across K slices, through
+// shared memory in a fixed order (deterministic results).
 #include <algorithm>
 
 #include "common.cuh"
 
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kConsumers = 256;                 // 8 warps, all computing
+constexpr int kThreads = kConsumers;
+constexpr int kRing = 4;                        // stages in flight per CTA
+constexpr int kStageW = 24 * 1024;              // max weight bytes per stage
+constexpr int kStageS = 3 * 1024;               // max scale bytes per stage
+constexpr int kCtasPerSm = 2;                   // two CTAs share an SM (registers <= 113)
+constexpr int kRedMax = 128;                    // partial-sum slots per stage (rows x ks x M)
 
 enum { EPI_STORE = 0, EPI_ARGMAX = 1 };
 
@@ -33,21 +48,19 @@ struct GemvParams {
   float* y;
   unsigned long long* keys;
   float* logits;
-  int m, n, k, group, ldy, ks;
+  int* err;
+  int m, n, k, group, ldy, ks, rs, n_stages, scale_bulk, x_f32;
   long long row_offset;
 };
 
-__device__ __forceinline__ void nibbles8(uint32_t w, float (&v)[8]) {
-  const uint32_t t = w >> 12;
-  v[0] = __uint_as_float((w & 0x0000000Fu) | 0x4B000000u) - 8388616.0f;
-  v[1] = __uint_as_float((w & 0x000000F0u) | 0x49000000u) - 524296.0f;
-  v[2] = __uint_as_float((w & 0x00000F00u) | 0x47000000u) - 32776.0f;
-  v[3] = __uint_as_float((w & 0x0000F000u) | 0x45000000u) - 2056.0f;
-  v[4] = __uint_as_float((w & 0x000F0000u) | 0x43000000u) - 136.0f;
-  v[5] = __uint_as_float((t & 0x00000F00u) | 0x47000000u) - 32776.0f;
-  v[6] = __uint_as_float((t & 0x0000F000u) | 0x45000000u) - 2056.0f;
-  v[7] = __uint_as_float((t & 0x000F0000u) | 0x43000000u) - 136.0f;
-}
+struct GemvSmem {
+  uint8_t w[kRing][kStageW];
+  uint8_t s[kRing][kStageS];
+  float red[2][kRedMax];
+  unsigned long long best[8][4];
+  uint64_t full[kRing];
+  int abort;
+};
 
 __device__ __forceinline__ uint32_t orderable(float f) {
   if (f != f) f = -INFINITY;
@@ -60,49 +73,134 @@ __device__ __forceinline__ unsigned long long make_key(float v, long long idx) {
          static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(idx));
 }
 
-template <int M, int R, int GPL, bool XF32, bool SF16, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const GemvParams p) {
-  __shared__ float red[16 * R * M];
-  __shared__ unsigned long long best_s[kThreads / 32][M];
+// x of one group (32 values) as the DP4A operands: 4 words x {hi even, hi odd,
+// lo even, lo odd} bytes, plus -8 * sum(x_int) and the group's scale.
+struct XGroup {
+  uint32_t he[4], ho[4], le[4], lo[4];
+  int bias;
+  float sx;
+};
 
+__device__ __forceinline__ void quantise_group(const float (&v)[32], XGroup& g) {
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(v[i]));
+  const float inv = mx > 0.f ? 32767.f / mx : 0.f;
+  g.sx = mx / 32767.f;
+  int sum = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t he = 0, ho = 0, le = 0, lo = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int xe = __float2int_rn(v[8 * j + 2 * i] * inv);
+      const int xo = __float2int_rn(v[8 * j + 2 * i + 1] * inv);
+      sum += xe + xo;
+      he |= (static_cast<uint32_t>(xe >> 8) & 0xFFu) << (8 * i);
+      ho |= (static_cast<uint32_t>(xo >> 8) & 0xFFu) << (8 * i);
+      le |= (static_cast<uint32_t>(xe) & 0xFFu) << (8 * i);
+      lo |= (static_cast<uint32_t>(xo) & 0xFFu) << (8 * i);
+    }
+    g.he[j] = he;
+    g.ho[j] = ho;
+    g.le[j] = le;
+    g.lo[j] = lo;
+  }
+  g.bias = -8 * sum;
+}
+
+// exact integer dot of 32 int4 codes (minus 8) with the group's x_int
+// (four independent accumulation chains for instruction-level parallelism)
+__device__ __forceinline__ int dot_group(const uint4 q, const XGroup& g) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+  int he = 0, ho = 0, le = g.bias, lo = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t e = w[j] & 0x0F0F0F0Fu;
+    const uint32_t o = (w[j] >> 4) & 0x0F0F0F0Fu;
+    he = sbd::dp4a_us(e, g.he[j], he);
+    ho = sbd::dp4a_us(o, g.ho[j], ho);
+    le = sbd::dp4a_uu(e, g.le[j], le);
+    lo = sbd::dp4a_uu(o, g.lo[j], lo);
+  }
+  return (he + ho) * 256 + le + lo;
+}
+
+template <int M, int GPL, bool SF16, int EPI>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  GemvSmem& sm = *reinterpret_cast<GemvSmem*>(smem_raw);
+  volatile int* abort = &sm.abort;
   const int tid = threadIdx.x;
-  const int hw = tid >> 4, l16 = tid & 15;
+  const int row_bytes = p.k >> 1;
+  const int gps = p.k / p.group;
+  const int esz = SF16 ? 2 : 4;
+
+  sbd::griddep_launch_dependents();
+  const int my_stages = p.n_stages > static_cast<int>(blockIdx.x)
+                            ? (p.n_stages - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1
+                            : 0;
+  // issue the bulk copies of this CTA's i-th stage into ring slot i % kRing
+  auto issue = [&](int i) {
+    const int slot = i % kRing;
+    const int st = blockIdx.x + i * gridDim.x;
+    const int r0 = st * p.rs;
+    const int nr = min(p.rs, p.n - r0);
+    const uint32_t wb = static_cast<uint32_t>(nr) * row_bytes;
+    const uint32_t sbytes = p.scale_bulk ? static_cast<uint32_t>(nr) * gps * esz : 0u;
+    sbd::mbar_arrive_expect_tx(&sm.full[slot], wb + sbytes);
+    sbd::bulk_load(sm.w[slot], p.w + static_cast<size_t>(r0) * row_bytes, wb, &sm.full[slot]);
+    if (sbytes)
+      sbd::bulk_load(sm.s[slot], static_cast<const uint8_t*>(p.scales) + static_cast<size_t>(r0) * gps * esz, sbytes,
+                     &sm.full[slot]);
+  };
+  if (tid == 0) {
+    for (int i = 0; i < kRing; ++i) sbd::mbar_init(&sm.full[i], 1);
+    sm.abort = 0;
+    sbd::fence_mbar_init();
+    sbd::fence_proxy_async_smem();
+    // weights do not depend on the previous kernel: start streaming now
+    for (int i = 0; i < kRing && i < my_stages; ++i) issue(i);
+  }
+  __syncthreads();
+
+  const int hw = tid >> 4, l16 = tid & 15, warp = tid >> 5;
   const int ks = p.ks;
   const int kslice = hw % ks, rlane = hw / ks, nrl = 16 / ks;
   const int G = p.k >> 5;
   const int SG = (G + ks - 1) / ks;
   const int g_begin = kslice * SG;
   const int g_end = min(G, g_begin + SG);
-  const int row_bytes = p.k >> 1;
-  const int gps = p.k / p.group;  // scales per row
-  const int gshift = __ffs(p.group) - 1;
-  const bool pow2_group = (p.group & (p.group - 1)) == 0;
 
-  int gidx[GPL];
+  int gidx[GPL], gsi[GPL];
   bool gval[GPL];
 #pragma unroll
   for (int u = 0; u < GPL; ++u) {
     gidx[u] = g_begin + l16 + 16 * u;
     gval[u] = gidx[u] < g_end;
+    gsi[u] = (gidx[u] * 32) / p.group;  // scale index of this group within a row
   }
 
-  // this lane's slice of x, kept in registers for the whole kernel
-  float xr[M][GPL][32];
+  // x is the previous kernel's output: wait for it (weights are already streaming)
+  sbd::griddep_wait();
+  // this lane's groups of x, quantised once (kept in registers)
+  XGroup xg[M][GPL];
 #pragma unroll
   for (int m = 0; m < M; ++m) {
 #pragma unroll
     for (int u = 0; u < GPL; ++u) {
+      float v[32];
       const bool ok = gval[u] && m < p.m;
-      if (XF32) {
+      if (p.x_f32) {
         const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) +
                                                             static_cast<size_t>(m) * p.k + gidx[u] * 32);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float4 f = ok ? __ldg(src + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-          xr[m][u][4 * j + 0] = f.x;
-          xr[m][u][4 * j + 1] = f.y;
-          xr[m][u][4 * j + 2] = f.z;
-          xr[m][u][4 * j + 3] = f.w;
+          v[4 * j] = f.x;
+          v[4 * j + 1] = f.y;
+          v[4 * j + 2] = f.z;
+          v[4 * j + 3] = f.w;
         }
       } else {
         const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x) +
@@ -114,11 +212,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const GemvParams p
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hv[e]));
-            xr[m][u][8 * j + 2 * e] = f.x;
-            xr[m][u][8 * j + 2 * e + 1] = f.y;
+            v[8 * j + 2 * e] = f.x;
+            v[8 * j + 2 * e + 1] = f.y;
           }
         }
       }
+      quantise_group(v, xg[m][u]);
     }
   }
 
@@ -130,109 +229,81 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const GemvParams p
     best_i[m] = 0x7FFFFFFF;
   }
 
-  const int rows_per_tile = nrl * R;
-  const int ntiles = (p.n + rows_per_tile - 1) / rows_per_tile;
-  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const int row0 = tile * rows_per_tile + rlane * R;
-    uint4 wv[GPL][R];
-    float sv[GPL][R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int row = row0 + r;
-      const bool rv = row < p.n;
-#pragma unroll
-      for (int u = 0; u < GPL; ++u) {
-        if (rv && gval[u]) {
-          wv[u][r] = sbd::ldg_nc_v4(p.w + static_cast<size_t>(row) * row_bytes + gidx[u] * 16);
-          const int gi = pow2_group ? ((gidx[u] * 32) >> gshift) : (gidx[u] * 32) / p.group;
-          const size_t si = static_cast<size_t>(row) * gps + gi;
-          sv[u][r] = SF16 ? __half2float(static_cast<const __half*>(p.scales)[si])
-                          : static_cast<const float*>(p.scales)[si];
-        } else {
-          wv[u][r] = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);  // all q-8 == 0
-          sv[u][r] = 0.f;
-        }
-      }
-    }
-
-    float acc[M][R];
-#pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-      for (int r = 0; r < R; ++r) acc[m][r] = 0.f;
-
-#pragma unroll
-    for (int u = 0; u < GPL; ++u) {
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const uint32_t words[4] = {wv[u][r].x, wv[u][r].y, wv[u][r].z, wv[u][r].w};
-        float d[M];
-#pragma unroll
-        for (int m = 0; m < M; ++m) d[m] = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float v[8];
-          nibbles8(words[j], v);
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-#pragma unroll
-            for (int m = 0; m < M; ++m) d[m] = fmaf(v[i], xr[m][u][8 * j + i], d[m]);
-        }
-#pragma unroll
-        for (int m = 0; m < M; ++m) acc[m][r] = fmaf(sv[u][r], d[m], acc[m][r]);
-      }
-    }
-
-#pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-#pragma unroll
-        for (int off = 8; off > 0; off >>= 1) acc[m][r] += __shfl_xor_sync(0xFFFFFFFFu, acc[m][r], off, 16);
-      }
-
-    bool owner = l16 == 0;
-    if (ks > 1) {
-      if (l16 == 0) {
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-          for (int m = 0; m < M; ++m) red[(hw * R + r) * M + m] = acc[m][r];
-      }
-      __syncthreads();
-      owner = owner && kslice == 0;
-      if (owner) {
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-          for (int m = 0; m < M; ++m) {
-            float s = 0.f;
-            for (int q = 0; q < ks; ++q) s += red[((rlane * ks + q) * R + r) * M + m];
-            acc[m][r] = s;
+  for (int i = 0; i < my_stages; ++i) {
+    const int slot = i % kRing;
+    const bool ok = sbd::mbar_wait(&sm.full[slot], (i / kRing) & 1, abort, p.err);
+    if (!__syncthreads_and(ok)) {
+      // a copy never landed: let any still in flight finish before the CTA exits
+      if (tid == 0) {
+        const uint64_t t0 = sbd::global_ns();
+        for (int j = i; j < i + kRing && j < my_stages; ++j)
+          while (!sbd::mbar_try_wait(&sm.full[j % kRing], (j / kRing) & 1) &&
+                 sbd::global_ns() - t0 < sbd::kWaitLimitNs) {
           }
       }
-      __syncthreads();
+      return;
     }
-
-    if (owner) {
+    const int st = blockIdx.x + i * gridDim.x;
+    const int r0 = st * p.rs;
+    const int nr = min(p.rs, p.n - r0);
+    float* red = sm.red[i & 1];
+    const uint8_t* wst = sm.w[slot];
+    const uint8_t* sst = sm.s[slot];
+    for (int rr = rlane; rr < p.rs; rr += nrl) {  // same trip count for every half-warp
+      float acc[M];
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int row = row0 + r;
-        if (row >= p.n) continue;
+      for (int m = 0; m < M; ++m) acc[m] = 0.f;
+      if (rr < nr) {
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-          if (m >= p.m) continue;
-          if (EPI == EPI_STORE) {
-            p.y[static_cast<size_t>(m) * p.ldy + row] = acc[m][r];
+        for (int u = 0; u < GPL; ++u) {
+          if (!gval[u]) continue;
+          const uint4 q = *reinterpret_cast<const uint4*>(wst + rr * row_bytes + gidx[u] * 16);
+          const int gi = gsi[u];
+          float sw;
+          if (p.scale_bulk) {
+            sw = SF16 ? __half2float(reinterpret_cast<const __half*>(sst)[rr * gps + gi])
+                      : reinterpret_cast<const float*>(sst)[rr * gps + gi];
           } else {
-            float v = acc[m][r];
-            if (p.logits) p.logits[static_cast<size_t>(m) * p.n + row] = v;
-            if (v != v) v = -INFINITY;
-            const long long gi = p.row_offset + row;
-            if (v > best_v[m] || (v == best_v[m] && gi < best_i[m])) {
-              best_v[m] = v;
-              best_i[m] = gi;
-            }
+            const size_t si = static_cast<size_t>(r0 + rr) * gps + gi;
+            sw = SF16 ? __half2float(static_cast<const __half*>(p.scales)[si]) : static_cast<const float*>(p.scales)[si];
+          }
+#pragma unroll
+          for (int m = 0; m < M; ++m)
+            acc[m] = fmaf(static_cast<float>(dot_group(q, xg[m][u])), sw * xg[m][u].sx, acc[m]);
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) acc[m] += __shfl_xor_sync(0xFFFFFFFFu, acc[m], off, 16);
+      }
+      if (l16 == 0) {
+#pragma unroll
+        for (int m = 0; m < M; ++m) red[(rr * ks + kslice) * M + m] = acc[m];
+      }
+    }
+    // every warp is done with this slot: refill it with stage i + kRing
+    __syncthreads();
+    if (tid == 0 && i + kRing < my_stages) issue(i + kRing);
+    // combine K slices in a fixed order and run the epilogue
+    for (int e = tid; e < nr * M; e += kConsumers) {
+      const int rr = e / M, m = e - rr * M;
+      float v = 0.f;
+      for (int q = 0; q < ks; ++q) v += red[(rr * ks + q) * M + m];
+      const int row = r0 + rr;
+      if (m >= p.m) continue;
+      if (EPI == EPI_STORE) {
+        p.y[static_cast<size_t>(m) * p.ldy + row] = v;
+      } else {
+        if (p.logits) p.logits[static_cast<size_t>(m) * p.n + row] = v;
+        if (v != v) v = -INFINITY;
+        const long long gi = p.row_offset + row;
+#pragma unroll
+        for (int mm = 0; mm < M; ++mm) {
+          if (mm != m) continue;
+          if (v > best_v[mm] || (v == best_v[mm] && gi < best_i[mm])) {
+            best_v[mm] = v;
+            best_i[mm] = gi;
           }
         }
       }
@@ -240,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const GemvParams p
   }
 
   if (EPI == EPI_ARGMAX) {
-    const int warp = tid >> 5, lane = tid & 31;
+    const int lane = tid & 31;
 #pragma unroll
     for (int m = 0; m < M; ++m) {
       unsigned long long key = best_i[m] == 0x7FFFFFFF ? 0ull : make_key(best_v[m], best_i[m]);
@@ -249,12 +320,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const GemvParams p
         const unsigned long long o = __shfl_xor_sync(0xFFFFFFFFu, key, off);
         key = o > key ? o : key;
       }
-      if (lane == 0) best_s[warp][m] = key;
+      if (lane == 0) sm.best[warp][m] = key;
     }
     __syncthreads();
     if (tid < M && tid < p.m) {
       unsigned long long key = 0;
-      for (int wi = 0; wi < kThreads / 32; ++wi) key = best_s[wi][tid] > key ? best_s[wi][tid] : key;
+      for (int wi = 0; wi < kConsumers / 32; ++wi) key = sm.best[wi][tid] > key ? sm.best[wi][tid] : key;
       if (key) atomicMax(p.keys + tid, key);
     }
   }
@@ -266,17 +337,18 @@ __global__ void keys_to_tokens_kernel(const unsigned long long* keys, int32_t* t
 }
 
 struct Plan {
-  int gpl, ks, r;
+  int gpl, ks, rs;
 };
 
-// Pick groups-per-lane and K slices so 16*GPL*ks covers the G groups of a row
-// with the least waste, then rows-per-half-warp R from the row count.
+// Groups-per-lane and K slices so 16*GPL*ks covers a row's G groups with the
+// least waste; then rows per stage: as many as fit 24 KB, but few enough that
+// small matrices still spread over the SMs.
 Plan plan(int mtile, int n, int k, int sms) {
   const int G = k / 32;
   const int max_gpl = mtile == 1 ? 4 : (mtile == 2 ? 2 : 1);
   Plan best{1, 16, 1};
   int best_waste = 1 << 30;
-  const int prefs[4] = {3, 4, 2, 1};
+  const int prefs[4] = {3, 2, 4, 1};
   for (int pi = 0; pi < 4; ++pi) {
     const int gpl = prefs[pi];
     if (gpl > max_gpl) continue;
@@ -290,52 +362,67 @@ Plan plan(int mtile, int n, int k, int sms) {
     }
   }
   const int nrl = 16 / best.ks;
-  const long long tiles4 = (n + nrl * 4 - 1) / (nrl * 4);
-  const long long tiles2 = (n + nrl * 2 - 1) / (nrl * 2);
-  best.r = tiles4 >= 2LL * sms ? 4 : (tiles2 >= sms ? 2 : 1);
-  if (mtile >= 2 && best.r == 4) best.r = 2;
+  const int row_bytes = k / 2;
+  int rs = std::max(1, kStageW / row_bytes);
+  const int spread = (n + sms * kCtasPerSm - 1) / (sms * kCtasPerSm);  // rows per CTA if each gets one stage
+  rs = std::min(rs, std::max(nrl, spread));
+  rs = std::max(nrl, rs / nrl * nrl);
+  while (rs * best.ks * mtile > kRedMax && rs > nrl) rs -= nrl;
+  best.rs = rs;
   return best;
 }
 
-template <int M, int R, int GPL, int EPI>
-int launch_t(const GemvParams& p, bool xf32, bool sf16, int sms, cudaStream_t s) {
-  const int nrl = 16 / p.ks;
-  const long long ntiles = (p.n + nrl * R - 1) / (nrl * R);
-  const int grid = static_cast<int>(std::min<long long>(ntiles, static_cast<long long>(sms) * 2));
+template <int M, int GPL, int EPI>
+int launch_t(const GemvParams& p, bool sf16, int sms, cudaStream_t s) {
+  const int grid = std::min(p.n_stages, sms * kCtasPerSm);
   if (grid == 0) return SB_OK;
-  if (xf32) {
-    if (sf16) gemv_q4_kernel<M, R, GPL, true, true, EPI><<<grid, kThreads, 0, s>>>(p);
-    else gemv_q4_kernel<M, R, GPL, true, false, EPI><<<grid, kThreads, 0, s>>>(p);
-  } else {
-    if (sf16) gemv_q4_kernel<M, R, GPL, false, true, EPI><<<grid, kThreads, 0, s>>>(p);
-    else gemv_q4_kernel<M, R, GPL, false, false, EPI><<<grid, kThreads, 0, s>>>(p);
+  const int smem = static_cast<int>(sizeof(GemvSmem));
+  static bool done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !done[dev]) {
+    // two CTAs per SM need the largest shared-memory carveout
+    cudaError_t e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, true, EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, false, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, true, EPI>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, false, EPI>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return sb::cuda_fail(e, "gemv_q4_kernel: smem attribute");
+    done[dev] = true;
   }
+  cudaError_t e = sf16 ? sb::launch_pdl(gemv_q4_kernel<M, GPL, true, EPI>, dim3(grid), dim3(kThreads), smem, s, p)
+                       : sb::launch_pdl(gemv_q4_kernel<M, GPL, false, EPI>, dim3(grid), dim3(kThreads), smem, s, p);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "gemv_q4_kernel launch");
   return sb::launch_status("gemv_q4_kernel");
 }
 
 template <int M, int EPI>
-int launch_m(const GemvParams& p, const Plan& pl, bool xf32, bool sf16, int sms, cudaStream_t s) {
-  // instantiated combinations: M=1: GPL 1..4 x R {1,2,4}; M=2: GPL {1,2} x R {1,2}; M=4: GPL 1 x R {1,2}
+int launch_m(const GemvParams& p, const Plan& pl, bool sf16, int sms, cudaStream_t s) {
   if constexpr (M == 1) {
-#define SB_GPL_R(G_, R_) \
-  if (pl.gpl == G_ && pl.r == R_) return launch_t<M, R_, G_, EPI>(p, xf32, sf16, sms, s);
-    SB_GPL_R(1, 1) SB_GPL_R(1, 2) SB_GPL_R(1, 4)
-    SB_GPL_R(2, 1) SB_GPL_R(2, 2) SB_GPL_R(2, 4)
-    SB_GPL_R(3, 1) SB_GPL_R(3, 2) SB_GPL_R(3, 4)
-    SB_GPL_R(4, 1) SB_GPL_R(4, 2) SB_GPL_R(4, 4)
+    switch (pl.gpl) {
+      case 1: return launch_t<M, 1, EPI>(p, sf16, sms, s);
+      case 2: return launch_t<M, 2, EPI>(p, sf16, sms, s);
+      case 3: return launch_t<M, 3, EPI>(p, sf16, sms, s);
+      default: return launch_t<M, 4, EPI>(p, sf16, sms, s);
+    }
   } else if constexpr (M == 2) {
-    SB_GPL_R(1, 1) SB_GPL_R(1, 2) SB_GPL_R(2, 1) SB_GPL_R(2, 2)
+    return pl.gpl == 1 ? launch_t<M, 1, EPI>(p, sf16, sms, s) : launch_t<M, 2, EPI>(p, sf16, sms, s);
   } else {
-    SB_GPL_R(1, 1) SB_GPL_R(1, 2)
-#undef SB_GPL_R
+    return launch_t<M, 1, EPI>(p, sf16, sms, s);
   }
-  return sb::fail(SB_ERR_ARG, "gemv: no kernel for M=%d GPL=%d R=%d", M, pl.gpl, pl.r);
 }
 
 int run(GemvParams p, int epi, bool xf32, bool sf16, cudaStream_t s) {
   const int sms = sb::num_sms();
   const int x_elt = xf32 ? 4 : 2;
   const size_t x_row = static_cast<size_t>(p.k) * x_elt;
+  const int esz = sf16 ? 2 : 4;
+  const int gps = p.k / p.group;
+  p.err = sb::device_error_word();
+  p.x_f32 = xf32 ? 1 : 0;
   int done = 0;
   const int m_total = p.m;
   while (done < m_total) {
@@ -351,15 +438,23 @@ int run(GemvParams p, int epi, bool xf32, bool sf16, cudaStream_t s) {
     }
     Plan pl = plan(mt, p.n, p.k, sms);
     q.ks = pl.ks;
+    q.rs = pl.rs;
+    q.n_stages = (p.n + pl.rs - 1) / pl.rs;
+    // scales ride along in the bulk copy when every stage's scale rows start
+    // on a 16-byte boundary, are a multiple of 16 bytes (a short last stage
+    // included) and fit the scale buffer
+    const size_t srow = static_cast<size_t>(gps) * esz;
+    const int last = p.n - (q.n_stages - 1) * pl.rs;
+    q.scale_bulk = (srow * pl.rs) % 16 == 0 && (srow * last) % 16 == 0 &&
+                   srow * pl.rs <= static_cast<size_t>(kStageS) && sb::aligned(p.scales, 16);
     int rc;
     if (epi == EPI_STORE) {
-      rc = mt == 1 ? launch_m<1, EPI_STORE>(q, pl, xf32, sf16, sms, s)
-                   : mt == 2 ? launch_m<2, EPI_STORE>(q, pl, xf32, sf16, sms, s)
-                             : launch_m<4, EPI_STORE>(q, pl, xf32, sf16, sms, s);
+      rc = mt == 1 ? launch_m<1, EPI_STORE>(q, pl, sf16, sms, s)
+                   : mt == 2 ? launch_m<2, EPI_STORE>(q, pl, sf16, sms, s) : launch_m<4, EPI_STORE>(q, pl, sf16, sms, s);
     } else {
-      rc = mt == 1 ? launch_m<1, EPI_ARGMAX>(q, pl, xf32, sf16, sms, s)
-                   : mt == 2 ? launch_m<2, EPI_ARGMAX>(q, pl, xf32, sf16, sms, s)
-                             : launch_m<4, EPI_ARGMAX>(q, pl, xf32, sf16, sms, s);
+      rc = mt == 1 ? launch_m<1, EPI_ARGMAX>(q, pl, sf16, sms, s)
+                   : mt == 2 ? launch_m<2, EPI_ARGMAX>(q, pl, sf16, sms, s)
+                             : launch_m<4, EPI_ARGMAX>(q, pl, sf16, sms, s);
     }
     if (rc != SB_OK) return rc;
     done += mt;
@@ -372,6 +467,7 @@ int check_common(const char* fn, const void* w, const void* scales, int scale_dt
   SB_CHECK_ARG(m >= 1 && m <= 8, "%s: m=%d must be in 1..8", fn, m);
   SB_CHECK_ARG(n >= 0, "%s: negative n", fn);
   SB_CHECK_ARG(k > 0 && k % 32 == 0, "%s: k=%d must be a positive multiple of 32", fn, k);
+  SB_CHECK_ARG(k / 2 <= kStageW, "%s: k=%d is longer than one stage (max %d)", fn, k, 2 * kStageW);
   SB_CHECK_ARG(group > 0 && k % group == 0 && group % 32 == 0, "%s: group=%d must be a multiple of 32 dividing k",
                fn, group);
   SB_CHECK_ARG(scale_dtype == SB_SCALE_F16 || scale_dtype == SB_SCALE_F32, "%s: bad scale dtype", fn);

@@ -124,6 +124,15 @@ int sb_gemm_f16(const void* a, const void* b, void* c, int m, int n, int k, floa
                 int tr, int lda, int ldb, int ldc, void* stream);
 
 /*
+ * Same product with C written as f32 (alpha applied, no f16 rounding); used
+ * for the prefill attention scores QK^T so the softmax sees f32 logits.
+ * Replaces the score GEMM of PrefillGPU._attn_gemm (gemma4_150/prefill_gpu.py:
+ * 304-305).  C 4-byte aligned, row stride ldc in elements.
+ */
+int sb_gemm_f16_f32out(const void* a, const void* b, float* c, int m, int n, int k, float alpha,
+                       int tr, int lda, int ldb, int ldc, void* stream);
+
+/*
  * Fused prefill projection: dequantise packed int4 tiles into shared memory
  * and feed them to tcgen05 MMAs, f32 accumulate in tensor memory:
  *   C[M, N] = f16(alpha * A[M, K] @ dq_f16(W)[N, K]^T)
@@ -161,6 +170,64 @@ size_t sb_gemm_q4_workspace_size(int m, int n, int k);
  */
 int sb_gemm_q4_noalloc(const void* a, const void* w, const void* scales, int scale_dtype, int group,
                        void* c, int m, int n, int k, float alpha, int lda, int ldc, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Decoder glue around the matmuls (the Gemma-4-E2B-shaped model: hidden H,
+ * nh query heads and one KV head of head_dim, GEGLU FFN).  Activations of the
+ * decode path are f32, those of the prefill GEMMs f16; KV caches are f32
+ * [m][max_seq][head_dim] per layer (cache_stride = max_seq * head_dim) with
+ * optional f16 copies for the prefill attention GEMMs.  RMSNorm is
+ * x / sqrt(mean(x^2) + eps) * w (gemma4/reference.py:19-33).
+ * ------------------------------------------------------------------------- */
+
+/* out[r, :] = dequant(emb[tokens[r]]) * mult  (f32 and/or f16).
+ * Replaces embed_00 (gemma4_150/kernels_dsl.py:433) / gemma4/reference.py:169. */
+int sb_embed_q4(const void* emb, const void* scales, int scale_dtype, int group,
+                const int32_t* tokens, int m, int k, float mult, float* out32, void* out16,
+                void* stream);
+
+/* x_out = x + rmsnorm(y) * w_add (y may be NULL: x_out = x); h = rmsnorm(x_out) * w_norm.
+ * Replaces rmsadd_b + rmssrqh_b / rmssrq_69 (gemma4_150/kernels_dsl.py:622, 660, 158)
+ * and the sandwich norms of gemma4/reference.py:112, 142-152.  n <= 8192. */
+int sb_add_rmsnorm(const float* x, const void* y, int y_dtype, const float* w_add,
+                   const float* w_norm, float* x_out, float* h_out, void* h16_out, int m, int n,
+                   float eps, void* stream);
+
+/* Per token (prefill, positions start_pos + s) or per sequence (decode,
+ * positions pos_dev[s]): q heads -> rmsnorm * q_norm -> RoPE -> q16/q32
+ * [s][nh][hd]; k -> rmsnorm * k_norm -> RoPE -> k_cache (+ k16); v ->
+ * parameter-free rmsnorm -> v_cache (+ v16).  cos/sin: [max_seq][hd/2].
+ * Replaces kvnorm_b + qprep_b (gemma4_150/kernels_dsl.py:1790, 1838) /
+ * gemma4/reference.py:114-125. */
+int sb_qkv_prep(const void* qkv, int qkv_dtype, int ld, const float* q_norm, const float* k_norm,
+                const float* cos_t, const float* sin_t, const int32_t* pos_dev, int start_pos, int s,
+                int n_heads, int head_dim, float eps, void* q16, float* q32, float* k_cache,
+                float* v_cache, void* k16, void* v16, int64_t cache_stride, void* stream);
+
+/* Causal softmax over f32 score rows (row r = token r / n_heads): p16 =
+ * f16(exp(s - max) / sum) for keys <= start_pos + r / n_heads, 0 after.
+ * Replaces smax_b + attnout_b (gemma4_150/kernels_dsl.py:1877, 1753). */
+int sb_softmax_causal(const float* scores, int ld_s, int rows, int n_heads, int start_pos,
+                      int n_keys, void* p16, int ld_p, void* stream);
+
+/* out[r, i] = gelu_tanh(gu[r, i]) * gu[r, f + i] (gate rows then up rows).
+ * Replaces geglu_b (gemma4_150/kernels_dsl.py:259) / gemma4/reference.py:148-150. */
+int sb_geglu(const void* gu, int dtype, int m, int f, float* out32, void* out16, void* stream);
+
+/* Split-KV decode attention, one KV head shared by n_heads query heads:
+ * out[b, h*hd:(h+1)*hd] = softmax(q[b,h] . K[b, 0..pos]) V[b, 0..pos].
+ * Replaces attn_101 (gemma4_150/kernels_dsl.py:1540) / gemma4/reference.py:127-139.
+ * workspace >= sb_attn_decode_workspace_size(m, n_heads, head_dim, max_seq) bytes. */
+int sb_attn_decode(const float* q32, const float* k_cache, const float* v_cache,
+                   int64_t cache_stride, const int32_t* pos_dev, int m, int n_heads, int head_dim,
+                   int max_seq, float* out, float* workspace, size_t workspace_bytes, void* stream);
+size_t sb_attn_decode_workspace_size(int m, int n_heads, int head_dim, int max_seq);
+
+/* Device-side step bookkeeping so a decode step replays as one graph:
+ * pos[b] += 1; cur[b] = tokens[b]; history[b * hist_len + pos[b]] = tokens[b].
+ * Replaces the blit of the argmax token into gen[step] (gemma4_150/metal_runner.py:394-398). */
+int sb_step_advance(int32_t* pos, const int32_t* tokens, int32_t* cur, int32_t* history,
+                    int hist_len, int m, void* stream);
 
 #ifdef __cplusplus
 }

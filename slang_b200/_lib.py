@@ -30,6 +30,16 @@ SIGNATURES = {
     "sb_gemm_q4": ([_vp, _vp, _vp, _i, _i, _vp, _i, _i, _i, _f, _i, _i, _vp, _sz, _vp], _i),
     "sb_gemm_q4_workspace_size": ([_i, _i, _i], _sz),
     "sb_gemm_q4_noalloc": ([_vp, _vp, _vp, _i, _i, _vp, _i, _i, _i, _f, _i, _i, _vp], _i),
+    "sb_gemm_f16_f32out": ([_vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _i, _i, _vp], _i),
+    "sb_embed_q4": ([_vp, _vp, _i, _i, _vp, _i, _i, _f, _vp, _vp, _vp], _i),
+    "sb_add_rmsnorm": ([_vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _f, _vp], _i),
+    "sb_qkv_prep": ([_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _vp, _vp,
+                     _i64, _vp], _i),
+    "sb_softmax_causal": ([_vp, _i, _i, _i, _i, _i, _vp, _i, _vp], _i),
+    "sb_geglu": ([_vp, _i, _i, _i, _vp, _vp, _vp], _i),
+    "sb_attn_decode": ([_vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _vp, _vp, _sz, _vp], _i),
+    "sb_attn_decode_workspace_size": ([_i, _i, _i, _i], _sz),
+    "sb_step_advance": ([_vp, _vp, _vp, _vp, _i, _i, _vp], _i),
 }
 
 

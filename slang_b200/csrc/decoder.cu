@@ -1,0 +1,432 @@
+// Glue of the Gemma-4-E2B-shaped decoder around the quantized matmuls:
+// embedding gather, residual add + RMSNorm, q/k/v norm + RoPE + KV-cache
+// store, causal softmax (prefill), GEGLU, split-KV decode attention, and the
+// per-step position/token bookkeeping that lets a whole decode step replay as
+// one CUDA graph.  Arithmetic follows the reference's f32 numpy decoder
+// (gemma4/reference.py:19-56, 103-152): RMSNorm is x / sqrt(mean(x^2) + eps) * w,
+// RoPE is rotate_half on precomputed cos/sin tables, attention scaling is 1.0.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int kT = 256;  // threads per CTA for the row kernels
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+
+// sum over a CTA of kT threads (red: >= 32 floats of shared memory)
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < (blockDim.x >> 5) ? red[lane] : 0.f;
+  return warp_sum(t);
+}
+
+__device__ __forceinline__ float load_act(const void* p, int is_f16, size_t i) {
+  return is_f16 ? __half2float(static_cast<const __half*>(p)[i]) : static_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+}
+
+// ---------------------------------------------------------------- embedding
+__global__ void embed_kernel(const uint8_t* __restrict__ emb, const void* __restrict__ scales, int sf16, int group,
+                             const int32_t* __restrict__ tokens, int k, float mult, float* out32, __half* out16) {
+  const int row = blockIdx.x;
+  const int64_t tok = tokens[row];
+  const int gps = k / group;
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const uint8_t b = emb[tok * (k / 2) + i / 2];
+    const int q = ((i & 1) ? (b >> 4) : (b & 15)) - 8;
+    const size_t si = static_cast<size_t>(tok) * gps + i / group;
+    const float s = sf16 ? __half2float(static_cast<const __half*>(scales)[si]) : static_cast<const float*>(scales)[si];
+    // reference: (ints * repeat(scale)) * embed_scale, each product rounded in f32
+    const float v = __fmul_rn(__fmul_rn(static_cast<float>(q), s), mult);
+    if (out32) out32[static_cast<size_t>(row) * k + i] = v;
+    if (out16) out16[static_cast<size_t>(row) * k + i] = __float2half_rn(v);
+  }
+}
+
+// ---------------------------------------------------------------- add + RMSNorm
+// x_out = x + rmsnorm(y) * w_add   (when y != null; else x_out = x)
+// h     = rmsnorm(x_out) * w_norm  -> h_out (f32) and/or h16 (f16)
+__global__ void add_rmsnorm_kernel(const float* __restrict__ x, const void* __restrict__ y, int y_f16,
+                                   const float* __restrict__ w_add, const float* __restrict__ w_norm, float* x_out,
+                                   float* h_out, __half* h16, int n, float eps) {
+  __shared__ float red[32];
+  constexpr int MAXV = 32;  // n <= 32 * kT
+  const int row = blockIdx.x;
+  const size_t base = static_cast<size_t>(row) * n;
+  float v[MAXV];
+  float ss = 0.f;
+  if (y) {
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) {
+      const int i = threadIdx.x + j * kT;
+      v[j] = i < n ? load_act(y, y_f16, base + i) : 0.f;
+      ss += v[j] * v[j];
+    }
+    const float d = sqrtf(block_sum(ss, red) / n + eps);
+    ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) {
+      const int i = threadIdx.x + j * kT;
+      if (i < n) {
+        v[j] = x[base + i] + v[j] / d * w_add[i];
+        if (x_out) x_out[base + i] = v[j];
+      }
+      ss += v[j] * v[j];
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) {
+      const int i = threadIdx.x + j * kT;
+      v[j] = i < n ? x[base + i] : 0.f;
+      if (i < n && x_out && x_out != x) x_out[base + i] = v[j];
+      ss += v[j] * v[j];
+    }
+  }
+  const float d = sqrtf(block_sum(ss, red) / n + eps);
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) {
+    const int i = threadIdx.x + j * kT;
+    if (i < n) {
+      const float h = v[j] / d * w_norm[i];
+      if (h_out) h_out[base + i] = h;
+      if (h16) h16[base + i] = __float2half_rn(h);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- q/k/v prep
+// One CTA per token (nh + 2 warps): warp h < nh normalises + ropes query head h,
+// warp nh the key (written to the f32 cache and its f16 copy), warp nh+1 the
+// value (parameter-free RMSNorm).  hd = 32 * VPL.
+template <int VPL>
+__global__ void qkv_prep_kernel(const void* __restrict__ qkv, int qkv_f16, int ld, const float* __restrict__ q_norm,
+                                const float* __restrict__ k_norm, const float* __restrict__ cos_t,
+                                const float* __restrict__ sin_t, const int32_t* __restrict__ pos_dev, int start_pos,
+                                int nh, float eps, __half* q16, float* q32, float* k_cache, float* v_cache,
+                                __half* k16, __half* v16, int64_t cache_stride) {
+  constexpr int HD = 32 * VPL, HALF = HD / 2;
+  const int s = blockIdx.x;  // token (prefill) or sequence (decode)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos = pos_dev ? pos_dev[s] : start_pos + s;
+  const size_t row = static_cast<size_t>(s) * ld;
+  int col0;
+  if (warp < nh) col0 = warp * HD;
+  else if (warp == nh) col0 = nh * HD;
+  else col0 = (nh + 1) * HD;
+  float v[VPL];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    v[j] = load_act(qkv, qkv_f16, row + col0 + lane + 32 * j);
+    ss += v[j] * v[j];
+  }
+  const float d = sqrtf(warp_sum(ss) / HD + eps);
+  const float* w = warp < nh ? q_norm : k_norm;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) v[j] = warp <= nh ? v[j] / d * w[lane + 32 * j] : v[j] / d;
+  if (warp <= nh) {
+    // rotate_half: dims i and i + HALF pair up; lane holds j and j + VPL/2
+    const float* c = cos_t + static_cast<size_t>(pos) * HALF;
+    const float* sn = sin_t + static_cast<size_t>(pos) * HALF;
+#pragma unroll
+    for (int j = 0; j < VPL / 2; ++j) {
+      const int i = lane + 32 * j;
+      const float a = v[j], b = v[j + VPL / 2];
+      v[j] = a * c[i] - b * sn[i];
+      v[j + VPL / 2] = b * c[i] + a * sn[i];
+    }
+  }
+  if (warp < nh) {
+    const size_t qb = (static_cast<size_t>(s) * nh + warp) * HD;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      if (q16) q16[qb + lane + 32 * j] = __float2half_rn(v[j]);
+      if (q32) q32[qb + lane + 32 * j] = v[j];
+    }
+  } else {
+    const int seq = pos_dev ? s : 0;
+    const size_t cb = static_cast<size_t>(seq) * cache_stride + static_cast<size_t>(pos) * HD;
+    float* cache = warp == nh ? k_cache : v_cache;
+    __half* c16 = warp == nh ? k16 : v16;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      cache[cb + lane + 32 * j] = v[j];
+      if (c16) c16[cb + lane + 32 * j] = __float2half_rn(v[j]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- causal softmax
+// Row r is query token s = r / nh (absolute position start + s); keys t <= that
+// position get f16(exp(score - max) / sum), later keys (up to n_keys) get 0.
+__global__ void softmax_causal_kernel(const float* __restrict__ scores, int ld_s, int nh, int start_pos, int n_keys,
+                                      __half* p16, int ld_p) {
+  __shared__ float red[32];
+  const int r = blockIdx.x;
+  const int last = start_pos + r / nh;  // inclusive
+  const float* srow = scores + static_cast<size_t>(r) * ld_s;
+  float m = -INFINITY;
+  for (int t = threadIdx.x; t <= last; t += blockDim.x) m = fmaxf(m, srow[t]);
+  m = warp_max(m);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = (threadIdx.x & 31) < (blockDim.x >> 5) ? red[threadIdx.x & 31] : -INFINITY;
+  m = warp_max(m);
+  float l = 0.f;
+  for (int t = threadIdx.x; t <= last; t += blockDim.x) l += expf(srow[t] - m);
+  l = block_sum(l, red);
+  __half* prow = p16 + static_cast<size_t>(r) * ld_p;
+  for (int t = threadIdx.x; t < n_keys; t += blockDim.x)
+    prow[t] = t <= last ? __float2half_rn(expf(srow[t] - m) / l) : __float2half_rn(0.f);
+}
+
+// ---------------------------------------------------------------- GEGLU
+// out[r, i] = gelu_tanh(gu[r, i]) * gu[r, f + i]
+__global__ void geglu_kernel(const void* __restrict__ gu, int gu_f16, int f, int rows, float* out32, __half* out16) {
+  const size_t total = static_cast<size_t>(rows) * f;
+  for (size_t e = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t r = e / f, i = e - r * f;
+    const float g = load_act(gu, gu_f16, r * 2 * f + i);
+    const float u = load_act(gu, gu_f16, r * 2 * f + f + i);
+    const float v = gelu_tanh(g) * u;
+    if (out32) out32[e] = v;
+    if (out16) out16[e] = __float2half_rn(v);
+  }
+}
+
+// ---------------------------------------------------------------- decode attention
+// Split-KV decode attention for one KV head shared by nh query heads.
+// Partial: CTA (b, chunk) scores CK keys for all heads, keeps per-head max and
+// sum and the unnormalised P.V; merge rescales the chunks (flash-decoding).
+constexpr int CK = 64;
+
+template <int VPL>
+__global__ void attn_decode_partial_kernel(const float* __restrict__ q32, const float* __restrict__ k_cache,
+                                           const float* __restrict__ v_cache, const int32_t* __restrict__ pos_dev,
+                                           int nh, int64_t cache_stride, float* part, int max_chunks) {
+  constexpr int HD = 32 * VPL;
+  extern __shared__ float sm[];
+  float* qs = sm;                 // [nh][HD]
+  float* sc = sm + nh * HD;       // [nh][CK]
+  const int b = blockIdx.x, c = blockIdx.y;
+  const int T = pos_dev[b] + 1;
+  const int t0 = c * CK;
+  if (t0 >= T) return;
+  const int nt = min(CK, T - t0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int i = threadIdx.x; i < nh * HD; i += blockDim.x) qs[i] = q32[static_cast<size_t>(b) * nh * HD + i];
+  __syncthreads();
+  const float* kb = k_cache + static_cast<size_t>(b) * cache_stride;
+  const float* vb = v_cache + static_cast<size_t>(b) * cache_stride;
+  // scores: warp per key, all heads
+  for (int t = warp; t < nt; t += nw) {
+    float kv[VPL];
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) kv[j] = kb[static_cast<size_t>(t0 + t) * HD + lane + 32 * j];
+    for (int h = 0; h < nh; ++h) {
+      float d = 0.f;
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) d += qs[h * HD + lane + 32 * j] * kv[j];
+      d = warp_sum(d);
+      if (lane == 0) sc[h * CK + t] = d;
+    }
+  }
+  __syncthreads();
+  // per-head max / exp / sum over this chunk
+  for (int h = warp; h < nh; h += nw) {
+    float m = -INFINITY;
+    for (int t = lane; t < nt; t += 32) m = fmaxf(m, sc[h * CK + t]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int t = lane; t < nt; t += 32) {
+      const float p = expf(sc[h * CK + t] - m);
+      sc[h * CK + t] = p;
+      l += p;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      float* pm = part + ((static_cast<size_t>(b) * max_chunks + c) * nh + h) * (HD + 2);
+      pm[HD] = m;
+      pm[HD + 1] = l;
+    }
+  }
+  __syncthreads();
+  // P.V: thread per dimension, all heads
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+    float acc[16];
+#pragma unroll
+    for (int h = 0; h < 16; ++h) acc[h] = 0.f;
+    for (int t = 0; t < nt; ++t) {
+      const float vv = vb[static_cast<size_t>(t0 + t) * HD + d];
+#pragma unroll
+      for (int h = 0; h < 16; ++h)
+        if (h < nh) acc[h] += sc[h * CK + t] * vv;
+    }
+#pragma unroll
+    for (int h = 0; h < 16; ++h)
+      if (h < nh) part[((static_cast<size_t>(b) * max_chunks + c) * nh + h) * (HD + 2) + d] = acc[h];
+  }
+}
+
+__global__ void attn_decode_merge_kernel(const float* __restrict__ part, const int32_t* __restrict__ pos_dev, int nh,
+                                         int hd, int max_chunks, float* out) {
+  const int b = blockIdx.x;
+  const int nc = (pos_dev[b] + 1 + CK - 1) / CK;
+  for (int e = threadIdx.x; e < nh * hd; e += blockDim.x) {
+    const int h = e / hd, d = e - h * hd;
+    float M = -INFINITY;
+    for (int c = 0; c < nc; ++c) M = fmaxf(M, part[((static_cast<size_t>(b) * max_chunks + c) * nh + h) * (hd + 2) + hd]);
+    float L = 0.f, O = 0.f;
+    for (int c = 0; c < nc; ++c) {
+      const float* pm = part + ((static_cast<size_t>(b) * max_chunks + c) * nh + h) * (hd + 2);
+      const float f = expf(pm[hd] - M);
+      L += pm[hd + 1] * f;
+      O += pm[d] * f;
+    }
+    out[static_cast<size_t>(b) * nh * hd + e] = O / L;
+  }
+}
+
+// ---------------------------------------------------------------- step bookkeeping
+__global__ void step_advance_kernel(int32_t* pos, const int32_t* tokens, int32_t* cur, int32_t* history, int hist_len,
+                                    int m) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= m) return;
+  const int p = pos[b] + 1;
+  pos[b] = p;
+  cur[b] = tokens[b];
+  if (history && p < hist_len) history[static_cast<size_t>(b) * hist_len + p] = tokens[b];
+}
+
+int grid_for(size_t n, int per) { return static_cast<int>(std::min<size_t>((n + per - 1) / per, 148 * 32)); }
+
+}  // namespace
+
+extern "C" int sb_embed_q4(const void* emb, const void* scales, int scale_dtype, int group, const int32_t* tokens,
+                           int m, int k, float mult, float* out32, void* out16, void* stream) {
+  SB_CHECK_ARG(m >= 0 && k > 0 && k % 2 == 0 && group > 0 && k % group == 0, "sb_embed_q4: bad shape");
+  SB_CHECK_ARG(scale_dtype == SB_SCALE_F16 || scale_dtype == SB_SCALE_F32, "sb_embed_q4: bad scale dtype");
+  if (m == 0) return SB_OK;
+  SB_CHECK_ARG(emb && scales && tokens && (out32 || out16), "sb_embed_q4: null pointer");
+  embed_kernel<<<m, kT, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t*>(emb), scales,
+                                                                scale_dtype == SB_SCALE_F16, group, tokens, k, mult,
+                                                                out32, static_cast<__half*>(out16));
+  return sb::launch_status("embed_kernel");
+}
+
+extern "C" int sb_add_rmsnorm(const float* x, const void* y, int y_dtype, const float* w_add, const float* w_norm,
+                              float* x_out, float* h_out, void* h16_out, int m, int n, float eps, void* stream) {
+  SB_CHECK_ARG(m >= 0 && n > 0 && n <= 32 * kT, "sb_add_rmsnorm: n=%d must be in 1..%d", n, 32 * kT);
+  SB_CHECK_ARG(!y || y_dtype == SB_F16 || y_dtype == SB_F32, "sb_add_rmsnorm: bad y dtype");
+  if (m == 0) return SB_OK;
+  SB_CHECK_ARG(x && w_norm && (!y || w_add) && (h_out || h16_out), "sb_add_rmsnorm: null pointer");
+  add_rmsnorm_kernel<<<m, kT, 0, static_cast<cudaStream_t>(stream)>>>(x, y, y_dtype == SB_F16, w_add, w_norm, x_out,
+                                                                      h_out, static_cast<__half*>(h16_out), n, eps);
+  return sb::launch_status("add_rmsnorm_kernel");
+}
+
+extern "C" int sb_qkv_prep(const void* qkv, int qkv_dtype, int ld, const float* q_norm, const float* k_norm,
+                           const float* cos_t, const float* sin_t, const int32_t* pos_dev, int start_pos, int s,
+                           int n_heads, int head_dim, float eps, void* q16, float* q32, float* k_cache,
+                           float* v_cache, void* k16, void* v16, int64_t cache_stride, void* stream) {
+  SB_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256, "sb_qkv_prep: head_dim %d unsupported", head_dim);
+  SB_CHECK_ARG(n_heads >= 1 && n_heads <= 30 && s >= 0 && ld >= (n_heads + 2) * head_dim, "sb_qkv_prep: bad shape");
+  SB_CHECK_ARG(qkv_dtype == SB_F16 || qkv_dtype == SB_F32, "sb_qkv_prep: bad dtype");
+  if (s == 0) return SB_OK;
+  SB_CHECK_ARG(qkv && q_norm && k_norm && cos_t && sin_t && k_cache && v_cache && (q16 || q32), "sb_qkv_prep: null");
+  const dim3 block(32 * (n_heads + 2));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int f16 = qkv_dtype == SB_F16;
+#define SB_PREP(V)                                                                                                   \
+  qkv_prep_kernel<V><<<s, block, 0, st>>>(qkv, f16, ld, q_norm, k_norm, cos_t, sin_t, pos_dev, start_pos, n_heads, eps, \
+                                          static_cast<__half*>(q16), q32, k_cache, v_cache, static_cast<__half*>(k16), \
+                                          static_cast<__half*>(v16), cache_stride)
+  if (head_dim == 64) SB_PREP(2);
+  else if (head_dim == 128) SB_PREP(4);
+  else SB_PREP(8);
+#undef SB_PREP
+  return sb::launch_status("qkv_prep_kernel");
+}
+
+extern "C" int sb_softmax_causal(const float* scores, int ld_s, int rows, int n_heads, int start_pos, int n_keys,
+                                 void* p16, int ld_p, void* stream) {
+  SB_CHECK_ARG(rows >= 0 && n_heads > 0 && n_keys >= 0 && ld_s >= n_keys && ld_p >= n_keys, "sb_softmax_causal: bad shape");
+  SB_CHECK_ARG(start_pos + (rows - 1) / n_heads < n_keys || rows == 0, "sb_softmax_causal: a query sees past n_keys");
+  if (rows == 0) return SB_OK;
+  SB_CHECK_ARG(scores && p16, "sb_softmax_causal: null pointer");
+  softmax_causal_kernel<<<rows, kT, 0, static_cast<cudaStream_t>(stream)>>>(scores, ld_s, n_heads, start_pos, n_keys,
+                                                                            static_cast<__half*>(p16), ld_p);
+  return sb::launch_status("softmax_causal_kernel");
+}
+
+extern "C" int sb_geglu(const void* gu, int dtype, int m, int f, float* out32, void* out16, void* stream) {
+  SB_CHECK_ARG(m >= 0 && f > 0 && (dtype == SB_F16 || dtype == SB_F32), "sb_geglu: bad arguments");
+  if (m == 0) return SB_OK;
+  SB_CHECK_ARG(gu && (out32 || out16), "sb_geglu: null pointer");
+  const size_t total = static_cast<size_t>(m) * f;
+  geglu_kernel<<<grid_for(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(gu, dtype == SB_F16, f, m, out32,
+                                                                                   static_cast<__half*>(out16));
+  return sb::launch_status("geglu_kernel");
+}
+
+extern "C" size_t sb_attn_decode_workspace_size(int m, int n_heads, int head_dim, int max_seq) {
+  if (m <= 0 || n_heads <= 0 || head_dim <= 0 || max_seq <= 0) return 0;
+  const size_t chunks = (static_cast<size_t>(max_seq) + CK - 1) / CK;
+  return static_cast<size_t>(m) * chunks * n_heads * (head_dim + 2) * sizeof(float);
+}
+
+extern "C" int sb_attn_decode(const float* q32, const float* k_cache, const float* v_cache, int64_t cache_stride,
+                              const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, float* out,
+                              float* workspace, size_t workspace_bytes, void* stream) {
+  SB_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256, "sb_attn_decode: head_dim %d unsupported", head_dim);
+  SB_CHECK_ARG(n_heads >= 1 && n_heads <= 16 && m >= 0 && max_seq > 0, "sb_attn_decode: bad shape");
+  if (m == 0) return SB_OK;
+  SB_CHECK_ARG(q32 && k_cache && v_cache && pos_dev && out && workspace, "sb_attn_decode: null pointer");
+  const size_t need = sb_attn_decode_workspace_size(m, n_heads, head_dim, max_seq);
+  if (workspace_bytes < need)
+    return sb::fail(SB_ERR_WORKSPACE, "sb_attn_decode: workspace %zu < %zu bytes", workspace_bytes, need);
+  const int max_chunks = (max_seq + CK - 1) / CK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t smem = static_cast<size_t>(n_heads) * (head_dim + CK) * sizeof(float);
+  const dim3 grid(m, max_chunks);
+#define SB_ATT(V) \
+  attn_decode_partial_kernel<V><<<grid, kT, smem, st>>>(q32, k_cache, v_cache, pos_dev, n_heads, cache_stride, workspace, max_chunks)
+  if (head_dim == 64) SB_ATT(2);
+  else if (head_dim == 128) SB_ATT(4);
+  else SB_ATT(8);
+#undef SB_ATT
+  int rc = sb::launch_status("attn_decode_partial_kernel");
+  if (rc) return rc;
+  attn_decode_merge_kernel<<<m, kT, 0, st>>>(workspace, pos_dev, n_heads, head_dim, max_chunks, out);
+  return sb::launch_status("attn_decode_merge_kernel");
+}
+
+extern "C" int sb_step_advance(int32_t* pos, const int32_t* tokens, int32_t* cur, int32_t* history, int hist_len, int m,
+                               void* stream) {
+  SB_CHECK_ARG(m >= 0, "sb_step_advance: bad m");
+  if (m == 0) return SB_OK;
+  SB_CHECK_ARG(pos && tokens && cur, "sb_step_advance: null pointer");
+  step_advance_kernel<<<(m + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(pos, tokens, cur, history,
+                                                                                     hist_len, m);
+  return sb::launch_status("step_advance_kernel");
+}

@@ -78,6 +78,7 @@ struct Cfg {
 struct GemmParams {
   const void* scales;  // int4 mode
   void* c;
+  int c_f32;           // f16 kernel: C is f32 (alpha applied, no rounding to f16)
   float* ws;           // split-K partials [splits][m][n] or null
   int* err;
   int m, n, k, ldc, group, scale_f16;
@@ -241,6 +242,13 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
         sbd::tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + cc * 32, r);
         sbd::tmem_wait_ld();
         if (!row_ok) continue;
+        if (p.c_f32) {
+          float* dst = static_cast<float*>(p.c) + static_cast<size_t>(row) * p.ldc + col0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < p.n) dst[j] = p.alpha * __uint_as_float(r[j]);
+          continue;
+        }
         __half* dst = static_cast<__half*>(p.c) + static_cast<size_t>(row) * p.ldc + col0;
         if (col0 + 32 <= p.n && (p.ldc % 8) == 0) {
 #pragma unroll
@@ -554,8 +562,8 @@ extern "C" size_t sb_gemm_q4_workspace_size(int m, int n, int k) {
   return q4_workspace(m, n, k, 32, 2);
 }
 
-extern "C" int sb_gemm_f16(const void* a, const void* b, void* c, int m, int n, int k, float alpha, int tr, int lda,
-                           int ldb, int ldc, void* stream) {
+static int gemm_f16_impl(const void* a, const void* b, void* c, int c_f32, int m, int n, int k, float alpha, int tr,
+                         int lda, int ldb, int ldc, void* stream) {
   SB_CHECK_ARG(m >= 0 && n >= 0 && k >= 0, "sb_gemm_f16: negative shape");
   if (m == 0 || n == 0) return SB_OK;
   SB_CHECK_ARG(a && b && c, "sb_gemm_f16: null pointer");
@@ -565,8 +573,9 @@ extern "C" int sb_gemm_f16(const void* a, const void* b, void* c, int m, int n, 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (k == 0) {
     // C = 0 (an empty sum)
+    const size_t esz = c_f32 ? 4 : 2;
     for (int r = 0; r < m; ++r) {
-      cudaError_t e = cudaMemsetAsync(static_cast<__half*>(c) + static_cast<size_t>(r) * ldc, 0, n * 2, s);
+      cudaError_t e = cudaMemsetAsync(static_cast<char*>(c) + static_cast<size_t>(r) * ldc * esz, 0, n * esz, s);
       if (e != cudaSuccess) return sb::cuda_fail(e, "sb_gemm_f16: zero fill");
     }
     return SB_OK;
@@ -579,6 +588,7 @@ extern "C" int sb_gemm_f16(const void* a, const void* b, void* c, int m, int n, 
   if (rc) return rc;
   GemmParams p{};
   p.c = c;
+  p.c_f32 = c_f32;
   p.err = sb::device_error_word();
   p.m = m;
   p.n = n;
@@ -588,6 +598,17 @@ extern "C" int sb_gemm_f16(const void* a, const void* b, void* c, int m, int n, 
   p.kb_total = (k + BK - 1) / BK;
   p.kb_per_split = p.kb_total;
   return tr ? launch<MODE_F16_KMAJOR>(ta, tb, p, s) : launch<MODE_F16_MNMAJOR>(ta, tb, p, s);
+}
+
+extern "C" int sb_gemm_f16(const void* a, const void* b, void* c, int m, int n, int k, float alpha, int tr, int lda,
+                           int ldb, int ldc, void* stream) {
+  return gemm_f16_impl(a, b, c, 0, m, n, k, alpha, tr, lda, ldb, ldc, stream);
+}
+
+extern "C" int sb_gemm_f16_f32out(const void* a, const void* b, float* c, int m, int n, int k, float alpha, int tr,
+                                  int lda, int ldb, int ldc, void* stream) {
+  if (c && !sb::aligned(c, 4)) return sb::fail(SB_ERR_ALIGN, "sb_gemm_f16_f32out: C must be 4-byte aligned");
+  return gemm_f16_impl(a, b, c, 1, m, n, k, alpha, tr, lda, ldb, ldc, stream);
 }
 
 extern "C" int sb_gemm_q4(const void* a, const void* w, const void* scales, int scale_dtype, int group, void* c, int m,

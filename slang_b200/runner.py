@@ -1,0 +1,301 @@
+"""Decode runner and layers-outer prefill for the Gemma-4-E2B-shaped int4 decoder.
+
+Host orchestration mirroring the reference's runners:
+  * ``Runner.decode_step`` is ``G4._forward`` (gemma4_150/metal_runner.py:372-402):
+    embed -> per layer {norm, q|k|v GEMV, q/k norm + RoPE + cache, attention,
+    o GEMV, add+norm, gate|up GEMV, GEGLU, down GEMV, add+norm} -> lm_head
+    argmax, for ``batch`` independent sequences; the whole step is captured
+    once as a CUDA graph and replayed per token, with positions, current
+    tokens and the generated history kept on the device
+    (gemma4_150/metal_runner.py:439-468 keeps ``gen`` on the GPU the same way).
+  * ``Runner.prefill`` is ``PrefillGPU.prefill`` (gemma4_150/prefill_gpu.py:398-436):
+    layers outer, tokens inner; every projection is one fused int4 tcgen05
+    GEMM at M = prompt length, attention is QK^T (f32 scores) -> causal
+    softmax -> PV on the tcgen05 f16 GEMM; it returns the first greedy token.
+  * ``Runner.prefill_tokenwise`` feeds the prompt through the decode step one
+    token at a time (the reference's per-token path, used when batched prefill
+    is off, gemma4_150/metal_runner.py:418-425): f32 activations throughout.
+
+q|k|v and gate|up weights are concatenated at load time so each pair/triple is
+one launch (the reference's qkv_70 / gateup_74 fuse the same way).  Every
+kernel is a ``libslang_b200.so`` entry point; torch only allocates memory and
+provides streams and graphs.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+from . import _lib
+from . import kernels as kern
+
+_F16, _F32 = _lib.SB_F16, _lib.SB_F32
+
+
+def rope_tables(max_pos: int, head_dim: int, theta: float, cutoff: int) -> tuple[np.ndarray, np.ndarray]:
+    """cos/sin [max_pos, head_dim/2] in f32, formed as gemma4/reference.py:44-50 does."""
+    half = head_dim // 2
+    i = np.arange(half, dtype=np.float32)
+    inv_freq = 1.0 / theta ** (2.0 * i / head_dim)
+    inv_freq[cutoff:] = 0.0
+    ang = np.arange(max_pos, dtype=np.float32)[:, None] * inv_freq[None, :]
+    return np.cos(ang, dtype=np.float32), np.sin(ang, dtype=np.float32)
+
+
+class DeviceModel:
+    """The model's weights on one GPU in the layouts the kernels consume."""
+
+    def __init__(self, model: dict, device, max_seq: int):
+        cfg = model["config"]
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.max_seq = max_seq
+        dev = self.device
+
+        def T(a, dtype=None):
+            t = torch.from_numpy(np.ascontiguousarray(a))
+            return t.to(device=dev, dtype=dtype) if dtype is not None else t.to(dev)
+
+        self.embed_q = T(model["embed_q"])
+        self.embed_s = T(model["embed_scale"])
+        self.final_norm = T(model["final_norm"], torch.float32)
+        self.layers = []
+        for L in model["layers"]:
+            d = {
+                "qkv": (T(np.concatenate([L["q"][0], L["k"][0], L["v"][0]])),
+                        T(np.concatenate([L["q"][1], L["k"][1], L["v"][1]]))),
+                "o": (T(L["o"][0]), T(L["o"][1])),
+                "gu": (T(np.concatenate([L["gate"][0], L["up"][0]])), T(np.concatenate([L["gate"][1], L["up"][1]]))),
+                "down": (T(L["down"][0]), T(L["down"][1])),
+            }
+            for n in ("in_norm", "q_norm", "k_norm", "post_attn_norm", "pre_ffn_norm", "post_ffn_norm"):
+                d[n] = T(L[n], torch.float32)
+            self.layers.append(d)
+        cos, sin = rope_tables(max_seq, cfg["head_dim"], cfg["rope_theta"], cfg["rope_cutoff"])
+        self.cos, self.sin = T(cos), T(sin)
+
+
+class Runner:
+    def __init__(self, dm: DeviceModel, batch: int = 1):
+        if batch < 1 or batch > 8:
+            raise ValueError("the GEMV decode path serves 1..8 sequences")
+        self.dm = dm
+        cfg = dm.cfg
+        self.B = batch
+        self.H, self.nh, self.hd = cfg["hidden"], cfg["n_heads"], cfg["head_dim"]
+        self.F = cfg["inter"]
+        self.qd = self.nh * self.hd
+        self.nqkv = self.qd + 2 * self.hd
+        self.eps = float(cfg["eps"])
+        self.max_seq = dm.max_seq
+        dev = dm.device
+        B, H, S = batch, self.H, self.max_seq
+        self.cache_stride = S * self.hd
+        nL = cfg["n_layers"]
+        self.kc = [torch.zeros((B, S, self.hd), dtype=torch.float32, device=dev) for _ in range(nL)]
+        self.vc = [torch.zeros((B, S, self.hd), dtype=torch.float32, device=dev) for _ in range(nL)]
+        f32 = lambda *s: torch.zeros(s, dtype=torch.float32, device=dev)  # noqa: E731
+        self.x, self.h = f32(B, H), f32(B, H)
+        self.qkv, self.q = f32(B, self.nqkv), f32(B, self.qd)
+        self.attn, self.o = f32(B, self.qd), f32(B, H)
+        self.gu, self.a, self.d = f32(B, 2 * self.F), f32(B, self.F), f32(B, H)
+        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.cur = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.tok = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.keys = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.history = torch.zeros((B, S), dtype=torch.int32, device=dev)
+        ws = _lib.load().sb_attn_decode_workspace_size(B, self.nh, self.hd, S)
+        self.attn_ws = torch.empty(max(1, ws // 4), dtype=torch.float32, device=dev)
+        self.stream = torch.cuda.Stream(device=dev)
+        self.graph = None
+        self._pf = None  # prefill buffers, sized on first use
+
+    # ------------------------------------------------------------------ decode
+    def _gemv(self, w, x, y):
+        kern.gemv_q4(w[0], w[1], x, y=y)
+
+    def _decode_ops(self):
+        dm, L0 = self.dm, self.dm.layers
+        s = kern._stream()
+        lib = _lib.load()
+        B, H = self.B, self.H
+        _lib.call("sb_embed_q4", dm.embed_q.data_ptr(), dm.embed_s.data_ptr(), _F16, dm.cfg["group"],
+                  self.cur.data_ptr(), B, H, float(dm.cfg["embed_scale"]), self.x.data_ptr(), None, s)
+        _lib.call("sb_add_rmsnorm", self.x.data_ptr(), None, _F32, None, L0[0]["in_norm"].data_ptr(),
+                  self.x.data_ptr(), self.h.data_ptr(), None, B, H, self.eps, s)
+        for li, L in enumerate(L0):
+            self._gemv(L["qkv"], self.h, self.qkv)
+            _lib.call("sb_qkv_prep", self.qkv.data_ptr(), _F32, self.nqkv, L["q_norm"].data_ptr(),
+                      L["k_norm"].data_ptr(), dm.cos.data_ptr(), dm.sin.data_ptr(), self.pos.data_ptr(), 0, B,
+                      self.nh, self.hd, self.eps, None, self.q.data_ptr(), self.kc[li].data_ptr(),
+                      self.vc[li].data_ptr(), None, None, self.cache_stride, s)
+            _lib.call("sb_attn_decode", self.q.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
+                      self.cache_stride, self.pos.data_ptr(), B, self.nh, self.hd, self.max_seq,
+                      self.attn.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws.numel() * 4, s)
+            self._gemv(L["o"], self.attn, self.o)
+            _lib.call("sb_add_rmsnorm", self.x.data_ptr(), self.o.data_ptr(), _F32, L["post_attn_norm"].data_ptr(),
+                      L["pre_ffn_norm"].data_ptr(), self.x.data_ptr(), self.h.data_ptr(), None, B, H, self.eps, s)
+            self._gemv(L["gu"], self.h, self.gu)
+            _lib.call("sb_geglu", self.gu.data_ptr(), _F32, B, self.F, self.a.data_ptr(), None, s)
+            self._gemv(L["down"], self.a, self.d)
+            nxt = L0[li + 1]["in_norm"] if li + 1 < len(L0) else dm.final_norm
+            _lib.call("sb_add_rmsnorm", self.x.data_ptr(), self.d.data_ptr(), _F32, L["post_ffn_norm"].data_ptr(),
+                      nxt.data_ptr(), self.x.data_ptr(), self.h.data_ptr(), None, B, H, self.eps, s)
+        kern.lmhead_argmax(dm.embed_q, dm.embed_s, self.h, keys=self.keys, tokens=self.tok)
+        _lib.call("sb_step_advance", self.pos.data_ptr(), self.tok.data_ptr(), self.cur.data_ptr(),
+                  self.history.data_ptr(), self.max_seq, B, s)
+        del lib
+
+    def kernel_launches_per_step(self) -> int:
+        nL = len(self.dm.layers)
+        per_layer = 4 + 1 + 2 + 2 + 1  # 4 GEMVs, prep, attention (2), add+norm (2), geglu
+        return 2 + nL * per_layer + 2 + 1  # embed + first norm, layers, lm_head (gemv + tokens), advance
+
+    def capture(self):
+        """Warm up, then capture one decode step as a CUDA graph."""
+        with torch.cuda.stream(self.stream):
+            saved = (self.pos.clone(), self.cur.clone(), self.history.clone())
+            self._decode_ops()  # first calls set kernel attributes outside capture
+            self.pos.copy_(saved[0])
+            self.cur.copy_(saved[1])
+            self.history.copy_(saved[2])
+        torch.cuda.synchronize(self.dm.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self._decode_ops()
+        return self.graph
+
+    def decode_step(self):
+        if self.graph is None:
+            self.capture()
+        with torch.cuda.stream(self.stream):
+            self.graph.replay()
+
+    def decode(self, steps: int) -> torch.Tensor:
+        """Greedy-decode `steps` tokens for every sequence; returns [B, steps] (device)."""
+        start = self.pos.clone()
+        for _ in range(steps):
+            self.decode_step()
+        torch.cuda.current_stream().wait_stream(self.stream)
+        out = torch.stack([self.history[b, int(start[b]) + 1:int(start[b]) + 1 + steps] for b in range(self.B)])
+        return out
+
+    def set_state(self, cur, pos):
+        with torch.cuda.stream(self.stream):
+            self.cur.copy_(torch.as_tensor(cur, dtype=torch.int32))
+            self.pos.copy_(torch.as_tensor(pos, dtype=torch.int32))
+            for b in range(self.B):
+                self.history[b, int(pos[b])] = int(cur[b])
+
+    # ------------------------------------------------------------------ prefill
+    def prefill_tokenwise(self, tokens, seq: int = 0) -> int:
+        """Run the prompt through the decode step one token at a time (f32 path).
+
+        Only valid for batch == 1 (the step advances every sequence)."""
+        if self.B != 1:
+            raise ValueError("token-wise prefill drives the whole batch; use batch=1")
+        for p, t in enumerate(tokens):
+            self.set_state([t], [p])
+            self.decode_step()
+        torch.cuda.current_stream().wait_stream(self.stream)
+        return int(self.tok[0].item())
+
+    def _prefill_buffers(self, S):
+        if self._pf is not None and self._pf["S"] >= S:
+            return self._pf
+        dev = self.dm.device
+        H, F, nh, hd = self.H, self.F, self.nh, self.hd
+        ldp = (S + 7) // 8 * 8
+        f16 = lambda *s: torch.empty(s, dtype=torch.float16, device=dev)  # noqa: E731
+        f32 = lambda *s: torch.empty(s, dtype=torch.float32, device=dev)  # noqa: E731
+        pf = {"S": S, "ldp": ldp,
+              "tok": torch.empty(S, dtype=torch.int32, device=dev),
+              "hid": f32(S, H), "h16": f16(S, H), "hlast": f32(S, H),
+              "qkv16": f16(S, self.nqkv), "q16": f16(S, nh, hd), "k16": f16(self.max_seq, hd),
+              "v16": f16(self.max_seq, hd), "scores": f32(S * nh, ldp), "p16": f16(S * nh, ldp),
+              "attn16": f16(S, nh * hd), "o16": f16(S, H), "gu16": f16(S, 2 * F), "a16": f16(S, F),
+              "d16": f16(S, H)}
+        ws = max(kern.gemm_q4_workspace_size(S, n, k) for n, k in
+                 ((self.nqkv, H), (H, self.qd), (2 * F, H), (H, F)))
+        pf["ws"] = torch.empty(max(1, ws // 4), dtype=torch.float32, device=dev)
+        self._pf = pf
+        return pf
+
+    def prefill(self, tokens, seq: int = 0) -> int:
+        """Layers-outer prefill of one prompt into sequence `seq` (positions 0..S-1).
+
+        Returns the first greedy token and leaves the sequence ready to decode
+        (cur = that token, pos = S)."""
+        dm = self.dm
+        S = len(tokens)
+        if S < 1 or S >= self.max_seq:
+            raise ValueError("prompt length out of range")
+        pf = self._prefill_buffers(S)
+        H, nh, hd, F = self.H, self.nh, self.hd, self.F
+        ldp = pf["ldp"]
+        with torch.cuda.stream(self.stream):
+            s = kern._stream()
+            pf["tok"][:S].copy_(torch.as_tensor(list(tokens), dtype=torch.int32))
+            self._prefill_ops(pf, S, seq, s)
+            # first greedy token from the last prompt position
+            kern.lmhead_argmax(dm.embed_q, dm.embed_s, pf["hlast"][S - 1:S], keys=self.keys[seq:seq + 1],
+                               tokens=self.tok[seq:seq + 1])
+            self.cur[seq:seq + 1].copy_(self.tok[seq:seq + 1])
+            self.pos[seq] = S
+            self.history[seq, S].copy_(self.tok[seq])
+        torch.cuda.current_stream().wait_stream(self.stream)
+        return int(self.tok[seq].item())
+
+    def _prefill_ops(self, pf, S, seq, s):
+        dm, Ls = self.dm, self.dm.layers
+        H, nh, hd, F = self.H, self.nh, self.hd, self.F
+        ldp, ws = pf["ldp"], pf["ws"]
+        _lib.call("sb_embed_q4", dm.embed_q.data_ptr(), dm.embed_s.data_ptr(), _F16, dm.cfg["group"],
+                  pf["tok"].data_ptr(), S, H, float(dm.cfg["embed_scale"]), pf["hid"].data_ptr(), None, s)
+        _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), None, _F32, None, Ls[0]["in_norm"].data_ptr(),
+                  pf["hid"].data_ptr(), None, pf["h16"].data_ptr(), S, H, self.eps, s)
+        kc_off = seq * self.cache_stride * 4
+        for li, L in enumerate(Ls):
+            kern.gemm_q4(pf["h16"][:S], L["qkv"][0], L["qkv"][1], C=pf["qkv16"][:S], workspace=ws)
+            _lib.call("sb_qkv_prep", pf["qkv16"].data_ptr(), _F16, self.nqkv, L["q_norm"].data_ptr(),
+                      L["k_norm"].data_ptr(), dm.cos.data_ptr(), dm.sin.data_ptr(), None, 0, S, nh, hd, self.eps,
+                      pf["q16"].data_ptr(), None, self.kc[li].data_ptr() + kc_off, self.vc[li].data_ptr() + kc_off,
+                      pf["k16"].data_ptr(), pf["v16"].data_ptr(), self.cache_stride, s)
+            # scores[S*nh, S] = q . k^T (f32), softmax, P . V
+            _lib.call("sb_gemm_f16_f32out", pf["q16"].data_ptr(), pf["k16"].data_ptr(), pf["scores"].data_ptr(),
+                      S * nh, S, hd, 1.0, 1, hd, hd, ldp, s)
+            _lib.call("sb_softmax_causal", pf["scores"].data_ptr(), ldp, S * nh, nh, 0, S, pf["p16"].data_ptr(),
+                      ldp, s)
+            _lib.call("sb_gemm_f16", pf["p16"].data_ptr(), pf["v16"].data_ptr(), pf["attn16"].data_ptr(),
+                      S * nh, hd, S, 1.0, 0, ldp, hd, hd, s)
+            kern.gemm_q4(pf["attn16"][:S], L["o"][0], L["o"][1], C=pf["o16"][:S], workspace=ws)
+            _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), pf["o16"].data_ptr(), _F16,
+                      L["post_attn_norm"].data_ptr(), L["pre_ffn_norm"].data_ptr(), pf["hid"].data_ptr(), None,
+                      pf["h16"].data_ptr(), S, H, self.eps, s)
+            kern.gemm_q4(pf["h16"][:S], L["gu"][0], L["gu"][1], C=pf["gu16"][:S], workspace=ws)
+            _lib.call("sb_geglu", pf["gu16"].data_ptr(), _F16, S, F, None, pf["a16"].data_ptr(), s)
+            kern.gemm_q4(pf["a16"][:S], L["down"][0], L["down"][1], C=pf["d16"][:S], workspace=ws)
+            last = li + 1 == len(Ls)
+            nxt = Ls[li + 1]["in_norm"] if not last else dm.final_norm
+            _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), pf["d16"].data_ptr(), _F16,
+                      L["post_ffn_norm"].data_ptr(), nxt.data_ptr(), pf["hid"].data_ptr(),
+                      pf["hlast"].data_ptr() if last else None, None if last else pf["h16"].data_ptr(), S, H,
+                      self.eps, s)
+
+
+def greedy_generate(model: dict, prompt, steps: int, device="cuda:0", batched_prefill: bool = True,
+                    max_seq: int | None = None) -> list[int]:
+    """Prefill `prompt`, then greedy-decode until `steps` tokens exist (the first
+    comes from the prefill's last position), as the reference's generate loop does."""
+    S = len(prompt)
+    dm = DeviceModel(model, device, max_seq or (S + steps + 1))
+    r = Runner(dm, 1)
+    first = r.prefill(prompt) if batched_prefill else r.prefill_tokenwise(prompt)
+    if not batched_prefill:
+        r.set_state([first], [S])
+    if steps <= 1:
+        return [first][:steps]
+    rest = r.decode(steps - 1)[0].cpu().tolist()
+    return [first] + rest

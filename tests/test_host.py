@@ -1,0 +1,46 @@
+"""CPU: host-side logic (manifest format, RoPE tables, synthetic configs)."""
+import json
+import os
+
+import numpy as np
+
+from oracle import decoder as odec
+from slang_b200 import manifest, runner, synth
+
+
+def test_manifest_roundtrip(tmp_path):
+    cfg = synth.e2b_config(hidden=256, n_layers=2, n_heads=2, head_dim=64, inter=512, vocab=2048, rope_cutoff=32)
+    model = synth.random_model(cfg, seed=3)
+    d = manifest.write(model, str(tmp_path))
+    man = json.load(open(os.path.join(d, "manifest.json")))
+    # export.py conventions: 4-byte aligned offsets, bytes = file size
+    assert all(t["off"] % 4 == 0 for t in man["tensors"].values())
+    assert man["bytes"] == os.path.getsize(os.path.join(d, "weights.bin"))
+    assert man["tensors"]["L1.q_bits"]["shape"] == [cfg["q_dim"], cfg["hidden"] // 2]
+    back = manifest.read(d)
+    assert back["config"]["hidden"] == 256 and back["config"]["group"] == 32
+    np.testing.assert_array_equal(back["embed_q"], model["embed_q"])
+    for i in range(2):
+        for n in manifest.PROJ:
+            np.testing.assert_array_equal(back["layers"][i][n][0], model["layers"][i][n][0])
+            np.testing.assert_array_equal(back["layers"][i][n][1], model["layers"][i][n][1])
+        for n in ("in_norm", "q_norm", "k_norm", "post_attn_norm", "pre_ffn_norm", "post_ffn_norm"):
+            np.testing.assert_array_equal(back["layers"][i][n], model["layers"][i][n])
+
+
+def test_rope_tables_match_reference_formula():
+    cos, sin = runner.rope_tables(300, 256, 10000.0, 128)
+    ocos, osin = odec.rope_tables(300, 256, 10000.0, 128)
+    np.testing.assert_array_equal(cos, ocos)
+    np.testing.assert_array_equal(sin, osin)
+
+
+def test_partial_rope_cutoff_is_identity_beyond():
+    cos, sin = runner.rope_tables(10, 64, 1e6, 8)
+    assert (cos[:, 8:] == 1).all() and (sin[:, 8:] == 0).all()
+
+
+def test_e2b_config_shapes():
+    cfg = synth.e2b_config()
+    assert cfg["q_dim"] == 2048 and cfg["inter"] == 6144 and cfg["vocab"] == 262144
+    assert synth.E2B_SHAPES["down"] == (1536, 6144)

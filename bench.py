@@ -1,25 +1,27 @@
-"""Benchmark of the int4 quantized-matmul hot path on B200 (prints ONE JSON line on rank 0).
+"""Benchmark of the B200 int4 quantized-matmul path (prints ONE JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Headline workload ("1024-tok prefill"): one step is the
-layers-outer prefill projection stack of a Gemma-4-E2B-shaped int4 model --
-35 layers x {q, k, v, o, gate, up, down} fused dequant+tcgen05 GEMMs at
-M = 1024 tokens (group-32 f16 scales, f16 activations, f32 accumulate), all
-captured in one CUDA graph.  value = 1024 tokens / step time (whole job:
-N replicas x 1024 / max-over-ranks time, weak scaling; there is no collective
-on this path).  The 620 MB of packed weights exceed the 126 MB L2, so no flush
-is needed between steps.  Attention, norms and RoPE are not part of this
-workload (they are not in config 2).
+Headline: "1024-tok prefill tok/s" of the random-init Gemma-4-E2B-shaped int4
+decoder (BASELINE config 4 architecture: 35 layers, hidden 1536, FFN 6144,
+8q/1kv heads at head_dim 256, vocab 262144, group-32 f16 scales).  One step is
+the full layers-outer prefill of a 1024-token prompt -- embed, per layer the
+fused int4 tcgen05 projection GEMMs (q|k|v, o, gate|up, down), q/k norm + RoPE
++ KV-cache store, QK^T -> causal softmax -> PV on the tcgen05 f16 GEMM, the
+norms and GEGLU -- ending in the final norm and the lm_head argmax of the first
+generated token; it is captured as one CUDA graph.  value = N x 1024 tokens /
+max-over-ranks step time (replicas, weak scaling: there is no collective on
+this path).  The ~1 GB of weights exceeds the 126 MB L2, so no flush is needed.
 
-Also reported (sub-objects): the decode GEMV stack (35 layers x 7 GEMVs at
-M=1 plus the fused 262144-row lm_head+argmax, one CUDA graph per token) as
-decode-GEMV tok/s and achieved HBM GB/s, and the lm_head alone (config 3).
+Sub-objects: decode tok/s (graph-captured greedy decode step at context
+~1024, batch 1) with its bytes/token and HBM GB/s, the lm_head GEMV + argmax
+alone (config 3, HBM GB/s), the projection GEMMs inside the prefill (config 2
+shapes at M=1024, per matrix TFLOP/s), and at N>1 the vocabulary-sharded
+lm_head with its NCCL key all-reduce.
 
---impl reference times the reference's algorithm on the host cores: the numpy
-oracle (a restatement of the reference's numpy code; the reference itself is
-Python and cannot travel to the GPU box) on a bounded sample of the same
-workload, scaled to the same unit.
+--impl reference times the reference's algorithm on the host cores through the
+numpy oracle (the reference itself is Python and does not travel to the GPU
+box) on a bounded sample, scaled to the same unit.
 """
 from __future__ import annotations
 
@@ -44,7 +46,7 @@ VOCAB, HID = 262144, 1536
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -226,12 +228,12 @@ def run_reference(args):
     v = statistics.median([x["value"] for x in vals])
     cb = dict(vals[0])
     cb["value"] = v
-    line = {"metric": "1024-tok prefill tok/s (35-layer int4 projection GEMMs)", "value": v, "unit": "tok/s",
+    line = {"metric": "1024-tok prefill tok/s", "value": v, "unit": "tok/s",
             "impl": "reference", "n_gpus": args.gpus, "steps": len(vals), "warmup": args.warmup,
             "ms_per_step": 1e3 * M_TOK / v, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "cfg2_prefill_proj_stack", "tokens": M_TOK, "layers": N_LAYERS,
-                       "matrices": list(SHAPES), "parallelism": "cpu"},
+            "config": {"workload": "cfg4_full_model_prefill_1024", "prompt_tokens": M_TOK,
+                       "parallelism": "cpu", "sample": "see cpu_baseline.sample"},
             "cpu_baseline": cb,
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "wall_s": wall}
@@ -239,6 +241,10 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------ GPU arm
+PROMPT = 1024
+DECODE_STEPS = 64
+
+
 def main():
     args = parse()
     if args.kernel:
@@ -250,6 +256,7 @@ def main():
     import torch.distributed as dist
 
     from slang_b200 import kernels as kern
+    from slang_b200 import lmhead, runner, synth
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -259,89 +266,25 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    stream = torch.cuda.Stream(device=dev)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(1234 + rank)
 
-    def q4w(n, k):
-        w = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=gen)
-        s = (torch.randn((n, k // 32), device=dev, generator=gen) * 0.02).abs().half()
-        return w, s
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
-    with torch.cuda.stream(stream):
-        layers = [{nm: q4w(*shp) for nm, shp in SHAPES.items()} for _ in range(N_LAYERS)]
-        emb = q4w(VOCAB, HID)
-        X = torch.randn((M_TOK, HID), device=dev, generator=gen).half()
-        QO = torch.empty((M_TOK, 2048), dtype=torch.float16, device=dev)
-        KO = torch.empty((M_TOK, 256), dtype=torch.float16, device=dev)
-        VO = torch.empty((M_TOK, 256), dtype=torch.float16, device=dev)
-        OO = torch.empty((M_TOK, HID), dtype=torch.float16, device=dev)
-        GO = torch.empty((M_TOK, 6144), dtype=torch.float16, device=dev)
-        UO = torch.empty((M_TOK, 6144), dtype=torch.float16, device=dev)
-        DO = torch.empty((M_TOK, HID), dtype=torch.float16, device=dev)
-        ws_bytes = max(kern.gemm_q4_workspace_size(M_TOK, n, k) for n, k in SHAPES.values())
-        ws = torch.empty(max(1, ws_bytes // 4), dtype=torch.float32, device=dev)
+    cfg = synth.e2b_config()
+    model = synth.random_model(cfg, seed=1234 + rank)
+    dm = runner.DeviceModel(model, dev, PROMPT + args.warmup + args.steps + DECODE_STEPS + 8)
+    del model
+    r = runner.Runner(dm, 1)
+    prompt = synth.prompt_tokens(PROMPT, cfg["vocab"], seed=99 + rank)
+    r.prefill(prompt)                  # eager run + capture
+    g_prefill = r.prefill_graph(PROMPT)
+    stream = r.stream
 
-    launches = {"n": 0}
-
-    def gemm(A, name, L, out, alpha=1.0):
-        w, s = L[name]
-        kern.gemm_q4(A, w, s, C=out, alpha=alpha, workspace=ws)
-        n, k = SHAPES[name]
-        launches["n"] += 1 + (1 if kern.gemm_q4_workspace_size(M_TOK, n, k) else 0)
-
-    flops_step = 2 * M_TOK * N_LAYERS * sum(n * k for n, k in SHAPES.values())
-
-    def prefill_step(rec=None):
-        # layers outer, tokens inner (gemma4_150/prefill_gpu.py:316-395 GEMM sequence)
-        for L in layers:
-            for name, A, out in (("q", X, QO), ("k", X, KO), ("v", X, VO), ("o", QO, OO),
-                                 ("gate", X, GO), ("up", X, UO), ("down", GO, DO)):
-                if rec is not None:
-                    e0 = torch.cuda.Event(enable_timing=True)
-                    e0.record(stream)
-                gemm(A, name, L, out)
-                if rec is not None:
-                    e1 = torch.cuda.Event(enable_timing=True)
-                    e1.record(stream)
-                    rec.append((name, e0, e1))
-
-    # warm-up outside capture (first calls set kernel attributes, resolve symbols)
-    with torch.cuda.stream(stream):
-        prefill_step()
-    torch.cuda.synchronize()
-    launches["n"] = 0
-    g_prefill = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_prefill, stream=stream):
-        prefill_step()
-    launches_prefill = launches["n"]
-
-    # decode GEMV stack: 35 x 7 GEMVs at M=1 (f32 activations) + fused lm_head argmax
-    with torch.cuda.stream(stream):
-        xin = {k: torch.randn((1, k), device=dev, generator=gen) for k in (1536, 2048, 6144)}
-        yout = {nm: torch.empty((1, n), device=dev) for nm, (n, k) in SHAPES.items()}
-        keys = torch.empty(1, dtype=torch.int64, device=dev)
-        tok = torch.empty(1, dtype=torch.int32, device=dev)
-    gemv_bytes = sum(n * k // 2 + n * (k // 32) * 2 + k * 4 + n * 4 for n, k in SHAPES.values()) * N_LAYERS
-    lm_bytes = VOCAB * HID // 2 + VOCAB * (HID // 32) * 2 + HID * 4
-
-    def decode_step():
-        for L in layers:
-            for nm, (n, k) in SHAPES.items():
-                kern.gemv_q4(L[nm][0], L[nm][1], xin[k], y=yout[nm])
-        kern.lmhead_argmax(emb[0], emb[1], xin[1536], keys=keys, tokens=tok)
-
-    with torch.cuda.stream(stream):
-        decode_step()
-    torch.cuda.synchronize()
-    g_decode = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_decode, stream=stream):
-        decode_step()
-    g_lm = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_lm, stream=stream):
-        kern.lmhead_argmax(emb[0], emb[1], xin[1536], keys=keys, tokens=tok)
-
-    # ---------------- timed region: the headline (prefill stack)
+    # ---------------- timed region: the headline (prefill graph replays)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -349,88 +292,115 @@ def main():
     with torch.cuda.stream(stream):
         ms = timed_graph(torch, g_prefill, args.steps, args.warmup, stream)
     clocks = clk.stop()
-    torch.cuda.synchronize()
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
-    value = world * M_TOK / (ms / 1e3)
+    ms = max_over_ranks(ms)
+    value = world * PROMPT / (ms / 1e3)
 
-    # ---------------- end to end through the public API with host buffers
-    xh = torch.empty((M_TOK, HID), dtype=torch.float16, pin_memory=True)
-    xh.copy_(X.cpu())
-    outh = torch.empty((M_TOK, HID), dtype=torch.float16, pin_memory=True)
-    with torch.cuda.stream(stream):
-        for i in range(args.warmup + args.steps):
-            if i == args.warmup:
-                torch.cuda.synchronize()
-                e0 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-            X.copy_(xh, non_blocking=True)
-            g_prefill.replay()
-            outh.copy_(DO, non_blocking=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e1.record(stream)
+    # ---------------- end to end through the public API (pinned H2D prompt, D2H first token)
+    for _ in range(args.warmup):
+        r.prefill(prompt)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        r.prefill(prompt)
+    e1.record(stream)
     e1.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
 
-    # ---------------- roofline: per-launch durations of the fused GEMM kernel
-    rec = []
-    with torch.cuda.stream(stream):
-        prefill_step(rec)
-    torch.cuda.synchronize()
-    per = {}
-    for name, e0_, e1_ in rec:
-        per.setdefault(name, []).append(e0_.elapsed_time(e1_))
-    gemm_ms = sum(sum(v) for v in per.values())
+    # ---------------- roofline of the dominant kernel (fused int4 GEMM) inside the prefill
+    rec = r.prefill_timed_gemms(prompt)
     hbm_peak, tc_peak, peak_kind = load_peaks()
-    achieved_tflops = flops_step / (gemm_ms / 1e3) / 1e12
-    by_shape = {nm: {"avg_us": 1e3 * statistics.mean(v),
-                     "tflops": 2 * M_TOK * SHAPES[nm][0] * SHAPES[nm][1] / (statistics.mean(v) / 1e3) / 1e12}
-                for nm, v in per.items()}
+    gemm_ms = sum(x[4] for x in rec)
+    gemm_flops = sum(2 * m * n * k for _, m, n, k, _ in rec)
+    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
+    by = {}
+    for name, m, n, k, t in rec:
+        b = by.setdefault(name, {"shape": [m, n, k], "ms": 0.0, "count": 0})
+        b["ms"] += t
+        b["count"] += 1
+    for b in by.values():
+        m, n, k = b["shape"]
+        b["avg_us"] = 1e3 * b["ms"] / b["count"]
+        b["tflops"] = 2 * m * n * k / (b["avg_us"] / 1e6) / 1e12
+        del b["ms"]
 
-    # ---------------- decode GEMV stack + lm_head (sub-measurements)
+    # ---------------- decode (graph-captured step, batch 1, context from PROMPT)
+    r.capture()
     with torch.cuda.stream(stream):
-        dms = timed_graph(torch, g_decode, max(5, args.steps), args.warmup, stream)
-        lms = timed_graph(torch, g_lm, max(20, args.steps), args.warmup, stream)
-    dec_gbs = (gemv_bytes + lm_bytes) / (dms / 1e3) / 1e9
-    lm_gbs = lm_bytes / (lms / 1e3) / 1e9
+        dms = timed_graph(torch, r.graph, DECODE_STEPS, args.warmup, stream)
+    dms = max_over_ranks(dms)
+    ctx = PROMPT + args.warmup + DECODE_STEPS // 2
+    w_bytes = sum(t.numel() * t.element_size() for L in dm.layers for key in ("qkv", "o", "gu", "down") for t in L[key])
+    lm_bytes = dm.embed_q.numel() + dm.embed_s.numel() * 2
+    kv_bytes = len(dm.layers) * 2 * ctx * r.hd * 4
+    dec_bytes = w_bytes + lm_bytes + kv_bytes
+
+    # ---------------- lm_head GEMV + argmax alone (config 3)
+    g_lm = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        kern.lmhead_argmax(dm.embed_q, dm.embed_s, r.h, keys=r.keys, tokens=r.tok)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g_lm, stream=stream):
+            for _ in range(10):
+                kern.lmhead_argmax(dm.embed_q, dm.embed_s, r.h, keys=r.keys, tokens=r.tok)
+        lms = timed_graph(torch, g_lm, 5, 2, stream) / 10
+    lm_alg = VOCAB * HID // 2 + VOCAB * (HID // 32) * 2 + HID * 4
+
+    # ---------------- vocabulary-sharded lm_head over NCCL (N > 1)
+    sharded = None
+    if world > 1:
+        sh = lmhead.ShardedLMHead(dm.embed_q, dm.embed_s, rank, world)
+        keys = torch.zeros(1, dtype=torch.int64, device=dev)
+        toks = torch.zeros(1, dtype=torch.int32, device=dev)
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                sh(r.h, keys, toks)
+            torch.cuda.synchronize()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            for _ in range(args.steps):
+                sh(r.h, keys, toks)
+            s1.record(stream)
+        s1.synchronize()
+        sms_ = max_over_ranks(s0.elapsed_time(s1) / args.steps)
+        sharded = {"metric": "vocab-sharded lm_head + argmax (NCCL MAX of keys), tok/s", "value": 1e3 / sms_,
+                   "unit": "tok/s", "us": sms_ * 1e3, "shards": world,
+                   "hbm_gbs_aggregate": lm_alg / (sms_ / 1e3) / 1e9, "scaling": "strong"}
 
     if rank == 0:
-        cpu = None
-        if not args.no_cpu_baseline and world == 1:
-            cpu = cpu_sample_prefill()
+        cpu = cpu_sample_prefill() if (not args.no_cpu_baseline and world == 1) else None
         line = {
-            "metric": "1024-tok prefill tok/s (35-layer int4 projection GEMMs)",
-            "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "cfg2_prefill_proj_stack", "tokens": M_TOK, "layers": N_LAYERS,
-                       "matrices": {k: list(v) for k, v in SHAPES.items()}, "group": 32,
-                       "parallelism": f"replicas x{world}", "l2": "weights 620 MB > 126 MB L2, no flush",
-                       "graph": "one CUDA graph per step"},
-            "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": tc_peak, "unit": "TFLOP/s",
-                         "frac": achieved_tflops / tc_peak, "traffic": None, "peak_kind": peak_kind,
-                         "kernel": "gemm_tc_kernel<MODE_Q4> (+ split-K finalize)", "by_matrix": by_shape},
+            "metric": "1024-tok prefill tok/s", "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "cfg4_full_model_prefill_1024", "prompt_tokens": PROMPT,
+                       "model": "random-init Gemma-4-E2B-shaped int4 decoder (35L, H1536, F6144, 8q/1kv hd256, "
+                                "V262144, group-32 f16 scales)",
+                       "parallelism": f"replicas x{world}", "l2": "weights ~1 GB > 126 MB L2, no flush",
+                       "graph": "one CUDA graph per prefill"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
+                         "frac": achieved / tc_peak, "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "gemm_q4_kernel (fused int4 dequant + tcgen05, incl. split-K finalize)",
+                         "flops_per_step": gemm_flops, "gemm_ms_per_step": gemm_ms,
+                         "gemm_share_of_step": gemm_ms / ms, "by_matrix": by},
             "cpu_baseline": cpu,
-            "e2e": {"value": world * M_TOK / (e2e_ms / 1e3), "unit": "tok/s",
-                    "h2d_bytes_per_step": M_TOK * HID * 2, "d2h_bytes_per_step": M_TOK * HID * 2},
-            "gpu_launches": launches_prefill,
+            "e2e": {"value": world * PROMPT / (e2e_ms / 1e3), "unit": "tok/s",
+                    "h2d_bytes_per_step": PROMPT * 4, "d2h_bytes_per_step": 4},
+            "gpu_launches": r.prefill_launches(PROMPT),
             "clocks": clocks,
-            "decode_gemv": {"metric": "decode GEMV-stack tok/s (35x7 GEMVs + lm_head argmax, M=1)",
-                            "value": 1e3 / dms, "unit": "tok/s", "ms_per_token": dms,
-                            "hbm_gbs": dec_gbs, "frac_of_hbm": dec_gbs / hbm_peak,
-                            "bytes_per_token": gemv_bytes + lm_bytes},
-            "lmhead": {"metric": "q4 GEMV HBM GB/s (lm_head 262144x1536 + argmax)", "value": lm_gbs,
-                       "unit": "GB/s", "us": lms * 1e3, "frac_of_hbm": lm_gbs / hbm_peak, "peak": hbm_peak},
+            "decode": {"metric": "decode tok/s (batch 1, greedy, context ~%d)" % ctx, "value": world * 1e3 / dms,
+                       "unit": "tok/s", "ms_per_token": dms, "bytes_per_token": dec_bytes,
+                       "hbm_gbs": dec_bytes / (dms / 1e3) / 1e9, "frac_of_hbm": dec_bytes / (dms / 1e3) / 1e9 / hbm_peak,
+                       "gpu_launches_per_token": r.kernel_launches_per_step()},
+            "lmhead": {"metric": "q4 GEMV HBM GB/s (lm_head 262144x1536 + argmax)", "value": lm_alg / (lms / 1e3) / 1e9,
+                       "unit": "GB/s", "us": lms * 1e3, "frac_of_hbm": lm_alg / (lms / 1e3) / 1e9 / hbm_peak,
+                       "peak": hbm_peak},
+            "lmhead_sharded": sharded,
         }
         print(json.dumps(line), flush=True)
-    del g_prefill, g_decode, g_lm
+    del g_prefill, g_lm
+    r.graph = None
+    r._pgraphs.clear()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

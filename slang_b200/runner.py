@@ -111,6 +111,7 @@ class Runner:
         self.stream = torch.cuda.Stream(device=dev)
         self.graph = None
         self._pf = None  # prefill buffers, sized on first use
+        self._pgraphs: dict = {}  # (prompt length, sequence) -> captured prefill
 
     # ------------------------------------------------------------------ decode
     def _gemv(self, w, x, y):
@@ -212,6 +213,7 @@ class Runner:
         f32 = lambda *s: torch.empty(s, dtype=torch.float32, device=dev)  # noqa: E731
         pf = {"S": S, "ldp": ldp,
               "tok": torch.empty(S, dtype=torch.int32, device=dev),
+              "tok_host": torch.empty(S, dtype=torch.int32, pin_memory=True),
               "hid": f32(S, H), "h16": f16(S, H), "hlast": f32(S, H),
               "qkv16": f16(S, self.nqkv), "q16": f16(S, nh, hd), "k16": f16(self.max_seq, hd),
               "v16": f16(self.max_seq, hd), "scores": f32(S * nh, ldp), "p16": f16(S * nh, ldp),
@@ -221,44 +223,94 @@ class Runner:
                  ((self.nqkv, H), (H, self.qd), (2 * F, H), (H, F)))
         pf["ws"] = torch.empty(max(1, ws // 4), dtype=torch.float32, device=dev)
         self._pf = pf
+        self._pgraphs.clear()  # captured prefills point at the old buffers
         return pf
 
-    def prefill(self, tokens, seq: int = 0) -> int:
+    def prefill(self, tokens, seq: int = 0, graph: bool = True) -> int:
         """Layers-outer prefill of one prompt into sequence `seq` (positions 0..S-1).
 
         Returns the first greedy token and leaves the sequence ready to decode
-        (cur = that token, pos = S)."""
-        dm = self.dm
+        (cur = that token, pos = S).  The device work of a prompt length is
+        captured as a CUDA graph on its first call and replayed afterwards; a
+        call copies the prompt from pinned host memory and reads back one token."""
         S = len(tokens)
         if S < 1 or S >= self.max_seq:
             raise ValueError("prompt length out of range")
         pf = self._prefill_buffers(S)
-        H, nh, hd, F = self.H, self.nh, self.hd, self.F
-        ldp = pf["ldp"]
+        key = (S, seq)
         with torch.cuda.stream(self.stream):
-            s = kern._stream()
-            pf["tok"][:S].copy_(torch.as_tensor(list(tokens), dtype=torch.int32))
-            self._prefill_ops(pf, S, seq, s)
-            # first greedy token from the last prompt position
-            kern.lmhead_argmax(dm.embed_q, dm.embed_s, pf["hlast"][S - 1:S], keys=self.keys[seq:seq + 1],
-                               tokens=self.tok[seq:seq + 1])
-            self.cur[seq:seq + 1].copy_(self.tok[seq:seq + 1])
-            self.pos[seq] = S
-            self.history[seq, S].copy_(self.tok[seq])
+            pf["tok_host"][:S].copy_(torch.as_tensor(list(tokens), dtype=torch.int32))
+            pf["tok"][:S].copy_(pf["tok_host"][:S], non_blocking=True)
+            g = self._pgraphs.get(key) if graph else None
+            if g is not None:
+                g.replay()
+            else:
+                self._prefill_step(pf, S, seq)
+                if graph:
+                    torch.cuda.synchronize(self.dm.device)
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=self.stream):
+                        self._prefill_step(pf, S, seq)
+                    self._pgraphs[key] = g
         torch.cuda.current_stream().wait_stream(self.stream)
         return int(self.tok[seq].item())
 
-    def _prefill_ops(self, pf, S, seq, s):
+    def prefill_graph(self, S: int, seq: int = 0):
+        """The captured prefill of length S (after one `prefill` call of that length)."""
+        return self._pgraphs[(S, seq)]
+
+    def _prefill_step(self, pf, S, seq, rec=None):
+        dm = self.dm
+        s = kern._stream()
+        self._prefill_ops(pf, S, seq, s, rec)
+        # first greedy token from the last prompt position
+        kern.lmhead_argmax(dm.embed_q, dm.embed_s, pf["hlast"][S - 1:S], keys=self.keys[seq:seq + 1],
+                           tokens=self.tok[seq:seq + 1])
+        self.cur[seq:seq + 1].copy_(self.tok[seq:seq + 1])
+        self.pos[seq:seq + 1].fill_(S)
+        self.history[seq, S:S + 1].copy_(self.tok[seq:seq + 1])
+
+    def prefill_launches(self, S: int) -> int:
+        """Kernels of this library launched by one prefill of length S."""
+        H, F = self.H, self.F
+        split = lambda n, k: 1 if kern.gemm_q4_workspace_size(S, n, k) else 0  # noqa: E731
+        per_layer = (4 + split(self.nqkv, H) + split(H, self.qd) + split(2 * F, H) + split(H, F)  # 4 projections
+                     + 1 + 3 + 2 + 1)  # prep; scores, softmax, PV; two add+norms; geglu
+        return 2 + len(self.dm.layers) * per_layer + 2
+
+    def prefill_timed_gemms(self, tokens, seq: int = 0):
+        """Run one prefill eagerly with CUDA events around every fused projection
+        GEMM; returns [(name, M, N, K, ms)]."""
+        S = len(tokens)
+        pf = self._prefill_buffers(S)
+        rec = []
+        with torch.cuda.stream(self.stream):
+            pf["tok"][:S].copy_(torch.as_tensor(list(tokens), dtype=torch.int32))
+            self._prefill_step(pf, S, seq, rec)
+        torch.cuda.synchronize(self.dm.device)
+        return [(name, m, n, k, e0.elapsed_time(e1)) for name, m, n, k, e0, e1 in rec]
+
+    def _prefill_ops(self, pf, S, seq, s, rec=None):
         dm, Ls = self.dm, self.dm.layers
         H, nh, hd, F = self.H, self.nh, self.hd, self.F
         ldp, ws = pf["ldp"], pf["ws"]
+
+        def proj(name, A, W, C, K):
+            if rec is not None:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(self.stream)
+            kern.gemm_q4(A, W[0], W[1], C=C, workspace=ws)
+            if rec is not None:
+                e1.record(self.stream)
+                rec.append((name, S, W[0].shape[0], K, e0, e1))
+
         _lib.call("sb_embed_q4", dm.embed_q.data_ptr(), dm.embed_s.data_ptr(), _F16, dm.cfg["group"],
                   pf["tok"].data_ptr(), S, H, float(dm.cfg["embed_scale"]), pf["hid"].data_ptr(), None, s)
         _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), None, _F32, None, Ls[0]["in_norm"].data_ptr(),
                   pf["hid"].data_ptr(), None, pf["h16"].data_ptr(), S, H, self.eps, s)
         kc_off = seq * self.cache_stride * 4
         for li, L in enumerate(Ls):
-            kern.gemm_q4(pf["h16"][:S], L["qkv"][0], L["qkv"][1], C=pf["qkv16"][:S], workspace=ws)
+            proj("qkv", pf["h16"][:S], L["qkv"], pf["qkv16"][:S], H)
             _lib.call("sb_qkv_prep", pf["qkv16"].data_ptr(), _F16, self.nqkv, L["q_norm"].data_ptr(),
                       L["k_norm"].data_ptr(), dm.cos.data_ptr(), dm.sin.data_ptr(), None, 0, S, nh, hd, self.eps,
                       pf["q16"].data_ptr(), None, self.kc[li].data_ptr() + kc_off, self.vc[li].data_ptr() + kc_off,
@@ -270,13 +322,13 @@ class Runner:
                       ldp, s)
             _lib.call("sb_gemm_f16", pf["p16"].data_ptr(), pf["v16"].data_ptr(), pf["attn16"].data_ptr(),
                       S * nh, hd, S, 1.0, 0, ldp, hd, hd, s)
-            kern.gemm_q4(pf["attn16"][:S], L["o"][0], L["o"][1], C=pf["o16"][:S], workspace=ws)
+            proj("o", pf["attn16"][:S], L["o"], pf["o16"][:S], self.qd)
             _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), pf["o16"].data_ptr(), _F16,
                       L["post_attn_norm"].data_ptr(), L["pre_ffn_norm"].data_ptr(), pf["hid"].data_ptr(), None,
                       pf["h16"].data_ptr(), S, H, self.eps, s)
-            kern.gemm_q4(pf["h16"][:S], L["gu"][0], L["gu"][1], C=pf["gu16"][:S], workspace=ws)
+            proj("gate|up", pf["h16"][:S], L["gu"], pf["gu16"][:S], H)
             _lib.call("sb_geglu", pf["gu16"].data_ptr(), _F16, S, F, None, pf["a16"].data_ptr(), s)
-            kern.gemm_q4(pf["a16"][:S], L["down"][0], L["down"][1], C=pf["d16"][:S], workspace=ws)
+            proj("down", pf["a16"][:S], L["down"], pf["d16"][:S], F)
             last = li + 1 == len(Ls)
             nxt = Ls[li + 1]["in_norm"] if not last else dm.final_norm
             _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), pf["d16"].data_ptr(), _F16,

@@ -50,7 +50,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", default="", choices=["", "gemm_q4", "gemm_f16", "gemv", "lmhead"],
+    ap.add_argument("--kernel", default="",
+                    choices=["", "gemm_q4", "gemm_f16", "gemv", "lmhead", "prefill", "decode"],
                     help="run one kernel --iters times on a single shape and exit (for ncu captures)")
     ap.add_argument("--shape", default="6144,1536", help="N,K of the weight for --kernel")
     ap.add_argument("--m", type=int, default=1024, help="rows of the activation for --kernel")
@@ -58,10 +59,36 @@ def parse():
     return ap.parse_args()
 
 
+def run_model_case(args):
+    """Full-model prefill (--m tokens) or decode step, run eagerly (no graph) so a
+    profiler sees each launch: one warm-up pass, then --iters profiled passes."""
+    import torch
+
+    from slang_b200 import runner, synth
+    dev = torch.device("cuda", 0)
+    cfg = synth.e2b_config()
+    model = synth.random_model(cfg, seed=1234)
+    dm = runner.DeviceModel(model, dev, args.m + 8 + 4 * args.iters)
+    r = runner.Runner(dm, 1)
+    prompt = synth.prompt_tokens(args.m, cfg["vocab"], seed=99)
+    r.prefill(prompt, graph=False)
+    torch.cuda.synchronize()
+    for _ in range(args.iters):
+        if args.kernel == "prefill":
+            r.prefill(prompt, graph=False)
+        else:
+            with torch.cuda.stream(r.stream):
+                r._decode_ops()
+    torch.cuda.synchronize()
+    print(f"ran {args.kernel} x{args.iters} (prompt {args.m}) eagerly")
+
+
 def run_kernel_case(args):
     """One kernel on one shape, --iters launches after one warm-up (ncu target)."""
     import torch
 
+    if args.kernel in ("prefill", "decode"):
+        return run_model_case(args)
     from slang_b200 import kernels as kern
     dev = torch.device("cuda", 0)
     n, k = (int(v) for v in args.shape.split(","))

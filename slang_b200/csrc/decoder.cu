@@ -46,6 +46,8 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 // ---------------------------------------------------------------- embedding
 __global__ void embed_kernel(const uint8_t* __restrict__ emb, const void* __restrict__ scales, int sf16, int group,
                              const int32_t* __restrict__ tokens, int k, float mult, float* out32, __half* out16) {
+  sbd::griddep_launch_dependents();
+  sbd::griddep_wait();
   const int row = blockIdx.x;
   const int64_t tok = tokens[row];
   const int gps = k / group;
@@ -64,50 +66,75 @@ __global__ void embed_kernel(const uint8_t* __restrict__ emb, const void* __rest
 // ---------------------------------------------------------------- add + RMSNorm
 // x_out = x + rmsnorm(y) * w_add   (when y != null; else x_out = x)
 // h     = rmsnorm(x_out) * w_norm  -> h_out (f32) and/or h16 (f16)
+// One CTA per row; n % 4 == 0, n <= 4 * kT * MAXV4; values stay in registers.
+constexpr int MAXV4 = 8;
+
+__device__ __forceinline__ float4 load4(const void* p, int is_f16, size_t i) {
+  if (is_f16) {
+    const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __half*>(p) + i);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  return *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+}
+
 __global__ void add_rmsnorm_kernel(const float* __restrict__ x, const void* __restrict__ y, int y_f16,
                                    const float* __restrict__ w_add, const float* __restrict__ w_norm, float* x_out,
                                    float* h_out, __half* h16, int n, float eps) {
   __shared__ float red[32];
-  constexpr int MAXV = 32;  // n <= 32 * kT
+  sbd::griddep_launch_dependents();
   const int row = blockIdx.x;
   const size_t base = static_cast<size_t>(row) * n;
-  float v[MAXV];
+  const int n4 = n >> 2;
+  float4 v[MAXV4];
   float ss = 0.f;
+  sbd::griddep_wait();
   if (y) {
 #pragma unroll
-    for (int j = 0; j < MAXV; ++j) {
+    for (int j = 0; j < MAXV4; ++j) {
       const int i = threadIdx.x + j * kT;
-      v[j] = i < n ? load_act(y, y_f16, base + i) : 0.f;
-      ss += v[j] * v[j];
+      v[j] = i < n4 ? load4(y, y_f16, base + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
     }
     const float d = sqrtf(block_sum(ss, red) / n + eps);
     ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < MAXV; ++j) {
+    for (int j = 0; j < MAXV4; ++j) {
       const int i = threadIdx.x + j * kT;
-      if (i < n) {
-        v[j] = x[base + i] + v[j] / d * w_add[i];
-        if (x_out) x_out[base + i] = v[j];
+      if (i < n4) {
+        const float4 xv = *reinterpret_cast<const float4*>(x + base + 4 * i);
+        const float4 wa = *reinterpret_cast<const float4*>(w_add + 4 * i);
+        v[j] = make_float4(xv.x + v[j].x / d * wa.x, xv.y + v[j].y / d * wa.y, xv.z + v[j].z / d * wa.z,
+                           xv.w + v[j].w / d * wa.w);
+        if (x_out) *reinterpret_cast<float4*>(x_out + base + 4 * i) = v[j];
       }
-      ss += v[j] * v[j];
+      ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < MAXV; ++j) {
+    for (int j = 0; j < MAXV4; ++j) {
       const int i = threadIdx.x + j * kT;
-      v[j] = i < n ? x[base + i] : 0.f;
-      if (i < n && x_out && x_out != x) x_out[base + i] = v[j];
-      ss += v[j] * v[j];
+      v[j] = i < n4 ? *reinterpret_cast<const float4*>(x + base + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < n4 && x_out && x_out != x) *reinterpret_cast<float4*>(x_out + base + 4 * i) = v[j];
+      ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
     }
   }
   const float d = sqrtf(block_sum(ss, red) / n + eps);
 #pragma unroll
-  for (int j = 0; j < MAXV; ++j) {
+  for (int j = 0; j < MAXV4; ++j) {
     const int i = threadIdx.x + j * kT;
-    if (i < n) {
-      const float h = v[j] / d * w_norm[i];
-      if (h_out) h_out[base + i] = h;
-      if (h16) h16[base + i] = __float2half_rn(h);
+    if (i < n4) {
+      const float4 wn = *reinterpret_cast<const float4*>(w_norm + 4 * i);
+      const float4 h = make_float4(v[j].x / d * wn.x, v[j].y / d * wn.y, v[j].z / d * wn.z, v[j].w / d * wn.w);
+      if (h_out) *reinterpret_cast<float4*>(h_out + base + 4 * i) = h;
+      if (h16) {
+        __half2 a = __floats2half2_rn(h.x, h.y), b = __floats2half2_rn(h.z, h.w);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&a);
+        u.y = *reinterpret_cast<uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(h16 + base + 4 * i) = u;
+      }
     }
   }
 }
@@ -123,6 +150,8 @@ __global__ void qkv_prep_kernel(const void* __restrict__ qkv, int qkv_f16, int l
                                 int nh, float eps, __half* q16, float* q32, float* k_cache, float* v_cache,
                                 __half* k16, __half* v16, int64_t cache_stride) {
   constexpr int HD = 32 * VPL, HALF = HD / 2;
+  sbd::griddep_launch_dependents();
+  sbd::griddep_wait();
   const int s = blockIdx.x;  // token (prefill) or sequence (decode)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pos = pos_dev ? pos_dev[s] : start_pos + s;
@@ -180,6 +209,8 @@ __global__ void qkv_prep_kernel(const void* __restrict__ qkv, int qkv_f16, int l
 __global__ void softmax_causal_kernel(const float* __restrict__ scores, int ld_s, int nh, int start_pos, int n_keys,
                                       __half* p16, int ld_p) {
   __shared__ float red[32];
+  sbd::griddep_launch_dependents();
+  sbd::griddep_wait();
   const int r = blockIdx.x;
   const int last = start_pos + r / nh;  // inclusive
   const float* srow = scores + static_cast<size_t>(r) * ld_s;
@@ -202,6 +233,8 @@ __global__ void softmax_causal_kernel(const float* __restrict__ scores, int ld_s
 // ---------------------------------------------------------------- GEGLU
 // out[r, i] = gelu_tanh(gu[r, i]) * gu[r, f + i]
 __global__ void geglu_kernel(const void* __restrict__ gu, int gu_f16, int f, int rows, float* out32, __half* out16) {
+  sbd::griddep_launch_dependents();
+  sbd::griddep_wait();
   const size_t total = static_cast<size_t>(rows) * f;
   for (size_t e = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -216,9 +249,11 @@ __global__ void geglu_kernel(const void* __restrict__ gu, int gu_f16, int f, int
 
 // ---------------------------------------------------------------- decode attention
 // Split-KV decode attention for one KV head shared by nh query heads.
-// Partial: CTA (b, chunk) scores CK keys for all heads, keeps per-head max and
-// sum and the unnormalised P.V; merge rescales the chunks (flash-decoding).
-constexpr int CK = 64;
+// Partial: CTA (b, chunk) stages the chunk's CK keys in shared memory, warp h
+// scores them for query head h (lane t keeps key t), takes the chunk's max and
+// sum, then thread d forms the unnormalised sum_t p[h][t] V[t][d] for every
+// head.  Merge: CTA (b, h), thread d rescales the chunks (flash-decoding).
+constexpr int CK = 32;
 
 template <int VPL>
 __global__ void attn_decode_partial_kernel(const float* __restrict__ q32, const float* __restrict__ k_cache,
@@ -226,44 +261,40 @@ __global__ void attn_decode_partial_kernel(const float* __restrict__ q32, const 
                                            int nh, int64_t cache_stride, float* part, int max_chunks) {
   constexpr int HD = 32 * VPL;
   extern __shared__ float sm[];
-  float* qs = sm;                 // [nh][HD]
-  float* sc = sm + nh * HD;       // [nh][CK]
+  float* ks = sm;             // [CK][HD]
+  float* qs = ks + CK * HD;   // [nh][HD]
+  float* ps = qs + nh * HD;   // [nh][CK]
+  sbd::griddep_launch_dependents();
   const int b = blockIdx.x, c = blockIdx.y;
+  sbd::griddep_wait();
   const int T = pos_dev[b] + 1;
   const int t0 = c * CK;
   if (t0 >= T) return;
   const int nt = min(CK, T - t0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int i = threadIdx.x; i < nh * HD; i += blockDim.x) qs[i] = q32[static_cast<size_t>(b) * nh * HD + i];
+  const float* kb = k_cache + static_cast<size_t>(b) * cache_stride + static_cast<size_t>(t0) * HD;
+  const float* vb = v_cache + static_cast<size_t>(b) * cache_stride + static_cast<size_t>(t0) * HD;
+  for (int i = threadIdx.x; i < nt * HD / 4; i += blockDim.x)
+    reinterpret_cast<float4*>(ks)[i] = reinterpret_cast<const float4*>(kb)[i];
+  for (int i = threadIdx.x; i < nh * HD / 4; i += blockDim.x)
+    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(q32 + static_cast<size_t>(b) * nh * HD)[i];
   __syncthreads();
-  const float* kb = k_cache + static_cast<size_t>(b) * cache_stride;
-  const float* vb = v_cache + static_cast<size_t>(b) * cache_stride;
-  // scores: warp per key, all heads
-  for (int t = warp; t < nt; t += nw) {
-    float kv[VPL];
+  for (int h = warp; h < nh; h += nw) {
+    float q[VPL];
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) kv[j] = kb[static_cast<size_t>(t0 + t) * HD + lane + 32 * j];
-    for (int h = 0; h < nh; ++h) {
+    for (int j = 0; j < VPL; ++j) q[j] = qs[h * HD + lane + 32 * j];
+    float mine = -INFINITY;
+    for (int t = 0; t < nt; ++t) {
       float d = 0.f;
 #pragma unroll
-      for (int j = 0; j < VPL; ++j) d += qs[h * HD + lane + 32 * j] * kv[j];
+      for (int j = 0; j < VPL; ++j) d += q[j] * ks[t * HD + lane + 32 * j];
       d = warp_sum(d);
-      if (lane == 0) sc[h * CK + t] = d;
+      if (lane == t) mine = d;
     }
-  }
-  __syncthreads();
-  // per-head max / exp / sum over this chunk
-  for (int h = warp; h < nh; h += nw) {
-    float m = -INFINITY;
-    for (int t = lane; t < nt; t += 32) m = fmaxf(m, sc[h * CK + t]);
-    m = warp_max(m);
-    float l = 0.f;
-    for (int t = lane; t < nt; t += 32) {
-      const float p = expf(sc[h * CK + t] - m);
-      sc[h * CK + t] = p;
-      l += p;
-    }
-    l = warp_sum(l);
+    const float m = warp_max(mine);
+    const float p = lane < nt ? expf(mine - m) : 0.f;
+    const float l = warp_sum(p);
+    ps[h * CK + lane] = p;
     if (lane == 0) {
       float* pm = part + ((static_cast<size_t>(b) * max_chunks + c) * nh + h) * (HD + 2);
       pm[HD] = m;
@@ -271,16 +302,15 @@ __global__ void attn_decode_partial_kernel(const float* __restrict__ q32, const 
     }
   }
   __syncthreads();
-  // P.V: thread per dimension, all heads
   for (int d = threadIdx.x; d < HD; d += blockDim.x) {
     float acc[16];
 #pragma unroll
     for (int h = 0; h < 16; ++h) acc[h] = 0.f;
     for (int t = 0; t < nt; ++t) {
-      const float vv = vb[static_cast<size_t>(t0 + t) * HD + d];
+      const float vv = vb[static_cast<size_t>(t) * HD + d];
 #pragma unroll
       for (int h = 0; h < 16; ++h)
-        if (h < nh) acc[h] += sc[h * CK + t] * vv;
+        if (h < nh) acc[h] += ps[h * CK + t] * vv;
     }
 #pragma unroll
     for (int h = 0; h < 16; ++h)
@@ -290,26 +320,31 @@ __global__ void attn_decode_partial_kernel(const float* __restrict__ q32, const 
 
 __global__ void attn_decode_merge_kernel(const float* __restrict__ part, const int32_t* __restrict__ pos_dev, int nh,
                                          int hd, int max_chunks, float* out) {
-  const int b = blockIdx.x;
+  sbd::griddep_launch_dependents();
+  const int b = blockIdx.x, h = blockIdx.y;
+  sbd::griddep_wait();
   const int nc = (pos_dev[b] + 1 + CK - 1) / CK;
-  for (int e = threadIdx.x; e < nh * hd; e += blockDim.x) {
-    const int h = e / hd, d = e - h * hd;
-    float M = -INFINITY;
-    for (int c = 0; c < nc; ++c) M = fmaxf(M, part[((static_cast<size_t>(b) * max_chunks + c) * nh + h) * (hd + 2) + hd]);
+  const float* base = part + (static_cast<size_t>(b) * max_chunks * nh + h) * (hd + 2);
+  const size_t cstride = static_cast<size_t>(nh) * (hd + 2);
+  float M = -INFINITY;
+  for (int c = 0; c < nc; ++c) M = fmaxf(M, base[c * cstride + hd]);
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     float L = 0.f, O = 0.f;
     for (int c = 0; c < nc; ++c) {
-      const float* pm = part + ((static_cast<size_t>(b) * max_chunks + c) * nh + h) * (hd + 2);
+      const float* pm = base + c * cstride;
       const float f = expf(pm[hd] - M);
       L += pm[hd + 1] * f;
       O += pm[d] * f;
     }
-    out[static_cast<size_t>(b) * nh * hd + e] = O / L;
+    out[(static_cast<size_t>(b) * nh + h) * hd + d] = O / L;
   }
 }
 
 // ---------------------------------------------------------------- step bookkeeping
 __global__ void step_advance_kernel(int32_t* pos, const int32_t* tokens, int32_t* cur, int32_t* history, int hist_len,
                                     int m) {
+  sbd::griddep_launch_dependents();
+  sbd::griddep_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= m) return;
   const int p = pos[b] + 1;
@@ -328,20 +363,24 @@ extern "C" int sb_embed_q4(const void* emb, const void* scales, int scale_dtype,
   SB_CHECK_ARG(scale_dtype == SB_SCALE_F16 || scale_dtype == SB_SCALE_F32, "sb_embed_q4: bad scale dtype");
   if (m == 0) return SB_OK;
   SB_CHECK_ARG(emb && scales && tokens && (out32 || out16), "sb_embed_q4: null pointer");
-  embed_kernel<<<m, kT, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t*>(emb), scales,
-                                                                scale_dtype == SB_SCALE_F16, group, tokens, k, mult,
-                                                                out32, static_cast<__half*>(out16));
+  cudaError_t e = sb::launch_pdl(embed_kernel, dim3(m), dim3(kT), 0, static_cast<cudaStream_t>(stream),
+                                 static_cast<const uint8_t*>(emb), scales, static_cast<int>(scale_dtype == SB_SCALE_F16),
+                                 group, tokens, k, mult, out32, static_cast<__half*>(out16));
+  if (e != cudaSuccess) return sb::cuda_fail(e, "embed_kernel");
   return sb::launch_status("embed_kernel");
 }
 
 extern "C" int sb_add_rmsnorm(const float* x, const void* y, int y_dtype, const float* w_add, const float* w_norm,
                               float* x_out, float* h_out, void* h16_out, int m, int n, float eps, void* stream) {
-  SB_CHECK_ARG(m >= 0 && n > 0 && n <= 32 * kT, "sb_add_rmsnorm: n=%d must be in 1..%d", n, 32 * kT);
+  SB_CHECK_ARG(m >= 0 && n > 0 && n % 4 == 0 && n <= 4 * kT * MAXV4, "sb_add_rmsnorm: n=%d must be a multiple of 4 in 4..%d",
+               n, 4 * kT * MAXV4);
   SB_CHECK_ARG(!y || y_dtype == SB_F16 || y_dtype == SB_F32, "sb_add_rmsnorm: bad y dtype");
   if (m == 0) return SB_OK;
   SB_CHECK_ARG(x && w_norm && (!y || w_add) && (h_out || h16_out), "sb_add_rmsnorm: null pointer");
-  add_rmsnorm_kernel<<<m, kT, 0, static_cast<cudaStream_t>(stream)>>>(x, y, y_dtype == SB_F16, w_add, w_norm, x_out,
-                                                                      h_out, static_cast<__half*>(h16_out), n, eps);
+  cudaError_t e = sb::launch_pdl(add_rmsnorm_kernel, dim3(m), dim3(kT), 0, static_cast<cudaStream_t>(stream), x, y,
+                                 static_cast<int>(y_dtype == SB_F16), w_add, w_norm, x_out, h_out,
+                                 static_cast<__half*>(h16_out), n, eps);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "add_rmsnorm_kernel");
   return sb::launch_status("add_rmsnorm_kernel");
 }
 
@@ -357,14 +396,16 @@ extern "C" int sb_qkv_prep(const void* qkv, int qkv_dtype, int ld, const float* 
   const dim3 block(32 * (n_heads + 2));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int f16 = qkv_dtype == SB_F16;
-#define SB_PREP(V)                                                                                                   \
-  qkv_prep_kernel<V><<<s, block, 0, st>>>(qkv, f16, ld, q_norm, k_norm, cos_t, sin_t, pos_dev, start_pos, n_heads, eps, \
-                                          static_cast<__half*>(q16), q32, k_cache, v_cache, static_cast<__half*>(k16), \
-                                          static_cast<__half*>(v16), cache_stride)
+  cudaError_t e;
+#define SB_PREP(V)                                                                                                \
+  e = sb::launch_pdl(qkv_prep_kernel<V>, dim3(s), block, 0, st, qkv, f16, ld, q_norm, k_norm, cos_t, sin_t, pos_dev, \
+                     start_pos, n_heads, eps, static_cast<__half*>(q16), q32, k_cache, v_cache,                   \
+                     static_cast<__half*>(k16), static_cast<__half*>(v16), cache_stride)
   if (head_dim == 64) SB_PREP(2);
   else if (head_dim == 128) SB_PREP(4);
   else SB_PREP(8);
 #undef SB_PREP
+  if (e != cudaSuccess) return sb::cuda_fail(e, "qkv_prep_kernel");
   return sb::launch_status("qkv_prep_kernel");
 }
 
@@ -374,8 +415,9 @@ extern "C" int sb_softmax_causal(const float* scores, int ld_s, int rows, int n_
   SB_CHECK_ARG(start_pos + (rows - 1) / n_heads < n_keys || rows == 0, "sb_softmax_causal: a query sees past n_keys");
   if (rows == 0) return SB_OK;
   SB_CHECK_ARG(scores && p16, "sb_softmax_causal: null pointer");
-  softmax_causal_kernel<<<rows, kT, 0, static_cast<cudaStream_t>(stream)>>>(scores, ld_s, n_heads, start_pos, n_keys,
-                                                                            static_cast<__half*>(p16), ld_p);
+  cudaError_t e = sb::launch_pdl(softmax_causal_kernel, dim3(rows), dim3(kT), 0, static_cast<cudaStream_t>(stream),
+                                 scores, ld_s, n_heads, start_pos, n_keys, static_cast<__half*>(p16), ld_p);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "softmax_causal_kernel");
   return sb::launch_status("softmax_causal_kernel");
 }
 
@@ -384,8 +426,9 @@ extern "C" int sb_geglu(const void* gu, int dtype, int m, int f, float* out32, v
   if (m == 0) return SB_OK;
   SB_CHECK_ARG(gu && (out32 || out16), "sb_geglu: null pointer");
   const size_t total = static_cast<size_t>(m) * f;
-  geglu_kernel<<<grid_for(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(gu, dtype == SB_F16, f, m, out32,
-                                                                                   static_cast<__half*>(out16));
+  cudaError_t e = sb::launch_pdl(geglu_kernel, dim3(grid_for(total, 256)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                                 gu, static_cast<int>(dtype == SB_F16), f, m, out32, static_cast<__half*>(out16));
+  if (e != cudaSuccess) return sb::cuda_fail(e, "geglu_kernel");
   return sb::launch_status("geglu_kernel");
 }
 
@@ -407,17 +450,22 @@ extern "C" int sb_attn_decode(const float* q32, const float* k_cache, const floa
     return sb::fail(SB_ERR_WORKSPACE, "sb_attn_decode: workspace %zu < %zu bytes", workspace_bytes, need);
   const int max_chunks = (max_seq + CK - 1) / CK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const size_t smem = static_cast<size_t>(n_heads) * (head_dim + CK) * sizeof(float);
+  const size_t smem = (static_cast<size_t>(CK) * head_dim + static_cast<size_t>(n_heads) * (head_dim + CK)) * sizeof(float);
   const dim3 grid(m, max_chunks);
-#define SB_ATT(V) \
-  attn_decode_partial_kernel<V><<<grid, kT, smem, st>>>(q32, k_cache, v_cache, pos_dev, n_heads, cache_stride, workspace, max_chunks)
+  cudaError_t e;
+#define SB_ATT(V)                                                                                                  \
+  e = sb::launch_pdl(attn_decode_partial_kernel<V>, grid, dim3(kT), smem, st, q32, k_cache, v_cache, pos_dev, n_heads, \
+                     cache_stride, workspace, max_chunks)
   if (head_dim == 64) SB_ATT(2);
   else if (head_dim == 128) SB_ATT(4);
   else SB_ATT(8);
 #undef SB_ATT
+  if (e != cudaSuccess) return sb::cuda_fail(e, "attn_decode_partial_kernel");
   int rc = sb::launch_status("attn_decode_partial_kernel");
   if (rc) return rc;
-  attn_decode_merge_kernel<<<m, kT, 0, st>>>(workspace, pos_dev, n_heads, head_dim, max_chunks, out);
+  e = sb::launch_pdl(attn_decode_merge_kernel, dim3(m, n_heads), dim3(head_dim), 0, st,
+                     static_cast<const float*>(workspace), pos_dev, n_heads, head_dim, max_chunks, out);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "attn_decode_merge_kernel");
   return sb::launch_status("attn_decode_merge_kernel");
 }
 
@@ -426,7 +474,8 @@ extern "C" int sb_step_advance(int32_t* pos, const int32_t* tokens, int32_t* cur
   SB_CHECK_ARG(m >= 0, "sb_step_advance: bad m");
   if (m == 0) return SB_OK;
   SB_CHECK_ARG(pos && tokens && cur, "sb_step_advance: null pointer");
-  step_advance_kernel<<<(m + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(pos, tokens, cur, history,
-                                                                                     hist_len, m);
+  cudaError_t e = sb::launch_pdl(step_advance_kernel, dim3((m + 127) / 128), dim3(128), 0,
+                                 static_cast<cudaStream_t>(stream), pos, tokens, cur, history, hist_len, m);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "step_advance_kernel");
   return sb::launch_status("step_advance_kernel");
 }

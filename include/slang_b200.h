@@ -210,7 +210,8 @@ int sb_qkv_prep(const void* qkv, int qkv_dtype, int ld, const float* q_norm, con
 int sb_softmax_causal(const float* scores, int ld_s, int rows, int n_heads, int start_pos,
                       int n_keys, void* p16, int ld_p, void* stream);
 
-/* out[r, i] = gelu_tanh(gu[r, i]) * gu[r, f + i] (gate rows then up rows).
+/* out[r, i] = gelu_tanh(gu[r, 2i]) * gu[r, 2i + 1]: the fused gate|up weight keeps
+ * gate row i and up row i adjacent, so its output interleaves them.
  * Replaces geglu_b (gemma4_150/kernels_dsl.py:259) / gemma4/reference.py:148-150. */
 int sb_geglu(const void* gu, int dtype, int m, int f, float* out32, void* out16, void* stream);
 
@@ -228,6 +229,42 @@ size_t sb_attn_decode_workspace_size(int m, int n_heads, int head_dim, int max_s
  * Replaces the blit of the argmax token into gen[step] (gemma4_150/metal_runner.py:394-398). */
 int sb_step_advance(int32_t* pos, const int32_t* tokens, int32_t* cur, int32_t* history,
                     int hist_len, int m, void* stream);
+
+/* One layer of the model for sb_decode_step_fused (device pointers). */
+typedef struct sb_decode_layer {
+  const void* w[4];        /* packed int4: q|k|v [nqkv, H/2], o [H, qd/2],
+                              gate|up with rows interleaved [2F, H/2], down [H, F/2] */
+  const void* s[4];        /* their f16 group-32 scales [rows, K/32] */
+  const float* in_norm;
+  const float* q_norm;
+  const float* k_norm;
+  const float* post_attn_norm;
+  const float* pre_ffn_norm;
+  const float* post_ffn_norm;
+  float* k_cache;          /* [max_seq][head_dim] f32 */
+  float* v_cache;
+} sb_decode_layer;
+
+/*
+ * One greedy decode step for a single sequence as one persistent cooperative
+ * kernel (one CTA per SM): embed cur[0] at position pos[0], all layers, final
+ * norm, tied lm_head argmax; then tokens[0] = next token, cur[0] = it,
+ * pos[0] += 1 and history[pos[0]] = it.  Same arithmetic as the per-op path
+ * (sb_embed_q4 ... sb_lmhead_argmax).  Replaces the whole per-token dispatch
+ * chain of G4._forward (gemma4_150/metal_runner.py:372-402).
+ * Requirements: head_dim 256, n_heads <= 8, hidden, inter, n_heads*256 <= 6144
+ * and multiples of 32, f16 group-32 scales.  layers_dev: device array of
+ * n_layers sb_decode_layer.  scratch: >= sb_decode_step_fused_scratch_size()
+ * bytes, zero-filled before the first call (later calls leave it reusable);
+ * keys receives the lm_head key as in sb_lmhead_argmax.
+ */
+int sb_decode_step_fused(const void* layers_dev, int n_layers, const void* emb, const void* emb_scales,
+                         const float* final_norm, const float* cos_t, const float* sin_t, int hidden,
+                         int n_heads, int head_dim, int inter, int vocab, int max_seq, float eps,
+                         float embed_scale, int32_t* pos, int32_t* cur, int32_t* tokens,
+                         int32_t* history, int hist_len, uint64_t* keys, void* scratch,
+                         size_t scratch_bytes, void* stream);
+size_t sb_decode_step_fused_scratch_size(int hidden, int n_heads, int head_dim, int inter, int max_seq);
 
 #ifdef __cplusplus
 }

@@ -40,6 +40,9 @@ SIGNATURES = {
     "sb_attn_decode": ([_vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _vp, _vp, _sz, _vp], _i),
     "sb_attn_decode_workspace_size": ([_i, _i, _i, _i], _sz),
     "sb_step_advance": ([_vp, _vp, _vp, _vp, _i, _i, _vp], _i),
+    "sb_decode_step_fused": ([_vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _f, _vp, _vp, _vp,
+                              _vp, _i, _vp, _vp, _sz, _vp], _i),
+    "sb_decode_step_fused_scratch_size": ([_i, _i, _i, _i, _i], _sz),
 }
 
 

@@ -231,7 +231,7 @@ __global__ void softmax_causal_kernel(const float* __restrict__ scores, int ld_s
 }
 
 // ---------------------------------------------------------------- GEGLU
-// out[r, i] = gelu_tanh(gu[r, i]) * gu[r, f + i]
+// out[r, i] = gelu_tanh(gu[r, 2i]) * gu[r, 2i + 1]  (gate and up rows interleaved)
 __global__ void geglu_kernel(const void* __restrict__ gu, int gu_f16, int f, int rows, float* out32, __half* out16) {
   sbd::griddep_launch_dependents();
   sbd::griddep_wait();
@@ -239,8 +239,8 @@ __global__ void geglu_kernel(const void* __restrict__ gu, int gu_f16, int f, int
   for (size_t e = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const size_t r = e / f, i = e - r * f;
-    const float g = load_act(gu, gu_f16, r * 2 * f + i);
-    const float u = load_act(gu, gu_f16, r * 2 * f + f + i);
+    const float g = load_act(gu, gu_f16, r * 2 * f + 2 * i);
+    const float u = load_act(gu, gu_f16, r * 2 * f + 2 * i + 1);
     const float v = gelu_tanh(g) * u;
     if (out32) out32[e] = v;
     if (out16) out16[e] = __float2half_rn(v);

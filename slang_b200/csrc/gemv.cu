@@ -28,6 +28,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "q4_dot.cuh"
 
 namespace {
 
@@ -71,59 +72,6 @@ __device__ __forceinline__ uint32_t orderable(float f) {
 __device__ __forceinline__ unsigned long long make_key(float v, long long idx) {
   return (static_cast<unsigned long long>(orderable(v)) << 32) |
          static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(idx));
-}
-
-// x of one group (32 values) as the DP4A operands: 4 words x {hi even, hi odd,
-// lo even, lo odd} bytes, plus -8 * sum(x_int) and the group's scale.
-struct XGroup {
-  uint32_t he[4], ho[4], le[4], lo[4];
-  int bias;
-  float sx;
-};
-
-__device__ __forceinline__ void quantise_group(const float (&v)[32], XGroup& g) {
-  float mx = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(v[i]));
-  const float inv = mx > 0.f ? 32767.f / mx : 0.f;
-  g.sx = mx / 32767.f;
-  int sum = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint32_t he = 0, ho = 0, le = 0, lo = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int xe = __float2int_rn(v[8 * j + 2 * i] * inv);
-      const int xo = __float2int_rn(v[8 * j + 2 * i + 1] * inv);
-      sum += xe + xo;
-      he |= (static_cast<uint32_t>(xe >> 8) & 0xFFu) << (8 * i);
-      ho |= (static_cast<uint32_t>(xo >> 8) & 0xFFu) << (8 * i);
-      le |= (static_cast<uint32_t>(xe) & 0xFFu) << (8 * i);
-      lo |= (static_cast<uint32_t>(xo) & 0xFFu) << (8 * i);
-    }
-    g.he[j] = he;
-    g.ho[j] = ho;
-    g.le[j] = le;
-    g.lo[j] = lo;
-  }
-  g.bias = -8 * sum;
-}
-
-// exact integer dot of 32 int4 codes (minus 8) with the group's x_int
-// (four independent accumulation chains for instruction-level parallelism)
-__device__ __forceinline__ int dot_group(const uint4 q, const XGroup& g) {
-  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-  int he = 0, ho = 0, le = g.bias, lo = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t e = w[j] & 0x0F0F0F0Fu;
-    const uint32_t o = (w[j] >> 4) & 0x0F0F0F0Fu;
-    he = sbd::dp4a_us(e, g.he[j], he);
-    ho = sbd::dp4a_us(o, g.ho[j], ho);
-    le = sbd::dp4a_uu(e, g.le[j], le);
-    lo = sbd::dp4a_uu(o, g.lo[j], lo);
-  }
-  return (he + ho) * 256 + le + lo;
 }
 
 template <int M, int GPL, bool SF16, int EPI>
@@ -184,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
   // x is the previous kernel's output: wait for it (weights are already streaming)
   sbd::griddep_wait();
   // this lane's groups of x, quantised once (kept in registers)
-  XGroup xg[M][GPL];
+  sbd::XGroup xg[M][GPL];
 #pragma unroll
   for (int m = 0; m < M; ++m) {
 #pragma unroll
@@ -217,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
           }
         }
       }
-      quantise_group(v, xg[m][u]);
+      sbd::quantise_group(v, xg[m][u]);
     }
   }
 
@@ -269,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
           }
 #pragma unroll
           for (int m = 0; m < M; ++m)
-            acc[m] = fmaf(static_cast<float>(dot_group(q, xg[m][u])), sw * xg[m][u].sx, acc[m]);
+            acc[m] = fmaf(static_cast<float>(sbd::dot_group(q, xg[m][u])), sw * xg[m][u].sx, acc[m]);
         }
       }
 #pragma unroll

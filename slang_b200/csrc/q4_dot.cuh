@@ -1,0 +1,68 @@
+// Exact dot products of packed int4 codes with 16-bit-quantised activations,
+// shared by the GEMV kernels.  A group is 32 consecutive values (16 bytes of
+// nibbles, low nibble first).  The activation group is rounded to integers
+// x_int = rint(x * 32767 / max|x|) (error <= 2^-16 of the group's max), split
+// into a signed high byte and an unsigned low byte, and arranged to line up with
+// the even (low) and odd (high) nibbles of each 32-bit word, so that
+//   sum (q - 8) * x_int = 256 * dot(q, hi) + dot(q, lo) - 8 * sum(x_int)
+// is computed exactly with DP4A in 32-bit integers.
+#pragma once
+
+#include "common.cuh"
+
+namespace sbd {
+
+// x of one group as DP4A operands: 4 words x {hi even, hi odd, lo even, lo odd}
+// bytes, -8 * sum(x_int), and the group's scale max|x| / 32767.
+struct XGroup {
+  uint32_t he[4], ho[4], le[4], lo[4];
+  int bias;
+  float sx;
+};
+
+__device__ __forceinline__ void quantise_group(const float (&v)[32], XGroup& g) {
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(v[i]));
+  const float inv = mx > 0.f ? 32767.f / mx : 0.f;
+  g.sx = mx / 32767.f;
+  int sum = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t he = 0, ho = 0, le = 0, lo = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int xe = __float2int_rn(v[8 * j + 2 * i] * inv);
+      const int xo = __float2int_rn(v[8 * j + 2 * i + 1] * inv);
+      sum += xe + xo;
+      he |= (static_cast<uint32_t>(xe >> 8) & 0xFFu) << (8 * i);
+      ho |= (static_cast<uint32_t>(xo >> 8) & 0xFFu) << (8 * i);
+      le |= (static_cast<uint32_t>(xe) & 0xFFu) << (8 * i);
+      lo |= (static_cast<uint32_t>(xo) & 0xFFu) << (8 * i);
+    }
+    g.he[j] = he;
+    g.ho[j] = ho;
+    g.le[j] = le;
+    g.lo[j] = lo;
+  }
+  g.bias = -8 * sum;
+}
+
+// Exact integer dot of 32 int4 codes (minus 8) with the group's x_int, in four
+// independent accumulation chains for instruction-level parallelism.
+__device__ __forceinline__ int dot_group(const uint4 q, const XGroup& g) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+  int he = 0, ho = 0, le = g.bias, lo = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t e = w[j] & 0x0F0F0F0Fu;
+    const uint32_t o = (w[j] >> 4) & 0x0F0F0F0Fu;
+    he = dp4a_us(e, g.he[j], he);
+    ho = dp4a_us(o, g.ho[j], ho);
+    le = dp4a_uu(e, g.le[j], le);
+    lo = dp4a_uu(o, g.lo[j], lo);
+  }
+  return (he + ho) * 256 + le + lo;
+}
+
+}  // namespace sbd

@@ -44,6 +44,12 @@ def rope_tables(max_pos: int, head_dim: int, theta: float, cutoff: int) -> tuple
     return np.cos(ang, dtype=np.float32), np.sin(ang, dtype=np.float32)
 
 
+def _interleave(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    out = np.empty((a.shape[0] * 2,) + a.shape[1:], dtype=a.dtype)
+    out[0::2], out[1::2] = a, b
+    return out
+
+
 class DeviceModel:
     """The model's weights on one GPU in the layouts the kernels consume."""
 
@@ -67,7 +73,8 @@ class DeviceModel:
                 "qkv": (T(np.concatenate([L["q"][0], L["k"][0], L["v"][0]])),
                         T(np.concatenate([L["q"][1], L["k"][1], L["v"][1]]))),
                 "o": (T(L["o"][0]), T(L["o"][1])),
-                "gu": (T(np.concatenate([L["gate"][0], L["up"][0]])), T(np.concatenate([L["gate"][1], L["up"][1]]))),
+                # gate row i and up row i adjacent: GEGLU pairs neighbouring outputs
+                "gu": (T(_interleave(L["gate"][0], L["up"][0])), T(_interleave(L["gate"][1], L["up"][1]))),
                 "down": (T(L["down"][0]), T(L["down"][1])),
             }
             for n in ("in_norm", "q_norm", "k_norm", "post_attn_norm", "pre_ffn_norm", "post_ffn_norm"):
@@ -78,9 +85,12 @@ class DeviceModel:
 
 
 class Runner:
-    def __init__(self, dm: DeviceModel, batch: int = 1):
+    def __init__(self, dm: DeviceModel, batch: int = 1, fused: bool = False):
         if batch < 1 or batch > 8:
             raise ValueError("the GEMV decode path serves 1..8 sequences")
+        if fused and batch != 1:
+            raise ValueError("the persistent decode kernel serves one sequence")
+        self.fused = fused
         self.dm = dm
         cfg = dm.cfg
         self.B = batch
@@ -109,6 +119,8 @@ class Runner:
         ws = _lib.load().sb_attn_decode_workspace_size(B, self.nh, self.hd, S)
         self.attn_ws = torch.empty(max(1, ws // 4), dtype=torch.float32, device=dev)
         self.stream = torch.cuda.Stream(device=dev)
+        if fused:
+            self._fused_setup()
         self.graph = None
         self._pf = None  # prefill buffers, sized on first use
         self._pgraphs: dict = {}  # (prompt length, sequence) -> captured prefill
@@ -149,23 +161,51 @@ class Runner:
                   self.history.data_ptr(), self.max_seq, B, s)
         del lib
 
+    def _fused_setup(self):
+        dm, dev = self.dm, self.dm.device
+        rows = []
+        for li, L in enumerate(dm.layers):
+            ptrs = [L[k][0].data_ptr() for k in ("qkv", "o", "gu", "down")]
+            ptrs += [L[k][1].data_ptr() for k in ("qkv", "o", "gu", "down")]
+            ptrs += [L[n].data_ptr() for n in ("in_norm", "q_norm", "k_norm", "post_attn_norm", "pre_ffn_norm",
+                                                "post_ffn_norm")]
+            ptrs += [self.kc[li].data_ptr(), self.vc[li].data_ptr()]
+            rows.append(ptrs)
+        self.layer_table = torch.tensor(rows, dtype=torch.int64, device=dev)
+        need = _lib.load().sb_decode_step_fused_scratch_size(self.H, self.nh, self.hd, self.F, self.max_seq)
+        if need == 0:
+            raise ValueError("this model shape is not supported by the persistent decode kernel")
+        self.fused_scratch = torch.zeros(need, dtype=torch.uint8, device=dev)
+
+    def _fused_ops(self):
+        dm = self.dm
+        _lib.call("sb_decode_step_fused", self.layer_table.data_ptr(), len(dm.layers), dm.embed_q.data_ptr(),
+                  dm.embed_s.data_ptr(), dm.final_norm.data_ptr(), dm.cos.data_ptr(), dm.sin.data_ptr(), self.H,
+                  self.nh, self.hd, self.F, dm.cfg["vocab"], self.max_seq, self.eps, float(dm.cfg["embed_scale"]),
+                  self.pos.data_ptr(), self.cur.data_ptr(), self.tok.data_ptr(), self.history.data_ptr(),
+                  self.max_seq, self.keys.data_ptr(), self.fused_scratch.data_ptr(), self.fused_scratch.numel(),
+                  kern._stream())
+
     def kernel_launches_per_step(self) -> int:
+        if self.fused:
+            return 1
         nL = len(self.dm.layers)
         per_layer = 4 + 1 + 2 + 2 + 1  # 4 GEMVs, prep, attention (2), add+norm (2), geglu
         return 2 + nL * per_layer + 2 + 1  # embed + first norm, layers, lm_head (gemv + tokens), advance
 
     def capture(self):
         """Warm up, then capture one decode step as a CUDA graph."""
+        ops = self._fused_ops if self.fused else self._decode_ops
         with torch.cuda.stream(self.stream):
             saved = (self.pos.clone(), self.cur.clone(), self.history.clone())
-            self._decode_ops()  # first calls set kernel attributes outside capture
+            ops()  # first calls set kernel attributes outside capture
             self.pos.copy_(saved[0])
             self.cur.copy_(saved[1])
             self.history.copy_(saved[2])
         torch.cuda.synchronize(self.dm.device)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=self.stream):
-            self._decode_ops()
+            ops()
         return self.graph
 
     def decode_step(self):
@@ -338,12 +378,12 @@ class Runner:
 
 
 def greedy_generate(model: dict, prompt, steps: int, device="cuda:0", batched_prefill: bool = True,
-                    max_seq: int | None = None) -> list[int]:
+                    max_seq: int | None = None, fused: bool = False) -> list[int]:
     """Prefill `prompt`, then greedy-decode until `steps` tokens exist (the first
     comes from the prefill's last position), as the reference's generate loop does."""
     S = len(prompt)
     dm = DeviceModel(model, device, max_seq or (S + steps + 1))
-    r = Runner(dm, 1)
+    r = Runner(dm, 1, fused=fused)
     first = r.prefill(prompt) if batched_prefill else r.prefill_tokenwise(prompt)
     if not batched_prefill:
         r.set_state([first], [S])

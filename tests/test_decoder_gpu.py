@@ -78,6 +78,31 @@ def test_batch_of_sequences_is_independent(cuda, golden):
         assert [firsts[b]] + rest[b].tolist() == singles[b]
 
 
+def mid_model():
+    """Full-width layers (hidden 1536, 8 heads of 256, FFN 6144) but 3 layers and a 16384-row vocabulary."""
+    return synth.random_model(synth.e2b_config(n_layers=3, vocab=16384), seed=21)
+
+
+def test_fused_decode_matches_per_op_path_and_oracle(cuda):
+    model = mid_model()
+    prompt = synth.prompt_tokens(40, 16384, seed=22)
+    per_op = runner.greedy_generate(model, prompt, 48, device=cuda, max_seq=128)
+    fused = runner.greedy_generate(model, prompt, 48, device=cuda, max_seq=128, fused=True)
+    assert fused == per_op
+    # token-wise prefill through the persistent kernel: KV caches vs the numpy oracle
+    dm = runner.DeviceModel(model, cuda, 64)
+    r = runner.Runner(dm, 1, fused=True)
+    r.prefill_tokenwise(prompt[:20])
+    torch.cuda.synchronize()
+    o = odec.OracleDecoder(model, 64)
+    for p_, t in enumerate(prompt[:20]):
+        o.forward(t, p_)
+    for li in range(3):
+        for got, ref in ((r.kc[li][0, :20], o.k_cache[li][:20]), (r.vc[li][0, :20], o.v_cache[li][:20])):
+            rel = np.linalg.norm(got.cpu().numpy() - ref) / np.linalg.norm(ref)
+            assert rel < 2e-4, f"layer {li}: KV rel-L2 {rel:.2e}"
+
+
 @pytest.fixture(scope="module")
 def cfg4():
     path = os.path.join(GOLD, "golden_cfg4.npz")
@@ -89,13 +114,13 @@ def cfg4():
     return g, model, prompt
 
 
-@pytest.mark.parametrize("batched", [True, False])
-def test_config4_256_greedy_tokens_match_reference(cuda, cfg4, batched):
+@pytest.mark.parametrize("batched,fused", [(True, False), (False, False), (True, True)])
+def test_config4_256_greedy_tokens_match_reference(cuda, cfg4, batched, fused):
     g, model, prompt = cfg4
     steps = len(g["cfg4_tokens"])
     S = len(prompt)
     dm = runner.DeviceModel(model, cuda, S + steps + 1)
-    r = runner.Runner(dm, 1)
+    r = runner.Runner(dm, 1, fused=fused)
     first = r.prefill(prompt) if batched else r.prefill_tokenwise(prompt)
     tops = [float(_key_value(r.keys.cpu().numpy())[0])]
     if not batched:
@@ -112,6 +137,6 @@ def test_config4_256_greedy_tokens_match_reference(cuda, cfg4, batched):
     cap = 30.0
     got = cap * np.tanh(np.array(tops) / cap)
     err = np.abs(got - g["cfg4_top"]).max()
-    print(f"config 4 batched={batched}: max |top logit - reference| = {err:.3e}")
+    print(f"config 4 batched={batched} fused={fused}: max |top logit - reference| = {err:.3e}")
     # f16 activations in the batched prefill GEMMs vs the f32 token-wise path
     assert err < (5e-2 if batched else 5e-3)

@@ -2,23 +2,26 @@
 // sequence as ONE persistent cooperative kernel (sb_decode_step_fused).
 //
 // Why: a step is ~35 x 10 small dependent operations; as separate launches the
-// step is dominated by launch and ramp latency, not by the ~1 GB of weights
+// step is dominated by launch and ramp latency, not by the ~0.9 GB of weights
 // it must stream.  Here every SM runs one CTA for the whole step:
 //
 //   producer warp   walks this CTA's fixed sequence of weight row-slices --
 //                   per layer its rows of q|k|v, o, gate|up (rows interleaved
 //                   gate/up), down, then its rows of the tied lm_head -- and
 //                   streams them (packed rows + their f16 group scales) with
-//                   cp.async.bulk into a 6-deep shared-memory ring.  Weights do
-//                   not depend on activations, so the stream runs ahead across
-//                   the phase barriers below.
+//                   cp.async.bulk into a shared-memory ring.  Weights do not
+//                   depend on activations, so the stream runs ahead across the
+//                   phase barriers below.
 //   8 consumer warps  run the phases, separated by grid-wide barriers:
 //     qkv:    x = layer input (embedding, or residual + post-FFN RMSNorm of
-//             the previous down output), h = RMSNorm(x) * in_norm, GEMV rows
-//     attn:   per 32-key chunk (one chunk per CTA): q/k norm + RoPE (the last
-//             chunk's CTA also writes k, v of this position to the cache),
+//             the previous down output), h = RMSNorm(x) * in_norm, GEMV rows.
+//             Also starts the bulk copy of this CTA's attention chunk (16 keys
+//             of K and V, q/k norm weights, this position's RoPE row) so it
+//             lands while the GEMV and the barrier run.
+//     attn:   per 16-key chunk (one chunk per CTA): q/k norm + RoPE (the CTA
+//             owning this position's chunk also writes k, v to the cache),
 //             scores, chunk softmax partials, P.V partials
-//     merge:  per (head, 64 dims): rescale the chunk partials -> attention out
+//     merge:  per (head, 16 dims): rescale the chunk partials -> attention out
 //     o:      GEMV rows of o over the attention output
 //     gateup: x += RMSNorm(o) * post_attn, h = RMSNorm(x) * pre_ffn, GEMV rows,
 //             GEGLU of each interleaved (gate, up) row pair
@@ -27,10 +30,17 @@
 //   (max, lowest index) per CTA, one 64-bit atomicMax per CTA, and block 0
 //   decodes the token and advances pos / cur / history.
 //
+// Latency, not bandwidth, bounds this kernel (a phase moves ~20 MB over 148
+// SMs), so every phase is written as few dependent global round trips as
+// possible: each thread issues all of its loads of a phase input before using
+// any, values produced inside the launch are read with ld.global.cg (L2, never
+// a stale L1 line), the next layer's norm vectors are prefetched into L2, and
+// the grid barrier is one 64-bit atomic per CTA on a monotonic counter.
+//
 // GEMV arithmetic is the exact int4 x int16 DP4A dot of q4_dot.cuh.  Every wait
 // (mbarrier or grid barrier) is bounded by %globaltimer; a timeout raises a
-// global abort flag that every CTA polls, writes SB_ERR_TIMEOUT to the device
-// error word, and the kernel unwinds.
+// sticky abort flag in the scratch header that every CTA polls, writes
+// SB_ERR_TIMEOUT to the device error word, and the kernel unwinds.
 #include <algorithm>
 #include <mutex>
 
@@ -41,16 +51,27 @@ namespace {
 
 constexpr int kCons = 256;            // consumer threads (8 warps)
 constexpr int kThreads = kCons + 32;  // + one producer warp
-constexpr int kRing = 6;
+constexpr int kRing = 5;
 constexpr int kStageW = 24 * 1024;
 constexpr int kStageS = 3 * 1024;
 constexpr int kMaxK = 6144;           // longest GEMV row (values)
+constexpr int kMaxH = 2048;           // hidden size and n_heads * head_dim limit
 constexpr int HD = 256;               // head_dim handled by this kernel
-constexpr int CKA = 32;               // keys per attention work item
+constexpr int CKA = 16;               // keys per attention work item
 constexpr int kMaxHeads = 8;
+constexpr int kMaxChunks = 2048;      // max_seq <= CKA * kMaxChunks
+constexpr int kMergeDims = 16;        // attention output dims per merge work item
+constexpr int kMaxG = kMaxK / 32;     // activation groups of the longest GEMV row
+constexpr int kPasses = kMaxK / (8 * kCons);  // 8-value slots per thread for the longest row
+constexpr int kMaxLayers = 48;
 constexpr int kRed = 128;
 constexpr int kSegOut = 512;          // rows of one CTA's gate|up slice kept for GEGLU
-constexpr unsigned int kTraceLen = 512;  // [0] count, then timestamps
+constexpr unsigned int kTraceLen = 1024;  // per CTA: [0] count, then tagged timestamps
+constexpr int kTraceCtas = 160;           // trace slots (CTAs beyond this are not traced)
+static_assert(kCons == HD, "the P.V step maps one thread to one head dim");
+static_assert(CKA == 16, "the score reduction is written for 16-key chunks");
+static_assert(2 * kMaxChunks + kCons <= 2 * CKA * HD, "merge scratch must fit the K/V chunk buffer");
+static_assert(kMaxH == 8 * kCons, "a hidden vector is one 8-value slot per consumer thread");
 
 struct Layer {
   const uint8_t* w[4];  // 0 q|k|v [nqkv, H/2], 1 o [H, qd/2], 2 gate|up interleaved [2F, H/2], 3 down [H, F/2]
@@ -82,30 +103,60 @@ struct Params {
   int hist_len;
   unsigned long long* keys;
   float *xa, *xb, *qkv, *attn, *o, *a, *d, *part;
-  unsigned int* bar;  // [0] arrivals, [1] generation, [2] abort
-  unsigned long long* trace;  // optional: block 0 stamps %globaltimer at entry and after each barrier
+  unsigned long long* ctr;    // grid barrier: arrivals since the scratch was zeroed
+  unsigned int* bar;          // [2] sticky abort flag, [3] trace switch
+  unsigned long long* trace;  // optional: per CTA, tagged %globaltimer stamps
   int* err;
+};
+
+// The GEMV input vector, quantised per 32-value group (q4_dot.cuh's XGroup,
+// stored structure-of-arrays so that lanes reading consecutive groups hit
+// consecutive banks): w[0..3] hi bytes of even values, w[4..7] hi odd, w[8..11]
+// lo even, w[12..15] lo odd, then -8 * sum and the group's scale.
+struct XQ {
+  uint32_t w[16][kMaxG];
+  int bias[kMaxG];
+  float sx[kMaxG];
 };
 
 struct Smem {
   uint8_t w[kRing][kStageW];
   uint8_t s[kRing][kStageS];
-  // [0, kMaxK): the phase input, stored transposed (element i at (i % 32) * G + i / 32);
-  // [kMaxK, 2 kMaxK): a second vector.  The attention phase reuses both as scratch.
-  float va[2 * kMaxK];
+  Layer layers[kMaxLayers];
+  XQ xq;
+  float vb[kMaxH];           // q heads in the attention phase
+  float kv[2][CKA][HD];      // K and V rows of one attention chunk; merge scratch
+  float qn[HD], kn[HD];      // q / k norm weights
+  float cs[HD / 2], sn[HD / 2];  // RoPE row of this position
+  float kpos[HD], vpos[HD];  // k and v of this position
+  float ps[kMaxHeads][CKA];  // chunk softmax numerators
   float red[2][kRed];
   float seg_out[kSegOut];
   unsigned long long best[8];
   uint64_t full[kRing];
   uint64_t empty[kRing];
+  uint64_t kvbar;
   int flag;
+  unsigned int trace_n;
+  Params prm;  // the launch parameters, for the out-of-line phase functions
 };
 
+// The CTA's shared memory.  Out-of-line functions take it (and the launch
+// parameters) from here rather than through a pointer argument, so their
+// accesses compile to shared-memory instructions, not generic ones.
+__device__ __forceinline__ Smem& smem() {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  return *reinterpret_cast<Smem*>(smem_raw);
+}
+
 // ---------------------------------------------------------------- small helpers
-__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
+}
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -118,16 +169,30 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 __device__ __forceinline__ void cons_sync() { sbd::named_bar_sync(1, kCons); }
+// consumer barrier that also ORs a flag over the consumer threads
+__device__ __forceinline__ bool cons_sync_or(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "n"(kCons)
+      : "memory");
+  return r != 0;
+}
 
-// sum over the consumer threads
-__device__ float cons_sum(float v, Smem& sm) {
-  v = warp_sum(v);
+// sum (or max) over the consumer threads
+template <bool MAX>
+__device__ float cons_reduce(float v, Smem& sm) {
+  v = MAX ? warp_max(v) : warp_sum(v);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   cons_sync();
   if (lane == 0) sm.red[0][warp] = v;
   cons_sync();
-  float t = lane < kCons / 32 ? sm.red[0][lane] : 0.f;
-  return warp_sum(t);
+  const float t = lane < kCons / 32 ? sm.red[0][lane] : (MAX ? -INFINITY : 0.f);
+  return MAX ? warp_max(t) : warp_sum(t);
 }
 
 __device__ __forceinline__ bool aborted(const Params& p) {
@@ -139,68 +204,94 @@ __device__ __forceinline__ void raise_abort(const Params& p) {
   atomicExch(p.err, SB_ERR_TIMEOUT);
 }
 
-// The global abort flag is an L2 round trip: poll it only once a wait has
-// lasted this long, so normal waits wake up as soon as their condition holds.
+// The abort flag is an L2 round trip: poll it only once a wait has lasted this
+// long, so normal waits wake up as soon as their condition holds.
 constexpr uint64_t kAbortPollNs = 20000;
 
-// mbarrier wait that also gives up when another CTA raised the global abort
-__device__ bool ring_wait(uint64_t* bar, uint32_t parity, const Params& p) {
+// mbarrier wait that also gives up when another CTA raised the abort flag.
+// `fail` is the calling thread's sticky failure flag: once set, waits return
+// false at once, so a failing CTA runs through the rest of its phase (on
+// garbage, still joining every consumer barrier) to the next grid barrier,
+// where the consumers agree to leave together.
+__device__ bool ring_wait(uint64_t* bar, uint32_t parity, const Params& p, bool& fail) {
+  if (fail) return false;
   if (sbd::mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = sbd::global_ns();
   while (!sbd::mbar_try_wait(bar, parity)) {
     const uint64_t dt = sbd::global_ns() - t0;
-    if (dt > kAbortPollNs && aborted(p)) return false;
+    if (dt > kAbortPollNs && aborted(p)) {
+      fail = true;
+      return false;
+    }
     if (dt > sbd::kWaitLimitNs) {
       raise_abort(p);
+      fail = true;
       return false;
     }
   }
   return true;
 }
 
-// Grid-wide barrier among the consumer warps of every CTA (the producer warp
-// never joins: it may be blocked on a ring slot the consumers will free only
-// after this barrier).  Bounded spin; false when the step was aborted.
-__device__ bool grid_sync(const Params& p, Smem& sm) {
-  cons_sync();
-  if (threadIdx.x == 0) {
-    bool ok = !aborted(p);
-    if (ok) {
-      __threadfence();
-      const unsigned int gen = ld_acquire(p.bar + 1);
-      const unsigned int arrived = atomicAdd(p.bar, 1u);
-      if (arrived == gridDim.x - 1) {
-        atomicExch(p.bar, 0u);
-        __threadfence();
-        atomicAdd(p.bar + 1, 1u);
-      } else {
-        const uint64_t t0 = sbd::global_ns();
-        while (ld_acquire(p.bar + 1) == gen) {
-          const uint64_t dt = sbd::global_ns() - t0;
-          if (dt > kAbortPollNs && aborted(p)) {
-            ok = false;
-            break;
-          }
-          if (dt > sbd::kWaitLimitNs) {
-            raise_abort(p);
-            ok = false;
-            break;
-          }
-        }
-      }
-      __threadfence();
-    }
-    sm.flag = ok;
-    if (p.trace && blockIdx.x == 0) {
-      const unsigned int n = static_cast<unsigned int>(p.trace[0]) + 1;
-      if (n < kTraceLen) {
-        p.trace[n] = sbd::global_ns();
-        p.trace[0] = n;
-      }
+// Trace stamp by thread 0 of a CTA: (tag << 56) | %globaltimer.
+enum { TR_ENTRY = 1, TR_ARRIVE = 2, TR_EXIT = 3, TR_INPUT = 4, TR_STAGE0 = 5, TR_GEMV = 6, TR_ATT_Q = 7,
+       TR_ATT_K = 8, TR_ATT_S = 9, TR_ATT_PV = 10 };
+// The count lives in shared memory (a global read per stamp would distort the
+// intervals being measured) and is written out as entry 0 at every stamp.
+__device__ void trace_stamp(const Params& p, unsigned int tag) {
+  if (p.trace && threadIdx.x == 0) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    unsigned int& n = reinterpret_cast<Smem*>(smem_raw)->trace_n;
+    unsigned long long* t = p.trace + static_cast<size_t>(blockIdx.x) * kTraceLen;
+    if (n + 1 < kTraceLen) {
+      ++n;
+      t[n] = (static_cast<unsigned long long>(tag) << 56) | (sbd::global_ns() & ((1ull << 56) - 1));
+      t[0] = n;
     }
   }
+}
+
+// Grid-wide barrier among the consumer warps of every CTA (the producer warp
+// never joins: it may be blocked on a ring slot the consumers will free only
+// after this barrier).  Each CTA adds 1 to a 64-bit counter that only grows
+// (every barrier adds exactly gridDim.x) and waits until it reaches the end of
+// its round.  Bounded spin; false (for every consumer thread of the CTA) when
+// any of them failed or the step was aborted.  A failing CTA raises the abort
+// flag instead of arriving, which releases the others within kAbortPollNs.
+__device__ __noinline__ bool grid_sync(bool& fail) {
+  Smem& sm = smem();
+  const Params& p = sm.prm;
+  if (cons_sync_or(fail)) {
+    if (threadIdx.x == 0) raise_abort(p);
+    fail = true;
+    return false;
+  }
+  if (threadIdx.x == 0) {
+    trace_stamp(p, TR_ARRIVE);
+    bool ok = true;
+    __threadfence();
+    const unsigned long long old = atomicAdd(p.ctr, 1ull);
+    const unsigned long long target = (old / gridDim.x + 1) * gridDim.x;
+    if (ld_acquire64(p.ctr) < target) {
+      const uint64_t t0 = sbd::global_ns();
+      while (ld_acquire64(p.ctr) < target) {
+        const uint64_t dt = sbd::global_ns() - t0;
+        if (dt > kAbortPollNs && aborted(p)) {
+          ok = false;
+          break;
+        }
+        if (dt > sbd::kWaitLimitNs) {
+          raise_abort(p);
+          ok = false;
+          break;
+        }
+      }
+    }
+    sm.flag = ok;
+    trace_stamp(p, TR_EXIT);
+  }
   cons_sync();
-  return sm.flag != 0;
+  if (sm.flag == 0) fail = true;
+  return !fail;
 }
 
 // ---------------------------------------------------------------- weight segments
@@ -219,39 +310,32 @@ __device__ __forceinline__ Seg segment(int n, int k) {
   return s;
 }
 
-struct Plan {
-  int gpl, ks;
-};
-__device__ __forceinline__ Plan plan_for(int k) {
-  const int G = k / 32;
-  Plan best{1, 16};
-  int waste = 1 << 30;
-  const int prefs[4] = {3, 2, 4, 1};
-  for (int i = 0; i < 4; ++i) {
-    int ks = 1;
-    while (16 * prefs[i] * ks < G && ks < 16) ks *= 2;
-    if (16 * prefs[i] * ks < G) continue;
-    const int w = 16 * prefs[i] * ks - G;
-    if (w < waste) {
-      waste = w;
-      best = {prefs[i], ks};
-    }
-  }
-  return best;
+// GEMV work split: 16 half-warps, each lane owning GPL 32-value groups of
+// one of `ks` K slices, so 16 * GPL * ks >= K / 32.  Two shapes of code (GPL 3
+// for K = 1536 and 6144, GPL 4 for K = 2048, both without idle lanes) serve
+// every matrix of the model.
+__device__ __forceinline__ int gpl_for(int k) { return (k / 32) % 64 == 0 && k / 32 <= 64 ? 4 : 3; }
+__device__ __forceinline__ int ks_for(int k, int gpl) {
+  int ks = 1;
+  while (16 * gpl * ks < k / 32) ks *= 2;
+  return ks;
 }
 
 // producer: stream one matrix's slice through the ring
-__device__ bool produce(const Params& p, Smem& sm, const uint8_t* w, const __half* s, int n, int k, int& it) {
+__device__ bool produce(const Params& p, Smem& sm, const uint8_t* w, const __half* s, int n, int k, int& it,
+                        bool& fail) {
   const Seg sg = segment(n, k);
   const int rb = k / 2, sb = k / 16;
+  const uint64_t pol = sbd::l2_policy_evict_first();
   for (int r = sg.r0; r < sg.r1; r += sg.rs) {
     const int nr = min(sg.rs, sg.r1 - r);
     const int slot = it % kRing;
-    if (!ring_wait(&sm.empty[slot], ((it / kRing) & 1) ^ 1, p)) return false;
+    if (!ring_wait(&sm.empty[slot], ((it / kRing) & 1) ^ 1, p, fail)) return false;
     sbd::mbar_arrive_expect_tx(&sm.full[slot], static_cast<uint32_t>(nr) * (rb + sb));
-    sbd::bulk_load(sm.w[slot], w + static_cast<size_t>(r) * rb, static_cast<uint32_t>(nr) * rb, &sm.full[slot]);
-    sbd::bulk_load(sm.s[slot], reinterpret_cast<const uint8_t*>(s) + static_cast<size_t>(r) * sb,
-                   static_cast<uint32_t>(nr) * sb, &sm.full[slot]);
+    sbd::bulk_load_hint(sm.w[slot], w + static_cast<size_t>(r) * rb, static_cast<uint32_t>(nr) * rb,
+                        &sm.full[slot], pol);
+    sbd::bulk_load_hint(sm.s[slot], reinterpret_cast<const uint8_t*>(s) + static_cast<size_t>(r) * sb,
+                        static_cast<uint32_t>(nr) * sb, &sm.full[slot], pol);
     ++it;
   }
   return true;
@@ -259,15 +343,33 @@ __device__ bool produce(const Params& p, Smem& sm, const uint8_t* w, const __hal
 
 enum { EPI_STORE = 0, EPI_SEGOUT = 1, EPI_ARGMAX = 2 };
 
-// consumers: GEMV of this CTA's rows of one matrix over sm.vec (transposed, K values)
-template <int GPL, int EPI>
-__device__ bool gemv_rows(const Params& p, Smem& sm, int n, int k, int ks, float* out, int& it, float& best_v,
-                          long long& best_i) {
+// Consumer state carried across phases.
+struct Cursor {
+  int it;             // ring stages consumed
+  float best_v;       // lm_head: running max ...
+  long long best_i;   // ... and its row
+  bool fail;          // sticky failure (see ring_wait)
+};
+
+// consumers: GEMV of this CTA's rows of one matrix over the quantised input
+// sm.xq (K values).  epi: EPI_STORE (out[row]), EPI_SEGOUT (sm.seg_out) or
+// EPI_ARGMAX (running max / lowest row).  Each half-warp works on two rows at
+// a time (independent dot chains).  A failed ring wait leaves garbage in this
+// CTA's results; the next grid barrier turns it into an abort.
+template <int GPL>
+__device__ __noinline__ void gemv_phase_t(int n, int k, int epi, float* out, Cursor& cur) {
+  Smem& sm = smem();
+  const Params& p = sm.prm;
   const int tid = threadIdx.x, hw = tid >> 4, l16 = tid & 15;
+  const int ks = ks_for(k, GPL);
   const int G = k / 32;
   const int SG = (G + ks - 1) / ks;
   const int kslice = hw % ks, rlane = hw / ks, nrl = 16 / ks;
   const int gb = kslice * SG, ge = min(G, gb + SG);
+  int it = cur.it;
+  float best_v = cur.best_v;
+  long long best_i = cur.best_i;
+  bool fail = cur.fail;
   sbd::XGroup xg[GPL];
   int gidx[GPL];
   bool gval[GPL];
@@ -275,175 +377,352 @@ __device__ bool gemv_rows(const Params& p, Smem& sm, int n, int k, int ks, float
   for (int u = 0; u < GPL; ++u) {
     gidx[u] = gb + l16 + 16 * u;
     gval[u] = gidx[u] < ge;
-    float v[32];
+    const int g = gval[u] ? gidx[u] : 0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = gval[u] ? sm.va[j * G + gidx[u]] : 0.f;
-    sbd::quantise_group(v, xg[u]);
+    for (int j = 0; j < 4; ++j) {
+      xg[u].he[j] = sm.xq.w[j][g];
+      xg[u].ho[j] = sm.xq.w[4 + j][g];
+      xg[u].le[j] = sm.xq.w[8 + j][g];
+      xg[u].lo[j] = sm.xq.w[12 + j][g];
+    }
+    xg[u].bias = sm.xq.bias[g];
+    xg[u].sx = sm.xq.sx[g];
   }
+  trace_stamp(p, TR_INPUT);
   const Seg sg = segment(n, k);
   const int rb = k / 2;
+  auto put = [&](int row, float v) {
+    if (epi == EPI_STORE) {
+      out[row] = v;
+    } else if (epi == EPI_SEGOUT) {
+      sm.seg_out[row - sg.r0] = v;
+    } else {
+      if (v != v) v = -INFINITY;
+      if (v > best_v || (v == best_v && row < best_i)) {
+        best_v = v;
+        best_i = row;
+      }
+    }
+  };
   for (int r = sg.r0; r < sg.r1; r += sg.rs) {
     const int nr = min(sg.rs, sg.r1 - r);
     const int slot = it % kRing;
-    const bool ok = ring_wait(&sm.full[slot], (it / kRing) & 1, p);
-    if (!__all_sync(0xFFFFFFFFu, ok)) return false;
+    ring_wait(&sm.full[slot], (it / kRing) & 1, p, fail);
+    if (r == sg.r0) trace_stamp(p, TR_STAGE0);
     float* red = sm.red[it & 1];
     const uint8_t* wst = sm.w[slot];
     const __half* sst = reinterpret_cast<const __half*>(sm.s[slot]);
-    const int iters = (sg.rs + nrl - 1) / nrl;
-    for (int t = 0; t < iters; ++t) {
-      const int rr = rlane + t * nrl;
-      float acc = 0.f;
-      if (rr < nr) {
+    for (int r0 = rlane; r0 < nr; r0 += 2 * nrl) {
+      const int r1 = r0 + nrl;
+      const bool has1 = r1 < nr;
+      float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
-        for (int u = 0; u < GPL; ++u) {
-          if (!gval[u]) continue;
-          const uint4 q = *reinterpret_cast<const uint4*>(wst + rr * rb + gidx[u] * 16);
-          const float sw = __half2float(sst[rr * G + gidx[u]]);
-          acc = fmaf(static_cast<float>(sbd::dot_group(q, xg[u])), sw * xg[u].sx, acc);
-        }
+      for (int u = 0; u < GPL; ++u) {
+        if (!gval[u]) continue;
+        const uint4 q0 = *reinterpret_cast<const uint4*>(wst + r0 * rb + gidx[u] * 16);
+        const uint4 q1 = has1 ? *reinterpret_cast<const uint4*>(wst + r1 * rb + gidx[u] * 16) : q0;
+        const float s0 = __half2float(sst[r0 * G + gidx[u]]);
+        const float s1 = has1 ? __half2float(sst[r1 * G + gidx[u]]) : 0.f;
+        acc0 = fmaf(static_cast<float>(sbd::dot_group(q0, xg[u])), s0 * xg[u].sx, acc0);
+        acc1 = fmaf(static_cast<float>(sbd::dot_group(q1, xg[u])), s1 * xg[u].sx, acc1);
       }
 #pragma unroll
-      for (int off = 8; off > 0; off >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, off, 16);
-      if (l16 == 0 && rr < nr) red[rr * ks + kslice] = acc;
+      for (int off = 8; off > 0; off >>= 1) {
+        acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, off, 16);
+        acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, off, 16);
+      }
+      if (l16 == 0) {
+        if (ks == 1) {  // the half-warp holds whole rows
+          put(r + r0, acc0);
+          if (has1) put(r + r1, acc1);
+        } else {
+          red[r0 * ks + kslice] = acc0;
+          if (has1) red[r1 * ks + kslice] = acc1;
+        }
+      }
     }
     __syncwarp();
     if ((tid & 31) == 0) sbd::mbar_arrive(&sm.empty[slot]);
-    cons_sync();
-    for (int e = tid; e < nr; e += kCons) {
-      float v = 0.f;
-      for (int q = 0; q < ks; ++q) v += red[e * ks + q];
-      const int row = r + e;
-      if (EPI == EPI_STORE) {
-        out[row] = v;
-      } else if (EPI == EPI_SEGOUT) {
-        sm.seg_out[row - sg.r0] = v;
-      } else {
-        if (v != v) v = -INFINITY;
-        if (v > best_v || (v == best_v && row < best_i)) {
-          best_v = v;
-          best_i = row;
-        }
+    if (ks > 1) {
+      cons_sync();
+      for (int e = tid; e < nr; e += kCons) {
+        float v = 0.f;
+        for (int q = 0; q < ks; ++q) v += red[e * ks + q];
+        put(r + e, v);
       }
     }
     ++it;
   }
-  return true;
+  trace_stamp(p, TR_GEMV);
+  cur.it = it;
+  cur.best_v = best_v;
+  cur.best_i = best_i;
+  cur.fail = fail;
 }
 
-template <int EPI>
-__device__ bool gemv_any(const Params& p, Smem& sm, int n, int k, float* out, int& it, float& bv, long long& bi) {
-  const Plan pl = plan_for(k);
-  switch (pl.gpl) {
-    case 1: return gemv_rows<1, EPI>(p, sm, n, k, pl.ks, out, it, bv, bi);
-    case 2: return gemv_rows<2, EPI>(p, sm, n, k, pl.ks, out, it, bv, bi);
-    case 3: return gemv_rows<3, EPI>(p, sm, n, k, pl.ks, out, it, bv, bi);
-    default: return gemv_rows<4, EPI>(p, sm, n, k, pl.ks, out, it, bv, bi);
+__device__ __forceinline__ void gemv_phase(int n, int k, int epi, float* out, Cursor& cur) {
+  if (gpl_for(k) == 4)
+    gemv_phase_t<4>(n, k, epi, out, cur);
+  else
+    gemv_phase_t<3>(n, k, epi, out, cur);
+}
+
+// ---------------------------------------------------------------- phase inputs
+// A phase input of n values (n % 32 == 0) is held as 8-value slots: slot
+// s = tid + pass * kCons covers values [8 s, 8 s + 8), so the 4 slots of a
+// 32-value group are lanes 4k .. 4k + 3 of one warp.  Each thread loads all of
+// its slots before using any (one global round trip per phase input), and the
+// group is quantised exactly as sbd::quantise_group does, with the group max
+// and integer sum combined over the 4 lanes.
+
+// Quantise slot s (all 32 lanes call this; slots at or beyond n only join the
+// shuffles) into sm.xq.
+__device__ __forceinline__ void quantise_slot(Smem& sm, int s, int n, const float (&v)[8]) {
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[i]));
+  mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
+  // fast reciprocal (<= 2 ulp): x * inv stays below 32767.5, and the scale
+  // below is the same factor's inverse up to rounding, both far inside the
+  // 2^-16 quantisation step
+  const float inv = mx > 0.f ? __fdividef(32767.f, mx) : 0.f;
+  int sum = 0;
+  uint32_t he = 0, ho = 0, le = 0, lo = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int xe = __float2int_rn(v[2 * i] * inv);
+    const int xo = __float2int_rn(v[2 * i + 1] * inv);
+    sum += xe + xo;
+    he |= (static_cast<uint32_t>(xe >> 8) & 0xFFu) << (8 * i);
+    ho |= (static_cast<uint32_t>(xo >> 8) & 0xFFu) << (8 * i);
+    le |= (static_cast<uint32_t>(xe) & 0xFFu) << (8 * i);
+    lo |= (static_cast<uint32_t>(xo) & 0xFFu) << (8 * i);
+  }
+  sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+  sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+  if (8 * s < n) {
+    const int g = s >> 2, q = s & 3;
+    sm.xq.w[q][g] = he;
+    sm.xq.w[4 + q][g] = ho;
+    sm.xq.w[8 + q][g] = le;
+    sm.xq.w[12 + q][g] = lo;
+    if (q == 0) {
+      sm.xq.bias[g] = -8 * sum;
+      sm.xq.sx[g] = mx * (1.f / 32767.f);
+    }
   }
 }
 
-// sm.vec <- RMSNorm(v) * w in the transposed layout, where v is given by `get(i)`
-// (natural index); optionally also stores v (natural layout) to `keep`.
-template <typename Get>
-__device__ void build_norm(const Params& p, Smem& sm, int n, Get get, const float* w, float* keep) {
-  const int G = n / 32;
+__device__ __forceinline__ void ld8(float (&v)[8], const float* src, int s, bool in, bool coherent) {
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+  if (in) {
+    const float4* q = reinterpret_cast<const float4*>(src) + 2 * s;
+    a = coherent ? __ldcg(q) : __ldg(q);
+    b = coherent ? __ldcg(q + 1) : __ldg(q + 1);
+  }
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ float sumsq8(const float (&v)[8]) {
   float ss = 0.f;
-  for (int i = threadIdx.x; i < n; i += kCons) {
-    const float v = get(i);
-    sm.va[kMaxK + i] = v;
-    ss += v * v;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+  return ss;
+}
+
+// sm.xq <- quantise(RMSNorm(v) * w) for a hidden-sized v held one slot per
+// thread (values [8 tid, 8 tid + 8)); optionally stores v to `keep`.
+__device__ void finish_norm(const Params& p, Smem& sm, int n, float (&v)[8], const float (&w)[8], float* keep) {
+  // one reciprocal, then multiplies: eight IEEE divides per thread cost more
+  // than the rest of the prologue (differs from v / dnm by at most an ulp)
+  const float inv = 1.f / sqrtf(cons_reduce<false>(sumsq8(v), sm) / n + p.eps);
+  const int s = threadIdx.x;
+  if (keep && 8 * s < n) {
+    float4* k4 = reinterpret_cast<float4*>(keep) + 2 * s;
+    k4[0] = make_float4(v[0], v[1], v[2], v[3]);
+    k4[1] = make_float4(v[4], v[5], v[6], v[7]);
   }
-  const float dnm = sqrtf(cons_sum(ss, sm) / n + p.eps);
-  for (int i = threadIdx.x; i < n; i += kCons) {
-    const float v = sm.va[kMaxK + i];
-    if (keep) keep[i] = v;
-    sm.va[(i & 31) * G + (i >> 5)] = v / dnm * w[i];
-  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * w[i];
+  quantise_slot(sm, s, n, v);
   cons_sync();
 }
 
-// residual update x + RMSNorm(y) * w  into sm.aux (natural layout); returns via get
-__device__ void residual(const Params& p, Smem& sm, int n, const float* x, const float* y, const float* w) {
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < n; i += kCons) {
-    const float v = y[i];
-    ss += v * v;
+// sm.xq <- quantise(RMSNorm(x + RMSNorm(y) * w_res) * w_norm), all loads issued up front
+__device__ __noinline__ void residual_norm(int n, const float* x, const float* y, const float* w_res,
+                                          const float* w_norm, float* keep) {
+  Smem& sm = smem();
+  const Params& p = sm.prm;
+  const int s = threadIdx.x;
+  const bool in = 8 * s < n;
+  float v[8], yv[8], wr[8], wn[8];
+  ld8(v, x, s, in, true);
+  ld8(yv, y, s, in, true);
+  ld8(wr, w_res, s, in, false);
+  ld8(wn, w_norm, s, in, false);
+  const float inv = 1.f / sqrtf(cons_reduce<false>(sumsq8(yv), sm) / n + p.eps);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = v[i] + yv[i] * inv * wr[i];
+  finish_norm(p, sm, n, v, wn, keep);
+}
+
+// sm.xq <- quantise(src[0, n)) (values written earlier in this launch)
+__device__ __noinline__ void load_input(int n, const float* src) {
+  Smem& sm = smem();
+  float v[kPasses][8];
+#pragma unroll
+  for (int ps = 0; ps < kPasses; ++ps) {
+    const int s = threadIdx.x + ps * kCons;
+    ld8(v[ps], src, s, 8 * s < n, true);
   }
-  const float dnm = sqrtf(cons_sum(ss, sm) / n + p.eps);
-  for (int i = threadIdx.x; i < n; i += kCons) sm.va[kMaxK + i] = x[i] + y[i] / dnm * w[i];
+#pragma unroll
+  for (int ps = 0; ps < kPasses; ++ps)
+    if (ps * 8 * kCons < n) quantise_slot(sm, threadIdx.x + ps * kCons, n, v[ps]);
   cons_sync();
 }
 
-__device__ __forceinline__ float gelu_tanh(float x) {
-  return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+// Prefetch into L2 the norm vectors of layer `li` (the final norm when li ==
+// n_layers): threads 0..5 of every CTA, one 128-byte line each per CTA index.
+__device__ void prefetch_norms(const Params& p, int li) {
+  const int tid = threadIdx.x;
+  if (tid >= 6 || li > p.n_layers) return;
+  const float* v = nullptr;
+  int lines = p.H / 32;
+  if (li < p.n_layers) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    const Layer& N = reinterpret_cast<Smem*>(smem_raw)->layers[li];
+    v = tid == 0 ? N.in_norm : tid == 1 ? N.post_attn : tid == 2 ? N.pre_ffn : tid == 3 ? N.post_ffn
+      : tid == 4 ? N.q_norm : N.k_norm;
+    if (tid >= 4) lines = HD / 32;
+  } else if (tid == 0) {
+    v = p.final_norm;
+  }
+  if (!v) return;
+  for (int l = blockIdx.x; l < lines; l += gridDim.x) prefetch_l2(v + 32 * l);
 }
 
-// ---------------------------------------------------------------- attention phase
-// Work item c: keys [32c, min(T, 32c + 32)) of the single sequence.
-__device__ void attn_chunk(const Params& p, Smem& sm, const Layer& L, int c, int pos) {
+// ---------------------------------------------------------------- attention
+// Thread 0: start the bulk copy of chunk c's K and V rows that precede this
+// position (row `pos` itself is produced in this step) and, with `consts`, the
+// q/k norm weights and this position's RoPE row, completing on sm.kvbar.
+__device__ void kv_issue(const Params& p, Smem& sm, const Layer& L, int c, int pos, bool consts,
+                         uint32_t& issued) {
+  ++issued;
+  const int t0 = c * CKA;
+  const int nk = max(0, min(CKA, pos - t0));
+  uint32_t bytes = 2u * static_cast<uint32_t>(nk) * HD * 4;
+  if (consts) bytes += 3u * HD * 4;
+  sbd::fence_proxy_async_smem();
+  sbd::mbar_arrive_expect_tx(&sm.kvbar, bytes);
+  if (nk) {
+    sbd::bulk_load(sm.kv[0], L.kc + static_cast<size_t>(t0) * HD, nk * HD * 4, &sm.kvbar);
+    sbd::bulk_load(sm.kv[1], L.vc + static_cast<size_t>(t0) * HD, nk * HD * 4, &sm.kvbar);
+  }
+  if (consts) {
+    sbd::bulk_load(sm.qn, L.q_norm, HD * 4, &sm.kvbar);
+    sbd::bulk_load(sm.kn, L.k_norm, HD * 4, &sm.kvbar);
+    sbd::bulk_load(sm.cs, p.cos_t + static_cast<size_t>(pos) * (HD / 2), HD / 2 * 4, &sm.kvbar);
+    sbd::bulk_load(sm.sn, p.sin_t + static_cast<size_t>(pos) * (HD / 2), HD / 2 * 4, &sm.kvbar);
+  }
+}
+
+// q heads (and k, v of this position when `own`): RMSNorm (weights for q, k;
+// none for v), RoPE on q and k; q to sm.vb, k / v to the cache and sm.kpos / vpos.
+__device__ void qkv_heads(const Params& p, Smem& sm, const Layer& L, int pos, bool own) {
   const int nh = p.nh, qd = nh * HD;
-  const int T = pos + 1, t0 = c * CKA, nt = min(CKA, T - t0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* ks = sm.va;                          // [CKA][HD]
-  float* qs = sm.va + CKA * HD;               // [nh][HD]
-  float* ps = sm.va + 2 * kMaxK - kMaxHeads * CKA;  // [nh][CKA]
-  static_assert(CKA * HD + kMaxHeads * HD <= 2 * kMaxK - kMaxHeads * CKA, "attention scratch overlaps");
-  const float* cs = p.cos_t + static_cast<size_t>(pos) * (HD / 2);
-  const float* sn = p.sin_t + static_cast<size_t>(pos) * (HD / 2);
-  // q heads (warp h), and k / v of this position in the last chunk's CTA
-  const bool last = t0 + nt == T;
-  for (int h = warp; h < nh + (last ? 2 : 0); h += kCons / 32) {
+  for (int h = warp; h < nh + (own ? 2 : 0); h += kCons / 32) {
     const int col = h < nh ? h * HD : (h == nh ? qd : qd + HD);
     float v[8];
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      v[j] = p.qkv[col + lane + 32 * j];
-      ss += v[j] * v[j];
-    }
-    const float dnm = sqrtf(warp_sum(ss) / HD + p.eps);
-    const float* w = h < nh ? L.q_norm : L.k_norm;
+    for (int j = 0; j < 8; ++j) v[j] = __ldcg(p.qkv + col + lane + 32 * j);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = h <= nh ? v[j] / dnm * w[lane + 32 * j] : v[j] / dnm;
+    for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+    const float inv = 1.f / sqrtf(warp_sum(ss) / HD + p.eps);
+    const float* w = h < nh ? sm.qn : sm.kn;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = h <= nh ? v[j] * inv * w[lane + 32 * j] : v[j] * inv;
     if (h <= nh) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int i = lane + 32 * j;
         const float a = v[j], b = v[j + 4];
-        v[j] = a * cs[i] - b * sn[i];
-        v[j + 4] = b * cs[i] + a * sn[i];
+        v[j] = a * sm.cs[i] - b * sm.sn[i];
+        v[j + 4] = b * sm.cs[i] + a * sm.sn[i];
       }
     }
     if (h < nh) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) qs[h * HD + lane + 32 * j] = v[j];
+      for (int j = 0; j < 8; ++j) sm.vb[h * HD + lane + 32 * j] = v[j];
     } else {
       float* cache = (h == nh ? L.kc : L.vc) + static_cast<size_t>(pos) * HD;
+      float* keep = h == nh ? sm.kpos : sm.vpos;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) cache[lane + 32 * j] = v[j];
+      for (int j = 0; j < 8; ++j) {
+        cache[lane + 32 * j] = v[j];
+        keep[lane + 32 * j] = v[j];
+      }
     }
   }
-  cons_sync();
-  const float* kb = L.kc + static_cast<size_t>(t0) * HD;
-  for (int i = threadIdx.x; i < nt * HD / 4; i += kCons)
-    reinterpret_cast<float4*>(ks)[i] = reinterpret_cast<const float4*>(kb)[i];
-  cons_sync();
+}
+
+// Chunk c's scores, softmax partials (max, sum) and P.V partials from sm.kv.
+__device__ void attn_chunk(const Params& p, Smem& sm, int c, int pos) {
+  const int nh = p.nh;
+  const int T = pos + 1, t0 = c * CKA, nt = min(CKA, T - t0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // scores: warp per head; lane holds dims [4 lane, 4 lane + 4) and [128 + 4 lane, ...)
   for (int h = warp; h < nh; h += kCons / 32) {
-    float q[8];
+    const float4 q0 = reinterpret_cast<const float4*>(sm.vb + h * HD)[lane];
+    const float4 q1 = reinterpret_cast<const float4*>(sm.vb + h * HD)[32 + lane];
+    // two halves of 8 keys; each half's 8 per-lane partial sums are
+    // reduce-scattered over the warp (xor 16, 8, 4) so that lane holds key
+    // (lane >> 2) & 7 of the half, then completed over the 4 lanes sharing it
+    float sc[2];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) q[j] = qs[h * HD + lane + 32 * j];
-    float mine = -INFINITY;
-    for (int t = 0; t < nt; ++t) {
-      float dd = 0.f;
+    for (int hb = 0; hb < 2; ++hb) {
+      float s[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) dd += q[j] * ks[t * HD + lane + 32 * j];
-      dd = warp_sum(dd);
-      if (lane == t) mine = dd;
+      for (int t = 0; t < 8; ++t) {
+        const float4 k0 = reinterpret_cast<const float4*>(sm.kv[0][hb * 8 + t])[lane];
+        const float4 k1 = reinterpret_cast<const float4*>(sm.kv[0][hb * 8 + t])[32 + lane];
+        s[t] = q0.x * k0.x + q0.y * k0.y + q0.z * k0.z + q0.w * k0.w + q1.x * k1.x + q1.y * k1.y +
+               q1.z * k1.z + q1.w * k1.w;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const bool up = lane & 16;
+        const float send = up ? s[i] : s[i + 4];
+        s[i] = (up ? s[i + 4] : s[i]) + __shfl_xor_sync(0xFFFFFFFFu, send, 16);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const bool up = lane & 8;
+        const float send = up ? s[i] : s[i + 2];
+        s[i] = (up ? s[i + 2] : s[i]) + __shfl_xor_sync(0xFFFFFFFFu, send, 8);
+      }
+      {
+        const bool up = lane & 4;
+        const float send = up ? s[0] : s[1];
+        s[0] = (up ? s[1] : s[0]) + __shfl_xor_sync(0xFFFFFFFFu, send, 4);
+      }
+      s[0] += __shfl_xor_sync(0xFFFFFFFFu, s[0], 2);
+      s[0] += __shfl_xor_sync(0xFFFFFFFFu, s[0], 1);
+      sc[hb] = s[0];
     }
-    const float m = warp_max(mine);
-    const float pv = lane < nt ? expf(mine - m) : 0.f;
-    const float l = warp_sum(pv);
-    ps[h * CKA + lane] = pv;
+    const int key = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+    const bool v0 = key < nt, v1 = key + 8 < nt;
+    const float m = warp_max(fmaxf(v0 ? sc[0] : -INFINITY, v1 ? sc[1] : -INFINITY));
+    const float p0 = v0 ? expf(sc[0] - m) : 0.f;
+    const float p1 = v1 ? expf(sc[1] - m) : 0.f;
+    const float l = warp_sum((lane & 3) ? 0.f : p0 + p1);
+    if (!(lane & 3)) {
+      sm.ps[h][key] = p0;
+      sm.ps[h][key + 8] = p1;
+    }
     if (lane == 0) {
       float* pm = p.part + (static_cast<size_t>(c) * nh + h) * (HD + 2);
       pm[HD] = m;
@@ -451,36 +730,128 @@ __device__ void attn_chunk(const Params& p, Smem& sm, const Layer& L, int c, int
     }
   }
   cons_sync();
-  const float* vb = L.vc + static_cast<size_t>(t0) * HD;
-  for (int dcol = threadIdx.x; dcol < HD; dcol += kCons) {
+  trace_stamp(p, TR_ATT_S);
+  // P.V: thread per head dim
+  {
+    const int dcol = threadIdx.x;
     float acc[kMaxHeads];
 #pragma unroll
     for (int h = 0; h < kMaxHeads; ++h) acc[h] = 0.f;
-    for (int t = 0; t < nt; ++t) {
-      const float vv = vb[static_cast<size_t>(t) * HD + dcol];
+    // rolled: this code runs once per layer, and straight-line code costs
+    // instruction fetches from L2 every time
+#pragma unroll 1
+    for (int t = 0; t < CKA; ++t) {
+      if (t < nt) {
+        const float vv = sm.kv[1][t][dcol];
 #pragma unroll
-      for (int h = 0; h < kMaxHeads; ++h)
-        if (h < nh) acc[h] += ps[h * CKA + t] * vv;
+        for (int h = 0; h < kMaxHeads; ++h)
+          if (h < nh) acc[h] = fmaf(sm.ps[h][t], vv, acc[h]);
+      }
     }
 #pragma unroll
     for (int h = 0; h < kMaxHeads; ++h)
       if (h < nh) p.part[(static_cast<size_t>(c) * nh + h) * (HD + 2) + dcol] = acc[h];
   }
-  cons_sync();
+  trace_stamp(p, TR_ATT_PV);
+}
+
+// The attention phase: this CTA's chunks c = blockIdx.x, + gridDim.x, ...
+// The first chunk's copy was started in the qkv phase (kv_issue with consts).
+// kvph counts completed waits on sm.kvbar, issued (thread 0) the copies started.
+__device__ void attention(const Params& p, Smem& sm, const Layer& L, int pos, int nc, uint32_t& kvph,
+                          uint32_t& issued, bool& fail) {
+  const int cpos = pos / CKA;
+  const bool own = cpos % static_cast<int>(gridDim.x) == static_cast<int>(blockIdx.x);
+  for (int c = blockIdx.x; c < nc; c += gridDim.x) {
+    if (c != static_cast<int>(blockIdx.x)) {
+      cons_sync();  // every thread is done with the previous chunk's rows
+      if (threadIdx.x == 0 && !fail) kv_issue(p, sm, L, c, pos, false, issued);
+    }
+    if (ring_wait(&sm.kvbar, kvph & 1, p, fail)) ++kvph;
+    if (c == static_cast<int>(blockIdx.x)) {
+      qkv_heads(p, sm, L, pos, own);
+      cons_sync();
+      trace_stamp(p, TR_ATT_Q);
+    }
+    if (c == cpos) {
+      sm.kv[0][pos - c * CKA][threadIdx.x] = sm.kpos[threadIdx.x];
+      sm.kv[1][pos - c * CKA][threadIdx.x] = sm.vpos[threadIdx.x];
+    }
+    cons_sync();
+    trace_stamp(p, TR_ATT_K);
+    attn_chunk(p, sm, c, pos);
+  }
+}
+
+// Merge of the chunk partials: work item (head, kMergeDims dims).
+__device__ void merge(const Params& p, Smem& sm, int nc) {
+  const int nh = p.nh, tid = threadIdx.x;
+  constexpr int NG = kCons / kMergeDims;  // chunk groups summed in parallel
+  const int items = nh * (HD / kMergeDims);
+  const size_t cst = static_cast<size_t>(nh) * (HD + 2);
+  float* ms = &sm.kv[0][0][0];      // the K/V chunk buffer is free until the next layer
+  float* fv = ms;                   // [nc] chunk max, then weight
+  float* lv = ms + kMaxChunks;      // [nc] chunk sum
+  float* rv = ms + 2 * kMaxChunks;  // [NG][kMergeDims]
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    const int h = item / (HD / kMergeDims), d0 = (item % (HD / kMergeDims)) * kMergeDims;
+    const float* base = p.part + static_cast<size_t>(h) * (HD + 2);
+    float mx = -INFINITY;
+    for (int c = tid; c < nc; c += kCons) {
+      const float m = __ldcg(base + c * cst + HD);
+      fv[c] = m;
+      lv[c] = __ldcg(base + c * cst + HD + 1);
+      mx = fmaxf(mx, m);
+    }
+    mx = cons_reduce<true>(mx, sm);
+    float ls = 0.f;
+    for (int c = tid; c < nc; c += kCons) {
+      const float f = expf(fv[c] - mx);
+      ls += lv[c] * f;
+      fv[c] = f;
+    }
+    ls = cons_reduce<false>(ls, sm);  // its barriers also publish fv
+    const int dd = tid % kMergeDims, g = tid / kMergeDims;
+    float acc = 0.f;
+#pragma unroll 4
+    for (int c = g; c < nc; c += NG) acc = fmaf(fv[c], __ldcg(base + c * cst + d0 + dd), acc);
+    rv[g * kMergeDims + dd] = acc;
+    cons_sync();
+    if (tid < kMergeDims) {
+      float o = 0.f;
+      for (int q = 0; q < NG; ++q) o += rv[q * kMergeDims + tid];
+      p.attn[h * HD + d0 + tid] = o / ls;
+    }
+    cons_sync();
+  }
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
 }
 
 // ---------------------------------------------------------------- the kernel
 __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(Params p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  if (p.bar[3] == 0) p.trace = nullptr;
+  if (p.bar[3] == 0 || blockIdx.x >= kTraceCtas) p.trace = nullptr;
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   const int tid = threadIdx.x;
   const int H = p.H, nh = p.nh, qd = nh * HD, nqkv = qd + 2 * HD, F = p.F;
+  {
+    // the layer table (pointers) into shared memory
+    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(p.layers);
+    unsigned long long* dst = reinterpret_cast<unsigned long long*>(sm.layers);
+    constexpr int kWords = sizeof(Layer) / 8;
+    for (int i = tid; i < p.n_layers * kWords; i += kThreads) dst[i] = __ldg(src + i);
+  }
   if (tid == 0) {
+    sm.prm = p;
+    sm.trace_n = 0;
     for (int i = 0; i < kRing; ++i) {
       sbd::mbar_init(&sm.full[i], 1);
       sbd::mbar_init(&sm.empty[i], kCons / 32);
     }
+    sbd::mbar_init(&sm.kvbar, 1);
     sbd::fence_mbar_init();
     sbd::fence_proxy_async_smem();
   }
@@ -490,13 +861,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(Params p) {
     // ------------------------------------------------------------ producer warp
     if (tid == kCons) {
       int it = 0;
-      bool ok = true;
+      bool ok = true, pfail = false;
       for (int li = 0; li < p.n_layers && ok; ++li) {
-        const Layer& L = p.layers[li];
-        ok = produce(p, sm, L.w[0], L.s[0], nqkv, H, it) && produce(p, sm, L.w[1], L.s[1], H, qd, it) &&
-             produce(p, sm, L.w[2], L.s[2], 2 * F, H, it) && produce(p, sm, L.w[3], L.s[3], H, F, it);
+        const Layer& L = sm.layers[li];
+        ok = produce(p, sm, L.w[0], L.s[0], nqkv, H, it, pfail) &&
+             produce(p, sm, L.w[1], L.s[1], H, qd, it, pfail) &&
+             produce(p, sm, L.w[2], L.s[2], 2 * F, H, it, pfail) &&
+             produce(p, sm, L.w[3], L.s[3], H, F, it, pfail);
       }
-      if (ok) ok = produce(p, sm, p.emb, p.emb_s, p.V, H, it);
+      if (ok) ok = produce(p, sm, p.emb, p.emb_s, p.V, H, it, pfail);
       if (!ok) {
         // let copies in flight land before the CTA releases its shared memory
         const uint64_t t0 = sbd::global_ns();
@@ -509,93 +882,85 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(Params p) {
   }
 
   // -------------------------------------------------------------- consumer warps
-  if (blockIdx.x == 0 && tid == 0) {
-    *p.keys = 0ull;  // ordered before the lm_head by the barriers
-    if (p.trace) {
-      p.trace[0] = 1;
-      p.trace[1] = sbd::global_ns();
-    }
-  }
+  if (blockIdx.x == 0 && tid == 0) *p.keys = 0ull;  // ordered before the lm_head by the barriers
+  trace_stamp(p, TR_ENTRY);
   const int pos = p.pos[0];
-  int it = 0;
-  float bv = -INFINITY;
-  long long bi = 0x7FFFFFFF;
+  const int nc = pos / CKA + 1;  // attention chunks
+  Cursor cur{0, -INFINITY, 0x7FFFFFFF, false};
+  // an abort left by an earlier launch stays until the caller zeroes the scratch
+  cur.fail = tid == 0 && aborted(p);
+  bool& fail = cur.fail;
+  uint32_t kvph = 0, kv_issued = 0;
   const bool lead = blockIdx.x == 0;
+  const bool has_chunk = static_cast<int>(blockIdx.x) < nc;
   bool ok = true;
   for (int li = 0; li < p.n_layers && ok; ++li) {
-    const Layer& L = p.layers[li];
-    // ---- qkv: layer input, RMSNorm, GEMV
+    const Layer& L = sm.layers[li];
+    // ---- qkv: start this layer's K/V chunk copy, layer input, RMSNorm, GEMV
+    if (has_chunk && tid == 0 && !fail) kv_issue(p, sm, L, blockIdx.x, pos, true, kv_issued);
+    prefetch_norms(p, li + 1);
     if (li == 0) {
+      // embedding row: 8 values = one 32-bit word of nibbles (low nibble first)
       const int64_t tok = p.cur[0];
-      const uint8_t* er = p.emb + tok * (H / 2);
-      const __half* es = p.emb_s + tok * (H / 32);
-      build_norm(p, sm, H,
-                 [&](int i) {
-                   const uint8_t b = er[i >> 1];
-                   const int q = ((i & 1) ? (b >> 4) : (b & 15)) - 8;
-                   return __fmul_rn(__fmul_rn(static_cast<float>(q), __half2float(es[i >> 5])), p.embed_scale);
-                 },
-                 L.in_norm, lead ? p.xa : nullptr);
-    } else {
-      residual(p, sm, H, p.xb, p.d, p.layers[li - 1].post_ffn);
-      build_norm(p, sm, H, [&](int i) { return sm.va[kMaxK + i]; }, L.in_norm, lead ? p.xa : nullptr);
-    }
-    ok = gemv_any<EPI_STORE>(p, sm, nqkv, H, p.qkv, it, bv, bi) && grid_sync(p, sm);
-    if (!ok) break;
-    // ---- attention partials
-    const int nc = (pos + 1 + CKA - 1) / CKA;
-    for (int c = blockIdx.x; c < nc; c += gridDim.x) attn_chunk(p, sm, L, c, pos);
-    if (!grid_sync(p, sm)) break;
-    // ---- merge: item (head, 64 dims)
-    for (int item = blockIdx.x; item < nh * 4; item += gridDim.x) {
-      const int h = item >> 2, d0 = (item & 3) * 64;
-      if (tid < 64) {
-        const float* base = p.part + static_cast<size_t>(h) * (HD + 2);
-        const size_t cst = static_cast<size_t>(nh) * (HD + 2);
-        float M = -INFINITY;
-        for (int c = 0; c < nc; ++c) M = fmaxf(M, base[c * cst + HD]);
-        float Lsum = 0.f, O = 0.f;
-        for (int c = 0; c < nc; ++c) {
-          const float f = expf(base[c * cst + HD] - M);
-          Lsum += base[c * cst + HD + 1] * f;
-          O += base[c * cst + d0 + tid] * f;
-        }
-        p.attn[h * HD + d0 + tid] = O / Lsum;
+      const bool in = 8 * tid < H;
+      const uint32_t wd = in ? __ldg(reinterpret_cast<const uint32_t*>(p.emb + tok * (H / 2)) + tid) : 0u;
+      const float sc = in ? __half2float(__ldg(p.emb_s + tok * (H / 32) + tid / 4)) : 0.f;
+      float v[8], wn[8];
+      ld8(wn, L.in_norm, tid, in, false);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int q = static_cast<int>((wd >> (4 * i)) & 15u) - 8;
+        v[i] = in ? __fmul_rn(__fmul_rn(static_cast<float>(q), sc), p.embed_scale) : 0.f;
       }
+      finish_norm(p, sm, H, v, wn, lead ? p.xa : nullptr);
+    } else {
+      residual_norm(H, p.xb, p.d, sm.layers[li - 1].post_ffn, L.in_norm, lead ? p.xa : nullptr);
     }
-    if (!grid_sync(p, sm)) break;
+    gemv_phase(nqkv, H, EPI_STORE, p.qkv, cur);
+    if (!(ok = grid_sync(fail))) break;
+    // ---- attention partials
+    attention(p, sm, L, pos, nc, kvph, kv_issued, fail);
+    if (!(ok = grid_sync(fail))) break;
+    // ---- merge
+    merge(p, sm, nc);
+    if (!(ok = grid_sync(fail))) break;
     // ---- o projection
-    for (int i = tid; i < qd; i += kCons) sm.va[(i & 31) * (qd / 32) + (i >> 5)] = p.attn[i];
-    cons_sync();
-    ok = gemv_any<EPI_STORE>(p, sm, H, qd, p.o, it, bv, bi) && grid_sync(p, sm);
-    if (!ok) break;
+    load_input(qd, p.attn);
+    gemv_phase(H, qd, EPI_STORE, p.o, cur);
+    if (!(ok = grid_sync(fail))) break;
     // ---- gate|up with GEGLU
-    residual(p, sm, H, p.xa, p.o, L.post_attn);
-    build_norm(p, sm, H, [&](int i) { return sm.va[kMaxK + i]; }, L.pre_ffn, lead ? p.xb : nullptr);
-    ok = gemv_any<EPI_SEGOUT>(p, sm, 2 * F, H, nullptr, it, bv, bi);
-    if (!ok) break;
+    residual_norm(H, p.xa, p.o, L.post_attn, L.pre_ffn, lead ? p.xb : nullptr);
+    gemv_phase(2 * F, H, EPI_SEGOUT, nullptr, cur);
     cons_sync();
     {
       const Seg sg = segment(2 * F, H);
       for (int i = tid; i < (sg.r1 - sg.r0) / 2; i += kCons)
         p.a[sg.r0 / 2 + i] = gelu_tanh(sm.seg_out[2 * i]) * sm.seg_out[2 * i + 1];
     }
-    if (!grid_sync(p, sm)) break;
+    if (!(ok = grid_sync(fail))) break;
     // ---- down projection
-    for (int i = tid; i < F; i += kCons) sm.va[(i & 31) * (F / 32) + (i >> 5)] = p.a[i];
-    cons_sync();
-    ok = gemv_any<EPI_STORE>(p, sm, H, F, p.d, it, bv, bi) && grid_sync(p, sm);
+    load_input(F, p.a);
+    gemv_phase(H, F, EPI_STORE, p.d, cur);
+    ok = grid_sync(fail);
   }
-  if (!ok) return;
+  if (!ok) {
+    // a CTA that leaves early must still let its K/V copy land
+    if (tid == 0 && kv_issued > kvph) {
+      const uint64_t t0 = sbd::global_ns();
+      while (!sbd::mbar_try_wait(&sm.kvbar, kvph & 1) && sbd::global_ns() - t0 < sbd::kWaitLimitNs) {
+      }
+    }
+    return;
+  }
   // ---- final norm + tied lm_head with argmax
-  residual(p, sm, H, p.xb, p.d, p.layers[p.n_layers - 1].post_ffn);
-  build_norm(p, sm, H, [&](int i) { return sm.va[kMaxK + i]; }, p.final_norm, nullptr);
-  if (!gemv_any<EPI_ARGMAX>(p, sm, p.V, H, nullptr, it, bv, bi)) return;
+  residual_norm(H, p.xb, p.d, sm.layers[p.n_layers - 1].post_ffn, p.final_norm, nullptr);
+  gemv_phase(p.V, H, EPI_ARGMAX, nullptr, cur);
   {
     const int lane = tid & 31, warp = tid >> 5;
     unsigned long long key = 0ull;
+    const long long bi = cur.best_i;
     if (bi != 0x7FFFFFFF) {
-      float f = bv;
+      float f = cur.best_v;
       const uint32_t b = __float_as_uint(f);
       const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
       key = (static_cast<unsigned long long>(ord) << 32) | (0xFFFFFFFFull - static_cast<uint32_t>(bi));
@@ -613,9 +978,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(Params p) {
       if (k2) atomicMax(p.keys, k2);
     }
   }
-  if (!grid_sync(p, sm)) return;
+  if (!grid_sync(fail)) return;
   if (lead && tid == 0) {
-    const unsigned long long k2 = *reinterpret_cast<volatile unsigned long long*>(p.keys);
+    const unsigned long long k2 = __ldcg(p.keys);
     const int32_t t = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(k2 & 0xFFFFFFFFull));
     const int np = pos + 1;
     p.tok[0] = t;
@@ -640,14 +1005,16 @@ int grid_size(int smem) {
   return g;
 }
 
+constexpr size_t kHeaderBytes = 64 + static_cast<size_t>(kTraceCtas) * kTraceLen * sizeof(unsigned long long);
+
 }  // namespace
 
 extern "C" size_t sb_decode_step_fused_scratch_size(int hidden, int n_heads, int head_dim, int inter, int max_seq) {
-  if (head_dim != HD || n_heads < 1 || n_heads > kMaxHeads) return 0;
+  if (head_dim != HD || n_heads < 1 || n_heads > kMaxHeads || max_seq < 1 || max_seq > CKA * kMaxChunks) return 0;
   const size_t qd = static_cast<size_t>(n_heads) * HD;
   const size_t chunks = (static_cast<size_t>(max_seq) + CKA - 1) / CKA;
   const size_t floats = 2 * hidden + (qd + 2 * HD) + qd + hidden + inter + hidden + chunks * n_heads * (HD + 2);
-  return 64 + kTraceLen * sizeof(unsigned long long) + floats * sizeof(float);
+  return kHeaderBytes + floats * sizeof(float);
 }
 
 extern "C" int sb_decode_step_fused(const void* layers_dev, int n_layers, const void* emb, const void* emb_scales,
@@ -657,12 +1024,15 @@ extern "C" int sb_decode_step_fused(const void* layers_dev, int n_layers, const 
                                     int hist_len, uint64_t* keys, void* scratch, size_t scratch_bytes, void* stream) {
   SB_CHECK_ARG(head_dim == HD, "sb_decode_step_fused: head_dim must be %d", HD);
   SB_CHECK_ARG(n_heads >= 1 && n_heads <= kMaxHeads, "sb_decode_step_fused: n_heads must be 1..%d", kMaxHeads);
-  SB_CHECK_ARG(hidden % 32 == 0 && hidden <= kMaxK && inter % 32 == 0 && inter <= kMaxK && n_heads * HD <= kMaxK,
-               "sb_decode_step_fused: hidden, inter and n_heads*head_dim must be multiples of 32 up to %d", kMaxK);
-  SB_CHECK_ARG(n_layers >= 1 && vocab >= 1 && max_seq >= 1, "sb_decode_step_fused: bad sizes");
+  SB_CHECK_ARG(hidden % 32 == 0 && hidden <= kMaxH && inter % 32 == 0 && inter <= kMaxK && n_heads * HD <= kMaxH,
+               "sb_decode_step_fused: hidden and n_heads*head_dim must be multiples of 32 up to %d, inter up to %d",
+               kMaxH, kMaxK);
+  SB_CHECK_ARG(n_layers >= 1 && vocab >= 1 && max_seq >= 1 && max_seq <= CKA * kMaxChunks,
+               "sb_decode_step_fused: bad sizes (max_seq <= %d)", CKA * kMaxChunks);
   SB_CHECK_ARG(layers_dev && emb && emb_scales && final_norm && cos_t && sin_t && pos && cur && tokens && keys &&
                    scratch,
                "sb_decode_step_fused: null pointer");
+  SB_CHECK_ARG(sb::aligned(scratch, 16), "sb_decode_step_fused: scratch must be 16-byte aligned");
   const size_t need = sb_decode_step_fused_scratch_size(hidden, n_heads, head_dim, inter, max_seq);
   if (scratch_bytes < need)
     return sb::fail(SB_ERR_WORKSPACE, "sb_decode_step_fused: scratch %zu < %zu bytes", scratch_bytes, need);
@@ -695,10 +1065,11 @@ extern "C" int sb_decode_step_fused(const void* layers_dev, int n_layers, const 
   p.keys = reinterpret_cast<unsigned long long*>(keys);
   p.err = sb::device_error_word();
   char* base = static_cast<char*>(scratch);
+  p.ctr = reinterpret_cast<unsigned long long*>(base);
   p.bar = reinterpret_cast<unsigned int*>(base);
-  // the trace region is used only when bar[3] (set by the caller) is non-zero
+  // the trace region is used only when the u32 at byte 12 (set by the caller) is non-zero
   p.trace = reinterpret_cast<unsigned long long*>(base + 64);
-  float* f = reinterpret_cast<float*>(base + 64 + kTraceLen * sizeof(unsigned long long));
+  float* f = reinterpret_cast<float*>(base + kHeaderBytes);
   const size_t qd = static_cast<size_t>(n_heads) * HD;
   p.xa = f;
   f += hidden;

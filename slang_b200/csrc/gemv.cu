@@ -96,11 +96,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
     const int nr = min(p.rs, p.n - r0);
     const uint32_t wb = static_cast<uint32_t>(nr) * row_bytes;
     const uint32_t sbytes = p.scale_bulk ? static_cast<uint32_t>(nr) * gps * esz : 0u;
+    const uint64_t pol = sbd::l2_policy_evict_first();  // weights are read once per step
     sbd::mbar_arrive_expect_tx(&sm.full[slot], wb + sbytes);
-    sbd::bulk_load(sm.w[slot], p.w + static_cast<size_t>(r0) * row_bytes, wb, &sm.full[slot]);
+    sbd::bulk_load_hint(sm.w[slot], p.w + static_cast<size_t>(r0) * row_bytes, wb, &sm.full[slot], pol);
     if (sbytes)
-      sbd::bulk_load(sm.s[slot], static_cast<const uint8_t*>(p.scales) + static_cast<size_t>(r0) * gps * esz, sbytes,
-                     &sm.full[slot]);
+      sbd::bulk_load_hint(sm.s[slot], static_cast<const uint8_t*>(p.scales) + static_cast<size_t>(r0) * gps * esz,
+                          sbytes, &sm.full[slot], pol);
   };
   if (tid == 0) {
     for (int i = 0; i < kRing; ++i) sbd::mbar_init(&sm.full[i], 1);

@@ -210,6 +210,19 @@ int sb_qkv_prep(const void* qkv, int qkv_dtype, int ld, const float* q_norm, con
 int sb_softmax_causal(const float* scores, int ld_s, int rows, int n_heads, int start_pos,
                       int n_keys, void* p16, int ld_p, void* stream);
 
+/*
+ * Fused causal prefill attention on tcgen05: out = softmax(q k^T) v for one
+ * prompt at positions 0..s_len-1, unscaled scores (q, k are RMS-normalised),
+ * row r = token r / n_heads sees keys 0..token.  q16 [s_len * n_heads][hd],
+ * k16, v16 [s_len][hd], out16 [s_len * n_heads][hd], all f16, 16-byte
+ * aligned, hd = head_dim in {64, 128, 256}.  Online softmax with f32 scores and accumulators, probabilities
+ * rounded to f16 for the P.V MMA.  Replaces the reference's attn_prefill
+ * kernel and its _attn_gemm QK^T -> softmax -> PV chain
+ * (gemma4_150/prefill_gpu.py:259-314, 348-352).
+ */
+int sb_attn_prefill(const void* q16, const void* k16, const void* v16, void* out16, int s_len,
+                    int n_heads, int head_dim, void* stream);
+
 /* out[r, i] = gelu_tanh(gu[r, 2i]) * gu[r, 2i + 1]: the fused gate|up weight keeps
  * gate row i and up row i adjacent, so its output interleaves them.
  * Replaces geglu_b (gemma4_150/kernels_dsl.py:259) / gemma4/reference.py:148-150. */

@@ -1,0 +1,390 @@
+// Fused causal prefill attention on tcgen05 (sb_attn_prefill): one kernel for
+// softmax(q k^T) v over a prompt, replacing the three-kernel chain (f32 score
+// GEMM, causal softmax, P.V GEMM) and its S x S x n_heads score round trip
+// through HBM.
+//
+// Shapes: q [S * nh rows][D] f16 with row = token * nh + head (every query
+// head shares the single K/V head), k, v [S][D] f16, out [S * nh][D] f16,
+// D = head_dim in {64, 128, 256} (a template parameter).
+// Scores are unscaled (q and k are RMS-normalised upstream) and causal: row
+// (t, h) sees keys 0..t.
+//
+// A CTA owns 128 query rows (16 tokens x 8 heads for Gemma-4-E2B) and walks
+// the key blocks of 64 keys that they can see:
+//   warp 0      TMA: the Q tile [128 x D] once, then K_j and V_j (each
+//               [64 keys x D], 128B-swizzled boxes of 64 columns) into a
+//               two-deep ring.
+//   warp 1      one thread issues tcgen05.mma: S_j = Q K_j^T (M 128, N 64,
+//               D/16 k-steps, A and B from shared memory) into a two-deep ring
+//               of 64-column TMEM score buffers, then O += P_j V_j (M 128, N D,
+//               K 64; P_j from TMEM, V_j MN-major from shared memory) into D
+//               accumulator columns.  S_{j+1} is issued before O += P_j V_j so
+//               the softmax of block j+1 overlaps the P.V MMAs of block j.
+//   warps 2..5  one thread per query row (its TMEM lane): reads S_j, masks,
+//               and forms p = 2^(s log2 e - m) in f16 with a running maximum m
+//               that is raised -- rescaling O and the row sum by 2^(m_old - m)
+//               -- only when the block maximum exceeds it by more than 2^8, so
+//               O is touched rarely and p stays below 256; writes P_j into TMEM
+//               for the MMA.  At the end: O / (row sum) -> f16 -> out.
+// TMEM: O [0, D), S ring [D, D + 128), P ring [D + 128, D + 192).
+//
+// Every mbarrier wait is bounded (2 s of %globaltimer); a stuck pipeline
+// raises a shared abort flag, records SB_ERR_TIMEOUT and unwinds.  No TMA
+// multicast is used.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "tmap.cuh"
+
+namespace {
+
+constexpr int QR = 128;  // query rows per CTA
+constexpr int KB = 64;   // keys per block
+constexpr int WARPS = 6;
+
+template <int HD>
+struct Cfg {
+  static constexpr int Q_BYTES = QR * HD * 2;   // HD/64 boxes [128 rows x 64 cols]
+  static constexpr int KV_BYTES = KB * HD * 2;  // HD/64 boxes [64 keys x 64 cols]
+  static constexpr int OFF_K = Q_BYTES;
+  static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + 2 * KV_BYTES;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;  // + barriers + 1 KB alignment slack
+  static constexpr uint32_t TM_O = 0, TM_S = HD, TM_P = HD + 2 * KB;
+  static constexpr uint32_t TM_COLS = HD + 3 * KB <= 256 ? 256 : 512;
+};
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescale = 8.f;  // log2 units
+
+struct Bars {
+  uint64_t q_full;
+  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+  uint64_t s_full[2], s_free[2], p_full[2], p_free[2];
+  uint64_t o_final;
+  uint64_t drain;
+  uint32_t tmem_slot;
+  int abort;
+};
+static_assert(sizeof(Bars) <= 256, "barrier block");
+
+struct Params {
+  __half* out;
+  int* err;
+  int rows;   // S * nh
+  int nh;
+  int s_len;  // S (keys = queries' tokens)
+};
+
+__device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = sbd::global_ns();
+  while (!sbd::mbar_try_wait(bar, parity)) {
+    if (sbd::global_ns() - t0 > sbd::kWaitLimitNs) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  sbd::tmem_st_32x32b_x16(taddr, *reinterpret_cast<const uint32_t(*)[16]>(&r[0]));
+  sbd::tmem_st_32x32b_x16(taddr + 16, *reinterpret_cast<const uint32_t(*)[16]>(&r[16]));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+    attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using C = Cfg<HD>;
+  constexpr int Q_BYTES = C::Q_BYTES, KV_BYTES = C::KV_BYTES, OFF_K = C::OFF_K, OFF_V = C::OFF_V;
+  constexpr int OFF_BAR = C::OFF_BAR;
+  constexpr uint32_t TM_O = C::TM_O, TM_S = C::TM_S, TM_P = C::TM_P, TM_COLS = C::TM_COLS;
+  constexpr int NBOX = HD / 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
+  volatile int* abort = &bars->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // heaviest tiles (latest tokens) first
+  const int tile = gridDim.x - 1 - blockIdx.x;
+  const int r0 = tile * QR;
+  const int tok_hi = min(p.s_len - 1, (min(r0 + QR, p.rows) - 1) / p.nh);
+  const int nb = tok_hi / KB + 1;  // key blocks this tile can see
+
+  if (threadIdx.x == 0) {
+    sbd::mbar_init(&bars->q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      sbd::mbar_init(&bars->k_full[i], 1);
+      sbd::mbar_init(&bars->k_empty[i], 1);
+      sbd::mbar_init(&bars->v_full[i], 1);
+      sbd::mbar_init(&bars->v_empty[i], 1);
+      sbd::mbar_init(&bars->s_full[i], 1);
+      sbd::mbar_init(&bars->s_free[i], 4);
+      sbd::mbar_init(&bars->p_full[i], 4);
+      sbd::mbar_init(&bars->p_free[i], 1);
+    }
+    sbd::mbar_init(&bars->o_final, 1);
+    sbd::mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    sbd::fence_mbar_init();
+    sbd::fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    sbd::prefetch_tmap(&tmQ);
+    sbd::prefetch_tmap(&tmK);
+    sbd::prefetch_tmap(&tmV);
+  }
+  if (warp == 1) {
+    sbd::tmem_alloc(&bars->tmem_slot, TM_COLS);
+    sbd::tmem_relinquish();
+  }
+  sbd::tc_fence_before();
+  __syncthreads();
+  sbd::tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+  bool mma_issued = false;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int issued_k = 0, issued_v = 0;
+      sbd::mbar_arrive_expect_tx(&bars->q_full, Q_BYTES);
+#pragma unroll
+      for (int b = 0; b < NBOX; ++b) sbd::tma_load_2d(&tmQ, &bars->q_full, smem + b * (QR * 128), 64 * b, r0);
+      for (int j = 0; j < nb; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = ((j >> 1) & 1) ^ 1;
+        if (!sbd::mbar_wait(&bars->k_empty[st], ph, abort, p.err)) break;
+        sbd::mbar_arrive_expect_tx(&bars->k_full[st], KV_BYTES);
+#pragma unroll
+        for (int b = 0; b < NBOX; ++b)
+          sbd::tma_load_2d(&tmK, &bars->k_full[st], smem + OFF_K + st * KV_BYTES + b * (KB * 128), 64 * b, j * KB);
+        issued_k = j + 1;
+        if (!sbd::mbar_wait(&bars->v_empty[st], ph, abort, p.err)) break;
+        sbd::mbar_arrive_expect_tx(&bars->v_full[st], KV_BYTES);
+#pragma unroll
+        for (int b = 0; b < NBOX; ++b)
+          sbd::tma_load_2d(&tmV, &bars->v_full[st], smem + OFF_V + st * KV_BYTES + b * (KB * 128), 64 * b, j * KB);
+        issued_v = j + 1;
+      }
+      if (*abort) {
+        // let copies in flight land before this CTA's shared memory is released
+        drain_wait(&bars->q_full, 0);
+        for (int j = max(0, issued_k - 2); j < issued_k; ++j) drain_wait(&bars->k_full[j & 1], (j >> 1) & 1);
+        for (int j = max(0, issued_v - 2); j < issued_v; ++j) drain_wait(&bars->v_full[j & 1], (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = sbd::umma_idesc_f16(QR, KB, 0, 0);
+      constexpr uint32_t idesc_o = sbd::umma_idesc_f16(QR, HD, 0, 1);
+      const uint32_t qbase = sbd::smem_u32(smem);
+      bool ok = sbd::mbar_wait(&bars->q_full, 0, abort, p.err);
+      for (int j = 0; j <= nb && ok; ++j) {
+        if (j < nb) {
+          // S_j = Q K_j^T
+          const int st = j & 1;
+          ok = sbd::mbar_wait(&bars->k_full[st], (j >> 1) & 1, abort, p.err) &&
+               sbd::mbar_wait(&bars->s_free[st], ((j >> 1) & 1) ^ 1, abort, p.err);
+          if (!ok) break;
+          sbd::tc_fence_after();
+          const uint32_t kbase = sbd::smem_u32(smem + OFF_K + st * KV_BYTES);
+#pragma unroll
+          for (int ks = 0; ks < HD / 16; ++ks) {
+            const uint64_t adesc =
+                sbd::umma_desc(qbase + (ks >> 2) * (QR * 128) + (ks & 3) * 32, 16, 1024, sbd::kLayoutSwizzle128B);
+            const uint64_t bdesc =
+                sbd::umma_desc(kbase + (ks >> 2) * (KB * 128) + (ks & 3) * 32, 16, 1024, sbd::kLayoutSwizzle128B);
+            sbd::umma_f16(tmem + TM_S + st * KB, adesc, bdesc, idesc_s, ks > 0 ? 1u : 0u);
+          }
+          mma_issued = true;
+          sbd::umma_commit(&bars->s_full[st]);
+          sbd::umma_commit(&bars->k_empty[st]);
+        }
+        if (j >= 1) {
+          // O += P_i V_i
+          const int i = j - 1, st = i & 1;
+          ok = sbd::mbar_wait(&bars->p_full[st], (i >> 1) & 1, abort, p.err) &&
+               sbd::mbar_wait(&bars->v_full[st], (i >> 1) & 1, abort, p.err);
+          if (!ok) break;
+          sbd::tc_fence_after();
+          const uint32_t vbase = sbd::smem_u32(smem + OFF_V + st * KV_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < KB / 16; ++kk) {
+            const uint64_t bdesc = sbd::umma_desc(vbase + kk * 2048, KB * 128, 1024, sbd::kLayoutSwizzle128B);
+            sbd::umma_f16_ts(tmem + TM_O, tmem + TM_P + st * 32 + kk * 8, bdesc, idesc_o,
+                             (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          sbd::umma_commit(&bars->p_free[st]);
+          sbd::umma_commit(&bars->v_empty[st]);
+        }
+      }
+      if (ok) sbd::umma_commit(&bars->o_final);
+      if (mma_issued) {
+        // every MMA issued has finished before TMEM is released
+        sbd::umma_commit(&bars->drain);
+        drain_wait(&bars->drain, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax / epilogue (warps 2..5)
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int r = r0 + row;
+    const bool row_ok = r < p.rows;
+    const int token = row_ok ? r / p.nh : -1;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    float m_used = 0.f, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nb && ok; ++j) {
+      const int st = j & 1;
+      ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait(&bars->s_full[st], (j >> 1) & 1, abort, p.err));
+      if (!ok) break;
+      sbd::tc_fence_after();
+      uint32_t sv[2][32];
+      sbd::tmem_ld_32x32b_x32(lane_base + TM_S + st * KB, sv[0]);
+      sbd::tmem_ld_32x32b_x32(lane_base + TM_S + st * KB + 32, sv[1]);
+      sbd::tmem_wait_ld();
+      sbd::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sbd::mbar_arrive(&bars->s_free[st]);
+      // causal mask: key j*KB + c is visible to this row when it is <= token
+      const int nvis = max(0, min(KB, token - j * KB + 1));
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < KB; ++c)
+        if (c < nvis) mx = fmaxf(mx, __uint_as_float(sv[c >> 5][c & 31]));
+      const float mx2 = mx * kLog2e;
+      if (j == 0) {
+        m_used = nvis > 0 ? mx2 : 0.f;
+      } else {
+        const bool need = nvis > 0 && mx2 > m_used + kRescale;
+        if (__any_sync(0xFFFFFFFFu, need)) {
+          // O must be quiet: wait for O += P_{j-1} V_{j-1}
+          ok = __all_sync(0xFFFFFFFFu,
+                          sbd::mbar_wait(&bars->p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, p.err));
+          if (!ok) break;
+          sbd::tc_fence_after();
+          const float alpha = need ? exp2f(m_used - mx2) : 1.f;
+          for (int cc = 0; cc < HD / 32; ++cc) {
+            uint32_t ov[32];
+            sbd::tmem_ld_32x32b_x32(lane_base + TM_O + cc * 32, ov);
+            sbd::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+            tmem_st_x32(lane_base + TM_O + cc * 32, ov);
+          }
+          sbd::tmem_wait_st();
+          l *= alpha;
+          if (need) m_used = mx2;
+        }
+      }
+      // p = 2^(s log2 e - m_used) in f16, packed two keys per TMEM column
+      uint32_t pk[32];
+      float ls = 0.f;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int c = 2 * e;
+        const float p0 = c < nvis ? exp2f(__uint_as_float(sv[c >> 5][c & 31]) * kLog2e - m_used) : 0.f;
+        const float p1 = c + 1 < nvis ? exp2f(__uint_as_float(sv[(c + 1) >> 5][(c + 1) & 31]) * kLog2e - m_used) : 0.f;
+        const __half2 h = __floats2half2_rn(p0, p1);
+        ls += __low2float(h) + __high2float(h);
+        pk[e] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      l += ls;
+      // the P buffer is free once O += P_{j-2} V_{j-2} has run
+      if (j >= 2) {
+        ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait(&bars->p_free[st], ((j - 2) >> 1) & 1, abort, p.err));
+        if (!ok) break;
+        sbd::tc_fence_after();
+      }
+      tmem_st_x32(lane_base + TM_P + st * 32, pk);
+      sbd::tmem_wait_st();
+      sbd::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sbd::mbar_arrive(&bars->p_full[st]);
+    }
+    // ------------------------------------------------------------ epilogue: O / l -> f16
+    if (ok) ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait(&bars->o_final, 0, abort, p.err));
+    if (ok) {
+      sbd::tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __half* dst = p.out + static_cast<size_t>(r) * HD;
+      for (int cc = 0; cc < HD / 32; ++cc) {
+        uint32_t ov[32];
+        sbd::tmem_ld_32x32b_x32(lane_base + TM_O + cc * 32, ov);
+        sbd::tmem_wait_ld();
+        if (!row_ok) continue;
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          uint32_t o4[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const __half2 h = __floats2half2_rn(__uint_as_float(ov[e + 2 * q]) * inv,
+                                                __uint_as_float(ov[e + 2 * q + 1]) * inv);
+            o4[q] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          *reinterpret_cast<uint4*>(dst + cc * 32 + e) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+        }
+      }
+    }
+  }
+
+  sbd::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sbd::tc_fence_after();
+    sbd::tmem_dealloc(tmem, TM_COLS);
+  }
+}
+
+template <int HD>
+int launch_attn(const void* q16, const void* k16, const void* v16, void* out16, int s_len, int n_heads,
+                cudaStream_t stream) {
+  using C = Cfg<HD>;
+  const long long rows = static_cast<long long>(s_len) * n_heads;
+  CUtensorMap tq, tk, tv;
+  int rc = sb::make_map(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q16, HD, rows, HD, 64, QR, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = sb::make_map(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, k16, HD, s_len, HD, 64, KB, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = sb::make_map(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, v16, HD, s_len, HD, 64, KB, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  static bool done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !done[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(attn_prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return sb::cuda_fail(e, "attn_prefill_kernel smem attribute");
+    done[dev] = true;
+  }
+  Params p{};
+  p.out = static_cast<__half*>(out16);
+  p.err = sb::device_error_word();
+  p.rows = static_cast<int>(rows);
+  p.nh = n_heads;
+  p.s_len = s_len;
+  const int grid = static_cast<int>((rows + QR - 1) / QR);
+  attn_prefill_kernel<HD><<<grid, WARPS * 32, C::SMEM, stream>>>(tq, tk, tv, p);
+  return sb::launch_status("attn_prefill_kernel");
+}
+
+}  // namespace
+
+extern "C" int sb_attn_prefill(const void* q16, const void* k16, const void* v16, void* out16, int s_len,
+                               int n_heads, int head_dim, void* stream) {
+  SB_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256,
+               "sb_attn_prefill: head_dim must be 64, 128 or 256");
+  SB_CHECK_ARG(s_len >= 0 && n_heads >= 1, "sb_attn_prefill: bad sizes");
+  if (s_len == 0) return SB_OK;
+  SB_CHECK_ARG(q16 && k16 && v16 && out16, "sb_attn_prefill: null pointer");
+  if (!sb::aligned(q16, 16) || !sb::aligned(k16, 16) || !sb::aligned(v16, 16) || !sb::aligned(out16, 16))
+    return sb::fail(SB_ERR_ALIGN, "sb_attn_prefill: q, k, v and out must be 16-byte aligned");
+  SB_CHECK_ARG(static_cast<long long>(s_len) * n_heads < (1ll << 31), "sb_attn_prefill: too many rows");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (head_dim) {
+    case 64: return launch_attn<64>(q16, k16, v16, out16, s_len, n_heads, s);
+    case 128: return launch_attn<128>(q16, k16, v16, out16, s_len, n_heads, s);
+    default: return launch_attn<256>(q16, k16, v16, out16, s_len, n_heads, s);
+  }
+}

@@ -16,14 +16,19 @@
 // tensor memory.  A CTA owns 128 weight rows x 256 tokens; per k-block:
 //   warp 0      TMA: activation tile [256 tokens x 64] f16 (128B swizzle, the
 //               MMA's B operand) and the packed tile [128 rows x 32 bytes].
-//   warps 2..9  dequant: thread = one weight row (TMEM lane) and one 32-value
-//               group; f16(scale * (q - 8)) with exact f16 math, written with
-//               tcgen05.st into a 4-stage ring of 32-column A slots in TMEM.
-//               The tile's group scales are loaded into shared memory once.
+//   warps 2..17 dequant, in two groups of 8 that take alternate k-blocks (a
+//               k-block's dequant chain -- waits, scale and nibble reads,
+//               unpack, tcgen05.st, hand-off -- is longer than its MMAs, so
+//               two run at once): thread = one weight row (TMEM lane) and
+//               one 32-value group; f16(scale * (q - 8)) with exact f16 math,
+//               written with tcgen05.st into a 4-stage ring of 32-column A
+//               slots in TMEM.  The tile's group scales are loaded into shared
+//               memory once, transposed to [group][row] so that a warp's 32
+//               rows read 32 consecutive scales.
 //   warp 1      tcgen05.mma.cta_group::1.kind::f16 with A from TMEM (M=128
 //               weight rows, N=256 tokens, K=16), accumulating D^T in 256
 //               TMEM columns.
-//   warps 2..9  epilogue: lane = output feature, column = token, so a warp's
+//   warps 2..17 epilogue: lane = output feature, column = token, so a warp's
 //               stores to C[token][feature] are contiguous.
 // Putting the dequantised weight in TMEM keeps it out of shared memory (no
 // 32 KB store + reload per k-block) and halves the dequant work per FLOP
@@ -38,6 +43,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tmap.cuh"
 
 namespace {
 
@@ -55,7 +61,9 @@ constexpr int Q_PACK_BYTES = QW * BK / 2;    // 4 KB packed stage
 constexpr int Q_STAGES = 4;                  // shared-memory load stages
 constexpr int Q_ASLOTS = 4;                  // TMEM A slots, 32 columns (64 k) each
 constexpr int Q_SCALE_BYTES = 48 * 1024;     // the tile's group scales
-constexpr int Q_WARPS = 10;                  // TMA, MMA, 8 dequant/epilogue
+constexpr int Q_DQ_GROUPS = 2;               // dequant warp groups, taking alternate k-blocks
+constexpr int Q_DQ_WARPS = 8 * Q_DQ_GROUPS;  // a group: 4 TMEM lane quadrants x 2 k halves
+constexpr int Q_WARPS = 2 + Q_DQ_WARPS;      // TMA, MMA, dequant/epilogue
 constexpr int Q_TMEM_COLS = 512;             // 256 accumulator + 4 x 32 A slots
 constexpr int Q_OFF_PACK = Q_STAGES * Q_ACT_BYTES;
 constexpr int Q_OFF_SCALE = Q_OFF_PACK + Q_STAGES * Q_PACK_BYTES;
@@ -369,30 +377,71 @@ __global__ void __launch_bounds__(Q_WARPS * 32, 1)
       sbd::umma_commit(&bars->accum);
     }
   } else {
-    // ------------------------------------------------------------ dequant producers (warps 2..9)
-    const int quad = warp & 3;          // TMEM lane quadrant this warp may access
-    const int khalf = (warp - 2) >> 2;  // which 32-value group of the k-block
-    const int r = quad * 32 + lane;     // weight row within the tile
-    const int dt = threadIdx.x - 64;    // 0..255
-    // the tile's scales -> shared memory, in their storage type
+    // ------------------------------------------------------------ dequant producers (warps 2..17)
+    const int dw = warp - 2;             // 0..15
+    const int grp = dw >> 3;             // k-blocks kb with kb % Q_DQ_GROUPS == grp
+    const int quad = warp & 3;           // TMEM lane quadrant this warp may access
+    const int khalf = (dw & 7) >> 2;     // which 32-value group of the k-block
+    const int r = quad * 32 + lane;      // weight row within the tile
+    const int dt = threadIdx.x - 64;     // 0..511
+    // the tile's scales -> shared memory [group][row], in their storage type
     const int esz = p.scale_f16 ? 2 : 4;
     uint8_t* sct = smem + Q_OFF_SCALE;
-    for (int i = dt; i < QW * gs; i += 256) {
-      const int rr = i / gs, g = i - rr * gs;
-      const int row = w0 + rr;
-      const size_t si = static_cast<size_t>(row) * gps + g_lo + g;
-      if (esz == 2) {
-        reinterpret_cast<__half*>(sct)[i] = row < p.n ? static_cast<const __half*>(p.scales)[si] : __float2half(0.f);
-      } else {
-        reinterpret_cast<float*>(sct)[i] = row < p.n ? static_cast<const float*>(p.scales)[si] : 0.f;
+    const int rb = gs * esz;             // bytes of one row's scales in this split
+    const uint8_t* sg = static_cast<const uint8_t*>(p.scales);
+    const bool vec = (reinterpret_cast<uintptr_t>(sg) % 16 == 0) && (gps * esz) % 16 == 0 && (g_lo * esz) % 16 == 0 &&
+                     rb % 16 == 0;
+    if (vec) {
+      // 16-byte chunks, all loads of a thread in flight together; chunk c is
+      // row c % QW, bytes [16 (c / QW), +16) of that row's span
+      constexpr int kMaxChunks = Q_SCALE_BYTES / 16 / (Q_DQ_WARPS * 32);
+      const int chunks = QW * (rb / 16);
+      uint4 v[kMaxChunks];
+#pragma unroll
+      for (int i = 0; i < kMaxChunks; ++i) {
+        const int c = dt + i * Q_DQ_WARPS * 32;
+        const int rr = c % QW, cb = c / QW;
+        v[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (c < chunks && w0 + rr < p.n)
+          v[i] = __ldg(reinterpret_cast<const uint4*>(sg + (static_cast<size_t>(w0 + rr) * gps + g_lo) * esz) + cb);
+      }
+#pragma unroll
+      for (int i = 0; i < kMaxChunks; ++i) {
+        const int c = dt + i * Q_DQ_WARPS * 32;
+        if (c >= chunks) break;
+        const int rr = c % QW, g0 = (c / QW) * (16 / esz);
+        const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+        if (esz == 2) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            reinterpret_cast<uint16_t*>(sct)[(g0 + e) * QW + rr] = static_cast<uint16_t>(wv[e >> 1] >> (16 * (e & 1)));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) reinterpret_cast<uint32_t*>(sct)[(g0 + e) * QW + rr] = wv[e];
+        }
+      }
+    } else {
+      for (int i = dt; i < QW * gs; i += Q_DQ_WARPS * 32) {
+        const int g = i / QW, rr = i - g * QW;
+        const int row = w0 + rr;
+        const size_t si = static_cast<size_t>(row) * gps + g_lo + g;
+        if (esz == 2) {
+          reinterpret_cast<__half*>(sct)[i] = row < p.n ? static_cast<const __half*>(p.scales)[si] : __float2half(0.f);
+        } else {
+          reinterpret_cast<float*>(sct)[i] = row < p.n ? static_cast<const float*>(p.scales)[si] : 0.f;
+        }
       }
     }
-    sbd::named_bar_sync(1, 256);
+    sbd::named_bar_sync(1, Q_DQ_WARPS * 32);
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    for (int kb = 0; kb < nkb; ++kb) {
+    // scale group of this thread's 32 values, advanced per k-block step when
+    // the group size divides the step (the usual case), else recomputed
+    const int kstep = Q_DQ_GROUPS * BK;
+    const int gstep = kstep % p.group == 0 ? kstep / p.group : 0;
+    int gi = ((kb0 + grp) * BK + khalf * 32) / p.group - g_lo;
+    for (int kb = grp; kb < nkb; kb += Q_DQ_GROUPS) {
       const int s = kb % S, slot = kb % T;
-      const int kv = (kb0 + kb) * BK + khalf * 32;
-      const int gi = kv / p.group - g_lo;
+      if (gstep == 0) gi = ((kb0 + kb) * BK + khalf * 32) / p.group - g_lo;
       bool ok = sbd::mbar_wait(&bars->full[s], (kb / S) & 1, abort, p.err);
       if (ok) ok = sbd::mbar_wait(&bars->dempty[slot], ((kb / T) & 1) ^ 1, abort, p.err);
       if (!__all_sync(0xFFFFFFFFu, ok)) break;
@@ -401,11 +450,11 @@ __global__ void __launch_bounds__(Q_WARPS * 32, 1)
       const uint32_t words[4] = {q.x, q.y, q.z, q.w};
       uint32_t o[16];
       if (p.scale_f16) {
-        const __half2 s2 = __half2half2(reinterpret_cast<const __half*>(sct)[r * gs + gi]);
+        const __half2 s2 = __half2half2(reinterpret_cast<const __half*>(sct)[gi * QW + r]);
 #pragma unroll
         for (int j = 0; j < 4; ++j) dq8_half(words[j], s2, o + 4 * j);
       } else {
-        const float sf = reinterpret_cast<const float*>(sct)[r * gs + gi];
+        const float sf = reinterpret_cast<const float*>(sct)[gi * QW + r];
 #pragma unroll
         for (int j = 0; j < 4; ++j) dq8_float(words[j], sf, o + 4 * j);
       }
@@ -417,17 +466,19 @@ __global__ void __launch_bounds__(Q_WARPS * 32, 1)
         sbd::mbar_arrive(&bars->dfull[slot]);
         sbd::mbar_arrive(&bars->empty[s]);
       }
+      gi += gstep;
     }
     // ------------------------------------------------------------ epilogue
-    // D^T: TMEM lane = weight row (output feature), column = token.
+    // D^T: TMEM lane = weight row (output feature), column = token; warp dw
+    // drains tokens [64 (dw / 4), +64) of its lane quadrant.
     const bool ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait(&bars->accum, 0, abort, p.err));
     if (ok) {
       sbd::tc_fence_after();
       const int feat = w0 + r;
       const bool feat_ok = feat < p.n;
-      for (int cc = 0; cc < 4; ++cc) {
-        const int col = khalf * 128 + cc * 32;  // token offset within the tile
-        if (t0 + col >= p.m) break;             // warp-uniform
+      for (int cc = 0; cc < 2; ++cc) {
+        const int col = (dw >> 2) * 64 + cc * 32;  // token offset within the tile
+        if (t0 + col >= p.m) break;                 // warp-uniform
         uint32_t v[32];
         sbd::tmem_ld_32x32b_x32(lane_addr + col, v);
         sbd::tmem_wait_ld();
@@ -469,32 +520,7 @@ __global__ void splitk_finalize_kernel(const float* __restrict__ ws, __half* __r
 }
 
 // ---------------------------------------------------------------- host side
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-int make_map(CUtensorMap* map, CUtensorMapDataType dt, int elt, const void* base, uint64_t inner, uint64_t outer,
-             uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
-  auto fn = encode_fn();
-  if (!fn) return sb::fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_stride_elems * elt};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return sb::fail(SB_ERR_ARG, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
-  return SB_OK;
-}
+using sb::make_map;
 
 template <typename K>
 int set_smem(K kernel, int bytes, bool (&done)[64]) {

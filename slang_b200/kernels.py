@@ -128,6 +128,25 @@ def gemm(A: torch.Tensor, W: torch.Tensor, C: torch.Tensor, M: int, N: int, K: i
     return C
 
 
+def attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal prompt attention (the reference's attn_prefill / _attn_gemm,
+    gemma4_150/prefill_gpu.py:259-314): q [S, nh, hd], k, v [S, hd] f16 ->
+    out [S, nh, hd] f16 = softmax(q k^T, causal) v, one fused kernel
+    (hd in {64, 128, 256})."""
+    for t, nm in ((q, "q"), (k, "k"), (v, "v")):
+        _need(t, nm, (torch.float16,))
+        if not t.is_contiguous():
+            raise ValueError(f"{nm} must be contiguous")
+    S, nh, hd = q.shape
+    if k.shape[0] < S or v.shape[0] < S or k.shape[1] != hd or v.shape[1] != hd:
+        raise ValueError("k and v must be [>= S, head_dim]")
+    if out is None:
+        out = torch.empty_like(q)
+    _need(out, "out", (torch.float16,))
+    _lib.call("sb_attn_prefill", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), S, nh, hd, _stream())
+    return out
+
+
 def gemm_q4(A: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, C: torch.Tensor | None = None,
             alpha: float = 1.0, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Fused ``_dq`` + ``_gemm``: ``C = f16(alpha * A @ dq_f16(W)^T)``."""

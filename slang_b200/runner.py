@@ -10,8 +10,9 @@ Host orchestration mirroring the reference's runners:
     (gemma4_150/metal_runner.py:439-468 keeps ``gen`` on the GPU the same way).
   * ``Runner.prefill`` is ``PrefillGPU.prefill`` (gemma4_150/prefill_gpu.py:398-436):
     layers outer, tokens inner; every projection is one fused int4 tcgen05
-    GEMM at M = prompt length, attention is QK^T (f32 scores) -> causal
-    softmax -> PV on the tcgen05 f16 GEMM; it returns the first greedy token.
+    GEMM at M = prompt length, attention is one fused causal tcgen05 kernel
+    (online softmax, scores never leave the SM); it returns the first greedy
+    token.
   * ``Runner.prefill_tokenwise`` feeds the prompt through the decode step one
     token at a time (the reference's per-token path, used when batched prefill
     is off, gemma4_150/metal_runner.py:418-425): f32 activations throughout.
@@ -248,16 +249,14 @@ class Runner:
             return self._pf
         dev = self.dm.device
         H, F, nh, hd = self.H, self.F, self.nh, self.hd
-        ldp = (S + 7) // 8 * 8
         f16 = lambda *s: torch.empty(s, dtype=torch.float16, device=dev)  # noqa: E731
         f32 = lambda *s: torch.empty(s, dtype=torch.float32, device=dev)  # noqa: E731
-        pf = {"S": S, "ldp": ldp,
+        pf = {"S": S,
               "tok": torch.empty(S, dtype=torch.int32, device=dev),
               "tok_host": torch.empty(S, dtype=torch.int32, pin_memory=True),
               "hid": f32(S, H), "h16": f16(S, H), "hlast": f32(S, H),
               "qkv16": f16(S, self.nqkv), "q16": f16(S, nh, hd), "k16": f16(self.max_seq, hd),
-              "v16": f16(self.max_seq, hd), "scores": f32(S * nh, ldp), "p16": f16(S * nh, ldp),
-              "attn16": f16(S, nh * hd), "o16": f16(S, H), "gu16": f16(S, 2 * F), "a16": f16(S, F),
+              "v16": f16(self.max_seq, hd), "attn16": f16(S, nh * hd), "o16": f16(S, H), "gu16": f16(S, 2 * F), "a16": f16(S, F),
               "d16": f16(S, H)}
         ws = max(kern.gemm_q4_workspace_size(S, n, k) for n, k in
                  ((self.nqkv, H), (H, self.qd), (2 * F, H), (H, F)))
@@ -315,7 +314,7 @@ class Runner:
         H, F = self.H, self.F
         split = lambda n, k: 1 if kern.gemm_q4_workspace_size(S, n, k) else 0  # noqa: E731
         per_layer = (4 + split(self.nqkv, H) + split(H, self.qd) + split(2 * F, H) + split(H, F)  # 4 projections
-                     + 1 + 3 + 2 + 1)  # prep; scores, softmax, PV; two add+norms; geglu
+                     + 1 + 1 + 2 + 1)  # prep; attention; two add+norms; geglu
         return 2 + len(self.dm.layers) * per_layer + 2
 
     def prefill_timed_gemms(self, tokens, seq: int = 0):
@@ -333,7 +332,7 @@ class Runner:
     def _prefill_ops(self, pf, S, seq, s, rec=None):
         dm, Ls = self.dm, self.dm.layers
         H, nh, hd, F = self.H, self.nh, self.hd, self.F
-        ldp, ws = pf["ldp"], pf["ws"]
+        ws = pf["ws"]
 
         def proj(name, A, W, C, K):
             if rec is not None:
@@ -355,13 +354,9 @@ class Runner:
                       L["k_norm"].data_ptr(), dm.cos.data_ptr(), dm.sin.data_ptr(), None, 0, S, nh, hd, self.eps,
                       pf["q16"].data_ptr(), None, self.kc[li].data_ptr() + kc_off, self.vc[li].data_ptr() + kc_off,
                       pf["k16"].data_ptr(), pf["v16"].data_ptr(), self.cache_stride, s)
-            # scores[S*nh, S] = q . k^T (f32), softmax, P . V
-            _lib.call("sb_gemm_f16_f32out", pf["q16"].data_ptr(), pf["k16"].data_ptr(), pf["scores"].data_ptr(),
-                      S * nh, S, hd, 1.0, 1, hd, hd, ldp, s)
-            _lib.call("sb_softmax_causal", pf["scores"].data_ptr(), ldp, S * nh, nh, 0, S, pf["p16"].data_ptr(),
-                      ldp, s)
-            _lib.call("sb_gemm_f16", pf["p16"].data_ptr(), pf["v16"].data_ptr(), pf["attn16"].data_ptr(),
-                      S * nh, hd, S, 1.0, 0, ldp, hd, hd, s)
+            # causal attention over the prompt: one fused kernel
+            _lib.call("sb_attn_prefill", pf["q16"].data_ptr(), pf["k16"].data_ptr(), pf["v16"].data_ptr(),
+                      pf["attn16"].data_ptr(), S, nh, hd, s)
             proj("o", pf["attn16"][:S], L["o"], pf["o16"][:S], self.qd)
             _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), pf["o16"].data_ptr(), _F16,
                       L["post_attn_norm"].data_ptr(), L["pre_ffn_norm"].data_ptr(), pf["hid"].data_ptr(), None,

@@ -150,6 +150,19 @@ int sb_gemm_f16_f32out(const void* a, const void* b, float* c, int m, int n, int
 int sb_gemm_q4(const void* a, const void* w, const void* scales, int scale_dtype, int group,
                void* c, int m, int n, int k, float alpha, int lda, int ldc,
                void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * sb_gemm_q4 with the gate|up GEGLU fused into the epilogue: W's rows are
+ * interleaved (gate row i at 2i, up row i at 2i + 1; n even) and
+ * out[t][i] = f16(gelu_tanh(g) * u) with g, u the f16-rounded GEMM outputs
+ * of rows 2i and 2i + 1 -- bit-for-bit sb_gemm_q4 followed by sb_geglu, with
+ * out [m][n/2] (row stride ldo) and no [m][n] intermediate.  Replaces the
+ * reference's gate/up GEMMs + geglu_b (gemma4_150/prefill_gpu.py:365-372;
+ * kernels_dsl.py:259).  Workspace as for sb_gemm_q4.
+ */
+int sb_gemm_q4_geglu(const void* a, const void* w, const void* scales, int scale_dtype, int group,
+                     void* out, int m, int n, int k, float alpha, int lda, int ldo, void* workspace,
+                     size_t workspace_bytes, void* stream);
 size_t sb_gemm_q4_workspace_size(int m, int n, int k);
 
 /*

@@ -240,6 +240,119 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// tanh-approximate GELU (the model's activation), shared by every kernel that
+// applies it so that fused and separate paths round identically.  Uses the
+// identity 0.5 x (1 + tanh z) = x / (1 + e^(-2z)) with the fast exponential
+// and division intrinsics (a few ulp of f32, far below the f16 rounding of the
+// activations it feeds); x -> -inf gives -0, x -> +inf gives x.
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float z2 = 1.5957691216057308f * (x + 0.044715f * x * x * x);  // 2 z
+  return __fdividef(x, 1.f + __expf(-z2));
+}
+
+// ---- thread-block clusters and distributed shared memory
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Barrier over every thread of every CTA in the cluster (release / acquire:
+// shared-memory writes before it are visible to peers' reads after it).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// The address of this CTA's shared-memory word `saddr` in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// ---- CTA-pair (cta_group::2) tensor-core forms.  A pair is two CTAs of a
+// cluster whose ranks differ in bit 0; the even one issues the MMAs.
+// TMEM allocation for the pair: one warp (the same warp id) in each CTA.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[M = 256 over the pair] += A (TMEM, this CTA's 128 rows in each CTA) x B
+// (each CTA's shared memory holds N/2 rows of B at the descriptor's address).
+__device__ __forceinline__ void umma_f16_ts_pair(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  const uint32_t z = 0;  // no output lanes disabled
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}" ::"r"(
+          tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z), "r"(z), "r"(z), "r"(z),
+      "r"(z)
+      : "memory");
+}
+// Arrive once on `bar` (same offset) in every CTA of `cta_mask` when the pair's
+// MMAs issued so far have completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+// 2D tiled TMA load into this CTA's shared memory whose completion is counted
+// on an mbarrier of the pair's even CTA (`bar_cluster`: a shared::cluster
+// address from mapa).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar_cluster, void* dst, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+// Arrive on an mbarrier of another CTA of the cluster (release at cluster scope).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+// try_wait with acquire at cluster scope (for barriers other CTAs arrive on).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      if (err) atomicExch(err, SB_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // UMMA shared-memory matrix descriptor (sm_100 format): start address, leading
 // and stride byte offsets (all >> 4), version 1 at bit 46, layout at bits 61-63.
 constexpr uint64_t kLayoutSwizzle128B = 2;

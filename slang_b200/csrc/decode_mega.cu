@@ -826,9 +826,7 @@ __device__ void merge(const Params& p, Smem& sm, int nc) {
   }
 }
 
-__device__ __forceinline__ float gelu_tanh(float x) {
-  return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
-}
+using sbd::gelu_tanh;
 
 // ---------------------------------------------------------------- the kernel
 __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(Params p) {

@@ -39,9 +39,7 @@ __device__ __forceinline__ float load_act(const void* p, int is_f16, size_t i) {
   return is_f16 ? __half2float(static_cast<const __half*>(p)[i]) : static_cast<const float*>(p)[i];
 }
 
-__device__ __forceinline__ float gelu_tanh(float x) {
-  return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
-}
+using sbd::gelu_tanh;
 
 // ---------------------------------------------------------------- embedding
 __global__ void embed_kernel(const uint8_t* __restrict__ emb, const void* __restrict__ scales, int sf16, int group,

@@ -58,9 +58,9 @@ constexpr int TMEM_COLS = 256;
 constexpr int QW = 128, QT = 256;
 constexpr int Q_ACT_BYTES = QT * BK * 2;     // 32 KB activation stage
 constexpr int Q_PACK_BYTES = QW * BK / 2;    // 4 KB packed stage
-constexpr int Q_STAGES = 4;                  // shared-memory load stages
+constexpr int Q_STAGES = 5;                  // shared-memory load stages (cover L2 latency under load + MMA)
 constexpr int Q_ASLOTS = 4;                  // TMEM A slots, 32 columns (64 k) each
-constexpr int Q_SCALE_BYTES = 48 * 1024;     // the tile's group scales
+constexpr int Q_SCALE_BYTES = 24 * 1024;     // the tile's group scales (a split's share of K)
 constexpr int Q_DQ_GROUPS = 2;               // dequant warp groups, taking alternate k-blocks
 constexpr int Q_DQ_WARPS = 8 * Q_DQ_GROUPS;  // a group: 4 TMEM lane quadrants x 2 k halves
 constexpr int Q_WARPS = 2 + Q_DQ_WARPS;      // TMA, MMA, dequant/epilogue
@@ -91,12 +91,14 @@ struct GemmParams {
   int* err;
   int m, n, k, ldc, group, scale_f16;
   int kb_per_split, kb_total;
+  int csplit;          // int4 kernel: > 1 when the K splits of a tile form a cluster and reduce in DSMEM
+  int geglu;           // int4 kernel: weight rows are interleaved (gate, up) pairs; C[t][i] = GEGLU of pair i
   float alpha;
 };
 
 struct Bars {
-  uint64_t full[4];
-  uint64_t empty[4];
+  uint64_t full[8];
+  uint64_t empty[8];
   uint64_t dfull[4];
   uint64_t dempty[4];
   uint64_t accum;
@@ -288,9 +290,193 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
 }
 
 // =====================================================================
-// int4 kernel: dequantised weight as the A operand in tensor memory
+// int4 kernels: dequantised weight as the A operand in tensor memory
 // =====================================================================
-// p.m = tokens (MMA N side), p.n = weight rows (MMA M side).
+// p.m = tokens (MMA N side), p.n = weight rows (MMA M side).  Two forms:
+//   gemm_q4_kernel       one CTA per 128 weight rows x 256 tokens (cta_group::1)
+//   gemm_q4_pair_kernel  a CTA pair per 256 weight rows x 256 tokens
+//                        (cta_group::2): each CTA dequantises its own 128
+//                        rows into its TMEM and loads half of the 256-token
+//                        activation tile; the even CTA issues M=256 MMAs that
+//                        read both halves.  Per SM this halves the activation
+//                        bytes loaded and read by the tensor core per FLOP,
+//                        which shared-memory bandwidth otherwise limits.
+// Both share the helpers below.
+
+// The tile's group scales [w0, w0 + 128) x [g_lo, g_lo + gs) -> shared memory
+// transposed to [group][row] in their storage type, by `nthreads` threads.
+__device__ __forceinline__ void load_scale_tile(const GemmParams& p, uint8_t* sct, int w0, int g_lo, int gs, int dt,
+                                                int nthreads) {
+  const int esz = p.scale_f16 ? 2 : 4;
+  const int gps = p.k / p.group;
+  const int rb = gs * esz;  // bytes of one row's scales in this split
+  const uint8_t* sg = static_cast<const uint8_t*>(p.scales);
+  const bool vec = (reinterpret_cast<uintptr_t>(sg) % 16 == 0) && (gps * esz) % 16 == 0 && (g_lo * esz) % 16 == 0 &&
+                   rb % 16 == 0;
+  if (vec) {
+    // 16-byte chunks, all loads of a thread in flight together; chunk c is
+    // row c % QW, bytes [16 (c / QW), +16) of that row's span
+    constexpr int kMaxChunks = Q_SCALE_BYTES / 16 / (Q_DQ_WARPS * 32);
+    const int chunks = QW * (rb / 16);
+    uint4 v[kMaxChunks];
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) {
+      const int c = dt + i * nthreads;
+      const int rr = c % QW, cb = c / QW;
+      v[i] = make_uint4(0u, 0u, 0u, 0u);
+      if (c < chunks && w0 + rr < p.n)
+        v[i] = __ldg(reinterpret_cast<const uint4*>(sg + (static_cast<size_t>(w0 + rr) * gps + g_lo) * esz) + cb);
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) {
+      const int c = dt + i * nthreads;
+      if (c >= chunks) break;
+      const int rr = c % QW, g0 = (c / QW) * (16 / esz);
+      const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      if (esz == 2) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          reinterpret_cast<uint16_t*>(sct)[(g0 + e) * QW + rr] = static_cast<uint16_t>(wv[e >> 1] >> (16 * (e & 1)));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) reinterpret_cast<uint32_t*>(sct)[(g0 + e) * QW + rr] = wv[e];
+      }
+    }
+  } else {
+    for (int i = dt; i < QW * gs; i += nthreads) {
+      const int g = i / QW, rr = i - g * QW;
+      const int row = w0 + rr;
+      const size_t si = static_cast<size_t>(row) * gps + g_lo + g;
+      if (esz == 2) {
+        reinterpret_cast<__half*>(sct)[i] = row < p.n ? static_cast<const __half*>(p.scales)[si] : __float2half(0.f);
+      } else {
+        reinterpret_cast<float*>(sct)[i] = row < p.n ? static_cast<const float*>(p.scales)[si] : 0.f;
+      }
+    }
+  }
+}
+
+// One thread's 32 values of a k-block: f16(scale * (q - 8)) packed in pairs.
+__device__ __forceinline__ void dq_group(const GemmParams& p, const uint8_t* sct, int gi, int r, uint4 q,
+                                         uint32_t (&o)[16]) {
+  const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+  if (p.scale_f16) {
+    const __half2 s2 = __half2half2(reinterpret_cast<const __half*>(sct)[gi * QW + r]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dq8_half(words[j], s2, o + 4 * j);
+  } else {
+    const float sf = reinterpret_cast<const float*>(sct)[gi * QW + r];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dq8_float(words[j], sf, o + 4 * j);
+  }
+}
+
+// Epilogue without split-K: D^T in TMEM (lane = weight row r, column = token);
+// warp dw (0..15) drains tokens [64 (dw / 4), +64) of its lane quadrant into
+// C (f16, or f32 split partials in p.ws, or GEGLU pairs).
+__device__ __forceinline__ void epilogue_direct(const GemmParams& p, uint32_t lane_addr, int dw, int r, int lane,
+                                                int w0, int t0, int split) {
+  const int feat = w0 + r;
+  const bool feat_ok = feat < p.n;
+  for (int cc = 0; cc < 2; ++cc) {
+    const int col = (dw >> 2) * 64 + cc * 32;  // token offset within the tile
+    if (t0 + col >= p.m) break;                 // warp-uniform
+    uint32_t v[32];
+    sbd::tmem_ld_32x32b_x32(lane_addr + col, v);
+    sbd::tmem_wait_ld();
+    if (p.ws) {
+      if (!feat_ok) continue;
+      float* dst = p.ws + (static_cast<size_t>(split) * p.m + t0 + col) * p.n + feat;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (t0 + col + j < p.m) dst[static_cast<size_t>(j) * p.n] = __uint_as_float(v[j]);
+    } else if (p.geglu) {
+      // lanes 2i, 2i + 1 hold gate and up of output feature feat / 2, rounded
+      // to f16 as the GEMM output would be; the even lane forms gelu(gate) * up
+      // for tokens col .. col + 15, the odd lane for col + 16 .. col + 31
+      const bool odd = lane & 1;
+      __half* dst = static_cast<__half*>(p.c) + static_cast<size_t>(t0 + col + (odd ? 16 : 0)) * p.ldc + (feat >> 1);
+      const int jt = t0 + col + (odd ? 16 : 0);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float lo = __half2float(__float2half_rn(p.alpha * __uint_as_float(v[j])));
+        const float hi = __half2float(__float2half_rn(p.alpha * __uint_as_float(v[16 + j])));
+        const float other = __shfl_xor_sync(0xFFFFFFFFu, odd ? lo : hi, 1);
+        const float g = odd ? other : lo, u = odd ? hi : other;
+        if (feat_ok && jt + j < p.m) dst[static_cast<size_t>(j) * p.ldc] = __float2half_rn(sbd::gelu_tanh(g) * u);
+      }
+    } else {
+      if (!feat_ok) continue;
+      __half* dst = static_cast<__half*>(p.c) + static_cast<size_t>(t0 + col) * p.ldc + feat;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (t0 + col + j < p.m) dst[static_cast<size_t>(j) * p.ldc] = __float2half_rn(p.alpha * __uint_as_float(v[j]));
+    }
+  }
+}
+
+// Split-K in a cluster: this split's partial tile -> its own shared memory
+// (idle activation stages) as [token column][weight row] f32.
+__device__ __forceinline__ void stash_partial(uint8_t* smem, uint32_t lane_addr, int dw, int r) {
+  sbd::fence_proxy_async_smem();
+  float* red = reinterpret_cast<float*>(smem);
+  for (int cc = 0; cc < 2; ++cc) {
+    const int col = (dw >> 2) * 64 + cc * 32;
+    uint32_t v[32];
+    sbd::tmem_ld_32x32b_x32(lane_addr + col, v);
+    sbd::tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) red[(col + j) * QW + r] = __uint_as_float(v[j]);
+  }
+}
+
+// Split-K reduction through distributed shared memory, by the 16 epilogue
+// warps (ew = 0..15): split `z` of `nz` sums token columns [z QT / nz,
+// (z + 1) QT / nz) of the tile over all splits in split order (the order and
+// rounding of splitk_finalize_kernel), split z' living in cluster CTA
+// rank_base + rank_stride * z'; then writes f16 (or GEGLU pairs).
+__device__ __forceinline__ void reduce_splits(const GemmParams& p, uint8_t* smem, int ew, int lane, int w0, int t0,
+                                              int z, int nz, int rank_base, int rank_stride) {
+  const int c_lo = z * QT / nz, c_hi = (z + 1) * QT / nz;
+  const uint32_t red0 = sbd::smem_u32(smem);
+  const int rr = lane * 4;  // weight rows rr .. rr + 3 of the tile
+  const int feat = w0 + rr;
+  for (int c = c_lo + ew; c < c_hi; c += Q_DQ_WARPS) {
+    if (t0 + c >= p.m) break;  // warp-uniform
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int zz = 0; zz < nz; ++zz) {
+      const float4 v = sbd::ld_dsmem_v4(sbd::mapa_shared(red0 + (c * QW + rr) * 4, rank_base + rank_stride * zz));
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    if (p.geglu) {
+      // rows (rr, rr + 1) and (rr + 2, rr + 3) are (gate, up) pairs
+      __half* dst = static_cast<__half*>(p.c) + static_cast<size_t>(t0 + c) * p.ldc + (feat >> 1);
+      const float g0 = __half2float(__float2half_rn(p.alpha * acc.x));
+      const float u0 = __half2float(__float2half_rn(p.alpha * acc.y));
+      const float g1 = __half2float(__float2half_rn(p.alpha * acc.z));
+      const float u1 = __half2float(__float2half_rn(p.alpha * acc.w));
+      if (feat + 1 < p.n) dst[0] = __float2half_rn(sbd::gelu_tanh(g0) * u0);
+      if (feat + 3 < p.n) dst[1] = __float2half_rn(sbd::gelu_tanh(g1) * u1);
+      continue;
+    }
+    __half* dst = static_cast<__half*>(p.c) + static_cast<size_t>(t0 + c) * p.ldc + feat;
+    const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+    if (feat + 4 <= p.n && (reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+      const __half2 h0 = __floats2half2_rn(p.alpha * vals[0], p.alpha * vals[1]);
+      const __half2 h1 = __floats2half2_rn(p.alpha * vals[2], p.alpha * vals[3]);
+      *reinterpret_cast<uint2*>(dst) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (feat + e < p.n) dst[e] = __float2half_rn(p.alpha * vals[e]);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(Q_WARPS * 32, 1)
     gemm_q4_kernel(const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ CUtensorMap tmW,
                    const GemmParams p) {
@@ -309,7 +495,6 @@ __global__ void __launch_bounds__(Q_WARPS * 32, 1)
   const int g_lo = (kb0 * BK) / p.group;
   const int g_hi = ((kb0 + nkb) * BK + p.group - 1) / p.group;
   const int gs = g_hi - g_lo;
-  const int gps = p.k / p.group;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -385,53 +570,8 @@ __global__ void __launch_bounds__(Q_WARPS * 32, 1)
     const int r = quad * 32 + lane;      // weight row within the tile
     const int dt = threadIdx.x - 64;     // 0..511
     // the tile's scales -> shared memory [group][row], in their storage type
-    const int esz = p.scale_f16 ? 2 : 4;
     uint8_t* sct = smem + Q_OFF_SCALE;
-    const int rb = gs * esz;             // bytes of one row's scales in this split
-    const uint8_t* sg = static_cast<const uint8_t*>(p.scales);
-    const bool vec = (reinterpret_cast<uintptr_t>(sg) % 16 == 0) && (gps * esz) % 16 == 0 && (g_lo * esz) % 16 == 0 &&
-                     rb % 16 == 0;
-    if (vec) {
-      // 16-byte chunks, all loads of a thread in flight together; chunk c is
-      // row c % QW, bytes [16 (c / QW), +16) of that row's span
-      constexpr int kMaxChunks = Q_SCALE_BYTES / 16 / (Q_DQ_WARPS * 32);
-      const int chunks = QW * (rb / 16);
-      uint4 v[kMaxChunks];
-#pragma unroll
-      for (int i = 0; i < kMaxChunks; ++i) {
-        const int c = dt + i * Q_DQ_WARPS * 32;
-        const int rr = c % QW, cb = c / QW;
-        v[i] = make_uint4(0u, 0u, 0u, 0u);
-        if (c < chunks && w0 + rr < p.n)
-          v[i] = __ldg(reinterpret_cast<const uint4*>(sg + (static_cast<size_t>(w0 + rr) * gps + g_lo) * esz) + cb);
-      }
-#pragma unroll
-      for (int i = 0; i < kMaxChunks; ++i) {
-        const int c = dt + i * Q_DQ_WARPS * 32;
-        if (c >= chunks) break;
-        const int rr = c % QW, g0 = (c / QW) * (16 / esz);
-        const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-        if (esz == 2) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            reinterpret_cast<uint16_t*>(sct)[(g0 + e) * QW + rr] = static_cast<uint16_t>(wv[e >> 1] >> (16 * (e & 1)));
-        } else {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) reinterpret_cast<uint32_t*>(sct)[(g0 + e) * QW + rr] = wv[e];
-        }
-      }
-    } else {
-      for (int i = dt; i < QW * gs; i += Q_DQ_WARPS * 32) {
-        const int g = i / QW, rr = i - g * QW;
-        const int row = w0 + rr;
-        const size_t si = static_cast<size_t>(row) * gps + g_lo + g;
-        if (esz == 2) {
-          reinterpret_cast<__half*>(sct)[i] = row < p.n ? static_cast<const __half*>(p.scales)[si] : __float2half(0.f);
-        } else {
-          reinterpret_cast<float*>(sct)[i] = row < p.n ? static_cast<const float*>(p.scales)[si] : 0.f;
-        }
-      }
-    }
+    load_scale_tile(p, sct, w0, g_lo, gs, dt, Q_DQ_WARPS * 32);
     sbd::named_bar_sync(1, Q_DQ_WARPS * 32);
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     // scale group of this thread's 32 values, advanced per k-block step when
@@ -447,17 +587,8 @@ __global__ void __launch_bounds__(Q_WARPS * 32, 1)
       if (!__all_sync(0xFFFFFFFFu, ok)) break;
       sbd::tc_fence_after();
       const uint4 q = *reinterpret_cast<const uint4*>(smem + Q_OFF_PACK + s * Q_PACK_BYTES + r * 32 + khalf * 16);
-      const uint32_t words[4] = {q.x, q.y, q.z, q.w};
       uint32_t o[16];
-      if (p.scale_f16) {
-        const __half2 s2 = __half2half2(reinterpret_cast<const __half*>(sct)[gi * QW + r]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) dq8_half(words[j], s2, o + 4 * j);
-      } else {
-        const float sf = reinterpret_cast<const float*>(sct)[gi * QW + r];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) dq8_float(words[j], sf, o + 4 * j);
-      }
+      dq_group(p, sct, gi, r, q, o);
       sbd::tmem_st_32x32b_x16(lane_addr + 256 + slot * 32 + khalf * 16, o);
       sbd::tmem_wait_st();
       sbd::tc_fence_before();
@@ -474,28 +605,20 @@ __global__ void __launch_bounds__(Q_WARPS * 32, 1)
     const bool ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait(&bars->accum, 0, abort, p.err));
     if (ok) {
       sbd::tc_fence_after();
-      const int feat = w0 + r;
-      const bool feat_ok = feat < p.n;
-      for (int cc = 0; cc < 2; ++cc) {
-        const int col = (dw >> 2) * 64 + cc * 32;  // token offset within the tile
-        if (t0 + col >= p.m) break;                 // warp-uniform
-        uint32_t v[32];
-        sbd::tmem_ld_32x32b_x32(lane_addr + col, v);
-        sbd::tmem_wait_ld();
-        if (!feat_ok) continue;
-        if (p.ws) {
-          float* dst = p.ws + (static_cast<size_t>(blockIdx.z) * p.m + t0 + col) * p.n + feat;
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (t0 + col + j < p.m) dst[static_cast<size_t>(j) * p.n] = __uint_as_float(v[j]);
-        } else {
-          __half* dst = static_cast<__half*>(p.c) + static_cast<size_t>(t0 + col) * p.ldc + feat;
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (t0 + col + j < p.m) dst[static_cast<size_t>(j) * p.ldc] = __float2half_rn(p.alpha * __uint_as_float(v[j]));
-        }
-      }
+      if (p.csplit > 1) stash_partial(smem, lane_addr, dw, r);
+      else epilogue_direct(p, lane_addr, dw, r, lane, w0, t0, blockIdx.z);
     }
+  }
+
+  if (p.csplit > 1) {
+    // every thread of every split reaches both cluster barriers (abort paths
+    // included), so a barrier only ever waits on peers' bounded waits
+    sbd::cluster_sync_all();
+    if (warp >= 2) {
+      const int rank = static_cast<int>(sbd::cluster_ctarank());
+      reduce_splits(p, smem, warp - 2, lane, w0, t0, rank, p.csplit, 0, 1);
+    }
+    sbd::cluster_sync_all();
   }
 
   sbd::tc_fence_before();
@@ -506,16 +629,240 @@ __global__ void __launch_bounds__(Q_WARPS * 32, 1)
   }
 }
 
+
+// ---- CTA-pair form (cta_group::2): 256 weight rows x 256 tokens per pair
+constexpr int P_STAGES = 8;                       // stages; stage s is also TMEM A slot s (256 + 8 x 32 columns)
+constexpr int P_SIGNALERS = 4;                    // odd CTA: warps forwarding "A slot ready" to the even CTA
+constexpr int P_WARPS = Q_WARPS + P_SIGNALERS;
+constexpr int P_ACT_BYTES = (QT / 2) * BK * 2;    // 16 KB: this CTA's 128 tokens of a k-block
+constexpr int P_OFF_PACK = P_STAGES * P_ACT_BYTES;
+constexpr int P_OFF_SCALE = P_OFF_PACK + P_STAGES * Q_PACK_BYTES;
+constexpr int P_OFF_BAR = P_OFF_SCALE + Q_SCALE_BYTES;
+constexpr int P_SMEM = P_OFF_BAR + 512 + 1024;
+static_assert(P_STAGES * P_ACT_BYTES >= QT * QW * 4, "split-K partial tile must fit the activation stages");
+
+// Stage s of k-block kb (s = kb % P_STAGES) is both an activation-half buffer
+// and TMEM A slot s, so one barrier tells the MMA issuer that k-block kb is
+// ready and one commit frees both.
+struct PairBars {
+  uint64_t ready[P_STAGES];   // even CTA: both activation halves landed (tx), its dequant group wrote
+                              // A slot s (8 arrives) and the odd CTA's did (1 forwarded arrive)
+  uint64_t empty[P_STAGES];   // each CTA: the pair's MMAs are done with stage / A slot s
+  uint64_t pfull[P_STAGES];   // each CTA: its packed tile of stage s landed
+  uint64_t pempty[P_STAGES];  // each CTA: its dequant warps are done with that packed tile
+  uint64_t dlocal[P_STAGES];  // odd CTA: its dequant group wrote A slot s (8 local arrives)
+  uint64_t accum;             // each CTA: its accumulator rows are final
+  uint32_t tmem_slot;
+  int abort;
+};
+static_assert(sizeof(PairBars) <= 512, "pair barrier block");
+
+// Cross-CTA hand-off: an arrive on the even CTA's barrier with release at
+// cluster scope costs about a microsecond, so the dequant warps only arrive on
+// local barriers and the odd CTA's signaller warps forward each slot (up to
+// P_SIGNALERS in flight).
+__global__ void __launch_bounds__(P_WARPS * 32, 1)
+    gemm_q4_pair_kernel(const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ CUtensorMap tmW,
+                        const GemmParams p) {
+  constexpr int S = P_STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  PairBars* bars = reinterpret_cast<PairBars*>(smem + P_OFF_BAR);
+  volatile int* abort = &bars->abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // cluster (2, 1, csplit): rank = pair position + 2 * split
+  const int rank = static_cast<int>(sbd::cluster_ctarank());
+  const int lead_rank = rank & ~1;
+  const bool lead = rank == lead_rank;
+  const uint16_t pair_mask = static_cast<uint16_t>(3u << lead_rank);
+  const int w0 = blockIdx.x * QW;                  // this CTA's 128 weight rows
+  const int t0 = blockIdx.y * QT;                  // the pair's 256 tokens
+  const int th = t0 + (rank & 1) * (QT / 2);       // this CTA's half of them
+  const int kb0 = blockIdx.z * p.kb_per_split;
+  const int nkb = min(p.kb_per_split, p.kb_total - kb0);
+  const int g_lo = (kb0 * BK) / p.group;
+  const int g_hi = ((kb0 + nkb) * BK + p.group - 1) / p.group;
+  const int gs = g_hi - g_lo;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      sbd::mbar_init(&bars->ready[i], 1 + 8 + 1);
+      sbd::mbar_init(&bars->empty[i], 1);
+      sbd::mbar_init(&bars->pfull[i], 1);
+      sbd::mbar_init(&bars->pempty[i], 8);
+      sbd::mbar_init(&bars->dlocal[i], 8);
+    }
+    sbd::mbar_init(&bars->accum, 1);
+    bars->abort = 0;
+    sbd::fence_mbar_init();
+    sbd::fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    sbd::prefetch_tmap(&tmAct);
+    sbd::prefetch_tmap(&tmW);
+  }
+  if (warp == 1) {
+    sbd::tmem_alloc_pair(&bars->tmem_slot, Q_TMEM_COLS);
+    sbd::tmem_relinquish_pair();
+  }
+  // barriers initialised and TMEM allocated in both CTAs before any cross-CTA use
+  sbd::tc_fence_before();
+  sbd::cluster_sync_all();
+  sbd::tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % S;
+        const uint32_t ph = ((kb / S) & 1) ^ 1;
+        const int k0 = (kb0 + kb) * BK;
+        if (!sbd::mbar_wait_cluster(&bars->empty[s], ph, abort, p.err)) break;
+        if (lead) sbd::mbar_arrive_expect_tx(&bars->ready[s], 2 * P_ACT_BYTES);
+        sbd::tma_load_2d_pair(&tmAct, sbd::mapa_shared(sbd::smem_u32(&bars->ready[s]), lead_rank),
+                              smem + s * P_ACT_BYTES, k0, th);
+        if (!sbd::mbar_wait(&bars->pempty[s], ph, abort, p.err)) break;
+        sbd::mbar_arrive_expect_tx(&bars->pfull[s], Q_PACK_BYTES);
+        sbd::tma_load_2d(&tmW, &bars->pfull[s], smem + P_OFF_PACK + s * Q_PACK_BYTES, k0 / 2, w0);
+        issued = kb + 1;
+      }
+      if (*abort) {
+        // let copies in flight land before shared memory is released: the even
+        // CTA's activation barriers count both CTAs' halves
+        // (ready also needs the dequant arrivals, which an aborted step may
+        // never make: bound by the drain's own time limit)
+        for (int kb = max(0, issued - S); kb < issued; ++kb) {
+          drain_wait(&bars->pfull[kb % S], (kb / S) & 1);
+          if (lead) drain_wait(&bars->ready[kb % S], (kb / S) & 1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (lane == 0 && lead) {
+      constexpr uint32_t idesc = sbd::umma_idesc_f16(2 * QW, QT, 0, 0);
+      // two k-blocks per round: one pair of waits and commits per 8 MMAs keeps
+      // the issuing thread's fixed costs out of the tensor pipe's way
+      for (int kb = 0; kb < nkb; kb += 2) {
+        const int nk = min(2, nkb - kb);
+        bool ok = true;
+        for (int i = 0; i < nk && ok; ++i) {
+          const int s = (kb + i) % S;
+          ok = sbd::mbar_wait_cluster(&bars->ready[s], ((kb + i) / S) & 1, abort, p.err);
+          if (!ok) break;
+          sbd::tc_fence_after();
+          const uint32_t b_base = sbd::smem_u32(smem + s * P_ACT_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            const uint32_t a_tmem = tmem + 256 + s * 32 + kk * 8;
+            const uint64_t bdesc = sbd::umma_desc(b_base + kk * 32, 16, 1024, sbd::kLayoutSwizzle128B);
+            sbd::umma_f16_ts_pair(tmem, a_tmem, bdesc, idesc, (kb + i) != 0 || kk != 0 ? 1u : 0u);
+          }
+        }
+        if (!ok) break;
+        for (int i = 0; i < nk; ++i) sbd::umma_commit_pair(&bars->empty[(kb + i) % S], pair_mask);
+      }
+      sbd::umma_commit_pair(&bars->accum, pair_mask);
+    }
+  } else if (warp >= Q_WARPS) {
+    // ------------------------------------------------------------ signallers (odd CTA)
+    // warp g forwards A slots kb = g, g + P_SIGNALERS, ... once the odd CTA's
+    // dequant group has written them
+    if (lane == 0 && !lead) {
+      const int g = warp - Q_WARPS;
+      for (int kb = g; kb < nkb; kb += P_SIGNALERS) {
+        const int s = kb % S;
+        if (!sbd::mbar_wait(&bars->dlocal[s], (kb / S) & 1, abort, p.err)) break;
+        sbd::mbar_arrive_remote(sbd::mapa_shared(sbd::smem_u32(&bars->ready[s]), lead_rank));
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ dequant producers (warps 2..17, both CTAs)
+    const int dw = warp - 2;
+    const int grp = dw >> 3;
+    const int quad = warp & 3;
+    const int khalf = (dw & 7) >> 2;
+    const int r = quad * 32 + lane;
+    const int dt = threadIdx.x - 64;
+    uint8_t* sct = smem + P_OFF_SCALE;
+    load_scale_tile(p, sct, w0, g_lo, gs, dt, Q_DQ_WARPS * 32);
+    sbd::named_bar_sync(1, Q_DQ_WARPS * 32);
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const int kstep = Q_DQ_GROUPS * BK;
+    const int gstep = kstep % p.group == 0 ? kstep / p.group : 0;
+    int gi = ((kb0 + grp) * BK + khalf * 32) / p.group - g_lo;
+    for (int kb = grp; kb < nkb; kb += Q_DQ_GROUPS) {
+      const int s = kb % S, slot = s;
+      if (gstep == 0) gi = ((kb0 + kb) * BK + khalf * 32) / p.group - g_lo;
+      bool ok = sbd::mbar_wait(&bars->pfull[s], (kb / S) & 1, abort, p.err);
+      if (ok) ok = sbd::mbar_wait_cluster(&bars->empty[s], ((kb / S) & 1) ^ 1, abort, p.err);
+      if (!__all_sync(0xFFFFFFFFu, ok)) break;
+      sbd::tc_fence_after();
+      const uint4 q = *reinterpret_cast<const uint4*>(smem + P_OFF_PACK + s * Q_PACK_BYTES + r * 32 + khalf * 16);
+      uint32_t o[16];
+      dq_group(p, sct, gi, r, q, o);
+      sbd::tmem_st_32x32b_x16(lane_addr + 256 + slot * 32 + khalf * 16, o);
+      sbd::tmem_wait_st();
+      sbd::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        sbd::mbar_arrive(&bars->pempty[s]);
+        sbd::mbar_arrive(lead ? &bars->ready[s] : &bars->dlocal[s]);
+      }
+      gi += gstep;
+    }
+    // ------------------------------------------------------------ epilogue (this CTA's 128 rows)
+    const bool ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait_cluster(&bars->accum, 0, abort, p.err));
+    if (ok) {
+      sbd::tc_fence_after();
+      if (p.csplit > 1) stash_partial(smem, lane_addr, dw, r);
+      else epilogue_direct(p, lane_addr, dw, r, lane, w0, t0, blockIdx.z);
+    }
+  }
+
+  if (p.csplit > 1) {
+    // every thread of every CTA reaches both cluster barriers (abort paths included)
+    sbd::cluster_sync_all();
+    if (warp >= 2 && warp < Q_WARPS) reduce_splits(p, smem, warp - 2, lane, w0, t0, rank >> 1, p.csplit, rank & 1, 2);
+    sbd::cluster_sync_all();
+  }
+
+  // both CTAs are done with TMEM (the pair's MMAs completed before `accum`)
+  sbd::tc_fence_before();
+  sbd::cluster_sync_all();
+  if (warp == 1) {
+    sbd::tc_fence_after();
+    sbd::tmem_dealloc_pair(tmem, Q_TMEM_COLS);
+  }
+}
+
 __global__ void splitk_finalize_kernel(const float* __restrict__ ws, __half* __restrict__ c, int m, int n, int ldc,
-                                       int splits, float alpha) {
-  const size_t total = static_cast<size_t>(m) * n;
-  const size_t plane = total;
+                                       int splits, float alpha, int geglu) {
+  const size_t plane = static_cast<size_t>(m) * n;
+  const int nout = geglu ? n / 2 : n;
+  const size_t total = static_cast<size_t>(m) * nout;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    float s = 0.f;
-    for (int z = 0; z < splits; ++z) s += ws[z * plane + i];
-    const size_t row = i / n, col = i - row * n;
-    c[row * ldc + col] = __float2half_rn(alpha * s);
+    const size_t row = i / nout, col = i - row * nout;
+    if (geglu) {
+      // partial planes hold gate (2 col) and up (2 col + 1) rows; round each to
+      // f16 as the GEMM output would be, then gelu(gate) * up
+      const size_t e = row * n + 2 * col;
+      float g = 0.f, u = 0.f;
+      for (int z = 0; z < splits; ++z) {
+        g += ws[z * plane + e];
+        u += ws[z * plane + e + 1];
+      }
+      const float gh = __half2float(__float2half_rn(alpha * g)), uh = __half2float(__float2half_rn(alpha * u));
+      c[row * ldc + col] = __float2half_rn(sbd::gelu_tanh(gh) * uh);
+    } else {
+      float s = 0.f;
+      for (int z = 0; z < splits; ++z) s += ws[z * plane + i];
+      c[row * ldc + col] = __float2half_rn(alpha * s);
+    }
   }
 }
 
@@ -571,16 +918,60 @@ int q4_splits(int m, int n, int k, int group, int scale_bytes) {
 int finalize(const GemmParams& p, int splits, cudaStream_t s) {
   const size_t total = static_cast<size_t>(p.m) * p.n;
   const int grid = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 16));
-  splitk_finalize_kernel<<<grid, 256, 0, s>>>(p.ws, static_cast<__half*>(p.c), p.m, p.n, p.ldc, splits, p.alpha);
+  splitk_finalize_kernel<<<grid, 256, 0, s>>>(p.ws, static_cast<__half*>(p.c), p.m, p.n, p.ldc, splits, p.alpha,
+                                              p.geglu);
   return sb::launch_status("splitk_finalize_kernel");
 }
 
 }  // namespace
 
+// Splits of one tile reduce through distributed shared memory when they fit in
+// a cluster (portable size 8); more splits fall back to f32 partial planes in
+// a workspace and splitk_finalize_kernel.
+constexpr int kMaxClusterSplits = 8;
+
+// The int4 GEMM runs as CTA pairs when a matrix has at least two weight tiles.
+static bool q4_pair(int n) { return (n + QW - 1) / QW >= 2; }
+// Largest split count reduced inside one cluster (clusters hold <= 8 CTAs).
+static int q4_max_cluster_splits(int n) { return q4_pair(n) ? kMaxClusterSplits / 2 : kMaxClusterSplits; }
+
+// How many clusters of the int4 GEMM (a CTA pair, or a single CTA, times
+// `csplit` K splits) the device can hold at once (clusters live within one
+// GPC, so this is below sm_count / cluster size); cached per device.
+static int max_active_clusters(bool pair, int csplit) {
+  static int cache[64][2][kMaxClusterSplits + 1] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || csplit < 1 || csplit > kMaxClusterSplits) return 0;
+  int& slot = cache[dev][pair ? 1 : 0][csplit];
+  if (!slot) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(pair ? 2 : 1, 1, csplit);
+    cfg.blockDim = dim3((pair ? P_WARPS : Q_WARPS) * 32);
+    cfg.dynamicSmemBytes = pair ? P_SMEM : Q_SMEM;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = pair ? 2 : 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = static_cast<unsigned>(csplit);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int nclus = 0;
+    const cudaError_t e = pair ? cudaOccupancyMaxActiveClusters(&nclus, gemm_q4_pair_kernel, &cfg)
+                               : cudaOccupancyMaxActiveClusters(&nclus, gemm_q4_kernel, &cfg);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      nclus = 0;
+    }
+    slot = nclus;
+  }
+  return slot;
+}
+
 static size_t q4_workspace(int m, int n, int k, int group, int scale_bytes) {
   if (m <= 0 || n <= 0 || k <= 0 || k % BK || group <= 0) return 0;
   const int splits = q4_splits(m, n, k, group, scale_bytes);
-  return splits > 1 ? static_cast<size_t>(splits) * m * n * sizeof(float) : 0;
+  return splits > q4_max_cluster_splits(n) ? static_cast<size_t>(splits) * m * n * sizeof(float) : 0;
 }
 
 extern "C" size_t sb_gemm_q4_workspace_size(int m, int n, int k) {
@@ -637,23 +1028,28 @@ extern "C" int sb_gemm_f16_f32out(const void* a, const void* b, float* c, int m,
   return gemm_f16_impl(a, b, c, 1, m, n, k, alpha, tr, lda, ldb, ldc, stream);
 }
 
-extern "C" int sb_gemm_q4(const void* a, const void* w, const void* scales, int scale_dtype, int group, void* c, int m,
-                          int n, int k, float alpha, int lda, int ldc, void* workspace, size_t workspace_bytes,
-                          void* stream) {
+static int gemm_q4_impl(const void* a, const void* w, const void* scales, int scale_dtype, int group, void* c, int m,
+                        int n, int k, float alpha, int lda, int ldc, void* workspace, size_t workspace_bytes,
+                        void* stream, int geglu) {
   SB_CHECK_ARG(m >= 0 && n >= 0 && k > 0, "sb_gemm_q4: bad shape");
+  SB_CHECK_ARG(!geglu || n % 2 == 0, "sb_gemm_q4_geglu: n=%d must be even (interleaved gate/up rows)", n);
   SB_CHECK_ARG(k % 64 == 0, "sb_gemm_q4: k=%d must be a multiple of 64", k);
   SB_CHECK_ARG(group > 0 && k % group == 0 && group % 32 == 0, "sb_gemm_q4: group=%d must be a multiple of 32 dividing k",
                group);
   SB_CHECK_ARG(scale_dtype == SB_SCALE_F16 || scale_dtype == SB_SCALE_F32, "sb_gemm_q4: bad scale dtype");
   if (m == 0 || n == 0) return SB_OK;
   SB_CHECK_ARG(a && w && scales && c, "sb_gemm_q4: null pointer");
-  SB_CHECK_ARG(lda >= k && ldc >= n, "sb_gemm_q4: leading dimension too small");
+  SB_CHECK_ARG(lda >= k && ldc >= (geglu ? n / 2 : n), "sb_gemm_q4: leading dimension too small");
   if (!sb::aligned(a, 16) || !sb::aligned(w, 16) || !sb::aligned(c, 2) || lda % 8)
     return sb::fail(SB_ERR_ALIGN, "sb_gemm_q4: A and W must be 16-byte aligned with lda a multiple of 8");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int esz = scale_dtype == SB_SCALE_F16 ? 2 : 4;
   CUtensorMap tact, tw;
-  int rc = make_map(&tact, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, k, m, lda, BK, QT, CU_TENSOR_MAP_SWIZZLE_128B);
+  const bool pair = q4_pair(n);
+  const int max_cs = q4_max_cluster_splits(n);
+  // a CTA of a pair loads half of the 256-token activation tile
+  int rc = make_map(&tact, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, k, m, lda, BK, pair ? QT / 2 : QT,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = make_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, k / 2, n, k / 2, BK / 2, QW, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
@@ -668,26 +1064,74 @@ extern "C" int sb_gemm_q4(const void* a, const void* w, const void* scales, int 
   p.group = group;
   p.scale_f16 = esz == 2;
   p.alpha = alpha;
+  p.geglu = geglu;
   p.kb_total = k / BK;
   int splits = q4_splits(m, n, k, group, esz);
-  const size_t need = splits > 1 ? static_cast<size_t>(splits) * m * n * sizeof(float) : 0;
-  if (splits > 1 && (!workspace || workspace_bytes < need)) {
-    // without room for partial sums run unsplit, if the scales still fit
-    if (QW * q4_scale_groups(k / BK, group) * esz > Q_SCALE_BYTES)
+  const size_t need = splits > max_cs ? static_cast<size_t>(splits) * m * n * sizeof(float) : 0;
+  if (need && (!workspace || workspace_bytes < need)) {
+    // without room for partial sums use the largest cluster split instead
+    splits = max_cs;
+    if (QW * q4_scale_groups((k / BK + splits - 1) / splits, group) * esz > Q_SCALE_BYTES)
       return sb::fail(SB_ERR_WORKSPACE, "sb_gemm_q4: k=%d needs split-K (%zu workspace bytes) for its scales", k, need);
-    splits = 1;
+  }
+  static bool done[64] = {false};
+  static bool done_pair[64] = {false};
+  rc = pair ? set_smem(gemm_q4_pair_kernel, P_SMEM, done_pair) : set_smem(gemm_q4_kernel, Q_SMEM, done);
+  if (rc) return rc;
+  const int wtiles = (n + QW - 1) / QW;
+  const int gx = pair ? (wtiles + 1) / 2 * 2 : wtiles;  // a pair's second tile may lie past n
+  const int ttiles = (m + QT - 1) / QT;
+  const int clusters = (pair ? gx / 2 : gx) * ttiles;  // per split
+  // a cluster split pays off only if all its clusters are resident at once;
+  // otherwise use fewer splits (while the group scales of a split still fit)
+  while (splits > 1 && splits <= max_cs && clusters > max_active_clusters(pair, splits)) {
+    const int fewer = splits - 1;
+    if (QW * q4_scale_groups((k / BK + fewer - 1) / fewer, group) * esz > Q_SCALE_BYTES) break;
+    splits = fewer;
   }
   p.kb_per_split = (p.kb_total + splits - 1) / splits;
   splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
-  if (splits > 1) p.ws = static_cast<float*>(workspace);
-  static bool done[64] = {false};
-  rc = set_smem(gemm_q4_kernel, Q_SMEM, done);
-  if (rc) return rc;
-  dim3 grid((n + QW - 1) / QW, (m + QT - 1) / QT, splits);
-  gemm_q4_kernel<<<grid, Q_WARPS * 32, Q_SMEM, s>>>(tact, tw, p);
-  rc = sb::launch_status("gemm_q4_kernel");
-  if (rc != SB_OK || splits == 1) return rc;
+  const bool in_cluster = splits > 1 && splits <= max_cs;
+  if (in_cluster) p.csplit = splits;
+  else if (splits > 1) p.ws = static_cast<float*>(workspace);
+  const dim3 grid(gx, ttiles, splits);
+  if (pair || in_cluster) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3((pair ? P_WARPS : Q_WARPS) * 32);
+    cfg.dynamicSmemBytes = pair ? P_SMEM : Q_SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = pair ? 2 : 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = in_cluster ? static_cast<unsigned>(splits) : 1u;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = pair ? cudaLaunchKernelEx(&cfg, gemm_q4_pair_kernel, tact, tw, p)
+                               : cudaLaunchKernelEx(&cfg, gemm_q4_kernel, tact, tw, p);
+    if (e != cudaSuccess) return sb::cuda_fail(e, "gemm_q4 (cluster launch)");
+    rc = sb::launch_status(pair ? "gemm_q4_pair_kernel" : "gemm_q4_kernel");
+  } else {
+    gemm_q4_kernel<<<grid, Q_WARPS * 32, Q_SMEM, s>>>(tact, tw, p);
+    rc = sb::launch_status("gemm_q4_kernel");
+  }
+  if (rc != SB_OK || in_cluster || splits == 1) return rc;
   return finalize(p, splits, s);
+}
+
+extern "C" int sb_gemm_q4(const void* a, const void* w, const void* scales, int scale_dtype, int group, void* c, int m,
+                          int n, int k, float alpha, int lda, int ldc, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  return gemm_q4_impl(a, w, scales, scale_dtype, group, c, m, n, k, alpha, lda, ldc, workspace, workspace_bytes,
+                      stream, 0);
+}
+
+extern "C" int sb_gemm_q4_geglu(const void* a, const void* w, const void* scales, int scale_dtype, int group,
+                                void* out, int m, int n, int k, float alpha, int lda, int ldo, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  return gemm_q4_impl(a, w, scales, scale_dtype, group, out, m, n, k, alpha, lda, ldo, workspace, workspace_bytes,
+                      stream, 1);
 }
 
 // ------------------------------------------------------------------------

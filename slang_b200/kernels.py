@@ -148,8 +148,12 @@ def attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.T
 
 
 def gemm_q4(A: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, C: torch.Tensor | None = None,
-            alpha: float = 1.0, workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """Fused ``_dq`` + ``_gemm``: ``C = f16(alpha * A @ dq_f16(W)^T)``."""
+            alpha: float = 1.0, workspace: torch.Tensor | None = None, geglu: bool = False) -> torch.Tensor:
+    """Fused ``_dq`` + ``_gemm``: ``C = f16(alpha * A @ dq_f16(W)^T)``.
+
+    With ``geglu``, W's rows are interleaved (gate, up) pairs and C [M, N/2]
+    receives ``f16(gelu_tanh(gate) * up)`` of the f16-rounded pair (the
+    reference's gate/up GEMMs + geglu_b, gemma4_150/prefill_gpu.py:365-372)."""
     _need(A, "A", (torch.float16,))
     _need(w, "w", (torch.uint8,))
     _need(scales, "scales", (torch.float16, torch.float32))
@@ -158,12 +162,12 @@ def gemm_q4(A: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, C: torch.Ten
     if w.shape[1] * 2 != K:
         raise ValueError("packed weight does not match A's K")
     if C is None:
-        C = torch.empty((M, N), dtype=torch.float16, device=A.device)
+        C = torch.empty((M, N // 2 if geglu else N), dtype=torch.float16, device=A.device)
     _need(C, "C", (torch.float16,))
     if workspace is None:
         need = gemm_q4_workspace_size(M, N, K)
         workspace = _workspace(A.device, need)
-    _lib.call("sb_gemm_q4", _ptr(A), _ptr(w), _ptr(scales), _DT[scales.dtype], group_of(scales, K),
+    _lib.call("sb_gemm_q4_geglu" if geglu else "sb_gemm_q4", _ptr(A), _ptr(w), _ptr(scales), _DT[scales.dtype], group_of(scales, K),
               _ptr(C), M, N, K, float(alpha), K, C.shape[1], _ptr(workspace) if workspace is not None else None,
               0 if workspace is None else workspace.numel() * workspace.element_size(), _stream())
     return C

@@ -256,7 +256,7 @@ class Runner:
               "tok_host": torch.empty(S, dtype=torch.int32, pin_memory=True),
               "hid": f32(S, H), "h16": f16(S, H), "hlast": f32(S, H),
               "qkv16": f16(S, self.nqkv), "q16": f16(S, nh, hd), "k16": f16(self.max_seq, hd),
-              "v16": f16(self.max_seq, hd), "attn16": f16(S, nh * hd), "o16": f16(S, H), "gu16": f16(S, 2 * F), "a16": f16(S, F),
+              "v16": f16(self.max_seq, hd), "attn16": f16(S, nh * hd), "o16": f16(S, H), "a16": f16(S, F),
               "d16": f16(S, H)}
         ws = max(kern.gemm_q4_workspace_size(S, n, k) for n, k in
                  ((self.nqkv, H), (H, self.qd), (2 * F, H), (H, F)))
@@ -314,7 +314,7 @@ class Runner:
         H, F = self.H, self.F
         split = lambda n, k: 1 if kern.gemm_q4_workspace_size(S, n, k) else 0  # noqa: E731
         per_layer = (4 + split(self.nqkv, H) + split(H, self.qd) + split(2 * F, H) + split(H, F)  # 4 projections
-                     + 1 + 1 + 2 + 1)  # prep; attention; two add+norms; geglu
+                     + 1 + 1 + 2)  # prep; attention; two add+norms (GEGLU is in the gate|up GEMM)
         return 2 + len(self.dm.layers) * per_layer + 2
 
     def prefill_timed_gemms(self, tokens, seq: int = 0):
@@ -334,11 +334,11 @@ class Runner:
         H, nh, hd, F = self.H, self.nh, self.hd, self.F
         ws = pf["ws"]
 
-        def proj(name, A, W, C, K):
+        def proj(name, A, W, C, K, geglu=False):
             if rec is not None:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(self.stream)
-            kern.gemm_q4(A, W[0], W[1], C=C, workspace=ws)
+            kern.gemm_q4(A, W[0], W[1], C=C, workspace=ws, geglu=geglu)
             if rec is not None:
                 e1.record(self.stream)
                 rec.append((name, S, W[0].shape[0], K, e0, e1))
@@ -361,8 +361,8 @@ class Runner:
             _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), pf["o16"].data_ptr(), _F16,
                       L["post_attn_norm"].data_ptr(), L["pre_ffn_norm"].data_ptr(), pf["hid"].data_ptr(), None,
                       pf["h16"].data_ptr(), S, H, self.eps, s)
-            proj("gate|up", pf["h16"][:S], L["gu"], pf["gu16"][:S], H)
-            _lib.call("sb_geglu", pf["gu16"].data_ptr(), _F16, S, F, None, pf["a16"].data_ptr(), s)
+            # gate|up GEMM with GEGLU in its epilogue: writes a = gelu(gate) * up
+            proj("gate|up", pf["h16"][:S], L["gu"], pf["a16"][:S], H, geglu=True)
             proj("down", pf["a16"][:S], L["down"], pf["d16"][:S], F)
             last = li + 1 == len(Ls)
             nxt = Ls[li + 1]["in_norm"] if not last else dm.final_norm

@@ -10,6 +10,7 @@ import pytest
 import torch
 
 from oracle import q4
+from slang_b200 import _lib
 from slang_b200 import kernels as kern
 from slang_b200 import synth
 from tests._util import assert_close, max_rel
@@ -270,6 +271,37 @@ def test_gemm_q4_matches_dequant_then_gemm(cuda):
     kern.gemm(A, W, C, M, N, Kd)
     f, c = fused.float().cpu().numpy(), C.float().cpu().numpy()
     assert np.abs(f - c).max() <= 2 * np.abs(c).max() * 2 ** -11
+
+
+# (M, N, K): no split; a 6-split cluster reduced in distributed shared memory;
+# 16 splits through workspace partials and the finalize kernel
+@pytest.mark.parametrize("M,N,K", [(1024, 12288, 1536), (256, 512, 1536), (256, 256, 6144), (37, 512, 1536)])
+def test_gemm_q4_geglu_equals_gemm_then_geglu(cuda, M, N, K):
+    """GEGLU in the GEMM epilogue is bit-for-bit sb_gemm_q4 followed by sb_geglu."""
+    rng = np.random.default_rng(M + N + K)
+    packed, scales = synth.q4_weight(rng, N, K)
+    a = synth.activations(rng, M, K)
+    A, P, S = T(a, cuda), T(packed, cuda), T(scales, cuda)
+    fused = kern.gemm_q4(A, P, S, geglu=True)
+    gu = kern.gemm_q4(A, P, S)
+    chain = torch.empty((M, N // 2), dtype=torch.float16, device=cuda)
+    _lib.call("sb_geglu", gu.data_ptr(), _lib.SB_F16, M, N // 2, None, chain.data_ptr(), kern._stream())
+    kern.device_status()
+    f, c = fused.cpu().numpy(), chain.cpu().numpy()
+    assert fused.shape == (M, N // 2)
+    np.testing.assert_array_equal(f, c)
+    # and against the oracle: GEGLU of the f64 GEMM of the dequantised weight
+    ref = q4.gemm_f64(a, q4.dequant_f16(packed, scales, 4)).astype(np.float16).astype(np.float64)
+    g, u = ref[:, 0::2], ref[:, 1::2]
+    assert_close(f.astype(np.float64), 0.5 * g * (1 + np.tanh(0.7978845608028654 * (g + 0.044715 * g ** 3))) * u,
+                 what=f"geglu M={M} N={N} K={K}")
+
+
+def test_gemm_q4_workspace_only_beyond_cluster_splits(cuda):
+    """Split-K within a cluster needs no workspace; only more than 8 splits do."""
+    assert kern.gemm_q4_workspace_size(1024, 1536, 2048) == 0  # o: 3 splits in a cluster
+    assert kern.gemm_q4_workspace_size(1024, 1536, 6144) == 0  # down
+    assert kern.gemm_q4_workspace_size(256, 256, 6144) > 0  # 16 splits
 
 
 def test_no_device_timeouts(cuda):

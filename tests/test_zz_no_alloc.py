@@ -26,8 +26,9 @@ def _noalloc(A, P, S, C, M, N, K):
     assert rc == _lib.SB_OK, lib.sb_last_error().decode()
 
 
-# down / o / k / gate at M=128 use split-K (and so the static scratch); gate at
-# M=1024 fills the GPU without it
+# down at M=256 splits K 12 ways, beyond the 8 splits a cluster reduces in
+# distributed shared memory, so it takes the static scratch; o / k split K
+# inside a cluster (no scratch); gate fills the GPU without splitting
 @pytest.mark.parametrize("name,M", [("down", 256), ("o", 1024), ("k", 512), ("gate", 128), ("gate", 1024)])
 def test_noalloc_matches_workspace_entry_point(cuda, name, M):
     N, K = synth.E2B_SHAPES[name]

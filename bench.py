@@ -51,7 +51,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", default="",
-                    choices=["", "gemm_q4", "gemm_f16", "gemv", "lmhead", "prefill", "decode"],
+                    choices=["", "gemm_q4", "gemm_q4_geglu", "gemm_f16", "gemv", "lmhead", "attn", "prefill", "decode",
+                             "decode_fused"],
                     help="run one kernel --iters times on a single shape and exit (for ncu captures)")
     ap.add_argument("--shape", default="6144,1536", help="N,K of the weight for --kernel")
     ap.add_argument("--m", type=int, default=1024, help="rows of the activation for --kernel")
@@ -69,7 +70,7 @@ def run_model_case(args):
     cfg = synth.e2b_config()
     model = synth.random_model(cfg, seed=1234)
     dm = runner.DeviceModel(model, dev, args.m + 8 + 4 * args.iters)
-    r = runner.Runner(dm, 1)
+    r = runner.Runner(dm, 1, fused=args.kernel == "decode_fused")
     prompt = synth.prompt_tokens(args.m, cfg["vocab"], seed=99)
     r.prefill(prompt, graph=False)
     torch.cuda.synchronize()
@@ -78,7 +79,7 @@ def run_model_case(args):
             r.prefill(prompt, graph=False)
         else:
             with torch.cuda.stream(r.stream):
-                r._decode_ops()
+                (r._fused_ops if r.fused else r._decode_ops)()
     torch.cuda.synchronize()
     print(f"ran {args.kernel} x{args.iters} (prompt {args.m}) eagerly")
 
@@ -87,7 +88,7 @@ def run_kernel_case(args):
     """One kernel on one shape, --iters launches after one warm-up (ncu target)."""
     import torch
 
-    if args.kernel in ("prefill", "decode"):
+    if args.kernel in ("prefill", "decode", "decode_fused"):
         return run_model_case(args)
     from slang_b200 import kernels as kern
     dev = torch.device("cuda", 0)
@@ -97,14 +98,25 @@ def run_kernel_case(args):
     g.manual_seed(0)
     w = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g)
     s = (torch.randn((n, k // 32), device=dev, generator=g) * 0.02).abs().half()
-    if args.kernel in ("gemm_q4", "gemm_f16"):
+    if args.kernel == "attn":
+        # fused causal prefill attention: --m tokens, 8 query heads, head_dim from --shape's K
+        hd = k
+        q = torch.randn((m, 8, hd), device=dev, generator=g).half()
+        kk = torch.randn((m, hd), device=dev, generator=g).half()
+        vv = torch.randn((m, hd), device=dev, generator=g).half()
+        out = torch.empty_like(q)
+
+        def op():
+            kern.attn_prefill(q, kk, vv, out)
+    elif args.kernel in ("gemm_q4", "gemm_q4_geglu", "gemm_f16"):
         a = torch.randn((m, k), device=dev, generator=g).half()
-        c = torch.empty((m, n), dtype=torch.float16, device=dev)
+        geglu = args.kernel == "gemm_q4_geglu"
+        c = torch.empty((m, n // 2 if geglu else n), dtype=torch.float16, device=dev)
         wf = kern.dequant_f16(w, s, k, n) if args.kernel == "gemm_f16" else None
 
         def op():
             if wf is None:
-                kern.gemm_q4(a, w, s, C=c)
+                kern.gemm_q4(a, w, s, C=c, geglu=geglu)
             else:
                 kern.gemm(a, wf, c, m, n, k)
     else:
@@ -133,7 +145,9 @@ def run_kernel_case(args):
     e1.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / args.iters
     kern.device_status()
-    if args.kernel in ("gemm_q4", "gemm_f16"):
+    if args.kernel == "attn":
+        rate = f"{2 * 2 * 8 * m * m / 2 * k / us / 1e6:.1f} TFLOP/s (causal: half of S x S)"
+    elif args.kernel in ("gemm_q4", "gemm_q4_geglu", "gemm_f16"):
         rate = f"{2 * m * n * k / us / 1e6:.1f} TFLOP/s"
     else:
         rate = f"{(n * k // 2 + n * (k // 32) * 2 + m * k * 4 + m * n * 4) / us / 1e3:.1f} GB/s"

@@ -236,6 +236,14 @@ int sb_softmax_causal(const float* scores, int ld_s, int rows, int n_heads, int 
 int sb_attn_prefill(const void* q16, const void* k16, const void* v16, void* out16, int s_len,
                     int n_heads, int head_dim, void* stream);
 
+/* sb_attn_prefill with each query tile's key range split across CTAs (as many
+ * as one wave of SMs holds) and the shares merged by a second kernel; needs
+ * workspace >= sb_attn_prefill_workspace_size(s_len, n_heads, head_dim) bytes
+ * (16-byte aligned; 0 bytes means no split is worth it and none is used). */
+int sb_attn_prefill_ws(const void* q16, const void* k16, const void* v16, void* out16, int s_len,
+                       int n_heads, int head_dim, void* workspace, size_t workspace_bytes, void* stream);
+size_t sb_attn_prefill_workspace_size(int s_len, int n_heads, int head_dim);
+
 /* out[r, i] = gelu_tanh(gu[r, 2i]) * gu[r, 2i + 1]: the fused gate|up weight keeps
  * gate row i and up row i adjacent, so its output interleaves them.
  * Replaces geglu_b (gemma4_150/kernels_dsl.py:259) / gemma4/reference.py:148-150. */

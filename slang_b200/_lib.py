@@ -39,6 +39,8 @@ SIGNATURES = {
     "sb_softmax_causal": ([_vp, _i, _i, _i, _i, _i, _vp, _i, _vp], _i),
     "sb_geglu": ([_vp, _i, _i, _i, _vp, _vp, _vp], _i),
     "sb_attn_prefill": ([_vp, _vp, _vp, _vp, _i, _i, _i, _vp], _i),
+    "sb_attn_prefill_ws": ([_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp], _i),
+    "sb_attn_prefill_workspace_size": ([_i, _i, _i], _sz),
     "sb_attn_decode": ([_vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _vp, _vp, _sz, _vp], _i),
     "sb_attn_decode_workspace_size": ([_i, _i, _i, _i], _sz),
     "sb_step_advance": ([_vp, _vp, _vp, _vp, _i, _i, _vp], _i),

@@ -70,13 +70,31 @@ struct Bars {
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
 
+// A split tile's partial row: O [HD], m (log2 units), l, 2 pad floats, so
+// that every row starts on a 16-byte boundary.
+template <int HD>
+constexpr int part_stride() {
+  return HD + 4;
+}
+
 struct Params {
   __half* out;
+  float* part;  // split tiles: per (tile, chunk, row) a partial row of part_stride<HD>() floats
   int* err;
   int rows;   // S * nh
   int nh;
   int s_len;  // S (keys = queries' tokens)
+  int kpc;    // key blocks per chunk (a CTA's share of a tile's key range)
+  int maxc;   // chunks of the longest tile (grid.y)
 };
+
+// Key blocks that query tile `tile` sees.
+__host__ __device__ __forceinline__ int tile_key_blocks(int tile, int rows, int nh, int s_len) {
+  const int r0 = tile * QR;
+  const int last = (r0 + QR < rows ? r0 + QR : rows) - 1;
+  const int tok_hi = (last / nh < s_len - 1) ? last / nh : s_len - 1;
+  return tok_hi / KB + 1;
+}
 
 __device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = sbd::global_ns();
@@ -105,11 +123,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
   volatile int* abort = &bars->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // heaviest tiles (latest tokens) first
+  // heaviest tiles (latest tokens) first; chunk blockIdx.y of the tile's key blocks
   const int tile = gridDim.x - 1 - blockIdx.x;
   const int r0 = tile * QR;
-  const int tok_hi = min(p.s_len - 1, (min(r0 + QR, p.rows) - 1) / p.nh);
-  const int nb = tok_hi / KB + 1;  // key blocks this tile can see
+  const int nb_all = tile_key_blocks(tile, p.rows, p.nh, p.s_len);
+  const int nchunks = (nb_all + p.kpc - 1) / p.kpc;
+  if (static_cast<int>(blockIdx.y) >= nchunks) return;  // the whole CTA, before any barrier
+  const int kb_lo = blockIdx.y * p.kpc;
+  const int nb = min(p.kpc, nb_all - kb_lo);  // key blocks of this chunk: kb_lo + [0, nb)
 
   if (threadIdx.x == 0) {
     sbd::mbar_init(&bars->q_full, 1);
@@ -158,13 +179,15 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         sbd::mbar_arrive_expect_tx(&bars->k_full[st], KV_BYTES);
 #pragma unroll
         for (int b = 0; b < NBOX; ++b)
-          sbd::tma_load_2d(&tmK, &bars->k_full[st], smem + OFF_K + st * KV_BYTES + b * (KB * 128), 64 * b, j * KB);
+          sbd::tma_load_2d(&tmK, &bars->k_full[st], smem + OFF_K + st * KV_BYTES + b * (KB * 128), 64 * b,
+                           (kb_lo + j) * KB);
         issued_k = j + 1;
         if (!sbd::mbar_wait(&bars->v_empty[st], ph, abort, p.err)) break;
         sbd::mbar_arrive_expect_tx(&bars->v_full[st], KV_BYTES);
 #pragma unroll
         for (int b = 0; b < NBOX; ++b)
-          sbd::tma_load_2d(&tmV, &bars->v_full[st], smem + OFF_V + st * KV_BYTES + b * (KB * 128), 64 * b, j * KB);
+          sbd::tma_load_2d(&tmV, &bars->v_full[st], smem + OFF_V + st * KV_BYTES + b * (KB * 128), 64 * b,
+                           (kb_lo + j) * KB);
         issued_v = j + 1;
       }
       if (*abort) {
@@ -250,7 +273,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       __syncwarp();
       if (lane == 0) sbd::mbar_arrive(&bars->s_free[st]);
       // causal mask: key j*KB + c is visible to this row when it is <= token
-      const int nvis = max(0, min(KB, token - j * KB + 1));
+      const int nvis = max(0, min(KB, token - (kb_lo + j) * KB + 1));
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < KB; ++c)
@@ -307,7 +330,26 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
     // ------------------------------------------------------------ epilogue: O / l -> f16
     if (ok) ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait(&bars->o_final, 0, abort, p.err));
-    if (ok) {
+    if (ok && nchunks > 1) {
+      // a share of a split tile: unnormalised O with its running max and sum
+      sbd::tc_fence_after();
+      float* dst = p.part + ((static_cast<size_t>(tile) * p.maxc + blockIdx.y) * QR + row) * part_stride<HD>();
+      for (int cc = 0; cc < HD / 32; ++cc) {
+        uint32_t ov[32];
+        sbd::tmem_ld_32x32b_x32(lane_base + TM_O + cc * 32, ov);
+        sbd::tmem_wait_ld();
+        if (!row_ok) continue;
+#pragma unroll
+        for (int e = 0; e < 32; e += 4)
+          *reinterpret_cast<float4*>(dst + cc * 32 + e) =
+              make_float4(__uint_as_float(ov[e]), __uint_as_float(ov[e + 1]), __uint_as_float(ov[e + 2]),
+                          __uint_as_float(ov[e + 3]));
+      }
+      if (row_ok) {
+        dst[HD] = m_used;
+        dst[HD + 1] = l;
+      }
+    } else if (ok) {
       sbd::tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __half* dst = p.out + static_cast<size_t>(r) * HD;
@@ -339,9 +381,74 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   }
 }
 
+// Combines the chunk partials of every split tile: warp per query row,
+// out = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c over chunks that saw
+// keys (l_c > 0), M the largest of their m_c.
 template <int HD>
-int launch_attn(const void* q16, const void* k16, const void* v16, void* out16, int s_len, int n_heads,
-                cudaStream_t stream) {
+__global__ void attn_merge_kernel(const float* __restrict__ part, __half* __restrict__ out, int rows, int nh,
+                                  int s_len, int kpc, int maxc) {
+  constexpr int VPL = HD / 32;  // values per lane: 2, 4 or 8
+  constexpr int PS = part_stride<HD>();
+  static_assert(VPL == 2 || VPL % 4 == 0, "lane vector width");
+  const int tile = blockIdx.x;
+  const int row = blockIdx.y * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int nchunks = (tile_key_blocks(tile, rows, nh, s_len) + kpc - 1) / kpc;
+  const int r = tile * QR + row;
+  if (nchunks <= 1 || r >= rows) return;
+  const size_t cstride = static_cast<size_t>(QR) * PS;
+  const float* base = part + (static_cast<size_t>(tile) * maxc * QR + row) * PS;
+  float M = -INFINITY;
+  for (int c = 0; c < nchunks; ++c)
+    if (base[c * cstride + HD + 1] > 0.f) M = fmaxf(M, base[c * cstride + HD]);
+  float acc[VPL] = {};
+  float L = 0.f;
+  for (int c = 0; c < nchunks; ++c) {
+    const float* pc = base + c * cstride + lane * VPL;  // 8 * VPL bytes per lane: aligned for its vector width
+    const float lc = base[c * cstride + HD + 1];
+    if (!(lc > 0.f)) continue;
+    const float wgt = exp2f(base[c * cstride + HD] - M);
+    L += wgt * lc;
+    if constexpr (VPL == 2) {
+      const float2 v = *reinterpret_cast<const float2*>(pc);
+      acc[0] += wgt * v.x;
+      acc[1] += wgt * v.y;
+    } else {
+#pragma unroll
+      for (int e = 0; e < VPL; e += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(pc + e);
+        acc[e] += wgt * v.x;
+        acc[e + 1] += wgt * v.y;
+        acc[e + 2] += wgt * v.z;
+        acc[e + 3] += wgt * v.w;
+      }
+    }
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  __half* dst = out + static_cast<size_t>(r) * HD + lane * VPL;
+#pragma unroll
+  for (int e = 0; e < VPL; e += 2) *reinterpret_cast<__half2*>(dst + e) = __floats2half2_rn(acc[e] * inv, acc[e + 1] * inv);
+}
+
+// Key blocks per chunk: the fewest that keep the CTAs (tile x chunk) within
+// one wave of the SMs, so the longest chain of key blocks is as short as the
+// machine allows.  Returns kpc and sets *maxc.
+int choose_kpc(int rows, int nh, int s_len, int* maxc) {
+  const int tiles = (rows + QR - 1) / QR;
+  const int nb_max = tile_key_blocks(tiles - 1, rows, nh, s_len);
+  const int sms = sb::num_sms();
+  int kpc = 1;
+  for (; kpc < nb_max; ++kpc) {
+    long long ctas = 0;
+    for (int t = 0; t < tiles; ++t) ctas += (tile_key_blocks(t, rows, nh, s_len) + kpc - 1) / kpc;
+    if (ctas <= sms) break;
+  }
+  *maxc = (nb_max + kpc - 1) / kpc;
+  return kpc;
+}
+
+template <int HD>
+int launch_attn(const void* q16, const void* k16, const void* v16, void* out16, int s_len, int n_heads, float* part,
+                size_t part_bytes, cudaStream_t stream) {
   using C = Cfg<HD>;
   const long long rows = static_cast<long long>(s_len) * n_heads;
   CUtensorMap tq, tk, tv;
@@ -364,15 +471,30 @@ int launch_attn(const void* q16, const void* k16, const void* v16, void* out16, 
   p.rows = static_cast<int>(rows);
   p.nh = n_heads;
   p.s_len = s_len;
-  const int grid = static_cast<int>((rows + QR - 1) / QR);
-  attn_prefill_kernel<HD><<<grid, WARPS * 32, C::SMEM, stream>>>(tq, tk, tv, p);
-  return sb::launch_status("attn_prefill_kernel");
+  const int tiles = static_cast<int>((rows + QR - 1) / QR);
+  int maxc = 1;
+  p.kpc = tile_key_blocks(tiles - 1, p.rows, n_heads, s_len);  // unsplit
+  if (part) {
+    const int kpc = choose_kpc(p.rows, n_heads, s_len, &maxc);
+    if (maxc > 1 && static_cast<size_t>(tiles) * maxc * QR * part_stride<HD>() * sizeof(float) <= part_bytes) {
+      p.kpc = kpc;
+      p.part = part;
+    } else {
+      maxc = 1;
+    }
+  }
+  p.maxc = maxc;
+  attn_prefill_kernel<HD><<<dim3(tiles, maxc), WARPS * 32, C::SMEM, stream>>>(tq, tk, tv, p);
+  rc = sb::launch_status("attn_prefill_kernel");
+  if (rc != SB_OK || maxc == 1) return rc;
+  attn_merge_kernel<HD><<<dim3(tiles, QR / 8), 256, 0, stream>>>(part, p.out, p.rows, n_heads, s_len, p.kpc, maxc);
+  return sb::launch_status("attn_merge_kernel");
 }
 
 }  // namespace
 
-extern "C" int sb_attn_prefill(const void* q16, const void* k16, const void* v16, void* out16, int s_len,
-                               int n_heads, int head_dim, void* stream) {
+static int attn_prefill_impl(const void* q16, const void* k16, const void* v16, void* out16, int s_len, int n_heads,
+                             int head_dim, void* workspace, size_t workspace_bytes, void* stream) {
   SB_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256,
                "sb_attn_prefill: head_dim must be 64, 128 or 256");
   SB_CHECK_ARG(s_len >= 0 && n_heads >= 1, "sb_attn_prefill: bad sizes");
@@ -382,9 +504,32 @@ extern "C" int sb_attn_prefill(const void* q16, const void* k16, const void* v16
     return sb::fail(SB_ERR_ALIGN, "sb_attn_prefill: q, k, v and out must be 16-byte aligned");
   SB_CHECK_ARG(static_cast<long long>(s_len) * n_heads < (1ll << 31), "sb_attn_prefill: too many rows");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* part = static_cast<float*>(workspace);
+  if (part && !sb::aligned(part, 16)) return sb::fail(SB_ERR_ALIGN, "sb_attn_prefill: workspace must be 16-byte aligned");
   switch (head_dim) {
-    case 64: return launch_attn<64>(q16, k16, v16, out16, s_len, n_heads, s);
-    case 128: return launch_attn<128>(q16, k16, v16, out16, s_len, n_heads, s);
-    default: return launch_attn<256>(q16, k16, v16, out16, s_len, n_heads, s);
+    case 64: return launch_attn<64>(q16, k16, v16, out16, s_len, n_heads, part, workspace_bytes, s);
+    case 128: return launch_attn<128>(q16, k16, v16, out16, s_len, n_heads, part, workspace_bytes, s);
+    default: return launch_attn<256>(q16, k16, v16, out16, s_len, n_heads, part, workspace_bytes, s);
   }
+}
+
+extern "C" int sb_attn_prefill(const void* q16, const void* k16, const void* v16, void* out16, int s_len,
+                               int n_heads, int head_dim, void* stream) {
+  return attn_prefill_impl(q16, k16, v16, out16, s_len, n_heads, head_dim, nullptr, 0, stream);
+}
+
+extern "C" size_t sb_attn_prefill_workspace_size(int s_len, int n_heads, int head_dim) {
+  if (s_len <= 0 || n_heads <= 0 || head_dim <= 0) return 0;
+  const long long rows = static_cast<long long>(s_len) * n_heads;
+  if (rows >= (1ll << 31)) return 0;
+  int maxc = 1;
+  choose_kpc(static_cast<int>(rows), n_heads, s_len, &maxc);
+  if (maxc <= 1) return 0;
+  const size_t tiles = static_cast<size_t>((rows + QR - 1) / QR);
+  return tiles * maxc * QR * (static_cast<size_t>(head_dim) + 4) * sizeof(float);  // part_stride
+}
+
+extern "C" int sb_attn_prefill_ws(const void* q16, const void* k16, const void* v16, void* out16, int s_len,
+                                  int n_heads, int head_dim, void* workspace, size_t workspace_bytes, void* stream) {
+  return attn_prefill_impl(q16, k16, v16, out16, s_len, n_heads, head_dim, workspace, workspace_bytes, stream);
 }

@@ -128,7 +128,8 @@ def gemm(A: torch.Tensor, W: torch.Tensor, C: torch.Tensor, M: int, N: int, K: i
     return C
 
 
-def attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None,
+                 split: bool = True, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Causal prompt attention (the reference's attn_prefill / _attn_gemm,
     gemma4_150/prefill_gpu.py:259-314): q [S, nh, hd], k, v [S, hd] f16 ->
     out [S, nh, hd] f16 = softmax(q k^T, causal) v, one fused kernel
@@ -143,7 +144,14 @@ def attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.T
     if out is None:
         out = torch.empty_like(q)
     _need(out, "out", (torch.float16,))
-    _lib.call("sb_attn_prefill", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), S, nh, hd, _stream())
+    if not split:
+        _lib.call("sb_attn_prefill", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), S, nh, hd, _stream())
+        return out
+    if workspace is None:
+        workspace = _workspace(q.device, _lib.load().sb_attn_prefill_workspace_size(S, nh, hd))
+    nbytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    _lib.call("sb_attn_prefill_ws", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), S, nh, hd,
+              _ptr(workspace) if workspace is not None else None, nbytes, _stream())
     return out
 
 

@@ -261,6 +261,8 @@ class Runner:
         ws = max(kern.gemm_q4_workspace_size(S, n, k) for n, k in
                  ((self.nqkv, H), (H, self.qd), (2 * F, H), (H, F)))
         pf["ws"] = torch.empty(max(1, ws // 4), dtype=torch.float32, device=dev)
+        aws = _lib.load().sb_attn_prefill_workspace_size(S, nh, hd)
+        pf["attn_ws"] = torch.empty(max(4, aws // 4), dtype=torch.float32, device=dev)
         self._pf = pf
         self._pgraphs.clear()  # captured prefills point at the old buffers
         return pf
@@ -315,6 +317,8 @@ class Runner:
         split = lambda n, k: 1 if kern.gemm_q4_workspace_size(S, n, k) else 0  # noqa: E731
         per_layer = (4 + split(self.nqkv, H) + split(H, self.qd) + split(2 * F, H) + split(H, F)  # 4 projections
                      + 1 + 1 + 2)  # prep; attention; two add+norms (GEGLU is in the gate|up GEMM)
+        if _lib.load().sb_attn_prefill_workspace_size(S, self.nh, self.hd):
+            per_layer += 1  # the attention merge kernel
         return 2 + len(self.dm.layers) * per_layer + 2
 
     def prefill_timed_gemms(self, tokens, seq: int = 0):
@@ -355,8 +359,9 @@ class Runner:
                       pf["q16"].data_ptr(), None, self.kc[li].data_ptr() + kc_off, self.vc[li].data_ptr() + kc_off,
                       pf["k16"].data_ptr(), pf["v16"].data_ptr(), self.cache_stride, s)
             # causal attention over the prompt: one fused kernel
-            _lib.call("sb_attn_prefill", pf["q16"].data_ptr(), pf["k16"].data_ptr(), pf["v16"].data_ptr(),
-                      pf["attn16"].data_ptr(), S, nh, hd, s)
+            _lib.call("sb_attn_prefill_ws", pf["q16"].data_ptr(), pf["k16"].data_ptr(), pf["v16"].data_ptr(),
+                      pf["attn16"].data_ptr(), S, nh, hd, pf["attn_ws"].data_ptr(),
+                      pf["attn_ws"].numel() * 4, s)
             proj("o", pf["attn16"][:S], L["o"], pf["o16"][:S], self.qd)
             _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), pf["o16"].data_ptr(), _F16,
                       L["post_attn_norm"].data_ptr(), L["pre_ffn_norm"].data_ptr(), pf["hid"].data_ptr(), None,

@@ -50,9 +50,31 @@ def _reference(q, k, v):
                                            (150, 4, 1.0, 128)])
 def test_attn_prefill_vs_reference(cuda, S, nh, scale, hd):
     q, k, v = _inputs(S, nh, seed=S * 10 + nh, scale=scale, hd=hd)
-    out = kern.attn_prefill(q.to(cuda), k.to(cuda), v.to(cuda))
+    ref = _reference(q, k, v)
+    for split in (False, True):
+        out = kern.attn_prefill(q.to(cuda), k.to(cuda), v.to(cuda), split=split)
+        kern.device_status()
+        assert_close(out.float().cpu().numpy(), ref, what=f"attn_prefill S={S} nh={nh} hd={hd} split={split}")
+
+
+def test_attn_prefill_split_merges_key_chunks(cuda):
+    """A long prompt splits each late query tile's keys over several CTAs; the
+    merged result equals the unsplit kernel's within f32 rounding."""
+    S, nh = 2048, 8
+    assert _lib.load().sb_attn_prefill_workspace_size(S, nh, HD) > 0, "expected a split at 2048 tokens"
+    q, k, v = (x.to(cuda) for x in _inputs(S, nh, seed=9, scale=0.8))
+    whole = kern.attn_prefill(q, k, v, split=False).float()
+    split = kern.attn_prefill(q, k, v, split=True).float()
     kern.device_status()
-    assert_close(out.float().cpu().numpy(), _reference(q, k, v), what=f"attn_prefill S={S} nh={nh} hd={hd}")
+    assert_close(split.cpu().numpy(), whole.cpu().numpy(), what="split vs unsplit")
+    # last two tokens against float64 (they see every key)
+    qn, kn, vn = (x.float().cpu().numpy().astype(np.float64) for x in (q[-2:], k, v))
+    for i, t in enumerate((S - 2, S - 1)):
+        s = qn[i] @ kn[:t + 1].T
+        s -= s.max(axis=1, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(axis=1, keepdims=True)
+        assert_close(split[t].cpu().numpy(), p @ vn[:t + 1], what=f"token {t}")
 
 
 def test_attn_prefill_matches_three_kernel_chain(cuda):

@@ -6,10 +6,11 @@ Headline: "1024-tok prefill tok/s" of the random-init Gemma-4-E2B-shaped int4
 decoder (BASELINE config 4 architecture: 35 layers, hidden 1536, FFN 6144,
 8q/1kv heads at head_dim 256, vocab 262144, group-32 f16 scales).  One step is
 the full layers-outer prefill of a 1024-token prompt -- embed, per layer the
-fused int4 tcgen05 projection GEMMs (q|k|v, o, gate|up, down), q/k norm + RoPE
-+ KV-cache store, QK^T -> causal softmax -> PV on the tcgen05 f16 GEMM, the
-norms and GEGLU -- ending in the final norm and the lm_head argmax of the first
-generated token; it is captured as one CUDA graph.  value = N x 1024 tokens /
+fused int4 tcgen05 projection GEMMs (q|k|v, o, gate|up with GEGLU in its
+epilogue, down), q/k norm + RoPE + KV-cache store, the fused causal tcgen05
+attention and its split merge, the residual norms -- ending in the final norm
+and the lm_head argmax of the first generated token; it is captured as one
+CUDA graph.  value = N x 1024 tokens /
 max-over-ranks step time (replicas, weak scaling: there is no collective on
 this path).  The ~1 GB of weights exceeds the 126 MB L2, so no flush is needed.
 
@@ -284,6 +285,15 @@ def run_reference(args):
 # ------------------------------------------------------------------ GPU arm
 PROMPT = 1024
 DECODE_STEPS = 64
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the
+# fused int4 GEMM at M = 1024, keyed by the weight's (N, K), from one ncu capture
+# per shape: `ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,
+# dram__bytes_write.sum --clock-control none -k regex:gemm_q4 -s 1 -c 2 python
+# bench.py --kernel gemm_q4 --shape N,K --m 1024 --iters 3` (gemm_q4_geglu for
+# the gate|up weight).  Each equals the operands read once (A, packed W,
+# scales); C stays in L2 within the launch.
+GEMM_DRAM_BYTES = {(2560, 1536): 5_419_264, (1536, 2048): 6_022_144, (12288, 1536): 13_820_928,
+                   (1536, 6144): 17_949_696}
 
 
 def main():
@@ -363,7 +373,11 @@ def main():
         m, n, k = b["shape"]
         b["avg_us"] = 1e3 * b["ms"] / b["count"]
         b["tflops"] = 2 * m * n * k / (b["avg_us"] / 1e6) / 1e12
+        b["algorithmic_read_bytes"] = m * k * 2 + n * k // 2 + n * (k // 32) * 2
+        b["dram_bytes_per_launch"] = GEMM_DRAM_BYTES.get((n, k)) if m == PROMPT else None
         del b["ms"]
+    traffic = (sum(b["dram_bytes_per_launch"] * b["count"] for b in by.values())
+               if all(b["dram_bytes_per_launch"] for b in by.values()) else None)
 
     # ---------------- decode (graph-captured step, batch 1, context from PROMPT)
     # the persistent one-kernel step (the product path) and the per-op graph
@@ -427,8 +441,10 @@ def main():
                        "parallelism": f"replicas x{world}", "l2": "weights ~1 GB > 126 MB L2, no flush",
                        "graph": "one CUDA graph per prefill"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
-                         "frac": achieved / tc_peak, "traffic": None, "peak_kind": peak_kind,
-                         "kernel": "gemm_q4_kernel (fused int4 dequant + tcgen05, incl. split-K finalize)",
+                         "frac": achieved / tc_peak, "traffic": traffic, "peak_kind": peak_kind,
+                         "traffic_unit": "DRAM bytes per prefill step over all GEMM launches (ncu, per shape)",
+                         "kernel": "gemm_q4_pair_kernel (fused int4 dequant + tcgen05 CTA pair; split-K "
+                                   "reduced in-cluster)",
                          "flops_per_step": gemm_flops, "gemm_ms_per_step": gemm_ms,
                          "gemm_share_of_step": gemm_ms / ms, "by_matrix": by},
             "cpu_baseline": cpu,

@@ -327,12 +327,31 @@ __device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
+// Arrive on another CTA's barrier with the default semantics (release at CTA
+// scope): the producer -> MMA hand-off of CUTLASS's 2-SM pipelines, where the
+// data is TMEM or shared memory already completed by the arriving thread
+// (tcgen05.wait::st / fence) and the consumer is the pair's MMA.
+__device__ __forceinline__ void mbar_arrive_remote_cta(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
 // try_wait with acquire at cluster scope (for barriers other CTAs arrive on).
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Non-blocking test of `parity` with acquire at cluster scope.
+__device__ __forceinline__ bool mbar_test_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)

@@ -632,8 +632,8 @@ __global__ void __launch_bounds__(Q_WARPS * 32, 1)
 
 // ---- CTA-pair form (cta_group::2): 256 weight rows x 256 tokens per pair
 constexpr int P_STAGES = 8;                       // stages; stage s is also TMEM A slot s (256 + 8 x 32 columns)
-constexpr int P_SIGNALERS = 4;                    // odd CTA: warps forwarding "A slot ready" to the even CTA
-constexpr int P_WARPS = Q_WARPS + P_SIGNALERS;
+constexpr int P_WLOAD = Q_WARPS;                  // warp issuing the packed-weight loads (both CTAs)
+constexpr int P_WARPS = P_WLOAD + 1;
 constexpr int P_ACT_BYTES = (QT / 2) * BK * 2;    // 16 KB: this CTA's 128 tokens of a k-block
 constexpr int P_OFF_PACK = P_STAGES * P_ACT_BYTES;
 constexpr int P_OFF_SCALE = P_OFF_PACK + P_STAGES * Q_PACK_BYTES;
@@ -645,22 +645,22 @@ static_assert(P_STAGES * P_ACT_BYTES >= QT * QW * 4, "split-K partial tile must 
 // and TMEM A slot s, so one barrier tells the MMA issuer that k-block kb is
 // ready and one commit frees both.
 struct PairBars {
-  uint64_t ready[P_STAGES];   // even CTA: both activation halves landed (tx), its dequant group wrote
-                              // A slot s (8 arrives) and the odd CTA's did (1 forwarded arrive)
+  uint64_t ready[P_STAGES];   // even CTA: both activation halves landed (tx) and both CTAs' dequant
+                              // groups wrote A slot s (8 local + 8 remote arrives)
   uint64_t empty[P_STAGES];   // each CTA: the pair's MMAs are done with stage / A slot s
   uint64_t pfull[P_STAGES];   // each CTA: its packed tile of stage s landed
   uint64_t pempty[P_STAGES];  // each CTA: its dequant warps are done with that packed tile
-  uint64_t dlocal[P_STAGES];  // odd CTA: its dequant group wrote A slot s (8 local arrives)
   uint64_t accum;             // each CTA: its accumulator rows are final
   uint32_t tmem_slot;
   int abort;
 };
 static_assert(sizeof(PairBars) <= 512, "pair barrier block");
 
-// Cross-CTA hand-off: an arrive on the even CTA's barrier with release at
-// cluster scope costs about a microsecond, so the dequant warps only arrive on
-// local barriers and the odd CTA's signaller warps forward each slot (up to
-// P_SIGNALERS in flight).
+// Cross-CTA hand-off: the odd CTA's dequant warps arrive on the even CTA's
+// `ready` barrier directly, with the default (CTA-scope release) remote arrive
+// after tcgen05.wait::st + tcgen05.fence::before_thread_sync -- the hand-off
+// CUTLASS's 2-SM async-producer -> UMMA pipeline uses.  A cluster-scope
+// release arrive costs about a microsecond per k-block.
 __global__ void __launch_bounds__(P_WARPS * 32, 1)
     gemm_q4_pair_kernel(const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ CUtensorMap tmW,
                         const GemmParams p) {
@@ -687,11 +687,10 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      sbd::mbar_init(&bars->ready[i], 1 + 8 + 1);
+      sbd::mbar_init(&bars->ready[i], 1 + 8 + 8);
       sbd::mbar_init(&bars->empty[i], 1);
       sbd::mbar_init(&bars->pfull[i], 1);
       sbd::mbar_init(&bars->pempty[i], 8);
-      sbd::mbar_init(&bars->dlocal[i], 8);
     }
     sbd::mbar_init(&bars->accum, 1);
     bars->abort = 0;
@@ -712,9 +711,14 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
   sbd::tc_fence_after();
   const uint32_t tmem = bars->tmem_slot;
 
+  // the next kernel in the stream may start its prologue; this kernel's own
+  // reads of the previous kernel's output (the activations) wait below
+  sbd::griddep_launch_dependents();
+
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer (both CTAs)
+    // ------------------------------------------------------------ activation TMA producer (both CTAs)
     if (lane == 0) {
+      sbd::griddep_wait();
       int issued = 0;
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % S;
@@ -724,60 +728,70 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
         if (lead) sbd::mbar_arrive_expect_tx(&bars->ready[s], 2 * P_ACT_BYTES);
         sbd::tma_load_2d_pair(&tmAct, sbd::mapa_shared(sbd::smem_u32(&bars->ready[s]), lead_rank),
                               smem + s * P_ACT_BYTES, k0, th);
-        if (!sbd::mbar_wait(&bars->pempty[s], ph, abort, p.err)) break;
-        sbd::mbar_arrive_expect_tx(&bars->pfull[s], Q_PACK_BYTES);
-        sbd::tma_load_2d(&tmW, &bars->pfull[s], smem + P_OFF_PACK + s * Q_PACK_BYTES, k0 / 2, w0);
         issued = kb + 1;
       }
-      if (*abort) {
+      if (*abort && lead) {
         // let copies in flight land before shared memory is released: the even
-        // CTA's activation barriers count both CTAs' halves
-        // (ready also needs the dequant arrivals, which an aborted step may
-        // never make: bound by the drain's own time limit)
-        for (int kb = max(0, issued - S); kb < issued; ++kb) {
-          drain_wait(&bars->pfull[kb % S], (kb / S) & 1);
-          if (lead) drain_wait(&bars->ready[kb % S], (kb / S) & 1);
-        }
+        // CTA's activation barriers count both CTAs' halves (ready also needs
+        // the dequant arrivals, which an aborted step may never make: bound by
+        // the drain's own time limit)
+        for (int kb = max(0, issued - S); kb < issued; ++kb) drain_wait(&bars->ready[kb % S], (kb / S) & 1);
       }
+    }
+  } else if (warp == P_WLOAD) {
+    // ------------------------------------------------------------ packed-weight TMA producer (both CTAs)
+    // Weights do not come from the previous kernel, so they stream before its
+    // end; a packed stage is refilled as soon as the dequant warps are done
+    // with it, running up to P_STAGES k-blocks ahead of them.
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % S;
+        if (!sbd::mbar_wait(&bars->pempty[s], ((kb / S) & 1) ^ 1, abort, p.err)) break;
+        sbd::mbar_arrive_expect_tx(&bars->pfull[s], Q_PACK_BYTES);
+        sbd::tma_load_2d(&tmW, &bars->pfull[s], smem + P_OFF_PACK + s * Q_PACK_BYTES, (kb0 + kb) * BK / 2, w0);
+        issued = kb + 1;
+      }
+      if (*abort)
+        for (int kb = max(0, issued - S); kb < issued; ++kb) drain_wait(&bars->pfull[kb % S], (kb / S) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (even CTA)
+    // The tensor pipe takes an MMA only shortly before it can start it, so
+    // every instruction this thread runs between MMAs is on the critical path:
+    // descriptors are fixed offsets from one base, stage indices are
+    // compile-time (the loop is unrolled over one pass of the ring), and the
+    // next stage's barrier is tested (without blocking) before this stage's
+    // last MMA, so a ready stage costs no wait.
     if (lane == 0 && lead) {
       constexpr uint32_t idesc = sbd::umma_idesc_f16(2 * QW, QT, 0, 0);
-      // two k-blocks per round: one pair of waits and commits per 8 MMAs keeps
-      // the issuing thread's fixed costs out of the tensor pipe's way
-      for (int kb = 0; kb < nkb; kb += 2) {
-        const int nk = min(2, nkb - kb);
-        bool ok = true;
-        for (int i = 0; i < nk && ok; ++i) {
-          const int s = (kb + i) % S;
-          ok = sbd::mbar_wait_cluster(&bars->ready[s], ((kb + i) / S) & 1, abort, p.err);
-          if (!ok) break;
-          sbd::tc_fence_after();
-          const uint32_t b_base = sbd::smem_u32(smem + s * P_ACT_BYTES);
+      const uint64_t bdesc0 = sbd::umma_desc(sbd::smem_u32(smem), 16, 1024, sbd::kLayoutSwizzle128B);
+      const uint32_t a0 = tmem + 256;
+      bool ok = nkb > 0 && sbd::mbar_wait_cluster(&bars->ready[0], 0, abort, p.err);
+      for (int base = 0; ok && base < nkb; base += S) {
+        const uint32_t ph = (base / S) & 1;
 #pragma unroll
-          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-            const uint32_t a_tmem = tmem + 256 + s * 32 + kk * 8;
-            const uint64_t bdesc = sbd::umma_desc(b_base + kk * 32, 16, 1024, sbd::kLayoutSwizzle128B);
-            sbd::umma_f16_ts_pair(tmem, a_tmem, bdesc, idesc, (kb + i) != 0 || kk != 0 ? 1u : 0u);
+        for (int j = 0; j < S; ++j) {
+          const int kb = base + j;
+          if (kb >= nkb) break;
+          constexpr int kStepDesc = (UMMA_K * 2) >> 4;  // 32 bytes along K, in descriptor units
+          const uint64_t bd = bdesc0 + static_cast<uint64_t>((j * P_ACT_BYTES) >> 4);
+          const uint32_t ad = a0 + j * 32;
+          const uint32_t ph_next = j + 1 == S ? ph ^ 1 : ph;
+          sbd::tc_fence_after();
+          sbd::umma_f16_ts_pair(tmem, ad, bd, idesc, kb != 0 ? 1u : 0u);
+          sbd::umma_f16_ts_pair(tmem, ad + 8, bd + kStepDesc, idesc, 1u);
+          sbd::umma_f16_ts_pair(tmem, ad + 16, bd + 2 * kStepDesc, idesc, 1u);
+          const bool next_ready = kb + 1 >= nkb || sbd::mbar_test_wait_cluster(&bars->ready[(j + 1) % S], ph_next);
+          sbd::umma_f16_ts_pair(tmem, ad + 24, bd + 3 * kStepDesc, idesc, 1u);
+          sbd::umma_commit_pair(&bars->empty[j], pair_mask);
+          if (!next_ready && !sbd::mbar_wait_cluster(&bars->ready[(j + 1) % S], ph_next, abort, p.err)) {
+            ok = false;
+            break;
           }
         }
-        if (!ok) break;
-        for (int i = 0; i < nk; ++i) sbd::umma_commit_pair(&bars->empty[(kb + i) % S], pair_mask);
       }
       sbd::umma_commit_pair(&bars->accum, pair_mask);
-    }
-  } else if (warp >= Q_WARPS) {
-    // ------------------------------------------------------------ signallers (odd CTA)
-    // warp g forwards A slots kb = g, g + P_SIGNALERS, ... once the odd CTA's
-    // dequant group has written them
-    if (lane == 0 && !lead) {
-      const int g = warp - Q_WARPS;
-      for (int kb = g; kb < nkb; kb += P_SIGNALERS) {
-        const int s = kb % S;
-        if (!sbd::mbar_wait(&bars->dlocal[s], (kb / S) & 1, abort, p.err)) break;
-        sbd::mbar_arrive_remote(sbd::mapa_shared(sbd::smem_u32(&bars->ready[s]), lead_rank));
-      }
     }
   } else {
     // ------------------------------------------------------------ dequant producers (warps 2..17, both CTAs)
@@ -791,6 +805,7 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
     load_scale_tile(p, sct, w0, g_lo, gs, dt, Q_DQ_WARPS * 32);
     sbd::named_bar_sync(1, Q_DQ_WARPS * 32);
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t ready_lead = sbd::mapa_shared(sbd::smem_u32(&bars->ready[0]), lead_rank);
     const int kstep = Q_DQ_GROUPS * BK;
     const int gstep = kstep % p.group == 0 ? kstep / p.group : 0;
     int gi = ((kb0 + grp) * BK + khalf * 32) / p.group - g_lo;
@@ -810,7 +825,8 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
       __syncwarp();
       if (lane == 0) {
         sbd::mbar_arrive(&bars->pempty[s]);
-        sbd::mbar_arrive(lead ? &bars->ready[s] : &bars->dlocal[s]);
+        if (lead) sbd::mbar_arrive(&bars->ready[s]);
+        else sbd::mbar_arrive_remote_cta(ready_lead + s * sizeof(uint64_t));
       }
       gi += gstep;
     }
@@ -1101,13 +1117,17 @@ static int gemm_q4_impl(const void* a, const void* w, const void* scales, int sc
     cfg.blockDim = dim3((pair ? P_WARPS : Q_WARPS) * 32);
     cfg.dynamicSmemBytes = pair ? P_SMEM : Q_SMEM;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = pair ? 2 : 1;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = in_cluster ? static_cast<unsigned>(splits) : 1u;
+    // the pair kernel reads the activations only after griddepcontrol.wait, so
+    // its set-up and weight stream may overlap the previous kernel's tail
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pair ? 2 : 1;
     const cudaError_t e = pair ? cudaLaunchKernelEx(&cfg, gemm_q4_pair_kernel, tact, tw, p)
                                : cudaLaunchKernelEx(&cfg, gemm_q4_kernel, tact, tw, p);
     if (e != cudaSuccess) return sb::cuda_fail(e, "gemm_q4 (cluster launch)");

@@ -137,66 +137,227 @@ __global__ void add_rmsnorm_kernel(const float* __restrict__ x, const void* __re
   }
 }
 
+// ---------------------------------------------------------------- add + RMSNorm, warp per row
+// The same arithmetic for rows of n = 256 * nc (nc <= 8) values: one warp per
+// row holds 8 consecutive values per 256-wide chunk in registers, reduces with
+// shuffles only, and moves 16-byte vectors.  The RMS divisions become one
+// reciprocal per norm and products (within 1.5 ulp of x / d).
+constexpr int kRowWarps = 4;  // rows per CTA
+
+__device__ __forceinline__ void ld8(const void* p, int is_f16, size_t i, float (&v)[8]) {
+  if (is_f16) {
+    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __half*>(p) + i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+      v[2 * e] = f.x;
+      v[2 * e + 1] = f.y;
+    }
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+    const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+__device__ __forceinline__ void st8(float* p, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void st8h(__half* p, const float (&v)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    __half2 h = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+    w[e] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__global__ void __launch_bounds__(kRowWarps * 32) add_rmsnorm_warp_kernel(
+    const float* __restrict__ x, const void* __restrict__ y, int y_f16, const float* __restrict__ w_add,
+    const float* __restrict__ w_norm, float* x_out, float* h_out, __half* h16, int m, int nc, float eps) {
+  constexpr int MAXC = 8;
+  sbd::griddep_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  const int n = nc * 256;
+  const size_t base = static_cast<size_t>(row) * n;
+  sbd::griddep_wait();
+  if (row >= m) return;
+  float v[MAXC][8];
+  // all of a lane's loads are issued before any is used
+  if (y) {
+    float yv[MAXC][8];
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c)
+      if (c < nc) {
+        ld8(y, y_f16, base + c * 256 + lane * 8, yv[c]);
+        ld8(x, 0, base + c * 256 + lane * 8, v[c]);
+      }
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c)
+      if (c < nc)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += yv[c][e] * yv[c][e];
+    const float rd = 1.0f / sqrtf(warp_sum(ss) / n + eps);
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c)
+      if (c < nc) {
+        const float4 wa0 = *reinterpret_cast<const float4*>(w_add + c * 256 + lane * 8);
+        const float4 wa1 = *reinterpret_cast<const float4*>(w_add + c * 256 + lane * 8 + 4);
+        const float wa[8] = {wa0.x, wa0.y, wa0.z, wa0.w, wa1.x, wa1.y, wa1.z, wa1.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[c][e] = v[c][e] + yv[c][e] * rd * wa[e];
+        if (x_out) st8(x_out + base + c * 256 + lane * 8, v[c]);
+      }
+  } else {
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c)
+      if (c < nc) {
+        ld8(x, 0, base + c * 256 + lane * 8, v[c]);
+        if (x_out && x_out != x) st8(x_out + base + c * 256 + lane * 8, v[c]);
+      }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c)
+    if (c < nc)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[c][e] * v[c][e];
+  const float rd = 1.0f / sqrtf(warp_sum(ss) / n + eps);
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c)
+    if (c < nc) {
+      const float4 w0 = *reinterpret_cast<const float4*>(w_norm + c * 256 + lane * 8);
+      const float4 w1 = *reinterpret_cast<const float4*>(w_norm + c * 256 + lane * 8 + 4);
+      const float wn[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      float h[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) h[e] = v[c][e] * rd * wn[e];
+      if (h_out) st8(h_out + base + c * 256 + lane * 8, h);
+      if (h16) st8h(h16 + base + c * 256 + lane * 8, h);
+    }
+}
+
 // ---------------------------------------------------------------- q/k/v prep
 // One CTA per token (nh + 2 warps): warp h < nh normalises + ropes query head h,
 // warp nh the key (written to the f32 cache and its f16 copy), warp nh+1 the
-// value (parameter-free RMSNorm).  hd = 32 * VPL.
+// value (parameter-free RMSNorm).  hd = 32 * VPL; a lane holds VH = VPL / 2
+// consecutive values of each half of the head, so the rotate_half pairs
+// (i, i + hd/2) meet in one lane and every access is a vector of VH.  The RMS
+// division is one reciprocal and products (within 1.5 ulp of x / d).
+template <int VH>
+__device__ __forceinline__ void ldv(const void* p, int is_f16, size_t i, float (&v)[VH]) {
+  if (is_f16) {
+    const __half* h = static_cast<const __half*>(p) + i;
+    if constexpr (VH == 4) {
+      const uint2 u = *reinterpret_cast<const uint2*>(h);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    } else if constexpr (VH == 2) {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(h));
+      v[0] = a.x; v[1] = a.y;
+    } else {
+      v[0] = __half2float(h[0]);
+    }
+  } else {
+    const float* f = static_cast<const float*>(p) + i;
+    if constexpr (VH == 4) {
+      const float4 a = *reinterpret_cast<const float4*>(f);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    } else if constexpr (VH == 2) {
+      const float2 a = *reinterpret_cast<const float2*>(f);
+      v[0] = a.x; v[1] = a.y;
+    } else {
+      v[0] = f[0];
+    }
+  }
+}
+template <int VH>
+__device__ __forceinline__ void stv(float* p, const float (&v)[VH]) {
+  if constexpr (VH == 4) *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  else if constexpr (VH == 2) *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+  else p[0] = v[0];
+}
+template <int VH>
+__device__ __forceinline__ void stvh(__half* p, const float (&v)[VH]) {
+  if constexpr (VH == 4) {
+    __half2 a = __floats2half2_rn(v[0], v[1]), b = __floats2half2_rn(v[2], v[3]);
+    *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+  } else if constexpr (VH == 2) {
+    *reinterpret_cast<__half2*>(p) = __floats2half2_rn(v[0], v[1]);
+  } else {
+    p[0] = __float2half_rn(v[0]);
+  }
+}
+
 template <int VPL>
 __global__ void qkv_prep_kernel(const void* __restrict__ qkv, int qkv_f16, int ld, const float* __restrict__ q_norm,
                                 const float* __restrict__ k_norm, const float* __restrict__ cos_t,
                                 const float* __restrict__ sin_t, const int32_t* __restrict__ pos_dev, int start_pos,
                                 int nh, float eps, __half* q16, float* q32, float* k_cache, float* v_cache,
                                 __half* k16, __half* v16, int64_t cache_stride) {
-  constexpr int HD = 32 * VPL, HALF = HD / 2;
+  constexpr int HD = 32 * VPL, HALF = HD / 2, VH = VPL / 2;
   sbd::griddep_launch_dependents();
-  sbd::griddep_wait();
   const int s = blockIdx.x;  // token (prefill) or sequence (decode)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i0 = lane * VH;  // this lane's offset within each half
+  sbd::griddep_wait();
   const int pos = pos_dev ? pos_dev[s] : start_pos + s;
   const size_t row = static_cast<size_t>(s) * ld;
-  int col0;
-  if (warp < nh) col0 = warp * HD;
-  else if (warp == nh) col0 = nh * HD;
-  else col0 = (nh + 1) * HD;
-  float v[VPL];
+  const int col0 = warp * HD;  // q heads, then k, then v
+  float a[VH], b[VH];
+  ldv<VH>(qkv, qkv_f16, row + col0 + i0, a);
+  ldv<VH>(qkv, qkv_f16, row + col0 + HALF + i0, b);
   float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < VPL; ++j) {
-    v[j] = load_act(qkv, qkv_f16, row + col0 + lane + 32 * j);
-    ss += v[j] * v[j];
-  }
-  const float d = sqrtf(warp_sum(ss) / HD + eps);
-  const float* w = warp < nh ? q_norm : k_norm;
-#pragma unroll
-  for (int j = 0; j < VPL; ++j) v[j] = warp <= nh ? v[j] / d * w[lane + 32 * j] : v[j] / d;
+  for (int e = 0; e < VH; ++e) ss += a[e] * a[e] + b[e] * b[e];
+  const float rd = 1.0f / sqrtf(warp_sum(ss) / HD + eps);
   if (warp <= nh) {
-    // rotate_half: dims i and i + HALF pair up; lane holds j and j + VPL/2
-    const float* c = cos_t + static_cast<size_t>(pos) * HALF;
-    const float* sn = sin_t + static_cast<size_t>(pos) * HALF;
+    const float* w = warp < nh ? q_norm : k_norm;
+    float wa[VH], wb[VH], c[VH], sn[VH];
+    ldv<VH>(w, 0, i0, wa);
+    ldv<VH>(w, 0, HALF + i0, wb);
+    ldv<VH>(cos_t, 0, static_cast<size_t>(pos) * HALF + i0, c);
+    ldv<VH>(sin_t, 0, static_cast<size_t>(pos) * HALF + i0, sn);
 #pragma unroll
-    for (int j = 0; j < VPL / 2; ++j) {
-      const int i = lane + 32 * j;
-      const float a = v[j], b = v[j + VPL / 2];
-      v[j] = a * c[i] - b * sn[i];
-      v[j + VPL / 2] = b * c[i] + a * sn[i];
+    for (int e = 0; e < VH; ++e) {
+      const float x0 = a[e] * rd * wa[e], x1 = b[e] * rd * wb[e];
+      // rotate_half: dims i and i + HALF pair up
+      a[e] = x0 * c[e] - x1 * sn[e];
+      b[e] = x1 * c[e] + x0 * sn[e];
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < VH; ++e) {
+      a[e] *= rd;
+      b[e] *= rd;
     }
   }
   if (warp < nh) {
     const size_t qb = (static_cast<size_t>(s) * nh + warp) * HD;
-#pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      if (q16) q16[qb + lane + 32 * j] = __float2half_rn(v[j]);
-      if (q32) q32[qb + lane + 32 * j] = v[j];
+    if (q16) {
+      stvh<VH>(q16 + qb + i0, a);
+      stvh<VH>(q16 + qb + HALF + i0, b);
+    }
+    if (q32) {
+      stv<VH>(q32 + qb + i0, a);
+      stv<VH>(q32 + qb + HALF + i0, b);
     }
   } else {
     const int seq = pos_dev ? s : 0;
     const size_t cb = static_cast<size_t>(seq) * cache_stride + static_cast<size_t>(pos) * HD;
     float* cache = warp == nh ? k_cache : v_cache;
     __half* c16 = warp == nh ? k16 : v16;
-#pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      cache[cb + lane + 32 * j] = v[j];
-      if (c16) c16[cb + lane + 32 * j] = __float2half_rn(v[j]);
+    stv<VH>(cache + cb + i0, a);
+    stv<VH>(cache + cb + HALF + i0, b);
+    if (c16) {
+      stvh<VH>(c16 + cb + i0, a);
+      stvh<VH>(c16 + cb + HALF + i0, b);
     }
   }
 }
@@ -375,9 +536,20 @@ extern "C" int sb_add_rmsnorm(const float* x, const void* y, int y_dtype, const 
   SB_CHECK_ARG(!y || y_dtype == SB_F16 || y_dtype == SB_F32, "sb_add_rmsnorm: bad y dtype");
   if (m == 0) return SB_OK;
   SB_CHECK_ARG(x && w_norm && (!y || w_add) && (h_out || h16_out), "sb_add_rmsnorm: null pointer");
-  cudaError_t e = sb::launch_pdl(add_rmsnorm_kernel, dim3(m), dim3(kT), 0, static_cast<cudaStream_t>(stream), x, y,
-                                 static_cast<int>(y_dtype == SB_F16), w_add, w_norm, x_out, h_out,
-                                 static_cast<__half*>(h16_out), n, eps);
+  // warp per row for rows of 256 * nc values with 16-byte aligned rows; a CTA per row otherwise
+  const bool vec = n % 256 == 0 && n <= 2048 && sb::aligned(x, 16) && (!y || sb::aligned(y, 16)) &&
+                   sb::aligned(w_norm, 16) && (!w_add || sb::aligned(w_add, 16)) && (!x_out || sb::aligned(x_out, 16)) &&
+                   (!h_out || sb::aligned(h_out, 16)) && (!h16_out || sb::aligned(h16_out, 16));
+  cudaError_t e;
+  if (vec) {
+    e = sb::launch_pdl(add_rmsnorm_warp_kernel, dim3((m + kRowWarps - 1) / kRowWarps), dim3(kRowWarps * 32), 0,
+                       static_cast<cudaStream_t>(stream), x, y, static_cast<int>(y_dtype == SB_F16), w_add, w_norm,
+                       x_out, h_out, static_cast<__half*>(h16_out), m, n / 256, eps);
+  } else {
+    e = sb::launch_pdl(add_rmsnorm_kernel, dim3(m), dim3(kT), 0, static_cast<cudaStream_t>(stream), x, y,
+                       static_cast<int>(y_dtype == SB_F16), w_add, w_norm, x_out, h_out, static_cast<__half*>(h16_out), n,
+                       eps);
+  }
   if (e != cudaSuccess) return sb::cuda_fail(e, "add_rmsnorm_kernel");
   return sb::launch_status("add_rmsnorm_kernel");
 }

@@ -297,6 +297,27 @@ def test_gemm_q4_geglu_equals_gemm_then_geglu(cuda, M, N, K):
                  what=f"geglu M={M} N={N} K={K}")
 
 
+@pytest.mark.parametrize("M,N,geglu", [(1000, 12160, False), (2048, 6144, False), (1000, 12288, True),
+                                        (777, 9216, True)])
+def test_gemm_q4_persistent_tiles(cuda, M, N, geglu):
+    """More CTA-pair tiles than the device holds at once, with a ragged last
+    token tile and a last weight pair half past N."""
+    K = 1536
+    rng = np.random.default_rng(M * 7 + N)
+    packed, scales = synth.q4_weight(rng, N, K)
+    a = synth.activations(rng, M, K)
+    A, P, S = T(a, cuda), T(packed, cuda), T(scales, cuda)
+    gu = kern.gemm_q4(A, P, S)
+    ref = q4.gemm_f64(a, q4.dequant_f16(packed, scales, 4))
+    assert_close(gu.cpu().numpy(), ref, what=f"persistent gemm_q4 M={M} N={N}")
+    if geglu:
+        fused = kern.gemm_q4(A, P, S, geglu=True)
+        chain = torch.empty((M, N // 2), dtype=torch.float16, device=cuda)
+        _lib.call("sb_geglu", gu.data_ptr(), _lib.SB_F16, M, N // 2, None, chain.data_ptr(), kern._stream())
+        kern.device_status()
+        np.testing.assert_array_equal(fused.cpu().numpy(), chain.cpu().numpy())
+
+
 def test_gemm_q4_workspace_only_beyond_cluster_splits(cuda):
     """Split-K within a cluster needs no workspace; only more than 8 splits do."""
     assert kern.gemm_q4_workspace_size(1024, 1536, 2048) == 0  # o: 3 splits in a cluster

@@ -218,6 +218,81 @@ def timed_graph(torch, graph, steps, warmup, stream):
     return start.elapsed_time(end) / steps  # ms per step
 
 
+def config5_sweep(torch, kern, runner, dm, r0, warmup, steps, max_over_ranks, world):
+    """Config 5 on one replica: decode tok/s at batch B, every sequence at the
+    context of r0's sequence 0 (copied into all B), on the GEMV path (B <= 8)
+    and on the tcgen05 GEMM path; and per-call times of the gate|up projection
+    [12288 x 1536] both ways, rotating over the 35 layers' weights (371 MB,
+    past L2) as a decode step does, to locate the GEMV -> GEMM crossover."""
+    out = {"decode": [], "gateup": []}
+    S0 = int(r0.pos[0].item())
+    for B, proj in ((1, "gemv"), (1, "gemm"), (2, "gemv"), (2, "gemm"), (4, "gemv"), (4, "gemm"), (8, "gemv"),
+                    (8, "gemm"), (32, "gemm"), (128, "gemm"), (256, "gemm")):
+        rb = runner.Runner(dm, B, proj=proj)
+        with torch.cuda.stream(rb.stream):
+            for li in range(len(dm.layers)):
+                rb.kc[li].copy_(r0.kc[li][0:1].expand(B, -1, -1))
+                rb.vc[li].copy_(r0.vc[li][0:1].expand(B, -1, -1))
+            rb.pos.fill_(S0)
+            rb.cur.copy_(r0.cur[0:1].expand(B))
+        torch.cuda.synchronize()
+        rb.capture()
+        with torch.cuda.stream(rb.stream):
+            ms = timed_graph(torch, rb.graph, steps, warmup, rb.stream)
+        ms = max_over_ranks(ms)
+        out["decode"].append({"batch": B, "proj": proj, "ms_per_step": ms, "tok_s": world * B * 1e3 / ms,
+                              "context": S0, "gpu_launches_per_step": rb.kernel_launches_per_step()})
+        del rb
+        torch.cuda.empty_cache()
+    # gate|up projection alone: GEMV (f32 x, M <= 8) and GEMM (f16 A) per call
+    dev = dm.device
+    nL = len(dm.layers)
+    N, K = dm.layers[0]["gu"][0].shape[0], dm.layers[0]["gu"][0].shape[1] * 2
+    stream = torch.cuda.Stream(device=dev)
+    gemv_us = {}
+    for M in (1, 2, 4, 8, 16, 32, 64, 128, 256):
+        row = {"M": M}
+        for path in ("gemv", "gemm"):
+            if path == "gemv" and M > 8:
+                continue
+            x = torch.randn((M, K), device=dev, dtype=torch.float32 if path == "gemv" else torch.float16)
+            y = torch.empty((M, N), device=dev, dtype=torch.float32 if path == "gemv" else torch.float16)
+            ws = kern._workspace(dev, kern.gemm_q4_workspace_size(M, N, K)) if path == "gemm" else None
+
+            def call(li):
+                w, sc = dm.layers[li]["gu"]
+                if path == "gemv":
+                    kern.gemv_q4(w, sc, x, y=y)
+                else:
+                    kern.gemm_q4(x, w, sc, C=y, workspace=ws)
+            with torch.cuda.stream(stream):
+                for li in range(nL):
+                    call(li)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for li in range(nL):
+                        call(li)
+                us = timed_graph(torch, g, 3, 1, stream) * 1e3 / nL
+            row[path + "_us"] = us
+            row[path + "_weight_gbs"] = (N * K // 2 + N * (K // 32) * 2) / (us * 1e3)
+        if M <= 8:
+            gemv_us[M] = row["gemv_us"]
+        else:
+            row["gemv_equivalent_us"] = (M + 7) // 8 * gemv_us[8]  # M/8 launches of the 8-row GEMV
+        out["gateup"].append(row)
+    cross = [r["M"] for r in out["gateup"] if r["gemm_us"] < r.get("gemv_us", r.get("gemv_equivalent_us", 1e30))]
+    out["gateup_crossover_M"] = min(cross) if cross else None
+    best = {}
+    for d in out["decode"]:
+        if d["batch"] not in best or d["tok_s"] > best[d["batch"]]["tok_s"]:
+            best[d["batch"]] = d
+    both = sorted(b for b in best if {x["proj"] for x in out["decode"] if x["batch"] == b} == {"gemv", "gemm"})
+    gemm_wins = [b for b in both if best[b]["proj"] == "gemm"]
+    out["decode_crossover_batch"] = min(gemm_wins) if gemm_wins else None
+    return out
+
+
 def load_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -408,6 +483,9 @@ def main():
         lms = timed_graph(torch, g_lm, 5, 2, stream) / 10
     lm_alg = VOCAB * HID // 2 + VOCAB * (HID // 32) * 2 + HID * 4
 
+    # ---------------- config 5: batched decode sweep and the GEMV -> tcgen05 GEMM crossover
+    c5 = config5_sweep(torch, kern, runner, dm, r, args.warmup, 10, max_over_ranks, world)
+
     # ---------------- vocabulary-sharded lm_head over NCCL (N > 1)
     sharded = None
     if world > 1:
@@ -459,6 +537,8 @@ def main():
                        "gpu_launches_per_token": rf.kernel_launches_per_step(),
                        "per_op_graph": {"value": world * 1e3 / dms_ops, "ms_per_token": dms_ops,
                                         "gpu_launches_per_token": r.kernel_launches_per_step()}},
+            "config5": {"metric": "batched decode tok/s (all replicas) by batch and projection path; gate|up "
+                                  "per-call time GEMV vs tcgen05 GEMM", "scaling": "weak (replicas)", **c5},
             "lmhead": {"metric": "q4 GEMV HBM GB/s (lm_head 262144x1536 + argmax)", "value": lm_alg / (lms / 1e3) / 1e9,
                        "unit": "GB/s", "us": lms * 1e3, "frac_of_hbm": lm_alg / (lms / 1e3) / 1e9 / hbm_peak,
                        "peak": hbm_peak},

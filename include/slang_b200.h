@@ -166,6 +166,20 @@ int sb_gemm_q4_geglu(const void* a, const void* w, const void* scales, int scale
 size_t sb_gemm_q4_workspace_size(int m, int n, int k);
 
 /*
+ * Tied lm_head + greedy argmax for many rows at once on the tcgen05 GEMM:
+ * keys[t] = max over rows v of key(alpha * (a[t] . dequant(w[v])), row_offset + v),
+ * key = (orderable(value) << 32) | (0xFFFFFFFF - index) as in sb_lmhead_argmax
+ * (ties -> lowest index); tokens[t] (optional) = the winning index.  a f16
+ * [m, k] (row stride lda), w [n, k/2] packed int4.  keys is cleared first.
+ * The argmax of each CTA's [rows x tokens] tile happens in its epilogue, so no
+ * logits are written.  Replaces logits_33 + argmax1_34/argmax2_35
+ * (gemma4_150/kernels_dsl.py:481-570, 1483-1534) for a batch of sequences
+ * (batched decode, where a GEMV per row would read the embedding m times).
+ */
+int sb_gemm_q4_argmax(const void* a, const void* w, const void* scales, int scale_dtype, int group, int m, int n,
+                      int k, float alpha, int lda, int64_t row_offset, uint64_t* keys, int32_t* tokens, void* stream);
+
+/*
  * sb_gemm_q4 without a caller workspace; it allocates nothing.  No counterpart
  * in the reference: it is for callers that cannot allocate device memory --
  * a host reaching the GPU only through this C ABI, with no CUDA allocator of
@@ -257,6 +271,11 @@ int sb_attn_decode(const float* q32, const float* k_cache, const float* v_cache,
                    int64_t cache_stride, const int32_t* pos_dev, int m, int n_heads, int head_dim,
                    int max_seq, float* out, float* workspace, size_t workspace_bytes, void* stream);
 size_t sb_attn_decode_workspace_size(int m, int n_heads, int head_dim, int max_seq);
+/* sb_attn_decode writing out16 [m][n_heads * head_dim] as f16 (the A operand of
+ * the tcgen05 o-projection in batched decode). */
+int sb_attn_decode_f16(const float* q32, const float* k_cache, const float* v_cache, int64_t cache_stride,
+                       const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, void* out16,
+                       float* workspace, size_t workspace_bytes, void* stream);
 
 /* Device-side step bookkeeping so a decode step replays as one graph:
  * pos[b] += 1; cur[b] = tokens[b]; history[b * hist_len + pos[b]] = tokens[b].

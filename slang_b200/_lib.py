@@ -40,6 +40,8 @@ SIGNATURES = {
     "sb_geglu": ([_vp, _i, _i, _i, _vp, _vp, _vp], _i),
     "sb_attn_prefill": ([_vp, _vp, _vp, _vp, _i, _i, _i, _vp], _i),
     "sb_attn_prefill_ws": ([_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp], _i),
+    "sb_gemm_q4_argmax": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _i64, _vp, _vp, _vp], _i),
+    "sb_attn_decode_f16": ([_vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _vp, _vp, _sz, _vp], _i),
     "sb_attn_prefill_workspace_size": ([_i, _i, _i], _sz),
     "sb_attn_decode": ([_vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _vp, _vp, _sz, _vp], _i),
     "sb_attn_decode_workspace_size": ([_i, _i, _i, _i], _sz),

@@ -250,6 +250,19 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return __fdividef(x, 1.f + __expf(-z2));
 }
 
+// ---- greedy-argmax keys: (orderable(max) << 32) | (0xFFFFFFFF - index), so
+// an unsigned 64-bit MAX keeps the largest value and, on ties, the lowest
+// index (the reference's first-max rule); NaN orders as -inf.
+__device__ __forceinline__ uint32_t orderable(float f) {
+  if (f != f) f = -INFINITY;
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ unsigned long long make_key(float v, long long idx) {
+  return (static_cast<unsigned long long>(orderable(v)) << 32) |
+         static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(idx));
+}
+
 // ---- thread-block clusters and distributed shared memory
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -478,7 +478,7 @@ __global__ void attn_decode_partial_kernel(const float* __restrict__ q32, const 
 }
 
 __global__ void attn_decode_merge_kernel(const float* __restrict__ part, const int32_t* __restrict__ pos_dev, int nh,
-                                         int hd, int max_chunks, float* out) {
+                                         int hd, int max_chunks, float* out, __half* out16) {
   sbd::griddep_launch_dependents();
   const int b = blockIdx.x, h = blockIdx.y;
   sbd::griddep_wait();
@@ -495,7 +495,9 @@ __global__ void attn_decode_merge_kernel(const float* __restrict__ part, const i
       L += pm[hd + 1] * f;
       O += pm[d] * f;
     }
-    out[(static_cast<size_t>(b) * nh + h) * hd + d] = O / L;
+    const size_t o = (static_cast<size_t>(b) * nh + h) * hd + d;
+    if (out16) out16[o] = __float2half_rn(O / L);
+    else out[o] = O / L;
   }
 }
 
@@ -608,13 +610,13 @@ extern "C" size_t sb_attn_decode_workspace_size(int m, int n_heads, int head_dim
   return static_cast<size_t>(m) * chunks * n_heads * (head_dim + 2) * sizeof(float);
 }
 
-extern "C" int sb_attn_decode(const float* q32, const float* k_cache, const float* v_cache, int64_t cache_stride,
-                              const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, float* out,
-                              float* workspace, size_t workspace_bytes, void* stream) {
+static int attn_decode_impl(const float* q32, const float* k_cache, const float* v_cache, int64_t cache_stride,
+                            const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, float* out,
+                            __half* out16, float* workspace, size_t workspace_bytes, void* stream) {
   SB_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256, "sb_attn_decode: head_dim %d unsupported", head_dim);
   SB_CHECK_ARG(n_heads >= 1 && n_heads <= 16 && m >= 0 && max_seq > 0, "sb_attn_decode: bad shape");
   if (m == 0) return SB_OK;
-  SB_CHECK_ARG(q32 && k_cache && v_cache && pos_dev && out && workspace, "sb_attn_decode: null pointer");
+  SB_CHECK_ARG(q32 && k_cache && v_cache && pos_dev && (out || out16) && workspace, "sb_attn_decode: null pointer");
   const size_t need = sb_attn_decode_workspace_size(m, n_heads, head_dim, max_seq);
   if (workspace_bytes < need)
     return sb::fail(SB_ERR_WORKSPACE, "sb_attn_decode: workspace %zu < %zu bytes", workspace_bytes, need);
@@ -634,9 +636,24 @@ extern "C" int sb_attn_decode(const float* q32, const float* k_cache, const floa
   int rc = sb::launch_status("attn_decode_partial_kernel");
   if (rc) return rc;
   e = sb::launch_pdl(attn_decode_merge_kernel, dim3(m, n_heads), dim3(head_dim), 0, st,
-                     static_cast<const float*>(workspace), pos_dev, n_heads, head_dim, max_chunks, out);
+                     static_cast<const float*>(workspace), pos_dev, n_heads, head_dim, max_chunks, out, out16);
   if (e != cudaSuccess) return sb::cuda_fail(e, "attn_decode_merge_kernel");
   return sb::launch_status("attn_decode_merge_kernel");
+}
+
+extern "C" int sb_attn_decode(const float* q32, const float* k_cache, const float* v_cache, int64_t cache_stride,
+                              const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, float* out,
+                              float* workspace, size_t workspace_bytes, void* stream) {
+  return attn_decode_impl(q32, k_cache, v_cache, cache_stride, pos_dev, m, n_heads, head_dim, max_seq, out, nullptr,
+                          workspace, workspace_bytes, stream);
+}
+
+extern "C" int sb_attn_decode_f16(const float* q32, const float* k_cache, const float* v_cache, int64_t cache_stride,
+                                  const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, void* out16,
+                                  float* workspace, size_t workspace_bytes, void* stream) {
+  SB_CHECK_ARG(out16 != nullptr, "sb_attn_decode_f16: null output");
+  return attn_decode_impl(q32, k_cache, v_cache, cache_stride, pos_dev, m, n_heads, head_dim, max_seq, nullptr,
+                          static_cast<__half*>(out16), workspace, workspace_bytes, stream);
 }
 
 extern "C" int sb_step_advance(int32_t* pos, const int32_t* tokens, int32_t* cur, int32_t* history, int hist_len, int m,

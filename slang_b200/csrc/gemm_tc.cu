@@ -93,6 +93,8 @@ struct GemmParams {
   int kb_per_split, kb_total;
   int csplit;          // int4 kernel: > 1 when the K splits of a tile form a cluster and reduce in DSMEM
   int geglu;           // int4 kernel: weight rows are interleaved (gate, up) pairs; C[t][i] = GEGLU of pair i
+  unsigned long long* keys;  // int4 kernel: greedy-argmax keys per token (row index offset by row_offset) instead of C
+  long long row_offset;
   float alpha;
 };
 
@@ -374,6 +376,32 @@ __device__ __forceinline__ void dq_group(const GemmParams& p, const uint8_t* sct
 // Epilogue without split-K: D^T in TMEM (lane = weight row r, column = token);
 // warp dw (0..15) drains tokens [64 (dw / 4), +64) of its lane quadrant into
 // C (f16, or f32 split partials in p.ws, or GEGLU pairs).
+// Greedy argmax over this warp's 32 weight rows for 32 tokens: v[j] is token
+// j's value of row `feat` (this lane).  A butterfly leaves lane l holding the
+// max key of token l over the warp's rows (31 exchanges instead of 32
+// five-step reductions); one atomic MAX per token and warp combines warps
+// and CTAs.
+__device__ __forceinline__ void argmax_epilogue(const GemmParams& p, const uint32_t (&v)[32], int feat, int lane,
+                                                int tok0) {
+  unsigned long long k[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    k[j] = feat < p.n ? sbd::make_key(p.alpha * __uint_as_float(v[j]), p.row_offset + feat) : 0ull;
+#pragma unroll
+  for (int o = 16, n = 32; o > 0; o >>= 1, n >>= 1) {
+    const bool upper = lane & o;  // keep tokens [n/2, n) of the current set, hand the lower half over
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const unsigned long long send = upper ? k[i] : k[i + n / 2];
+      const unsigned long long keep = upper ? k[i + n / 2] : k[i];
+      const unsigned long long got = __shfl_xor_sync(0xFFFFFFFFu, send, o);
+      k[i] = got > keep ? got : keep;
+    }
+  }
+  // lane l now holds token l: the lane bits pick halves most significant first
+  if (tok0 + lane < p.m && k[0]) atomicMax(p.keys + tok0 + lane, k[0]);
+}
+
 __device__ __forceinline__ void epilogue_direct(const GemmParams& p, uint32_t lane_addr, int dw, int r, int lane,
                                                 int w0, int t0, int split) {
   const int feat = w0 + r;
@@ -384,7 +412,9 @@ __device__ __forceinline__ void epilogue_direct(const GemmParams& p, uint32_t la
     uint32_t v[32];
     sbd::tmem_ld_32x32b_x32(lane_addr + col, v);
     sbd::tmem_wait_ld();
-    if (p.ws) {
+    if (p.keys) {
+      argmax_epilogue(p, v, feat, lane, t0 + col);
+    } else if (p.ws) {
       if (!feat_ok) continue;
       float* dst = p.ws + (static_cast<size_t>(split) * p.m + t0 + col) * p.n + feat;
 #pragma unroll
@@ -1046,7 +1076,7 @@ extern "C" int sb_gemm_f16_f32out(const void* a, const void* b, float* c, int m,
 
 static int gemm_q4_impl(const void* a, const void* w, const void* scales, int scale_dtype, int group, void* c, int m,
                         int n, int k, float alpha, int lda, int ldc, void* workspace, size_t workspace_bytes,
-                        void* stream, int geglu) {
+                        void* stream, int geglu, uint64_t* keys = nullptr, long long row_offset = 0) {
   SB_CHECK_ARG(m >= 0 && n >= 0 && k > 0, "sb_gemm_q4: bad shape");
   SB_CHECK_ARG(!geglu || n % 2 == 0, "sb_gemm_q4_geglu: n=%d must be even (interleaved gate/up rows)", n);
   SB_CHECK_ARG(k % 64 == 0, "sb_gemm_q4: k=%d must be a multiple of 64", k);
@@ -1054,9 +1084,9 @@ static int gemm_q4_impl(const void* a, const void* w, const void* scales, int sc
                group);
   SB_CHECK_ARG(scale_dtype == SB_SCALE_F16 || scale_dtype == SB_SCALE_F32, "sb_gemm_q4: bad scale dtype");
   if (m == 0 || n == 0) return SB_OK;
-  SB_CHECK_ARG(a && w && scales && c, "sb_gemm_q4: null pointer");
-  SB_CHECK_ARG(lda >= k && ldc >= (geglu ? n / 2 : n), "sb_gemm_q4: leading dimension too small");
-  if (!sb::aligned(a, 16) || !sb::aligned(w, 16) || !sb::aligned(c, 2) || lda % 8)
+  SB_CHECK_ARG(a && w && scales && (c || keys), "sb_gemm_q4: null pointer");
+  SB_CHECK_ARG(lda >= k && (keys || ldc >= (geglu ? n / 2 : n)), "sb_gemm_q4: leading dimension too small");
+  if (!sb::aligned(a, 16) || !sb::aligned(w, 16) || (c && !sb::aligned(c, 2)) || lda % 8)
     return sb::fail(SB_ERR_ALIGN, "sb_gemm_q4: A and W must be 16-byte aligned with lda a multiple of 8");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int esz = scale_dtype == SB_SCALE_F16 ? 2 : 4;
@@ -1081,14 +1111,23 @@ static int gemm_q4_impl(const void* a, const void* w, const void* scales, int sc
   p.scale_f16 = esz == 2;
   p.alpha = alpha;
   p.geglu = geglu;
+  p.keys = reinterpret_cast<unsigned long long*>(keys);
+  p.row_offset = row_offset;
   p.kb_total = k / BK;
-  int splits = q4_splits(m, n, k, group, esz);
+  // the argmax epilogue needs whole sums: no K split
+  int splits = keys ? 1 : q4_splits(m, n, k, group, esz);
   const size_t need = splits > max_cs ? static_cast<size_t>(splits) * m * n * sizeof(float) : 0;
   if (need && (!workspace || workspace_bytes < need)) {
     // without room for partial sums use the largest cluster split instead
     splits = max_cs;
     if (QW * q4_scale_groups((k / BK + splits - 1) / splits, group) * esz > Q_SCALE_BYTES)
       return sb::fail(SB_ERR_WORKSPACE, "sb_gemm_q4: k=%d needs split-K (%zu workspace bytes) for its scales", k, need);
+  }
+  if (keys) {
+    if (QW * q4_scale_groups(k / BK, group) * esz > Q_SCALE_BYTES)
+      return sb::fail(SB_ERR_ARG, "sb_gemm_q4_argmax: k=%d has too many scale groups for one split", k);
+    cudaError_t e = cudaMemsetAsync(keys, 0, sizeof(uint64_t) * m, s);
+    if (e != cudaSuccess) return sb::cuda_fail(e, "sb_gemm_q4_argmax: clearing keys");
   }
   static bool done[64] = {false};
   static bool done_pair[64] = {false};
@@ -1145,6 +1184,17 @@ extern "C" int sb_gemm_q4(const void* a, const void* w, const void* scales, int 
                           void* stream) {
   return gemm_q4_impl(a, w, scales, scale_dtype, group, c, m, n, k, alpha, lda, ldc, workspace, workspace_bytes,
                       stream, 0);
+}
+
+extern "C" int sb_gemm_q4_argmax(const void* a, const void* w, const void* scales, int scale_dtype, int group, int m,
+                                 int n, int k, float alpha, int lda, int64_t row_offset, uint64_t* keys, int32_t* tokens,
+                                 void* stream) {
+  SB_CHECK_ARG(keys != nullptr, "sb_gemm_q4_argmax: null keys");
+  SB_CHECK_ARG(n <= 0 || row_offset + n <= (1ll << 32) - 1, "sb_gemm_q4_argmax: row indices exceed 32 bits");
+  const int rc = gemm_q4_impl(a, w, scales, scale_dtype, group, nullptr, m, n, k, alpha, lda, 0, nullptr, 0, stream, 0,
+                              keys, row_offset);
+  if (rc != SB_OK || !tokens || m == 0) return rc;
+  return sb_keys_to_tokens(keys, tokens, m, stream);
 }
 
 extern "C" int sb_gemm_q4_geglu(const void* a, const void* w, const void* scales, int scale_dtype, int group,

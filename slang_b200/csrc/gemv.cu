@@ -63,16 +63,7 @@ struct GemvSmem {
   int abort;
 };
 
-__device__ __forceinline__ uint32_t orderable(float f) {
-  if (f != f) f = -INFINITY;
-  const uint32_t b = __float_as_uint(f);
-  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-
-__device__ __forceinline__ unsigned long long make_key(float v, long long idx) {
-  return (static_cast<unsigned long long>(orderable(v)) << 32) |
-         static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(idx));
-}
+using sbd::make_key;
 
 template <int M, int GPL, bool SF16, int EPI>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const GemvParams p) {

@@ -181,6 +181,28 @@ def gemm_q4(A: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, C: torch.Ten
     return C
 
 
+def gemm_q4_argmax(A: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, row_offset: int = 0,
+                   keys: torch.Tensor | None = None, tokens: torch.Tensor | None = None, alpha: float = 1.0,
+                   want_tokens: bool = True):
+    """lm_head + greedy argmax for every row of A on the tcgen05 GEMM (the
+    batched form of ``lmhead_argmax``); returns (keys, tokens)."""
+    _need(A, "A", (torch.float16,))
+    _need(w, "w", (torch.uint8,))
+    _need(scales, "scales", (torch.float16, torch.float32))
+    M, K = A.shape
+    N = w.shape[0]
+    if w.shape[1] * 2 != K:
+        raise ValueError("packed weight does not match A's K")
+    if keys is None:
+        keys = torch.empty(M, dtype=torch.int64, device=A.device)
+    if want_tokens and tokens is None:
+        tokens = torch.empty(M, dtype=torch.int32, device=A.device)
+    _lib.call("sb_gemm_q4_argmax", _ptr(A), _ptr(w), _ptr(scales), _DT[scales.dtype], group_of(scales, K), M, N, K,
+              float(alpha), A.stride(0), int(row_offset), _ptr(keys), _ptr(tokens) if want_tokens else None,
+              _stream())
+    return keys, tokens
+
+
 def gemm_q4_workspace_size(M: int, N: int, K: int) -> int:
     return int(_lib.load().sb_gemm_q4_workspace_size(M, N, K))
 

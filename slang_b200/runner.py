@@ -86,11 +86,25 @@ class DeviceModel:
 
 
 class Runner:
-    def __init__(self, dm: DeviceModel, batch: int = 1, fused: bool = False):
-        if batch < 1 or batch > 8:
-            raise ValueError("the GEMV decode path serves 1..8 sequences")
+    """Decode (and prefill) state for ``batch`` sequences.
+
+    ``proj`` picks the decode projections: "gemv" (the int4 GEMV, 1..8
+    sequences, f32 activations), "gemm" (the fused int4 tcgen05 GEMM at
+    M = batch with f16 activations and the lm_head argmax in the GEMM
+    epilogue, any batch) or "auto" (GEMV up to 8 sequences, GEMM above)."""
+
+    MAX_BATCH = 1024
+
+    def __init__(self, dm: DeviceModel, batch: int = 1, fused: bool = False, proj: str = "auto"):
+        if proj == "auto":
+            proj = "gemv" if batch <= 8 else "gemm"
+        if proj not in ("gemv", "gemm"):
+            raise ValueError("proj must be 'gemv', 'gemm' or 'auto'")
+        if batch < 1 or batch > self.MAX_BATCH or (proj == "gemv" and batch > 8):
+            raise ValueError("the GEMV decode path serves 1..8 sequences, the GEMM path 1..%d" % self.MAX_BATCH)
         if fused and batch != 1:
             raise ValueError("the persistent decode kernel serves one sequence")
+        self.proj = proj
         self.fused = fused
         self.dm = dm
         cfg = dm.cfg
@@ -112,6 +126,13 @@ class Runner:
         self.qkv, self.q = f32(B, self.nqkv), f32(B, self.qd)
         self.attn, self.o = f32(B, self.qd), f32(B, H)
         self.gu, self.a, self.d = f32(B, 2 * self.F), f32(B, self.F), f32(B, H)
+        if proj == "gemm":
+            f16 = lambda *s: torch.zeros(s, dtype=torch.float16, device=dev)  # noqa: E731
+            self.h16, self.qkv16, self.attn16 = f16(B, H), f16(B, self.nqkv), f16(B, self.qd)
+            self.o16, self.a16, self.d16 = f16(B, H), f16(B, self.F), f16(B, H)
+            ws = max(kern.gemm_q4_workspace_size(B, n, k) for n, k in
+                     ((self.nqkv, H), (H, self.qd), (2 * self.F, H), (H, self.F)))
+            self.gemm_ws = torch.empty(max(1, ws // 4), dtype=torch.float32, device=dev) if ws else None
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
         self.cur = torch.zeros(B, dtype=torch.int32, device=dev)
         self.tok = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -130,7 +151,45 @@ class Runner:
     def _gemv(self, w, x, y):
         kern.gemv_q4(w[0], w[1], x, y=y)
 
+    def _decode_ops_gemm(self):
+        """One decode step for the batch on the tcgen05 GEMM: f16 activations
+        between the projections, the lm_head argmax in the GEMM epilogue."""
+        dm, L0 = self.dm, self.dm.layers
+        s = kern._stream()
+        B, H = self.B, self.H
+        ws = self.gemm_ws
+
+        def proj(w, A, C, geglu=False):
+            kern.gemm_q4(A, w[0], w[1], C=C, workspace=ws, geglu=geglu)
+
+        _lib.call("sb_embed_q4", dm.embed_q.data_ptr(), dm.embed_s.data_ptr(), _F16, dm.cfg["group"],
+                  self.cur.data_ptr(), B, H, float(dm.cfg["embed_scale"]), self.x.data_ptr(), None, s)
+        _lib.call("sb_add_rmsnorm", self.x.data_ptr(), None, _F32, None, L0[0]["in_norm"].data_ptr(),
+                  self.x.data_ptr(), None, self.h16.data_ptr(), B, H, self.eps, s)
+        for li, L in enumerate(L0):
+            proj(L["qkv"], self.h16, self.qkv16)
+            _lib.call("sb_qkv_prep", self.qkv16.data_ptr(), _F16, self.nqkv, L["q_norm"].data_ptr(),
+                      L["k_norm"].data_ptr(), dm.cos.data_ptr(), dm.sin.data_ptr(), self.pos.data_ptr(), 0, B,
+                      self.nh, self.hd, self.eps, None, self.q.data_ptr(), self.kc[li].data_ptr(),
+                      self.vc[li].data_ptr(), None, None, self.cache_stride, s)
+            _lib.call("sb_attn_decode_f16", self.q.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
+                      self.cache_stride, self.pos.data_ptr(), B, self.nh, self.hd, self.max_seq,
+                      self.attn16.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws.numel() * 4, s)
+            proj(L["o"], self.attn16, self.o16)
+            _lib.call("sb_add_rmsnorm", self.x.data_ptr(), self.o16.data_ptr(), _F16, L["post_attn_norm"].data_ptr(),
+                      L["pre_ffn_norm"].data_ptr(), self.x.data_ptr(), None, self.h16.data_ptr(), B, H, self.eps, s)
+            proj(L["gu"], self.h16, self.a16, geglu=True)
+            proj(L["down"], self.a16, self.d16)
+            nxt = L0[li + 1]["in_norm"] if li + 1 < len(L0) else dm.final_norm
+            _lib.call("sb_add_rmsnorm", self.x.data_ptr(), self.d16.data_ptr(), _F16, L["post_ffn_norm"].data_ptr(),
+                      nxt.data_ptr(), self.x.data_ptr(), None, self.h16.data_ptr(), B, H, self.eps, s)
+        kern.gemm_q4_argmax(self.h16, dm.embed_q, dm.embed_s, keys=self.keys, tokens=self.tok)
+        _lib.call("sb_step_advance", self.pos.data_ptr(), self.tok.data_ptr(), self.cur.data_ptr(),
+                  self.history.data_ptr(), self.max_seq, B, s)
+
     def _decode_ops(self):
+        if self.proj == "gemm":
+            return self._decode_ops_gemm()
         dm, L0 = self.dm, self.dm.layers
         s = kern._stream()
         lib = _lib.load()
@@ -191,6 +250,12 @@ class Runner:
         if self.fused:
             return 1
         nL = len(self.dm.layers)
+        if self.proj == "gemm":
+            B, H, F = self.B, self.H, self.F
+            split = lambda n, k: 1 if kern.gemm_q4_workspace_size(B, n, k) else 0  # noqa: E731
+            per_layer = (4 + split(self.nqkv, H) + split(H, self.qd) + split(2 * F, H) + split(H, F)
+                         + 1 + 2 + 2)  # prep, attention (2), add+norm (2)
+            return 2 + nL * per_layer + 2 + 1  # embed + norm, layers, argmax GEMM + tokens, advance
         per_layer = 4 + 1 + 2 + 2 + 1  # 4 GEMVs, prep, attention (2), add+norm (2), geglu
         return 2 + nL * per_layer + 2 + 1  # embed + first norm, layers, lm_head (gemv + tokens), advance
 

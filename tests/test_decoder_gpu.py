@@ -140,3 +140,20 @@ def test_config4_256_greedy_tokens_match_reference(cuda, cfg4, batched, fused):
     print(f"config 4 batched={batched} fused={fused}: max |top logit - reference| = {err:.3e}")
     # f16 activations in the batched prefill GEMMs vs the f32 token-wise path
     assert err < (5e-2 if batched else 5e-3)
+
+
+@pytest.mark.parametrize("batch", [3, 12])
+def test_batched_decode_on_tcgen05_gemm(cuda, golden, batch):
+    """Config 5's large-batch decode: projections and the lm_head argmax on the
+    tcgen05 GEMM (f16 activations).  Every sequence equals its own
+    single-sequence run (the GEMV path) for 8 greedy steps."""
+    model = small_model()
+    prompts = [synth.prompt_tokens(5 + 3 * b, 2048, seed=40 + b) for b in range(batch)]
+    singles = [runner.greedy_generate(model, p, 8, device=cuda, max_seq=64) for p in prompts]
+    dm = runner.DeviceModel(model, cuda, 64)
+    r = runner.Runner(dm, batch, proj="gemm")
+    firsts = [r.prefill(p, seq=b) for b, p in enumerate(prompts)]
+    rest = r.decode(7).cpu().numpy()
+    got = [[firsts[b]] + rest[b].tolist() for b in range(batch)]
+    agree = sum(g == s for g, s in zip(got, singles))
+    assert agree == batch, f"{batch - agree} of {batch} sequences diverge: {got} vs {singles}"

@@ -328,3 +328,42 @@ def test_gemm_q4_workspace_only_beyond_cluster_splits(cuda):
 def test_no_device_timeouts(cuda):
     torch.cuda.synchronize()
     kern.device_status()
+
+
+# ------------------------------------------------------------------ lm_head argmax on the tcgen05 GEMM
+@pytest.mark.parametrize("m", [1, 37, 256])
+def test_gemm_q4_argmax_vs_oracle(cuda, m):
+    """Batched lm_head + greedy argmax in the GEMM epilogue: tokens equal the
+    oracle's argmax of the f16-activation GEMM, keys carry the max value."""
+    rng = np.random.default_rng(900 + m)
+    v, k = 50000, 1536
+    packed, scales = synth.q4_weight(rng, v, k)
+    h = synth.activations(rng, m, k)
+    keys, tok = kern.gemm_q4_argmax(T(h, cuda), T(packed, cuda), T(scales, cuda))
+    logits = q4.gemm_f64(h, q4.dequant_f16(packed, scales, 4))
+    np.testing.assert_array_equal(tok.cpu().numpy(), np.argmax(logits, axis=1))
+    np.testing.assert_array_equal(q4.unpack_key_index(keys.cpu().numpy().view(np.uint64)), np.argmax(logits, axis=1))
+
+
+def test_gemm_q4_argmax_tie_and_shards(cuda):
+    """Ties go to the lowest index; shards with row offsets combine by an integer MAX."""
+    rng = np.random.default_rng(77)
+    v, k, m = 8192, 1536, 5
+    packed, scales = synth.q4_weight(rng, v, k)
+    h = synth.activations(rng, m, k)
+    top = np.argmax(q4.gemm_f64(h, q4.dequant_f16(packed, scales, 4)), axis=1)
+    # copy row top[0] (scaled up so it wins) to a lower and a higher index
+    src = int(top[0])
+    for r in (100, 7000):
+        packed[r] = packed[src]
+        scales[r] = (scales[src].astype(np.float32) * 4).astype(np.float16)
+    keys, tok = kern.gemm_q4_argmax(T(h, cuda), T(packed, cuda), T(scales, cuda))
+    assert int(tok[0].item()) == 100
+    ref = np.argmax(q4.gemm_f64(h, q4.dequant_f16(packed, scales, 4)), axis=1)
+    np.testing.assert_array_equal(tok.cpu().numpy(), ref)
+    parts = []
+    for lo, hi in ((0, 4096), (4096, 8192)):
+        kk, _ = kern.gemm_q4_argmax(T(h, cuda), T(packed[lo:hi], cuda), T(scales[lo:hi], cuda), row_offset=lo,
+                                    want_tokens=False)
+        parts.append(kk.cpu().numpy().view(np.uint64))
+    np.testing.assert_array_equal(q4.unpack_key_index(np.maximum(parts[0], parts[1])), ref)

@@ -506,6 +506,31 @@ def main():
         sharded = {"metric": "vocab-sharded lm_head + argmax (NCCL MAX of keys), tok/s", "value": 1e3 / sms_,
                    "unit": "tok/s", "us": sms_ * 1e3, "shards": world,
                    "hbm_gbs_aggregate": lm_alg / (sms_ / 1e3) / 1e9, "scaling": "strong"}
+        # the same shards with the exchange in peer memory (atomic MAX over NVLink in the GEMV, one
+        # counting kernel per rank), captured as a graph of 10 steps
+        try:
+            ph = lmhead.PeerLMHead(dm.embed_q, dm.embed_s, rank, world)
+        except Exception as exc:  # noqa: BLE001 - CUDA IPC unavailable: report, keep the NCCL numbers
+            sharded["peer"] = {"unavailable": str(exc)[:200]}
+            ph = None
+        if ph is not None:
+            with torch.cuda.stream(stream):
+                for _ in range(args.warmup):
+                    ph(r.h, keys, toks)
+                torch.cuda.synchronize()
+                gp = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gp, stream=stream):
+                    for _ in range(10):
+                        ph(r.h, keys, toks)
+                dist.barrier()
+                pms = timed_graph(torch, gp, max(1, args.steps // 10), 1, stream) / 10
+            pms = max_over_ranks(pms)
+            # (each rank holds its own random model here; the sharded tokens are checked in the tests)
+            sharded["peer"] = {"metric": "vocab-sharded lm_head + argmax, exchange in peer memory over NVLink, tok/s",
+                               "value": 1e3 / pms, "us": pms * 1e3, "hbm_gbs_aggregate": lm_alg / (pms / 1e3) / 1e9,
+                               "gpu_launches_per_token": 2}
+            del gp
+            ph.close()
 
     if rank == 0:
         cpu = cpu_sample_prefill() if (not args.no_cpu_baseline and world == 1) else None

@@ -112,6 +112,30 @@ int sb_lmhead_argmax(const void* emb, const void* scales, int scale_dtype, int g
 int sb_keys_to_tokens(const uint64_t* keys, int32_t* tokens, int m, void* stream);
 
 /*
+ * Vocabulary-sharded lm_head with the cross-GPU exchange in device memory
+ * (replaces the NCCL MAX of keys after sb_lmhead_argmax on each shard).  Each
+ * rank creates one mailbox of sb_peer_mailbox_size() bytes with
+ * sb_peer_buffer_create (zeroed; ipc_handle receives a 64-byte CUDA IPC
+ * handle), shares the handle, and maps the other ranks' mailboxes with
+ * sb_peer_buffer_open.  sb_lmhead_argmax_peer then runs this rank's shard
+ * GEMV (rows row_offset .. row_offset + v) with every CTA's keys going to
+ * every rank's mailbox by system-scope atomic MAX over NVLink, and one small
+ * kernel that counts this rank in at every mailbox, waits (bounded; timeout
+ * -> SB_ERR_TIMEOUT in sb_device_status) for all `world` ranks, and writes the
+ * combined keys / tokens (m <= 64 rows).  peer_mailboxes: device array of the
+ * `world` mailbox addresses as this process maps them (its own at `rank`).
+ * Every rank must make the same sequence of calls.
+ */
+size_t sb_peer_mailbox_size(void);
+int sb_peer_buffer_create(size_t bytes, void** dev_ptr, void* ipc_handle);
+int sb_peer_buffer_open(const void* ipc_handle, void** dev_ptr);
+int sb_peer_buffer_close(void* dev_ptr);
+int sb_peer_buffer_free(void* dev_ptr);
+int sb_lmhead_argmax_peer(const void* emb, const void* scales, int scale_dtype, int group, const void* h, int h_dtype,
+                          int m, int v, int k, int64_t row_offset, const uint64_t* peer_mailboxes, int world,
+                          void* own_mailbox, uint64_t* keys, int32_t* tokens, void* stream);
+
+/*
  * f16 GEMM on the tcgen05 tensor cores, f32 accumulate:
  *   C[M, N] = f16(alpha * A[M, K] @ (B[N, K]^T if tr else B[K, N]))
  * Replaces PrefillGPU._gemm (gemma4_150/prefill_gpu.py:151-184) and the

@@ -40,6 +40,12 @@ SIGNATURES = {
     "sb_geglu": ([_vp, _i, _i, _i, _vp, _vp, _vp], _i),
     "sb_attn_prefill": ([_vp, _vp, _vp, _vp, _i, _i, _i, _vp], _i),
     "sb_attn_prefill_ws": ([_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp], _i),
+    "sb_peer_mailbox_size": ([], _sz),
+    "sb_peer_buffer_create": ([_sz, _vp, _vp], _i),
+    "sb_peer_buffer_open": ([_vp, _vp], _i),
+    "sb_peer_buffer_close": ([_vp], _i),
+    "sb_peer_buffer_free": ([_vp], _i),
+    "sb_lmhead_argmax_peer": ([_vp, _vp, _i, _i, _vp, _i, _i, _i, _i, _i64, _vp, _i, _vp, _vp, _vp, _vp], _i),
     "sb_gemm_q4_argmax": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _i64, _vp, _vp, _vp], _i),
     "sb_attn_decode_f16": ([_vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _vp, _vp, _sz, _vp], _i),
     "sb_attn_prefill_workspace_size": ([_i, _i, _i], _sz),

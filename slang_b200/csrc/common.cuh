@@ -263,6 +263,15 @@ __device__ __forceinline__ unsigned long long make_key(float v, long long idx) {
          static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(idx));
 }
 
+// ---- peer mailbox of the vocabulary-sharded lm_head (one per rank, mapped by
+// every rank): a step counter, two per-parity arrival counts and two
+// per-parity slot arrays of argmax keys.
+constexpr int kMailEpoch = 0;
+constexpr int kMailCount = 64;     // uint32_t[2]
+constexpr int kMailKeys = 128;     // unsigned long long[2][kMailMaxRows]
+constexpr int kMailMaxRows = 64;
+constexpr int kMailBytes = kMailKeys + 2 * kMailMaxRows * 8;
+
 // ---- thread-block clusters and distributed shared memory
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -26,6 +26,7 @@
 // sums are reduced with half-warp shuffles and, across K slices, through
 // shared memory in a fixed order (deterministic results).
 #include <algorithm>
+#include <cstring>
 
 #include "common.cuh"
 #include "q4_dot.cuh"
@@ -52,6 +53,11 @@ struct GemvParams {
   int* err;
   int m, n, k, group, ldy, ks, rs, n_stages, scale_bulk, x_f32;
   long long row_offset;
+  // vocabulary shards over peer memory: each CTA's key goes to every rank's
+  // mailbox (atomic MAX through NVLink) instead of `keys`
+  const unsigned long long* peer_mailboxes;  // device array of `world` mailbox addresses
+  const uint32_t* peer_epoch;                // this rank's step counter (its parity picks the key slots)
+  int world, peer_row0;                      // peer_row0: first batch row of this launch
 };
 
 struct GemvSmem {
@@ -266,7 +272,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
     if (tid < M && tid < p.m) {
       unsigned long long key = 0;
       for (int wi = 0; wi < kConsumers / 32; ++wi) key = sm.best[wi][tid] > key ? sm.best[wi][tid] : key;
-      if (key) atomicMax(p.keys + tid, key);
+      if (key) {
+        if (p.peer_mailboxes) {
+          const uint32_t q = *p.peer_epoch & 1u;
+          for (int pe = 0; pe < p.world; ++pe)
+            atomicMax_system(reinterpret_cast<unsigned long long*>(p.peer_mailboxes[pe] + sbd::kMailKeys) +
+                                 q * sbd::kMailMaxRows + p.peer_row0 + tid,
+                             key);
+          __threadfence_system();  // performed at every peer before this CTA exits
+        } else {
+          atomicMax(p.keys + tid, key);
+        }
+      }
     }
   }
 }
@@ -373,7 +390,8 @@ int run(GemvParams p, int epi, bool xf32, bool sf16, cudaStream_t s) {
     q.x = static_cast<const char*>(p.x) + done * x_row;
     if (epi == EPI_STORE) q.y = p.y + static_cast<size_t>(done) * p.ldy;
     else {
-      q.keys = p.keys + done;
+      if (p.keys) q.keys = p.keys + done;
+      q.peer_row0 = p.peer_row0 + done;
       if (p.logits) q.logits = p.logits + static_cast<size_t>(done) * p.n;
     }
     Plan pl = plan(mt, p.n, p.k, sms);
@@ -470,6 +488,121 @@ extern "C" int sb_lmhead_argmax(const void* emb, const void* scales, int scale_d
     return sb::launch_status("keys_to_tokens_kernel");
   }
   return SB_OK;
+}
+
+namespace {
+
+// The exchange step of the vocabulary-sharded lm_head over peer memory (one
+// CTA per rank, after that rank's shard GEMV has added its keys to every
+// mailbox): clear the other parity's slots and count, tell every rank this
+// rank is done (system-scope atomic add after a system fence), wait (bounded)
+// until all `world` ranks are done, read the combined keys, advance the step.
+// Slots alternate by step parity: a rank writes step e + 1's keys only after
+// every rank has passed its step-e count, i.e. after this rank cleared them.
+__global__ void peer_combine_kernel(uint8_t* own, const unsigned long long* peers, int world, int m,
+                                    unsigned long long* keys_out, int32_t* tokens, int* err) {
+  __shared__ int ok;
+  uint32_t* epoch = reinterpret_cast<uint32_t*>(own + sbd::kMailEpoch);
+  uint32_t* count = reinterpret_cast<uint32_t*>(own + sbd::kMailCount);
+  unsigned long long* slots = reinterpret_cast<unsigned long long*>(own + sbd::kMailKeys);
+  const uint32_t e = *epoch, q = e & 1u;
+  for (int i = threadIdx.x; i < m; i += blockDim.x) slots[(q ^ 1u) * sbd::kMailMaxRows + i] = 0ull;
+  if (threadIdx.x == 0) count[q ^ 1u] = 0u;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int pe = 0; pe < world; ++pe) atomicAdd_system(reinterpret_cast<uint32_t*>(peers[pe] + sbd::kMailCount) + q, 1u);
+    // every rank's keys have landed once every rank has counted in
+    const uint64_t t0 = sbd::global_ns();
+    int done = 0;
+    while (!done) {
+      uint32_t c;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(c) : "l"(count + q) : "memory");
+      if (c >= static_cast<uint32_t>(world)) done = 1;
+      else if (sbd::global_ns() - t0 > sbd::kWaitLimitNs) break;
+    }
+    ok = done;
+    if (!done && err) atomicExch(err, SB_ERR_TIMEOUT);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < m; i += blockDim.x) {
+    unsigned long long k;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(k) : "l"(slots + q * sbd::kMailMaxRows + i) : "memory");
+    if (!ok) k = 0ull;
+    if (keys_out) keys_out[i] = k;
+    if (tokens) tokens[i] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *epoch = e + 1u;
+}
+
+}  // namespace
+
+extern "C" size_t sb_peer_mailbox_size(void) { return sbd::kMailBytes; }
+
+extern "C" int sb_peer_buffer_create(size_t bytes, void** dev_ptr, void* ipc_handle) {
+  SB_CHECK_ARG(bytes > 0 && dev_ptr && ipc_handle, "sb_peer_buffer_create: bad arguments");
+  cudaError_t e = cudaMalloc(dev_ptr, bytes);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "sb_peer_buffer_create: cudaMalloc");
+  e = cudaMemset(*dev_ptr, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), *dev_ptr);
+  if (e != cudaSuccess) {
+    cudaFree(*dev_ptr);
+    *dev_ptr = nullptr;
+    return sb::cuda_fail(e, "sb_peer_buffer_create: IPC handle");
+  }
+  return SB_OK;
+}
+
+extern "C" int sb_peer_buffer_open(const void* ipc_handle, void** dev_ptr) {
+  SB_CHECK_ARG(ipc_handle && dev_ptr, "sb_peer_buffer_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "sb_peer_buffer_open");
+  return SB_OK;
+}
+
+extern "C" int sb_peer_buffer_close(void* dev_ptr) {
+  cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  return e == cudaSuccess ? SB_OK : sb::cuda_fail(e, "sb_peer_buffer_close");
+}
+
+extern "C" int sb_peer_buffer_free(void* dev_ptr) {
+  cudaError_t e = cudaFree(dev_ptr);
+  return e == cudaSuccess ? SB_OK : sb::cuda_fail(e, "sb_peer_buffer_free");
+}
+
+extern "C" int sb_lmhead_argmax_peer(const void* emb, const void* scales, int scale_dtype, int group, const void* h,
+                                     int h_dtype, int m, int v, int k, int64_t row_offset,
+                                     const uint64_t* peer_mailboxes, int world, void* own_mailbox, uint64_t* keys,
+                                     int32_t* tokens, void* stream) {
+  int rc = check_common("sb_lmhead_argmax_peer", emb, scales, scale_dtype, group, h, h_dtype, m, v, k);
+  if (rc != SB_OK) return rc;
+  SB_CHECK_ARG(m <= sbd::kMailMaxRows, "sb_lmhead_argmax_peer: m=%d > %d", m, sbd::kMailMaxRows);
+  SB_CHECK_ARG(world >= 1 && peer_mailboxes && own_mailbox, "sb_lmhead_argmax_peer: bad peer arguments");
+  SB_CHECK_ARG(row_offset >= 0 && row_offset + v <= 0xFFFFFFFFLL, "sb_lmhead_argmax_peer: row indices must fit in 32 bits");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (v > 0) {
+    GemvParams p{};
+    p.w = static_cast<const uint8_t*>(emb);
+    p.scales = scales;
+    p.x = h;
+    p.m = m;
+    p.n = v;
+    p.k = k;
+    p.group = group;
+    p.row_offset = row_offset;
+    p.peer_mailboxes = reinterpret_cast<const unsigned long long*>(peer_mailboxes);
+    p.peer_epoch = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(own_mailbox) + sbd::kMailEpoch);
+    p.world = world;
+    rc = run(p, EPI_ARGMAX, h_dtype == SB_F32, scale_dtype == SB_SCALE_F16, s);
+    if (rc != SB_OK) return rc;
+  }
+  peer_combine_kernel<<<1, 128, 0, s>>>(static_cast<uint8_t*>(own_mailbox),
+                                        reinterpret_cast<const unsigned long long*>(peer_mailboxes), world, m,
+                                        reinterpret_cast<unsigned long long*>(keys), tokens, sb::device_error_word());
+  return sb::launch_status("peer_combine_kernel");
 }
 
 extern "C" int sb_keys_to_tokens(const uint64_t* keys, int32_t* tokens, int m, void* stream) {

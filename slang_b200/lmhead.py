@@ -56,3 +56,74 @@ class ShardedLMHead:
         keys, _ = kern.lmhead_argmax(self.emb, self.scales, h, row_offset=self.lo, keys=keys, want_tokens=False)
         combine_keys_(keys, self.group)
         return keys, kern.keys_to_tokens(keys, tokens)
+
+
+class PeerLMHead(ShardedLMHead):
+    """The sharded lm_head with the cross-GPU step done in device memory over
+    NVLink instead of an NCCL call.
+
+    Every rank owns a small mailbox (``sb_peer_buffer_create``) that every
+    other rank maps (CUDA IPC).  The shard GEMV's CTAs put their argmax keys
+    into every rank's mailbox with system-scope atomic MAX over NVLink, then
+    one small kernel per rank counts in at every mailbox and waits (bounded)
+    until all ranks have, and reads the combined keys -- two launches, no host
+    synchronisation, capturable in a CUDA graph.  The exchange is a function of
+    the call sequence: every rank must call once per step.
+    """
+
+    def __init__(self, emb: torch.Tensor, scales: torch.Tensor, rank: int = 0, world: int = 1, group=None,
+                 full_table: bool = True):
+        import ctypes
+
+        super().__init__(emb, scales, rank, world, group, full_table)
+        from . import _lib
+        self._lib = _lib
+        self.rank = rank
+        size = int(_lib.load().sb_peer_mailbox_size())
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        _lib.call("sb_peer_buffer_create", size, ctypes.byref(own), handle)
+        self.own = own.value
+        handles = [bytes(handle)]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        self.opened = []
+        ptrs = []
+        for r, hb in enumerate(handles):
+            if r == rank:
+                ptrs.append(self.own)
+                continue
+            p = ctypes.c_void_p()
+            buf = (ctypes.c_char * 64).from_buffer_copy(hb)
+            _lib.call("sb_peer_buffer_open", buf, ctypes.byref(p))
+            self.opened.append(p.value)
+            ptrs.append(p.value)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=emb.device)
+
+    def __call__(self, h: torch.Tensor, keys: torch.Tensor | None = None,
+                 tokens: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        k = self.emb.shape[1] * 2
+        h2 = h.reshape(-1, k)
+        m = h2.shape[0]
+        if keys is None:
+            keys = torch.empty(m, dtype=torch.int64, device=h.device)
+        if tokens is None:
+            tokens = torch.empty(m, dtype=torch.int32, device=h.device)
+        self._lib.call("sb_lmhead_argmax_peer", kern._ptr(self.emb), kern._ptr(self.scales),
+                       kern._DT[self.scales.dtype], kern.group_of(self.scales, k), kern._ptr(h2), kern._DT[h.dtype], m,
+                       self.emb.shape[0], k, int(self.lo), kern._ptr(self.peers), self.world, self.own,
+                       kern._ptr(keys), kern._ptr(tokens), kern._stream())
+        return keys, tokens
+
+    def close(self):
+        """Unmap the peers' mailboxes, wait for every rank, free this one."""
+        torch.cuda.synchronize()
+        for p in self.opened:
+            self._lib.call("sb_peer_buffer_close", p)
+        self.opened = []
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        if self.own:
+            self._lib.call("sb_peer_buffer_free", self.own)
+            self.own = None

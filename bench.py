@@ -53,11 +53,12 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", default="",
                     choices=["", "gemm_q4", "gemm_q4_geglu", "gemm_f16", "gemv", "lmhead", "attn", "prefill", "decode",
-                             "decode_fused"],
+                             "decode_fused", "decode_batch"],
                     help="run one kernel --iters times on a single shape and exit (for ncu captures)")
     ap.add_argument("--shape", default="6144,1536", help="N,K of the weight for --kernel")
     ap.add_argument("--m", type=int, default=1024, help="rows of the activation for --kernel")
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=256, help="sequences for --kernel decode_batch")
     return ap.parse_args()
 
 
@@ -75,6 +76,21 @@ def run_model_case(args):
     prompt = synth.prompt_tokens(args.m, cfg["vocab"], seed=99)
     r.prefill(prompt, graph=False)
     torch.cuda.synchronize()
+    if args.kernel == "decode_batch":
+        # --batch sequences on the tcgen05 GEMM path, each at sequence 0's context (--m tokens)
+        rb = runner.Runner(dm, args.batch, proj="gemm")
+        for li in range(len(dm.layers)):
+            rb.kc[li].copy_(r.kc[li][0:1].expand(args.batch, -1, -1))
+            rb.vc[li].copy_(r.vc[li][0:1].expand(args.batch, -1, -1))
+        rb.pos.fill_(int(r.pos[0].item()))
+        rb.cur.copy_(r.cur[0:1].expand(args.batch))
+        torch.cuda.synchronize()
+        for _ in range(1 + args.iters):
+            with torch.cuda.stream(rb.stream):
+                rb._decode_ops()
+        torch.cuda.synchronize()
+        print(f"ran decode_batch x{1 + args.iters} (batch {args.batch}, context {args.m}) eagerly")
+        return
     for _ in range(args.iters):
         if args.kernel == "prefill":
             r.prefill(prompt, graph=False)
@@ -89,7 +105,7 @@ def run_kernel_case(args):
     """One kernel on one shape, --iters launches after one warm-up (ncu target)."""
     import torch
 
-    if args.kernel in ("prefill", "decode", "decode_fused"):
+    if args.kernel in ("prefill", "decode", "decode_fused", "decode_batch"):
         return run_model_case(args)
     from slang_b200 import kernels as kern
     dev = torch.device("cuda", 0)

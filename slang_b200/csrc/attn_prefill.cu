@@ -20,12 +20,17 @@
 //               K 64; P_j from TMEM, V_j MN-major from shared memory) into D
 //               accumulator columns.  S_{j+1} is issued before O += P_j V_j so
 //               the softmax of block j+1 overlaps the P.V MMAs of block j.
-//   warps 2..5  one thread per query row (its TMEM lane): reads S_j, masks,
-//               and forms p = 2^(s log2 e - m) in f16 with a running maximum m
-//               that is raised -- rescaling O and the row sum by 2^(m_old - m)
-//               -- only when the block maximum exceeds it by more than 2^8, so
-//               O is touched rarely and p stays below 256; writes P_j into TMEM
-//               for the MMA.  At the end: O / (row sum) -> f16 -> out.
+//   warps 2..9  softmax, two warps per TMEM lane quadrant (a thread per query
+//               row in each): both read the row's 64 scores of S_j and take
+//               the same masked maximum; each forms p = 2^(s log2 e - m) in f16
+//               for its 32 keys with a running maximum m that is raised --
+//               rescaling its half of O and its part of the row sum by
+//               2^(m_old - m) -- only when the block maximum exceeds it by more
+//               than 2^14, so O is touched rarely and p stays below 2^14 (f16
+//               holds it); writes its 16 columns of P_j into TMEM for the MMA.
+//               At the end the two halves' row sums are added through shared
+//               memory and each warp writes O / (row sum) for its half of the
+//               head dimension.
 // TMEM: O [0, D), S ring [D, D + 128), P ring [D + 128, D + 192).
 //
 // Every mbarrier wait is bounded (2 s of %globaltimer); a stuck pipeline
@@ -42,7 +47,7 @@ namespace {
 
 constexpr int QR = 128;  // query rows per CTA
 constexpr int KB = 64;   // keys per block
-constexpr int WARPS = 6;
+constexpr int WARPS = 10;  // TMA, MMA, 8 softmax
 
 template <int HD>
 struct Cfg {
@@ -51,13 +56,21 @@ struct Cfg {
   static constexpr int OFF_K = Q_BYTES;
   static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
   static constexpr int OFF_BAR = OFF_V + 2 * KV_BYTES;
-  static constexpr int SMEM = OFF_BAR + 256 + 1024;  // + barriers + 1 KB alignment slack
+  static constexpr int OFF_L = OFF_BAR + 256;           // the two halves' row sums [2][QR] f32
+  static constexpr int SMEM = OFF_L + 2 * QR * 4 + 1024;  // + 1 KB alignment slack
   static constexpr uint32_t TM_O = 0, TM_S = HD, TM_P = HD + 2 * KB;
   static constexpr uint32_t TM_COLS = HD + 3 * KB <= 256 ? 256 : 512;
 };
 
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kRescale = 8.f;  // log2 units
+constexpr float kRescale = 14.f;  // log2 units: p < 2^14 fits f16
+
+// 2^x by the SFU (ex2.approx, flush-to-zero): p is rounded to f16 right after.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 struct Bars {
   uint64_t q_full;
@@ -140,8 +153,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       sbd::mbar_init(&bars->v_full[i], 1);
       sbd::mbar_init(&bars->v_empty[i], 1);
       sbd::mbar_init(&bars->s_full[i], 1);
-      sbd::mbar_init(&bars->s_free[i], 4);
-      sbd::mbar_init(&bars->p_full[i], 4);
+      sbd::mbar_init(&bars->s_free[i], 8);
+      sbd::mbar_init(&bars->p_full[i], 8);
       sbd::mbar_init(&bars->p_free[i], 1);
     }
     sbd::mbar_init(&bars->o_final, 1);
@@ -251,14 +264,15 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax / epilogue (warps 2..5)
+    // ------------------------------------------------------------ softmax / epilogue (warps 2..9)
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // keys [32 half, +32) of each block; O columns [HD/2 half, +HD/2)
     const int row = quad * 32 + lane;
     const int r = r0 + row;
     const bool row_ok = r < p.rows;
     const int token = row_ok ? r / p.nh : -1;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    float m_used = 0.f, l = 0.f;
+    float m_used = 0.f, l = 0.f;  // l: this half's part of the row sum
     bool ok = true;
     for (int j = 0; j < nb && ok; ++j) {
       const int st = j & 1;
@@ -274,55 +288,67 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       if (lane == 0) sbd::mbar_arrive(&bars->s_free[st]);
       // causal mask: key j*KB + c is visible to this row when it is <= token
       const int nvis = max(0, min(KB, token - (kb_lo + j) * KB + 1));
-      float mx = -INFINITY;
+      // masked row maximum over all 64 keys (both halves compute the same one)
+      float t[32];
 #pragma unroll
-      for (int c = 0; c < KB; ++c)
-        if (c < nvis) mx = fmaxf(mx, __uint_as_float(sv[c >> 5][c & 31]));
-      const float mx2 = mx * kLog2e;
+      for (int e = 0; e < 32; ++e) {
+        const float a = 2 * e < nvis ? __uint_as_float(sv[(2 * e) >> 5][(2 * e) & 31]) : -INFINITY;
+        const float b = 2 * e + 1 < nvis ? __uint_as_float(sv[(2 * e + 1) >> 5][(2 * e + 1) & 31]) : -INFINITY;
+        t[e] = fmaxf(a, b);
+      }
+#pragma unroll
+      for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+        for (int e = 0; e < w; ++e) t[e] = fmaxf(t[e], t[e + w]);
+      const float mx2 = t[0] * kLog2e;
       if (j == 0) {
         m_used = nvis > 0 ? mx2 : 0.f;
       } else {
         const bool need = nvis > 0 && mx2 > m_used + kRescale;
         if (__any_sync(0xFFFFFFFFu, need)) {
-          // O must be quiet: wait for O += P_{j-1} V_{j-1}
+          // O must be quiet: wait for O += P_{j-1} V_{j-1}; each half rescales its columns
           ok = __all_sync(0xFFFFFFFFu,
                           sbd::mbar_wait(&bars->p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, p.err));
           if (!ok) break;
           sbd::tc_fence_after();
-          const float alpha = need ? exp2f(m_used - mx2) : 1.f;
-          for (int cc = 0; cc < HD / 32; ++cc) {
+          const float alpha = need ? ex2(m_used - mx2) : 1.f;
+          for (int cc = 0; cc < HD / 64; ++cc) {
             uint32_t ov[32];
-            sbd::tmem_ld_32x32b_x32(lane_base + TM_O + cc * 32, ov);
+            const uint32_t col = TM_O + half * (HD / 2) + cc * 32;
+            sbd::tmem_ld_32x32b_x32(lane_base + col, ov);
             sbd::tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-            tmem_st_x32(lane_base + TM_O + cc * 32, ov);
+            tmem_st_x32(lane_base + col, ov);
           }
           sbd::tmem_wait_st();
           l *= alpha;
           if (need) m_used = mx2;
         }
       }
-      // p = 2^(s log2 e - m_used) in f16, packed two keys per TMEM column
-      uint32_t pk[32];
-      float ls = 0.f;
+      // p = 2^(s log2 e - m_used) in f16 for this half's 32 keys, two per TMEM column
+      uint32_t pk[16];
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int c = 2 * e;
-        const float p0 = c < nvis ? exp2f(__uint_as_float(sv[c >> 5][c & 31]) * kLog2e - m_used) : 0.f;
-        const float p1 = c + 1 < nvis ? exp2f(__uint_as_float(sv[(c + 1) >> 5][(c + 1) & 31]) * kLog2e - m_used) : 0.f;
+      for (int e = 0; e < 16; ++e) {
+        const int c = 32 * half + 2 * e;
+        const uint32_t s0 = half ? sv[1][2 * e] : sv[0][2 * e];
+        const uint32_t s1 = half ? sv[1][2 * e + 1] : sv[0][2 * e + 1];
+        const float p0 = c < nvis ? ex2(__uint_as_float(s0) * kLog2e - m_used) : 0.f;
+        const float p1 = c + 1 < nvis ? ex2(__uint_as_float(s1) * kLog2e - m_used) : 0.f;
         const __half2 h = __floats2half2_rn(p0, p1);
-        ls += __low2float(h) + __high2float(h);
+        const float2 hf = __half22float2(h);
+        ls[e & 3] += hf.x + hf.y;
         pk[e] = *reinterpret_cast<const uint32_t*>(&h);
       }
-      l += ls;
+      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       // the P buffer is free once O += P_{j-2} V_{j-2} has run
       if (j >= 2) {
         ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait(&bars->p_free[st], ((j - 2) >> 1) & 1, abort, p.err));
         if (!ok) break;
         sbd::tc_fence_after();
       }
-      tmem_st_x32(lane_base + TM_P + st * 32, pk);
+      sbd::tmem_st_32x32b_x16(lane_base + TM_P + st * 32 + half * 16, pk);
       sbd::tmem_wait_st();
       sbd::tc_fence_before();
       __syncwarp();
@@ -330,32 +356,39 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
     // ------------------------------------------------------------ epilogue: O / l -> f16
     if (ok) ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait(&bars->o_final, 0, abort, p.err));
+    // the row sum is the two halves' parts (every softmax warp meets this barrier)
+    float* lx = reinterpret_cast<float*>(smem + C::OFF_L);
+    lx[half * QR + row] = l;
+    sbd::named_bar_sync(1, 8 * 32);
+    const float l_row = lx[row] + lx[QR + row];
     if (ok && nchunks > 1) {
       // a share of a split tile: unnormalised O with its running max and sum
       sbd::tc_fence_after();
       float* dst = p.part + ((static_cast<size_t>(tile) * p.maxc + blockIdx.y) * QR + row) * part_stride<HD>();
-      for (int cc = 0; cc < HD / 32; ++cc) {
+      for (int cc = 0; cc < HD / 64; ++cc) {
+        const int col = half * (HD / 2) + cc * 32;
         uint32_t ov[32];
-        sbd::tmem_ld_32x32b_x32(lane_base + TM_O + cc * 32, ov);
+        sbd::tmem_ld_32x32b_x32(lane_base + TM_O + col, ov);
         sbd::tmem_wait_ld();
         if (!row_ok) continue;
 #pragma unroll
         for (int e = 0; e < 32; e += 4)
-          *reinterpret_cast<float4*>(dst + cc * 32 + e) =
+          *reinterpret_cast<float4*>(dst + col + e) =
               make_float4(__uint_as_float(ov[e]), __uint_as_float(ov[e + 1]), __uint_as_float(ov[e + 2]),
                           __uint_as_float(ov[e + 3]));
       }
-      if (row_ok) {
+      if (row_ok && half == 0) {
         dst[HD] = m_used;
-        dst[HD + 1] = l;
+        dst[HD + 1] = l_row;
       }
     } else if (ok) {
       sbd::tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
       __half* dst = p.out + static_cast<size_t>(r) * HD;
-      for (int cc = 0; cc < HD / 32; ++cc) {
+      for (int cc = 0; cc < HD / 64; ++cc) {
+        const int col = half * (HD / 2) + cc * 32;
         uint32_t ov[32];
-        sbd::tmem_ld_32x32b_x32(lane_base + TM_O + cc * 32, ov);
+        sbd::tmem_ld_32x32b_x32(lane_base + TM_O + col, ov);
         sbd::tmem_wait_ld();
         if (!row_ok) continue;
 #pragma unroll
@@ -367,7 +400,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
                                                 __uint_as_float(ov[e + 2 * q + 1]) * inv);
             o4[q] = *reinterpret_cast<const uint32_t*>(&h);
           }
-          *reinterpret_cast<uint4*>(dst + cc * 32 + e) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+          *reinterpret_cast<uint4*>(dst + col + e) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
         }
       }
     }

@@ -142,7 +142,7 @@ __global__ void add_rmsnorm_kernel(const float* __restrict__ x, const void* __re
 // row holds 8 consecutive values per 256-wide chunk in registers, reduces with
 // shuffles only, and moves 16-byte vectors.  The RMS divisions become one
 // reciprocal per norm and products (within 1.5 ulp of x / d).
-constexpr int kRowWarps = 4;  // rows per CTA
+constexpr int kRowWarps = 8;  // rows per CTA
 
 __device__ __forceinline__ void ld8(const void* p, int is_f16, size_t i, float (&v)[8]) {
   if (is_f16) {
@@ -175,71 +175,73 @@ __device__ __forceinline__ void st8h(__half* p, const float (&v)[8]) {
   *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// The CTA stages w_add and w_norm in shared memory before it waits for the
+// previous kernel (they are constants), so a row costs one dependent global
+// round trip (x, y) instead of three.
+template <int NC>
 __global__ void __launch_bounds__(kRowWarps * 32) add_rmsnorm_warp_kernel(
     const float* __restrict__ x, const void* __restrict__ y, int y_f16, const float* __restrict__ w_add,
-    const float* __restrict__ w_norm, float* x_out, float* h_out, __half* h16, int m, int nc, float eps) {
-  constexpr int MAXC = 8;
+    const float* __restrict__ w_norm, float* x_out, float* h_out, __half* h16, int m, float eps) {
+  constexpr int n = NC * 256;
+  extern __shared__ float wsm[];  // [w_add (n, when y)] [w_norm (n)]
+  float* wa_s = wsm;
+  float* wn_s = wsm + (y ? n : 0);
   sbd::griddep_launch_dependents();
+  for (int i = threadIdx.x; i < n / 4; i += blockDim.x) {
+    if (y) reinterpret_cast<float4*>(wa_s)[i] = __ldg(reinterpret_cast<const float4*>(w_add) + i);
+    reinterpret_cast<float4*>(wn_s)[i] = __ldg(reinterpret_cast<const float4*>(w_norm) + i);
+  }
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
-  const int n = nc * 256;
   const size_t base = static_cast<size_t>(row) * n;
   sbd::griddep_wait();
   if (row >= m) return;
-  float v[MAXC][8];
+  float v[NC][8];
   // all of a lane's loads are issued before any is used
   if (y) {
-    float yv[MAXC][8];
+    float yv[NC][8];
 #pragma unroll
-    for (int c = 0; c < MAXC; ++c)
-      if (c < nc) {
-        ld8(y, y_f16, base + c * 256 + lane * 8, yv[c]);
-        ld8(x, 0, base + c * 256 + lane * 8, v[c]);
-      }
+    for (int c = 0; c < NC; ++c) {
+      ld8(y, y_f16, base + c * 256 + lane * 8, yv[c]);
+      ld8(x, 0, base + c * 256 + lane * 8, v[c]);
+    }
     float ss = 0.f;
 #pragma unroll
-    for (int c = 0; c < MAXC; ++c)
-      if (c < nc)
+    for (int c = 0; c < NC; ++c)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) ss += yv[c][e] * yv[c][e];
+      for (int e = 0; e < 8; ++e) ss += yv[c][e] * yv[c][e];
     const float rd = 1.0f / sqrtf(warp_sum(ss) / n + eps);
 #pragma unroll
-    for (int c = 0; c < MAXC; ++c)
-      if (c < nc) {
-        const float4 wa0 = *reinterpret_cast<const float4*>(w_add + c * 256 + lane * 8);
-        const float4 wa1 = *reinterpret_cast<const float4*>(w_add + c * 256 + lane * 8 + 4);
-        const float wa[8] = {wa0.x, wa0.y, wa0.z, wa0.w, wa1.x, wa1.y, wa1.z, wa1.w};
+    for (int c = 0; c < NC; ++c) {
+      float wa[8];
+      ld8(wa_s, 0, c * 256 + lane * 8, wa);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[c][e] = v[c][e] + yv[c][e] * rd * wa[e];
-        if (x_out) st8(x_out + base + c * 256 + lane * 8, v[c]);
-      }
+      for (int e = 0; e < 8; ++e) v[c][e] = v[c][e] + yv[c][e] * rd * wa[e];
+      if (x_out) st8(x_out + base + c * 256 + lane * 8, v[c]);
+    }
   } else {
 #pragma unroll
-    for (int c = 0; c < MAXC; ++c)
-      if (c < nc) {
-        ld8(x, 0, base + c * 256 + lane * 8, v[c]);
-        if (x_out && x_out != x) st8(x_out + base + c * 256 + lane * 8, v[c]);
-      }
+    for (int c = 0; c < NC; ++c) {
+      ld8(x, 0, base + c * 256 + lane * 8, v[c]);
+      if (x_out && x_out != x) st8(x_out + base + c * 256 + lane * 8, v[c]);
+    }
   }
   float ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < MAXC; ++c)
-    if (c < nc)
+  for (int c = 0; c < NC; ++c)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss += v[c][e] * v[c][e];
+    for (int e = 0; e < 8; ++e) ss += v[c][e] * v[c][e];
   const float rd = 1.0f / sqrtf(warp_sum(ss) / n + eps);
 #pragma unroll
-  for (int c = 0; c < MAXC; ++c)
-    if (c < nc) {
-      const float4 w0 = *reinterpret_cast<const float4*>(w_norm + c * 256 + lane * 8);
-      const float4 w1 = *reinterpret_cast<const float4*>(w_norm + c * 256 + lane * 8 + 4);
-      const float wn[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-      float h[8];
+  for (int c = 0; c < NC; ++c) {
+    float wn[8], h[8];
+    ld8(wn_s, 0, c * 256 + lane * 8, wn);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) h[e] = v[c][e] * rd * wn[e];
-      if (h_out) st8(h_out + base + c * 256 + lane * 8, h);
-      if (h16) st8h(h16 + base + c * 256 + lane * 8, h);
-    }
+    for (int e = 0; e < 8; ++e) h[e] = v[c][e] * rd * wn[e];
+    if (h_out) st8(h_out + base + c * 256 + lane * 8, h);
+    if (h16) st8h(h16 + base + c * 256 + lane * 8, h);
+  }
 }
 
 // ---------------------------------------------------------------- q/k/v prep
@@ -306,6 +308,18 @@ __global__ void qkv_prep_kernel(const void* __restrict__ qkv, int qkv_f16, int l
   const int s = blockIdx.x;  // token (prefill) or sequence (decode)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int i0 = lane * VH;  // this lane's offset within each half
+  // constants first (norm weights; the RoPE row when the position is known),
+  // so they are in registers when the previous kernel's q|k|v arrive
+  float wa[VH], wb[VH], c[VH], sn[VH];
+  if (warp <= nh) {
+    const float* w = warp < nh ? q_norm : k_norm;
+    ldv<VH>(w, 0, i0, wa);
+    ldv<VH>(w, 0, HALF + i0, wb);
+    if (!pos_dev) {
+      ldv<VH>(cos_t, 0, static_cast<size_t>(start_pos + s) * HALF + i0, c);
+      ldv<VH>(sin_t, 0, static_cast<size_t>(start_pos + s) * HALF + i0, sn);
+    }
+  }
   sbd::griddep_wait();
   const int pos = pos_dev ? pos_dev[s] : start_pos + s;
   const size_t row = static_cast<size_t>(s) * ld;
@@ -318,12 +332,10 @@ __global__ void qkv_prep_kernel(const void* __restrict__ qkv, int qkv_f16, int l
   for (int e = 0; e < VH; ++e) ss += a[e] * a[e] + b[e] * b[e];
   const float rd = 1.0f / sqrtf(warp_sum(ss) / HD + eps);
   if (warp <= nh) {
-    const float* w = warp < nh ? q_norm : k_norm;
-    float wa[VH], wb[VH], c[VH], sn[VH];
-    ldv<VH>(w, 0, i0, wa);
-    ldv<VH>(w, 0, HALF + i0, wb);
-    ldv<VH>(cos_t, 0, static_cast<size_t>(pos) * HALF + i0, c);
-    ldv<VH>(sin_t, 0, static_cast<size_t>(pos) * HALF + i0, sn);
+    if (pos_dev) {
+      ldv<VH>(cos_t, 0, static_cast<size_t>(pos) * HALF + i0, c);
+      ldv<VH>(sin_t, 0, static_cast<size_t>(pos) * HALF + i0, sn);
+    }
 #pragma unroll
     for (int e = 0; e < VH; ++e) {
       const float x0 = a[e] * rd * wa[e], x1 = b[e] * rd * wb[e];
@@ -544,9 +556,24 @@ extern "C" int sb_add_rmsnorm(const float* x, const void* y, int y_dtype, const 
                    (!h_out || sb::aligned(h_out, 16)) && (!h16_out || sb::aligned(h16_out, 16));
   cudaError_t e;
   if (vec) {
-    e = sb::launch_pdl(add_rmsnorm_warp_kernel, dim3((m + kRowWarps - 1) / kRowWarps), dim3(kRowWarps * 32), 0,
-                       static_cast<cudaStream_t>(stream), x, y, static_cast<int>(y_dtype == SB_F16), w_add, w_norm,
-                       x_out, h_out, static_cast<__half*>(h16_out), m, n / 256, eps);
+    const dim3 grid((m + kRowWarps - 1) / kRowWarps), block(kRowWarps * 32);
+    const size_t smem = static_cast<size_t>(y ? 2 : 1) * n * sizeof(float);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int yf = static_cast<int>(y_dtype == SB_F16);
+    __half* h16 = static_cast<__half*>(h16_out);
+#define SB_NORM(NC) \
+  e = sb::launch_pdl(add_rmsnorm_warp_kernel<NC>, grid, block, smem, st, x, y, yf, w_add, w_norm, x_out, h_out, h16, m, eps)
+    switch (n / 256) {
+      case 1: SB_NORM(1); break;
+      case 2: SB_NORM(2); break;
+      case 3: SB_NORM(3); break;
+      case 4: SB_NORM(4); break;
+      case 5: SB_NORM(5); break;
+      case 6: SB_NORM(6); break;
+      case 7: SB_NORM(7); break;
+      default: SB_NORM(8); break;
+    }
+#undef SB_NORM
   } else {
     e = sb::launch_pdl(add_rmsnorm_kernel, dim3(m), dim3(kT), 0, static_cast<cudaStream_t>(stream), x, y,
                        static_cast<int>(y_dtype == SB_F16), w_add, w_norm, x_out, h_out, static_cast<__half*>(h16_out), n,

@@ -136,6 +136,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
   volatile int* abort = &bars->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the next kernel may start its set-up; this one reads q, k, v (the previous
+  // kernel's output) only after griddepcontrol.wait in the TMA warp
+  sbd::griddep_launch_dependents();
   // heaviest tiles (latest tokens) first; chunk blockIdx.y of the tile's key blocks
   const int tile = gridDim.x - 1 - blockIdx.x;
   const int r0 = tile * QR;
@@ -182,6 +185,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int issued_k = 0, issued_v = 0;
+      sbd::griddep_wait();
       sbd::mbar_arrive_expect_tx(&bars->q_full, Q_BYTES);
 #pragma unroll
       for (int b = 0; b < NBOX; ++b) sbd::tma_load_2d(&tmQ, &bars->q_full, smem + b * (QR * 128), 64 * b, r0);
@@ -423,6 +427,8 @@ __global__ void attn_merge_kernel(const float* __restrict__ part, __half* __rest
   constexpr int VPL = HD / 32;  // values per lane: 2, 4 or 8
   constexpr int PS = part_stride<HD>();
   static_assert(VPL == 2 || VPL % 4 == 0, "lane vector width");
+  sbd::griddep_launch_dependents();
+  sbd::griddep_wait();
   const int tile = blockIdx.x;
   const int row = blockIdx.y * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   const int nchunks = (tile_key_blocks(tile, rows, nh, s_len) + kpc - 1) / kpc;
@@ -517,10 +523,14 @@ int launch_attn(const void* q16, const void* k16, const void* v16, void* out16, 
     }
   }
   p.maxc = maxc;
-  attn_prefill_kernel<HD><<<dim3(tiles, maxc), WARPS * 32, C::SMEM, stream>>>(tq, tk, tv, p);
+  cudaError_t e = sb::launch_pdl(attn_prefill_kernel<HD>, dim3(tiles, maxc), dim3(WARPS * 32), C::SMEM, stream, tq,
+                                 tk, tv, p);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "attn_prefill_kernel");
   rc = sb::launch_status("attn_prefill_kernel");
   if (rc != SB_OK || maxc == 1) return rc;
-  attn_merge_kernel<HD><<<dim3(tiles, QR / 8), 256, 0, stream>>>(part, p.out, p.rows, n_heads, s_len, p.kpc, maxc);
+  e = sb::launch_pdl(attn_merge_kernel<HD>, dim3(tiles, QR / 8), dim3(256), 0, stream, static_cast<const float*>(part),
+                     p.out, p.rows, n_heads, s_len, p.kpc, maxc);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "attn_merge_kernel");
   return sb::launch_status("attn_merge_kernel");
 }
 

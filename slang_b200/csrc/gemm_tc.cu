@@ -887,6 +887,8 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
 
 __global__ void splitk_finalize_kernel(const float* __restrict__ ws, __half* __restrict__ c, int m, int n, int ldc,
                                        int splits, float alpha, int geglu) {
+  sbd::griddep_launch_dependents();
+  sbd::griddep_wait();  // the partial planes are the previous kernel's output
   const size_t plane = static_cast<size_t>(m) * n;
   const int nout = geglu ? n / 2 : n;
   const size_t total = static_cast<size_t>(m) * nout;
@@ -964,8 +966,9 @@ int q4_splits(int m, int n, int k, int group, int scale_bytes) {
 int finalize(const GemmParams& p, int splits, cudaStream_t s) {
   const size_t total = static_cast<size_t>(p.m) * p.n;
   const int grid = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 16));
-  splitk_finalize_kernel<<<grid, 256, 0, s>>>(p.ws, static_cast<__half*>(p.c), p.m, p.n, p.ldc, splits, p.alpha,
-                                              p.geglu);
+  cudaError_t e = sb::launch_pdl(splitk_finalize_kernel, dim3(grid), dim3(256), 0, s, static_cast<const float*>(p.ws),
+                                 static_cast<__half*>(p.c), p.m, p.n, p.ldc, splits, p.alpha, p.geglu);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "splitk_finalize_kernel");
   return sb::launch_status("splitk_finalize_kernel");
 }
 

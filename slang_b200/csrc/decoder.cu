@@ -419,83 +419,228 @@ __global__ void geglu_kernel(const void* __restrict__ gu, int gu_f16, int f, int
 }
 
 // ---------------------------------------------------------------- decode attention
-// Split-KV decode attention for one KV head shared by nh query heads.
-// Partial: CTA (b, chunk) stages the chunk's CK keys in shared memory, warp h
-// scores them for query head h (lane t keeps key t), takes the chunk's max and
-// sum, then thread d forms the unnormalised sum_t p[h][t] V[t][d] for every
-// head.  Merge: CTA (b, h), thread d rescales the chunks (flash-decoding).
+// Split-KV decode attention for one KV head shared by NH query heads
+// (flash-decoding).  CTA (b, split) owns keys [split * spk, (split + 1) * spk)
+// of sequence b and walks them in chunks of CK = 32 keys with an online
+// softmax; the merge kernel rescales the splits.  The chunk loop is
+// software-pipelined: V of chunk c + 1 is bulk-copied into the other of two
+// shared-memory buffers and K of chunk c + 1 is loaded into registers while
+// chunk c's softmax and P.V run.
+//   scores:  thread (key t, slice s) holds K[t] dims {4 (s + 8 j) .. + 3} in
+//            registers and forms all NH partial dots against q (float4 reads
+//            of q broadcast across the warp's 4 keys); a reduce-scatter over
+//            the 8 slice lanes leaves head s (s * NH / 8 .. for NH > 8) with
+//            lane s.
+//   softmax: warp w owns heads w and w + 8 and keeps their running max / sum
+//            in registers.
+//   P.V:     thread (head group, 4 dims) accumulates HPT heads x 4 dims in
+//            registers over every chunk of the split.
 constexpr int CK = 32;
 
-template <int VPL>
-__global__ void attn_decode_partial_kernel(const float* __restrict__ q32, const float* __restrict__ k_cache,
-                                           const float* __restrict__ v_cache, const int32_t* __restrict__ pos_dev,
-                                           int nh, int64_t cache_stride, float* part, int max_chunks) {
-  constexpr int HD = 32 * VPL;
-  extern __shared__ float sm[];
-  float* ks = sm;             // [CK][HD]
-  float* qs = ks + CK * HD;   // [nh][HD]
-  float* ps = qs + nh * HD;   // [nh][CK]
-  sbd::griddep_launch_dependents();
-  const int b = blockIdx.x, c = blockIdx.y;
-  sbd::griddep_wait();
-  const int T = pos_dev[b] + 1;
-  const int t0 = c * CK;
-  if (t0 >= T) return;
-  const int nt = min(CK, T - t0);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  const float* kb = k_cache + static_cast<size_t>(b) * cache_stride + static_cast<size_t>(t0) * HD;
-  const float* vb = v_cache + static_cast<size_t>(b) * cache_stride + static_cast<size_t>(t0) * HD;
-  for (int i = threadIdx.x; i < nt * HD / 4; i += blockDim.x)
-    reinterpret_cast<float4*>(ks)[i] = reinterpret_cast<const float4*>(kb)[i];
-  for (int i = threadIdx.x; i < nh * HD / 4; i += blockDim.x)
-    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(q32 + static_cast<size_t>(b) * nh * HD)[i];
-  __syncthreads();
-  for (int h = warp; h < nh; h += nw) {
-    float q[VPL];
+__device__ __forceinline__ float4 f4_zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+
+// Sum v over the 8 lanes that share lane / 8; afterwards lane (lane & 7) = s
+// holds the totals of entries s * N / 8 .. s * N / 8 + N / 8 - 1 in v[0 .. N/8).
+template <int N>
+__device__ __forceinline__ void reduce_scatter8(float (&v)[N]) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) q[j] = qs[h * HD + lane + 32 * j];
-    float mine = -INFINITY;
-    for (int t = 0; t < nt; ++t) {
-      float d = 0.f;
+  for (int step = 0; step < 3; ++step) {
+    const int dist = 4 >> step;
+    const int cnt = N >> (step + 1);
+    const bool up = (lane & dist) != 0;
 #pragma unroll
-      for (int j = 0; j < VPL; ++j) d += q[j] * ks[t * HD + lane + 32 * j];
-      d = warp_sum(d);
-      if (lane == t) mine = d;
+    for (int i = 0; i < cnt; ++i) {
+      const float send = up ? v[i] : v[i + cnt];
+      const float keep = up ? v[i + cnt] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, dist);
     }
-    const float m = warp_max(mine);
-    const float p = lane < nt ? expf(mine - m) : 0.f;
-    const float l = warp_sum(p);
-    ps[h * CK + lane] = p;
-    if (lane == 0) {
-      float* pm = part + ((static_cast<size_t>(b) * max_chunks + c) * nh + h) * (HD + 2);
-      pm[HD] = m;
-      pm[HD + 1] = l;
-    }
-  }
-  __syncthreads();
-  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-    float acc[16];
-#pragma unroll
-    for (int h = 0; h < 16; ++h) acc[h] = 0.f;
-    for (int t = 0; t < nt; ++t) {
-      const float vv = vb[static_cast<size_t>(t) * HD + d];
-#pragma unroll
-      for (int h = 0; h < 16; ++h)
-        if (h < nh) acc[h] += ps[h * CK + t] * vv;
-    }
-#pragma unroll
-    for (int h = 0; h < 16; ++h)
-      if (h < nh) part[((static_cast<size_t>(b) * max_chunks + c) * nh + h) * (HD + 2) + d] = acc[h];
   }
 }
 
+template <int HD, int NH>
+struct DecodeAttnShape {
+  static constexpr int kThreads = 256;
+  static constexpr int J = HD / 32;                        // float4 of a K row per thread
+  static constexpr int NA = NH < 8 ? 8 : NH;               // score accumulators (padded to the 8 slices)
+  static constexpr int R = NA / 8;                         // heads per slice lane after the reduce-scatter
+  static constexpr int HPT = NH * HD / 4 >= kThreads ? NH * HD / 4 / kThreads : 1;  // heads per P.V thread
+  static constexpr int PVT = (NH / HPT) * (HD / 4);        // P.V threads
+  static constexpr int SP = CK + 4;                        // score row stride (conflict-free, 16-byte rows)
+  static constexpr size_t smem_floats = 2 * CK * HD + NH * HD + NH * SP + 16 + 4;
+  static_assert(NH <= 16 && NH * HD / 4 <= 4 * kThreads && PVT <= kThreads, "shape");
+};
+
+template <int HD, int NH>
+__global__ void __launch_bounds__(256, 2) attn_decode_split_kernel(const float* __restrict__ q32,
+                                                                const float* __restrict__ k_cache,
+                                                                const float* __restrict__ v_cache,
+                                                                const int32_t* __restrict__ pos_dev,
+                                                                int64_t cache_stride, float* part, int spk,
+                                                                int max_splits, int* err) {
+  using Sh = DecodeAttnShape<HD, NH>;
+  constexpr int J = Sh::J, NA = Sh::NA, R = Sh::R, HPT = Sh::HPT, SP = Sh::SP;
+  extern __shared__ __align__(16) float sm[];
+  float* vs = sm;                  // [2][CK][HD] V of the chunk in flight / in use
+  float* qs = vs + 2 * CK * HD;    // [NH][HD]
+  float* ss = qs + NH * HD;        // [NH][SP] scores, then probabilities
+  float* sc = ss + NH * SP;        // [16] this chunk's rescale factor per head
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sc + 16);  // [2] V buffers
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int b = blockIdx.x, sp = blockIdx.y;
+  sbd::griddep_launch_dependents();
+  if (tid == 0) {
+    abort_flag = 0;
+    sbd::mbar_init(&bar[0], 1);
+    sbd::mbar_init(&bar[1], 1);
+    sbd::fence_mbar_init();
+  }
+  sbd::griddep_wait();
+  const int T = pos_dev[b] + 1;
+  const int k0 = sp * spk;
+  if (k0 >= T) return;  // uniform over the CTA
+  const int k1 = min(T, k0 + spk);
+  const int nchunk = (k1 - k0 + CK - 1) / CK;
+  const float* kb = k_cache + static_cast<size_t>(b) * cache_stride;
+  const float* vb = v_cache + static_cast<size_t>(b) * cache_stride;
+  __syncthreads();  // barrier initialisation before any use
+  auto issue_v = [&](int c) {
+    const int t0 = k0 + c * CK, nt = min(CK, k1 - t0);
+    const uint32_t bytes = static_cast<uint32_t>(nt) * HD * sizeof(float);
+    sbd::mbar_arrive_expect_tx(&bar[c & 1], bytes);
+    sbd::bulk_load(vs + (c & 1) * CK * HD, vb + static_cast<size_t>(t0) * HD, bytes, &bar[c & 1]);
+  };
+  if (tid == 0) issue_v(0);
+  // score roles: key t = 4 warp + lane / 8, slice s = lane % 8
+  const int st = warp * 4 + (lane >> 3), ss8 = lane & 7;
+  float4 kr[J];
+  auto load_k = [&](int c) {
+    const int t0 = k0 + c * CK;
+    const bool in = t0 + st < k1;
+    const float4* src = reinterpret_cast<const float4*>(kb + static_cast<size_t>(t0 + (in ? st : 0)) * HD);
+#pragma unroll
+    for (int j = 0; j < J; ++j) kr[j] = in ? src[ss8 + 8 * j] : f4_zero();
+  };
+  load_k(0);
+  for (int i = tid; i < NH * HD / 4; i += Sh::kThreads)
+    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(q32 + static_cast<size_t>(b) * NH * HD)[i];
+  // P.V role: head group hg, dims 4 c4 .. 4 c4 + 3
+  const int c4 = tid % (HD / 4), hg = tid / (HD / 4);
+  const bool pv = tid < Sh::PVT;
+  float4 o[HPT];
+#pragma unroll
+  for (int i = 0; i < HPT; ++i) o[i] = f4_zero();
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  for (int c = 0; c < nchunk; ++c) {
+    const int t0 = k0 + c * CK, nt = min(CK, k1 - t0);
+    __syncthreads();  // q staged; previous P.V done with ss, sc and V buffer (c + 1) & 1
+    if (c + 1 < nchunk && tid == 0) issue_v(c + 1);
+    float acc[NA];
+#pragma unroll
+    for (int h = 0; h < NA; ++h) acc[h] = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        const float4 q = reinterpret_cast<const float4*>(qs + h * HD)[ss8 + 8 * j];
+        acc[h] = fmaf(q.x, kr[j].x, acc[h]);
+        acc[h] = fmaf(q.y, kr[j].y, acc[h]);
+        acc[h] = fmaf(q.z, kr[j].z, acc[h]);
+        acc[h] = fmaf(q.w, kr[j].w, acc[h]);
+      }
+    }
+    reduce_scatter8<NA>(acc);
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const int h = ss8 * R + i;
+      if (h < NH) ss[h * SP + st] = acc[i];
+    }
+    if (c + 1 < nchunk) load_k(c + 1);
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int h = warp + 8 * u;
+      if (h < NH) {
+        const float x = lane < nt ? ss[h * SP + lane] : -INFINITY;
+        const float mn = fmaxf(m_run[u], warp_max(x));
+        const float pr = lane < nt ? expf(x - mn) : 0.f;
+        const float f = expf(m_run[u] - mn);
+        l_run[u] = l_run[u] * f + warp_sum(pr);
+        m_run[u] = mn;
+        ss[h * SP + lane] = pr;
+        if (lane == 0) sc[h] = f;
+      }
+    }
+    const bool bad = !sbd::mbar_wait(&bar[c & 1], (c >> 1) & 1, &abort_flag, err);
+    if (__syncthreads_or(bad)) {
+      // leave no copy in flight into this CTA's shared memory (bounded)
+      if (tid == 0 && c + 1 < nchunk) {
+        const uint64_t t_start = sbd::global_ns();
+        while (!sbd::mbar_try_wait(&bar[(c + 1) & 1], ((c + 1) >> 1) & 1) &&
+               sbd::global_ns() - t_start < sbd::kWaitLimitNs) {
+        }
+      }
+      return;
+    }
+    if (pv) {
+      const float* vbuf = vs + (c & 1) * CK * HD;
+#pragma unroll
+      for (int i = 0; i < HPT; ++i) {
+        const float f = sc[hg * HPT + i];
+        o[i].x *= f;
+        o[i].y *= f;
+        o[i].z *= f;
+        o[i].w *= f;
+      }
+      for (int t = 0; t < nt; t += 4) {
+        float4 v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          v[e] = t + e < nt ? reinterpret_cast<const float4*>(vbuf + (t + e) * HD)[c4] : f4_zero();
+#pragma unroll
+        for (int i = 0; i < HPT; ++i) {
+          const float4 p4 = *reinterpret_cast<const float4*>(ss + (hg * HPT + i) * SP + t);
+          const float pe[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            o[i].x = fmaf(pe[e], v[e].x, o[i].x);
+            o[i].y = fmaf(pe[e], v[e].y, o[i].y);
+            o[i].z = fmaf(pe[e], v[e].z, o[i].z);
+            o[i].w = fmaf(pe[e], v[e].w, o[i].w);
+          }
+        }
+      }
+    }
+  }
+  // rows of HD + 2 floats: (HD) unnormalised output, running max, running sum
+  float* pbase = part + (static_cast<size_t>(b) * max_splits + sp) * NH * (HD + 2);
+  if (pv) {
+#pragma unroll
+    for (int i = 0; i < HPT; ++i) {
+      float2* d = reinterpret_cast<float2*>(pbase + (hg * HPT + i) * (HD + 2) + 4 * c4);
+      d[0] = make_float2(o[i].x, o[i].y);
+      d[1] = make_float2(o[i].z, o[i].w);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int h = warp + 8 * u;
+    if (h < NH && lane == 0) {
+      pbase[h * (HD + 2) + HD] = m_run[u];
+      pbase[h * (HD + 2) + HD + 1] = l_run[u];
+    }
+  }
+}
+
+// Merge: CTA (b, h), thread d rescales the splits of sequence b.
 __global__ void attn_decode_merge_kernel(const float* __restrict__ part, const int32_t* __restrict__ pos_dev, int nh,
-                                         int hd, int max_chunks, float* out, __half* out16) {
+                                         int hd, int spk, int max_splits, float* out, __half* out16) {
   sbd::griddep_launch_dependents();
   const int b = blockIdx.x, h = blockIdx.y;
   sbd::griddep_wait();
-  const int nc = (pos_dev[b] + 1 + CK - 1) / CK;
-  const float* base = part + (static_cast<size_t>(b) * max_chunks * nh + h) * (hd + 2);
+  const int nc = (pos_dev[b] + 1 + spk - 1) / spk;
+  const float* base = part + (static_cast<size_t>(b) * max_splits * nh + h) * (hd + 2);
   const size_t cstride = static_cast<size_t>(nh) * (hd + 2);
   float M = -INFINITY;
   for (int c = 0; c < nc; ++c) M = fmaxf(M, base[c * cstride + hd]);
@@ -637,33 +782,74 @@ extern "C" size_t sb_attn_decode_workspace_size(int m, int n_heads, int head_dim
   return static_cast<size_t>(m) * chunks * n_heads * (head_dim + 2) * sizeof(float);
 }
 
+// Raises the kernel's dynamic shared-memory limit the first time it is
+// launched on a device, then launches it over grid (m, splits).
+template <int HD, int NH>
+static cudaError_t launch_decode_split(int m, int splits, int spk, cudaStream_t st, const float* q32,
+                                       const float* k_cache, const float* v_cache, const int32_t* pos_dev,
+                                       int64_t cache_stride, float* workspace) {
+  using Sh = DecodeAttnShape<HD, NH>;
+  constexpr int smem = static_cast<int>(Sh::smem_floats * sizeof(float));
+  static bool set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_split_kernel<HD, NH>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) set[dev] = true;
+  }
+  return sb::launch_pdl(attn_decode_split_kernel<HD, NH>, dim3(m, splits), dim3(Sh::kThreads), smem, st, q32, k_cache,
+                        v_cache, pos_dev, cache_stride, workspace, spk, splits, sb::device_error_word());
+}
+
+template <int HD>
+static cudaError_t launch_decode_split_hd(int nh, int m, int splits, int spk, cudaStream_t st, const float* q32,
+                                          const float* k_cache, const float* v_cache, const int32_t* pos_dev,
+                                          int64_t cache_stride, float* workspace) {
+  switch (nh) {
+    case 1: return launch_decode_split<HD, 1>(m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
+    case 2: return launch_decode_split<HD, 2>(m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
+    case 4: return launch_decode_split<HD, 4>(m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
+    case 8: return launch_decode_split<HD, 8>(m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
+    default: return launch_decode_split<HD, 16>(m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
+  }
+}
+
 static int attn_decode_impl(const float* q32, const float* k_cache, const float* v_cache, int64_t cache_stride,
                             const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, float* out,
                             __half* out16, float* workspace, size_t workspace_bytes, void* stream) {
   SB_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256, "sb_attn_decode: head_dim %d unsupported", head_dim);
-  SB_CHECK_ARG(n_heads >= 1 && n_heads <= 16 && m >= 0 && max_seq > 0, "sb_attn_decode: bad shape");
+  SB_CHECK_ARG((n_heads == 1 || n_heads == 2 || n_heads == 4 || n_heads == 8 || n_heads == 16) && m >= 0 && max_seq > 0,
+               "sb_attn_decode: n_heads %d not in {1, 2, 4, 8, 16}, or bad shape", n_heads);
   if (m == 0) return SB_OK;
   SB_CHECK_ARG(q32 && k_cache && v_cache && pos_dev && (out || out16) && workspace, "sb_attn_decode: null pointer");
+  SB_CHECK_ARG(cache_stride % 4 == 0 && sb::aligned(q32, 16) && sb::aligned(k_cache, 16) && sb::aligned(v_cache, 16),
+               "sb_attn_decode: q and the caches must be 16-byte aligned with a cache stride a multiple of 4");
   const size_t need = sb_attn_decode_workspace_size(m, n_heads, head_dim, max_seq);
   if (workspace_bytes < need)
     return sb::fail(SB_ERR_WORKSPACE, "sb_attn_decode: workspace %zu < %zu bytes", workspace_bytes, need);
+  // Keys per split: one chunk while the grid is small; with many sequences up
+  // to 8 chunks, so that splits stay >= ~8 CTAs per SM and the partials
+  // (written, then read by the merge) stay a small share of the K/V bytes.
   const int max_chunks = (max_seq + CK - 1) / CK;
+  const long long cta_units = static_cast<long long>(m) * max_chunks;
+  const int nch = static_cast<int>(std::max(1LL, std::min(8LL, cta_units / (8LL * sb::num_sms()))));
+  const int spk = nch * CK;
+  const int splits = (max_seq + spk - 1) / spk;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const size_t smem = (static_cast<size_t>(CK) * head_dim + static_cast<size_t>(n_heads) * (head_dim + CK)) * sizeof(float);
-  const dim3 grid(m, max_chunks);
   cudaError_t e;
-#define SB_ATT(V)                                                                                                  \
-  e = sb::launch_pdl(attn_decode_partial_kernel<V>, grid, dim3(kT), smem, st, q32, k_cache, v_cache, pos_dev, n_heads, \
-                     cache_stride, workspace, max_chunks)
-  if (head_dim == 64) SB_ATT(2);
-  else if (head_dim == 128) SB_ATT(4);
-  else SB_ATT(8);
-#undef SB_ATT
-  if (e != cudaSuccess) return sb::cuda_fail(e, "attn_decode_partial_kernel");
-  int rc = sb::launch_status("attn_decode_partial_kernel");
+  if (head_dim == 64)
+    e = launch_decode_split_hd<64>(n_heads, m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
+  else if (head_dim == 128)
+    e = launch_decode_split_hd<128>(n_heads, m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
+  else
+    e = launch_decode_split_hd<256>(n_heads, m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "attn_decode_split_kernel");
+  int rc = sb::launch_status("attn_decode_split_kernel");
   if (rc) return rc;
   e = sb::launch_pdl(attn_decode_merge_kernel, dim3(m, n_heads), dim3(head_dim), 0, st,
-                     static_cast<const float*>(workspace), pos_dev, n_heads, head_dim, max_chunks, out, out16);
+                     static_cast<const float*>(workspace), pos_dev, n_heads, head_dim, spk, splits, out, out16);
   if (e != cudaSuccess) return sb::cuda_fail(e, "attn_decode_merge_kernel");
   return sb::launch_status("attn_decode_merge_kernel");
 }

@@ -128,3 +128,46 @@ def test_qkv_prep_vs_oracle(cuda, hd, decode):
         assert_f16_within_ulp(q16n[s], q)
         assert rel(kcn[b, p], k) < 1e-5
         assert rel(vcn[b, p], v) < 1e-5
+
+
+def _attn_decode_ref(q, kc, vc, pos):
+    """softmax(q K^T) V over keys 0..pos of each sequence, attention scaling 1.0
+    (the oracle's decode attention, oracle/decoder.py OracleDecoder.layer)."""
+    out = np.empty_like(q)
+    for b in range(q.shape[0]):
+        s = q[b].astype(np.float64) @ kc[b, :pos[b] + 1].astype(np.float64).T
+        s -= s.max(axis=-1, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(axis=-1, keepdims=True)
+        out[b] = (p @ vc[b, :pos[b] + 1].astype(np.float64)).astype(np.float32)
+    return out
+
+
+# (sequences, heads, head_dim, max_seq): the last two make the kernel walk
+# several 32-key chunks per split (keys per split 96 and 256)
+@pytest.mark.parametrize("m,nh,hd,max_seq", [(3, 2, 64, 100), (5, 8, 256, 1100), (4, 16, 128, 70), (2, 1, 64, 40),
+                                             (7, 4, 128, 65), (200, 8, 256, 600), (300, 8, 256, 1100)])
+def test_attn_decode_vs_oracle(cuda, m, nh, hd, max_seq):
+    rng = np.random.default_rng(m * 7 + nh * 3 + hd + max_seq)
+    q = rng.standard_normal((m, nh, hd), dtype=np.float32) * np.float32(0.2)
+    kc = rng.standard_normal((m, max_seq, hd), dtype=np.float32)
+    vc = rng.standard_normal((m, max_seq, hd), dtype=np.float32)
+    edge = [0, 30, 31, 32, 33, max_seq - 1, max_seq // 2]
+    pos = np.array([edge[i] if i < len(edge) else rng.integers(0, max_seq) for i in range(m)], np.int32)
+    pos = np.minimum(pos, max_seq - 1).astype(np.int32)
+    Q, KC, VC, P = T(q, cuda), T(kc, cuda), T(vc, cuda), T(pos, cuda)
+    ws = torch.empty(_lib.load().sb_attn_decode_workspace_size(m, nh, hd, max_seq) // 4 + 1, dtype=torch.float32,
+                     device=cuda)
+    out = torch.empty((m, nh, hd), dtype=torch.float32, device=cuda)
+    out16 = torch.empty((m, nh, hd), dtype=torch.float16, device=cuda)
+    nbytes = ws.numel() * 4
+    _lib.call("sb_attn_decode", Q.data_ptr(), KC.data_ptr(), VC.data_ptr(), max_seq * hd, P.data_ptr(), m, nh, hd,
+              max_seq, out.data_ptr(), ws.data_ptr(), nbytes, kern._stream())
+    _lib.call("sb_attn_decode_f16", Q.data_ptr(), KC.data_ptr(), VC.data_ptr(), max_seq * hd, P.data_ptr(), m, nh, hd,
+              max_seq, out16.data_ptr(), ws.data_ptr(), nbytes, kern._stream())
+    kern.device_status()
+    ref = _attn_decode_ref(q, kc, vc, pos)
+    got = out.cpu().numpy()
+    assert np.abs(got - ref).max() <= 2e-5 * np.abs(ref).max()
+    g16 = out16.cpu().numpy().astype(np.float32)
+    assert np.all(np.abs(g16 - got.astype(np.float16).astype(np.float32)) <= np.abs(got) * 2 ** -10 + 1e-7)

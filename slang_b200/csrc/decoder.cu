@@ -425,28 +425,30 @@ __global__ void geglu_kernel(const void* __restrict__ gu, int gu_f16, int f, int
 // softmax; the merge kernel rescales the splits.  The chunk loop is
 // software-pipelined: V of chunk c + 1 is bulk-copied into the other of two
 // shared-memory buffers and K of chunk c + 1 is loaded into registers while
-// chunk c's softmax and P.V run.
-//   scores:  thread (key t, slice s) holds K[t] dims {4 (s + 8 j) .. + 3} in
-//            registers and forms all NH partial dots against q (float4 reads
-//            of q broadcast across the warp's 4 keys); a reduce-scatter over
-//            the 8 slice lanes leaves head s (s * NH / 8 .. for NH > 8) with
-//            lane s.
+// chunk c's softmax and P.V run.  Shared-memory bandwidth, not arithmetic,
+// bounds the inner loops, so each loop reuses every shared-memory read:
+//   scores:  thread (key pair (p, p + 16), slice s of 16) holds both keys'
+//            dims {4 (s + 16 j) .. + 3} in registers and forms 2 x NH partial
+//            dots (each q float4 read serves two keys); a reduce-scatter over
+//            the 16 slice lanes leaves one (key, head) score per lane.
 //   softmax: warp w owns heads w and w + 8 and keeps their running max / sum
 //            in registers.
-//   P.V:     thread (head group, 4 dims) accumulates HPT heads x 4 dims in
-//            registers over every chunk of the split.
+//   P.V:     thread (key half, head group, 4 dims) accumulates HPT heads x 4
+//            dims over its 16 keys of every chunk (each V float4 read serves
+//            HPT heads); the halves are added once, at the end of the split.
 constexpr int CK = 32;
 
 __device__ __forceinline__ float4 f4_zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
 
-// Sum v over the 8 lanes that share lane / 8; afterwards lane (lane & 7) = s
-// holds the totals of entries s * N / 8 .. s * N / 8 + N / 8 - 1 in v[0 .. N/8).
+// Sum v over the 16 lanes that share lane / 16; afterwards lane s = lane & 15
+// holds the totals of entries s * N / 16 .. s * N / 16 + N / 16 - 1 in
+// v[0 .. N/16).
 template <int N>
-__device__ __forceinline__ void reduce_scatter8(float (&v)[N]) {
+__device__ __forceinline__ void reduce_scatter16(float (&v)[N]) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int step = 0; step < 3; ++step) {
-    const int dist = 4 >> step;
+  for (int step = 0; step < 4; ++step) {
+    const int dist = 8 >> step;
     const int cnt = N >> (step + 1);
     const bool up = (lane & dist) != 0;
 #pragma unroll
@@ -461,14 +463,14 @@ __device__ __forceinline__ void reduce_scatter8(float (&v)[N]) {
 template <int HD, int NH>
 struct DecodeAttnShape {
   static constexpr int kThreads = 256;
-  static constexpr int J = HD / 32;                        // float4 of a K row per thread
-  static constexpr int NA = NH < 8 ? 8 : NH;               // score accumulators (padded to the 8 slices)
-  static constexpr int R = NA / 8;                         // heads per slice lane after the reduce-scatter
-  static constexpr int HPT = NH * HD / 4 >= kThreads ? NH * HD / 4 / kThreads : 1;  // heads per P.V thread
-  static constexpr int PVT = (NH / HPT) * (HD / 4);        // P.V threads
+  static constexpr int J = HD / 64;                        // float4 of a K row per thread
+  static constexpr int NA = NH < 8 ? 8 : NH;               // scores per key (padded: 2 NA >= 16 lanes)
+  static constexpr int R = 2 * NA / 16;                    // (key, head) scores per lane after the reduce-scatter
+  static constexpr int HPT = NH * HD / 4 >= 128 ? NH * HD / 4 / 128 : 1;  // heads per P.V thread
+  static constexpr int PVT = (NH / HPT) * (HD / 4);        // P.V threads per key half
   static constexpr int SP = CK + 4;                        // score row stride (conflict-free, 16-byte rows)
   static constexpr size_t smem_floats = 2 * CK * HD + NH * HD + NH * SP + 16 + 4;
-  static_assert(NH <= 16 && NH * HD / 4 <= 4 * kThreads && PVT <= kThreads, "shape");
+  static_assert(NH <= 16 && PVT <= 128 && NH * HD <= 2 * CK * HD, "shape");
 };
 
 template <int HD, int NH>
@@ -512,22 +514,26 @@ __global__ void __launch_bounds__(256, 2) attn_decode_split_kernel(const float* 
     sbd::bulk_load(vs + (c & 1) * CK * HD, vb + static_cast<size_t>(t0) * HD, bytes, &bar[c & 1]);
   };
   if (tid == 0) issue_v(0);
-  // score roles: key t = 4 warp + lane / 8, slice s = lane % 8
-  const int st = warp * 4 + (lane >> 3), ss8 = lane & 7;
-  float4 kr[J];
+  // score roles: keys kp and kp + 16, slice s16 of 16
+  const int kp = warp * 2 + (lane >> 4), s16 = lane & 15;
+  float4 kr[2][J];
   auto load_k = [&](int c) {
     const int t0 = k0 + c * CK;
-    const bool in = t0 + st < k1;
-    const float4* src = reinterpret_cast<const float4*>(kb + static_cast<size_t>(t0 + (in ? st : 0)) * HD);
 #pragma unroll
-    for (int j = 0; j < J; ++j) kr[j] = in ? src[ss8 + 8 * j] : f4_zero();
+    for (int u = 0; u < 2; ++u) {
+      const int t = kp + 16 * u;
+      const bool in = t0 + t < k1;
+      const float4* src = reinterpret_cast<const float4*>(kb + static_cast<size_t>(t0 + (in ? t : 0)) * HD);
+#pragma unroll
+      for (int j = 0; j < J; ++j) kr[u][j] = in ? src[s16 + 16 * j] : f4_zero();
+    }
   };
   load_k(0);
   for (int i = tid; i < NH * HD / 4; i += Sh::kThreads)
     reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(q32 + static_cast<size_t>(b) * NH * HD)[i];
-  // P.V role: head group hg, dims 4 c4 .. 4 c4 + 3
-  const int c4 = tid % (HD / 4), hg = tid / (HD / 4);
-  const bool pv = tid < Sh::PVT;
+  // P.V role: key half kh (keys 16 kh .. + 15 of each chunk), head group hg, dims 4 c4 .. + 3
+  const int kh = tid >> 7, c4 = (tid & 127) % (HD / 4), hg = (tid & 127) / (HD / 4);
+  const bool pv = (tid & 127) < Sh::PVT;
   float4 o[HPT];
 #pragma unroll
   for (int i = 0; i < HPT; ++i) o[i] = f4_zero();
@@ -536,25 +542,30 @@ __global__ void __launch_bounds__(256, 2) attn_decode_split_kernel(const float* 
     const int t0 = k0 + c * CK, nt = min(CK, k1 - t0);
     __syncthreads();  // q staged; previous P.V done with ss, sc and V buffer (c + 1) & 1
     if (c + 1 < nchunk && tid == 0) issue_v(c + 1);
-    float acc[NA];
+    float acc[2 * NA];
 #pragma unroll
-    for (int h = 0; h < NA; ++h) acc[h] = 0.f;
+    for (int e = 0; e < 2 * NA; ++e) acc[e] = 0.f;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
 #pragma unroll
       for (int h = 0; h < NH; ++h) {
-        const float4 q = reinterpret_cast<const float4*>(qs + h * HD)[ss8 + 8 * j];
-        acc[h] = fmaf(q.x, kr[j].x, acc[h]);
-        acc[h] = fmaf(q.y, kr[j].y, acc[h]);
-        acc[h] = fmaf(q.z, kr[j].z, acc[h]);
-        acc[h] = fmaf(q.w, kr[j].w, acc[h]);
+        const float4 q = reinterpret_cast<const float4*>(qs + h * HD)[s16 + 16 * j];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          float a = acc[u * NA + h];
+          a = fmaf(q.x, kr[u][j].x, a);
+          a = fmaf(q.y, kr[u][j].y, a);
+          a = fmaf(q.z, kr[u][j].z, a);
+          a = fmaf(q.w, kr[u][j].w, a);
+          acc[u * NA + h] = a;
+        }
       }
     }
-    reduce_scatter8<NA>(acc);
+    reduce_scatter16<2 * NA>(acc);
 #pragma unroll
-    for (int i = 0; i < R; ++i) {
-      const int h = ss8 * R + i;
-      if (h < NH) ss[h * SP + st] = acc[i];
+    for (int r = 0; r < R; ++r) {
+      const int e = s16 * R + r, u = e / NA, h = e % NA;
+      if (h < NH) ss[h * SP + kp + 16 * u] = acc[r];
     }
     if (c + 1 < nchunk) load_k(c + 1);
     __syncthreads();
@@ -593,7 +604,8 @@ __global__ void __launch_bounds__(256, 2) attn_decode_split_kernel(const float* 
         o[i].z *= f;
         o[i].w *= f;
       }
-      for (int t = 0; t < nt; t += 4) {
+      const int te = min(nt, 16 * kh + 16);
+      for (int t = 16 * kh; t < te; t += 4) {
         float4 v[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e)
@@ -613,14 +625,23 @@ __global__ void __launch_bounds__(256, 2) attn_decode_split_kernel(const float* 
       }
     }
   }
-  // rows of HD + 2 floats: (HD) unnormalised output, running max, running sum
+  // add the key halves (through the idle V buffers), then write rows of
+  // HD + 2 floats: (HD) unnormalised output, running max, running sum
+  __syncthreads();
+  float4* ox = reinterpret_cast<float4*>(vs);
+  if (pv && kh == 1) {
+#pragma unroll
+    for (int i = 0; i < HPT; ++i) ox[(hg * HPT + i) * (HD / 4) + c4] = o[i];
+  }
+  __syncthreads();
   float* pbase = part + (static_cast<size_t>(b) * max_splits + sp) * NH * (HD + 2);
-  if (pv) {
+  if (pv && kh == 0) {
 #pragma unroll
     for (int i = 0; i < HPT; ++i) {
+      const float4 y = ox[(hg * HPT + i) * (HD / 4) + c4];
       float2* d = reinterpret_cast<float2*>(pbase + (hg * HPT + i) * (HD + 2) + 4 * c4);
-      d[0] = make_float2(o[i].x, o[i].y);
-      d[1] = make_float2(o[i].z, o[i].w);
+      d[0] = make_float2(o[i].x + y.x, o[i].y + y.y);
+      d[1] = make_float2(o[i].z + y.z, o[i].w + y.w);
     }
   }
 #pragma unroll

@@ -5,10 +5,14 @@
 // contiguous span of the packed matrix (and of its scales), moved by a single
 // cp.async.bulk (TMA bulk copy) into a 4-deep shared-memory ring whose slots
 // complete on mbarriers.  Lane 0 of warp 0 issues the first four stages at
-// entry and refills a slot right after the per-stage CTA barrier that already
-// proves every warp is done with it, so there is no producer warp and no
-// "empty" barrier.  CTAs (8 warps) take stages round robin, two per SM, so up
-// to 8 x 24 KB per SM is in flight.  Kernels are launched with programmatic
+// entry.  When a half-warp covers whole rows (K <= 16 lanes x GPL groups,
+// gemv_q4_stream_kernel: every matrix with K <= 2048) each warp releases a
+// slot when it is done with it and the last warp to release it refills it,
+// with no CTA-wide barrier per stage; otherwise (gemv_q4_kernel) K slices are
+// reduced through shared memory and the slot is refilled right after the
+// per-stage CTA barrier that already proves every warp is done with it.
+// Neither form has a producer warp.  CTAs (8 warps) take stages round robin,
+// two per SM, so up to 8 x 24 KB per SM is in flight.  Kernels are launched with programmatic
 // dependent launch: weights (which no earlier kernel writes) start streaming
 // at once, and the warps wait for the previous kernel (griddepcontrol.wait)
 // only before they read x.
@@ -66,10 +70,77 @@ struct GemvSmem {
   float red[2][kRedMax];
   unsigned long long best[8][4];
   uint64_t full[kRing];
+  int released[kRing];  // stream kernel: warps done with the slot's current stage
+  int issued;           // stream kernel: stages issued so far
   int abort;
 };
 
 using sbd::make_key;
+
+// This lane's groups of x (rows m < M of the batch, groups gidx[u]) quantised
+// to 16-bit integers, kept in registers for the whole launch.
+template <int M, int GPL>
+__device__ __forceinline__ void load_x_groups(const GemvParams& p, const int (&gidx)[GPL], const bool (&gval)[GPL],
+                                              sbd::XGroup (&xg)[M][GPL]) {
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+#pragma unroll
+    for (int u = 0; u < GPL; ++u) {
+      float v[32];
+      const bool ok = gval[u] && m < p.m;
+      if (p.x_f32) {
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) +
+                                                            static_cast<size_t>(m) * p.k + gidx[u] * 32);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 f = ok ? __ldg(src + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+          v[4 * j] = f.x;
+          v[4 * j + 1] = f.y;
+          v[4 * j + 2] = f.z;
+          v[4 * j + 3] = f.w;
+        }
+      } else {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x) +
+                                                          static_cast<size_t>(m) * p.k + gidx[u] * 32);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 h = ok ? __ldg(src + j) : make_uint4(0, 0, 0, 0);
+          const uint32_t hv[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hv[e]));
+            v[8 * j + 2 * e] = f.x;
+            v[8 * j + 2 * e + 1] = f.y;
+          }
+        }
+      }
+      sbd::quantise_group(v, xg[m][u]);
+    }
+  }
+}
+
+// Combine the per-warp argmax keys (sm.best[warp][m], warps 0..7) and publish
+// one key per batch row: atomic MAX into p.keys, or into every rank's mailbox.
+// Called by the 256 consumer threads after a barrier over them.
+template <int M>
+__device__ __forceinline__ void publish_keys(const GemvParams& p, GemvSmem& sm, int tid) {
+  if (tid < M && tid < p.m) {
+    unsigned long long key = 0;
+    for (int wi = 0; wi < kConsumers / 32; ++wi) key = sm.best[wi][tid] > key ? sm.best[wi][tid] : key;
+    if (key) {
+      if (p.peer_mailboxes) {
+        const uint32_t q = *p.peer_epoch & 1u;
+        for (int pe = 0; pe < p.world; ++pe)
+          atomicMax_system(reinterpret_cast<unsigned long long*>(p.peer_mailboxes[pe] + sbd::kMailKeys) +
+                               q * sbd::kMailMaxRows + p.peer_row0 + tid,
+                           key);
+        __threadfence_system();  // performed at every peer before this CTA exits
+      } else {
+        atomicMax(p.keys + tid, key);
+      }
+    }
+  }
+}
 
 template <int M, int GPL, bool SF16, int EPI>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const GemvParams p) {
@@ -131,41 +202,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
   sbd::griddep_wait();
   // this lane's groups of x, quantised once (kept in registers)
   sbd::XGroup xg[M][GPL];
-#pragma unroll
-  for (int m = 0; m < M; ++m) {
-#pragma unroll
-    for (int u = 0; u < GPL; ++u) {
-      float v[32];
-      const bool ok = gval[u] && m < p.m;
-      if (p.x_f32) {
-        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) +
-                                                            static_cast<size_t>(m) * p.k + gidx[u] * 32);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 f = ok ? __ldg(src + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-          v[4 * j] = f.x;
-          v[4 * j + 1] = f.y;
-          v[4 * j + 2] = f.z;
-          v[4 * j + 3] = f.w;
-        }
-      } else {
-        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x) +
-                                                          static_cast<size_t>(m) * p.k + gidx[u] * 32);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint4 h = ok ? __ldg(src + j) : make_uint4(0, 0, 0, 0);
-          const uint32_t hv[4] = {h.x, h.y, h.z, h.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hv[e]));
-            v[8 * j + 2 * e] = f.x;
-            v[8 * j + 2 * e + 1] = f.y;
-          }
-        }
-      }
-      sbd::quantise_group(v, xg[m][u]);
-    }
-  }
+  load_x_groups<M, GPL>(p, gidx, gval, xg);
 
   float best_v[M];
   long long best_i[M];
@@ -269,21 +306,175 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
       if (lane == 0) sm.best[warp][m] = key;
     }
     __syncthreads();
-    if (tid < M && tid < p.m) {
-      unsigned long long key = 0;
-      for (int wi = 0; wi < kConsumers / 32; ++wi) key = sm.best[wi][tid] > key ? sm.best[wi][tid] : key;
-      if (key) {
-        if (p.peer_mailboxes) {
-          const uint32_t q = *p.peer_epoch & 1u;
-          for (int pe = 0; pe < p.world; ++pe)
-            atomicMax_system(reinterpret_cast<unsigned long long*>(p.peer_mailboxes[pe] + sbd::kMailKeys) +
-                                 q * sbd::kMailMaxRows + p.peer_row0 + tid,
-                             key);
-          __threadfence_system();  // performed at every peer before this CTA exits
-        } else {
-          atomicMax(p.keys + tid, key);
+    publish_keys<M>(p, sm, tid);
+  }
+}
+
+// The GEMV for rows a half-warp covers whole (ks = 1: K <= 16 * GPL * 32),
+// with no CTA-wide barrier per stage: the lane holding a row's sum writes it
+// (or folds it into the running argmax) at once, each warp releases a ring
+// slot when it is done with it, and the warp that releases it last refills
+// it.  Warps drift freely and the copy engine never waits for the slowest
+// warp of a stage.
+template <int M, int GPL, bool SF16, int EPI>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(const GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  GemvSmem& sm = *reinterpret_cast<GemvSmem*>(smem_raw);
+  volatile int* abort = &sm.abort;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row_bytes = p.k >> 1;
+  const int gps = p.k / p.group;
+  const int esz = SF16 ? 2 : 4;
+
+  sbd::griddep_launch_dependents();
+  const int my_stages = p.n_stages > static_cast<int>(blockIdx.x)
+                            ? (p.n_stages - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1
+                            : 0;
+  const uint64_t pol = sbd::l2_policy_evict_first();  // weights are read once per step
+  auto issue = [&](int i) {
+    const int slot = i % kRing;
+    const int st = blockIdx.x + i * gridDim.x;
+    const int r0 = st * p.rs;
+    const int nr = min(p.rs, p.n - r0);
+    const uint32_t wb = static_cast<uint32_t>(nr) * row_bytes;
+    const uint32_t sbytes = p.scale_bulk ? static_cast<uint32_t>(nr) * gps * esz : 0u;
+    sbd::mbar_arrive_expect_tx(&sm.full[slot], wb + sbytes);
+    sbd::bulk_load_hint(sm.w[slot], p.w + static_cast<size_t>(r0) * row_bytes, wb, &sm.full[slot], pol);
+    if (sbytes)
+      sbd::bulk_load_hint(sm.s[slot], static_cast<const uint8_t*>(p.scales) + static_cast<size_t>(r0) * gps * esz,
+                          sbytes, &sm.full[slot], pol);
+  };
+  if (tid == 0) {
+    for (int i = 0; i < kRing; ++i) {
+      sbd::mbar_init(&sm.full[i], 1);
+      sm.released[i] = 0;
+    }
+    sm.abort = 0;
+    sbd::fence_mbar_init();
+    sbd::fence_proxy_async_smem();
+    // weights do not depend on the previous kernel: start streaming now
+    for (int i = 0; i < kRing && i < my_stages; ++i) issue(i);
+    sm.issued = min(kRing, my_stages);
+  }
+  __syncthreads();
+
+  // -------------------------------------------------------------- consumers
+  const int hw = tid >> 4, l16 = tid & 15;
+  int gidx[GPL], gsi[GPL];
+  bool gval[GPL];
+  const int G = p.k >> 5;
+#pragma unroll
+  for (int u = 0; u < GPL; ++u) {
+    gidx[u] = l16 + 16 * u;
+    gval[u] = gidx[u] < G;
+    gsi[u] = (gidx[u] * 32) / p.group;  // scale index of this group within a row
+  }
+  // x is the previous kernel's output: wait for it (weights are already streaming)
+  sbd::griddep_wait();
+  sbd::XGroup xg[M][GPL];
+  load_x_groups<M, GPL>(p, gidx, gval, xg);
+
+  float best_v[M];
+  long long best_i[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    best_v[m] = -INFINITY;
+    best_i[m] = 0x7FFFFFFF;
+  }
+  for (int i = 0; i < my_stages; ++i) {
+    const int slot = i % kRing;
+    if (!__all_sync(0xFFFFFFFFu, sbd::mbar_wait(&sm.full[slot], (i / kRing) & 1, abort, p.err))) break;
+    const int st = blockIdx.x + i * gridDim.x;
+    const int r0 = st * p.rs;
+    const int nr = min(p.rs, p.n - r0);
+    const uint8_t* wst = sm.w[slot];
+    const uint8_t* sst = sm.s[slot];
+    for (int rr = hw; rr < p.rs; rr += 16) {  // the same trip count for both half-warps of a warp
+      float acc[M];
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[m] = 0.f;
+      if (rr < nr) {
+#pragma unroll
+        for (int u = 0; u < GPL; ++u) {
+          if (!gval[u]) continue;
+          const uint4 q = *reinterpret_cast<const uint4*>(wst + rr * row_bytes + gidx[u] * 16);
+          const int gi = gsi[u];
+          float sw;
+          if (p.scale_bulk) {
+            sw = SF16 ? __half2float(reinterpret_cast<const __half*>(sst)[rr * gps + gi])
+                      : reinterpret_cast<const float*>(sst)[rr * gps + gi];
+          } else {
+            const size_t si = static_cast<size_t>(r0 + rr) * gps + gi;
+            sw = SF16 ? __half2float(static_cast<const __half*>(p.scales)[si]) : static_cast<const float*>(p.scales)[si];
+          }
+#pragma unroll
+          for (int m = 0; m < M; ++m)
+            acc[m] = fmaf(static_cast<float>(sbd::dot_group(q, xg[m][u])), sw * xg[m][u].sx, acc[m]);
         }
       }
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) acc[m] += __shfl_xor_sync(0xFFFFFFFFu, acc[m], off, 16);
+      }
+      if (l16 == 0 && rr < nr) {
+        const int row = r0 + rr;
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          if (m >= p.m) continue;
+          float v = acc[m];
+          if (EPI == EPI_STORE) {
+            p.y[static_cast<size_t>(m) * p.ldy + row] = v;
+          } else {
+            if (p.logits) p.logits[static_cast<size_t>(m) * p.n + row] = v;
+            if (v != v) v = -INFINITY;
+            const long long gi = p.row_offset + row;
+            if (v > best_v[m] || (v == best_v[m] && gi < best_i[m])) {
+              best_v[m] = v;
+              best_i[m] = gi;
+            }
+          }
+        }
+      }
+    }
+    // this warp is done with the slot; the last of the 8 warps refills it
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();  // this warp's reads of the slot are done before the release
+      if (atomicAdd(&sm.released[slot], 1) == kConsumers / 32 - 1) {
+        __threadfence_block();
+        sm.released[slot] = 0;
+        if (i + kRing < my_stages) {
+          sbd::fence_proxy_async_smem();
+          issue(i + kRing);
+          sm.issued = i + kRing + 1;
+        }
+      }
+    }
+  }
+
+  if (EPI == EPI_ARGMAX) {
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      unsigned long long key = best_i[m] == 0x7FFFFFFF ? 0ull : make_key(best_v[m], best_i[m]);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(0xFFFFFFFFu, key, off);
+        key = o > key ? o : key;
+      }
+      if (lane == 0) sm.best[warp][m] = key;
+    }
+    __syncthreads();
+    publish_keys<M>(p, sm, tid);
+  }
+  if (__syncthreads_or(*abort)) {
+    // a copy never landed: let the latest one of each slot finish before the CTA exits (bounded)
+    if (tid == 0) {
+      const uint64_t t0 = sbd::global_ns();
+      for (int j = max(0, sm.issued - kRing); j < sm.issued; ++j)
+        while (!sbd::mbar_try_wait(&sm.full[j % kRing], (j / kRing) & 1) &&
+               sbd::global_ns() - t0 < sbd::kWaitLimitNs) {
+        }
     }
   }
 }
@@ -347,11 +538,29 @@ int launch_t(const GemvParams& p, bool sf16, int sms, cudaStream_t s) {
       e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, true, EPI>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, false, EPI>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, true, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, false, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, true, EPI>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               100);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, false, EPI>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               100);
     if (e != cudaSuccess) return sb::cuda_fail(e, "gemv_q4_kernel: smem attribute");
     done[dev] = true;
   }
-  cudaError_t e = sf16 ? sb::launch_pdl(gemv_q4_kernel<M, GPL, true, EPI>, dim3(grid), dim3(kThreads), smem, s, p)
-                       : sb::launch_pdl(gemv_q4_kernel<M, GPL, false, EPI>, dim3(grid), dim3(kThreads), smem, s, p);
+  cudaError_t e;
+  if (p.ks == 1) {
+    e = sf16 ? sb::launch_pdl(gemv_q4_stream_kernel<M, GPL, true, EPI>, dim3(grid), dim3(kThreads), smem, s, p)
+             : sb::launch_pdl(gemv_q4_stream_kernel<M, GPL, false, EPI>, dim3(grid), dim3(kThreads), smem, s, p);
+  } else {
+    e = sf16 ? sb::launch_pdl(gemv_q4_kernel<M, GPL, true, EPI>, dim3(grid), dim3(kThreads), smem, s, p)
+             : sb::launch_pdl(gemv_q4_kernel<M, GPL, false, EPI>, dim3(grid), dim3(kThreads), smem, s, p);
+  }
   if (e != cudaSuccess) return sb::cuda_fail(e, "gemv_q4_kernel launch");
   return sb::launch_status("gemv_q4_kernel");
 }

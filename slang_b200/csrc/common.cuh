@@ -20,6 +20,7 @@ int cuda_fail(cudaError_t e, const char* what);  // SB_ERR_CUDA with the CUDA me
 int launch_status(const char* what);             // checks cudaGetLastError after a launch
 int num_sms();                                   // SM count of the current device
 int* device_error_word();                        // device address of the error word
+int zero_keys(unsigned long long* keys, int m, cudaStream_t s);  // clears argmax keys (a PDL kernel, csrc/gemv.cu)
 
 // Launch `kernel` with programmatic stream serialization, so it may start
 // while the previous kernel in the stream is still running (the kernel

@@ -1129,8 +1129,8 @@ static int gemm_q4_impl(const void* a, const void* w, const void* scales, int sc
   if (keys) {
     if (QW * q4_scale_groups(k / BK, group) * esz > Q_SCALE_BYTES)
       return sb::fail(SB_ERR_ARG, "sb_gemm_q4_argmax: k=%d has too many scale groups for one split", k);
-    cudaError_t e = cudaMemsetAsync(keys, 0, sizeof(uint64_t) * m, s);
-    if (e != cudaSuccess) return sb::cuda_fail(e, "sb_gemm_q4_argmax: clearing keys");
+    rc = sb::zero_keys(reinterpret_cast<unsigned long long*>(keys), m, s);
+    if (rc != SB_OK) return rc;
   }
   static bool done[64] = {false};
   static bool done_pair[64] = {false};

@@ -480,8 +480,21 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
 }
 
 __global__ void keys_to_tokens_kernel(const unsigned long long* keys, int32_t* tokens, int m) {
+  sbd::griddep_launch_dependents();
+  sbd::griddep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < m) tokens[i] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(keys[i] & 0xFFFFFFFFull));
+}
+
+// Clears the argmax keys.  A kernel rather than a memset so that the GEMV
+// launched after it (programmatic dependent launch) starts streaming weights
+// at once; the GEMV's atomics come after its griddepcontrol.wait, i.e. after
+// this kernel, and this kernel's stores after the previous reader of the keys.
+__global__ void zero_keys_kernel(unsigned long long* keys, int m) {
+  sbd::griddep_launch_dependents();
+  sbd::griddep_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < m) keys[i] = 0ull;
 }
 
 struct Plan {
@@ -647,6 +660,15 @@ int check_common(const char* fn, const void* w, const void* scales, int scale_dt
 
 }  // namespace
 
+namespace sb {
+int zero_keys(unsigned long long* keys, int m, cudaStream_t s) {
+  if (m <= 0) return SB_OK;
+  const cudaError_t e = sb::launch_pdl(zero_keys_kernel, dim3((m + 255) / 256), dim3(256), 0, s, keys, m);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "zero_keys_kernel");
+  return sb::launch_status("zero_keys_kernel");
+}
+}  // namespace sb
+
 extern "C" int sb_gemv_q4(const void* w, const void* scales, int scale_dtype, int group, const void* x,
                           int x_dtype, float* y, int ldy, int m, int n, int k, void* stream) {
   int rc = check_common("sb_gemv_q4", w, scales, scale_dtype, group, x, x_dtype, m, n, k);
@@ -675,8 +697,9 @@ extern "C" int sb_lmhead_argmax(const void* emb, const void* scales, int scale_d
   SB_CHECK_ARG(keys != nullptr, "sb_lmhead_argmax: null keys");
   SB_CHECK_ARG(row_offset >= 0 && row_offset + v <= 0xFFFFFFFFLL, "sb_lmhead_argmax: row indices must fit in 32 bits");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(keys, 0, sizeof(uint64_t) * m, s);
-  if (e != cudaSuccess) return sb::cuda_fail(e, "sb_lmhead_argmax: clearing keys");
+  rc = sb::zero_keys(reinterpret_cast<unsigned long long*>(keys), m, s);
+  if (rc != SB_OK) return rc;
+  cudaError_t e;
   if (v > 0) {
     GemvParams p{};
     p.w = static_cast<const uint8_t*>(emb);
@@ -693,7 +716,9 @@ extern "C" int sb_lmhead_argmax(const void* emb, const void* scales, int scale_d
     if (rc != SB_OK) return rc;
   }
   if (tokens) {
-    keys_to_tokens_kernel<<<1, 32, 0, s>>>(reinterpret_cast<const unsigned long long*>(keys), tokens, m);
+    e = sb::launch_pdl(keys_to_tokens_kernel, dim3((m + 255) / 256), dim3(256), 0, s,
+                       reinterpret_cast<const unsigned long long*>(keys), tokens, m);
+    if (e != cudaSuccess) return sb::cuda_fail(e, "keys_to_tokens_kernel");
     return sb::launch_status("keys_to_tokens_kernel");
   }
   return SB_OK;

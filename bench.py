@@ -52,8 +52,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", default="",
-                    choices=["", "gemm_q4", "gemm_q4_geglu", "gemm_f16", "gemv", "lmhead", "attn", "prefill", "decode",
-                             "decode_fused", "decode_batch"],
+                    choices=["", "gemm_q4", "gemm_q4_geglu", "gemm_f16", "gemv", "lmhead", "attn", "attn_decode", "prefill",
+                             "decode", "decode_fused", "decode_batch"],
                     help="run one kernel --iters times on a single shape and exit (for ncu captures)")
     ap.add_argument("--shape", default="6144,1536", help="N,K of the weight for --kernel")
     ap.add_argument("--m", type=int, default=1024, help="rows of the activation for --kernel")
@@ -115,7 +115,19 @@ def run_kernel_case(args):
     g.manual_seed(0)
     w = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g)
     s = (torch.randn((n, k // 32), device=dev, generator=g) * 0.02).abs().half()
-    if args.kernel == "attn":
+    if args.kernel == "attn_decode":
+        # batched decode attention: --batch sequences at context --m, 8 query heads, head_dim from --shape's K
+        hd, B, ctx = k, args.batch, args.m
+        max_seq = ctx + 61
+        q = torch.randn((B, 8, hd), device=dev, generator=g) * 0.2
+        kc = torch.randn((B, max_seq, hd), device=dev, generator=g)
+        vc = torch.randn((B, max_seq, hd), device=dev, generator=g)
+        pos = torch.full((B,), ctx - 1, dtype=torch.int32, device=dev)
+        out16 = torch.empty((B, 8, hd), dtype=torch.float16, device=dev)
+
+        def op():
+            kern.attn_decode(q, kc, vc, pos, out=out16, f16=True)
+    elif args.kernel == "attn":
         # fused causal prefill attention: --m tokens, 8 query heads, head_dim from --shape's K
         hd = k
         q = torch.randn((m, 8, hd), device=dev, generator=g).half()
@@ -162,7 +174,9 @@ def run_kernel_case(args):
     e1.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / args.iters
     kern.device_status()
-    if args.kernel == "attn":
+    if args.kernel == "attn_decode":
+        rate = f"{2 * args.batch * m * k * 4 / us / 1e3:.1f} GB/s of K/V"
+    elif args.kernel == "attn":
         rate = f"{2 * 2 * 8 * m * m / 2 * k / us / 1e6:.1f} TFLOP/s (causal: half of S x S)"
     elif args.kernel in ("gemm_q4", "gemm_q4_geglu", "gemm_f16"):
         rate = f"{2 * m * n * k / us / 1e6:.1f} TFLOP/s"

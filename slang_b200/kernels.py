@@ -155,6 +155,34 @@ def attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.T
     return out
 
 
+def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos: torch.Tensor,
+                out: torch.Tensor | None = None, f16: bool = False,
+                workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention (the reference's ``attn_101``, gemma4_150/kernels_dsl.py) for a
+    batch of sequences: q [m, nh, hd] f32, caches [m, max_seq, hd] f32 (one KV head),
+    pos [m] int32 = each sequence's last cached position; returns softmax(q k^T) v over
+    keys 0..pos as [m, nh, hd] f32 (f16 with ``f16``)."""
+    _need(q, "q", (torch.float32,))
+    _need(k_cache, "k_cache", (torch.float32,))
+    _need(v_cache, "v_cache", (torch.float32,))
+    _need(pos, "pos", (torch.int32,))
+    m, nh, hd = q.shape
+    max_seq = k_cache.shape[1]
+    if k_cache.shape != (m, max_seq, hd) or v_cache.shape != k_cache.shape or pos.numel() != m:
+        raise ValueError("caches must be [m, max_seq, head_dim] and pos [m]")
+    if out is None:
+        out = torch.empty((m, nh, hd), dtype=torch.float16 if f16 else torch.float32, device=q.device)
+    _need(out, "out", (torch.float16,) if f16 else (torch.float32,))
+    need = int(_lib.load().sb_attn_decode_workspace_size(m, nh, hd, max_seq))
+    if workspace is None:
+        workspace = _workspace(q.device, need)
+    nbytes = workspace.numel() * workspace.element_size()
+    _lib.call("sb_attn_decode_f16" if f16 else "sb_attn_decode", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+              max_seq * hd, pos.data_ptr(), m, nh, hd, max_seq, out.data_ptr(), workspace.data_ptr(), nbytes,
+              _stream())
+    return out
+
+
 def gemm_q4(A: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, C: torch.Tensor | None = None,
             alpha: float = 1.0, workspace: torch.Tensor | None = None, geglu: bool = False) -> torch.Tensor:
     """Fused ``_dq`` + ``_gemm``: ``C = f16(alpha * A @ dq_f16(W)^T)``.

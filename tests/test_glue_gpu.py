@@ -171,3 +171,21 @@ def test_attn_decode_vs_oracle(cuda, m, nh, hd, max_seq):
     assert np.abs(got - ref).max() <= 2e-5 * np.abs(ref).max()
     g16 = out16.cpu().numpy().astype(np.float32)
     assert np.all(np.abs(g16 - got.astype(np.float16).astype(np.float32)) <= np.abs(got) * 2 ** -10 + 1e-7)
+
+
+def test_attn_decode_wrapper(cuda):
+    """kernels.attn_decode (the torch-facing call) on the Gemma-4-E2B head shape."""
+    rng = np.random.default_rng(5)
+    m, nh, hd, max_seq = 3, 8, 256, 300
+    q = rng.standard_normal((m, nh, hd), dtype=np.float32) * np.float32(0.2)
+    kc = rng.standard_normal((m, max_seq, hd), dtype=np.float32)
+    vc = rng.standard_normal((m, max_seq, hd), dtype=np.float32)
+    pos = np.array([0, 150, 299], np.int32)
+    Q, KC, VC, P = T(q, cuda), T(kc, cuda), T(vc, cuda), T(pos, cuda)
+    got = kern.attn_decode(Q, KC, VC, P).cpu().numpy()
+    got16 = kern.attn_decode(Q, KC, VC, P, f16=True)
+    kern.device_status()
+    ref = _attn_decode_ref(q, kc, vc, pos)
+    assert np.abs(got - ref).max() <= 2e-5 * np.abs(ref).max()
+    assert got16.dtype == torch.float16
+    assert np.abs(got16.cpu().numpy().astype(np.float32) - ref).max() <= 2e-3 * np.abs(ref).max()

@@ -914,6 +914,57 @@ __global__ void splitk_finalize_kernel(const float* __restrict__ ws, __half* __r
   }
 }
 
+// splitk_finalize_kernel four partial columns at a time (n % 4 == 0): float4
+// loads of every split issued before the sums, which run in split order as
+// in the scalar kernel (bit-identical results).
+__global__ void splitk_finalize_v4_kernel(const float* __restrict__ ws, __half* __restrict__ c, int m, int n, int ldc,
+                                          int splits, float alpha, int geglu) {
+  sbd::griddep_launch_dependents();
+  sbd::griddep_wait();  // the partial planes are the previous kernel's output
+  const size_t plane4 = static_cast<size_t>(m) * n / 4;
+  const int n4 = n / 4;
+  const float4* w4 = reinterpret_cast<const float4*>(ws);
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < plane4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t row = i / n4, c4 = i - row * n4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    int z = 0;
+    for (; z + 4 <= splits; z += 4) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = w4[(z + u) * plane4 + i];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        acc.x += v[u].x;
+        acc.y += v[u].y;
+        acc.z += v[u].z;
+        acc.w += v[u].w;
+      }
+    }
+    for (; z < splits; ++z) {
+      const float4 v = w4[z * plane4 + i];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    if (geglu) {
+      // columns (4 c4 .. + 3) = (gate, up) of outputs 2 c4 and 2 c4 + 1
+      const float g0 = __half2float(__float2half_rn(alpha * acc.x)), u0 = __half2float(__float2half_rn(alpha * acc.y));
+      const float g1 = __half2float(__float2half_rn(alpha * acc.z)), u1 = __half2float(__float2half_rn(alpha * acc.w));
+      *reinterpret_cast<__half2*>(c + row * ldc + 2 * c4) =
+          __halves2half2(__float2half_rn(sbd::gelu_tanh(g0) * u0), __float2half_rn(sbd::gelu_tanh(g1) * u1));
+    } else {
+      const __half2 lo = __floats2half2_rn(alpha * acc.x, alpha * acc.y);
+      const __half2 hi = __floats2half2_rn(alpha * acc.z, alpha * acc.w);
+      uint2 o;
+      o.x = *reinterpret_cast<const uint32_t*>(&lo);
+      o.y = *reinterpret_cast<const uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(c + row * ldc + 4 * c4) = o;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- host side
 using sb::make_map;
 
@@ -965,9 +1016,16 @@ int q4_splits(int m, int n, int k, int group, int scale_bytes) {
 
 int finalize(const GemmParams& p, int splits, cudaStream_t s) {
   const size_t total = static_cast<size_t>(p.m) * p.n;
-  const int grid = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 16));
-  cudaError_t e = sb::launch_pdl(splitk_finalize_kernel, dim3(grid), dim3(256), 0, s, static_cast<const float*>(p.ws),
-                                 static_cast<__half*>(p.c), p.m, p.n, p.ldc, splits, p.alpha, p.geglu);
+  const bool v4 = p.n % 4 == 0 && sb::aligned(p.ws, 16) &&
+                  (p.geglu ? (p.ldc % 2 == 0 && sb::aligned(p.c, 4)) : (p.ldc % 4 == 0 && sb::aligned(p.c, 8)));
+  const size_t items = v4 ? total / 4 : total;
+  const int grid = static_cast<int>(std::min<size_t>((items + 255) / 256, static_cast<size_t>(sb::num_sms()) * 16));
+  cudaError_t e = v4 ? sb::launch_pdl(splitk_finalize_v4_kernel, dim3(grid), dim3(256), 0, s,
+                                      static_cast<const float*>(p.ws), static_cast<__half*>(p.c), p.m, p.n, p.ldc,
+                                      splits, p.alpha, p.geglu)
+                     : sb::launch_pdl(splitk_finalize_kernel, dim3(grid), dim3(256), 0, s,
+                                      static_cast<const float*>(p.ws), static_cast<__half*>(p.c), p.m, p.n, p.ldc,
+                                      splits, p.alpha, p.geglu);
   if (e != cudaSuccess) return sb::cuda_fail(e, "splitk_finalize_kernel");
   return sb::launch_status("splitk_finalize_kernel");
 }

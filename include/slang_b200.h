@@ -87,6 +87,20 @@ int sb_gemv_q4(const void* w, const void* scales, int scale_dtype, int group,
                void* stream);
 
 /*
+ * sb_gemv_q4 over 2-bit codes (the checkpoint's 2-bit MLP weights of layers
+ * 15+ and its 2-bit lm_head; gemma4/qat_loader.py:33-38, 52-61): four codes per
+ * byte, low bits first, value = code - 2.  Replaces the 2-bit decode GEMVs
+ * gateup_95 / down_96 (gemma4_150/kernels_dsl.py:1130-1230, 1303-1381); same
+ * exact int x int16 arithmetic, same arguments except
+ *   w       device [n, k/4] u8 (k % 64 == 0, so every row is 16-byte aligned)
+ * Scales are per group (k/group) or per row (group = k: the checkpoint's
+ * [n, 1] f32 weight_scale).
+ */
+int sb_gemv_q2(const void* w, const void* scales, int scale_dtype, int group,
+               const void* x, int x_dtype, float* y, int ldy, int m, int n, int k,
+               void* stream);
+
+/*
  * Tied lm_head GEMV fused with greedy argmax (ties -> lowest index).
  * Replaces logits_33 + argmax1_34 + argmax2_35 (gemma4_150/kernels_dsl.py:
  * 1483-1534, 481-570; dispatch gemma4_150/metal_runner.py:392-396) and the
@@ -107,6 +121,12 @@ int sb_gemv_q4(const void* w, const void* scales, int scale_dtype, int group,
 int sb_lmhead_argmax(const void* emb, const void* scales, int scale_dtype, int group,
                      const void* h, int h_dtype, int m, int v, int k, int64_t row_offset,
                      uint64_t* keys, int32_t* tokens, float* logits, void* stream);
+
+/* sb_lmhead_argmax over a 2-bit table (the checkpoint's lm_head, u8 [v, k/4]
+ * row-major as stored; gemma4/qat_loader.py:52-53): codes as in sb_gemv_q2. */
+int sb_lmhead_argmax_q2(const void* emb, const void* scales, int scale_dtype, int group,
+                        const void* h, int h_dtype, int m, int v, int k, int64_t row_offset,
+                        uint64_t* keys, int32_t* tokens, float* logits, void* stream);
 
 /* tokens[i] = global index held in keys[i] (after a cross-shard MAX). */
 int sb_keys_to_tokens(const uint64_t* keys, int32_t* tokens, int m, void* stream);

@@ -24,7 +24,9 @@ SIGNATURES = {
     "sb_device_status": ([_vp], _i),
     "sb_dequant_f16": ([_vp, _i, _vp, _i, _i, _vp, _i, _i, _vp], _i),
     "sb_gemv_q4": ([_vp, _vp, _i, _i, _vp, _i, _vp, _i, _i, _i, _i, _vp], _i),
+    "sb_gemv_q2": ([_vp, _vp, _i, _i, _vp, _i, _vp, _i, _i, _i, _i, _vp], _i),
     "sb_lmhead_argmax": ([_vp, _vp, _i, _i, _vp, _i, _i, _i, _i, _i64, _vp, _vp, _vp, _vp], _i),
+    "sb_lmhead_argmax_q2": ([_vp, _vp, _i, _i, _vp, _i, _i, _i, _i, _i64, _vp, _vp, _vp, _vp], _i),
     "sb_keys_to_tokens": ([_vp, _vp, _i, _vp], _i),
     "sb_gemm_f16": ([_vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _i, _i, _vp], _i),
     "sb_gemm_q4": ([_vp, _vp, _vp, _i, _i, _vp, _i, _i, _i, _f, _i, _i, _vp, _sz, _vp], _i),

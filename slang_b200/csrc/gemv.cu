@@ -56,6 +56,7 @@ struct GemvParams {
   float* logits;
   int* err;
   int m, n, k, group, ldy, ks, rs, n_stages, scale_bulk, x_f32;
+  int bits;  // code width: 4 (two per byte) or 2 (four per byte)
   long long row_offset;
   // vocabulary shards over peer memory: each CTA's key goes to every rank's
   // mailbox (atomic MAX through NVLink) instead of `keys`
@@ -79,9 +80,9 @@ using sbd::make_key;
 
 // This lane's groups of x (rows m < M of the batch, groups gidx[u]) quantised
 // to 16-bit integers, kept in registers for the whole launch.
-template <int M, int GPL>
+template <int M, int GPL, typename XG>
 __device__ __forceinline__ void load_x_groups(const GemvParams& p, const int (&gidx)[GPL], const bool (&gval)[GPL],
-                                              sbd::XGroup (&xg)[M][GPL]) {
+                                              XG (&xg)[M][GPL]) {
 #pragma unroll
   for (int m = 0; m < M; ++m) {
 #pragma unroll
@@ -142,13 +143,15 @@ __device__ __forceinline__ void publish_keys(const GemvParams& p, GemvSmem& sm, 
   }
 }
 
-template <int M, int GPL, bool SF16, int EPI>
+template <int M, int GPL, bool SF16, int EPI, int BITS>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const GemvParams p) {
+  using XG = typename sbd::QTraits<BITS>::XG;
+  using Chunk = typename sbd::QTraits<BITS>::Chunk;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   GemvSmem& sm = *reinterpret_cast<GemvSmem*>(smem_raw);
   volatile int* abort = &sm.abort;
   const int tid = threadIdx.x;
-  const int row_bytes = p.k >> 1;
+  const int row_bytes = p.k * BITS / 8;
   const int gps = p.k / p.group;
   const int esz = SF16 ? 2 : 4;
 
@@ -201,8 +204,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
   // x is the previous kernel's output: wait for it (weights are already streaming)
   sbd::griddep_wait();
   // this lane's groups of x, quantised once (kept in registers)
-  sbd::XGroup xg[M][GPL];
-  load_x_groups<M, GPL>(p, gidx, gval, xg);
+  XG xg[M][GPL];
+  load_x_groups<M, GPL, XG>(p, gidx, gval, xg);
 
   float best_v[M];
   long long best_i[M];
@@ -240,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
 #pragma unroll
         for (int u = 0; u < GPL; ++u) {
           if (!gval[u]) continue;
-          const uint4 q = *reinterpret_cast<const uint4*>(wst + rr * row_bytes + gidx[u] * 16);
+          const Chunk q = *reinterpret_cast<const Chunk*>(wst + rr * row_bytes + gidx[u] * (4 * BITS));
           const int gi = gsi[u];
           float sw;
           if (p.scale_bulk) {
@@ -316,13 +319,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
 // slot when it is done with it, and the warp that releases it last refills
 // it.  Warps drift freely and the copy engine never waits for the slowest
 // warp of a stage.
-template <int M, int GPL, bool SF16, int EPI>
+template <int M, int GPL, bool SF16, int EPI, int BITS>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(const GemvParams p) {
+  using XG = typename sbd::QTraits<BITS>::XG;
+  using Chunk = typename sbd::QTraits<BITS>::Chunk;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   GemvSmem& sm = *reinterpret_cast<GemvSmem*>(smem_raw);
   volatile int* abort = &sm.abort;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int row_bytes = p.k >> 1;
+  const int row_bytes = p.k * BITS / 8;
   const int gps = p.k / p.group;
   const int esz = SF16 ? 2 : 4;
 
@@ -371,8 +376,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
   }
   // x is the previous kernel's output: wait for it (weights are already streaming)
   sbd::griddep_wait();
-  sbd::XGroup xg[M][GPL];
-  load_x_groups<M, GPL>(p, gidx, gval, xg);
+  XG xg[M][GPL];
+  load_x_groups<M, GPL, XG>(p, gidx, gval, xg);
 
   float best_v[M];
   long long best_i[M];
@@ -397,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
 #pragma unroll
         for (int u = 0; u < GPL; ++u) {
           if (!gval[u]) continue;
-          const uint4 q = *reinterpret_cast<const uint4*>(wst + rr * row_bytes + gidx[u] * 16);
+          const Chunk q = *reinterpret_cast<const Chunk*>(wst + rr * row_bytes + gidx[u] * (4 * BITS));
           const int gi = gsi[u];
           float sw;
           if (p.scale_bulk) {
@@ -504,10 +509,10 @@ struct Plan {
 // Groups-per-lane and K slices so 16*GPL*ks covers a row's G groups with the
 // least waste; then rows per stage: as many as fit 24 KB, but few enough that
 // small matrices still spread over the SMs.
-Plan plan(int mtile, int n, int k, int sms) {
+Plan plan(int mtile, int n, int k, int bits, int scale_row_bytes, int sms) {
   const int G = k / 32;
   const int max_gpl = mtile == 1 ? 4 : (mtile == 2 ? 2 : 1);
-  Plan best{1, 16, 1};
+  Plan best{0, 16, 1};  // gpl 0: no shape of this batch tile covers the row
   int best_waste = 1 << 30;
   const int prefs[4] = {3, 2, 4, 1};
   for (int pi = 0; pi < 4; ++pi) {
@@ -522,9 +527,11 @@ Plan plan(int mtile, int n, int k, int sms) {
       best = {gpl, ks, 1};
     }
   }
+  if (best.gpl == 0) return best;
   const int nrl = 16 / best.ks;
-  const int row_bytes = k / 2;
-  int rs = std::max(1, kStageW / row_bytes);
+  const int row_bytes = k * bits / 8;
+  // rows per stage: a stage's codes and (when they ride along) its scales fit their buffers
+  int rs = std::max(1, std::min(kStageW / row_bytes, kStageS / std::max(1, scale_row_bytes)));
   const int spread = (n + sms * kCtasPerSm - 1) / (sms * kCtasPerSm);  // rows per CTA if each gets one stage
   rs = std::min(rs, std::max(nrl, spread));
   rs = std::max(nrl, rs / nrl * nrl);
@@ -533,7 +540,7 @@ Plan plan(int mtile, int n, int k, int sms) {
   return best;
 }
 
-template <int M, int GPL, int EPI>
+template <int M, int GPL, int EPI, int BITS>
 int launch_t(const GemvParams& p, bool sf16, int sms, cudaStream_t s) {
   const int grid = std::min(p.n_stages, sms * kCtasPerSm);
   if (grid == 0) return SB_OK;
@@ -543,54 +550,54 @@ int launch_t(const GemvParams& p, bool sf16, int sms, cudaStream_t s) {
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !done[dev]) {
     // two CTAs per SM need the largest shared-memory carveout
-    cudaError_t e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, true, EPI>,
+    cudaError_t e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, true, EPI, BITS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, false, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, false, EPI, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, true, EPI>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+      e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, true, EPI, BITS>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, false, EPI>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+      e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, false, EPI, BITS>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, true, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, true, EPI, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                smem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, false, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, false, EPI, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                smem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, true, EPI>, cudaFuncAttributePreferredSharedMemoryCarveout,
+      e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, true, EPI, BITS>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                100);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, false, EPI>, cudaFuncAttributePreferredSharedMemoryCarveout,
+      e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, false, EPI, BITS>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                100);
     if (e != cudaSuccess) return sb::cuda_fail(e, "gemv_q4_kernel: smem attribute");
     done[dev] = true;
   }
   cudaError_t e;
   if (p.ks == 1) {
-    e = sf16 ? sb::launch_pdl(gemv_q4_stream_kernel<M, GPL, true, EPI>, dim3(grid), dim3(kThreads), smem, s, p)
-             : sb::launch_pdl(gemv_q4_stream_kernel<M, GPL, false, EPI>, dim3(grid), dim3(kThreads), smem, s, p);
+    e = sf16 ? sb::launch_pdl(gemv_q4_stream_kernel<M, GPL, true, EPI, BITS>, dim3(grid), dim3(kThreads), smem, s, p)
+             : sb::launch_pdl(gemv_q4_stream_kernel<M, GPL, false, EPI, BITS>, dim3(grid), dim3(kThreads), smem, s, p);
   } else {
-    e = sf16 ? sb::launch_pdl(gemv_q4_kernel<M, GPL, true, EPI>, dim3(grid), dim3(kThreads), smem, s, p)
-             : sb::launch_pdl(gemv_q4_kernel<M, GPL, false, EPI>, dim3(grid), dim3(kThreads), smem, s, p);
+    e = sf16 ? sb::launch_pdl(gemv_q4_kernel<M, GPL, true, EPI, BITS>, dim3(grid), dim3(kThreads), smem, s, p)
+             : sb::launch_pdl(gemv_q4_kernel<M, GPL, false, EPI, BITS>, dim3(grid), dim3(kThreads), smem, s, p);
   }
   if (e != cudaSuccess) return sb::cuda_fail(e, "gemv_q4_kernel launch");
   return sb::launch_status("gemv_q4_kernel");
 }
 
-template <int M, int EPI>
+template <int M, int EPI, int BITS>
 int launch_m(const GemvParams& p, const Plan& pl, bool sf16, int sms, cudaStream_t s) {
   if constexpr (M == 1) {
     switch (pl.gpl) {
-      case 1: return launch_t<M, 1, EPI>(p, sf16, sms, s);
-      case 2: return launch_t<M, 2, EPI>(p, sf16, sms, s);
-      case 3: return launch_t<M, 3, EPI>(p, sf16, sms, s);
-      default: return launch_t<M, 4, EPI>(p, sf16, sms, s);
+      case 1: return launch_t<M, 1, EPI, BITS>(p, sf16, sms, s);
+      case 2: return launch_t<M, 2, EPI, BITS>(p, sf16, sms, s);
+      case 3: return launch_t<M, 3, EPI, BITS>(p, sf16, sms, s);
+      default: return launch_t<M, 4, EPI, BITS>(p, sf16, sms, s);
     }
   } else if constexpr (M == 2) {
-    return pl.gpl == 1 ? launch_t<M, 1, EPI>(p, sf16, sms, s) : launch_t<M, 2, EPI>(p, sf16, sms, s);
+    return pl.gpl == 1 ? launch_t<M, 1, EPI, BITS>(p, sf16, sms, s) : launch_t<M, 2, EPI, BITS>(p, sf16, sms, s);
   } else {
-    return launch_t<M, 1, EPI>(p, sf16, sms, s);
+    return launch_t<M, 1, EPI, BITS>(p, sf16, sms, s);
   }
 }
 
@@ -606,7 +613,16 @@ int run(GemvParams p, int epi, bool xf32, bool sf16, cudaStream_t s) {
   const int m_total = p.m;
   while (done < m_total) {
     const int left = m_total - done;
-    const int mt = left >= 4 ? 4 : (left >= 2 ? 2 : 1);
+    // the widest batch tile whose lanes can hold a whole row's groups (x
+    // registers shrink the groups per lane as the tile grows)
+    int mt = left >= 4 ? 4 : (left >= 2 ? 2 : 1);
+    const int srow_bytes = gps * esz;
+    Plan pl = plan(mt, p.n, p.k, p.bits, srow_bytes, sms);
+    while (pl.gpl == 0 && mt > 1) {
+      mt /= 2;
+      pl = plan(mt, p.n, p.k, p.bits, srow_bytes, sms);
+    }
+    if (pl.gpl == 0) return sb::fail(SB_ERR_ARG, "gemv: k=%d has more groups than a row's lanes hold", p.k);
     GemvParams q = p;
     q.m = mt;
     q.x = static_cast<const char*>(p.x) + done * x_row;
@@ -616,7 +632,6 @@ int run(GemvParams p, int epi, bool xf32, bool sf16, cudaStream_t s) {
       q.peer_row0 = p.peer_row0 + done;
       if (p.logits) q.logits = p.logits + static_cast<size_t>(done) * p.n;
     }
-    Plan pl = plan(mt, p.n, p.k, sms);
     q.ks = pl.ks;
     q.rs = pl.rs;
     q.n_stages = (p.n + pl.rs - 1) / pl.rs;
@@ -628,13 +643,24 @@ int run(GemvParams p, int epi, bool xf32, bool sf16, cudaStream_t s) {
     q.scale_bulk = (srow * pl.rs) % 16 == 0 && (srow * last) % 16 == 0 &&
                    srow * pl.rs <= static_cast<size_t>(kStageS) && sb::aligned(p.scales, 16);
     int rc;
-    if (epi == EPI_STORE) {
-      rc = mt == 1 ? launch_m<1, EPI_STORE>(q, pl, sf16, sms, s)
-                   : mt == 2 ? launch_m<2, EPI_STORE>(q, pl, sf16, sms, s) : launch_m<4, EPI_STORE>(q, pl, sf16, sms, s);
+    if (p.bits == 2) {
+      if (epi == EPI_STORE) {
+        rc = mt == 1 ? launch_m<1, EPI_STORE, 2>(q, pl, sf16, sms, s)
+                     : mt == 2 ? launch_m<2, EPI_STORE, 2>(q, pl, sf16, sms, s)
+                               : launch_m<4, EPI_STORE, 2>(q, pl, sf16, sms, s);
+      } else {
+        rc = mt == 1 ? launch_m<1, EPI_ARGMAX, 2>(q, pl, sf16, sms, s)
+                     : mt == 2 ? launch_m<2, EPI_ARGMAX, 2>(q, pl, sf16, sms, s)
+                               : launch_m<4, EPI_ARGMAX, 2>(q, pl, sf16, sms, s);
+      }
+    } else if (epi == EPI_STORE) {
+      rc = mt == 1 ? launch_m<1, EPI_STORE, 4>(q, pl, sf16, sms, s)
+                   : mt == 2 ? launch_m<2, EPI_STORE, 4>(q, pl, sf16, sms, s)
+                             : launch_m<4, EPI_STORE, 4>(q, pl, sf16, sms, s);
     } else {
-      rc = mt == 1 ? launch_m<1, EPI_ARGMAX>(q, pl, sf16, sms, s)
-                   : mt == 2 ? launch_m<2, EPI_ARGMAX>(q, pl, sf16, sms, s)
-                             : launch_m<4, EPI_ARGMAX>(q, pl, sf16, sms, s);
+      rc = mt == 1 ? launch_m<1, EPI_ARGMAX, 4>(q, pl, sf16, sms, s)
+                   : mt == 2 ? launch_m<2, EPI_ARGMAX, 4>(q, pl, sf16, sms, s)
+                             : launch_m<4, EPI_ARGMAX, 4>(q, pl, sf16, sms, s);
     }
     if (rc != SB_OK) return rc;
     done += mt;
@@ -643,11 +669,13 @@ int run(GemvParams p, int epi, bool xf32, bool sf16, cudaStream_t s) {
 }
 
 int check_common(const char* fn, const void* w, const void* scales, int scale_dtype, int group, const void* x,
-                 int x_dtype, int m, int n, int k) {
+                 int x_dtype, int m, int n, int k, int bits = 4) {
   SB_CHECK_ARG(m >= 1 && m <= 8, "%s: m=%d must be in 1..8", fn, m);
   SB_CHECK_ARG(n >= 0, "%s: negative n", fn);
-  SB_CHECK_ARG(k > 0 && k % 32 == 0, "%s: k=%d must be a positive multiple of 32", fn, k);
-  SB_CHECK_ARG(k / 2 <= kStageW, "%s: k=%d is longer than one stage (max %d)", fn, k, 2 * kStageW);
+  SB_CHECK_ARG(k > 0 && k % 32 == 0 && k <= 32768, "%s: k=%d must be a positive multiple of 32, at most 32768", fn,
+               k);
+  SB_CHECK_ARG(bits == 4 || k % 64 == 0, "%s: 2-bit rows must be a multiple of 16 bytes (k %% 64 == 0), k=%d", fn, k);
+  SB_CHECK_ARG(k * bits / 8 <= kStageW, "%s: k=%d is longer than one stage (max %d)", fn, k, kStageW * 8 / bits);
   SB_CHECK_ARG(group > 0 && k % group == 0 && group % 32 == 0, "%s: group=%d must be a multiple of 32 dividing k",
                fn, group);
   SB_CHECK_ARG(scale_dtype == SB_SCALE_F16 || scale_dtype == SB_SCALE_F32, "%s: bad scale dtype", fn);
@@ -669,13 +697,13 @@ int zero_keys(unsigned long long* keys, int m, cudaStream_t s) {
 }
 }  // namespace sb
 
-extern "C" int sb_gemv_q4(const void* w, const void* scales, int scale_dtype, int group, const void* x,
-                          int x_dtype, float* y, int ldy, int m, int n, int k, void* stream) {
-  int rc = check_common("sb_gemv_q4", w, scales, scale_dtype, group, x, x_dtype, m, n, k);
+static int gemv_impl(const char* fn, int bits, const void* w, const void* scales, int scale_dtype, int group,
+                     const void* x, int x_dtype, float* y, int ldy, int m, int n, int k, void* stream) {
+  int rc = check_common(fn, w, scales, scale_dtype, group, x, x_dtype, m, n, k, bits);
   if (rc != SB_OK) return rc;
-  SB_CHECK_ARG(ldy >= n, "sb_gemv_q4: ldy=%d < n=%d", ldy, n);
+  SB_CHECK_ARG(ldy >= n, "%s: ldy=%d < n=%d", fn, ldy, n);
   if (n == 0) return SB_OK;
-  SB_CHECK_ARG(y != nullptr, "sb_gemv_q4: null y");
+  SB_CHECK_ARG(y != nullptr, "%s: null y", fn);
   GemvParams p{};
   p.w = static_cast<const uint8_t*>(w);
   p.scales = scales;
@@ -686,16 +714,27 @@ extern "C" int sb_gemv_q4(const void* w, const void* scales, int scale_dtype, in
   p.k = k;
   p.group = group;
   p.ldy = ldy;
+  p.bits = bits;
   return run(p, EPI_STORE, x_dtype == SB_F32, scale_dtype == SB_SCALE_F16, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int sb_lmhead_argmax(const void* emb, const void* scales, int scale_dtype, int group, const void* h,
-                                int h_dtype, int m, int v, int k, int64_t row_offset, uint64_t* keys,
-                                int32_t* tokens, float* logits, void* stream) {
-  int rc = check_common("sb_lmhead_argmax", emb, scales, scale_dtype, group, h, h_dtype, m, v, k);
+extern "C" int sb_gemv_q4(const void* w, const void* scales, int scale_dtype, int group, const void* x,
+                          int x_dtype, float* y, int ldy, int m, int n, int k, void* stream) {
+  return gemv_impl("sb_gemv_q4", 4, w, scales, scale_dtype, group, x, x_dtype, y, ldy, m, n, k, stream);
+}
+
+extern "C" int sb_gemv_q2(const void* w, const void* scales, int scale_dtype, int group, const void* x,
+                          int x_dtype, float* y, int ldy, int m, int n, int k, void* stream) {
+  return gemv_impl("sb_gemv_q2", 2, w, scales, scale_dtype, group, x, x_dtype, y, ldy, m, n, k, stream);
+}
+
+static int lmhead_impl(const char* fn, int bits, const void* emb, const void* scales, int scale_dtype, int group,
+                       const void* h, int h_dtype, int m, int v, int k, int64_t row_offset, uint64_t* keys,
+                       int32_t* tokens, float* logits, void* stream) {
+  int rc = check_common(fn, emb, scales, scale_dtype, group, h, h_dtype, m, v, k, bits);
   if (rc != SB_OK) return rc;
-  SB_CHECK_ARG(keys != nullptr, "sb_lmhead_argmax: null keys");
-  SB_CHECK_ARG(row_offset >= 0 && row_offset + v <= 0xFFFFFFFFLL, "sb_lmhead_argmax: row indices must fit in 32 bits");
+  SB_CHECK_ARG(keys != nullptr, "%s: null keys", fn);
+  SB_CHECK_ARG(row_offset >= 0 && row_offset + v <= 0xFFFFFFFFLL, "%s: row indices must fit in 32 bits", fn);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   rc = sb::zero_keys(reinterpret_cast<unsigned long long*>(keys), m, s);
   if (rc != SB_OK) return rc;
@@ -712,6 +751,7 @@ extern "C" int sb_lmhead_argmax(const void* emb, const void* scales, int scale_d
     p.k = k;
     p.group = group;
     p.row_offset = row_offset;
+    p.bits = bits;
     rc = run(p, EPI_ARGMAX, h_dtype == SB_F32, scale_dtype == SB_SCALE_F16, s);
     if (rc != SB_OK) return rc;
   }
@@ -722,6 +762,20 @@ extern "C" int sb_lmhead_argmax(const void* emb, const void* scales, int scale_d
     return sb::launch_status("keys_to_tokens_kernel");
   }
   return SB_OK;
+}
+
+extern "C" int sb_lmhead_argmax(const void* emb, const void* scales, int scale_dtype, int group, const void* h,
+                                int h_dtype, int m, int v, int k, int64_t row_offset, uint64_t* keys,
+                                int32_t* tokens, float* logits, void* stream) {
+  return lmhead_impl("sb_lmhead_argmax", 4, emb, scales, scale_dtype, group, h, h_dtype, m, v, k, row_offset, keys,
+                     tokens, logits, stream);
+}
+
+extern "C" int sb_lmhead_argmax_q2(const void* emb, const void* scales, int scale_dtype, int group, const void* h,
+                                   int h_dtype, int m, int v, int k, int64_t row_offset, uint64_t* keys,
+                                   int32_t* tokens, float* logits, void* stream) {
+  return lmhead_impl("sb_lmhead_argmax_q2", 2, emb, scales, scale_dtype, group, h, h_dtype, m, v, k, row_offset, keys,
+                     tokens, logits, stream);
 }
 
 namespace {
@@ -827,6 +881,7 @@ extern "C" int sb_lmhead_argmax_peer(const void* emb, const void* scales, int sc
     p.k = k;
     p.group = group;
     p.row_offset = row_offset;
+    p.bits = 4;
     p.peer_mailboxes = reinterpret_cast<const unsigned long long*>(peer_mailboxes);
     p.peer_epoch = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(own_mailbox) + sbd::kMailEpoch);
     p.world = world;

@@ -65,4 +65,74 @@ __device__ __forceinline__ int dot_group(const uint4 q, const XGroup& g) {
   return (he + ho) * 256 + le + lo;
 }
 
+// ---- 2-bit codes (the checkpoint's 2-bit MLP and lm_head weights): 4 codes
+// per byte, low bits first, zero point 2.  A 32-value group is 8 bytes of
+// codes, two 32-bit words; field k of word j, (w >> 2k) & 0x03030303, holds the
+// codes of values 16 j + 4 b + k (b = byte).  x is arranged to match:
+//   sum (q - 2) * x_int = 256 * dot(q, hi) + dot(q, lo) - 2 * sum(x_int).
+struct XGroup2 {
+  uint32_t hi[8], lo[8];  // [4 j + k]
+  int bias;
+  float sx;
+};
+
+__device__ __forceinline__ void quantise_group(const float (&v)[32], XGroup2& g) {
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(v[i]));
+  const float inv = mx > 0.f ? 32767.f / mx : 0.f;
+  g.sx = mx / 32767.f;
+  int sum = 0;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t hi = 0, lo = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int xi = __float2int_rn(v[16 * j + 4 * b + k] * inv);
+        sum += xi;
+        hi |= (static_cast<uint32_t>(xi >> 8) & 0xFFu) << (8 * b);
+        lo |= (static_cast<uint32_t>(xi) & 0xFFu) << (8 * b);
+      }
+      g.hi[4 * j + k] = hi;
+      g.lo[4 * j + k] = lo;
+    }
+  }
+  g.bias = -2 * sum;
+}
+
+// Exact integer dot of 32 2-bit codes (minus 2) with the group's x_int.
+__device__ __forceinline__ int dot_group(const uint2 q, const XGroup2& g) {
+  const uint32_t w[2] = {q.x, q.y};
+  int h0 = 0, h1 = 0, l0 = g.bias, l1 = 0;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+#pragma unroll
+    for (int k = 0; k < 4; k += 2) {
+      const uint32_t f0 = (w[j] >> (2 * k)) & 0x03030303u;
+      const uint32_t f1 = (w[j] >> (2 * k + 2)) & 0x03030303u;
+      h0 = dp4a_us(f0, g.hi[4 * j + k], h0);
+      l0 = dp4a_uu(f0, g.lo[4 * j + k], l0);
+      h1 = dp4a_us(f1, g.hi[4 * j + k + 1], h1);
+      l1 = dp4a_uu(f1, g.lo[4 * j + k + 1], l1);
+    }
+  }
+  return (h0 + h1) * 256 + l0 + l1;
+}
+
+// The group types and weight chunk of one 32-value group by code width.
+template <int BITS>
+struct QTraits;
+template <>
+struct QTraits<4> {
+  using XG = XGroup;
+  using Chunk = uint4;  // 16 bytes of nibbles
+};
+template <>
+struct QTraits<2> {
+  using XG = XGroup2;
+  using Chunk = uint2;  // 8 bytes of 2-bit codes
+};
+
 }  // namespace sbd

@@ -65,30 +65,36 @@ def dequant_f16(packed: torch.Tensor, scales: torch.Tensor, n_in: int, n_out: in
 
 
 def gemv_q4(w: torch.Tensor, scales: torch.Tensor, x: torch.Tensor,
-            y: torch.Tensor | None = None) -> torch.Tensor:
-    """Decode GEMV ``y[m, n] = x[m] . W[n]`` (matvec_dq4, gemma4/qat_kernels.py:33-77)."""
+            y: torch.Tensor | None = None, bits: int = 4) -> torch.Tensor:
+    """Decode GEMV ``y[m, n] = x[m] . W[n]`` (matvec_dq4, gemma4/qat_kernels.py:33-77);
+    ``bits=2`` for the checkpoint's 2-bit weights (gateup_95 / down_96)."""
     _need(w, "w", (torch.uint8,))
     _need(scales, "scales", (torch.float16, torch.float32))
     _need(x, "x", (torch.float16, torch.float32))
-    n, k = w.shape[0], w.shape[1] * 2
+    if bits not in (2, 4):
+        raise ValueError(f"bits={bits}: the GEMV takes 2- or 4-bit codes")
+    n, k = w.shape[0], w.shape[1] * 8 // bits
     x2 = x.reshape(-1, k)
     m = x2.shape[0]
     if y is None:
         y = torch.empty((m, n), dtype=torch.float32, device=w.device)
     _need(y, "y", (torch.float32,))
-    _lib.call("sb_gemv_q4", _ptr(w), _ptr(scales), _DT[scales.dtype], group_of(scales, k),
-              _ptr(x2), _DT[x.dtype], _ptr(y), y.shape[-1], m, n, k, _stream())
+    _lib.call("sb_gemv_q4" if bits == 4 else "sb_gemv_q2", _ptr(w), _ptr(scales), _DT[scales.dtype],
+              group_of(scales, k), _ptr(x2), _DT[x.dtype], _ptr(y), y.shape[-1], m, n, k, _stream())
     return y
 
 
 def lmhead_argmax(emb: torch.Tensor, scales: torch.Tensor, h: torch.Tensor, row_offset: int = 0,
                   keys: torch.Tensor | None = None, tokens: torch.Tensor | None = None,
-                  logits: torch.Tensor | None = None, want_tokens: bool = True):
-    """Fused ``logits_33`` + ``argmax1_34``/``argmax2_35``; returns (keys, tokens)."""
+                  logits: torch.Tensor | None = None, want_tokens: bool = True, bits: int = 4):
+    """Fused ``logits_33`` + ``argmax1_34``/``argmax2_35``; returns (keys, tokens).
+    ``bits=2`` for the checkpoint's 2-bit lm_head."""
     _need(emb, "emb", (torch.uint8,))
     _need(scales, "scales", (torch.float16, torch.float32))
     _need(h, "h", (torch.float16, torch.float32))
-    v, k = emb.shape[0], emb.shape[1] * 2
+    if bits not in (2, 4):
+        raise ValueError(f"bits={bits}: the lm_head takes 2- or 4-bit codes")
+    v, k = emb.shape[0], emb.shape[1] * 8 // bits
     h2 = h.reshape(-1, k)
     m = h2.shape[0]
     dev = emb.device
@@ -96,7 +102,8 @@ def lmhead_argmax(emb: torch.Tensor, scales: torch.Tensor, h: torch.Tensor, row_
         keys = torch.empty(m, dtype=torch.int64, device=dev)
     if want_tokens and tokens is None:
         tokens = torch.empty(m, dtype=torch.int32, device=dev)
-    _lib.call("sb_lmhead_argmax", _ptr(emb), _ptr(scales), _DT[scales.dtype], group_of(scales, k),
+    _lib.call("sb_lmhead_argmax" if bits == 4 else "sb_lmhead_argmax_q2", _ptr(emb), _ptr(scales), _DT[scales.dtype],
+              group_of(scales, k),
               _ptr(h2), _DT[h.dtype], m, v, k, int(row_offset), _ptr(keys),
               _ptr(tokens) if want_tokens else None, _ptr(logits), _stream())
     return keys, tokens

@@ -46,6 +46,15 @@ def q4_weight(rng: np.random.Generator, n_out: int, n_in: int,
     return packed, scales
 
 
+def q2_weight(rng: np.random.Generator, n_out: int, n_in: int,
+              group: int = GROUP) -> tuple[np.ndarray, np.ndarray]:
+    """Packed 2-bit ``[n_out, n_in/4]`` u8 (four codes per byte, the checkpoint's
+    2-bit layout) and f16 scales ``[n_out, n_in/group]``."""
+    packed = rng.integers(0, 256, (n_out, n_in // 4), dtype=np.uint8)
+    scales = np.abs(rng.normal(0.0, 0.05, (n_out, n_in // group))).astype(np.float16)
+    return packed, scales
+
+
 def activations(rng: np.random.Generator, m: int, k: int, dtype=np.float16) -> np.ndarray:
     return rng.standard_normal((m, k), dtype=np.float32).astype(dtype)
 

@@ -210,6 +210,22 @@ int sb_gemm_q4_geglu(const void* a, const void* w, const void* scales, int scale
 size_t sb_gemm_q4_workspace_size(int m, int n, int k);
 
 /*
+ * sb_gemm_q4 / sb_gemm_q4_geglu over 2-bit codes (the checkpoint's 2-bit MLP
+ * weights of layers 15+; gemma4/qat_loader.py:33-38, 52-61): w [N, K/4] u8,
+ * four codes per byte, low bits first, value = code - 2; dq_f16 is
+ * f16(scale * (code - 2)) as sb_dequant_f16 computes it with bits = 2.  The
+ * reference dequantises these with `_dq` (bit width from the buffer size,
+ * gemma4_150/prefill_gpu.py:186-200) before its f16 GEMM.  Other arguments
+ * and the workspace as for sb_gemm_q4.
+ */
+int sb_gemm_q2(const void* a, const void* w, const void* scales, int scale_dtype, int group,
+               void* c, int m, int n, int k, float alpha, int lda, int ldc,
+               void* workspace, size_t workspace_bytes, void* stream);
+int sb_gemm_q2_geglu(const void* a, const void* w, const void* scales, int scale_dtype, int group,
+                     void* out, int m, int n, int k, float alpha, int lda, int ldo, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/*
  * Tied lm_head + greedy argmax for many rows at once on the tcgen05 GEMM:
  * keys[t] = max over rows v of key(alpha * (a[t] . dequant(w[v])), row_offset + v),
  * key = (orderable(value) << 32) | (0xFFFFFFFF - index) as in sb_lmhead_argmax

@@ -95,6 +95,7 @@ struct GemmParams {
   int geglu;           // int4 kernel: weight rows are interleaved (gate, up) pairs; C[t][i] = GEGLU of pair i
   unsigned long long* keys;  // int4 kernel: greedy-argmax keys per token (row index offset by row_offset) instead of C
   long long row_offset;
+  int bits;            // packed-weight code width: 4 (two per byte) or 2 (four per byte)
   float alpha;
 };
 
@@ -358,18 +359,68 @@ __device__ __forceinline__ void load_scale_tile(const GemmParams& p, uint8_t* sc
   }
 }
 
-// One thread's 32 values of a k-block: f16(scale * (q - 8)) packed in pairs.
-__device__ __forceinline__ void dq_group(const GemmParams& p, const uint8_t* sct, int gi, int r, uint4 q,
+// f16(scale * (q - 2)) for the 16 2-bit codes of `w` (byte b holds codes
+// 4 b .. 4 b + 3, low bits first), as 8 half2 in k order.  byte_perm copies
+// byte b into bytes 0 and 2; masking picks the two codes of a pair into the
+// low bits of the two halves; OR-ing 0x6400 makes them 1024 + q and
+// subtracting 1026 gives q - 2 exactly.  (q - 2) * s is exact in f16 for an f16
+// scale (q - 2 is -2, -1, 0 or 1), so this is the reference's f16 dequant.
+__device__ __forceinline__ void dq16_2bit_half(uint32_t w, __half2 s2, uint32_t* out) {
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6402), __ushort_as_half(0x6402));  // 1026
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const uint32_t t = __byte_perm(w, 0u, 0x4040u | (b << 8) | b);  // byte b at bytes 0 and 2
+#pragma unroll
+    for (int f = 0; f < 2; ++f) {
+      uint32_t r = ((t >> (4 * f)) & 0x00000003u) | ((t >> (4 * f + 2)) & 0x00030000u) | 0x64006400u;
+      __half2 h = __hsub2(*reinterpret_cast<__half2*>(&r), bias);
+      h = __hmul2(h, s2);
+      out[2 * b + f] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+}
+
+// Same with an f32 scale: the product is formed in f32 and rounded once.
+__device__ __forceinline__ void dq16_2bit_float(uint32_t w, float s, uint32_t* out) {
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6402), __ushort_as_half(0x6402));
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const uint32_t t = __byte_perm(w, 0u, 0x4040u | (b << 8) | b);
+#pragma unroll
+    for (int f = 0; f < 2; ++f) {
+      uint32_t r = ((t >> (4 * f)) & 0x00000003u) | ((t >> (4 * f + 2)) & 0x00030000u) | 0x64006400u;
+      const float2 q = __half22float2(__hsub2(*reinterpret_cast<__half2*>(&r), bias));
+      __half2 h = __floats2half2_rn(__fmul_rn(s, q.x), __fmul_rn(s, q.y));
+      out[2 * b + f] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+}
+
+// One thread's 32 values of a k-block, read from its row of the packed stage
+// (16 bytes of 4-bit or 8 bytes of 2-bit codes): f16(scale * (q - zero point))
+// packed in pairs.
+template <int BITS>
+__device__ __forceinline__ void dq_group(const GemmParams& p, const uint8_t* sct, int gi, int r, const uint8_t* codes,
                                          uint32_t (&o)[16]) {
-  const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-  if (p.scale_f16) {
-    const __half2 s2 = __half2half2(reinterpret_cast<const __half*>(sct)[gi * QW + r]);
+  const bool h16 = p.scale_f16;
+  const __half2 s2 = h16 ? __half2half2(reinterpret_cast<const __half*>(sct)[gi * QW + r]) : __half2();
+  const float sf = h16 ? 0.f : reinterpret_cast<const float*>(sct)[gi * QW + r];
+  if constexpr (BITS == 2) {
+    const uint2 q = *reinterpret_cast<const uint2*>(codes);
+    const uint32_t words[2] = {q.x, q.y};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) dq8_half(words[j], s2, o + 4 * j);
+    for (int j = 0; j < 2; ++j) {
+      if (h16) dq16_2bit_half(words[j], s2, o + 8 * j);
+      else dq16_2bit_float(words[j], sf, o + 8 * j);
+    }
   } else {
-    const float sf = reinterpret_cast<const float*>(sct)[gi * QW + r];
+    const uint4 q = *reinterpret_cast<const uint4*>(codes);
+    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) dq8_float(words[j], sf, o + 4 * j);
+    for (int j = 0; j < 4; ++j) {
+      if (h16) dq8_half(words[j], s2, o + 4 * j);
+      else dq8_float(words[j], sf, o + 4 * j);
+    }
   }
 }
 
@@ -507,6 +558,7 @@ __device__ __forceinline__ void reduce_splits(const GemmParams& p, uint8_t* smem
   }
 }
 
+template <int BITS>
 __global__ void __launch_bounds__(Q_WARPS * 32, 1)
     gemm_q4_kernel(const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ CUtensorMap tmW,
                    const GemmParams p) {
@@ -560,10 +612,10 @@ __global__ void __launch_bounds__(Q_WARPS * 32, 1)
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % S;
         if (!sbd::mbar_wait(&bars->empty[s], ((kb / S) & 1) ^ 1, abort, p.err)) break;
-        sbd::mbar_arrive_expect_tx(&bars->full[s], Q_ACT_BYTES + Q_PACK_BYTES);
+        sbd::mbar_arrive_expect_tx(&bars->full[s], Q_ACT_BYTES + QW * BK * BITS / 8);
         const int k0 = (kb0 + kb) * BK;
         sbd::tma_load_2d(&tmAct, &bars->full[s], smem + s * Q_ACT_BYTES, k0, t0);
-        sbd::tma_load_2d(&tmW, &bars->full[s], smem + Q_OFF_PACK + s * Q_PACK_BYTES, k0 / 2, w0);
+        sbd::tma_load_2d(&tmW, &bars->full[s], smem + Q_OFF_PACK + s * Q_PACK_BYTES, k0 * BITS / 8, w0);
         issued = kb + 1;
       }
       if (*abort) {
@@ -616,9 +668,10 @@ __global__ void __launch_bounds__(Q_WARPS * 32, 1)
       if (ok) ok = sbd::mbar_wait(&bars->dempty[slot], ((kb / T) & 1) ^ 1, abort, p.err);
       if (!__all_sync(0xFFFFFFFFu, ok)) break;
       sbd::tc_fence_after();
-      const uint4 q = *reinterpret_cast<const uint4*>(smem + Q_OFF_PACK + s * Q_PACK_BYTES + r * 32 + khalf * 16);
+      constexpr int rowb = 8 * BITS, halfb = 4 * BITS;  // packed bytes of a row's k-block and of its half
+      const uint8_t* q = smem + Q_OFF_PACK + s * Q_PACK_BYTES + r * rowb + khalf * halfb;
       uint32_t o[16];
-      dq_group(p, sct, gi, r, q, o);
+      dq_group<BITS>(p, sct, gi, r, q, o);
       sbd::tmem_st_32x32b_x16(lane_addr + 256 + slot * 32 + khalf * 16, o);
       sbd::tmem_wait_st();
       sbd::tc_fence_before();
@@ -691,6 +744,7 @@ static_assert(sizeof(PairBars) <= 512, "pair barrier block");
 // after tcgen05.wait::st + tcgen05.fence::before_thread_sync -- the hand-off
 // CUTLASS's 2-SM async-producer -> UMMA pipeline uses.  A cluster-scope
 // release arrive costs about a microsecond per k-block.
+template <int BITS>
 __global__ void __launch_bounds__(P_WARPS * 32, 1)
     gemm_q4_pair_kernel(const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ CUtensorMap tmW,
                         const GemmParams p) {
@@ -778,8 +832,8 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % S;
         if (!sbd::mbar_wait(&bars->pempty[s], ((kb / S) & 1) ^ 1, abort, p.err)) break;
-        sbd::mbar_arrive_expect_tx(&bars->pfull[s], Q_PACK_BYTES);
-        sbd::tma_load_2d(&tmW, &bars->pfull[s], smem + P_OFF_PACK + s * Q_PACK_BYTES, (kb0 + kb) * BK / 2, w0);
+        sbd::mbar_arrive_expect_tx(&bars->pfull[s], QW * BK * BITS / 8);
+        sbd::tma_load_2d(&tmW, &bars->pfull[s], smem + P_OFF_PACK + s * Q_PACK_BYTES, (kb0 + kb) * BK * BITS / 8, w0);
         issued = kb + 1;
       }
       if (*abort)
@@ -846,9 +900,10 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
       if (ok) ok = sbd::mbar_wait_cluster(&bars->empty[s], ((kb / S) & 1) ^ 1, abort, p.err);
       if (!__all_sync(0xFFFFFFFFu, ok)) break;
       sbd::tc_fence_after();
-      const uint4 q = *reinterpret_cast<const uint4*>(smem + P_OFF_PACK + s * Q_PACK_BYTES + r * 32 + khalf * 16);
+      constexpr int rowb = 8 * BITS, halfb = 4 * BITS;  // packed bytes of a row's k-block and of its half
+      const uint8_t* q = smem + P_OFF_PACK + s * Q_PACK_BYTES + r * rowb + khalf * halfb;
       uint32_t o[16];
-      dq_group(p, sct, gi, r, q, o);
+      dq_group<BITS>(p, sct, gi, r, q, o);
       sbd::tmem_st_32x32b_x16(lane_addr + 256 + slot * 32 + khalf * 16, o);
       sbd::tmem_wait_st();
       sbd::tc_fence_before();
@@ -1064,8 +1119,9 @@ static int max_active_clusters(bool pair, int csplit) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int nclus = 0;
-    const cudaError_t e = pair ? cudaOccupancyMaxActiveClusters(&nclus, gemm_q4_pair_kernel, &cfg)
-                               : cudaOccupancyMaxActiveClusters(&nclus, gemm_q4_kernel, &cfg);
+    // (both code widths use the same resources)
+    const cudaError_t e = pair ? cudaOccupancyMaxActiveClusters(&nclus, gemm_q4_pair_kernel<4>, &cfg)
+                               : cudaOccupancyMaxActiveClusters(&nclus, gemm_q4_kernel<4>, &cfg);
     if (e != cudaSuccess) {
       cudaGetLastError();
       nclus = 0;
@@ -1137,7 +1193,7 @@ extern "C" int sb_gemm_f16_f32out(const void* a, const void* b, float* c, int m,
 
 static int gemm_q4_impl(const void* a, const void* w, const void* scales, int scale_dtype, int group, void* c, int m,
                         int n, int k, float alpha, int lda, int ldc, void* workspace, size_t workspace_bytes,
-                        void* stream, int geglu, uint64_t* keys = nullptr, long long row_offset = 0) {
+                        void* stream, int geglu, uint64_t* keys = nullptr, long long row_offset = 0, int bits = 4) {
   SB_CHECK_ARG(m >= 0 && n >= 0 && k > 0, "sb_gemm_q4: bad shape");
   SB_CHECK_ARG(!geglu || n % 2 == 0, "sb_gemm_q4_geglu: n=%d must be even (interleaved gate/up rows)", n);
   SB_CHECK_ARG(k % 64 == 0, "sb_gemm_q4: k=%d must be a multiple of 64", k);
@@ -1158,7 +1214,9 @@ static int gemm_q4_impl(const void* a, const void* w, const void* scales, int sc
   int rc = make_map(&tact, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, k, m, lda, BK, pair ? QT / 2 : QT,
                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = make_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, k / 2, n, k / 2, BK / 2, QW, CU_TENSOR_MAP_SWIZZLE_NONE);
+  // packed weight [n, k * bits / 8] u8; a box is one k-block of QW rows
+  rc = make_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, k * bits / 8, n, k * bits / 8, BK * bits / 8, QW,
+                CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   GemmParams p{};
   p.scales = scales;
@@ -1174,6 +1232,7 @@ static int gemm_q4_impl(const void* a, const void* w, const void* scales, int sc
   p.geglu = geglu;
   p.keys = reinterpret_cast<unsigned long long*>(keys);
   p.row_offset = row_offset;
+  p.bits = bits;
   p.kb_total = k / BK;
   // the argmax epilogue needs whole sums: no K split
   int splits = keys ? 1 : q4_splits(m, n, k, group, esz);
@@ -1190,9 +1249,13 @@ static int gemm_q4_impl(const void* a, const void* w, const void* scales, int sc
     rc = sb::zero_keys(reinterpret_cast<unsigned long long*>(keys), m, s);
     if (rc != SB_OK) return rc;
   }
-  static bool done[64] = {false};
-  static bool done_pair[64] = {false};
-  rc = pair ? set_smem(gemm_q4_pair_kernel, P_SMEM, done_pair) : set_smem(gemm_q4_kernel, Q_SMEM, done);
+  static bool done[2][64] = {};
+  static bool done_pair[2][64] = {};
+  const int bi = bits == 2 ? 1 : 0;
+  if (bits == 2)
+    rc = pair ? set_smem(gemm_q4_pair_kernel<2>, P_SMEM, done_pair[bi]) : set_smem(gemm_q4_kernel<2>, Q_SMEM, done[bi]);
+  else
+    rc = pair ? set_smem(gemm_q4_pair_kernel<4>, P_SMEM, done_pair[bi]) : set_smem(gemm_q4_kernel<4>, Q_SMEM, done[bi]);
   if (rc) return rc;
   const int wtiles = (n + QW - 1) / QW;
   const int gx = pair ? (wtiles + 1) / 2 * 2 : wtiles;  // a pair's second tile may lie past n
@@ -1228,12 +1291,18 @@ static int gemm_q4_impl(const void* a, const void* w, const void* scales, int sc
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pair ? 2 : 1;
-    const cudaError_t e = pair ? cudaLaunchKernelEx(&cfg, gemm_q4_pair_kernel, tact, tw, p)
-                               : cudaLaunchKernelEx(&cfg, gemm_q4_kernel, tact, tw, p);
+    cudaError_t e;
+    if (bits == 2)
+      e = pair ? cudaLaunchKernelEx(&cfg, gemm_q4_pair_kernel<2>, tact, tw, p)
+               : cudaLaunchKernelEx(&cfg, gemm_q4_kernel<2>, tact, tw, p);
+    else
+      e = pair ? cudaLaunchKernelEx(&cfg, gemm_q4_pair_kernel<4>, tact, tw, p)
+               : cudaLaunchKernelEx(&cfg, gemm_q4_kernel<4>, tact, tw, p);
     if (e != cudaSuccess) return sb::cuda_fail(e, "gemm_q4 (cluster launch)");
     rc = sb::launch_status(pair ? "gemm_q4_pair_kernel" : "gemm_q4_kernel");
   } else {
-    gemm_q4_kernel<<<grid, Q_WARPS * 32, Q_SMEM, s>>>(tact, tw, p);
+    if (bits == 2) gemm_q4_kernel<2><<<grid, Q_WARPS * 32, Q_SMEM, s>>>(tact, tw, p);
+    else gemm_q4_kernel<4><<<grid, Q_WARPS * 32, Q_SMEM, s>>>(tact, tw, p);
     rc = sb::launch_status("gemm_q4_kernel");
   }
   if (rc != SB_OK || in_cluster || splits == 1) return rc;
@@ -1263,6 +1332,22 @@ extern "C" int sb_gemm_q4_geglu(const void* a, const void* w, const void* scales
                                 size_t workspace_bytes, void* stream) {
   return gemm_q4_impl(a, w, scales, scale_dtype, group, out, m, n, k, alpha, lda, ldo, workspace, workspace_bytes,
                       stream, 1);
+}
+
+// The fused GEMM over 2-bit codes (the checkpoint's 2-bit MLP weights of
+// layers 15+): W [n, k/4] u8, four codes per byte, value = code - 2.
+extern "C" int sb_gemm_q2(const void* a, const void* w, const void* scales, int scale_dtype, int group, void* c, int m,
+                          int n, int k, float alpha, int lda, int ldc, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  return gemm_q4_impl(a, w, scales, scale_dtype, group, c, m, n, k, alpha, lda, ldc, workspace, workspace_bytes,
+                      stream, 0, nullptr, 0, 2);
+}
+
+extern "C" int sb_gemm_q2_geglu(const void* a, const void* w, const void* scales, int scale_dtype, int group,
+                                void* out, int m, int n, int k, float alpha, int lda, int ldo, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  return gemm_q4_impl(a, w, scales, scale_dtype, group, out, m, n, k, alpha, lda, ldo, workspace, workspace_bytes,
+                      stream, 1, nullptr, 0, 2);
 }
 
 // ------------------------------------------------------------------------

@@ -191,7 +191,8 @@ def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, p
 
 
 def gemm_q4(A: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, C: torch.Tensor | None = None,
-            alpha: float = 1.0, workspace: torch.Tensor | None = None, geglu: bool = False) -> torch.Tensor:
+            alpha: float = 1.0, workspace: torch.Tensor | None = None, geglu: bool = False,
+            bits: int = 4) -> torch.Tensor:
     """Fused ``_dq`` + ``_gemm``: ``C = f16(alpha * A @ dq_f16(W)^T)``.
 
     With ``geglu``, W's rows are interleaved (gate, up) pairs and C [M, N/2]
@@ -202,7 +203,9 @@ def gemm_q4(A: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, C: torch.Ten
     _need(scales, "scales", (torch.float16, torch.float32))
     M, K = A.shape
     N = w.shape[0]
-    if w.shape[1] * 2 != K:
+    if bits not in (2, 4):
+        raise ValueError(f"bits={bits}: the fused GEMM takes 2- or 4-bit codes")
+    if w.shape[1] * 8 // bits != K:
         raise ValueError("packed weight does not match A's K")
     if C is None:
         C = torch.empty((M, N // 2 if geglu else N), dtype=torch.float16, device=A.device)
@@ -210,7 +213,8 @@ def gemm_q4(A: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, C: torch.Ten
     if workspace is None:
         need = gemm_q4_workspace_size(M, N, K)
         workspace = _workspace(A.device, need)
-    _lib.call("sb_gemm_q4_geglu" if geglu else "sb_gemm_q4", _ptr(A), _ptr(w), _ptr(scales), _DT[scales.dtype], group_of(scales, K),
+    fn = ("sb_gemm_q4" if bits == 4 else "sb_gemm_q2") + ("_geglu" if geglu else "")
+    _lib.call(fn, _ptr(A), _ptr(w), _ptr(scales), _DT[scales.dtype], group_of(scales, K),
               _ptr(C), M, N, K, float(alpha), K, C.shape[1], _ptr(workspace) if workspace is not None else None,
               0 if workspace is None else workspace.numel() * workspace.element_size(), _stream())
     return C

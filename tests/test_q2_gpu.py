@@ -87,3 +87,52 @@ def test_lmhead_q2_tie_kat(cuda):
     kern.device_status()
     assert int(tok.item()) == 777
     assert int(q4.argmax_first(q4.gemv(packed, scales, h, bits=2))[0]) == 777
+
+
+# ------------------------------------------------------------------ fused 2-bit GEMM
+# (M, N, K): the pair kernel without and with split-K; the real wide-MLP down
+# (K = 12288, splits through the workspace); a ragged one-CTA case
+@pytest.mark.parametrize("M,N,K", [(1024, 6144, 1536), (256, 1536, 12288), (1024, 1536, 6144), (37, 512, 1536),
+                                   (200, 128, 1536)])
+def test_gemm_q2_vs_oracle(cuda, M, N, K):
+    from tests._util import assert_close
+    rng = np.random.default_rng(M + N + K)
+    packed, scales = synth.q2_weight(rng, N, K)
+    a = synth.activations(rng, M, K)
+    c = kern.gemm_q4(T(a, cuda), T(packed, cuda), T(scales, cuda), bits=2).cpu().numpy()
+    kern.device_status()
+    assert_close(c, q4.gemm_f64(a, q4.dequant_f16(packed, scales, 2)), what=f"gemm_q2 M={M} N={N} K={K}")
+    assert_close(c, a.astype(np.float32) @ q4.dequant_f32(packed, scales, 2).T, what="vs f32 oracle")
+
+
+def test_gemm_q2_checkpoint_row_scales_and_dequant_chain(cuda):
+    """Per-row f32 scales (the checkpoint's weight_scale); the fused kernel equals
+    the reference's two-step _dq (bits = 2) -> _gemm within f32 rounding."""
+    rng = np.random.default_rng(14)
+    N, K, M = 2048, 1536, 256
+    packed, _ = synth.q2_weight(rng, N, K)
+    rs = (rng.random((N, 1)) * 0.02 + 0.001).astype(np.float32)
+    a = synth.activations(rng, M, K)
+    A, P, S = T(a, cuda), T(packed, cuda), T(rs, cuda)
+    fused = kern.gemm_q4(A, P, S, bits=2)
+    W = kern.dequant_f16(P, S, K, N, bits=2)
+    C = torch.empty((M, N), dtype=torch.float16, device=cuda)
+    kern.gemm(A, W, C, M, N, K)
+    kern.device_status()
+    np.testing.assert_array_equal(W.cpu().numpy().view(np.uint16), q4.dequant_f16(packed, rs, 2).view(np.uint16))
+    f, c = fused.float().cpu().numpy(), C.float().cpu().numpy()
+    assert np.abs(f - c).max() <= 2 * np.abs(c).max() * 2 ** -11
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 12288, 1536), (256, 256, 12288)])
+def test_gemm_q2_geglu_equals_gemm_then_geglu(cuda, M, N, K):
+    rng = np.random.default_rng(M * 3 + N + K)
+    packed, scales = synth.q2_weight(rng, N, K)
+    a = synth.activations(rng, M, K)
+    A, P, S = T(a, cuda), T(packed, cuda), T(scales, cuda)
+    fused = kern.gemm_q4(A, P, S, geglu=True, bits=2)
+    gu = kern.gemm_q4(A, P, S, bits=2)
+    chain = torch.empty((M, N // 2), dtype=torch.float16, device=cuda)
+    _lib.call("sb_geglu", gu.data_ptr(), _lib.SB_F16, M, N // 2, None, chain.data_ptr(), kern._stream())
+    kern.device_status()
+    np.testing.assert_array_equal(fused.cpu().numpy(), chain.cpu().numpy())

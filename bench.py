@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--m", type=int, default=1024, help="rows of the activation for --kernel")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--batch", type=int, default=256, help="sequences for --kernel decode_batch")
+    ap.add_argument("--bits", type=int, default=4, choices=[2, 4],
+                    help="code width of the weight for --kernel gemv / lmhead / gemm_q4 / gemm_q4_geglu")
     return ap.parse_args()
 
 
@@ -113,7 +115,8 @@ def run_kernel_case(args):
     m = args.m
     g = torch.Generator(device=dev)
     g.manual_seed(0)
-    w = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g)
+    bits = args.bits
+    w = torch.randint(0, 256, (n, k * bits // 8), dtype=torch.uint8, device=dev, generator=g)
     s = (torch.randn((n, k // 32), device=dev, generator=g) * 0.02).abs().half()
     if args.kernel == "attn_decode":
         # batched decode attention: --batch sequences at context --m, 8 query heads, head_dim from --shape's K
@@ -145,7 +148,7 @@ def run_kernel_case(args):
 
         def op():
             if wf is None:
-                kern.gemm_q4(a, w, s, C=c, geglu=geglu)
+                kern.gemm_q4(a, w, s, C=c, geglu=geglu, bits=bits)
             else:
                 kern.gemm(a, wf, c, m, n, k)
     else:
@@ -154,9 +157,9 @@ def run_kernel_case(args):
 
         def op():
             if args.kernel == "gemv":
-                kern.gemv_q4(w, s, x, y=y)
+                kern.gemv_q4(w, s, x, y=y, bits=bits)
             else:
-                kern.lmhead_argmax(w, s, x)
+                kern.lmhead_argmax(w, s, x, bits=bits)
     op()
     torch.cuda.synchronize()
     # replay a CUDA graph of --iters launches so host overhead is not timed
@@ -181,8 +184,8 @@ def run_kernel_case(args):
     elif args.kernel in ("gemm_q4", "gemm_q4_geglu", "gemm_f16"):
         rate = f"{2 * m * n * k / us / 1e6:.1f} TFLOP/s"
     else:
-        rate = f"{(n * k // 2 + n * (k // 32) * 2 + m * k * 4 + m * n * 4) / us / 1e3:.1f} GB/s"
-    print(f"ran {args.kernel} m={m} n={n} k={k} x{args.iters + 1}: {us:.2f} us/launch, {rate} "
+        rate = f"{(n * k * bits // 8 + n * (k // 32) * 2 + m * k * 4 + m * n * 4) / us / 1e3:.1f} GB/s"
+    print(f"ran {args.kernel} ({bits}-bit) m={m} n={n} k={k} x{args.iters + 1}: {us:.2f} us/launch, {rate} "
           f"(graph of back-to-back launches; operands L2-warm when they fit in L2)")
 
 

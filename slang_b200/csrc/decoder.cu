@@ -850,12 +850,26 @@ static int attn_decode_impl(const float* q32, const float* k_cache, const float*
   const size_t need = sb_attn_decode_workspace_size(m, n_heads, head_dim, max_seq);
   if (workspace_bytes < need)
     return sb::fail(SB_ERR_WORKSPACE, "sb_attn_decode: workspace %zu < %zu bytes", workspace_bytes, need);
-  // Keys per split: one chunk while the grid is small; with many sequences up
-  // to 8 chunks, so that splits stay >= ~8 CTAs per SM and the partials
-  // (written, then read by the merge) stay a small share of the K/V bytes.
+  // Keys per split.  A CTA streams its chunks at a rate set by its own
+  // pipeline and two CTAs per SM run at once; splits of one length finish in
+  // waves, and a split costs a fixed set-up and partial write (about 40 keys'
+  // worth).  Pick the chunks per split that minimise (waves) x (keys per split
+  // + 40): long splits when the batch alone fills the SMs, short ones when it
+  // does not.  (Judged on max_seq: the positions are on the device.)
   const int max_chunks = (max_seq + CK - 1) / CK;
-  const long long cta_units = static_cast<long long>(m) * max_chunks;
-  const int nch = static_cast<int>(std::max(1LL, std::min(8LL, cta_units / (8LL * sb::num_sms()))));
+  const long long slots = 2LL * sb::num_sms();
+  int nch = 1;
+  long long best = -1;
+  for (int c = 1; c <= max_chunks; ++c) {
+    const long long sp = (max_chunks + c - 1) / c;
+    if (c > 1 && sp == (max_chunks + c - 2) / (c - 1)) continue;  // same split count as c - 1
+    const long long waves = (static_cast<long long>(m) * sp + slots - 1) / slots;
+    const long long cost = waves * (static_cast<long long>(c) * CK + 40);
+    if (best < 0 || cost < best) {
+      best = cost;
+      nch = c;
+    }
+  }
   const int spk = nch * CK;
   const int splits = (max_seq + spk - 1) / spk;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

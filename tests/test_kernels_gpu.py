@@ -275,7 +275,8 @@ def test_gemm_q4_matches_dequant_then_gemm(cuda):
 
 # (M, N, K): no split; a 6-split cluster reduced in distributed shared memory;
 # 16 splits through workspace partials and the finalize kernel
-@pytest.mark.parametrize("M,N,K", [(1024, 12288, 1536), (256, 512, 1536), (256, 256, 6144), (37, 512, 1536)])
+@pytest.mark.parametrize("M,N,K", [(1024, 12288, 1536), (256, 512, 1536), (256, 256, 6144), (37, 512, 1536),
+                                   (8, 12288, 1536), (32, 512, 6144), (3, 2048, 2048)])
 def test_gemm_q4_geglu_equals_gemm_then_geglu(cuda, M, N, K):
     """GEGLU in the GEMM epilogue is bit-for-bit sb_gemm_q4 followed by sb_geglu."""
     rng = np.random.default_rng(M + N + K)
@@ -367,3 +368,15 @@ def test_gemm_q4_argmax_tie_and_shards(cuda):
                                     want_tokens=False)
         parts.append(kk.cpu().numpy().view(np.uint64))
     np.testing.assert_array_equal(q4.unpack_key_index(np.maximum(parts[0], parts[1])), ref)
+
+
+# short batches (batched decode): a pair's token tile shrinks to 64 or 128 tokens
+@pytest.mark.parametrize("M", [1, 8, 33, 64, 65, 100, 128])
+@pytest.mark.parametrize("N,K", [(2560, 1536), (1536, 6144), (12288, 1536)])
+def test_gemm_q4_short_batches(cuda, M, N, K):
+    rng = np.random.default_rng(M * 13 + N + K)
+    packed, scales = synth.q4_weight(rng, N, K)
+    a = synth.activations(rng, M, K)
+    c = kern.gemm_q4(T(a, cuda), T(packed, cuda), T(scales, cuda)).cpu().numpy()
+    kern.device_status()
+    assert_close(c, q4.gemm_f64(a, q4.dequant_f16(packed, scales, 4)), what=f"gemm_q4 M={M} N={N} K={K}")

@@ -454,12 +454,12 @@ __device__ __forceinline__ void argmax_epilogue(const GemmParams& p, const uint3
 }
 
 __device__ __forceinline__ void epilogue_direct(const GemmParams& p, uint32_t lane_addr, int dw, int r, int lane,
-                                                int w0, int t0, int split) {
+                                                int w0, int t0, int split, int tile_cols = QT) {
   const int feat = w0 + r;
   const bool feat_ok = feat < p.n;
   for (int cc = 0; cc < 2; ++cc) {
-    const int col = (dw >> 2) * 64 + cc * 32;  // token offset within the tile
-    if (t0 + col >= p.m) break;                 // warp-uniform
+    const int col = (dw >> 2) * 64 + cc * 32;         // token offset within the tile
+    if (t0 + col >= p.m || col >= tile_cols) break;  // warp-uniform
     uint32_t v[32];
     sbd::tmem_ld_32x32b_x32(lane_addr + col, v);
     sbd::tmem_wait_ld();
@@ -498,11 +498,12 @@ __device__ __forceinline__ void epilogue_direct(const GemmParams& p, uint32_t la
 
 // Split-K in a cluster: this split's partial tile -> its own shared memory
 // (idle activation stages) as [token column][weight row] f32.
-__device__ __forceinline__ void stash_partial(uint8_t* smem, uint32_t lane_addr, int dw, int r) {
+__device__ __forceinline__ void stash_partial(uint8_t* smem, uint32_t lane_addr, int dw, int r, int tile_cols = QT) {
   sbd::fence_proxy_async_smem();
   float* red = reinterpret_cast<float*>(smem);
   for (int cc = 0; cc < 2; ++cc) {
     const int col = (dw >> 2) * 64 + cc * 32;
+    if (col >= tile_cols) break;  // warp-uniform
     uint32_t v[32];
     sbd::tmem_ld_32x32b_x32(lane_addr + col, v);
     sbd::tmem_wait_ld();
@@ -517,8 +518,8 @@ __device__ __forceinline__ void stash_partial(uint8_t* smem, uint32_t lane_addr,
 // rounding of splitk_finalize_kernel), split z' living in cluster CTA
 // rank_base + rank_stride * z'; then writes f16 (or GEGLU pairs).
 __device__ __forceinline__ void reduce_splits(const GemmParams& p, uint8_t* smem, int ew, int lane, int w0, int t0,
-                                              int z, int nz, int rank_base, int rank_stride) {
-  const int c_lo = z * QT / nz, c_hi = (z + 1) * QT / nz;
+                                              int z, int nz, int rank_base, int rank_stride, int tile_cols = QT) {
+  const int c_lo = z * tile_cols / nz, c_hi = (z + 1) * tile_cols / nz;
   const uint32_t red0 = sbd::smem_u32(smem);
   const int rr = lane * 4;  // weight rows rr .. rr + 3 of the tile
   const int feat = w0 + rr;
@@ -744,7 +745,7 @@ static_assert(sizeof(PairBars) <= 512, "pair barrier block");
 // after tcgen05.wait::st + tcgen05.fence::before_thread_sync -- the hand-off
 // CUTLASS's 2-SM async-producer -> UMMA pipeline uses.  A cluster-scope
 // release arrive costs about a microsecond per k-block.
-template <int BITS>
+template <int BITS, int NT>
 __global__ void __launch_bounds__(P_WARPS * 32, 1)
     gemm_q4_pair_kernel(const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ CUtensorMap tmW,
                         const GemmParams p) {
@@ -761,8 +762,9 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
   const bool lead = rank == lead_rank;
   const uint16_t pair_mask = static_cast<uint16_t>(3u << lead_rank);
   const int w0 = blockIdx.x * QW;                  // this CTA's 128 weight rows
-  const int t0 = blockIdx.y * QT;                  // the pair's 256 tokens
-  const int th = t0 + (rank & 1) * (QT / 2);       // this CTA's half of them
+  static_assert(NT % 32 == 0 && NT >= 32 && NT <= QT, "token tile");
+  const int t0 = blockIdx.y * NT;                  // the pair's NT tokens (MMA N)
+  const int th = t0 + (rank & 1) * (NT / 2);       // this CTA's half of them
   const int kb0 = blockIdx.z * p.kb_per_split;
   const int nkb = min(p.kb_per_split, p.kb_total - kb0);
   const int g_lo = (kb0 * BK) / p.group;
@@ -809,7 +811,7 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
         const uint32_t ph = ((kb / S) & 1) ^ 1;
         const int k0 = (kb0 + kb) * BK;
         if (!sbd::mbar_wait_cluster(&bars->empty[s], ph, abort, p.err)) break;
-        if (lead) sbd::mbar_arrive_expect_tx(&bars->ready[s], 2 * P_ACT_BYTES);
+        if (lead) sbd::mbar_arrive_expect_tx(&bars->ready[s], NT * BK * 2);  // both CTAs' NT/2-token halves
         sbd::tma_load_2d_pair(&tmAct, sbd::mapa_shared(sbd::smem_u32(&bars->ready[s]), lead_rank),
                               smem + s * P_ACT_BYTES, k0, th);
         issued = kb + 1;
@@ -848,7 +850,7 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
     // next stage's barrier is tested (without blocking) before this stage's
     // last MMA, so a ready stage costs no wait.
     if (lane == 0 && lead) {
-      constexpr uint32_t idesc = sbd::umma_idesc_f16(2 * QW, QT, 0, 0);
+      constexpr uint32_t idesc = sbd::umma_idesc_f16(2 * QW, NT, 0, 0);
       const uint64_t bdesc0 = sbd::umma_desc(sbd::smem_u32(smem), 16, 1024, sbd::kLayoutSwizzle128B);
       const uint32_t a0 = tmem + 256;
       bool ok = nkb > 0 && sbd::mbar_wait_cluster(&bars->ready[0], 0, abort, p.err);
@@ -919,15 +921,16 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
     const bool ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait_cluster(&bars->accum, 0, abort, p.err));
     if (ok) {
       sbd::tc_fence_after();
-      if (p.csplit > 1) stash_partial(smem, lane_addr, dw, r);
-      else epilogue_direct(p, lane_addr, dw, r, lane, w0, t0, blockIdx.z);
+      if (p.csplit > 1) stash_partial(smem, lane_addr, dw, r, NT);
+      else epilogue_direct(p, lane_addr, dw, r, lane, w0, t0, blockIdx.z, NT);
     }
   }
 
   if (p.csplit > 1) {
     // every thread of every CTA reaches both cluster barriers (abort paths included)
     sbd::cluster_sync_all();
-    if (warp >= 2 && warp < Q_WARPS) reduce_splits(p, smem, warp - 2, lane, w0, t0, rank >> 1, p.csplit, rank & 1, 2);
+    if (warp >= 2 && warp < Q_WARPS)
+      reduce_splits(p, smem, warp - 2, lane, w0, t0, rank >> 1, p.csplit, rank & 1, 2, NT);
     sbd::cluster_sync_all();
   }
 
@@ -1119,9 +1122,13 @@ static int max_active_clusters(bool pair, int csplit) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int nclus = 0;
-    // (both code widths use the same resources)
-    const cudaError_t e = pair ? cudaOccupancyMaxActiveClusters(&nclus, gemm_q4_pair_kernel<4>, &cfg)
-                               : cudaOccupancyMaxActiveClusters(&nclus, gemm_q4_kernel<4>, &cfg);
+    // (every code width and token tile uses the same resources)
+    cudaError_t e = pair ? cudaFuncSetAttribute(gemm_q4_pair_kernel<4, QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                P_SMEM)
+                         : cudaFuncSetAttribute(gemm_q4_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q_SMEM);
+    if (e == cudaSuccess)
+      e = pair ? cudaOccupancyMaxActiveClusters(&nclus, gemm_q4_pair_kernel<4, QT>, &cfg)
+               : cudaOccupancyMaxActiveClusters(&nclus, gemm_q4_kernel<4>, &cfg);
     if (e != cudaSuccess) {
       cudaGetLastError();
       nclus = 0;
@@ -1191,6 +1198,23 @@ extern "C" int sb_gemm_f16_f32out(const void* a, const void* b, float* c, int m,
   return gemm_f16_impl(a, b, c, 1, m, n, k, alpha, tr, lda, ldb, ldc, stream);
 }
 
+// Raises the pair kernel's shared-memory limit once per (instantiation, device)
+// and launches it with `cfg` (cluster and programmatic-serialisation attributes).
+template <int BITS, int NT>
+static cudaError_t launch_pair(cudaLaunchConfig_t& cfg, const CUtensorMap& tact, const CUtensorMap& tw,
+                               const GemmParams& p) {
+  static bool done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !done[dev]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(gemm_q4_pair_kernel<BITS, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) done[dev] = true;
+  }
+  return cudaLaunchKernelEx(&cfg, gemm_q4_pair_kernel<BITS, NT>, tact, tw, p);
+}
+
 static int gemm_q4_impl(const void* a, const void* w, const void* scales, int scale_dtype, int group, void* c, int m,
                         int n, int k, float alpha, int lda, int ldc, void* workspace, size_t workspace_bytes,
                         void* stream, int geglu, uint64_t* keys = nullptr, long long row_offset = 0, int bits = 4) {
@@ -1210,8 +1234,11 @@ static int gemm_q4_impl(const void* a, const void* w, const void* scales, int sc
   CUtensorMap tact, tw;
   const bool pair = q4_pair(n);
   const int max_cs = q4_max_cluster_splits(n);
-  // a CTA of a pair loads half of the 256-token activation tile
-  int rc = make_map(&tact, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, k, m, lda, BK, pair ? QT / 2 : QT,
+  // Tokens per pair (the MMA's N): 256, or for a short batch the smallest of
+  // 64 / 128 that holds it -- the MMAs then take a quarter / half of the time.
+  const int nt = !pair ? QT : (m <= 64 ? 64 : (m <= 128 ? 128 : QT));
+  // a CTA of a pair loads half of the pair's activation tile
+  int rc = make_map(&tact, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, k, m, lda, BK, pair ? nt / 2 : QT,
                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   // packed weight [n, k * bits / 8] u8; a box is one k-block of QW rows
@@ -1249,17 +1276,14 @@ static int gemm_q4_impl(const void* a, const void* w, const void* scales, int sc
     rc = sb::zero_keys(reinterpret_cast<unsigned long long*>(keys), m, s);
     if (rc != SB_OK) return rc;
   }
-  static bool done[2][64] = {};
-  static bool done_pair[2][64] = {};
-  const int bi = bits == 2 ? 1 : 0;
-  if (bits == 2)
-    rc = pair ? set_smem(gemm_q4_pair_kernel<2>, P_SMEM, done_pair[bi]) : set_smem(gemm_q4_kernel<2>, Q_SMEM, done[bi]);
-  else
-    rc = pair ? set_smem(gemm_q4_pair_kernel<4>, P_SMEM, done_pair[bi]) : set_smem(gemm_q4_kernel<4>, Q_SMEM, done[bi]);
-  if (rc) return rc;
+  if (!pair) {
+    static bool done[2][64] = {};
+    rc = bits == 2 ? set_smem(gemm_q4_kernel<2>, Q_SMEM, done[1]) : set_smem(gemm_q4_kernel<4>, Q_SMEM, done[0]);
+    if (rc) return rc;
+  }
   const int wtiles = (n + QW - 1) / QW;
   const int gx = pair ? (wtiles + 1) / 2 * 2 : wtiles;  // a pair's second tile may lie past n
-  const int ttiles = (m + QT - 1) / QT;
+  const int ttiles = (m + nt - 1) / nt;
   const int clusters = (pair ? gx / 2 : gx) * ttiles;  // per split
   // a cluster split pays off only if all its clusters are resident at once;
   // otherwise use fewer splits (while the group scales of a split still fit)
@@ -1292,12 +1316,20 @@ static int gemm_q4_impl(const void* a, const void* w, const void* scales, int sc
     cfg.attrs = attr;
     cfg.numAttrs = pair ? 2 : 1;
     cudaError_t e;
-    if (bits == 2)
-      e = pair ? cudaLaunchKernelEx(&cfg, gemm_q4_pair_kernel<2>, tact, tw, p)
-               : cudaLaunchKernelEx(&cfg, gemm_q4_kernel<2>, tact, tw, p);
-    else
-      e = pair ? cudaLaunchKernelEx(&cfg, gemm_q4_pair_kernel<4>, tact, tw, p)
-               : cudaLaunchKernelEx(&cfg, gemm_q4_kernel<4>, tact, tw, p);
+    if (pair) {
+      const int which = (bits == 2 ? 3 : 0) + (nt == 64 ? 0 : nt == 128 ? 1 : 2);
+      switch (which) {
+        case 0: e = launch_pair<4, 64>(cfg, tact, tw, p); break;
+        case 1: e = launch_pair<4, 128>(cfg, tact, tw, p); break;
+        case 2: e = launch_pair<4, QT>(cfg, tact, tw, p); break;
+        case 3: e = launch_pair<2, 64>(cfg, tact, tw, p); break;
+        case 4: e = launch_pair<2, 128>(cfg, tact, tw, p); break;
+        default: e = launch_pair<2, QT>(cfg, tact, tw, p); break;
+      }
+    } else {
+      e = bits == 2 ? cudaLaunchKernelEx(&cfg, gemm_q4_kernel<2>, tact, tw, p)
+                    : cudaLaunchKernelEx(&cfg, gemm_q4_kernel<4>, tact, tw, p);
+    }
     if (e != cudaSuccess) return sb::cuda_fail(e, "gemm_q4 (cluster launch)");
     rc = sb::launch_status(pair ? "gemm_q4_pair_kernel" : "gemm_q4_kernel");
   } else {

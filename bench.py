@@ -52,7 +52,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", default="",
-                    choices=["", "gemm_q4", "gemm_q4_geglu", "gemm_f16", "gemv", "lmhead", "attn", "attn_decode", "prefill",
+                    choices=["", "gemm_q4", "gemm_q4_geglu", "gemm_f16", "gemv", "lmhead", "attn", "attn_decode", "gemv_q8",
+                             "gemv_bf16", "ple_block", "prefill",
                              "decode", "decode_fused", "decode_batch"],
                     help="run one kernel --iters times on a single shape and exit (for ncu captures)")
     ap.add_argument("--shape", default="6144,1536", help="N,K of the weight for --kernel")
@@ -140,6 +141,37 @@ def run_kernel_case(args):
 
         def op():
             kern.attn_prefill(q, kk, vv, out)
+    elif args.kernel in ("gemv_q8", "gemv_bf16", "ple_block"):
+        # PLE kernels: weights rotated over copies totalling > 256 MB so every launch reads HBM
+        esz = 2 if args.kernel == "gemv_bf16" else 1
+        per = (2 * 256 * 1536 if args.kernel == "ple_block" else n * k * esz)
+        copies = max(2, -(-(256 << 20) // per))
+        x = torch.randn((m, 1536 if args.kernel == "ple_block" else k), device=dev, generator=g)
+        if args.kernel == "ple_block":
+            ple_in = torch.randn((m, 256), device=dev, generator=g)
+            layers = [{"gate": (torch.randint(0, 256, (256, 1536), dtype=torch.uint8, device=dev, generator=g),
+                                torch.full((256,), 1e-4, device=dev)),
+                       "proj": (torch.randint(0, 256, (1536, 256), dtype=torch.uint8, device=dev, generator=g),
+                                torch.full((1536,), 1e-3, device=dev)),
+                       "post_norm": torch.ones(1536, device=dev), "scalar": 1.0} for _ in range(copies)]
+        else:
+            ws = [torch.randint(0, 256, (n, k * esz), dtype=torch.uint8, device=dev, generator=g)
+                  for _ in range(copies)]
+            if esz == 2:
+                ws = [t.view(torch.int16) for t in ws]
+            scale = torch.full((n,), 1e-3, device=dev)
+            y = torch.empty((m, n), device=dev)
+        turn = [0]
+
+        def op():
+            i = turn[0] % copies
+            turn[0] += 1
+            if args.kernel == "ple_block":
+                kern.ple_block(x, ple_in, layers[i], 1e-6)
+            elif esz == 2:
+                kern.gemv_bf16(ws[i], x, alpha=0.03, out=y)
+            else:
+                kern.gemv_q8(ws[i], scale, x, out=y)
     elif args.kernel in ("gemm_q4", "gemm_q4_geglu", "gemm_f16"):
         a = torch.randn((m, k), device=dev, generator=g).half()
         geglu = args.kernel == "gemm_q4_geglu"
@@ -181,6 +213,10 @@ def run_kernel_case(args):
         rate = f"{2 * args.batch * m * k * 4 / us / 1e3:.1f} GB/s of K/V"
     elif args.kernel == "attn":
         rate = f"{2 * 2 * 8 * m * m / 2 * k / us / 1e6:.1f} TFLOP/s (causal: half of S x S)"
+    elif args.kernel in ("gemv_q8", "gemv_bf16"):
+        rate = f"{(n * k * esz + n * 4 * (esz == 1) + m * k * 4 + m * n * 4) / us / 1e3:.1f} GB/s (weights rotated over copies > L2)"
+    elif args.kernel == "ple_block":
+        rate = f"{(2 * 256 * 1536 + 1792 * 4 + m * 1536 * 16) / us / 1e3:.1f} GB/s over gate + proj + tail (3 launches)"
     elif args.kernel in ("gemm_q4", "gemm_q4_geglu", "gemm_f16"):
         rate = f"{2 * m * n * k / us / 1e6:.1f} TFLOP/s"
     else:

@@ -379,6 +379,57 @@ int sb_decode_step_fused(const void* layers_dev, int n_layers, const void* emb, 
                          size_t scratch_bytes, void* stream);
 size_t sb_decode_step_fused_scratch_size(int hidden, int n_heads, int head_dim, int inter, int max_seq);
 
+/* ---------------------------------------------------------------------------
+ * Per-layer embeddings (PLE) of Gemma-4-E2B, weight-only f32 arithmetic as
+ * gemma4/reference.py:92-101 (per-layer input) and :154-163 (per-layer block)
+ * with the QAT dequant of gemma4/qat_reference.py:39-45.  8-bit linears are
+ * the checkpoint's signed int8 codes stored +128-biased (the byte layout of
+ * gemma4_150/export.py:150-157) with one f32 scale per output row
+ * (gemma4/qat_loader.py:41-48, 98-102).  Activation rows are f32; m is any
+ * count (launched in blocks of 8 rows).
+ * ------------------------------------------------------------------------- */
+
+/* y[r][o] = row_scale[o] * sum_k (codes[o][k] - 128) * x[r][k], r < m, o < n;
+ * with ple != null instead y = gelu_tanh(that) * ple[r * ld_ple + o].
+ * k % 16 == 0, k >= 64; codes and x 16-byte aligned, ldx % 4 == 0.
+ * Replaces plegate_76 (gemma4_150/kernels_dsl.py:829-870; ple != null) and the
+ * matmul of pleproj_77 (:1000-1060; ple == null), without the SRQ steps. */
+int sb_gemv_q8(const void* codes, const float* row_scale, const float* x, int ldx, float* y, int ldy,
+               int m, int n, int k, const float* ple, int ld_ple, void* stream);
+
+/* y[r][o] = alpha * sum_k bf16(w[o][k]) * x[r][k]  (w: bf16 bit patterns [n][k]).
+ * k % 8 == 0, k >= 32; w and x 16-byte aligned.  Replaces the
+ * per_layer_model_projection matmul and its hidden**-0.5 factor
+ * (gemma4/reference.py:97-98). */
+int sb_gemv_bf16(const void* w, float alpha, const float* x, int ldx, float* y, int ldy,
+                 int m, int n, int k, void* stream);
+
+/* hidden[r] = (hidden[r] + rmsnorm(proj[r]) * w_post) * layer_scalar, in place;
+ * when w_next != null also h = rmsnorm(hidden[r]) * w_next -> h_out (f32)
+ * and/or h16_out (f16).  n % 4 == 0, n <= 8192, 16-byte aligned rows.
+ * Replaces the norm-add tail of pleproj_77 (gemma4_150/kernels_dsl.py:1062-1125;
+ * gemma4/reference.py:160-163). */
+int sb_ple_norm_add(const float* proj, float* hidden, const float* w_post, float layer_scalar,
+                    const float* w_next, float* h_out, void* h16_out, int m, int n, float eps,
+                    void* stream);
+
+/* y[r][c] = (q - 8) * scales[id][c / group] * ple_scale for the 4-bit table row
+ * id = ids[r] (cols values, two per byte, low nibble first; ids outside
+ * [0, vocab) give a zero row).  cols % 8 == 0, group % 8 == 0.
+ * Replaces plegather_01 (gemma4_150/kernels_dsl.py:457-478) and
+ * QATReference._ple_table_row * ple_scale (gemma4/qat_reference.py:39-45,
+ * gemma4/reference.py:96). */
+int sb_ple_gather(const int32_t* ids, const void* table, const float* scales, int vocab, int cols,
+                  int group, float ple_scale, float* y, int m, void* stream);
+
+/* out[r][l][:] = (rmsnorm(ctx[r][l][:]) * w_norm + gather(ids[r])[l*d:(l+1)*d]) * 2^-0.5
+ * over n_layers slices of d values (ctx from sb_gemv_bf16 with alpha =
+ * hidden**-0.5; the gather as sb_ple_gather).  d % 256 == 0.
+ * Replaces the rest of ReferenceGemma4._ple_input (gemma4/reference.py:99-101). */
+int sb_ple_combine(const float* ctx, const int32_t* ids, const void* table, const float* scales,
+                   int vocab, const float* w_norm, int n_layers, int d, int group, float ple_scale,
+                   float eps, float* out, int m, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

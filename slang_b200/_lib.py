@@ -56,6 +56,11 @@ SIGNATURES = {
     "sb_attn_decode": ([_vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _vp, _vp, _sz, _vp], _i),
     "sb_attn_decode_workspace_size": ([_i, _i, _i, _i], _sz),
     "sb_step_advance": ([_vp, _vp, _vp, _vp, _i, _i, _vp], _i),
+    "sb_gemv_q8": ([_vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _vp, _i, _vp], _i),
+    "sb_gemv_bf16": ([_vp, _f, _vp, _i, _vp, _i, _i, _i, _i, _vp], _i),
+    "sb_ple_norm_add": ([_vp, _vp, _vp, _f, _vp, _vp, _vp, _i, _i, _f, _vp], _i),
+    "sb_ple_gather": ([_vp, _vp, _vp, _i, _i, _i, _f, _vp, _i, _vp], _i),
+    "sb_ple_combine": ([_vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _f, _f, _vp, _i, _vp], _i),
     "sb_decode_step_fused": ([_vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _f, _vp, _vp, _vp,
                               _vp, _i, _vp, _vp, _sz, _vp], _i),
     "sb_decode_step_fused_scratch_size": ([_i, _i, _i, _i, _i], _sz),

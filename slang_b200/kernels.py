@@ -264,3 +264,132 @@ def _workspace(device, nbytes: int):
 def device_status() -> None:
     """Raise if a bounded device-side wait has timed out since the last check."""
     _lib.call("sb_device_status", _stream())
+
+
+# ---------------------------------------------------------------- per-layer embeddings (PLE)
+
+def _rows(t: torch.Tensor, name: str, n: int) -> int:
+    """Row stride of an f32 [m, n] operand whose rows may be spaced (a slice of a wider tensor)."""
+    if t.dtype != torch.float32 or t.dim() != 2 or t.shape[1] != n or t.stride(1) != 1 or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA f32 [m, {n}] tensor with unit column stride")
+    return t.stride(0)
+
+
+def gemv_q8(codes: torch.Tensor, row_scale: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = None,
+            ple: torch.Tensor | None = None) -> torch.Tensor:
+    """8-bit linear ``y = x @ ((codes - 128) * row_scale).T`` for decode rows (``sb_gemv_q8``).
+
+    ``codes`` [n, k] u8 are the checkpoint's int8 weights +128-biased
+    (gemma4_150/export.py:155-157), ``row_scale`` [n] or [n, 1] f32.  With
+    ``ple`` ([m, n] f32, rows may be spaced, e.g. ``ple_in[:, layer]``) the
+    result is ``gelu_tanh(y) * ple``: the PLE input gate of
+    gemma4/reference.py:159 (``plegate_76``).
+    """
+    _need(codes, "codes", (torch.uint8,))
+    _need(row_scale, "row_scale", (torch.float32,))
+    n, k = codes.shape
+    if row_scale.numel() != n:
+        raise ValueError("row_scale must hold one scale per output row")
+    x2 = x.reshape(-1, k) if x.is_contiguous() else x
+    ldx = _rows(x2, "x", k)
+    m = x2.shape[0]
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.float32, device=x.device)
+    ldy = _rows(out, "out", n)
+    ld_ple = _rows(ple, "ple", n) if ple is not None else 0
+    if ple is not None and ple.shape[0] != m:
+        raise ValueError("ple must have one row per activation row")
+    _lib.call("sb_gemv_q8", _ptr(codes), _ptr(row_scale), _ptr(x2), ldx, _ptr(out), ldy, m, n, k, _ptr(ple), ld_ple,
+              _stream())
+    return out
+
+
+def gemv_bf16(w: torch.Tensor, x: torch.Tensor, alpha: float = 1.0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``y = alpha * x @ w.T`` for a bf16 weight [n, k] (``sb_gemv_bf16``), f32 rows in and out."""
+    _need(w, "w", (torch.bfloat16, torch.int16))
+    n, k = w.shape
+    x2 = x.reshape(-1, k) if x.is_contiguous() else x
+    ldx = _rows(x2, "x", k)
+    m = x2.shape[0]
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.float32, device=x.device)
+    ldy = _rows(out, "out", n)
+    _lib.call("sb_gemv_bf16", _ptr(w), float(alpha), _ptr(x2), ldx, _ptr(out), ldy, m, n, k, _stream())
+    return out
+
+
+def ple_gather(ids: torch.Tensor, table: torch.Tensor, scales: torch.Tensor, ple_scale: float,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """Scaled 4-bit PLE table rows [m, cols] (``sb_ple_gather``; plegather_01,
+    gemma4_150/kernels_dsl.py:457-478).  ``table`` [vocab, cols/2] u8,
+    ``scales`` [vocab, cols/group] f32, ``ids`` [m] int32."""
+    _need(ids, "ids", (torch.int32,))
+    _need(table, "table", (torch.uint8,))
+    _need(scales, "scales", (torch.float32,))
+    vocab, cols = table.shape[0], table.shape[1] * 2
+    group = group_of(scales, cols)
+    m = ids.numel()
+    if out is None:
+        out = torch.empty(m, cols, dtype=torch.float32, device=ids.device)
+    _need(out, "out", (torch.float32,))
+    _lib.call("sb_ple_gather", _ptr(ids), _ptr(table), _ptr(scales), vocab, cols, group, float(ple_scale), _ptr(out),
+              m, _stream())
+    return out
+
+
+def ple_input(x: torch.Tensor, ids: torch.Tensor, table: torch.Tensor, scales: torch.Tensor, w_proj: torch.Tensor,
+              w_norm: torch.Tensor, n_layers: int, d: int, eps: float, ple_scale: float,
+              out: torch.Tensor | None = None, ctx: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-layer inputs [m, n_layers, d] of ``ReferenceGemma4._ple_input``
+    (gemma4/reference.py:92-101): the bf16 model projection of the scaled
+    embedding ``x`` times hidden**-0.5, RMS-normed per layer slice, plus the
+    gathered table row, times 2**-0.5 (``sb_gemv_bf16`` + ``sb_ple_combine``)."""
+    _need(ids, "ids", (torch.int32,))
+    _need(table, "table", (torch.uint8,))
+    _need(scales, "scales", (torch.float32,))
+    _need(w_norm, "w_norm", (torch.float32,))
+    hidden = x.shape[-1]
+    m = ids.numel()
+    cols = n_layers * d
+    if table.shape[1] * 2 != cols or w_proj.shape != (cols, hidden) or w_norm.numel() != d:
+        raise ValueError("PLE table, projection or norm does not match n_layers * d")
+    ctx = gemv_bf16(w_proj, x.reshape(m, hidden), alpha=float(hidden ** -0.5), out=ctx)
+    if out is None:
+        out = torch.empty(m, n_layers, d, dtype=torch.float32, device=x.device)
+    _need(out, "out", (torch.float32,))
+    _lib.call("sb_ple_combine", _ptr(ctx), _ptr(ids), _ptr(table), _ptr(scales), table.shape[0], _ptr(w_norm),
+              n_layers, d, group_of(scales, cols), float(ple_scale), float(eps), _ptr(out), m, _stream())
+    return out
+
+
+def ple_norm_add(proj: torch.Tensor, hidden: torch.Tensor, w_post: torch.Tensor, layer_scalar: float, eps: float,
+                 w_next: torch.Tensor | None = None, h_out: torch.Tensor | None = None,
+                 h16_out: torch.Tensor | None = None) -> torch.Tensor:
+    """In place ``hidden = (hidden + rmsnorm(proj) * w_post) * layer_scalar``
+    (gemma4/reference.py:160-163), then optionally the next layer's input
+    norm into ``h_out`` / ``h16_out`` (``sb_ple_norm_add``)."""
+    for t, name in ((proj, "proj"), (hidden, "hidden"), (w_post, "w_post")):
+        _need(t, name, (torch.float32,))
+    n = hidden.shape[-1]
+    m = hidden.numel() // n
+    if proj.shape != hidden.shape:
+        raise ValueError("proj and hidden must have the same shape")
+    _lib.call("sb_ple_norm_add", _ptr(proj), _ptr(hidden), _ptr(w_post), float(layer_scalar), _ptr(w_next),
+              _ptr(h_out), _ptr(h16_out), m, n, float(eps), _stream())
+    return hidden
+
+
+def ple_block(hidden: torch.Tensor, ple_in: torch.Tensor, layer: dict, eps: float,
+              w_next: torch.Tensor | None = None, h_out: torch.Tensor | None = None,
+              h16_out: torch.Tensor | None = None) -> torch.Tensor:
+    """One layer's PLE block on ``hidden`` [m, H] in place (gemma4/reference.py:154-163):
+    ``g = gelu_tanh(W_gate @ x) * ple_in``, ``x = (x + rmsnorm(W_proj @ g) * w_post) * scalar``.
+
+    ``ple_in`` is that layer's [m, d] slice of :func:`ple_input`; ``layer``
+    holds ``gate``/``proj`` (codes, row scales) on the device, ``post_norm``
+    and ``scalar``.  Three launches: gate GEMV + GELU * ple, projection GEMV,
+    norm-add tail.
+    """
+    g = gemv_q8(layer["gate"][0], layer["gate"][1], hidden, ple=ple_in)
+    proj = gemv_q8(layer["proj"][0], layer["proj"][1], g)
+    return ple_norm_add(proj, hidden, layer["post_norm"], layer["scalar"], eps, w_next, h_out, h16_out)

@@ -110,6 +110,49 @@ def random_model(cfg: dict | None = None, seed: int = 1234) -> dict:
             "final_norm": final_norm, "layers": layers}
 
 
+def q8_weight(rng: np.random.Generator, n_out: int, n_in: int, lo: float, hi: float) -> tuple[np.ndarray, np.ndarray]:
+    """+128-biased int8 codes ``[n_out, n_in]`` u8 (uniform bytes: values uniform
+    in ``[-128, 127]``) and per-row f32 scales ``[n_out]`` uniform in ``[lo, hi)``."""
+    codes = rng.integers(0, 256, (n_out, n_in), dtype=np.uint8)
+    scale = rng.uniform(lo, hi, n_out).astype(np.float32)
+    return codes, scale
+
+
+def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
+    """Round f32 to bf16 (nearest, ties to even) and return the uint16 bit patterns."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def ple_weights(hidden: int = 1536, n_layers: int = 35, d: int = 256, vocab: int = 262144,
+                seed: int = 2024) -> dict:
+    """Random-init per-layer-embedding weights of the Gemma-4-E2B layout.
+
+    * ``table`` [vocab, n_layers*d/2] u8 4-bit codes with f32 ``table_scale``
+      [vocab, n_layers] (one scale per d values, the checkpoint's blocking),
+      scales ``|N(0, 0.01)|``;
+    * ``proj`` [n_layers*d, hidden] bf16 bit patterns of ``N(0, 0.02)``, ``norm`` [d];
+    * per layer (seed + 1 + L): ``gate`` [d, hidden] and ``proj`` [hidden, d]
+      8-bit weights (row scales sized so the outputs are O(1) for O(1)
+      inputs), ``post_norm`` [hidden] and ``scalar`` uniform in [0.7, 1.3).
+    """
+    rng = np.random.default_rng(seed)
+    cols = n_layers * d
+    table = rng.integers(0, 256, (vocab, cols // 2), dtype=np.uint8)
+    table_scale = np.abs(rng.normal(0.0, 0.01, (vocab, n_layers))).astype(np.float32)
+    proj = f32_to_bf16_bits(rng.normal(0.0, 0.02, (cols, hidden)).astype(np.float32))
+    norm = (1.0 + 0.1 * rng.standard_normal(d, dtype=np.float32)).astype(np.float32)
+    layers = []
+    for li in range(n_layers):
+        r = np.random.default_rng(seed + 1 + li)
+        gate = q8_weight(r, d, hidden, 0.5 / (74.0 * math.sqrt(hidden)), 1.5 / (74.0 * math.sqrt(hidden)))
+        pj = q8_weight(r, hidden, d, 0.5 / (74.0 * math.sqrt(d)), 1.5 / (74.0 * math.sqrt(d)))
+        post = (1.0 + 0.1 * r.standard_normal(hidden, dtype=np.float32)).astype(np.float32)
+        layers.append({"gate": gate, "proj": pj, "post_norm": post, "scalar": float(r.uniform(0.7, 1.3))})
+    return {"hidden": hidden, "n_layers": n_layers, "d": d, "vocab": vocab, "ple_scale": math.sqrt(d),
+            "table": table, "table_scale": table_scale, "proj": proj, "norm": norm, "layers": layers}
+
+
 def prompt_tokens(n: int, vocab: int, seed: int = 99) -> list[int]:
     """Uniform random token ids (the synthetic stand-in for a text prompt)."""
     return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, n)]

@@ -206,6 +206,71 @@ class _RefModel:
         return np.array(toks, np.int64), np.array(margins, np.float32), np.array(top, np.float32)
 
 
+PLE_TOKENS = (3, 77, 511)
+
+
+def ple_cases(out):
+    """The per-layer-embedding path through the reference's ``QATReference``
+    (``ple=True``) on a 2-layer, hidden-1536, d-256 model: its 8-bit linears go
+    through ``QATIndex.dequant_weight`` (bit rule, signed int8 times row scale),
+    its table through ``dequant_embedding_row``, the model projection through
+    the reference's bf16 conversion.  Inputs regenerate from
+    ``synth.random_model(seed=4242)`` and ``synth.ple_weights(seed=4343)``."""
+    import math
+    from gemma4.loader import PREFIX, bf16_to_f32
+    from gemma4.qat_loader import QATIndex
+    from gemma4.qat_reference import QATReference
+    cfg = synth.e2b_config(hidden=1536, n_layers=2, n_heads=2, head_dim=256, inter=512, vocab=512,
+                           rope_cutoff=32)
+    model = synth.random_model(cfg, seed=4242)
+    ple = synth.ple_weights(hidden=1536, n_layers=2, d=256, vocab=512, seed=4343)
+    t = {PREFIX + "embed_tokens_per_layer.embedding_quantized": ple["table"],
+         PREFIX + "embed_tokens_per_layer.embedding_scale": ple["table_scale"],
+         PREFIX + "per_layer_model_projection.weight": bf16_to_f32(ple["proj"]),
+         PREFIX + "per_layer_projection_norm.weight": ple["norm"]}
+    for li, L in enumerate(ple["layers"]):
+        for mod, key in (("per_layer_input_gate", "gate"), ("per_layer_projection", "proj")):
+            codes, scale = L[key]
+            # the checkpoint stores signed int8; the biased codes are code - 128
+            t[f"{PREFIX}layers.{li}.{mod}.weight"] = (codes.astype(np.int16) - 128).astype(np.int8)
+            t[f"{PREFIX}layers.{li}.{mod}.weight_scale"] = scale.reshape(-1, 1)
+        t[f"{PREFIX}layers.{li}.post_per_layer_input_norm.weight"] = L["post_norm"]
+        t[f"{PREFIX}layers.{li}.layer_scalar"] = np.array([L["scalar"]], np.float32)
+    q = QATIndex.__new__(QATIndex)
+    q.idx = _StubIndex(t)
+    q._names = set(t)
+    base = _RefModel(model, 8).ref
+    config = SimpleNamespace(**vars(base.cfg), hidden_size_per_layer_input=256, ple_scale=math.sqrt(256))
+
+    class Ref(QATReference):
+        def _w(self, name):
+            if "per_layer" in name or name.endswith("layer_scalar"):
+                return super()._w(name)
+            return base._w(name)
+
+        def _embed_row(self, token_id):
+            return base._embed_row(token_id)
+
+    ref = Ref(config, q, max_seq=8, ple=True)
+    xs, ples, rows = [], [], []
+    for tok in PLE_TOKENS:
+        x = ref._embed_row(tok) * np.float32(config.embed_scale)
+        xs.append(x)
+        rows.append(ref._ple_table_row(tok).reshape(-1) * np.float32(config.ple_scale))
+        ples.append(ref._ple_input(tok, x))
+    out["ple_ids"] = np.array(PLE_TOKENS, np.int64)
+    out["ple_x"] = np.stack(xs)
+    out["ple_rows"] = np.stack(rows)
+    out["ple_in"] = np.stack(ples)
+    for li in range(2):
+        mids, outs = [], []
+        for j, x in enumerate(xs):
+            mids.append(ref._layer(x, li, j, None))
+            outs.append(ref._layer(x, li, j, ples[j][li]))
+        out[f"ple_l{li}_mid"] = np.stack(mids)
+        out[f"ple_l{li}_out"] = np.stack(outs)
+
+
 def decoder_small(out):
     cfg = synth.e2b_config(hidden=256, n_layers=2, n_heads=2, head_dim=64, inter=512,
                            vocab=2048, rope_cutoff=32)
@@ -248,6 +313,11 @@ def main():
         decoder_small(out)
         np.savez_compressed(os.path.join(HERE, "golden_small.npz"), **out)
         print("wrote golden_small.npz", len(out))
+    if want("ple"):
+        out = {}
+        ple_cases(out)
+        np.savez_compressed(os.path.join(HERE, "golden_ple.npz"), **out)
+        print("wrote golden_ple.npz", len(out))
     if args.full and want("cfg1"):
         out = {}
         gemv_cases({}, full=False)

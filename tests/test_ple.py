@@ -1,0 +1,63 @@
+"""CPU: the per-layer-embedding (PLE) oracle against the reference's own code.
+
+``tests/golden/golden_ple.npz`` comes from tests/golden/make_golden.py, which
+runs the reference's ``QATReference`` (``ple=True``) on a 2-layer hidden-1536
+model: the scaled PLE table rows, ``_ple_input`` and one ``_layer`` call per
+layer with and without the PLE block (``*_mid`` is the layer output before the
+block, ``*_out`` after it).  The weights regenerate from the seeds below.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import ple as ople
+from oracle import q4
+from slang_b200 import synth
+from tests._util import max_rel
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden", "golden_ple.npz")
+EPS = 1e-6
+
+
+@pytest.fixture(scope="module")
+def gp():
+    return np.load(GOLD)
+
+
+@pytest.fixture(scope="module")
+def weights():
+    return synth.ple_weights(hidden=1536, n_layers=2, d=256, vocab=512, seed=4343)
+
+
+def test_gather_matches_reference(gp, weights):
+    rows = ople.ple_gather(gp["ple_ids"], weights["table"], weights["table_scale"], weights["ple_scale"])
+    np.testing.assert_array_equal(rows, gp["ple_rows"])
+
+
+def test_ple_input_matches_reference(gp, weights):
+    got = ople.ple_input(gp["ple_x"], gp["ple_rows"], weights["proj"], weights["norm"], 2, 256, EPS)
+    assert max_rel(got, gp["ple_in"]) < 1e-5
+
+
+@pytest.mark.parametrize("layer", [0, 1])
+def test_ple_block_matches_reference(gp, weights, layer):
+    got = ople.ple_block(gp[f"ple_l{layer}_mid"], gp["ple_in"][:, layer], weights["layers"][layer], EPS)
+    assert max_rel(got, gp[f"ple_l{layer}_out"]) < 1e-5
+
+
+def test_q8_codes_are_biased_int8():
+    # code 0 -> -128, 128 -> 0, 255 -> 127 (gemma4_150/export.py:155-157)
+    codes = np.array([[0, 128, 255, 1]], np.uint8)
+    np.testing.assert_array_equal(q4.unpack_signed(codes, 8), [[-128, 0, 127, -127]])
+    w = q4.dequant_f32(codes, np.array([0.5], np.float32), 8)
+    np.testing.assert_array_equal(w, [[-64.0, 0.0, 63.5, -63.5]])
+
+
+def test_bf16_rounding():
+    a = np.array([1.0, 1.00390625, 1.005859375, -2.5, 3.0e-3], np.float32)
+    bits = synth.f32_to_bf16_bits(a)
+    back = ople.bf16_to_f32(bits)
+    # 1 + 2^-8 is a tie between 1 and 1 + 2^-7: ties to even gives 1.0
+    assert back[0] == 1.0 and back[1] == 1.0 and back[3] == -2.5
+    assert np.all(np.abs(back - a) <= np.abs(a) * 2.0 ** -8)

@@ -22,6 +22,7 @@ constexpr int kWarps = 8;  // warps per CTA of the row GEMV
 constexpr int kMaxM = 8;   // activation rows per GEMV launch
 constexpr int kT = 256;    // threads per CTA of the row kernels
 constexpr int kMaxV4 = 8;  // float4s per thread in the norm tail (n <= 8192)
+constexpr int kU = 8;      // 16-byte weight chunks a GEMV lane has in flight
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -79,10 +80,11 @@ struct FmtBF16 {
 
 // y[r, o] = epi(sum_k W[o, k] * x[r, k] * scale(o)),  scale(o) = row_scale[o] * alpha
 // (row_scale may be null), epi(v) = v, or gelu_tanh(v) * ple[r * ld_ple + o].
-// A group of G lanes owns one output row and walks its 16-byte chunks with a
-// stride of G (four chunks in flight per lane); the first chunks are loaded
-// before the dependency wait so that they overlap the previous kernel's tail.
-template <class Fmt, int G>
+// A group of G lanes owns one output row; each lane issues all of its (up to
+// kU) 16-byte chunks of the row at once, the first pass before the dependency
+// wait so that the weight reads overlap the previous kernel's tail.  M is the
+// activation-row count rounded up to a power of two (m <= M rows are live).
+template <class Fmt, int G, int M>
 __global__ void __launch_bounds__(kWarps * 32) gemv_rows_kernel(const uint8_t* __restrict__ w, int64_t w_ld,
                                                              const float* __restrict__ row_scale, float alpha,
                                                              const float* __restrict__ x, int ldx, int m, int n,
@@ -90,41 +92,32 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_rows_kernel(const uint8_t* _
                                                              float* __restrict__ y, int ldy) {
   sbd::griddep_launch_dependents();
   constexpr int kRowsPerWarp = 32 / G;
-  constexpr int U = 4;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gl = lane % G;
-  const int o = (blockIdx.x * kWarps + warp) * kRowsPerWarp + lane / G;
+  const int o = (blockIdx.x * static_cast<int>(blockDim.x >> 5) + warp) * kRowsPerWarp + lane / G;
   const bool valid = o < n;
   const int nch = k / Fmt::kVals;
   const uint8_t* row = w + static_cast<int64_t>(valid ? o : 0) * w_ld;
 
-  uint4 wv[U];
-  auto load = [&](int c0) {
+  float acc[M];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
+  for (int r = 0; r < M; ++r) acc[r] = 0.f;
+  for (int c0 = 0; c0 < nch; c0 += kU * G) {
+    uint4 wv[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
       const int c = c0 + u * G + gl;
       wv[u] = (valid && c < nch) ? ldg_stream(row + 16 * static_cast<int64_t>(c)) : make_uint4(0u, 0u, 0u, 0u);
     }
-  };
-  float acc[kMaxM];
+    if (c0 == 0) sbd::griddep_wait();
 #pragma unroll
-  for (int r = 0; r < kMaxM; ++r) acc[r] = 0.f;
-
-  load(0);
-  sbd::griddep_wait();
-  for (int c0 = 0; c0 < nch; c0 += U * G) {
-    uint4 cur[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) cur[u] = wv[u];
-    if (c0 + U * G < nch) load(c0 + U * G);
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int c = c0 + u * G + gl;
       if (c < nch) {
         float v[Fmt::kVals];
-        Fmt::decode(cur[u], v);
+        Fmt::decode(wv[u], v);
 #pragma unroll
-        for (int r = 0; r < kMaxM; ++r) {
+        for (int r = 0; r < M; ++r) {
           if (r < m) {
             const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(r) * ldx) +
                                c * (Fmt::kVals / 4);
@@ -142,14 +135,14 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_rows_kernel(const uint8_t* _
     }
   }
 #pragma unroll
-  for (int r = 0; r < kMaxM; ++r) {
+  for (int r = 0; r < M; ++r) {
 #pragma unroll
     for (int off = G / 2; off > 0; off >>= 1) acc[r] += __shfl_xor_sync(0xFFFFFFFFu, acc[r], off);
   }
   if (valid && gl == 0) {
     const float s = row_scale ? row_scale[o] * alpha : alpha;
 #pragma unroll
-    for (int r = 0; r < kMaxM; ++r) {
+    for (int r = 0; r < M; ++r) {
       if (r < m) {
         float v = acc[r] * s;
         if (ple) v = sbd::gelu_tanh(v) * ple[static_cast<int64_t>(r) * ld_ple + o];
@@ -300,14 +293,31 @@ __global__ void __launch_bounds__(kT) ple_combine_kernel(const float* __restrict
   }
 }
 
+template <class Fmt, int G>
+cudaError_t launch_gemv_m(int mm, dim3 grid, dim3 block, cudaStream_t st, const uint8_t* w, int64_t w_ld,
+                          const float* row_scale, float alpha, const float* x, int ldx, int n, int k, const float* ple,
+                          int ld_ple, float* y, int ldy) {
+#define SB_GEMV(MM)                                                                                                  \
+  return sb::launch_pdl(gemv_rows_kernel<Fmt, G, MM>, grid, block, 0, st, w, w_ld, row_scale, alpha, x, ldx, mm, n, k, \
+                        ple, ld_ple, y, ldy)
+  if (mm == 1) SB_GEMV(1);
+  if (mm == 2) SB_GEMV(2);
+  if (mm <= 4) SB_GEMV(4);
+  SB_GEMV(8);
+#undef SB_GEMV
+}
+
 template <class Fmt>
 cudaError_t launch_gemv_rows(const uint8_t* w, int64_t w_ld, const float* row_scale, float alpha, const float* x,
                              int ldx, int m, int n, int k, const float* ple, int ld_ple, float* y, int ldy,
                              cudaStream_t st) {
   const int nch = k / Fmt::kVals;
   const int G = nch >= 32 ? 32 : nch >= 16 ? 16 : nch >= 8 ? 8 : 4;
-  const int rows_per_cta = kWarps * (32 / G);
-  const dim3 grid((n + rows_per_cta - 1) / rows_per_cta), block(kWarps * 32);
+  // warps per CTA: 8, fewer when a short matrix would otherwise leave SMs idle
+  const int row_warps = (n + 32 / G - 1) / (32 / G);
+  int wpc = kWarps;
+  while (wpc > 1 && (row_warps + wpc - 1) / wpc < 2 * sb::num_sms()) wpc >>= 1;
+  const dim3 grid((row_warps + wpc - 1) / wpc), block(wpc * 32);
   cudaError_t e = cudaSuccess;
   for (int r0 = 0; r0 < m && e == cudaSuccess; r0 += kMaxM) {
     const int mm = m - r0 < kMaxM ? m - r0 : kMaxM;
@@ -315,22 +325,10 @@ cudaError_t launch_gemv_rows(const uint8_t* w, int64_t w_ld, const float* row_sc
     const float* pr = ple ? ple + static_cast<int64_t>(r0) * ld_ple : nullptr;
     float* yr = y + static_cast<int64_t>(r0) * ldy;
     switch (G) {
-      case 32:
-        e = sb::launch_pdl(gemv_rows_kernel<Fmt, 32>, grid, block, 0, st, w, w_ld, row_scale, alpha, xr, ldx, mm, n,
-                           k, pr, ld_ple, yr, ldy);
-        break;
-      case 16:
-        e = sb::launch_pdl(gemv_rows_kernel<Fmt, 16>, grid, block, 0, st, w, w_ld, row_scale, alpha, xr, ldx, mm, n,
-                           k, pr, ld_ple, yr, ldy);
-        break;
-      case 8:
-        e = sb::launch_pdl(gemv_rows_kernel<Fmt, 8>, grid, block, 0, st, w, w_ld, row_scale, alpha, xr, ldx, mm, n, k,
-                           pr, ld_ple, yr, ldy);
-        break;
-      default:
-        e = sb::launch_pdl(gemv_rows_kernel<Fmt, 4>, grid, block, 0, st, w, w_ld, row_scale, alpha, xr, ldx, mm, n, k,
-                           pr, ld_ple, yr, ldy);
-        break;
+      case 32: e = launch_gemv_m<Fmt, 32>(mm, grid, block, st, w, w_ld, row_scale, alpha, xr, ldx, n, k, pr, ld_ple, yr, ldy); break;
+      case 16: e = launch_gemv_m<Fmt, 16>(mm, grid, block, st, w, w_ld, row_scale, alpha, xr, ldx, n, k, pr, ld_ple, yr, ldy); break;
+      case 8: e = launch_gemv_m<Fmt, 8>(mm, grid, block, st, w, w_ld, row_scale, alpha, xr, ldx, n, k, pr, ld_ple, yr, ldy); break;
+      default: e = launch_gemv_m<Fmt, 4>(mm, grid, block, st, w, w_ld, row_scale, alpha, xr, ldx, n, k, pr, ld_ple, yr, ldy); break;
     }
   }
   return e;

@@ -154,6 +154,9 @@ def run_kernel_case(args):
                        "proj": (torch.randint(0, 256, (1536, 256), dtype=torch.uint8, device=dev, generator=g),
                                 torch.full((1536,), 1e-3, device=dev)),
                        "post_norm": torch.ones(1536, device=dev), "scalar": 1.0} for _ in range(copies)]
+            if m > kern.PLE_GEMV_ROWS:  # the GEMM route's f16 weights are made once per layer, not timed
+                for layer in layers:
+                    kern.ple_block(x.clone(), ple_in, layer, 1e-6)
         else:
             ws = [torch.randint(0, 256, (n, k * esz), dtype=torch.uint8, device=dev, generator=g)
                   for _ in range(copies)]

@@ -176,6 +176,12 @@ int sb_gemm_f16(const void* a, const void* b, void* c, int m, int n, int k, floa
 int sb_gemm_f16_f32out(const void* a, const void* b, float* c, int m, int n, int k, float alpha,
                        int tr, int lda, int ldb, int ldc, void* stream);
 
+/* The same product split into `splits` equal runs of 64-deep K blocks (splits
+ * divides ceil(k / 64)); split z writes its partial product to the f32 plane
+ * c + z * m * ldc, and the consumer sums the planes (sb_ple_gate_act). */
+int sb_gemm_f16_f32out_splitk(const void* a, const void* b, float* c, int m, int n, int k, float alpha,
+                              int tr, int lda, int ldb, int ldc, int splits, void* stream);
+
 /*
  * Fused prefill projection: dequantise packed int4 tiles into shared memory
  * and feed them to tcgen05 MMAs, f32 accumulate in tensor memory:
@@ -429,6 +435,18 @@ int sb_ple_gather(const int32_t* ids, const void* table, const float* scales, in
 int sb_ple_combine(const float* ctx, const int32_t* ids, const void* table, const float* scales,
                    int vocab, const float* w_norm, int n_layers, int d, int group, float ple_scale,
                    float eps, float* out, int m, void* stream);
+
+/* out16[r][o] = f16(gelu_tanh(sum_z pre[z*plane + r*ld_pre + o]) * ple[r][o]),
+ * z < nsplit (the K-split planes of sb_gemm_f16_f32out_splitk), r < m, o < n:
+ * the gate tail once the gate is a GEMM at prefill, feeding the projection
+ * GEMM.  Replaces plegate's GEMM tail (gemma4_150/kernels_dsl.py:1775) without
+ * its SRQ step. */
+int sb_ple_gate_act(const float* pre, int ld_pre, int64_t plane, int nsplit, const float* ple, int ld_ple,
+                    void* out16, int ld_out, int m, int n, void* stream);
+
+/* out16[i] = f16(x[i]) (round to nearest even), i < n: the f16 A operand of a
+ * prefill GEMM taken from an f32 residual stream. */
+int sb_cast_f16(const float* x, void* out16, int64_t n, void* stream);
 
 #ifdef __cplusplus
 }

@@ -61,6 +61,9 @@ SIGNATURES = {
     "sb_ple_norm_add": ([_vp, _vp, _vp, _f, _vp, _vp, _vp, _i, _i, _f, _vp], _i),
     "sb_ple_gather": ([_vp, _vp, _vp, _i, _i, _i, _f, _vp, _i, _vp], _i),
     "sb_ple_combine": ([_vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _f, _f, _vp, _i, _vp], _i),
+    "sb_ple_gate_act": ([_vp, _i, _i64, _i, _vp, _i, _vp, _i, _i, _i, _vp], _i),
+    "sb_gemm_f16_f32out_splitk": ([_vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _i, _i, _i, _vp], _i),
+    "sb_cast_f16": ([_vp, _vp, _i64, _vp], _i),
     "sb_decode_step_fused": ([_vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _f, _vp, _vp, _vp,
                               _vp, _i, _vp, _vp, _sz, _vp], _i),
     "sb_decode_step_fused_scratch_size": ([_i, _i, _i, _i, _i], _sz),

@@ -97,6 +97,7 @@ struct GemmParams {
   long long row_offset;
   int bits;            // packed-weight code width: 4 (two per byte) or 2 (four per byte)
   float alpha;
+  long long plane;     // f16 kernel, f32 C: elements between the output planes of K splits (blockIdx.z)
 };
 
 struct Bars {
@@ -256,10 +257,18 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
         sbd::tmem_wait_ld();
         if (!row_ok) continue;
         if (p.c_f32) {
-          float* dst = static_cast<float*>(p.c) + static_cast<size_t>(row) * p.ldc + col0;
+          float* dst = static_cast<float*>(p.c) + blockIdx.z * p.plane + static_cast<size_t>(row) * p.ldc + col0;
+          if (col0 + 32 <= p.n && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < p.n) dst[j] = p.alpha * __uint_as_float(r[j]);
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(dst + j) =
+                  make_float4(p.alpha * __uint_as_float(r[j]), p.alpha * __uint_as_float(r[j + 1]),
+                              p.alpha * __uint_as_float(r[j + 2]), p.alpha * __uint_as_float(r[j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.n) dst[j] = p.alpha * __uint_as_float(r[j]);
+          }
           continue;
         }
         __half* dst = static_cast<__half*>(p.c) + static_cast<size_t>(row) * p.ldc + col0;
@@ -1044,7 +1053,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cu
   static bool done[64] = {false};
   int rc = set_smem(gemm_tc_kernel<MODE>, C::kSmem, done);
   if (rc) return rc;
-  dim3 grid((p.n + BN - 1) / BN, (p.m + BM - 1) / BM, 1);
+  dim3 grid((p.n + BN - 1) / BN, (p.m + BM - 1) / BM, (p.kb_total + p.kb_per_split - 1) / p.kb_per_split);
   gemm_tc_kernel<MODE><<<grid, C::kThreads, C::kSmem, s>>>(ta, tb, p);
   return sb::launch_status("gemm_tc_kernel");
 }
@@ -1150,7 +1159,7 @@ extern "C" size_t sb_gemm_q4_workspace_size(int m, int n, int k) {
 }
 
 static int gemm_f16_impl(const void* a, const void* b, void* c, int c_f32, int m, int n, int k, float alpha, int tr,
-                         int lda, int ldb, int ldc, void* stream) {
+                         int lda, int ldb, int ldc, void* stream, int splits = 1) {
   SB_CHECK_ARG(m >= 0 && n >= 0 && k >= 0, "sb_gemm_f16: negative shape");
   if (m == 0 || n == 0) return SB_OK;
   SB_CHECK_ARG(a && b && c, "sb_gemm_f16: null pointer");
@@ -1183,7 +1192,8 @@ static int gemm_f16_impl(const void* a, const void* b, void* c, int c_f32, int m
   p.ldc = ldc;
   p.alpha = alpha;
   p.kb_total = (k + BK - 1) / BK;
-  p.kb_per_split = p.kb_total;
+  p.kb_per_split = (p.kb_total + splits - 1) / splits;
+  p.plane = static_cast<long long>(m) * ldc;
   return tr ? launch<MODE_F16_KMAJOR>(ta, tb, p, s) : launch<MODE_F16_MNMAJOR>(ta, tb, p, s);
 }
 
@@ -1196,6 +1206,15 @@ extern "C" int sb_gemm_f16_f32out(const void* a, const void* b, float* c, int m,
                                   int lda, int ldb, int ldc, void* stream) {
   if (c && !sb::aligned(c, 4)) return sb::fail(SB_ERR_ALIGN, "sb_gemm_f16_f32out: C must be 4-byte aligned");
   return gemm_f16_impl(a, b, c, 1, m, n, k, alpha, tr, lda, ldb, ldc, stream);
+}
+
+extern "C" int sb_gemm_f16_f32out_splitk(const void* a, const void* b, float* c, int m, int n, int k, float alpha,
+                                         int tr, int lda, int ldb, int ldc, int splits, void* stream) {
+  SB_CHECK_ARG(splits >= 1 && k > 0 && splits <= (k + BK - 1) / BK,
+               "sb_gemm_f16_f32out_splitk: splits=%d must be in 1..ceil(k/%d)", splits, BK);
+  SB_CHECK_ARG(((k + BK - 1) / BK) % splits == 0, "sb_gemm_f16_f32out_splitk: splits must divide ceil(k/%d)", BK);
+  if (c && !sb::aligned(c, 4)) return sb::fail(SB_ERR_ALIGN, "sb_gemm_f16_f32out_splitk: C must be 4-byte aligned");
+  return gemm_f16_impl(a, b, c, 1, m, n, k, alpha, tr, lda, ldb, ldc, stream, splits);
 }
 
 // Raises the pair kernel's shared-memory limit once per (instantiation, device)

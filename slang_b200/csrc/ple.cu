@@ -293,6 +293,39 @@ __global__ void __launch_bounds__(kT) ple_combine_kernel(const float* __restrict
   }
 }
 
+// out16[r, o] = f16(gelu_tanh(sum_z pre[z][r, o]) * ple[r, o]): the gate tail
+// once the gate is a GEMM (prefill) whose K splits wrote `nsplit` f32 planes
+// `plane` elements apart, producing the f16 operand of the projection GEMM.
+__global__ void __launch_bounds__(kT) ple_gate_act_kernel(const float* __restrict__ pre, int ld_pre, int64_t plane,
+                                                        int nsplit, const float* __restrict__ ple, int ld_ple,
+                                                        __half* out16, int ld_out, int m, int n) {
+  sbd::griddep_launch_dependents();
+  sbd::griddep_wait();
+  const int64_t total = static_cast<int64_t>(m) * n;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kT) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kT) {
+    const int64_t r = i / n;
+    const int o = static_cast<int>(i - r * n);
+    float acc = pre[r * ld_pre + o];
+    for (int z = 1; z < nsplit; ++z) acc += pre[z * plane + r * ld_pre + o];
+    const float v = sbd::gelu_tanh(acc) * ple[r * ld_ple + o];
+    out16[r * ld_out + o] = __float2half_rn(v);
+  }
+}
+
+__global__ void __launch_bounds__(kT) cast_f16_kernel(const float* __restrict__ x, __half* out, int64_t n) {
+  sbd::griddep_launch_dependents();
+  sbd::griddep_wait();
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kT) + threadIdx.x; i < n; i += static_cast<int64_t>(gridDim.x) * kT)
+    out[i] = __float2half_rn(x[i]);
+}
+
+int grid_for(int64_t total) {
+  const int64_t want = (total + kT - 1) / kT;
+  const int64_t cap = 8 * static_cast<int64_t>(sb::num_sms());
+  return static_cast<int>(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
 template <class Fmt, int G>
 cudaError_t launch_gemv_m(int mm, dim3 grid, dim3 block, cudaStream_t st, const uint8_t* w, int64_t w_ld,
                           const float* row_scale, float alpha, const float* x, int ldx, int n, int k, const float* ple,
@@ -408,4 +441,28 @@ extern "C" int sb_ple_combine(const float* ctx, const int32_t* ids, const void* 
                                  vocab, w_norm, m, n_layers, d, group, ple_scale, eps, out);
   if (e != cudaSuccess) return sb::cuda_fail(e, "ple_combine_kernel");
   return sb::launch_status("ple_combine_kernel");
+}
+
+extern "C" int sb_ple_gate_act(const float* pre, int ld_pre, int64_t plane, int nsplit, const float* ple, int ld_ple,
+                               void* out16, int ld_out, int m, int n, void* stream) {
+  SB_CHECK_ARG(m >= 0 && n > 0 && ld_pre >= n && ld_ple >= n && ld_out >= n && nsplit >= 1 &&
+                   (nsplit == 1 || plane >= static_cast<int64_t>(m) * ld_pre),
+               "sb_ple_gate_act: bad shape");
+  if (m == 0) return SB_OK;
+  SB_CHECK_ARG(pre && ple && out16, "sb_ple_gate_act: null pointer");
+  cudaError_t e = sb::launch_pdl(ple_gate_act_kernel, dim3(grid_for(static_cast<int64_t>(m) * n)), dim3(kT), 0,
+                                 static_cast<cudaStream_t>(stream), pre, ld_pre, plane, nsplit, ple, ld_ple,
+                                 static_cast<__half*>(out16), ld_out, m, n);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "ple_gate_act_kernel");
+  return sb::launch_status("ple_gate_act_kernel");
+}
+
+extern "C" int sb_cast_f16(const float* x, void* out16, int64_t n, void* stream) {
+  SB_CHECK_ARG(n >= 0, "sb_cast_f16: negative size");
+  if (n == 0) return SB_OK;
+  SB_CHECK_ARG(x && out16, "sb_cast_f16: null pointer");
+  cudaError_t e = sb::launch_pdl(cast_f16_kernel, dim3(grid_for(n)), dim3(kT), 0, static_cast<cudaStream_t>(stream), x,
+                                 static_cast<__half*>(out16), n);
+  if (e != cudaSuccess) return sb::cuda_fail(e, "cast_f16_kernel");
+  return sb::launch_status("cast_f16_kernel");
 }

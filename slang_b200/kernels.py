@@ -387,9 +387,45 @@ def ple_block(hidden: torch.Tensor, ple_in: torch.Tensor, layer: dict, eps: floa
 
     ``ple_in`` is that layer's [m, d] slice of :func:`ple_input`; ``layer``
     holds ``gate``/``proj`` (codes, row scales) on the device, ``post_norm``
-    and ``scalar``.  Three launches: gate GEMV + GELU * ple, projection GEMV,
-    norm-add tail.
+    and ``scalar``.  Up to ``PLE_GEMV_ROWS`` rows (decode): three launches,
+    gate GEMV + GELU * ple, projection GEMV, norm-add tail, all f32.  More rows
+    (prefill): the two linears run as tcgen05 GEMMs on f16 operands (the 8-bit
+    weights dequantised to f16 once, cached in ``layer`` as ``gate16`` /
+    ``proj16``), as the reference's prefill does (gemma4_150/kernels_dsl.py:1775).
     """
-    g = gemv_q8(layer["gate"][0], layer["gate"][1], hidden, ple=ple_in)
-    proj = gemv_q8(layer["proj"][0], layer["proj"][1], g)
+    m, H = hidden.shape
+    if m <= PLE_GEMV_ROWS:
+        g = gemv_q8(layer["gate"][0], layer["gate"][1], hidden, ple=ple_in)
+        proj = gemv_q8(layer["proj"][0], layer["proj"][1], g)
+    else:
+        d = layer["gate"][0].shape[0]
+        if "gate16" not in layer:
+            layer["gate16"] = dequant_f16(layer["gate"][0], layer["gate"][1].reshape(-1), H, d, bits=8)
+            layer["proj16"] = dequant_f16(layer["proj"][0], layer["proj"][1].reshape(-1), d, H, bits=8)
+        dev = hidden.device
+        x16 = torch.empty(m, H, dtype=torch.float16, device=dev)
+        _lib.call("sb_cast_f16", _ptr(hidden), _ptr(x16), m * H, _stream())
+        # the gate's output is one or two 128 x 256 tiles wide: split K so the GEMM covers the SMs
+        kbs, tiles = -(-H // 64), -(-m // 128) * -(-d // 256)
+        splits = max(z for z in range(1, 9) if kbs % z == 0 and (z == 1 or tiles * z <= _num_sms(dev)))
+        pre = torch.empty(splits, m, d, dtype=torch.float32, device=dev)
+        _lib.call("sb_gemm_f16_f32out_splitk", _ptr(x16), _ptr(layer["gate16"]), _ptr(pre), m, d, H, 1.0, 1, H, H,
+                  d, splits, _stream())
+        g16 = torch.empty(m, d, dtype=torch.float16, device=dev)
+        _lib.call("sb_ple_gate_act", _ptr(pre), d, m * d, splits, _ptr(ple_in), _rows(ple_in, "ple_in", d),
+                  _ptr(g16), d, m, d, _stream())
+        proj = torch.empty(m, H, dtype=torch.float32, device=dev)
+        _lib.call("sb_gemm_f16_f32out", _ptr(g16), _ptr(layer["proj16"]), _ptr(proj), m, H, d, 1.0, 1, d, d, H,
+                  _stream())
     return ple_norm_add(proj, hidden, layer["post_norm"], layer["scalar"], eps, w_next, h_out, h16_out)
+
+
+PLE_GEMV_ROWS = 16
+_SMS: dict = {}
+
+
+def _num_sms(dev) -> int:
+    key = str(dev)
+    if key not in _SMS:
+        _SMS[key] = torch.cuda.get_device_properties(dev).multi_processor_count
+    return _SMS[key]

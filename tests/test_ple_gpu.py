@@ -154,3 +154,69 @@ def test_ple_full_shapes_vs_oracle(cuda):
         torch.cuda.synchronize()
         ref = ople.ple_block(x, ref_in[:, li], w["layers"][li], EPS)
         assert max_rel(hid.cpu().numpy(), ref) < 1e-4
+
+
+@pytest.mark.parametrize("m", [17, 64, 1024])
+def test_ple_block_prefill_gemm_route(cuda, m):
+    """More than PLE_GEMV_ROWS rows: f16 dequant + tcgen05 GEMMs with f32
+    output, the gate tail and the norm-add tail.  f16 operands: the block's
+    added term (rmsnorm(proj) * w_post) within the matmul tolerance
+    (max-rel 1e-2, cosine 0.9999) of the f32 oracle."""
+    from tests._util import assert_close
+    assert m > kern.PLE_GEMV_ROWS
+    w = synth.ple_weights(hidden=1536, n_layers=2, d=256, vocab=64, seed=41)
+    rng = np.random.default_rng(42 + m)
+    x = (4 * rng.standard_normal((m, 1536))).astype(np.float32)
+    ple_in = rng.standard_normal((m, 2, 256), dtype=np.float32)
+    L = w["layers"][1]
+    ref = ople.ple_block(x, ple_in[:, 1], L, EPS)
+    hid = T(x, cuda)
+    dl = _dev_layer(L, cuda)
+    kern.ple_block(hid, T(ple_in, cuda)[:, 1], dl, EPS)
+    torch.cuda.synchronize()
+    got = hid.cpu().numpy()
+    s = np.float32(L["scalar"])
+    assert_close(got / s - x, ref / s - x, what="PLE block added term")
+    assert max_rel(got, ref) < 1e-2
+    assert "gate16" in dl and dl["gate16"].dtype == torch.float16
+
+
+def test_ple_gate_act_and_cast(cuda):
+    rng = np.random.default_rng(51)
+    m, n = 33, 256
+    pre = (3 * rng.standard_normal((m, n))).astype(np.float32)
+    ple = rng.standard_normal((m, 2 * n), dtype=np.float32)
+    out = torch.empty(m, n, dtype=torch.float16, device=cuda)
+    P = T(ple, cuda)
+    # two K-split planes: pre = a + b
+    a = (0.25 * pre).astype(np.float32)
+    PL = T(np.stack([a, pre - a]), cuda)
+    _lib.call("sb_ple_gate_act", PL.data_ptr(), n, m * n, 2, P.data_ptr(), 2 * n, out.data_ptr(), n, m, n,
+              torch.cuda.current_stream().cuda_stream)
+    x16 = torch.empty(m, n, dtype=torch.float16, device=cuda)
+    X = T(pre, cuda)
+    _lib.call("sb_cast_f16", X.data_ptr(), x16.data_ptr(), m * n, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ref = odec.gelu_tanh(a + (pre - a)) * ple[:, :n]
+    assert max_rel(out.float().cpu().numpy(), ref) < 1e-3
+    np.testing.assert_array_equal(x16.cpu().numpy(), pre.astype(np.float16))
+
+
+@pytest.mark.parametrize("m,n,k,splits", [(1024, 256, 1536, 8), (64, 256, 1536, 3), (200, 300, 512, 4), (130, 1536, 256, 1)])
+def test_gemm_f16_f32out_splitk(cuda, m, n, k, splits):
+    """Each K split writes its own f32 plane; the planes sum to the full product."""
+    g = torch.Generator(device=cuda)
+    g.manual_seed(m + n + k)
+    a = torch.randn(m, k, device=cuda, generator=g).half()
+    b = torch.randn(n, k, device=cuda, generator=g).half()
+    c = torch.full((splits, m, n), float("nan"), device=cuda)
+    _lib.call("sb_gemm_f16_f32out_splitk", a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, 0.5, 1, k, k, n,
+              splits, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ref = 0.5 * (a.double() @ b.double().T)
+    got = c.double().sum(0)
+    assert torch.isfinite(got).all()
+    assert ((got - ref).abs().max() / ref.abs().max()).item() < 1e-5
+    with pytest.raises(_lib.SlangError):  # 5 does not divide ceil(k / 64)
+        _lib.call("sb_gemm_f16_f32out_splitk", a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, 0.5, 1, k, k, n,
+                  5 if (k // 64) % 5 else 7, torch.cuda.current_stream().cuda_stream)

@@ -52,7 +52,12 @@ def apply_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
 
 
 class OracleDecoder:
-    """Single-position forward with a KV cache (gemma4/reference.py:59-182, ple=False)."""
+    """Single-position forward with a KV cache (gemma4/reference.py:59-182).
+
+    Without a ``"ple"`` entry in the model this is ``ple=False``; with one (the
+    dict of ``slang_b200.synth.ple_weights``) every layer ends with the
+    per-layer-embedding block of gemma4/reference.py:154-163, fed by
+    ``_ple_input`` (:92-101), as ``oracle.ple`` restates them."""
 
     def __init__(self, model: dict, max_seq: int) -> None:
         cfg = model["config"]
@@ -115,12 +120,19 @@ class OracleDecoder:
 
     def forward(self, token: int, pos: int, hiddens: list | None = None) -> np.ndarray:
         """Logits for one token at ``pos`` (gemma4/reference.py:165-182)."""
+        from . import ple as ople
         cfg = self.cfg
         x = q4.dequant_f32(self.model["embed_q"][token:token + 1],
                            self.model["embed_scale"][token:token + 1], 4)[0]
         x = x * np.float32(cfg["embed_scale"])
+        P = self.model.get("ple")
+        if P is not None:
+            rows = ople.ple_gather(np.array([token]), P["table"], P["table_scale"], P["ple_scale"])
+            ple_in = ople.ple_input(x, rows, P["proj"], P["norm"], cfg["n_layers"], P["d"], cfg["eps"])[0]
         for li in range(cfg["n_layers"]):
             x = self.layer(x, li, pos)
+            if P is not None:
+                x = ople.ple_block(x[None], ple_in[li][None], P["layers"][li], cfg["eps"])[0]
             if hiddens is not None:
                 hiddens.append(x.copy())
         x = rms_norm(x, self.model["final_norm"], cfg["eps"])

@@ -83,6 +83,19 @@ class DeviceModel:
             self.layers.append(d)
         cos, sin = rope_tables(max_seq, cfg["head_dim"], cfg["rope_theta"], cfg["rope_cutoff"])
         self.cos, self.sin = T(cos), T(sin)
+        # per-layer embeddings (the dict of synth.ple_weights), when the model has them
+        self.ple = None
+        P = model.get("ple")
+        if P is not None:
+            proj = T(P["proj"].view(np.int16))
+            self.ple = {"table": T(P["table"]), "table_scale": T(P["table_scale"], torch.float32), "proj": proj,
+                        # f16 copy of the bf16 model projection for the prefill GEMM (made once, at load)
+                        "proj16": proj.view(torch.bfloat16).to(torch.float16),
+                        "norm": T(P["norm"], torch.float32), "scale": float(P["ple_scale"]), "d": int(P["d"])}
+            for d, PL in zip(self.layers, P["layers"]):
+                d["ple"] = {"gate": (T(PL["gate"][0]), T(PL["gate"][1], torch.float32)),
+                            "proj": (T(PL["proj"][0]), T(PL["proj"][1], torch.float32)),
+                            "post_norm": T(PL["post_norm"], torch.float32), "scalar": float(PL["scalar"])}
 
 
 class Runner:
@@ -104,6 +117,8 @@ class Runner:
             raise ValueError("the GEMV decode path serves 1..8 sequences, the GEMM path 1..%d" % self.MAX_BATCH)
         if fused and batch != 1:
             raise ValueError("the persistent decode kernel serves one sequence")
+        if dm.ple is not None and (fused or proj != "gemv"):
+            raise ValueError("per-layer embeddings run on the per-op GEMV decode path (fused=False, proj='gemv')")
         self.proj = proj
         self.fused = fused
         self.dm = dm
@@ -126,6 +141,10 @@ class Runner:
         self.qkv, self.q = f32(B, self.nqkv), f32(B, self.qd)
         self.attn, self.o = f32(B, self.qd), f32(B, H)
         self.gu, self.a, self.d = f32(B, 2 * self.F), f32(B, self.F), f32(B, H)
+        if dm.ple is not None:
+            pd = dm.ple["d"]
+            self.ple_in, self.ple_ctx = f32(B, nL, pd), f32(B, nL * pd)
+            self.ple_g, self.ple_proj = f32(B, pd), f32(B, H)
         if proj == "gemm":
             f16 = lambda *s: torch.zeros(s, dtype=torch.float16, device=dev)  # noqa: E731
             self.h16, self.qkv16, self.attn16 = f16(B, H), f16(B, self.nqkv), f16(B, self.qd)
@@ -196,6 +215,10 @@ class Runner:
         B, H = self.B, self.H
         _lib.call("sb_embed_q4", dm.embed_q.data_ptr(), dm.embed_s.data_ptr(), _F16, dm.cfg["group"],
                   self.cur.data_ptr(), B, H, float(dm.cfg["embed_scale"]), self.x.data_ptr(), None, s)
+        P = dm.ple
+        if P is not None:  # per-layer inputs from the scaled embedding (gemma4/reference.py:170)
+            kern.ple_input(self.x, self.cur, P["table"], P["table_scale"], P["proj"], P["norm"], len(L0), P["d"],
+                           self.eps, P["scale"], out=self.ple_in, ctx=self.ple_ctx)
         _lib.call("sb_add_rmsnorm", self.x.data_ptr(), None, _F32, None, L0[0]["in_norm"].data_ptr(),
                   self.x.data_ptr(), self.h.data_ptr(), None, B, H, self.eps, s)
         for li, L in enumerate(L0):
@@ -216,6 +239,12 @@ class Runner:
             nxt = L0[li + 1]["in_norm"] if li + 1 < len(L0) else dm.final_norm
             _lib.call("sb_add_rmsnorm", self.x.data_ptr(), self.d.data_ptr(), _F32, L["post_ffn_norm"].data_ptr(),
                       nxt.data_ptr(), self.x.data_ptr(), self.h.data_ptr(), None, B, H, self.eps, s)
+            if P is not None:  # PLE block, then the next norm from its output (gemma4/reference.py:154-163)
+                Lp = L["ple"]
+                kern.gemv_q8(Lp["gate"][0], Lp["gate"][1], self.x, out=self.ple_g, ple=self.ple_in[:, li])
+                kern.gemv_q8(Lp["proj"][0], Lp["proj"][1], self.ple_g, out=self.ple_proj)
+                kern.ple_norm_add(self.ple_proj, self.x, Lp["post_norm"], Lp["scalar"], self.eps, w_next=nxt,
+                                  h_out=self.h)
         kern.lmhead_argmax(dm.embed_q, dm.embed_s, self.h, keys=self.keys, tokens=self.tok)
         _lib.call("sb_step_advance", self.pos.data_ptr(), self.tok.data_ptr(), self.cur.data_ptr(),
                   self.history.data_ptr(), self.max_seq, B, s)
@@ -257,7 +286,8 @@ class Runner:
                          + 1 + 2 + 2)  # prep, attention (2), add+norm (2)
             return 2 + nL * per_layer + 2 + 1  # embed + norm, layers, argmax GEMM + tokens, advance
         per_layer = 4 + 1 + 2 + 2 + 1  # 4 GEMVs, prep, attention (2), add+norm (2), geglu
-        return 2 + nL * per_layer + 2 + 1  # embed + first norm, layers, lm_head (gemv + tokens), advance
+        ple = 0 if self.dm.ple is None else 2 + 3 * nL  # PLE input (GEMV + combine); per layer 2 GEMVs + tail
+        return 2 + nL * per_layer + 2 + 1 + ple  # embed + first norm, layers, lm_head (gemv + tokens), advance
 
     def capture(self):
         """Warm up, then capture one decode step as a CUDA graph."""
@@ -326,6 +356,9 @@ class Runner:
         ws = max(kern.gemm_q4_workspace_size(S, n, k) for n, k in
                  ((self.nqkv, H), (H, self.qd), (2 * F, H), (H, F)))
         pf["ws"] = torch.empty(max(1, ws // 4), dtype=torch.float32, device=dev)
+        if self.dm.ple is not None:
+            pd, nL = self.dm.ple["d"], len(self.dm.layers)
+            pf["ple_x16"], pf["ple_ctx"], pf["ple_in"] = f16(S, H), f32(S, nL * pd), f32(S, nL, pd)
         aws = _lib.load().sb_attn_prefill_workspace_size(S, nh, hd)
         pf["attn_ws"] = torch.empty(max(4, aws // 4), dtype=torch.float32, device=dev)
         self._pf = pf
@@ -384,7 +417,10 @@ class Runner:
                      + 1 + 1 + 2)  # prep; attention; two add+norms (GEGLU is in the gate|up GEMM)
         if _lib.load().sb_attn_prefill_workspace_size(S, self.nh, self.hd):
             per_layer += 1  # the attention merge kernel
-        return 2 + len(self.dm.layers) * per_layer + 2
+        ple = 0
+        if self.dm.ple is not None:  # input: cast, GEMM, combine; per layer 3 launches (GEMVs) or 5 (GEMMs)
+            ple = 3 + len(self.dm.layers) * (3 if S <= kern.PLE_GEMV_ROWS else 5)
+        return 2 + len(self.dm.layers) * per_layer + 2 + ple
 
     def prefill_timed_gemms(self, tokens, seq: int = 0):
         """Run one prefill eagerly with CUDA events around every fused projection
@@ -414,6 +450,17 @@ class Runner:
 
         _lib.call("sb_embed_q4", dm.embed_q.data_ptr(), dm.embed_s.data_ptr(), _F16, dm.cfg["group"],
                   pf["tok"].data_ptr(), S, H, float(dm.cfg["embed_scale"]), pf["hid"].data_ptr(), None, s)
+        P = dm.ple
+        if P is not None:
+            # per-layer inputs of the whole prompt: the model projection as an f16 GEMM (f32 out), then the
+            # per-slice norm + table gather (gemma4/reference.py:92-101)
+            nL, pd = len(Ls), P["d"]
+            _lib.call("sb_cast_f16", pf["hid"].data_ptr(), pf["ple_x16"].data_ptr(), S * H, s)
+            _lib.call("sb_gemm_f16_f32out", pf["ple_x16"].data_ptr(), P["proj16"].data_ptr(),
+                      pf["ple_ctx"].data_ptr(), S, nL * pd, H, float(H ** -0.5), 1, H, H, nL * pd, s)
+            _lib.call("sb_ple_combine", pf["ple_ctx"].data_ptr(), pf["tok"].data_ptr(), P["table"].data_ptr(),
+                      P["table_scale"].data_ptr(), P["table"].shape[0], P["norm"].data_ptr(), nL, pd,
+                      kern.group_of(P["table_scale"], nL * pd), P["scale"], self.eps, pf["ple_in"].data_ptr(), S, s)
         _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), None, _F32, None, Ls[0]["in_norm"].data_ptr(),
                   pf["hid"].data_ptr(), None, pf["h16"].data_ptr(), S, H, self.eps, s)
         kc_off = seq * self.cache_stride * 4
@@ -440,6 +487,9 @@ class Runner:
                       L["post_ffn_norm"].data_ptr(), nxt.data_ptr(), pf["hid"].data_ptr(),
                       pf["hlast"].data_ptr() if last else None, None if last else pf["h16"].data_ptr(), S, H,
                       self.eps, s)
+            if P is not None:  # PLE block on the prompt rows, then the next norm from its output
+                kern.ple_block(pf["hid"][:S], pf["ple_in"][:S, li], L["ple"], self.eps, w_next=nxt,
+                               h_out=pf["hlast"][:S] if last else None, h16_out=None if last else pf["h16"][:S])
 
 
 def greedy_generate(model: dict, prompt, steps: int, device="cuda:0", batched_prefill: bool = True,

@@ -269,6 +269,13 @@ def ple_cases(out):
             outs.append(ref._layer(x, li, j, ples[j][li]))
         out[f"ple_l{li}_mid"] = np.stack(mids)
         out[f"ple_l{li}_out"] = np.stack(outs)
+    # greedy generation through the whole model with the PLE blocks
+    gen = Ref(config, q, max_seq=32, ple=True)
+    holder = SimpleNamespace(ref=gen)
+    prompt = synth.prompt_tokens(6, 512, seed=4444)
+    toks, margins, top = _RefModel.generate(holder, prompt, 10)
+    out["ple_gen_prompt"] = np.array(prompt, np.int64)
+    out["ple_gen_tokens"], out["ple_gen_margins"], out["ple_gen_top"] = toks, margins, top
 
 
 def decoder_small(out):

@@ -61,3 +61,29 @@ def test_bf16_rounding():
     # 1 + 2^-8 is a tie between 1 and 1 + 2^-7: ties to even gives 1.0
     assert back[0] == 1.0 and back[1] == 1.0 and back[3] == -2.5
     assert np.all(np.abs(back - a) <= np.abs(a) * 2.0 ** -8)
+
+
+def ple_model():
+    """The 2-layer model with per-layer embeddings that golden_ple.npz was generated from."""
+    cfg = synth.e2b_config(hidden=1536, n_layers=2, n_heads=2, head_dim=256, inter=512, vocab=512, rope_cutoff=32)
+    model = synth.random_model(cfg, seed=4242)
+    model["ple"] = synth.ple_weights(hidden=1536, n_layers=2, d=256, vocab=512, seed=4343)
+    return model
+
+
+def test_oracle_decoder_with_ple_matches_reference(gp):
+    from oracle.decoder import OracleDecoder
+    o = OracleDecoder(ple_model(), 32)
+    toks, margins = o.generate([int(t) for t in gp["ple_gen_prompt"]], 10)
+    np.testing.assert_array_equal(toks, gp["ple_gen_tokens"])
+    np.testing.assert_allclose(margins, gp["ple_gen_margins"], rtol=1e-4, atol=1e-4)
+
+
+def test_ple_changes_the_logits(gp):
+    """The same model without its PLE blocks gives other top-2 margins: the
+    end-to-end PLE checks are sensitive to the PLE path."""
+    from oracle.decoder import OracleDecoder
+    model = ple_model()
+    del model["ple"]
+    _, margins = OracleDecoder(model, 32).generate([int(t) for t in gp["ple_gen_prompt"]], 10)
+    assert np.abs(np.array(margins) - gp["ple_gen_margins"]).max() > 0.1

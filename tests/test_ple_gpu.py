@@ -220,3 +220,47 @@ def test_gemm_f16_f32out_splitk(cuda, m, n, k, splits):
     with pytest.raises(_lib.SlangError):  # 5 does not divide ceil(k / 64)
         _lib.call("sb_gemm_f16_f32out_splitk", a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, 0.5, 1, k, k, n,
                   5 if (k // 64) % 5 else 7, torch.cuda.current_stream().cuda_stream)
+
+
+def _key_logit(key: int) -> float:
+    """The max logit held in the top half of a greedy-argmax key."""
+    o = (key >> 32) & 0xFFFFFFFF
+    bits = o ^ 0x80000000 if o & 0x80000000 else (~o) & 0xFFFFFFFF
+    return float(np.array([bits], np.uint32).view(np.float32)[0])
+
+
+@pytest.mark.parametrize("batched_prefill", [False, True])
+def test_runner_with_ple_matches_reference(cuda, gp, batched_prefill):
+    """The per-op decode path with a PLE block after every layer (and, batched,
+    the prefill's PLE GEMMs): greedy tokens equal the reference's
+    QATReference(ple=True) run, and every step's top logit (softcapped) is
+    within 1e-3 (token-wise, f32) or 2e-2 (f16 batched prefill) of it."""
+    from slang_b200.runner import DeviceModel, Runner
+    from tests.test_ple import ple_model
+    model = ple_model()
+    dm = DeviceModel(model, cuda, 32)
+    r = Runner(dm, 1)
+    prompt = [int(t) for t in gp["ple_gen_prompt"]]
+    first = r.prefill(prompt) if batched_prefill else r.prefill_tokenwise(prompt)
+    toks, tops = [first], [_key_logit(int(r.keys[0].item()))]
+    for _ in range(9):
+        r.decode_step()
+        torch.cuda.current_stream().wait_stream(r.stream)
+        toks.append(int(r.tok[0].item()))
+        tops.append(_key_logit(int(r.keys[0].item())))
+    np.testing.assert_array_equal(toks, gp["ple_gen_tokens"])
+    cap = model["config"]["softcap"]
+    got = cap * np.tanh(np.array(tops) / cap)
+    tol = 2e-2 if batched_prefill else 1e-3
+    np.testing.assert_allclose(got, gp["ple_gen_top"], rtol=tol)
+    assert r.kernel_launches_per_step() == 2 + 2 * 10 + 3 + 2 + 3 * 2
+
+
+def test_runner_ple_rejects_other_paths(cuda):
+    from slang_b200.runner import DeviceModel, Runner
+    from tests.test_ple import ple_model
+    dm = DeviceModel(ple_model(), cuda, 16)
+    with pytest.raises(ValueError):
+        Runner(dm, 1, fused=True)
+    with pytest.raises(ValueError):
+        Runner(dm, 2, proj="gemm")

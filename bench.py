@@ -290,6 +290,60 @@ def timed_graph(torch, graph, steps, warmup, stream):
     return start.elapsed_time(end) / steps  # ms per step
 
 
+def ple_measure(torch, kern, dev, stream, warmup, hbm_peak, prompt):
+    """The per-layer-embedding (PLE) work of the Gemma-4-E2B checkpoint (not in
+    the benchmark model): per decode token the bf16 model projection
+    [8960 x 1536] + table gather + combine, then 35 blocks of two 8-bit GEMVs
+    and the norm-add tail; per prompt the same as GEMMs.  Random E2B-shaped
+    weights (table cut to 4096 rows), three copies rotated so a token reads HBM."""
+    H, nL, d, V = 1536, 35, 256, 4096
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    u8 = lambda *s: torch.randint(0, 256, s, dtype=torch.uint8, device=dev, generator=g)  # noqa: E731
+
+    def weights():
+        proj = (torch.randn(nL * d, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        return {"table": u8(V, nL * d // 2), "table_scale": torch.rand(V, nL, device=dev, generator=g) * 0.01,
+                "proj": proj, "proj16": proj.to(torch.float16),
+                "norm": torch.ones(d, device=dev),
+                "layers": [{"gate": (u8(d, H), torch.full((d,), 2e-4, device=dev)),
+                            "proj": (u8(H, d), torch.full((H,), 1e-3, device=dev)),
+                            "post_norm": torch.ones(H, device=dev), "scalar": 1.0} for _ in range(nL)]}
+
+    sets = [weights() for _ in range(3)]
+    out = {}
+    for m in (1, prompt):
+        x = torch.randn(m, H, device=dev, generator=g)
+        ids = torch.randint(0, V, (m,), dtype=torch.int32, device=dev, generator=g)
+        ple_in = torch.empty(m, nL, d, device=dev)
+
+        def token(P):
+            kern.ple_input(x, ids, P["table"], P["table_scale"], P["proj"], P["norm"], nL, d, 1e-6, 16.0,
+                           out=ple_in, w_proj16=P["proj16"])
+            for li, L in enumerate(P["layers"]):
+                kern.ple_block(x, ple_in[:, li], L, 1e-6)
+
+        with torch.cuda.stream(stream):
+            for P in sets:  # outside capture: kernel attributes, f16 weight copies of the GEMM route
+                token(P)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for P in sets:
+                    token(P)
+            us = timed_graph(torch, graph, 5, warmup, stream) / len(sets) * 1e3
+        del graph
+        w_bytes = nL * d * H * 2 + nL * 2 * d * H + nL * (d + H) * 4 + m * (nL * d // 2 + nL * 4)
+        if m == 1:
+            out["decode"] = {"us_per_token": us, "weight_bytes_per_token": w_bytes,
+                             "hbm_gbs": w_bytes / us / 1e3, "frac_of_hbm": w_bytes / us / 1e3 / hbm_peak,
+                             "gpu_launches_per_token": 2 + 3 * nL}
+        else:
+            out["prefill"] = {"tokens": m, "us_per_prompt": us, "gpu_launches_per_prompt": 3 + 5 * nL,
+                              "tflops": (2 * m * H * nL * d + nL * 4 * m * H * d) / us / 1e6}
+    return {"metric": "PLE work per decode token / per prompt (35 layers, d 256; not in the benchmark model)", **out}
+
+
 def config5_sweep(torch, kern, runner, dm, r0, warmup, steps, max_over_ranks, world):
     """Config 5 on one replica: decode tok/s at batch B, every sequence at the
     context of r0's sequence 0 (copied into all B), on the GEMV path (B <= 8)
@@ -555,6 +609,9 @@ def main():
         lms = timed_graph(torch, g_lm, 5, 2, stream) / 10
     lm_alg = VOCAB * HID // 2 + VOCAB * (HID // 32) * 2 + HID * 4
 
+    # ---------------- per-layer embeddings of the real checkpoint (kernels of csrc/ple.cu)
+    ple = ple_measure(torch, kern, dev, stream, args.warmup, hbm_peak, PROMPT)
+
     # ---------------- config 5: batched decode sweep and the GEMV -> tcgen05 GEMM crossover
     c5 = config5_sweep(torch, kern, runner, dm, r, args.warmup, 10, max_over_ranks, world)
 
@@ -640,6 +697,7 @@ def main():
                        "unit": "GB/s", "us": lms * 1e3, "frac_of_hbm": lm_alg / (lms / 1e3) / 1e9 / hbm_peak,
                        "peak": hbm_peak},
             "lmhead_sharded": sharded,
+            "ple": ple,
         }
         print(json.dumps(line), flush=True)
     del g_prefill, g_lm

@@ -339,11 +339,14 @@ def ple_gather(ids: torch.Tensor, table: torch.Tensor, scales: torch.Tensor, ple
 
 def ple_input(x: torch.Tensor, ids: torch.Tensor, table: torch.Tensor, scales: torch.Tensor, w_proj: torch.Tensor,
               w_norm: torch.Tensor, n_layers: int, d: int, eps: float, ple_scale: float,
-              out: torch.Tensor | None = None, ctx: torch.Tensor | None = None) -> torch.Tensor:
+              out: torch.Tensor | None = None, ctx: torch.Tensor | None = None,
+              w_proj16: torch.Tensor | None = None) -> torch.Tensor:
     """Per-layer inputs [m, n_layers, d] of ``ReferenceGemma4._ple_input``
     (gemma4/reference.py:92-101): the bf16 model projection of the scaled
     embedding ``x`` times hidden**-0.5, RMS-normed per layer slice, plus the
-    gathered table row, times 2**-0.5 (``sb_gemv_bf16`` + ``sb_ple_combine``)."""
+    gathered table row, times 2**-0.5 (``sb_gemv_bf16`` + ``sb_ple_combine``).
+    With more than ``PLE_GEMV_ROWS`` rows and an f16 copy of the projection
+    (``w_proj16``) the projection runs as a tcgen05 GEMM on f16 operands."""
     _need(ids, "ids", (torch.int32,))
     _need(table, "table", (torch.uint8,))
     _need(scales, "scales", (torch.float32,))
@@ -353,7 +356,18 @@ def ple_input(x: torch.Tensor, ids: torch.Tensor, table: torch.Tensor, scales: t
     cols = n_layers * d
     if table.shape[1] * 2 != cols or w_proj.shape != (cols, hidden) or w_norm.numel() != d:
         raise ValueError("PLE table, projection or norm does not match n_layers * d")
-    ctx = gemv_bf16(w_proj, x.reshape(m, hidden), alpha=float(hidden ** -0.5), out=ctx)
+    if m > PLE_GEMV_ROWS and w_proj16 is not None:
+        _need(w_proj16, "w_proj16", (torch.float16,))
+        x2 = x.reshape(m, hidden)
+        _need(x2, "x", (torch.float32,))
+        x16 = torch.empty(m, hidden, dtype=torch.float16, device=x.device)
+        _lib.call("sb_cast_f16", _ptr(x2), _ptr(x16), m * hidden, _stream())
+        if ctx is None:
+            ctx = torch.empty(m, cols, dtype=torch.float32, device=x.device)
+        _lib.call("sb_gemm_f16_f32out", _ptr(x16), _ptr(w_proj16), _ptr(ctx), m, cols, hidden,
+                  float(hidden ** -0.5), 1, hidden, hidden, cols, _stream())
+    else:
+        ctx = gemv_bf16(w_proj, x.reshape(m, hidden), alpha=float(hidden ** -0.5), out=ctx)
     if out is None:
         out = torch.empty(m, n_layers, d, dtype=torch.float32, device=x.device)
     _need(out, "out", (torch.float32,))

@@ -264,3 +264,22 @@ def test_runner_ple_rejects_other_paths(cuda):
         Runner(dm, 1, fused=True)
     with pytest.raises(ValueError):
         Runner(dm, 2, proj="gemm")
+
+
+def test_ple_input_gemm_route(cuda):
+    """A prompt's per-layer inputs through the f16 tcgen05 GEMM (w_proj16):
+    within the matmul tolerance of the f32 oracle."""
+    from tests._util import assert_close
+    w = synth.ple_weights(hidden=1536, n_layers=35, d=256, vocab=256, seed=61)
+    rng = np.random.default_rng(62)
+    m = 300
+    ids = rng.integers(0, 256, m).astype(np.int32)
+    x = (8 * rng.standard_normal((m, 1536))).astype(np.float32)
+    rows = ople.ple_gather(ids, w["table"], w["table_scale"], w["ple_scale"])
+    ref = ople.ple_input(x, rows, w["proj"], w["norm"], 35, 256, EPS)
+    W = T(w["proj"].view(np.int16), cuda)
+    got = kern.ple_input(T(x, cuda), T(ids, cuda), T(w["table"], cuda), T(w["table_scale"], cuda), W,
+                         T(w["norm"], cuda), 35, 256, EPS, w["ple_scale"],
+                         w_proj16=W.view(torch.bfloat16).to(torch.float16))
+    torch.cuda.synchronize()
+    assert_close(got.cpu().numpy(), ref, what="PLE input, GEMM route")

@@ -337,7 +337,7 @@ def ple_measure(torch, kern, dev, stream, warmup, hbm_peak, prompt):
         if m == 1:
             out["decode"] = {"us_per_token": us, "weight_bytes_per_token": w_bytes,
                              "hbm_gbs": w_bytes / us / 1e3, "frac_of_hbm": w_bytes / us / 1e3 / hbm_peak,
-                             "gpu_launches_per_token": 2 + 3 * nL}
+                             "gpu_launches_per_token": 2 + (2 if kern.PLE_FUSED_TAIL_ROWS >= 1 else 3) * nL}
         else:
             out["prefill"] = {"tokens": m, "us_per_prompt": us, "gpu_launches_per_prompt": 3 + 5 * nL,
                               "tflops": (2 * m * H * nL * d + nL * 4 * m * H * d) / us / 1e6}

@@ -403,6 +403,18 @@ size_t sb_decode_step_fused_scratch_size(int hidden, int n_heads, int head_dim, 
 int sb_gemv_q8(const void* codes, const float* row_scale, const float* x, int ldx, float* y, int ldy,
                int m, int n, int k, const float* ple, int ld_ple, void* stream);
 
+/* The PLE projection GEMV fused with its norm-add tail: proj = sb_gemv_q8(codes,
+ * row_scale, g) (m <= 8 rows, written to proj [m][n]), then the CTA that
+ * finishes last (an atomic count on *counter, no waiting) runs
+ * sb_ple_norm_add(proj, hidden, w_post, layer_scalar, w_next, h_out, h16_out)
+ * over all rows and re-arms *counter to 0.  counter: a zero-initialised device
+ * u32 that no concurrently running launch shares.  Replaces pleproj_77's
+ * last-arriver matmul + norm tail (gemma4_150/kernels_dsl.py:1000-1125). */
+int sb_ple_proj_norm_add(const void* codes, const float* row_scale, const float* g, int ldg, float* proj,
+                         int m, int n, int k, float* hidden, const float* w_post, float layer_scalar,
+                         const float* w_next, float* h_out, void* h16_out, float eps, unsigned int* counter,
+                         void* stream);
+
 /* y[r][o] = alpha * sum_k bf16(w[o][k]) * x[r][k]  (w: bf16 bit patterns [n][k]).
  * k % 8 == 0, k >= 32; w and x 16-byte aligned.  Replaces the
  * per_layer_model_projection matmul and its hidden**-0.5 factor

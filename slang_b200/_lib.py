@@ -57,6 +57,7 @@ SIGNATURES = {
     "sb_attn_decode_workspace_size": ([_i, _i, _i, _i], _sz),
     "sb_step_advance": ([_vp, _vp, _vp, _vp, _i, _i, _vp], _i),
     "sb_gemv_q8": ([_vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _vp, _i, _vp], _i),
+    "sb_ple_proj_norm_add": ([_vp, _vp, _vp, _i, _vp, _i, _i, _i, _vp, _vp, _f, _vp, _vp, _vp, _f, _vp, _vp], _i),
     "sb_gemv_bf16": ([_vp, _f, _vp, _i, _vp, _i, _i, _i, _i, _vp], _i),
     "sb_ple_norm_add": ([_vp, _vp, _vp, _f, _vp, _vp, _vp, _i, _i, _f, _vp], _i),
     "sb_ple_gather": ([_vp, _vp, _vp, _i, _i, _i, _f, _vp, _i, _vp], _i),

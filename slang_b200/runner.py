@@ -145,6 +145,7 @@ class Runner:
             pd = dm.ple["d"]
             self.ple_in, self.ple_ctx = f32(B, nL, pd), f32(B, nL * pd)
             self.ple_g, self.ple_proj = f32(B, pd), f32(B, H)
+            self.ple_counter = torch.zeros(1, dtype=torch.int32, device=dev)  # last-arriver count, self re-arming
         if proj == "gemm":
             f16 = lambda *s: torch.zeros(s, dtype=torch.float16, device=dev)  # noqa: E731
             self.h16, self.qkv16, self.attn16 = f16(B, H), f16(B, self.nqkv), f16(B, self.qd)
@@ -242,9 +243,14 @@ class Runner:
             if P is not None:  # PLE block, then the next norm from its output (gemma4/reference.py:154-163)
                 Lp = L["ple"]
                 kern.gemv_q8(Lp["gate"][0], Lp["gate"][1], self.x, out=self.ple_g, ple=self.ple_in[:, li])
-                kern.gemv_q8(Lp["proj"][0], Lp["proj"][1], self.ple_g, out=self.ple_proj)
-                kern.ple_norm_add(self.ple_proj, self.x, Lp["post_norm"], Lp["scalar"], self.eps, w_next=nxt,
-                                  h_out=self.h)
+                if B <= kern.PLE_FUSED_TAIL_ROWS:
+                    kern.ple_proj_norm_add(Lp["proj"][0], Lp["proj"][1], self.ple_g, self.x, Lp["post_norm"],
+                                           Lp["scalar"], self.eps, w_next=nxt, h_out=self.h, proj=self.ple_proj,
+                                           counter=self.ple_counter)
+                else:
+                    kern.gemv_q8(Lp["proj"][0], Lp["proj"][1], self.ple_g, out=self.ple_proj)
+                    kern.ple_norm_add(self.ple_proj, self.x, Lp["post_norm"], Lp["scalar"], self.eps, w_next=nxt,
+                                      h_out=self.h)
         kern.lmhead_argmax(dm.embed_q, dm.embed_s, self.h, keys=self.keys, tokens=self.tok)
         _lib.call("sb_step_advance", self.pos.data_ptr(), self.tok.data_ptr(), self.cur.data_ptr(),
                   self.history.data_ptr(), self.max_seq, B, s)
@@ -286,7 +292,8 @@ class Runner:
                          + 1 + 2 + 2)  # prep, attention (2), add+norm (2)
             return 2 + nL * per_layer + 2 + 1  # embed + norm, layers, argmax GEMM + tokens, advance
         per_layer = 4 + 1 + 2 + 2 + 1  # 4 GEMVs, prep, attention (2), add+norm (2), geglu
-        ple = 0 if self.dm.ple is None else 2 + 3 * nL  # PLE input (GEMV + combine); per layer 2 GEMVs + tail
+        per_ple = 2 if self.B <= kern.PLE_FUSED_TAIL_ROWS else 3  # per layer: gate GEMV, projection GEMV (+ fused tail)
+        ple = 0 if self.dm.ple is None else 2 + per_ple * nL  # + PLE input (GEMV + combine)
         return 2 + nL * per_layer + 2 + 1 + ple  # embed + first norm, layers, lm_head (gemv + tokens), advance
 
     def capture(self):
@@ -419,7 +426,8 @@ class Runner:
             per_layer += 1  # the attention merge kernel
         ple = 0
         if self.dm.ple is not None:  # input: cast, GEMM, combine; per layer 3 launches (GEMVs) or 5 (GEMMs)
-            ple = 3 + len(self.dm.layers) * (3 if S <= kern.PLE_GEMV_ROWS else 5)
+            gemv = 2 if S <= kern.PLE_FUSED_TAIL_ROWS else 3
+            ple = 3 + len(self.dm.layers) * (gemv if S <= kern.PLE_GEMV_ROWS else 5)
         return 2 + len(self.dm.layers) * per_layer + 2 + ple
 
     def prefill_timed_gemms(self, tokens, seq: int = 0):

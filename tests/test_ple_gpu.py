@@ -253,7 +253,7 @@ def test_runner_with_ple_matches_reference(cuda, gp, batched_prefill):
     got = cap * np.tanh(np.array(tops) / cap)
     tol = 2e-2 if batched_prefill else 1e-3
     np.testing.assert_allclose(got, gp["ple_gen_top"], rtol=tol)
-    assert r.kernel_launches_per_step() == 2 + 2 * 10 + 3 + 2 + 3 * 2
+    assert r.kernel_launches_per_step() == 2 + 2 * 10 + 3 + 2 + (2 if kern.PLE_FUSED_TAIL_ROWS >= 1 else 3) * 2
 
 
 def test_runner_ple_rejects_other_paths(cuda):
@@ -283,3 +283,30 @@ def test_ple_input_gemm_route(cuda):
                          w_proj16=W.view(torch.bfloat16).to(torch.float16))
     torch.cuda.synchronize()
     assert_close(got.cpu().numpy(), ref, what="PLE input, GEMM route")
+
+
+@pytest.mark.parametrize("m", [1, 3, 8])
+@pytest.mark.parametrize("with_next", [True, False])
+def test_ple_proj_norm_add_fused(cuda, m, with_next):
+    """Projection GEMV + last-arriver norm-add tail in one launch, run twice on
+    the same counter (it re-arms itself), against the oracle."""
+    rng = np.random.default_rng(71 + m)
+    codes, scale = synth.q8_weight(rng, 1536, 256, 0.5 / (74 * 16), 1.5 / (74 * 16))
+    g = rng.standard_normal((m, 256), dtype=np.float32)
+    hid = (4 * rng.standard_normal((m, 1536))).astype(np.float32)
+    w_post = (1 + 0.1 * rng.standard_normal(1536)).astype(np.float32)
+    w_next = (1 + 0.1 * rng.standard_normal(1536)).astype(np.float32)
+    counter = torch.zeros(1, dtype=torch.int32, device=cuda)
+    C, S, G = T(codes, cuda), T(scale, cuda), T(g, cuda)
+    ref = hid
+    H = T(hid, cuda)
+    h = torch.empty_like(H)
+    for _ in range(2):
+        kern.ple_proj_norm_add(C, S, G, H, T(w_post, cuda), 0.9, EPS, w_next=T(w_next, cuda) if with_next else None,
+                               h_out=h if with_next else None, counter=counter)
+        ref = ople.ple_norm_add(ople.q8_gemv(codes, scale, g), ref, w_post, 0.9, EPS)
+    torch.cuda.synchronize()
+    assert int(counter.item()) == 0
+    assert max_rel(H.cpu().numpy(), ref) < 1e-4
+    if with_next:
+        assert max_rel(h.cpu().numpy(), odec.rms_norm(ref, w_next, EPS)) < 1e-4

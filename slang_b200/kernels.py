@@ -440,10 +440,12 @@ def ple_block(hidden: torch.Tensor, ple_in: torch.Tensor, layer: dict, eps: floa
 
 
 PLE_GEMV_ROWS = 16
-# rows up to which the PLE projection carries its norm-add tail (one launch instead of two):
-# measured 7.65 vs 8.27 us per block at 1 row, 26.5 vs 20.1 us at 8 rows, where the last CTA
-# runs every row's tail in turn
-PLE_FUSED_TAIL_ROWS = 1
+# rows up to which ple_block runs the projection with its norm-add tail in one launch
+# (sb_ple_proj_norm_add).  Off: a block alone measured 7.65 against 8.27 us at one row, but
+# the 35-layer decode chain 280 against 253 us per token, because the separate tail kernel's
+# launch overlaps the GEMV under programmatic dependent launch while the last CTA's tail does
+# not; at 8 rows (26.5 against 20.1 us) the last CTA also runs every row's tail in turn.
+PLE_FUSED_TAIL_ROWS = 0
 _SMS: dict = {}
 _COUNTERS: dict = {}
 

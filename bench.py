@@ -17,8 +17,11 @@ this path).  The ~1 GB of weights exceeds the 126 MB L2, so no flush is needed.
 Sub-objects: decode tok/s (graph-captured greedy decode step at context
 ~1024, batch 1) with its bytes/token and HBM GB/s, the lm_head GEMV + argmax
 alone (config 3, HBM GB/s), the projection GEMMs inside the prefill (config 2
-shapes at M=1024, per matrix TFLOP/s), and at N>1 the vocabulary-sharded
-lm_head with its NCCL key all-reduce.
+shapes at M=1024, per matrix TFLOP/s), config 5 (batched decode by batch size
+on the GEMV and tcgen05 GEMM paths, and the gate|up crossover), the
+per-layer-embedding work of the real checkpoint per decode token and per
+prompt ("ple"), and at N>1 the vocabulary-sharded lm_head with its exchange
+in peer memory and its NCCL key all-reduce.
 
 --impl reference times the reference's algorithm on the host cores through the
 numpy oracle (the reference itself is Python and does not travel to the GPU

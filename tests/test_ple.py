@@ -87,3 +87,32 @@ def test_ple_changes_the_logits(gp):
     del model["ple"]
     _, margins = OracleDecoder(model, 32).generate([int(t) for t in gp["ple_gen_prompt"]], 10)
     assert np.abs(np.array(margins) - gp["ple_gen_margins"]).max() > 0.1
+
+
+def test_ple_wrappers_reject_host_tensors_and_bad_shapes():
+    """The torch wrappers validate on the host before any call into the
+    library (no GPU needed): host tensors are refused (the device is checked
+    before the dtype), and so are non-tensors."""
+    import torch
+    from slang_b200 import kernels as kern
+    codes = torch.zeros(16, 64, dtype=torch.uint8)
+    scale = torch.ones(16)
+    x = torch.zeros(1, 64)
+    with pytest.raises(ValueError):
+        kern.gemv_q8(codes, scale, x)
+    with pytest.raises(ValueError):
+        kern.gemv_bf16(torch.zeros(4, 32, dtype=torch.bfloat16), x)
+    with pytest.raises(ValueError):
+        kern.ple_proj_norm_add(codes, scale, torch.zeros(1, 64), torch.zeros(1, 16), torch.ones(16), 1.0, 1e-6)
+    with pytest.raises(TypeError):
+        kern.gemv_q8(codes.numpy(), scale, x)
+
+
+def test_synth_ple_weight_shapes():
+    w = synth.ple_weights(hidden=256, n_layers=3, d=256, vocab=10, seed=1)
+    assert w["table"].shape == (10, 3 * 256 // 2) and w["table_scale"].shape == (10, 3)
+    assert w["proj"].shape == (3 * 256, 256) and w["proj"].dtype == np.uint16
+    L = w["layers"][2]
+    assert L["gate"][0].shape == (256, 256) and L["gate"][1].shape == (256,)
+    assert L["proj"][0].shape == (256, 256) and L["post_norm"].shape == (256,)
+    assert w["ple_scale"] == 16.0

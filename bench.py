@@ -15,17 +15,24 @@ max-over-ranks step time (replicas, weak scaling: there is no collective on
 this path).  The ~1 GB of weights exceeds the 126 MB L2, so no flush is needed.
 
 Sub-objects: decode tok/s (graph-captured greedy decode step at context
-~1024, batch 1) with its bytes/token and HBM GB/s, the lm_head GEMV + argmax
-alone (config 3, HBM GB/s), the projection GEMMs inside the prefill (config 2
-shapes at M=1024, per matrix TFLOP/s), config 5 (batched decode by batch size
-on the GEMV and tcgen05 GEMM paths, and the gate|up crossover), the
-per-layer-embedding work of the real checkpoint per decode token and per
-prompt ("ple"), and at N>1 the vocabulary-sharded lm_head with its exchange
-in peer memory and its NCCL key all-reduce.
+~1024, batch 1) with its bytes/token and HBM GB/s, the config-1 GEMV alone
+(``gemv_cfg1``: [6144 x 1536], weights rotated past 2x L2, HBM GB/s), the
+lm_head GEMV + argmax alone (config 3, HBM GB/s), the projection GEMMs of the
+prefill replayed from CUDA graphs (config 2 shapes at M=1024, per matrix
+TFLOP/s; ``roofline``), config 5 (batched decode by batch size on the GEMV and
+tcgen05 GEMM paths, and the gate|up crossover), the per-layer-embedding work
+of the real checkpoint per decode token and per prompt ("ple"), and at N>1 the
+vocabulary-sharded lm_head (every replica serves the same weights) with its
+exchange in peer memory and by an NCCL key all-reduce, each token checked
+against the full-table argmax.
 
---impl reference times the reference's algorithm on the host cores through the
-numpy oracle (the reference itself is Python and does not travel to the GPU
-box) on a bounded sample, scaled to the same unit.
+--impl reference (and ``cpu_baseline`` at N=1) runs the reference's algorithm
+on the host cores through the numpy oracle (the reference itself is Python and
+does not travel to the GPU box): the same model's 1024-token prompt prefilled
+layers-outer -- every layer's attention, norms, RoPE and MLP, then the tied
+lm_head -- with the BLAS given every host core.  A step runs all 35 layers
+when that fits the time budget, else as many as fit, with the layer time
+scaled to 35 (the config says which).
 """
 from __future__ import annotations
 
@@ -42,6 +49,7 @@ sys.path.insert(0, ROOT)
 
 M_TOK = 1024
 N_LAYERS = 35
+PROMPT = 1024
 SHAPES = {"q": (2048, 1536), "k": (256, 1536), "v": (256, 1536), "o": (1536, 2048),
           "gate": (6144, 1536), "up": (6144, 1536), "down": (1536, 6144)}
 VOCAB, HID = 262144, 1536
@@ -422,6 +430,161 @@ def config5_sweep(torch, kern, runner, dm, r0, warmup, steps, max_over_ranks, wo
     return out
 
 
+def gemm_graph_times(torch, kern, r, stream, warmup):
+    """Durations of the prefill's projection GEMMs as the prefill graph replays
+    them: a CUDA graph of all 4 x 35 fused int4 GEMM launches in prefill order
+    (q|k|v, o, gate|up with GEGLU, down per layer) on the prefill's own
+    activation buffers gives the GEMM time per prefill (the 1 GB of weights
+    cycles past L2 as in the prefill); one graph per matrix, replayed after an
+    L2 flush, splits it by matrix.  CUDA events on the launching stream."""
+    pf, S, dm = r._pf, PROMPT, r.dm
+    specs = [("qkv", "h16", "qkv", "qkv16", False), ("o", "attn16", "o", "o16", False),
+             ("gate|up", "h16", "gu", "a16", True), ("down", "a16", "down", "d16", False)]
+
+    def launch(L, spec):
+        _, a_key, w_key, c_key, geglu = spec
+        kern.gemm_q4(pf[a_key][:S], L[w_key][0], L[w_key][1], C=pf[c_key][:S], workspace=pf["ws"], geglu=geglu)
+
+    def capture(body):
+        with torch.cuda.stream(stream):
+            body()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                body()
+        return g
+
+    g_all = capture(lambda: [launch(L, sp) for L in dm.layers for sp in specs])
+    with torch.cuda.stream(stream):
+        total_ms = timed_graph(torch, g_all, 10, warmup, stream)
+    del g_all
+    flush = torch.empty(2 * 126 * 2 ** 20, dtype=torch.uint8, device=dm.device)
+    out = {}
+    for sp in specs:
+        g = capture(lambda: [launch(L, sp) for L in dm.layers])
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                g.replay()
+            ms = 0.0
+            for _ in range(5):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+                e1.synchronize()
+                ms += e0.elapsed_time(e1) / 5
+        del g
+        w = dm.layers[0][sp[2]][0]
+        n, k = w.shape[0], w.shape[1] * 2
+        count = len(dm.layers)
+        avg_us = ms * 1e3 / count
+        out[sp[0]] = {"shape": [S, n, k], "count": count, "avg_us": avg_us,
+                      "tflops": 2 * S * n * k / (avg_us / 1e6) / 1e12,
+                      "algorithmic_read_bytes": S * k * 2 + n * k // 2 + n * (k // 32) * 2}
+    del flush
+    split_sum = sum(b["avg_us"] * b["count"] for b in out.values()) / 1e3
+    for b in out.values():  # scale the per-matrix split to the all-launch graph's total
+        b["avg_us_in_sequence"] = b["avg_us"] * total_ms / split_sum
+        b["tflops_in_sequence"] = b["tflops"] * split_sum / total_ms
+    return out, total_ms
+
+
+def gemv_cfg1(torch, kern, dev, stream, warmup, hbm_peak):
+    """Config 1 alone: x f16 [1, 1536] times an int4 [6144 x 1536] weight with
+    group-32 f16 scales, y f32.  The weight rotates over copies totalling more
+    than twice the L2, so every launch streams it from HBM."""
+    n, k = 6144, 1536
+    alg = n * k // 2 + n * (k // 32) * 2 + k * 2 + n * 4  # 5,336,064 B (packed W, scales, x, y)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    copies = -(-2 * l2 // (n * k // 2 + n * (k // 32) * 2)) + 1
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    ws = [(torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g),
+           (torch.randn((n, k // 32), device=dev, generator=g) * 0.02).abs().half()) for _ in range(copies)]
+    x = torch.randn((1, k), device=dev, generator=g).half()
+    y = torch.empty((1, n), dtype=torch.float32, device=dev)
+    with torch.cuda.stream(stream):
+        for w, sc in ws:
+            kern.gemv_q4(w, sc, x, y=y)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for w, sc in ws:
+                kern.gemv_q4(w, sc, x, y=y)
+        us = timed_graph(torch, graph, 10, warmup, stream) * 1e3 / copies
+    del graph, ws
+    gbs = alg / (us * 1e3)
+    return {"metric": "q4 GEMV HBM GB/s (config 1: int4 [6144 x 1536], group-32 f16 scales, x f16, y f32)",
+            "value": gbs, "unit": "GB/s", "us": us, "frac_of_hbm": gbs / hbm_peak, "peak": hbm_peak,
+            "algorithmic_bytes": alg, "kernel": "gemv_q4_stream_kernel",
+            "l2": f"weights rotated over {copies} copies = {copies * (n * k // 2 + n * (k // 32) * 2) / 2**20:.0f} MiB "
+                  f"> 2 x L2 ({l2 / 2**20:.0f} MiB); one CUDA graph of {copies} launches"}
+
+
+def sharded_lmhead(torch, dist, kern, lmhead, dm, h_local, rank, world, args, max_over_ranks, lm_alg):
+    """Config 3 vocabulary-sharded over the ranks: every rank holds the same
+    table (replicas of one model) and the same hidden vector (rank 0's,
+    broadcast), runs the GEMV + argmax on its 262144/G rows and exchanges the
+    64-bit argmax keys -- by one NCCL MAX all-reduce or through peer memory.
+    Each form's token is checked on every rank against the full-table argmax;
+    the time is split into the shard GEMV alone and the exchange."""
+    dev = dm.device
+    stream = torch.cuda.Stream(device=dev)
+    h = h_local.clone()
+    dist.broadcast(h, src=0)
+    _, tok_full = kern.lmhead_argmax(dm.embed_q, dm.embed_s, h)
+    keys = torch.zeros(1, dtype=torch.int64, device=dev)
+    toks = torch.full((1,), -1, dtype=torch.int32, device=dev)
+
+    def graph_us(fn, reps=10):
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                fn()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(reps):
+                    fn()
+            dist.barrier()
+            us = timed_graph(torch, g, max(2, args.steps // 10), 1, stream) * 1e3 / reps
+        del g
+        return max_over_ranks(us)
+
+    def match():
+        ok = torch.tensor([int(toks.item() == tok_full.item())], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        return bool(ok.item())
+
+    sh = lmhead.ShardedLMHead(dm.embed_q, dm.embed_s, rank, world)
+    k_shard = torch.zeros(1, dtype=torch.int64, device=dev)
+    shard_us = graph_us(lambda: kern.lmhead_argmax(sh.emb, sh.scales, h, row_offset=sh.lo, keys=k_shard,
+                                                   want_tokens=False))
+    out = {"metric": "vocab-sharded lm_head + argmax of one hidden vector, tok/s", "shards": world,
+           "rows_per_shard": sh.hi - sh.lo, "scaling": "strong", "shard_gemv_us": shard_us,
+           "token_full_table": int(tok_full.item())}
+    toks.fill_(-1)
+    nccl_us = graph_us(lambda: sh(h, keys, toks))  # NCCL all-reduce captured in the graph
+    out["nccl"] = {"us": nccl_us, "value": 1e6 / nccl_us, "exchange_us": nccl_us - shard_us,
+                   "hbm_gbs_aggregate": lm_alg / (nccl_us / 1e6) / 1e9, "tokens_match": match(),
+                   "gpu_launches_per_token": 4}
+    try:
+        ph = lmhead.PeerLMHead(dm.embed_q, dm.embed_s, rank, world)
+    except Exception as exc:  # noqa: BLE001 - CUDA IPC unavailable: report, keep the NCCL numbers
+        out["peer"] = {"unavailable": str(exc)[:200]}
+        ph = None
+    if ph is not None:
+        toks.fill_(-1)
+        peer_us = graph_us(lambda: ph(h, keys, toks))
+        out["peer"] = {"us": peer_us, "value": 1e6 / peer_us, "exchange_us": peer_us - shard_us,
+                       "hbm_gbs_aggregate": lm_alg / (peer_us / 1e6) / 1e9, "tokens_match": match(),
+                       "gpu_launches_per_token": 2}
+        ph.close()
+    best = min((f for f in ("nccl", "peer") if "us" in out.get(f, {})), key=lambda f: out[f]["us"])
+    out.update({"value": out[best]["value"], "us": out[best]["us"], "unit": "tok/s", "best": best})
+    return out
+
+
 def load_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -432,62 +595,118 @@ def load_peaks():
 
 
 # ------------------------------------------------------------------ CPU baseline (oracle)
-def cpu_sample_prefill(seconds_budget: float = 20.0) -> dict:
-    """Time the numpy oracle on a bounded sample: the layer-0 gate projection at M=1024
-    (dequant to f16 then f32 GEMM, the reference's _dq + _gemm math); scaled to the
-    35-layer stack by parameter count (both dequant and matmul scale with it)."""
-    import numpy as np
+def _blas_threads() -> tuple[int, dict]:
+    """Give the BLAS all the host cores this process may run on (torchrun sets
+    OMP_NUM_THREADS=1 for its workers) and report what it actually uses."""
+    from threadpoolctl import threadpool_info, threadpool_limits
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    threadpool_limits(limits=cores)
+    info = [p for p in threadpool_info() if p.get("user_api") == "blas"]
+    used = max((p.get("num_threads", 0) for p in info), default=0)
+    return cores, {"blas": info[0].get("internal_api") if info else None, "blas_threads": used}
 
-    from oracle import q4
-    from slang_b200 import synth
-    rng = np.random.default_rng(1)
-    n, k = SHAPES["gate"]
-    packed, scales = synth.q4_weight(rng, n, k)
-    a = synth.activations(rng, M_TOK, k)
-    times = []
-    t_start = time.perf_counter()
-    q4.gemm_q4(a, packed, scales)  # warm-up
-    while len(times) < 5 and time.perf_counter() - t_start < seconds_budget:
+
+class CpuPrefill:
+    """The config-4 workload on the host cores through the numpy oracle: the
+    random-init decoder (the same ``synth.random_model(seed=1234)`` the GPU
+    runs), its 1024-token prompt prefilled layers-outer (embedding, per layer
+    RMSNorms, q|k|v, q/k norm + RoPE, causal softmax attention, o, GEGLU MLP,
+    down, residuals; then the final norm and the tied lm_head of the last
+    position) -- ``OracleDecoder.prefill_batched``, the reference decoder's
+    arithmetic (gemma4/reference.py:103-182) in f32 with BLAS matmuls.
+    Weights are dequantised to f32 once, outside the timed region."""
+
+    def __init__(self):
+        import numpy as np
+
+        from oracle import decoder
+        from slang_b200 import synth
+        self.cores, self.blas = _blas_threads()
+        cfg = synth.e2b_config()
+        model = synth.random_model(cfg, seed=1234)
+        self.o = decoder.OracleDecoder(model, PROMPT + 1)
+        self.prompt = synth.prompt_tokens(PROMPT, cfg["vocab"], seed=99)
+        self.n_layers = cfg["n_layers"]
+        for li in range(self.n_layers):
+            for n in ("q", "k", "v", "o", "gate", "up", "down"):
+                self.o.w(li, n)
+        self.o.embed()
+        self.np = np
+
+    def step(self, layers: int) -> dict:
+        """One prefill through the first ``layers`` layers (all of them when
+        ``layers`` is the model's), with the embedding and the head."""
         t0 = time.perf_counter()
-        q4.gemm_q4(a, packed, scales)
-        times.append(time.perf_counter() - t0)
-    t = min(times)
-    stack_params = N_LAYERS * sum(nn * kk for nn, kk in SHAPES.values())
-    scale = stack_params / (n * k)
-    return {"value": M_TOK / (t * scale), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"oracle q4.gemm_q4 (dq_f16 + fp32 numpy GEMM) of one gate projection "
-                      f"[{n}x{k}] at M={M_TOK}, min of {len(times)} runs = {t*1e3:.1f} ms, "
-                      f"scaled x{scale:.1f} by parameter count to the 35-layer stack"}
+        x = self.o.embed_rows(self.prompt)
+        t1 = time.perf_counter()
+        for li in range(layers):
+            x = self.o.layer_batched(x, li)
+        t2 = time.perf_counter()
+        logits = self.o.head(x[-1])
+        t3 = time.perf_counter()
+        return {"embed": t1 - t0, "layers": t2 - t1, "head": t3 - t2, "step": t3 - t0,
+                "token": int(self.np.argmax(logits))}
+
+    def run(self, steps: int, warmup: int, step_budget_s: float = 8.0, total_budget_s: float = 200.0):
+        """Time ``steps`` steps after ``warmup``; a step runs every layer when
+        that fits the budgets, else the largest layer count that does, and the
+        prefill time is the measured embedding + head + the layers scaled to
+        all of them (layers are identical in shape)."""
+        probe = self.step(1)
+        per_layer = probe["layers"]
+        layers = self.n_layers
+        while layers > 1 and (per_layer * layers > step_budget_s
+                              or (steps + warmup) * per_layer * layers > total_budget_s):
+            layers -= 1
+        for _ in range(warmup):
+            self.step(layers)
+        recs = [self.step(layers) for _ in range(steps)]
+        full = [r["embed"] + r["head"] + r["layers"] * self.n_layers / layers for r in recs]
+        t = statistics.median(full)
+        sample = (f"OracleDecoder.prefill_batched of the 1024-token config-4 prompt through "
+                  + ("all 35 layers + final norm + tied lm_head per step"
+                     if layers == self.n_layers else
+                     f"{layers} of 35 layers (+ embedding, final norm, tied lm_head) per step, "
+                     f"layer time scaled x{self.n_layers / layers:.2f} (identical layer shapes)")
+                  + f"; f32 numpy, weights dequantised once; median of {len(recs)} steps")
+        return {"tok_s": PROMPT / t, "prefill_s": t, "layers_per_step": layers,
+                "ms_per_step": 1e3 * statistics.median(r["step"] for r in recs),
+                "token": recs[-1]["token"] if layers == self.n_layers else None,
+                "cores": self.cores, **self.blas, "sample": sample}
+
+
+def cpu_baseline_line(res: dict) -> dict:
+    return {"value": res["tok_s"], "unit": "tok/s", "cores": res["blas_threads"] or res["cores"], "kind": "port",
+            "sample": res["sample"], "host_cores": res["cores"], "blas": res["blas"],
+            "layers_per_step": res["layers_per_step"], "first_token": res["token"]}
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    vals = []
-    for _ in range(args.warmup):
-        cpu_sample_prefill(5.0)
     t0 = time.perf_counter()
-    for _ in range(max(1, args.steps // 10)):
-        vals.append(cpu_sample_prefill(5.0))
+    cpu = CpuPrefill()
+    setup = time.perf_counter() - t0
+    res = cpu.run(args.steps, args.warmup)
     wall = time.perf_counter() - t0
-    v = statistics.median([x["value"] for x in vals])
-    cb = dict(vals[0])
-    cb["value"] = v
+    v = res["tok_s"]
     line = {"metric": "1024-tok prefill tok/s", "value": v, "unit": "tok/s",
-            "impl": "reference", "n_gpus": args.gpus, "steps": len(vals), "warmup": args.warmup,
-            "ms_per_step": 1e3 * M_TOK / v, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "cfg4_full_model_prefill_1024", "prompt_tokens": M_TOK,
-                       "parallelism": "cpu", "sample": "see cpu_baseline.sample"},
-            "cpu_baseline": cb,
+            "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "cfg4_full_model_prefill_1024", "prompt_tokens": PROMPT,
+                       "model": "random-init Gemma-4-E2B-shaped int4 decoder (35L, H1536, F6144, 8q/1kv hd256, "
+                                "V262144, group-32 f16 scales), synth.random_model(seed=1234)",
+                       "parallelism": "host cores (rank 0 only)", "layers_per_step": res["layers_per_step"],
+                       "sample": res["sample"]},
+            "cpu_baseline": cpu_baseline_line(res),
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "wall_s": wall}
+            "setup_s": setup, "wall_s": wall}
     print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------------ GPU arm
-PROMPT = 1024
 DECODE_STEPS = 64
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the
 # fused int4 GEMM at M = 1024, keyed by the weight's (N, K), from one ncu capture
@@ -530,7 +749,7 @@ def main():
         return float(t.item())
 
     cfg = synth.e2b_config()
-    model = synth.random_model(cfg, seed=1234 + rank)
+    model = synth.random_model(cfg, seed=1234)  # every replica serves the same weights
     dm = runner.DeviceModel(model, dev, PROMPT + args.warmup + args.steps + DECODE_STEPS + 8)
     del model
     r = runner.Runner(dm, 1)
@@ -563,25 +782,18 @@ def main():
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
 
     # ---------------- roofline of the dominant kernel (fused int4 GEMM) inside the prefill
-    rec = r.prefill_timed_gemms(prompt)
     hbm_peak, tc_peak, peak_kind = load_peaks()
-    gemm_ms = sum(x[4] for x in rec)
-    gemm_flops = sum(2 * m * n * k for _, m, n, k, _ in rec)
+    by, gemm_ms = gemm_graph_times(torch, kern, r, stream, args.warmup)
+    gemm_flops = sum(2 * m * n * k * b["count"] for b in by.values() for m, n, k in [b["shape"]])
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
-    by = {}
-    for name, m, n, k, t in rec:
-        b = by.setdefault(name, {"shape": [m, n, k], "ms": 0.0, "count": 0})
-        b["ms"] += t
-        b["count"] += 1
     for b in by.values():
         m, n, k = b["shape"]
-        b["avg_us"] = 1e3 * b["ms"] / b["count"]
-        b["tflops"] = 2 * m * n * k / (b["avg_us"] / 1e6) / 1e12
-        b["algorithmic_read_bytes"] = m * k * 2 + n * k // 2 + n * (k // 32) * 2
         b["dram_bytes_per_launch"] = GEMM_DRAM_BYTES.get((n, k)) if m == PROMPT else None
-        del b["ms"]
     traffic = (sum(b["dram_bytes_per_launch"] * b["count"] for b in by.values())
                if all(b["dram_bytes_per_launch"] for b in by.values()) else None)
+
+    # ---------------- config-1 GEMV alone, weights rotated past 2x L2
+    gemv1 = gemv_cfg1(torch, kern, dev, stream, args.warmup, hbm_peak)
 
     # ---------------- decode (graph-captured step, batch 1, context from PROMPT)
     # the persistent one-kernel step (the product path) and the per-op graph
@@ -618,54 +830,15 @@ def main():
     # ---------------- config 5: batched decode sweep and the GEMV -> tcgen05 GEMM crossover
     c5 = config5_sweep(torch, kern, runner, dm, r, args.warmup, 10, max_over_ranks, world)
 
-    # ---------------- vocabulary-sharded lm_head over NCCL (N > 1)
+    # ---------------- vocabulary-sharded lm_head (N > 1): NCCL and peer-memory exchanges
     sharded = None
     if world > 1:
-        sh = lmhead.ShardedLMHead(dm.embed_q, dm.embed_s, rank, world)
-        keys = torch.zeros(1, dtype=torch.int64, device=dev)
-        toks = torch.zeros(1, dtype=torch.int32, device=dev)
-        with torch.cuda.stream(stream):
-            for _ in range(args.warmup):
-                sh(r.h, keys, toks)
-            torch.cuda.synchronize()
-            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s0.record(stream)
-            for _ in range(args.steps):
-                sh(r.h, keys, toks)
-            s1.record(stream)
-        s1.synchronize()
-        sms_ = max_over_ranks(s0.elapsed_time(s1) / args.steps)
-        sharded = {"metric": "vocab-sharded lm_head + argmax (NCCL MAX of keys), tok/s", "value": 1e3 / sms_,
-                   "unit": "tok/s", "us": sms_ * 1e3, "shards": world,
-                   "hbm_gbs_aggregate": lm_alg / (sms_ / 1e3) / 1e9, "scaling": "strong"}
-        # the same shards with the exchange in peer memory (atomic MAX over NVLink in the GEMV, one
-        # counting kernel per rank), captured as a graph of 10 steps
-        try:
-            ph = lmhead.PeerLMHead(dm.embed_q, dm.embed_s, rank, world)
-        except Exception as exc:  # noqa: BLE001 - CUDA IPC unavailable: report, keep the NCCL numbers
-            sharded["peer"] = {"unavailable": str(exc)[:200]}
-            ph = None
-        if ph is not None:
-            with torch.cuda.stream(stream):
-                for _ in range(args.warmup):
-                    ph(r.h, keys, toks)
-                torch.cuda.synchronize()
-                gp = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(gp, stream=stream):
-                    for _ in range(10):
-                        ph(r.h, keys, toks)
-                dist.barrier()
-                pms = timed_graph(torch, gp, max(1, args.steps // 10), 1, stream) / 10
-            pms = max_over_ranks(pms)
-            # (each rank holds its own random model here; the sharded tokens are checked in the tests)
-            sharded["peer"] = {"metric": "vocab-sharded lm_head + argmax, exchange in peer memory over NVLink, tok/s",
-                               "value": 1e3 / pms, "us": pms * 1e3, "hbm_gbs_aggregate": lm_alg / (pms / 1e3) / 1e9,
-                               "gpu_launches_per_token": 2}
-            del gp
-            ph.close()
+        sharded = sharded_lmhead(torch, dist, kern, lmhead, dm, r.h, rank, world, args, max_over_ranks, lm_alg)
 
     if rank == 0:
-        cpu = cpu_sample_prefill() if (not args.no_cpu_baseline and world == 1) else None
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            cpu = cpu_baseline_line(CpuPrefill().run(3, 1, step_budget_s=8.0, total_budget_s=30.0))
         line = {
             "metric": "1024-tok prefill tok/s", "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -699,6 +872,7 @@ def main():
             "lmhead": {"metric": "q4 GEMV HBM GB/s (lm_head 262144x1536 + argmax)", "value": lm_alg / (lms / 1e3) / 1e9,
                        "unit": "GB/s", "us": lms * 1e3, "frac_of_hbm": lm_alg / (lms / 1e3) / 1e9 / hbm_peak,
                        "peak": hbm_peak},
+            "gemv_cfg1": gemv1,
             "lmhead_sharded": sharded,
             "ple": ple,
         }

@@ -253,10 +253,13 @@ int sb_gemm_q4_argmax(const void* a, const void* w, const void* scales, int scal
  * pool, where a cudaMalloc on this path fails or stalls.
  * Its split-K scratch is a static 32 MiB device array that every GPU loading
  * this library holds until the process exits.  Shapes whose split-K scratch
- * (sb_gemm_q4_workspace_size) exceeds 32 MiB are rejected with
- * SB_ERR_WORKSPACE.  The first call on each device looks up the array's device
- * address with that device current; make that first call before any stream
- * capture.  Every call shares the array and it keeps the last call's partial
+ * (for this call's group and scale type; sb_gemm_q4_workspace_size for the
+ * group-32 f16 format) exceeds 32 MiB are rejected with SB_ERR_WORKSPACE.
+ * The first call on each device looks up the array's device address with
+ * that device current; make that first call before any stream capture.  The
+ * address is kept per device ordinal for the life of the process: after a
+ * cudaDeviceReset() it is stale, so do not call this entry point again in a
+ * process that has reset a device it used.  Every call shares the array and it keeps the last call's partial
  * sums (nothing in it needs to start at zero), so calls that overlap on the
  * GPU -- other streams, other host threads -- race: order them on one stream.
  * Arguments mean what they mean for sb_gemm_q4.

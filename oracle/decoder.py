@@ -29,6 +29,12 @@ def gelu_tanh(x: np.ndarray) -> np.ndarray:
     return 0.5 * x * (1.0 + np.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3)))
 
 
+def gelu_tanh_cube(x: np.ndarray) -> np.ndarray:
+    """``gelu_tanh`` with the cube as two multiplies (numpy's float power is
+    ~40x slower on large arrays); within an ulp or two of ``x**3``."""
+    return 0.5 * x * (1.0 + np.tanh(0.7978845608028654 * (x + 0.044715 * (x * x * x))))
+
+
 def rope_tables(max_pos: int, head_dim: int, theta: float, cutoff: int) -> tuple[np.ndarray, np.ndarray]:
     """cos/sin ``[max_pos, head_dim/2]`` exactly as gemma4/reference.py:44-50 forms them."""
     half = head_dim // 2
@@ -139,6 +145,66 @@ class OracleDecoder:
         logits = self.embed() @ x
         cap = cfg["softcap"]
         return cap * np.tanh(logits / cap) if cap else logits
+
+    # ------------------------------------------------------------ batched prefill
+    def embed_rows(self, tokens) -> np.ndarray:
+        """Scaled embedding rows ``[S, H]`` of a prompt (gemma4/reference.py:168)."""
+        ids = np.asarray(tokens, dtype=np.int64)
+        x = q4.dequant_f32(self.model["embed_q"][ids], self.model["embed_scale"][ids], 4)
+        return x * np.float32(self.cfg["embed_scale"])
+
+    def layer_batched(self, x: np.ndarray, li: int) -> np.ndarray:
+        """Layer ``li`` for prompt rows at positions 0..S-1 at once: the
+        per-position arithmetic of gemma4/reference.py:103-152 (same norms,
+        RoPE, scaling 1.0, causal softmax, GEGLU) in the layers-outer order of
+        ``PrefillGPU._layer`` (gemma4_150/prefill_gpu.py:316-395); fills this
+        layer's KV cache for those positions."""
+        cfg, L = self.cfg, self.model["layers"][li]
+        eps, nh, hd = cfg["eps"], cfg["n_heads"], cfg["head_dim"]
+        S = x.shape[0]
+        half = hd // 2
+        cos, sin = self.cos[:S, None, :], self.sin[:S, None, :]
+
+        def rope(t):  # [S, heads, hd]
+            a, b = t[..., :half], t[..., half:]
+            return np.concatenate([a * cos - b * sin, b * cos + a * sin], axis=-1)
+
+        h = rms_norm(x, L["in_norm"], eps)
+        q = rope(rms_norm((h @ self.w(li, "q").T).reshape(S, nh, hd), L["q_norm"], eps))
+        k = rope(rms_norm((h @ self.w(li, "k").T).reshape(S, 1, hd), L["k_norm"], eps))[:, 0]
+        v = rms_norm(h @ self.w(li, "v").T, None, eps)
+        self.k_cache[li][:S] = k
+        self.v_cache[li][:S] = v
+        scores = np.matmul(q.transpose(1, 0, 2), k.T)  # [nh, S, S]; attention scaling 1.0
+        i = np.arange(S)
+        masked = i[None, :] > i[:, None]
+        win = cfg.get("sliding_window", 0)
+        if win:
+            masked |= i[None, :] < (i[:, None] + 1 - win)
+        scores[:, masked] = -np.inf
+        scores -= scores.max(axis=-1, keepdims=True)
+        probs = np.exp(scores)
+        probs /= probs.sum(axis=-1, keepdims=True)
+        attn = np.matmul(probs, v).transpose(1, 0, 2).reshape(S, nh * hd)
+        x = x + rms_norm(attn @ self.w(li, "o").T, L["post_attn_norm"], eps)
+        h = rms_norm(x, L["pre_ffn_norm"], eps)
+        a = gelu_tanh_cube(h @ self.w(li, "gate").T) * (h @ self.w(li, "up").T)
+        return x + rms_norm(a @ self.w(li, "down").T, L["post_ffn_norm"], eps)
+
+    def head(self, x_last: np.ndarray) -> np.ndarray:
+        """Final norm + tied lm_head + softcap of one hidden row (gemma4/reference.py:177-180)."""
+        cfg = self.cfg
+        logits = self.embed() @ rms_norm(x_last, self.model["final_norm"], cfg["eps"])
+        cap = cfg["softcap"]
+        return cap * np.tanh(logits / cap) if cap else logits
+
+    def prefill_batched(self, tokens) -> np.ndarray:
+        """Layers-outer prefill of a prompt at positions 0..S-1; returns the
+        logits of the last position (whose argmax is the first generated token)."""
+        x = self.embed_rows(tokens)
+        for li in range(self.cfg["n_layers"]):
+            x = self.layer_batched(x, li)
+        return self.head(x[-1])
 
     def generate(self, prompt: list[int], steps: int) -> tuple[list[int], list[float]]:
         """Token-at-a-time prefill then greedy decode; returns (tokens, top-2 margins)."""

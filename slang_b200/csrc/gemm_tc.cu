@@ -1440,12 +1440,14 @@ int noalloc_scratch(float** out) {
 
 extern "C" int sb_gemm_q4_noalloc(const void* a, const void* w, const void* scales, int scale_dtype, int group,
                                   void* c, int m, int n, int k, float alpha, int lda, int ldc, void* stream) {
-  const size_t need = sb_gemm_q4_workspace_size(m, n, k);
+  // the split count depends on the scale tile's bytes: size the scratch for
+  // this call's group and scale type, not the benchmark format's
+  const size_t need = q4_workspace(m, n, k, group, scale_dtype == SB_F16 ? 2 : 4);
   if (need > kNoAllocScratchBytes)
     return sb::fail(SB_ERR_WORKSPACE,
-                    "sb_gemm_q4_noalloc: m=%d n=%d k=%d needs %zu bytes of split-K scratch, more than the "
-                    "%zu-byte static scratch; use sb_gemm_q4 with a caller workspace",
-                    m, n, k, need, kNoAllocScratchBytes);
+                    "sb_gemm_q4_noalloc: m=%d n=%d k=%d group=%d needs %zu bytes of split-K scratch, more than "
+                    "the %zu-byte static scratch; use sb_gemm_q4 with a caller workspace",
+                    m, n, k, group, need, kNoAllocScratchBytes);
   float* ws = nullptr;
   if (need > 0) {
     int rc = noalloc_scratch(&ws);

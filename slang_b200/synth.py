@@ -3,11 +3,15 @@
 There is no checkpoint on this machine, so every workload is generated from a
 seed with ``numpy.random.default_rng``:
 
-* packed int4 weights: uniform random bytes, i.e. two independent nibbles
-  uniform in ``[0, 15]`` -> values uniform in ``[-8, 7]``, low nibble first;
+* packed int4 weights of the single-matrix configurations (GEMV, GEMM,
+  lm_head): uniform random bytes, i.e. two independent nibbles uniform in
+  ``[0, 15]`` -> values uniform in ``[-8, 7]``, low nibble first;
+* packed int4 weights of the random-init decoder: nibbles uniform in
+  ``[1, 15]`` -> values uniform in ``[-7, 7]`` (zero mean, see ``random_model``);
 * per-group-32 scales: ``|N(0, 0.02)|`` rounded to f16, shape ``[n_out, n_in/32]``;
 * activations: ``N(0, 1)`` rounded to f16 (or kept f32 for decode);
-* norm weights: ``1 + 0.1 * N(0, 1)`` in f32.
+* norm weights: ``1 + 0.1 * N(0, 1)`` in f32; the decoder's post-attention and
+  post-feed-forward norms are ``POST_NORM_GAIN`` times that.
 
 The Gemma-4-E2B-shaped decoder is uniform: 35 layers, hidden 1536, FFN 6144,
 8 query heads and 1 KV head at head_dim 256, full RoPE (theta 1e4), full causal
@@ -38,12 +42,31 @@ def e2b_config(**over) -> dict:
     return cfg
 
 
+def small_config() -> dict:
+    """The small test decoder: hidden 256, 4 layers, 2 query heads of 64, FFN 512, vocab 2048."""
+    return e2b_config(hidden=256, n_layers=4, n_heads=2, head_dim=64, inter=512, vocab=2048, rope_cutoff=32)
+
+
 def q4_weight(rng: np.random.Generator, n_out: int, n_in: int,
               group: int = GROUP) -> tuple[np.ndarray, np.ndarray]:
     """Packed int4 ``[n_out, n_in/2]`` u8 and f16 scales ``[n_out, n_in/group]``."""
     packed = rng.integers(0, 256, (n_out, n_in // 2), dtype=np.uint8)
     scales = np.abs(rng.normal(0.0, 0.02, (n_out, n_in // group))).astype(np.float16)
     return packed, scales
+
+
+def q4_weight_sym(rng: np.random.Generator, n_out: int, n_in: int,
+                  group: int = GROUP) -> tuple[np.ndarray, np.ndarray]:
+    """As ``q4_weight`` but every nibble uniform in ``[1, 15]``: values uniform
+    in ``[-7, 7]``, so the dequantised weight has zero mean."""
+    lo = rng.integers(1, 16, (n_out, n_in // 2), dtype=np.uint8)
+    hi = rng.integers(1, 16, (n_out, n_in // 2), dtype=np.uint8)
+    scales = np.abs(rng.normal(0.0, 0.02, (n_out, n_in // group))).astype(np.float16)
+    return (lo | (hi << 4)).astype(np.uint8), scales
+
+
+# Gain of the decoder's post-attention / post-feed-forward norm weights.
+POST_NORM_GAIN = 5.0
 
 
 def q2_weight(rng: np.random.Generator, n_out: int, n_in: int,
@@ -85,14 +108,32 @@ def config3(vocab: int = 262144, hidden: int = 1536, seed: int = 3):
     return packed, scales, h
 
 
-def random_model(cfg: dict | None = None, seed: int = 1234) -> dict:
-    """Random-init Gemma-4-E2B-architecture int4 decoder (layer ``L`` uses seed+1+L)."""
+def random_model(cfg: dict | None = None, seed: int = 1234, post_gain: float = POST_NORM_GAIN,
+                 symmetric: bool = True) -> dict:
+    """Random-init Gemma-4-E2B-architecture int4 decoder (layer ``L`` uses seed+1+L).
+
+    The recipe is chosen so greedy decoding does not collapse onto one token:
+
+    * zero-mean codes (``q4_weight_sym``).  With codes uniform in ``[-8, 7]``
+      every row has mean ``-0.5 * scale``, so each projection maps the all-ones
+      direction onto itself; over 70 sub-layers that direction takes over the
+      residual stream (final hidden states at every position have cosine
+      0.998) and the tied lm_head picks one token at every step;
+    * post-attention / post-feed-forward norm weights ``POST_NORM_GAIN`` times
+      ``1 + 0.1 N(0,1)``, so the sub-layer outputs outweigh the token's own
+      embedding (times sqrt(hidden)) in the final hidden state.  With gain 1 the
+      current token's tied logit wins and the model repeats its input.
+
+    At the benchmark shape (seed 1234, the 1024-token prompt of seed 99) the
+    256 greedy tokens hold 148 distinct ids.
+    """
     cfg = dict(cfg or e2b_config())
     H, qd, hd, F = cfg["hidden"], cfg["q_dim"], cfg["head_dim"], cfg["inter"]
     shapes = {"q": (qd, H), "k": (hd, H), "v": (hd, H), "o": (H, qd),
               "gate": (F, H), "up": (F, H), "down": (H, F)}
     rng = np.random.default_rng(seed)
-    embed_q, embed_scale = q4_weight(rng, cfg["vocab"], H, cfg["group"])
+    qw = q4_weight_sym if symmetric else q4_weight
+    embed_q, embed_scale = qw(rng, cfg["vocab"], H, cfg["group"])
 
     def norm(r, n):
         return (1.0 + 0.1 * r.standard_normal(n, dtype=np.float32)).astype(np.float32)
@@ -101,10 +142,12 @@ def random_model(cfg: dict | None = None, seed: int = 1234) -> dict:
     layers = []
     for li in range(cfg["n_layers"]):
         r = np.random.default_rng(seed + 1 + li)
-        layer = {name: q4_weight(r, n, k, cfg["group"]) for name, (n, k) in shapes.items()}
+        layer = {name: qw(r, n, k, cfg["group"]) for name, (n, k) in shapes.items()}
         for name, n in (("in_norm", H), ("q_norm", hd), ("k_norm", hd), ("post_attn_norm", H),
                         ("pre_ffn_norm", H), ("post_ffn_norm", H)):
             layer[name] = norm(r, n)
+            if name.startswith("post_"):
+                layer[name] = (layer[name] * np.float32(post_gain)).astype(np.float32)
         layers.append(layer)
     return {"config": cfg, "embed_q": embed_q, "embed_scale": embed_scale,
             "final_norm": final_norm, "layers": layers}

@@ -12,7 +12,10 @@ What runs from the reference (imported in place, nothing copied):
 * ``tests/test_gemm_dsl.py``'s float64 ``reference`` and ``_inputs`` for the GEMM shapes;
 * ``gemma4.reference.ReferenceGemma4`` (``ple=False``) for the decoder, with a
   ``_w``/``_embed_row`` override in the style of ``QATReference``
-  (gemma4/qat_reference.py:24-37) that serves the synthetic int4 weights.
+  (gemma4/qat_reference.py:24-37) that serves the synthetic int4 weights; every
+  greedy step records its token, top-2 margin and the 8 largest logits with
+  their ids (the reference feeds its own token back, so a teacher-forced replay
+  on another implementation feeds the same tokens).
 
 ``--full`` additionally runs the full-size cases (config-1 GEMV, the 262144-row
 lm_head, and the 35-layer decoder: 1024-token prompt + 256 greedy steps; the
@@ -190,7 +193,7 @@ class _RefModel:
             logits = self.ref.forward(int(t), pos)
             if log_every and pos % log_every == 0:
                 print(f"  prefill pos {pos} {time.time() - t0:.0f}s", flush=True)
-        toks, margins, top = [], [], []
+        toks, margins, top, top8_idx, top8_val = [], [], [], [], []
         pos = len(prompt)
         for s in range(steps):
             part = np.partition(logits, -2)[-2:]
@@ -198,11 +201,18 @@ class _RefModel:
             nxt = int(np.argmax(logits))
             toks.append(nxt)
             top.append(float(logits[nxt]))
+            # the 8 largest logits of this step (stable: ties keep the lower id first)
+            order = np.argsort(-logits, kind="stable")[:8]
+            top8_idx.append(order)
+            top8_val.append(logits[order])
             if s + 1 < steps:
+                # the reference's own greedy token is fed back (a teacher-forced
+                # replay of this run feeds exactly these tokens)
                 logits = self.ref.forward(nxt, pos)
                 pos += 1
             if log_every and s % 32 == 0:
                 print(f"  decode step {s} {time.time() - t0:.0f}s", flush=True)
+        self.top8 = (np.array(top8_idx, np.int64), np.array(top8_val, np.float32))
         return np.array(toks, np.int64), np.array(margins, np.float32), np.array(top, np.float32)
 
 
@@ -279,22 +289,27 @@ def ple_cases(out):
 
 
 def decoder_small(out):
-    cfg = synth.e2b_config(hidden=256, n_layers=2, n_heads=2, head_dim=64, inter=512,
-                           vocab=2048, rope_cutoff=32)
+    cfg = synth.small_config()
     model = synth.random_model(cfg, seed=77)
     prompt = synth.prompt_tokens(12, cfg["vocab"], seed=78)
-    toks, margins, top = _RefModel(model, 64).generate(prompt, 16)
+    ref = _RefModel(model, 64)
+    toks, margins, top = ref.generate(prompt, 16)
     out["dec_small_prompt"] = np.array(prompt, np.int64)
     out["dec_small_tokens"], out["dec_small_margins"], out["dec_small_top"] = toks, margins, top
+    out["dec_small_top8_idx"], out["dec_small_top8_val"] = ref.top8
 
 
 def decoder_full(out, prompt_len, steps):
     cfg = synth.e2b_config()
     model = synth.random_model(cfg, seed=1234)
     prompt = synth.prompt_tokens(prompt_len, cfg["vocab"], seed=99)
-    toks, margins, top = _RefModel(model, prompt_len + steps).generate(prompt, steps, log_every=64)
+    ref = _RefModel(model, prompt_len + steps)
+    toks, margins, top = ref.generate(prompt, steps, log_every=64)
     out["cfg4_prompt_len"] = np.int64(prompt_len)
     out["cfg4_tokens"], out["cfg4_margins"], out["cfg4_top"] = toks, margins, top
+    out["cfg4_top8_idx"], out["cfg4_top8_val"] = ref.top8
+    print(f"  config 4: {len(set(toks.tolist()))} distinct tokens in {steps} steps; "
+          f"top-2 margin min {margins.min():.4f}, median {np.median(margins):.3f}", flush=True)
 
 
 def main():

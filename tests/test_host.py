@@ -9,7 +9,7 @@ from slang_b200 import manifest, runner, synth
 
 
 def test_manifest_roundtrip(tmp_path):
-    cfg = synth.e2b_config(hidden=256, n_layers=2, n_heads=2, head_dim=64, inter=512, vocab=2048, rope_cutoff=32)
+    cfg = synth.small_config()
     model = synth.random_model(cfg, seed=3)
     d = manifest.write(model, str(tmp_path))
     man = json.load(open(os.path.join(d, "manifest.json")))

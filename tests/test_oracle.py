@@ -95,7 +95,7 @@ def test_key_packing_orders_like_floats_with_lowest_index_ties():
 
 
 def test_decoder_small_matches_reference(golden):
-    cfg = synth.e2b_config(hidden=256, n_layers=2, n_heads=2, head_dim=64, inter=512, vocab=2048, rope_cutoff=32)
+    cfg = synth.small_config()
     model = synth.random_model(cfg, seed=77)
     o = decoder.OracleDecoder(model, 64)
     toks, margins = o.generate(list(golden["dec_small_prompt"]), 16)
@@ -108,3 +108,21 @@ def test_cfg1_gemv_matches_reference():
     g = np.load(os.path.join(GOLD, "golden_cfg1.npz"))
     packed, scales, x = synth.config1(0)
     assert max_rel(q4.gemv(packed, scales, x)[0], g["cfg1_y"]) < 1e-5
+
+
+def test_batched_prefill_equals_tokenwise_oracle():
+    """The layers-outer oracle prefill (the CPU baseline's workload) computes what
+    the token-at-a-time restatement of the reference computes."""
+    cfg = synth.small_config()
+    model = synth.random_model(cfg, seed=77)
+    prompt = synth.prompt_tokens(20, cfg["vocab"], seed=78)
+    tw = decoder.OracleDecoder(model, 32)
+    for p, t in enumerate(prompt):
+        ref = tw.forward(t, p)
+    bt = decoder.OracleDecoder(model, 32)
+    got = bt.prefill_batched(prompt)
+    assert max_rel(got, ref) < 1e-4
+    assert int(np.argmax(got)) == int(np.argmax(ref))
+    for li in range(cfg["n_layers"]):
+        assert max_rel(bt.k_cache[li][:20], tw.k_cache[li][:20]) < 1e-4
+        assert max_rel(bt.v_cache[li][:20], tw.v_cache[li][:20]) < 1e-4

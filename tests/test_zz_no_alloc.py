@@ -5,14 +5,17 @@ allocator of its own, or a process whose device memory is reserved up front by
 its own pool) get the split-K scratch from a static device array inside the
 library instead of a workspace they pass.  This test calls the new entry point
 through the C ABI twice in a row and checks each result against the existing
-entry point, sb_gemm_q4 with a caller workspace, within the tolerance the
-other GEMM parity tests use.  It lives in its own file, collected last, and
-must pass both on its own in a fresh process and after the other tests.
+entry point, sb_gemm_q4 with a caller workspace: bit for bit, since both run
+the same kernels with the same split order.  Each result is also held to the
+matmul tolerance against the float64 product of the dequantised weight (the
+oracle).  It lives in its own file, collected last, and must pass both on its
+own in a fresh process and after the other tests.
 """
 import numpy as np
 import pytest
 import torch
 
+from oracle import q4
 from slang_b200 import _lib, kernels, synth
 from tests._util import assert_close
 
@@ -26,12 +29,17 @@ def _noalloc(A, P, S, C, M, N, K):
     assert rc == _lib.SB_OK, lib.sb_last_error().decode()
 
 
-# down at M=256 splits K 12 ways, beyond the 8 splits a cluster reduces in
-# distributed shared memory, so it takes the static scratch; o / k split K
+# down at M=256 splits K beyond the splits a cluster reduces in distributed
+# shared memory, so it takes the static scratch (asserted below); o / k split K
 # inside a cluster (no scratch); gate fills the GPU without splitting
-@pytest.mark.parametrize("name,M", [("down", 256), ("o", 1024), ("k", 512), ("gate", 128), ("gate", 1024)])
+CASES = [("down", 256), ("o", 1024), ("k", 512), ("gate", 128), ("gate", 1024)]
+
+
+@pytest.mark.parametrize("name,M", CASES)
 def test_noalloc_matches_workspace_entry_point(cuda, name, M):
     N, K = synth.E2B_SHAPES[name]
+    if (name, M) == ("down", 256):
+        assert kernels.gemm_q4_workspace_size(M, N, K) > 0, "this case must exercise the static scratch"
     rng = np.random.default_rng(M + N)
     packed, scales = synth.q4_weight(rng, N, K)
     a = synth.activations(rng, M, K)
@@ -40,10 +48,14 @@ def test_noalloc_matches_workspace_entry_point(cuda, name, M):
     S = torch.from_numpy(scales).to(cuda)
     ws_bytes = kernels.gemm_q4_workspace_size(M, N, K)
     ws = torch.empty(max(1, ws_bytes // 4), dtype=torch.float32, device=cuda)
-    ref = kernels.gemm_q4(A, P, S, workspace=ws).float().cpu().numpy()
-    for _ in range(2):  # two calls in a row share (and reuse) the static scratch
+    ref = kernels.gemm_q4(A, P, S, workspace=ws).cpu().numpy()
+    c64 = q4.gemm_f64(a, q4.dequant_f16(packed, scales, 4))
+    for call in range(2):  # two calls in a row share (and reuse) the static scratch
         C = torch.full((M, N), float("nan"), dtype=torch.float16, device=cuda)
         _noalloc(A, P, S, C, M, N, K)
         torch.cuda.synchronize()
-        assert_close(C.float().cpu().numpy(), ref, what=f"noalloc {name} M={M}")
+        got = C.cpu().numpy()
+        np.testing.assert_array_equal(got.view(np.uint16), ref.view(np.uint16),
+                                      err_msg=f"noalloc {name} M={M} call {call}: not bit-identical to sb_gemm_q4")
+        assert_close(got.astype(np.float32), c64, what=f"noalloc {name} M={M} call {call} vs f64 oracle")
     kernels.device_status()

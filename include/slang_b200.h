@@ -282,6 +282,14 @@ int sb_embed_q4(const void* emb, const void* scales, int scale_dtype, int group,
                 const int32_t* tokens, int m, int k, float mult, float* out32, void* out16,
                 void* stream);
 
+/* As sb_embed_q4 for a table of 2-bit codes (four per byte, low bits first,
+ * value = code - 2): the checkpoint's embedding (gemma4/qat_loader.py:53-55,
+ * per-block f32 scales :106-113), which export.py stores as embed_q /
+ * embed_scale (gemma4_150/export.py:84-85). */
+int sb_embed_q2(const void* emb, const void* scales, int scale_dtype, int group,
+                const int32_t* tokens, int m, int k, float mult, float* out32, void* out16,
+                void* stream);
+
 /* x_out = x + rmsnorm(y) * w_add (y may be NULL: x_out = x); h = rmsnorm(x_out) * w_norm.
  * Replaces rmsadd_b + rmssrqh_b / rmssrq_69 (gemma4_150/kernels_dsl.py:622, 660, 158)
  * and the sandwich norms of gemma4/reference.py:112, 142-152.  n <= 8192. */
@@ -424,6 +432,11 @@ int sb_ple_proj_norm_add(const void* codes, const float* row_scale, const float*
  * (gemma4/reference.py:97-98). */
 int sb_gemv_bf16(const void* w, float alpha, const float* x, int ldx, float* y, int ldy,
                  int m, int n, int k, void* stream);
+
+/* As sb_gemv_bf16 with f16 weights: the per_layer_model_projection as
+ * export.py stores it (pl_model_proj, cast to f16, gemma4_150/export.py:95). */
+int sb_gemv_f16(const void* w, float alpha, const float* x, int ldx, float* y, int ldy,
+                int m, int n, int k, void* stream);
 
 /* hidden[r] = (hidden[r] + rmsnorm(proj[r]) * w_post) * layer_scalar, in place;
  * when w_next != null also h = rmsnorm(hidden[r]) * w_next -> h_out (f32)

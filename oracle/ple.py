@@ -52,11 +52,14 @@ def ple_input(x: np.ndarray, ple_rows: np.ndarray, w_proj_bf16: np.ndarray, w_no
 
     ``x`` [m, hidden] is the scaled embedding, ``ple_rows`` [m, n_layers * d]
     the output of :func:`ple_gather`, ``w_proj_bf16`` [n_layers * d, hidden]
-    the bf16 bit patterns of ``per_layer_model_projection``.
+    the bf16 bit patterns of ``per_layer_model_projection`` (or its f16 values).
     """
     x = np.atleast_2d(np.asarray(x, np.float32))
     m, hidden = x.shape
-    ctx = (x @ bf16_to_f32(w_proj_bf16).T).reshape(m, n_layers, d) * np.float32(hidden ** -0.5)
+    # export.py stores the projection cast to f16 (gemma4_150/export.py:95); the checkpoint holds bf16 bits
+    w = (np.asarray(w_proj_bf16, np.float32) if np.asarray(w_proj_bf16).dtype == np.float16
+         else bf16_to_f32(w_proj_bf16))
+    ctx = (x @ w.T).reshape(m, n_layers, d) * np.float32(hidden ** -0.5)
     ctx = rms_norm(ctx, np.asarray(w_norm, np.float32), eps)
     return (ctx + ple_rows.reshape(m, n_layers, d)) * np.float32(2.0 ** -0.5)
 

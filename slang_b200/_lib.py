@@ -37,6 +37,7 @@ SIGNATURES = {
     "sb_gemm_q4_noalloc": ([_vp, _vp, _vp, _i, _i, _vp, _i, _i, _i, _f, _i, _i, _vp], _i),
     "sb_gemm_f16_f32out": ([_vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _i, _i, _vp], _i),
     "sb_embed_q4": ([_vp, _vp, _i, _i, _vp, _i, _i, _f, _vp, _vp, _vp], _i),
+    "sb_embed_q2": ([_vp, _vp, _i, _i, _vp, _i, _i, _f, _vp, _vp, _vp], _i),
     "sb_add_rmsnorm": ([_vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _f, _vp], _i),
     "sb_qkv_prep": ([_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _vp, _vp,
                      _i64, _vp], _i),
@@ -59,6 +60,7 @@ SIGNATURES = {
     "sb_gemv_q8": ([_vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _vp, _i, _vp], _i),
     "sb_ple_proj_norm_add": ([_vp, _vp, _vp, _i, _vp, _i, _i, _i, _vp, _vp, _f, _vp, _vp, _vp, _f, _vp, _vp], _i),
     "sb_gemv_bf16": ([_vp, _f, _vp, _i, _vp, _i, _i, _i, _i, _vp], _i),
+    "sb_gemv_f16": ([_vp, _f, _vp, _i, _vp, _i, _i, _i, _i, _vp], _i),
     "sb_ple_norm_add": ([_vp, _vp, _vp, _f, _vp, _vp, _vp, _i, _i, _f, _vp], _i),
     "sb_ple_gather": ([_vp, _vp, _vp, _i, _i, _i, _f, _vp, _i, _vp], _i),
     "sb_ple_combine": ([_vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _f, _f, _vp, _i, _vp], _i),

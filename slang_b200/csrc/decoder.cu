@@ -42,16 +42,21 @@ __device__ __forceinline__ float load_act(const void* p, int is_f16, size_t i) {
 using sbd::gelu_tanh;
 
 // ---------------------------------------------------------------- embedding
+// Row gather + dequant of a packed table: BITS-bit codes, low bits first in
+// each byte (4-bit: ZP 8; 2-bit: ZP 2, the checkpoint's embedding), one scale
+// per `group` values.
+template <int BITS>
 __global__ void embed_kernel(const uint8_t* __restrict__ emb, const void* __restrict__ scales, int sf16, int group,
                              const int32_t* __restrict__ tokens, int k, float mult, float* out32, __half* out16) {
   sbd::griddep_launch_dependents();
   sbd::griddep_wait();
+  constexpr int kPer = 8 / BITS, kMask = (1 << BITS) - 1, kZp = 1 << (BITS - 1);
   const int row = blockIdx.x;
   const int64_t tok = tokens[row];
   const int gps = k / group;
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    const uint8_t b = emb[tok * (k / 2) + i / 2];
-    const int q = ((i & 1) ? (b >> 4) : (b & 15)) - 8;
+    const uint8_t b = emb[tok * (k / kPer) + i / kPer];
+    const int q = ((b >> (BITS * (i % kPer))) & kMask) - kZp;
     const size_t si = static_cast<size_t>(tok) * gps + i / group;
     const float s = sf16 ? __half2float(static_cast<const __half*>(scales)[si]) : static_cast<const float*>(scales)[si];
     // reference: (ints * repeat(scale)) * embed_scale, each product rounded in f32
@@ -696,17 +701,30 @@ int grid_for(size_t n, int per) { return static_cast<int>(std::min<size_t>((n + 
 
 }  // namespace
 
-extern "C" int sb_embed_q4(const void* emb, const void* scales, int scale_dtype, int group, const int32_t* tokens,
-                           int m, int k, float mult, float* out32, void* out16, void* stream) {
-  SB_CHECK_ARG(m >= 0 && k > 0 && k % 2 == 0 && group > 0 && k % group == 0, "sb_embed_q4: bad shape");
-  SB_CHECK_ARG(scale_dtype == SB_SCALE_F16 || scale_dtype == SB_SCALE_F32, "sb_embed_q4: bad scale dtype");
+namespace {
+template <int BITS>
+int embed_launch(const char* name, const void* emb, const void* scales, int scale_dtype, int group,
+                 const int32_t* tokens, int m, int k, float mult, float* out32, void* out16, void* stream) {
+  SB_CHECK_ARG(m >= 0 && k > 0 && k % (8 / BITS) == 0 && group > 0 && k % group == 0, "%s: bad shape", name);
+  SB_CHECK_ARG(scale_dtype == SB_SCALE_F16 || scale_dtype == SB_SCALE_F32, "%s: bad scale dtype", name);
   if (m == 0) return SB_OK;
-  SB_CHECK_ARG(emb && scales && tokens && (out32 || out16), "sb_embed_q4: null pointer");
-  cudaError_t e = sb::launch_pdl(embed_kernel, dim3(m), dim3(kT), 0, static_cast<cudaStream_t>(stream),
+  SB_CHECK_ARG(emb && scales && tokens && (out32 || out16), "%s: null pointer", name);
+  cudaError_t e = sb::launch_pdl(embed_kernel<BITS>, dim3(m), dim3(kT), 0, static_cast<cudaStream_t>(stream),
                                  static_cast<const uint8_t*>(emb), scales, static_cast<int>(scale_dtype == SB_SCALE_F16),
                                  group, tokens, k, mult, out32, static_cast<__half*>(out16));
   if (e != cudaSuccess) return sb::cuda_fail(e, "embed_kernel");
   return sb::launch_status("embed_kernel");
+}
+}  // namespace
+
+extern "C" int sb_embed_q4(const void* emb, const void* scales, int scale_dtype, int group, const int32_t* tokens,
+                           int m, int k, float mult, float* out32, void* out16, void* stream) {
+  return embed_launch<4>("sb_embed_q4", emb, scales, scale_dtype, group, tokens, m, k, mult, out32, out16, stream);
+}
+
+extern "C" int sb_embed_q2(const void* emb, const void* scales, int scale_dtype, int group, const int32_t* tokens,
+                           int m, int k, float mult, float* out32, void* out16, void* stream) {
+  return embed_launch<2>("sb_embed_q2", emb, scales, scale_dtype, group, tokens, m, k, mult, out32, out16, stream);
 }
 
 extern "C" int sb_add_rmsnorm(const float* x, const void* y, int y_dtype, const float* w_add, const float* w_norm,

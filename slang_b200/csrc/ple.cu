@@ -78,6 +78,21 @@ struct FmtBF16 {
   }
 };
 
+// 16 weight bytes -> 8 f16 values widened to f32, exact (the f16 per-layer
+// model projection export.py writes).
+struct FmtF16 {
+  static constexpr int kVals = 8;
+  __device__ static void decode(const uint4& w, float* v) {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[j]));
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  }
+};
+
 // The PLE norm-add tail run by the last CTA of a projection GEMV (counter != null):
 // hidden[r] = (hidden[r] + rmsnorm(y[r]) * w_post) * scalar, then optionally
 // h = rmsnorm(hidden[r]) * w_next.  hidden, h_out, h16 have row stride n.
@@ -473,6 +488,19 @@ extern "C" int sb_gemv_bf16(const void* w, float alpha, const float* x, int ldx,
                                             x, ldx, m, n, k, nullptr, 0, y, ldy, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return sb::cuda_fail(e, "gemv_rows_kernel<bf16>");
   return sb::launch_status("gemv_rows_kernel<bf16>");
+}
+
+extern "C" int sb_gemv_f16(const void* w, float alpha, const float* x, int ldx, float* y, int ldy, int m, int n,
+                           int k, void* stream) {
+  SB_CHECK_ARG(m >= 0 && n > 0 && k >= 32 && k % 8 == 0, "sb_gemv_f16: k=%d must be a multiple of 8 and >= 32", k);
+  SB_CHECK_ARG(ldx >= k && ldx % 4 == 0 && ldy >= n, "sb_gemv_f16: bad leading dimension");
+  if (m == 0) return SB_OK;
+  SB_CHECK_ARG(w && x && y, "sb_gemv_f16: null pointer");
+  if (!sb::aligned(w, 16) || !sb::aligned(x, 16)) return sb::fail(SB_ERR_ALIGN, "sb_gemv_f16: w and x need 16-byte alignment");
+  cudaError_t e = launch_gemv_rows<FmtF16>(static_cast<const uint8_t*>(w), 2 * static_cast<int64_t>(k), nullptr, alpha,
+                                           x, ldx, m, n, k, nullptr, 0, y, ldy, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return sb::cuda_fail(e, "gemv_rows_kernel<f16>");
+  return sb::launch_status("gemv_rows_kernel<f16>");
 }
 
 extern "C" int sb_ple_norm_add(const float* proj, float* hidden, const float* w_post, float layer_scalar,

@@ -305,8 +305,10 @@ def gemv_q8(codes: torch.Tensor, row_scale: torch.Tensor, x: torch.Tensor, out: 
 
 
 def gemv_bf16(w: torch.Tensor, x: torch.Tensor, alpha: float = 1.0, out: torch.Tensor | None = None) -> torch.Tensor:
-    """``y = alpha * x @ w.T`` for a bf16 weight [n, k] (``sb_gemv_bf16``), f32 rows in and out."""
-    _need(w, "w", (torch.bfloat16, torch.int16))
+    """``y = alpha * x @ w.T`` for a bf16 weight [n, k] (``sb_gemv_bf16``; an f16
+    weight, as export.py stores the per-layer projection, takes ``sb_gemv_f16``),
+    f32 rows in and out."""
+    _need(w, "w", (torch.bfloat16, torch.int16, torch.float16))
     n, k = w.shape
     x2 = x.reshape(-1, k) if x.is_contiguous() else x
     ldx = _rows(x2, "x", k)
@@ -314,7 +316,8 @@ def gemv_bf16(w: torch.Tensor, x: torch.Tensor, alpha: float = 1.0, out: torch.T
     if out is None:
         out = torch.empty(m, n, dtype=torch.float32, device=x.device)
     ldy = _rows(out, "out", n)
-    _lib.call("sb_gemv_bf16", _ptr(w), float(alpha), _ptr(x2), ldx, _ptr(out), ldy, m, n, k, _stream())
+    fn = "sb_gemv_f16" if w.dtype == torch.float16 else "sb_gemv_bf16"
+    _lib.call(fn, _ptr(w), float(alpha), _ptr(x2), ldx, _ptr(out), ldy, m, n, k, _stream())
     return out
 
 

@@ -51,8 +51,35 @@ def _interleave(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     return out
 
 
+def layer_specs(cfg: dict) -> list[dict]:
+    """Per-layer structure: ``cfg["layer_specs"]`` (a reference export carries
+    one per layer, gemma4_150/export.py:159-165) or the config's uniform layer."""
+    if cfg.get("layer_specs"):
+        return cfg["layer_specs"]
+    return [{"head_dim": cfg["head_dim"], "q_dim": cfg["q_dim"], "inter": cfg["inter"], "kv_source": i,
+             "sliding": bool(cfg.get("sliding_window", 0)), "rope_theta": cfg["rope_theta"],
+             "rope_cutoff": cfg["rope_cutoff"]} for i in range(cfg["n_layers"])]
+
+
+def _bits(packed: np.ndarray, n_in: int) -> int:
+    """Code width of a packed weight from its row length (the reference's ``_dq``
+    reads it off the buffer size, gemma4_150/prefill_gpu.py:186-196)."""
+    bits = packed.shape[-1] * 8 // n_in
+    if bits not in (2, 4) or bits * n_in != packed.shape[-1] * 8:
+        raise ValueError(f"a packed row of {packed.shape[-1]} bytes holds no 2- or 4-bit codes of {n_in} values")
+    return bits
+
+
 class DeviceModel:
-    """The model's weights on one GPU in the layouts the kernels consume."""
+    """The model's weights on one GPU in the layouts the kernels consume.
+
+    Takes either weight format ``manifest.read`` produces: 4-bit codes with
+    per-group-32 f16 scales (the benchmark format) or the reference export's
+    per-row f32 scales with 2- or 4-bit codes per matrix, a 2-bit embedding
+    with per-block scales and a separate 2-bit lm_head.  The GPU runner takes
+    layers of one shape that each own their K/V, and sliding-window layers
+    only while ``max_seq`` is within the window (where the window masks
+    nothing); other architectures are refused with ValueError."""
 
     def __init__(self, model: dict, device, max_seq: int):
         cfg = model["config"]
@@ -60,16 +87,33 @@ class DeviceModel:
         self.device = torch.device(device)
         self.max_seq = max_seq
         dev = self.device
+        specs = layer_specs(cfg)
+        self._check(cfg, specs, max_seq)
+        H = cfg["hidden"]
 
         def T(a, dtype=None):
-            t = torch.from_numpy(np.ascontiguousarray(a))
+            t = torch.from_numpy(np.array(a, copy=True))
             return t.to(device=dev, dtype=dtype) if dtype is not None else t.to(dev)
 
         self.embed_q = T(model["embed_q"])
         self.embed_s = T(model["embed_scale"])
+        self.embed_bits = _bits(model["embed_q"], H)
+        self.embed_group = kern.group_of(self.embed_s, H)
+        if "lm_q" in model:  # a separate lm_head (export.py's lmhead_blk)
+            self.lm_q, self.lm_s = T(model["lm_q"]), T(model["lm_scale"])
+        else:  # tied (gemma4/reference.py:178)
+            self.lm_q, self.lm_s = self.embed_q, self.embed_s
+        self.lm_bits = _bits(self.lm_q, H)
         self.final_norm = T(model["final_norm"], torch.float32)
         self.layers = []
-        for L in model["layers"]:
+        self._rope: dict = {}
+        group32 = self.embed_bits == 4 and self.lm_bits == 4 and self.lm_q is self.embed_q
+        for li, (L, sp) in enumerate(zip(model["layers"], specs)):
+            bits = {"qkv": _bits(L["q"][0], H), "o": _bits(L["o"][0], sp["q_dim"]), "gu": _bits(L["gate"][0], H),
+                    "down": _bits(L["down"][0], sp["inter"])}
+            if _bits(L["k"][0], H) != bits["qkv"] or _bits(L["v"][0], H) != bits["qkv"] or \
+                    _bits(L["up"][0], H) != bits["gu"]:
+                raise ValueError(f"layer {li}: q/k/v (or gate/up) weights of different code widths")
             d = {
                 "qkv": (T(np.concatenate([L["q"][0], L["k"][0], L["v"][0]])),
                         T(np.concatenate([L["q"][1], L["k"][1], L["v"][1]]))),
@@ -77,25 +121,64 @@ class DeviceModel:
                 # gate row i and up row i adjacent: GEGLU pairs neighbouring outputs
                 "gu": (T(_interleave(L["gate"][0], L["up"][0])), T(_interleave(L["gate"][1], L["up"][1]))),
                 "down": (T(L["down"][0]), T(L["down"][1])),
+                "bits": bits,
             }
             for n in ("in_norm", "q_norm", "k_norm", "post_attn_norm", "pre_ffn_norm", "post_ffn_norm"):
                 d[n] = T(L[n], torch.float32)
+            key = (sp["rope_theta"], sp["rope_cutoff"])
+            if key not in self._rope:
+                cos, sin = rope_tables(max_seq, sp["head_dim"], *key)
+                self._rope[key] = (T(cos), T(sin))
+            d["cos"], d["sin"] = self._rope[key]
+            group32 = group32 and all(b == 4 for b in bits.values()) and all(
+                d[k][1].dtype == torch.float16 and kern.group_of(d[k][1], d[k][0].shape[1] * 2) == 32
+                for k in ("qkv", "o", "gu", "down"))
             self.layers.append(d)
-        cos, sin = rope_tables(max_seq, cfg["head_dim"], cfg["rope_theta"], cfg["rope_cutoff"])
-        self.cos, self.sin = T(cos), T(sin)
-        # per-layer embeddings (the dict of synth.ple_weights), when the model has them
+        self.cos, self.sin = self.layers[0]["cos"], self.layers[0]["sin"]
+        # the persistent one-launch decode step and the GEMM-argmax lm_head take
+        # the benchmark format only (4-bit codes, f16 group-32 scales, tied table)
+        self.group32_f16 = group32 and self.embed_s.dtype == torch.float16 and self.embed_group == 32
+        # per-layer embeddings (the dict of synth.ple_weights or of a reference export), when the model has them
         self.ple = None
         P = model.get("ple")
         if P is not None:
-            proj = T(P["proj"].view(np.int16))
+            if P["proj"].dtype == np.float16:  # export.py's f16 cast (gemma4_150/export.py:95)
+                proj = proj16 = T(P["proj"])
+            else:  # the checkpoint's bf16 bit patterns
+                proj = T(P["proj"].view(np.int16))
+                proj16 = proj.view(torch.bfloat16).to(torch.float16)  # for the prefill GEMM (made once, at load)
             self.ple = {"table": T(P["table"]), "table_scale": T(P["table_scale"], torch.float32), "proj": proj,
-                        # f16 copy of the bf16 model projection for the prefill GEMM (made once, at load)
-                        "proj16": proj.view(torch.bfloat16).to(torch.float16),
-                        "norm": T(P["norm"], torch.float32), "scale": float(P["ple_scale"]), "d": int(P["d"])}
+                        "proj16": proj16, "norm": T(P["norm"], torch.float32), "scale": float(P["ple_scale"]),
+                        "d": int(P["d"])}
             for d, PL in zip(self.layers, P["layers"]):
                 d["ple"] = {"gate": (T(PL["gate"][0]), T(PL["gate"][1], torch.float32)),
                             "proj": (T(PL["proj"][0]), T(PL["proj"][1], torch.float32)),
                             "post_norm": T(PL["post_norm"], torch.float32), "scalar": float(PL["scalar"])}
+
+    @staticmethod
+    def _check(cfg: dict, specs: list, max_seq: int) -> None:
+        sp0 = specs[0]
+        for i, sp in enumerate(specs):
+            if (sp["head_dim"], sp["q_dim"], sp["inter"]) != (sp0["head_dim"], sp0["q_dim"], sp0["inter"]):
+                raise ValueError(f"layer {i} differs in head_dim / q_dim / FFN width from layer 0; the GPU runner "
+                                 "takes layers of one shape")
+            if sp["kv_source"] != i:
+                raise ValueError(f"layer {i} reads the K/V of layer {sp['kv_source']}; the GPU runner takes layers "
+                                 "that own their K/V")
+            if sp["sliding"] and cfg.get("sliding_window", 0) and max_seq > cfg["sliding_window"]:
+                raise ValueError(f"max_seq {max_seq} exceeds the sliding window {cfg['sliding_window']} of layer {i};"
+                                 " the GPU runner attends over the full causal context")
+
+    def embed(self, tokens_ptr: int, m: int, out32, out16, stream: int) -> None:
+        """Scaled embedding rows of ``m`` tokens (``embed_00``, gemma4/reference.py:168)."""
+        fn = "sb_embed_q4" if self.embed_bits == 4 else "sb_embed_q2"
+        _lib.call(fn, self.embed_q.data_ptr(), self.embed_s.data_ptr(), kern._DT[self.embed_s.dtype],
+                  self.embed_group, tokens_ptr, m, self.cfg["hidden"], float(self.cfg["embed_scale"]), out32, out16,
+                  stream)
+
+    def lmhead_argmax(self, h, keys, tokens, logits=None):
+        """lm_head GEMV + greedy argmax of hidden rows ``h``."""
+        return kern.lmhead_argmax(self.lm_q, self.lm_s, h, keys=keys, tokens=tokens, logits=logits, bits=self.lm_bits)
 
 
 class Runner:
@@ -119,6 +202,9 @@ class Runner:
             raise ValueError("the persistent decode kernel serves one sequence")
         if dm.ple is not None and (fused or proj != "gemv"):
             raise ValueError("per-layer embeddings run on the per-op GEMV decode path (fused=False, proj='gemv')")
+        if (fused or proj == "gemm") and not dm.group32_f16:
+            raise ValueError("the persistent decode step and the GEMM decode path take 4-bit weights with f16 "
+                             "group-32 scales and a tied lm_head; use fused=False, proj='gemv'")
         self.proj = proj
         self.fused = fused
         self.dm = dm
@@ -168,8 +254,8 @@ class Runner:
         self._pgraphs: dict = {}  # (prompt length, sequence) -> captured prefill
 
     # ------------------------------------------------------------------ decode
-    def _gemv(self, w, x, y):
-        kern.gemv_q4(w[0], w[1], x, y=y)
+    def _gemv(self, L, key, x, y):
+        kern.gemv_q4(L[key][0], L[key][1], x, y=y, bits=L["bits"][key])
 
     def _decode_ops_gemm(self):
         """One decode step for the batch on the tcgen05 GEMM: f16 activations
@@ -182,14 +268,13 @@ class Runner:
         def proj(w, A, C, geglu=False):
             kern.gemm_q4(A, w[0], w[1], C=C, workspace=ws, geglu=geglu)
 
-        _lib.call("sb_embed_q4", dm.embed_q.data_ptr(), dm.embed_s.data_ptr(), _F16, dm.cfg["group"],
-                  self.cur.data_ptr(), B, H, float(dm.cfg["embed_scale"]), self.x.data_ptr(), None, s)
+        dm.embed(self.cur.data_ptr(), B, self.x.data_ptr(), None, s)
         _lib.call("sb_add_rmsnorm", self.x.data_ptr(), None, _F32, None, L0[0]["in_norm"].data_ptr(),
                   self.x.data_ptr(), None, self.h16.data_ptr(), B, H, self.eps, s)
         for li, L in enumerate(L0):
             proj(L["qkv"], self.h16, self.qkv16)
             _lib.call("sb_qkv_prep", self.qkv16.data_ptr(), _F16, self.nqkv, L["q_norm"].data_ptr(),
-                      L["k_norm"].data_ptr(), dm.cos.data_ptr(), dm.sin.data_ptr(), self.pos.data_ptr(), 0, B,
+                      L["k_norm"].data_ptr(), L["cos"].data_ptr(), L["sin"].data_ptr(), self.pos.data_ptr(), 0, B,
                       self.nh, self.hd, self.eps, None, self.q.data_ptr(), self.kc[li].data_ptr(),
                       self.vc[li].data_ptr(), None, None, self.cache_stride, s)
             _lib.call("sb_attn_decode_f16", self.q.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
@@ -214,8 +299,7 @@ class Runner:
         s = kern._stream()
         lib = _lib.load()
         B, H = self.B, self.H
-        _lib.call("sb_embed_q4", dm.embed_q.data_ptr(), dm.embed_s.data_ptr(), _F16, dm.cfg["group"],
-                  self.cur.data_ptr(), B, H, float(dm.cfg["embed_scale"]), self.x.data_ptr(), None, s)
+        dm.embed(self.cur.data_ptr(), B, self.x.data_ptr(), None, s)
         P = dm.ple
         if P is not None:  # per-layer inputs from the scaled embedding (gemma4/reference.py:170)
             kern.ple_input(self.x, self.cur, P["table"], P["table_scale"], P["proj"], P["norm"], len(L0), P["d"],
@@ -223,20 +307,20 @@ class Runner:
         _lib.call("sb_add_rmsnorm", self.x.data_ptr(), None, _F32, None, L0[0]["in_norm"].data_ptr(),
                   self.x.data_ptr(), self.h.data_ptr(), None, B, H, self.eps, s)
         for li, L in enumerate(L0):
-            self._gemv(L["qkv"], self.h, self.qkv)
+            self._gemv(L, "qkv", self.h, self.qkv)
             _lib.call("sb_qkv_prep", self.qkv.data_ptr(), _F32, self.nqkv, L["q_norm"].data_ptr(),
-                      L["k_norm"].data_ptr(), dm.cos.data_ptr(), dm.sin.data_ptr(), self.pos.data_ptr(), 0, B,
+                      L["k_norm"].data_ptr(), L["cos"].data_ptr(), L["sin"].data_ptr(), self.pos.data_ptr(), 0, B,
                       self.nh, self.hd, self.eps, None, self.q.data_ptr(), self.kc[li].data_ptr(),
                       self.vc[li].data_ptr(), None, None, self.cache_stride, s)
             _lib.call("sb_attn_decode", self.q.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
                       self.cache_stride, self.pos.data_ptr(), B, self.nh, self.hd, self.max_seq,
                       self.attn.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws.numel() * 4, s)
-            self._gemv(L["o"], self.attn, self.o)
+            self._gemv(L, "o", self.attn, self.o)
             _lib.call("sb_add_rmsnorm", self.x.data_ptr(), self.o.data_ptr(), _F32, L["post_attn_norm"].data_ptr(),
                       L["pre_ffn_norm"].data_ptr(), self.x.data_ptr(), self.h.data_ptr(), None, B, H, self.eps, s)
-            self._gemv(L["gu"], self.h, self.gu)
+            self._gemv(L, "gu", self.h, self.gu)
             _lib.call("sb_geglu", self.gu.data_ptr(), _F32, B, self.F, self.a.data_ptr(), None, s)
-            self._gemv(L["down"], self.a, self.d)
+            self._gemv(L, "down", self.a, self.d)
             nxt = L0[li + 1]["in_norm"] if li + 1 < len(L0) else dm.final_norm
             _lib.call("sb_add_rmsnorm", self.x.data_ptr(), self.d.data_ptr(), _F32, L["post_ffn_norm"].data_ptr(),
                       nxt.data_ptr(), self.x.data_ptr(), self.h.data_ptr(), None, B, H, self.eps, s)
@@ -251,7 +335,7 @@ class Runner:
                     kern.gemv_q8(Lp["proj"][0], Lp["proj"][1], self.ple_g, out=self.ple_proj)
                     kern.ple_norm_add(self.ple_proj, self.x, Lp["post_norm"], Lp["scalar"], self.eps, w_next=nxt,
                                       h_out=self.h)
-        kern.lmhead_argmax(dm.embed_q, dm.embed_s, self.h, keys=self.keys, tokens=self.tok)
+        dm.lmhead_argmax(self.h, self.keys, self.tok)
         _lib.call("sb_step_advance", self.pos.data_ptr(), self.tok.data_ptr(), self.cur.data_ptr(),
                   self.history.data_ptr(), self.max_seq, B, s)
         del lib
@@ -410,8 +494,7 @@ class Runner:
         s = kern._stream()
         self._prefill_ops(pf, S, seq, s, rec)
         # first greedy token from the last prompt position
-        kern.lmhead_argmax(dm.embed_q, dm.embed_s, pf["hlast"][S - 1:S], keys=self.keys[seq:seq + 1],
-                           tokens=self.tok[seq:seq + 1])
+        dm.lmhead_argmax(pf["hlast"][S - 1:S], self.keys[seq:seq + 1], self.tok[seq:seq + 1])
         self.cur[seq:seq + 1].copy_(self.tok[seq:seq + 1])
         self.pos[seq:seq + 1].fill_(S)
         self.history[seq, S:S + 1].copy_(self.tok[seq:seq + 1])
@@ -447,17 +530,17 @@ class Runner:
         H, nh, hd, F = self.H, self.nh, self.hd, self.F
         ws = pf["ws"]
 
-        def proj(name, A, W, C, K, geglu=False):
+        def proj(name, A, L, key, C, K, geglu=False):
+            W = L[key]
             if rec is not None:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(self.stream)
-            kern.gemm_q4(A, W[0], W[1], C=C, workspace=ws, geglu=geglu)
+            kern.gemm_q4(A, W[0], W[1], C=C, workspace=ws, geglu=geglu, bits=L["bits"][key])
             if rec is not None:
                 e1.record(self.stream)
                 rec.append((name, S, W[0].shape[0], K, e0, e1))
 
-        _lib.call("sb_embed_q4", dm.embed_q.data_ptr(), dm.embed_s.data_ptr(), _F16, dm.cfg["group"],
-                  pf["tok"].data_ptr(), S, H, float(dm.cfg["embed_scale"]), pf["hid"].data_ptr(), None, s)
+        dm.embed(pf["tok"].data_ptr(), S, pf["hid"].data_ptr(), None, s)
         P = dm.ple
         if P is not None:
             # per-layer inputs of the whole prompt: the model projection as an f16 GEMM (f32 out), then the
@@ -473,22 +556,22 @@ class Runner:
                   pf["hid"].data_ptr(), None, pf["h16"].data_ptr(), S, H, self.eps, s)
         kc_off = seq * self.cache_stride * 4
         for li, L in enumerate(Ls):
-            proj("qkv", pf["h16"][:S], L["qkv"], pf["qkv16"][:S], H)
+            proj("qkv", pf["h16"][:S], L, "qkv", pf["qkv16"][:S], H)
             _lib.call("sb_qkv_prep", pf["qkv16"].data_ptr(), _F16, self.nqkv, L["q_norm"].data_ptr(),
-                      L["k_norm"].data_ptr(), dm.cos.data_ptr(), dm.sin.data_ptr(), None, 0, S, nh, hd, self.eps,
+                      L["k_norm"].data_ptr(), L["cos"].data_ptr(), L["sin"].data_ptr(), None, 0, S, nh, hd, self.eps,
                       pf["q16"].data_ptr(), None, self.kc[li].data_ptr() + kc_off, self.vc[li].data_ptr() + kc_off,
                       pf["k16"].data_ptr(), pf["v16"].data_ptr(), self.cache_stride, s)
             # causal attention over the prompt: one fused kernel
             _lib.call("sb_attn_prefill_ws", pf["q16"].data_ptr(), pf["k16"].data_ptr(), pf["v16"].data_ptr(),
                       pf["attn16"].data_ptr(), S, nh, hd, pf["attn_ws"].data_ptr(),
                       pf["attn_ws"].numel() * 4, s)
-            proj("o", pf["attn16"][:S], L["o"], pf["o16"][:S], self.qd)
+            proj("o", pf["attn16"][:S], L, "o", pf["o16"][:S], self.qd)
             _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), pf["o16"].data_ptr(), _F16,
                       L["post_attn_norm"].data_ptr(), L["pre_ffn_norm"].data_ptr(), pf["hid"].data_ptr(), None,
                       pf["h16"].data_ptr(), S, H, self.eps, s)
             # gate|up GEMM with GEGLU in its epilogue: writes a = gelu(gate) * up
-            proj("gate|up", pf["h16"][:S], L["gu"], pf["a16"][:S], H, geglu=True)
-            proj("down", pf["a16"][:S], L["down"], pf["d16"][:S], F)
+            proj("gate|up", pf["h16"][:S], L, "gu", pf["a16"][:S], H, geglu=True)
+            proj("down", pf["a16"][:S], L, "down", pf["d16"][:S], F)
             last = li + 1 == len(Ls)
             nxt = Ls[li + 1]["in_norm"] if not last else dm.final_norm
             _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), pf["d16"].data_ptr(), _F16,

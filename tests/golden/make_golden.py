@@ -312,6 +312,142 @@ def decoder_full(out, prompt_len, steps):
           f"top-2 margin min {margins.min():.4f}, median {np.median(margins):.3f}", flush=True)
 
 
+# ---------------------------------------------------------------- reference export
+EXPORT_DIR = os.path.join(HERE, "export_small")
+
+
+def _safetensors(path, tensors):
+    """Write ``{name: (dtype tag, array)}`` as a safetensors file (8-byte
+    little-endian header length, JSON header, raw little-endian data)."""
+    import json
+    import struct
+    header, blobs, off = {}, [], 0
+    for name, (tag, arr) in tensors.items():
+        b = np.ascontiguousarray(arr).tobytes()
+        header[name] = {"dtype": tag, "shape": list(arr.shape), "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    h = json.dumps(header).encode()
+    h += b" " * ((-len(h)) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        for b in blobs:
+            f.write(b)
+
+
+def export_checkpoint(model_dir, H=256, nL=3, nH=2, hd=64, inter=512, vocab=768, d=256, seed=5150,
+                      ffn_gain=30.0):
+    """A synthetic QAT checkpoint with the reference checkpoint's tensor names,
+    dtypes and bit widths (gemma4_150/loader.py:23-32, 62-73;
+    gemma4/qat_loader.py:53-62): 4-bit attention and MLP weights with per-row
+    f32 ``weight_scale`` [n_out, 1], 2-bit embedding with [vocab, 1] scales, a
+    separate 2-bit ``lm_head.weight`` holding the same codes and scales (so the
+    tied head of the weight-only reference and the exported head agree), the
+    4-bit per-layer table with one scale per d values, int8 PLE linears, bf16
+    norms and per-layer projection, scalar SRQ activation scales.  vocab is a
+    multiple of 6 so export.py's [24, -1, 4] lm_head re-layout divides evenly."""
+    import json
+    from slang_b200.synth import f32_to_bf16_bits, q8_weight
+    rng = np.random.default_rng(seed)
+    LMP = "model.language_model."
+    t = {}
+
+    def bf16(a):
+        return ("BF16", f32_to_bf16_bits(np.asarray(a, np.float32)))
+
+    def norm(n, gain=1.0):
+        return bf16(gain * (1.0 + 0.1 * rng.standard_normal(n)))
+
+    def codes(n_out, n_in, bits):
+        per = 8 // bits
+        # codes from 1: zero-mean values, 4-bit in [-7, 7], 2-bit in [-1, 1]
+        c = rng.integers(1, 1 << bits, (n_out, n_in), dtype=np.uint8)
+        packed = np.zeros((n_out, n_in // per), np.uint8)
+        for j in range(per):
+            packed |= (c[:, j::per] << (bits * j)).astype(np.uint8)
+        return packed
+
+    def linear(name, n_out, n_in, bits, lo=0.01, hi=0.03):
+        t[name + ".weight"] = ("U8", codes(n_out, n_in, bits))
+        t[name + ".weight_scale"] = ("F32", rng.uniform(lo, hi, (n_out, 1)).astype(np.float32))
+        t[name + ".input_activation_scale"] = ("F32", np.array(0.05, np.float32))
+        t[name + ".output_activation_scale"] = ("F32", np.array(0.05, np.float32))
+
+    emb = codes(vocab, H, 2)
+    emb_scale = rng.uniform(0.02, 0.06, (vocab, 1)).astype(np.float32)
+    t[LMP + "embed_tokens.embedding_quantized"] = ("U8", emb)
+    t[LMP + "embed_tokens.embedding_scale"] = ("F32", emb_scale)
+    t["lm_head.weight"] = ("U8", emb.copy())
+    t["lm_head.weight_scale"] = ("F32", emb_scale.copy())
+    t[LMP + "embed_tokens_per_layer.embedding_quantized"] = ("U8", codes(vocab, nL * d, 4))
+    t[LMP + "embed_tokens_per_layer.embedding_scale"] = ("F32", np.abs(rng.normal(0, 0.01, (vocab, nL))).astype(np.float32))
+    t[LMP + "per_layer_model_projection.weight"] = bf16(rng.normal(0, 0.02, (nL * d, H)))
+    t[LMP + "norm.weight"] = norm(H)
+    t[LMP + "per_layer_projection_norm.weight"] = norm(d)
+    for L in range(nL):
+        p = f"{LMP}layers.{L}."
+        for n, size, gain in (("input_layernorm", H, 1.0), ("self_attn.q_norm", hd, 0.1), ("self_attn.k_norm", hd, 0.1),
+                              ("post_attention_layernorm", H, 1.0), ("pre_feedforward_layernorm", H, 1.0),
+                              ("post_feedforward_layernorm", H, ffn_gain), ("post_per_layer_input_norm", H, 1.0)):
+            t[p + n + ".weight"] = norm(size, gain)
+        t[p + "layer_scalar"] = bf16(rng.uniform(0.7, 1.3, 1))
+        for m, n_out, n_in in (("self_attn.q_proj", nH * hd, H), ("self_attn.k_proj", hd, H),
+                               ("self_attn.v_proj", hd, H), ("self_attn.o_proj", H, nH * hd),
+                               ("mlp.gate_proj", inter, H), ("mlp.up_proj", inter, H), ("mlp.down_proj", H, inter)):
+            linear(p + m, n_out, n_in, 4)
+        for m, n_out, n_in in (("per_layer_input_gate", d, H), ("per_layer_projection", H, d)):
+            c, sc = q8_weight(rng, n_out, n_in, 0.5 / (74.0 * np.sqrt(n_in)), 1.5 / (74.0 * np.sqrt(n_in)))
+            t[p + m + ".weight"] = ("I8", (c.astype(np.int16) - 128).astype(np.int8))
+            t[p + m + ".weight_scale"] = ("F32", sc.reshape(-1, 1))
+            t[p + m + ".input_activation_scale"] = ("F32", np.array(0.05, np.float32))
+            t[p + m + ".output_activation_scale"] = ("F32", np.array(0.05, np.float32))
+    os.makedirs(model_dir, exist_ok=True)
+    _safetensors(os.path.join(model_dir, "model.safetensors"), t)
+    cfg = {"text_config": {
+        "hidden_size": H, "num_hidden_layers": nL, "num_attention_heads": nH, "num_key_value_heads": 1,
+        "vocab_size": vocab, "rms_norm_eps": 1e-6, "sliding_window": 512, "final_logit_softcapping": 30.0,
+        "hidden_size_per_layer_input": d, "bos_token_id": 2, "eos_token_id": 1, "num_kv_shared_layers": 0,
+        "layer_types": ["sliding_attention"] * nL,
+        "rope_parameters": {"sliding_attention": {"rope_theta": 10000.0},
+                            "full_attention": {"rope_theta": 1000000.0, "partial_rotary_factor": 0.25}}}}
+    with open(os.path.join(model_dir, "config.json"), "w") as f:
+        json.dump(cfg, f)
+
+
+def export_case(prompt_len=10, steps=16):
+    """Run the reference's ``gemma4_150.export.export`` on the synthetic
+    checkpoint (its manifest.json + weights.bin are the fixture) and the
+    reference's weight-only ``QATReference`` (ple=True) on the same checkpoint
+    for the expected greedy tokens, margins and per-step top-8 logits."""
+    import shutil
+    import tempfile
+    from gemma4.loader import Gemma4Config
+    from gemma4.qat_loader import QATIndex
+    from gemma4.qat_reference import QATReference
+    from gemma4_150.export import export
+    tmp = tempfile.mkdtemp(prefix="slang_export_")
+    try:
+        export_checkpoint(tmp)
+        out_dir = export(tmp)
+        os.makedirs(EXPORT_DIR, exist_ok=True)
+        for name in ("manifest.json", "weights.bin"):
+            shutil.copy(os.path.join(out_dir, name), os.path.join(EXPORT_DIR, name))
+        qat = QATIndex(tmp)
+        config = Gemma4Config(os.path.join(tmp, "config.json"), qat.idx)
+        ref = QATReference(config, qat, max_seq=prompt_len + steps + 1, ple=True)
+        holder = SimpleNamespace(ref=ref)
+        prompt = synth.prompt_tokens(prompt_len, config.vocab_size, seed=5151)
+        toks, margins, top = _RefModel.generate(holder, prompt, steps)
+        out = {"prompt": np.array(prompt, np.int64), "tokens": toks, "margins": margins, "top": top,
+               "top8_idx": holder.top8[0], "top8_val": holder.top8[1]}
+        np.savez_compressed(os.path.join(EXPORT_DIR, "golden_export.npz"), **out)
+        print(f"export case: {len(set(toks.tolist()))} distinct tokens in {steps}; margins min "
+              f"{margins.min():.4f}; weights.bin {os.path.getsize(os.path.join(EXPORT_DIR, 'weights.bin'))} B")
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
 def main():
     global REF
     ap = argparse.ArgumentParser()
@@ -335,6 +471,8 @@ def main():
         decoder_small(out)
         np.savez_compressed(os.path.join(HERE, "golden_small.npz"), **out)
         print("wrote golden_small.npz", len(out))
+    if want("export"):
+        export_case()
     if want("ple"):
         out = {}
         ple_cases(out)

@@ -53,7 +53,7 @@ def test_small_decoder_tokens_match_reference(cuda, golden, batched):
     model = small_model()
     prompt = [int(t) for t in golden["dec_small_prompt"]]
     ref = golden["dec_small_tokens"]
-    assert len(set(ref.tolist())) >= 6, "the fixture's trajectory should move"
+    assert len(set(ref.tolist())) >= 8, "the fixture's trajectory should move"
     toks = runner.greedy_generate(model, prompt, 17, device=cuda, batched_prefill=batched, max_seq=64)
     first_divergence(toks[:16], ref, golden["dec_small_margins"], TOL_F16 if batched else TOL_F32,
                      f"small decoder batched={batched}")
@@ -121,8 +121,8 @@ def test_batch_of_sequences_is_independent(cuda, golden):
 
 
 def mid_model():
-    """Full-width layers (hidden 1536, 8 heads of 256, FFN 6144) but 3 layers and a 16384-row vocabulary."""
-    return synth.random_model(synth.e2b_config(n_layers=3, vocab=16384), seed=21)
+    """Full-width layers (hidden 1536, 8 heads of 256, FFN 6144), 4 layers, a 16384-row vocabulary."""
+    return synth.random_model(synth.mid_config(), seed=21)
 
 
 @pytest.mark.parametrize("fused", [False, True])
@@ -145,7 +145,7 @@ def test_mid_model_decode_vs_oracle(cuda, fused):
     o = odec.OracleDecoder(model, 64)
     for p_, t in enumerate(prompt[:20]):
         o.forward(t, p_)
-    for li in range(3):
+    for li in range(4):
         for got_, ref_ in ((r.kc[li][0, :20], o.k_cache[li][:20]), (r.vc[li][0, :20], o.v_cache[li][:20])):
             rel = np.linalg.norm(got_.cpu().numpy() - ref_) / np.linalg.norm(ref_)
             assert rel < 2e-4, f"layer {li}: KV rel-L2 {rel:.2e}"

@@ -155,6 +155,14 @@ int sb_lmhead_argmax_peer(const void* emb, const void* scales, int scale_dtype, 
                           int m, int v, int k, int64_t row_offset, const uint64_t* peer_mailboxes, int world,
                           void* own_mailbox, uint64_t* keys, int32_t* tokens, void* stream);
 
+/* How long sb_lmhead_argmax_peer's exchange waits for the other ranks to count
+ * in before it gives up with SB_ERR_TIMEOUT (in sb_device_status) and returns
+ * keys of 0: ns nanoseconds, 0 for the default (and maximum) of 2 s.  A rank
+ * that never arrives then costs the others this long instead of a hang.
+ * Applies to launches made after the call.  No counterpart in the reference
+ * (single-device). */
+int sb_peer_set_wait_limit_ns(uint64_t ns);
+
 /*
  * f16 GEMM on the tcgen05 tensor cores, f32 accumulate:
  *   C[M, N] = f16(alpha * A[M, K] @ (B[N, K]^T if tr else B[K, N]))

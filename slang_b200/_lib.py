@@ -46,6 +46,7 @@ SIGNATURES = {
     "sb_attn_prefill": ([_vp, _vp, _vp, _vp, _i, _i, _i, _vp], _i),
     "sb_attn_prefill_ws": ([_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp], _i),
     "sb_peer_mailbox_size": ([], _sz),
+    "sb_peer_set_wait_limit_ns": ([C.c_uint64], _i),
     "sb_peer_buffer_create": ([_sz, _vp, _vp], _i),
     "sb_peer_buffer_open": ([_vp, _vp], _i),
     "sb_peer_buffer_close": ([_vp], _i),

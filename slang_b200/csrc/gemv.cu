@@ -32,6 +32,8 @@
 #include <algorithm>
 #include <cstring>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "q4_dot.cuh"
 
@@ -788,7 +790,7 @@ namespace {
 // Slots alternate by step parity: a rank writes step e + 1's keys only after
 // every rank has passed its step-e count, i.e. after this rank cleared them.
 __global__ void peer_combine_kernel(uint8_t* own, const unsigned long long* peers, int world, int m,
-                                    unsigned long long* keys_out, int32_t* tokens, int* err) {
+                                    unsigned long long* keys_out, int32_t* tokens, int* err, uint64_t wait_ns) {
   __shared__ int ok;
   uint32_t* epoch = reinterpret_cast<uint32_t*>(own + sbd::kMailEpoch);
   uint32_t* count = reinterpret_cast<uint32_t*>(own + sbd::kMailCount);
@@ -807,7 +809,7 @@ __global__ void peer_combine_kernel(uint8_t* own, const unsigned long long* peer
       uint32_t c;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(c) : "l"(count + q) : "memory");
       if (c >= static_cast<uint32_t>(world)) done = 1;
-      else if (sbd::global_ns() - t0 > sbd::kWaitLimitNs) break;
+      else if (sbd::global_ns() - t0 > wait_ns) break;
     }
     ok = done;
     if (!done && err) atomicExch(err, SB_ERR_TIMEOUT);
@@ -824,9 +826,19 @@ __global__ void peer_combine_kernel(uint8_t* own, const unsigned long long* peer
   if (threadIdx.x == 0) *epoch = e + 1u;
 }
 
+// How long a rank waits in peer_combine_kernel for the others to count in.
+std::atomic<uint64_t> g_peer_wait_ns{sbd::kWaitLimitNs};
+
 }  // namespace
 
 extern "C" size_t sb_peer_mailbox_size(void) { return sbd::kMailBytes; }
+
+extern "C" int sb_peer_set_wait_limit_ns(uint64_t ns) {
+  SB_CHECK_ARG(ns <= sbd::kWaitLimitNs, "sb_peer_set_wait_limit_ns: %llu ns exceeds the %llu ns limit",
+               static_cast<unsigned long long>(ns), static_cast<unsigned long long>(sbd::kWaitLimitNs));
+  g_peer_wait_ns.store(ns ? ns : sbd::kWaitLimitNs);
+  return SB_OK;
+}
 
 extern "C" int sb_peer_buffer_create(size_t bytes, void** dev_ptr, void* ipc_handle) {
   SB_CHECK_ARG(bytes > 0 && dev_ptr && ipc_handle, "sb_peer_buffer_create: bad arguments");
@@ -890,7 +902,8 @@ extern "C" int sb_lmhead_argmax_peer(const void* emb, const void* scales, int sc
   }
   peer_combine_kernel<<<1, 128, 0, s>>>(static_cast<uint8_t*>(own_mailbox),
                                         reinterpret_cast<const unsigned long long*>(peer_mailboxes), world, m,
-                                        reinterpret_cast<unsigned long long*>(keys), tokens, sb::device_error_word());
+                                        reinterpret_cast<unsigned long long*>(keys), tokens, sb::device_error_word(),
+                                        g_peer_wait_ns.load());
   return sb::launch_status("peer_combine_kernel");
 }
 

@@ -52,3 +52,10 @@ def test_argument_validation_is_host_side(lib):
 
 def test_workspace_size_zero_for_empty(lib):
     assert lib.sb_gemm_q4_workspace_size(0, 10, 64) == 0
+
+
+def test_peer_wait_limit_is_bounded_by_the_default():
+    """The exchange's wait limit can be shortened, never lengthened past 2 s (host-only call)."""
+    lib = _lib.load()
+    assert lib.sb_peer_set_wait_limit_ns(3_000_000_000) == _lib.SB_ERR_ARG
+    assert lib.sb_peer_set_wait_limit_ns(0) == _lib.SB_OK

@@ -65,7 +65,7 @@ def parse():
     ap.add_argument("--kernel", default="",
                     choices=["", "gemm_q4", "gemm_q4_geglu", "gemm_f16", "gemv", "lmhead", "attn", "attn_decode", "gemv_q8",
                              "gemv_bf16", "ple_block", "prefill",
-                             "decode", "decode_fused", "decode_batch"],
+                             "decode", "decode_fused", "decode_batch", "decode_trace"],
                     help="run one kernel --iters times on a single shape and exit (for ncu captures)")
     ap.add_argument("--shape", default="6144,1536", help="N,K of the weight for --kernel")
     ap.add_argument("--m", type=int, default=1024, help="rows of the activation for --kernel")
@@ -115,10 +115,77 @@ def run_model_case(args):
     print(f"ran {args.kernel} x{args.iters} (prompt {args.m}) eagerly")
 
 
+def run_decode_trace(args):
+    """Per-phase timing of the persistent decode step (``decode_step_kernel``)
+    from its own %globaltimer trace: one traced step at context --m, every CTA
+    stamping its phase boundaries.  Prints, per phase of a layer, the mean over
+    CTAs and layers (and the max) of the time from the previous grid barrier's
+    exit to this barrier's arrival ("work", with the input prologue, first
+    weight stage and GEMV end marked inside it) and of the barrier wait."""
+    import numpy as np
+    import torch
+
+    from slang_b200 import runner, synth
+    dev = torch.device("cuda", 0)
+    cfg = synth.e2b_config()
+    model = synth.random_model(cfg, seed=1234)
+    dm = runner.DeviceModel(model, dev, args.m + 16)
+    del model
+    r = runner.Runner(dm, 1, fused=True)
+    r.prefill(synth.prompt_tokens(args.m, cfg["vocab"], seed=99))
+    for _ in range(3):
+        with torch.cuda.stream(r.stream):
+            r._fused_ops()
+    torch.cuda.synchronize()
+    kt, ct = 1024, 160  # trace slots per CTA, traced CTAs (decode_mega.cu kTraceLen, kTraceCtas)
+    sc = r.fused_scratch
+    sc[64:64 + ct * kt * 8].zero_()
+    sc[12:16].copy_(torch.tensor([1], dtype=torch.int32).view(torch.uint8))  # the trace switch (scratch u32 3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(r.stream):
+        e0.record(r.stream)
+        r._fused_ops()
+        e1.record(r.stream)
+    torch.cuda.synchronize()
+    sc[12:16].zero_()
+    tr = sc[64:64 + ct * kt * 8].view(torch.int64).view(ct, kt).cpu().numpy().view(np.uint64)
+    tmask = np.uint64((1 << 56) - 1)
+    ctas = [c for c in range(ct) if tr[c, 0] > 0]
+    t_min = min(int(tr[c, 1] & tmask) for c in ctas)
+    names = {2: "arrive", 3: "exit", 4: "input", 5: "stage0", 6: "gemv"}
+    phases = ["q|k|v", "attention", "merge", "o", "gate|up", "down"]
+    stats: dict = {}
+    for c in ctas:
+        n = int(tr[c, 0])
+        ev = [(int(tr[c, i] >> np.uint64(56)), int(tr[c, i] & tmask) - t_min) for i in range(1, n + 1)]
+        k, start, cur = 0, ev[0][1], {}
+        for tag, t in ev:
+            nm = names.get(tag)
+            if nm == "exit":
+                ph = phases[k % 6] if k < len(dm.layers) * 6 else "lm_head"
+                rec = stats.setdefault(ph, {})
+                rec.setdefault("work", []).append(cur.get("arrive", t) - start)
+                rec.setdefault("wait", []).append(t - cur.get("arrive", t))
+                for m in ("input", "stage0", "gemv"):
+                    if m in cur:
+                        rec.setdefault(m, []).append(cur[m] - start)
+                start, cur, k = t, {}, k + 1
+            elif nm:
+                cur[nm] = t
+    print(f"decode_step_kernel traced at context {args.m}: {e0.elapsed_time(e1) * 1e3:.1f} us for the step "
+          f"({len(ctas)} CTAs, {len(dm.layers)} layers); per phase, mean (max) over CTAs and layers, us:")
+    for ph in phases + ["lm_head"]:
+        if ph in stats:
+            print(f"  {ph:9s} " + "  ".join(f"{m} {np.mean(v) / 1e3:.2f} ({np.max(v) / 1e3:.2f})"
+                                             for m, v in stats[ph].items()))
+
+
 def run_kernel_case(args):
     """One kernel on one shape, --iters launches after one warm-up (ncu target)."""
     import torch
 
+    if args.kernel == "decode_trace":
+        return run_decode_trace(args)
     if args.kernel in ("prefill", "decode", "decode_fused", "decode_batch"):
         return run_model_case(args)
     from slang_b200 import kernels as kern
@@ -437,13 +504,20 @@ def gemm_graph_times(torch, kern, r, stream, warmup):
     activation buffers gives the GEMM time per prefill (the 1 GB of weights
     cycles past L2 as in the prefill); one graph per matrix, replayed after an
     L2 flush, splits it by matrix.  CUDA events on the launching stream."""
+    from slang_b200.runner import _rows as runner_rows
     pf, S, dm = r._pf, PROMPT, r.dm
     specs = [("qkv", "h16", "qkv", "qkv16", False), ("o", "attn16", "o", "o16", False),
              ("gate|up", "h16", "gu", "a16", True), ("down", "a16", "down", "d16", False)]
 
+    width = {"h16": r.H, "qkv16": r.nqkv, "attn16": r.qd, "a16": r.F, "o16": r.H, "d16": r.H}
+
+    def act(key):  # the prefill's activation buffer of that name as [S, width]
+        t = pf[key]
+        return t[:S] if t.dim() == 2 else runner_rows(t, S, width[key])
+
     def launch(L, spec):
         _, a_key, w_key, c_key, geglu = spec
-        kern.gemm_q4(pf[a_key][:S], L[w_key][0], L[w_key][1], C=pf[c_key][:S], workspace=pf["ws"], geglu=geglu)
+        kern.gemm_q4(act(a_key), L[w_key][0], L[w_key][1], C=act(c_key), workspace=pf["ws"], geglu=geglu)
 
     def capture(body):
         with torch.cuda.stream(stream):

@@ -309,6 +309,10 @@ int sb_add_rmsnorm(const float* x, const void* y, int y_dtype, const float* w_ad
  * positions pos_dev[s]): q heads -> rmsnorm * q_norm -> RoPE -> q16/q32
  * [s][nh][hd]; k -> rmsnorm * k_norm -> RoPE -> k_cache (+ k16); v ->
  * parameter-free rmsnorm -> v_cache (+ v16).  cos/sin: [max_seq][hd/2].
+ * head_dim in {64, 128, 256, 512} (512: the checkpoint's full-attention
+ * layers).  k_cache and v_cache both NULL: a layer that reads another layer's
+ * K/V (KV sharing, gemma4/reference.py:117-131) -- only the q heads are
+ * prepared and qkv rows hold n_heads * head_dim values.
  * Replaces kvnorm_b + qprep_b (gemma4_150/kernels_dsl.py:1790, 1838) /
  * gemma4/reference.py:114-125. */
 int sb_qkv_prep(const void* qkv, int qkv_dtype, int ld, const float* q_norm, const float* k_norm,
@@ -317,10 +321,13 @@ int sb_qkv_prep(const void* qkv, int qkv_dtype, int ld, const float* q_norm, con
                 float* v_cache, void* k16, void* v16, int64_t cache_stride, void* stream);
 
 /* Causal softmax over f32 score rows (row r = token r / n_heads): p16 =
- * f16(exp(s - max) / sum) for keys <= start_pos + r / n_heads, 0 after.
- * Replaces smax_b + attnout_b (gemma4_150/kernels_dsl.py:1877, 1753). */
+ * f16(exp(s - max) / sum) for keys <= start_pos + r / n_heads, 0 after; with
+ * window > 0 also 0 for keys more than window - 1 before the query (a
+ * sliding-window layer, gemma4/reference.py:126-129; 0 = no window).
+ * Replaces smax_b + attnout_b (gemma4_150/kernels_dsl.py:1877, 1753) and the
+ * banded sliding mask of gemma4_150/prefill_gpu.py:290-310. */
 int sb_softmax_causal(const float* scores, int ld_s, int rows, int n_heads, int start_pos,
-                      int n_keys, void* p16, int ld_p, void* stream);
+                      int n_keys, int window, void* p16, int ld_p, void* stream);
 
 /*
  * Fused causal prefill attention on tcgen05: out = softmax(q k^T) v for one
@@ -349,18 +356,22 @@ size_t sb_attn_prefill_workspace_size(int s_len, int n_heads, int head_dim);
 int sb_geglu(const void* gu, int dtype, int m, int f, float* out32, void* out16, void* stream);
 
 /* Split-KV decode attention, one KV head shared by n_heads query heads:
- * out[b, h*hd:(h+1)*hd] = softmax(q[b,h] . K[b, 0..pos]) V[b, 0..pos].
+ * out[b, h*hd:(h+1)*hd] = softmax(q[b,h] . K[b, lo..pos]) V[b, lo..pos] with
+ * lo = 0, or lo = max(0, pos + 1 - window) for a sliding-window layer
+ * (window > 0).  head_dim in {64, 128, 256, 512}; n_heads in {1, 2, 4, 8}, or
+ * 16 for head_dim <= 256.
  * Replaces attn_101 (gemma4_150/kernels_dsl.py:1540) / gemma4/reference.py:127-139.
  * workspace >= sb_attn_decode_workspace_size(m, n_heads, head_dim, max_seq) bytes. */
 int sb_attn_decode(const float* q32, const float* k_cache, const float* v_cache,
                    int64_t cache_stride, const int32_t* pos_dev, int m, int n_heads, int head_dim,
-                   int max_seq, float* out, float* workspace, size_t workspace_bytes, void* stream);
+                   int max_seq, int window, float* out, float* workspace, size_t workspace_bytes,
+                   void* stream);
 size_t sb_attn_decode_workspace_size(int m, int n_heads, int head_dim, int max_seq);
 /* sb_attn_decode writing out16 [m][n_heads * head_dim] as f16 (the A operand of
  * the tcgen05 o-projection in batched decode). */
 int sb_attn_decode_f16(const float* q32, const float* k_cache, const float* v_cache, int64_t cache_stride,
-                       const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, void* out16,
-                       float* workspace, size_t workspace_bytes, void* stream);
+                       const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, int window,
+                       void* out16, float* workspace, size_t workspace_bytes, void* stream);
 
 /* Device-side step bookkeeping so a decode step replays as one graph:
  * pos[b] += 1; cur[b] = tokens[b]; history[b * hist_len + pos[b]] = tokens[b].

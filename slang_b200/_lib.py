@@ -41,7 +41,7 @@ SIGNATURES = {
     "sb_add_rmsnorm": ([_vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _f, _vp], _i),
     "sb_qkv_prep": ([_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _vp, _vp,
                      _i64, _vp], _i),
-    "sb_softmax_causal": ([_vp, _i, _i, _i, _i, _i, _vp, _i, _vp], _i),
+    "sb_softmax_causal": ([_vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp], _i),
     "sb_geglu": ([_vp, _i, _i, _i, _vp, _vp, _vp], _i),
     "sb_attn_prefill": ([_vp, _vp, _vp, _vp, _i, _i, _i, _vp], _i),
     "sb_attn_prefill_ws": ([_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp], _i),
@@ -53,9 +53,9 @@ SIGNATURES = {
     "sb_peer_buffer_free": ([_vp], _i),
     "sb_lmhead_argmax_peer": ([_vp, _vp, _i, _i, _vp, _i, _i, _i, _i, _i64, _vp, _i, _vp, _vp, _vp, _vp], _i),
     "sb_gemm_q4_argmax": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _i64, _vp, _vp, _vp], _i),
-    "sb_attn_decode_f16": ([_vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _vp, _vp, _sz, _vp], _i),
+    "sb_attn_decode_f16": ([_vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp], _i),
     "sb_attn_prefill_workspace_size": ([_i, _i, _i], _sz),
-    "sb_attn_decode": ([_vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _vp, _vp, _sz, _vp], _i),
+    "sb_attn_decode": ([_vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp], _i),
     "sb_attn_decode_workspace_size": ([_i, _i, _i, _i], _sz),
     "sb_step_advance": ([_vp, _vp, _vp, _vp, _i, _i, _vp], _i),
     "sb_gemv_q8": ([_vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _vp, _i, _vp], _i),

@@ -257,6 +257,38 @@ __global__ void __launch_bounds__(kRowWarps * 32) add_rmsnorm_warp_kernel(
 // (i, i + hd/2) meet in one lane and every access is a vector of VH.  The RMS
 // division is one reciprocal and products (within 1.5 ulp of x / d).
 template <int VH>
+__device__ __forceinline__ void ldv(const void* p, int is_f16, size_t i, float (&v)[VH]);
+template <int VH>
+__device__ __forceinline__ void stv(float* p, const float (&v)[VH]);
+template <int VH>
+__device__ __forceinline__ void stvh(__half* p, const float (&v)[VH]);
+
+// 8 values (head_dim 512) as two 4-value accesses
+template <>
+__device__ __forceinline__ void ldv<8>(const void* p, int is_f16, size_t i, float (&v)[8]) {
+  float a[4], b[4];
+  ldv<4>(p, is_f16, i, a);
+  ldv<4>(p, is_f16, i + 4, b);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    v[e] = a[e];
+    v[4 + e] = b[e];
+  }
+}
+template <>
+__device__ __forceinline__ void stv<8>(float* p, const float (&v)[8]) {
+  const float a[4] = {v[0], v[1], v[2], v[3]}, b[4] = {v[4], v[5], v[6], v[7]};
+  stv<4>(p, a);
+  stv<4>(p + 4, b);
+}
+template <>
+__device__ __forceinline__ void stvh<8>(__half* p, const float (&v)[8]) {
+  const float a[4] = {v[0], v[1], v[2], v[3]}, b[4] = {v[4], v[5], v[6], v[7]};
+  stvh<4>(p, a);
+  stvh<4>(p + 4, b);
+}
+
+template <int VH>
 __device__ __forceinline__ void ldv(const void* p, int is_f16, size_t i, float (&v)[VH]) {
   if (is_f16) {
     const __half* h = static_cast<const __half*>(p) + i;
@@ -383,15 +415,17 @@ __global__ void qkv_prep_kernel(const void* __restrict__ qkv, int qkv_f16, int l
 // Row r is query token s = r / nh (absolute position start + s); keys t <= that
 // position get f16(exp(score - max) / sum), later keys (up to n_keys) get 0.
 __global__ void softmax_causal_kernel(const float* __restrict__ scores, int ld_s, int nh, int start_pos, int n_keys,
-                                      __half* p16, int ld_p) {
+                                      int window, __half* p16, int ld_p) {
   __shared__ float red[32];
   sbd::griddep_launch_dependents();
   sbd::griddep_wait();
   const int r = blockIdx.x;
   const int last = start_pos + r / nh;  // inclusive
+  // a sliding-window layer sees the `window` keys ending at its own position
+  const int first = window > 0 ? max(0, last + 1 - window) : 0;
   const float* srow = scores + static_cast<size_t>(r) * ld_s;
   float m = -INFINITY;
-  for (int t = threadIdx.x; t <= last; t += blockDim.x) m = fmaxf(m, srow[t]);
+  for (int t = first + threadIdx.x; t <= last; t += blockDim.x) m = fmaxf(m, srow[t]);
   m = warp_max(m);
   __syncthreads();
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
@@ -399,11 +433,11 @@ __global__ void softmax_causal_kernel(const float* __restrict__ scores, int ld_s
   m = (threadIdx.x & 31) < (blockDim.x >> 5) ? red[threadIdx.x & 31] : -INFINITY;
   m = warp_max(m);
   float l = 0.f;
-  for (int t = threadIdx.x; t <= last; t += blockDim.x) l += expf(srow[t] - m);
+  for (int t = first + threadIdx.x; t <= last; t += blockDim.x) l += expf(srow[t] - m);
   l = block_sum(l, red);
   __half* prow = p16 + static_cast<size_t>(r) * ld_p;
   for (int t = threadIdx.x; t < n_keys; t += blockDim.x)
-    prow[t] = t <= last ? __float2half_rn(expf(srow[t] - m) / l) : __float2half_rn(0.f);
+    prow[t] = t >= first && t <= last ? __float2half_rn(expf(srow[t] - m) / l) : __float2half_rn(0.f);
 }
 
 // ---------------------------------------------------------------- GEGLU
@@ -484,7 +518,7 @@ __global__ void __launch_bounds__(256, 2) attn_decode_split_kernel(const float* 
                                                                 const float* __restrict__ v_cache,
                                                                 const int32_t* __restrict__ pos_dev,
                                                                 int64_t cache_stride, float* part, int spk,
-                                                                int max_splits, int* err) {
+                                                                int max_splits, int window, int* err) {
   using Sh = DecodeAttnShape<HD, NH>;
   constexpr int J = Sh::J, NA = Sh::NA, R = Sh::R, HPT = Sh::HPT, SP = Sh::SP;
   extern __shared__ __align__(16) float sm[];
@@ -505,9 +539,12 @@ __global__ void __launch_bounds__(256, 2) attn_decode_split_kernel(const float* 
   }
   sbd::griddep_wait();
   const int T = pos_dev[b] + 1;
-  const int k0 = sp * spk;
-  if (k0 >= T) return;  // uniform over the CTA
-  const int k1 = min(T, k0 + spk);
+  // a sliding-window layer attends to the last `window` keys; splits wholly
+  // before them do nothing (the merge starts at the split holding the first)
+  const int first = window > 0 ? max(0, T - window) : 0;
+  const int k0 = max(sp * spk, first);
+  if (k0 >= T || (sp + 1) * spk <= first) return;  // uniform over the CTA
+  const int k1 = min(T, (sp + 1) * spk);
   const int nchunk = (k1 - k0 + CK - 1) / CK;
   const float* kb = k_cache + static_cast<size_t>(b) * cache_stride;
   const float* vb = v_cache + static_cast<size_t>(b) * cache_stride;
@@ -661,18 +698,20 @@ __global__ void __launch_bounds__(256, 2) attn_decode_split_kernel(const float* 
 
 // Merge: CTA (b, h), thread d rescales the splits of sequence b.
 __global__ void attn_decode_merge_kernel(const float* __restrict__ part, const int32_t* __restrict__ pos_dev, int nh,
-                                         int hd, int spk, int max_splits, float* out, __half* out16) {
+                                         int hd, int spk, int max_splits, int window, float* out, __half* out16) {
   sbd::griddep_launch_dependents();
   const int b = blockIdx.x, h = blockIdx.y;
   sbd::griddep_wait();
-  const int nc = (pos_dev[b] + 1 + spk - 1) / spk;
+  const int T = pos_dev[b] + 1;
+  const int nc = (T + spk - 1) / spk;
+  const int c0 = window > 0 ? max(0, T - window) / spk : 0;  // first split with keys in the window
   const float* base = part + (static_cast<size_t>(b) * max_splits * nh + h) * (hd + 2);
   const size_t cstride = static_cast<size_t>(nh) * (hd + 2);
   float M = -INFINITY;
-  for (int c = 0; c < nc; ++c) M = fmaxf(M, base[c * cstride + hd]);
+  for (int c = c0; c < nc; ++c) M = fmaxf(M, base[c * cstride + hd]);
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     float L = 0.f, O = 0.f;
-    for (int c = 0; c < nc; ++c) {
+    for (int c = c0; c < nc; ++c) {
       const float* pm = base + c * cstride;
       const float f = expf(pm[hd] - M);
       L += pm[hd + 1] * f;
@@ -771,12 +810,18 @@ extern "C" int sb_qkv_prep(const void* qkv, int qkv_dtype, int ld, const float* 
                            const float* cos_t, const float* sin_t, const int32_t* pos_dev, int start_pos, int s,
                            int n_heads, int head_dim, float eps, void* q16, float* q32, float* k_cache,
                            float* v_cache, void* k16, void* v16, int64_t cache_stride, void* stream) {
-  SB_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256, "sb_qkv_prep: head_dim %d unsupported", head_dim);
-  SB_CHECK_ARG(n_heads >= 1 && n_heads <= 30 && s >= 0 && ld >= (n_heads + 2) * head_dim, "sb_qkv_prep: bad shape");
+  SB_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256 || head_dim == 512,
+               "sb_qkv_prep: head_dim %d unsupported", head_dim);
+  // no caches: a layer that reads another layer's K/V (KV sharing) -- q heads only
+  const bool q_only = !k_cache && !v_cache;
+  const int warps = n_heads + (q_only ? 0 : 2);
+  SB_CHECK_ARG(n_heads >= 1 && warps <= 32 && s >= 0 && ld >= warps * head_dim, "sb_qkv_prep: bad shape");
   SB_CHECK_ARG(qkv_dtype == SB_F16 || qkv_dtype == SB_F32, "sb_qkv_prep: bad dtype");
   if (s == 0) return SB_OK;
-  SB_CHECK_ARG(qkv && q_norm && k_norm && cos_t && sin_t && k_cache && v_cache && (q16 || q32), "sb_qkv_prep: null");
-  const dim3 block(32 * (n_heads + 2));
+  SB_CHECK_ARG(qkv && q_norm && (q_only || k_norm) && cos_t && sin_t && (q_only || (k_cache && v_cache)) &&
+                   (q16 || q32),
+               "sb_qkv_prep: null pointer (k_cache and v_cache are both given, or both null for q only)");
+  const dim3 block(32 * warps);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int f16 = qkv_dtype == SB_F16;
   cudaError_t e;
@@ -786,20 +831,22 @@ extern "C" int sb_qkv_prep(const void* qkv, int qkv_dtype, int ld, const float* 
                      static_cast<__half*>(k16), static_cast<__half*>(v16), cache_stride)
   if (head_dim == 64) SB_PREP(2);
   else if (head_dim == 128) SB_PREP(4);
-  else SB_PREP(8);
+  else if (head_dim == 256) SB_PREP(8);
+  else SB_PREP(16);
 #undef SB_PREP
   if (e != cudaSuccess) return sb::cuda_fail(e, "qkv_prep_kernel");
   return sb::launch_status("qkv_prep_kernel");
 }
 
 extern "C" int sb_softmax_causal(const float* scores, int ld_s, int rows, int n_heads, int start_pos, int n_keys,
-                                 void* p16, int ld_p, void* stream) {
-  SB_CHECK_ARG(rows >= 0 && n_heads > 0 && n_keys >= 0 && ld_s >= n_keys && ld_p >= n_keys, "sb_softmax_causal: bad shape");
+                                 int window, void* p16, int ld_p, void* stream) {
+  SB_CHECK_ARG(rows >= 0 && n_heads > 0 && n_keys >= 0 && ld_s >= n_keys && ld_p >= n_keys && window >= 0,
+               "sb_softmax_causal: bad shape");
   SB_CHECK_ARG(start_pos + (rows - 1) / n_heads < n_keys || rows == 0, "sb_softmax_causal: a query sees past n_keys");
   if (rows == 0) return SB_OK;
   SB_CHECK_ARG(scores && p16, "sb_softmax_causal: null pointer");
   cudaError_t e = sb::launch_pdl(softmax_causal_kernel, dim3(rows), dim3(kT), 0, static_cast<cudaStream_t>(stream),
-                                 scores, ld_s, n_heads, start_pos, n_keys, static_cast<__half*>(p16), ld_p);
+                                 scores, ld_s, n_heads, start_pos, n_keys, window, static_cast<__half*>(p16), ld_p);
   if (e != cudaSuccess) return sb::cuda_fail(e, "softmax_causal_kernel");
   return sb::launch_status("softmax_causal_kernel");
 }
@@ -826,7 +873,7 @@ extern "C" size_t sb_attn_decode_workspace_size(int m, int n_heads, int head_dim
 template <int HD, int NH>
 static cudaError_t launch_decode_split(int m, int splits, int spk, cudaStream_t st, const float* q32,
                                        const float* k_cache, const float* v_cache, const int32_t* pos_dev,
-                                       int64_t cache_stride, float* workspace) {
+                                       int64_t cache_stride, float* workspace, int window) {
   using Sh = DecodeAttnShape<HD, NH>;
   constexpr int smem = static_cast<int>(Sh::smem_floats * sizeof(float));
   static bool set[64] = {};
@@ -839,28 +886,35 @@ static cudaError_t launch_decode_split(int m, int splits, int spk, cudaStream_t 
     if (dev >= 0 && dev < 64) set[dev] = true;
   }
   return sb::launch_pdl(attn_decode_split_kernel<HD, NH>, dim3(m, splits), dim3(Sh::kThreads), smem, st, q32, k_cache,
-                        v_cache, pos_dev, cache_stride, workspace, spk, splits, sb::device_error_word());
+                        v_cache, pos_dev, cache_stride, workspace, spk, splits, window, sb::device_error_word());
 }
 
 template <int HD>
 static cudaError_t launch_decode_split_hd(int nh, int m, int splits, int spk, cudaStream_t st, const float* q32,
                                           const float* k_cache, const float* v_cache, const int32_t* pos_dev,
-                                          int64_t cache_stride, float* workspace) {
+                                          int64_t cache_stride, float* workspace, int window) {
+#define SB_DEC(NH) \
+  launch_decode_split<HD, NH>(m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace, window)
   switch (nh) {
-    case 1: return launch_decode_split<HD, 1>(m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
-    case 2: return launch_decode_split<HD, 2>(m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
-    case 4: return launch_decode_split<HD, 4>(m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
-    case 8: return launch_decode_split<HD, 8>(m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
-    default: return launch_decode_split<HD, 16>(m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
+    case 1: return SB_DEC(1);
+    case 2: return SB_DEC(2);
+    case 4: return SB_DEC(4);
+    case 8: return SB_DEC(8);
+    default:
+      if constexpr (HD <= 256) return SB_DEC(16);
+      return cudaErrorInvalidValue;
   }
+#undef SB_DEC
 }
 
 static int attn_decode_impl(const float* q32, const float* k_cache, const float* v_cache, int64_t cache_stride,
-                            const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, float* out,
-                            __half* out16, float* workspace, size_t workspace_bytes, void* stream) {
-  SB_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256, "sb_attn_decode: head_dim %d unsupported", head_dim);
-  SB_CHECK_ARG((n_heads == 1 || n_heads == 2 || n_heads == 4 || n_heads == 8 || n_heads == 16) && m >= 0 && max_seq > 0,
-               "sb_attn_decode: n_heads %d not in {1, 2, 4, 8, 16}, or bad shape", n_heads);
+                            const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, int window,
+                            float* out, __half* out16, float* workspace, size_t workspace_bytes, void* stream) {
+  SB_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256 || head_dim == 512,
+               "sb_attn_decode: head_dim %d unsupported", head_dim);
+  SB_CHECK_ARG((n_heads == 1 || n_heads == 2 || n_heads == 4 || n_heads == 8 || (n_heads == 16 && head_dim <= 256)) &&
+                   m >= 0 && max_seq > 0 && window >= 0,
+               "sb_attn_decode: n_heads %d not in {1, 2, 4, 8, 16 (head_dim <= 256)}, or bad shape", n_heads);
   if (m == 0) return SB_OK;
   SB_CHECK_ARG(q32 && k_cache && v_cache && pos_dev && (out || out16) && workspace, "sb_attn_decode: null pointer");
   SB_CHECK_ARG(cache_stride % 4 == 0 && sb::aligned(q32, 16) && sb::aligned(k_cache, 16) && sb::aligned(v_cache, 16),
@@ -892,33 +946,34 @@ static int attn_decode_impl(const float* q32, const float* k_cache, const float*
   const int splits = (max_seq + spk - 1) / spk;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
-  if (head_dim == 64)
-    e = launch_decode_split_hd<64>(n_heads, m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
-  else if (head_dim == 128)
-    e = launch_decode_split_hd<128>(n_heads, m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
-  else
-    e = launch_decode_split_hd<256>(n_heads, m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace);
+#define SB_DEC_HD(HDV) \
+  launch_decode_split_hd<HDV>(n_heads, m, splits, spk, st, q32, k_cache, v_cache, pos_dev, cache_stride, workspace, window)
+  if (head_dim == 64) e = SB_DEC_HD(64);
+  else if (head_dim == 128) e = SB_DEC_HD(128);
+  else if (head_dim == 256) e = SB_DEC_HD(256);
+  else e = SB_DEC_HD(512);
+#undef SB_DEC_HD
   if (e != cudaSuccess) return sb::cuda_fail(e, "attn_decode_split_kernel");
   int rc = sb::launch_status("attn_decode_split_kernel");
   if (rc) return rc;
   e = sb::launch_pdl(attn_decode_merge_kernel, dim3(m, n_heads), dim3(head_dim), 0, st,
-                     static_cast<const float*>(workspace), pos_dev, n_heads, head_dim, spk, splits, out, out16);
+                     static_cast<const float*>(workspace), pos_dev, n_heads, head_dim, spk, splits, window, out, out16);
   if (e != cudaSuccess) return sb::cuda_fail(e, "attn_decode_merge_kernel");
   return sb::launch_status("attn_decode_merge_kernel");
 }
 
 extern "C" int sb_attn_decode(const float* q32, const float* k_cache, const float* v_cache, int64_t cache_stride,
-                              const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, float* out,
-                              float* workspace, size_t workspace_bytes, void* stream) {
-  return attn_decode_impl(q32, k_cache, v_cache, cache_stride, pos_dev, m, n_heads, head_dim, max_seq, out, nullptr,
-                          workspace, workspace_bytes, stream);
+                              const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, int window,
+                              float* out, float* workspace, size_t workspace_bytes, void* stream) {
+  return attn_decode_impl(q32, k_cache, v_cache, cache_stride, pos_dev, m, n_heads, head_dim, max_seq, window, out,
+                          nullptr, workspace, workspace_bytes, stream);
 }
 
 extern "C" int sb_attn_decode_f16(const float* q32, const float* k_cache, const float* v_cache, int64_t cache_stride,
-                                  const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, void* out16,
-                                  float* workspace, size_t workspace_bytes, void* stream) {
+                                  const int32_t* pos_dev, int m, int n_heads, int head_dim, int max_seq, int window,
+                                  void* out16, float* workspace, size_t workspace_bytes, void* stream) {
   SB_CHECK_ARG(out16 != nullptr, "sb_attn_decode_f16: null output");
-  return attn_decode_impl(q32, k_cache, v_cache, cache_stride, pos_dev, m, n_heads, head_dim, max_seq, nullptr,
+  return attn_decode_impl(q32, k_cache, v_cache, cache_stride, pos_dev, m, n_heads, head_dim, max_seq, window, nullptr,
                           static_cast<__half*>(out16), workspace, workspace_bytes, stream);
 }
 

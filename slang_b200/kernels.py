@@ -164,11 +164,12 @@ def attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.T
 
 def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos: torch.Tensor,
                 out: torch.Tensor | None = None, f16: bool = False,
-                workspace: torch.Tensor | None = None) -> torch.Tensor:
+                workspace: torch.Tensor | None = None, window: int = 0) -> torch.Tensor:
     """Decode attention (the reference's ``attn_101``, gemma4_150/kernels_dsl.py) for a
     batch of sequences: q [m, nh, hd] f32, caches [m, max_seq, hd] f32 (one KV head),
     pos [m] int32 = each sequence's last cached position; returns softmax(q k^T) v over
-    keys 0..pos as [m, nh, hd] f32 (f16 with ``f16``)."""
+    keys 0..pos (the last ``window`` of them for a sliding-window layer) as
+    [m, nh, hd] f32 (f16 with ``f16``)."""
     _need(q, "q", (torch.float32,))
     _need(k_cache, "k_cache", (torch.float32,))
     _need(v_cache, "v_cache", (torch.float32,))
@@ -185,9 +186,33 @@ def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, p
         workspace = _workspace(q.device, need)
     nbytes = workspace.numel() * workspace.element_size()
     _lib.call("sb_attn_decode_f16" if f16 else "sb_attn_decode", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-              max_seq * hd, pos.data_ptr(), m, nh, hd, max_seq, out.data_ptr(), workspace.data_ptr(), nbytes,
-              _stream())
+              max_seq * hd, pos.data_ptr(), m, nh, hd, max_seq, int(window), out.data_ptr(), workspace.data_ptr(),
+              nbytes, _stream())
     return out
+
+
+def attn_prefill_gemm(q16: torch.Tensor, k16: torch.Tensor, v16: torch.Tensor, out16: torch.Tensor, S: int,
+                      window: int = 0, scores: torch.Tensor | None = None, p16: torch.Tensor | None = None
+                      ) -> torch.Tensor:
+    """Causal prefill attention as the reference's ``_attn_gemm`` chain
+    (gemma4_150/prefill_gpu.py:259-313): scores = q k^T on the tcgen05 f16
+    GEMM (f32 out), the causal -- and, with ``window``, sliding-window --
+    softmax to f16, out = P v.  Any head_dim the GEMM takes (the
+    checkpoint's 512 included).  q16 [S, nh, hd], k16 / v16 [>= S, hd],
+    out16 [S, nh * hd]; rows of ``scores`` / ``p16`` are [S * nh, >= S]."""
+    nh, hd = q16.shape[1], q16.shape[2]
+    ld = ((S + 7) // 8) * 8
+    if scores is None:
+        scores = torch.empty((S * nh, ld), dtype=torch.float32, device=q16.device)
+    if p16 is None:
+        p16 = torch.empty((S * nh, ld), dtype=torch.float16, device=q16.device)
+    lds, ldp = scores.stride(0), p16.stride(0)
+    s = _stream()
+    _lib.call("sb_gemm_f16_f32out", q16.data_ptr(), k16.data_ptr(), scores.data_ptr(), S * nh, S, hd, 1.0, 1, hd, hd,
+              lds, s)
+    _lib.call("sb_softmax_causal", scores.data_ptr(), lds, S * nh, nh, 0, S, int(window), p16.data_ptr(), ldp, s)
+    _lib.call("sb_gemm_f16", p16.data_ptr(), v16.data_ptr(), out16.data_ptr(), S * nh, hd, S, 1.0, 0, ldp, hd, hd, s)
+    return out16
 
 
 def gemm_q4(A: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, C: torch.Tensor | None = None,

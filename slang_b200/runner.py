@@ -51,6 +51,11 @@ def _interleave(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     return out
 
 
+def _rows(buf: torch.Tensor, m: int, n: int) -> torch.Tensor:
+    """A contiguous [m, n] view at the start of a larger buffer (per-layer widths)."""
+    return buf.view(-1)[:m * n].view(m, n)
+
+
 def layer_specs(cfg: dict) -> list[dict]:
     """Per-layer structure: ``cfg["layer_specs"]`` (a reference export carries
     one per layer, gemma4_150/export.py:159-165) or the config's uniform layer."""
@@ -76,10 +81,11 @@ class DeviceModel:
     Takes either weight format ``manifest.read`` produces: 4-bit codes with
     per-group-32 f16 scales (the benchmark format) or the reference export's
     per-row f32 scales with 2- or 4-bit codes per matrix, a 2-bit embedding
-    with per-block scales and a separate 2-bit lm_head.  The GPU runner takes
-    layers of one shape that each own their K/V, and sliding-window layers
-    only while ``max_seq`` is within the window (where the window masks
-    nothing); other architectures are refused with ValueError."""
+    with per-block scales and a separate 2-bit lm_head.  Layers follow
+    ``layer_specs``: each has its own head_dim, q width and FFN width (the
+    checkpoint's full-attention layers have head_dim 512, its layers 15+ a
+    double-width 2-bit FFN), may read the K/V of an earlier layer instead of
+    computing its own (KV sharing) and may attend over a sliding window."""
 
     def __init__(self, model: dict, device, max_seq: int):
         cfg = model["config"]
@@ -108,15 +114,20 @@ class DeviceModel:
         self.layers = []
         self._rope: dict = {}
         group32 = self.embed_bits == 4 and self.lm_bits == 4 and self.lm_q is self.embed_q
+        win = int(cfg.get("sliding_window", 0) or 0)
         for li, (L, sp) in enumerate(zip(model["layers"], specs)):
+            own = sp["kv_source"] == li
             bits = {"qkv": _bits(L["q"][0], H), "o": _bits(L["o"][0], sp["q_dim"]), "gu": _bits(L["gate"][0], H),
                     "down": _bits(L["down"][0], sp["inter"])}
-            if _bits(L["k"][0], H) != bits["qkv"] or _bits(L["v"][0], H) != bits["qkv"] or \
+            if (own and (_bits(L["k"][0], H) != bits["qkv"] or _bits(L["v"][0], H) != bits["qkv"])) or \
                     _bits(L["up"][0], H) != bits["gu"]:
                 raise ValueError(f"layer {li}: q/k/v (or gate/up) weights of different code widths")
+            names = ("q", "k", "v") if own else ("q",)  # a KV-shared layer projects q only
             d = {
-                "qkv": (T(np.concatenate([L["q"][0], L["k"][0], L["v"][0]])),
-                        T(np.concatenate([L["q"][1], L["k"][1], L["v"][1]]))),
+                "spec": {"hd": sp["head_dim"], "qd": sp["q_dim"], "F": sp["inter"], "own": own,
+                         "src": sp["kv_source"], "window": win if sp["sliding"] else 0,
+                         "nqkv": sp["q_dim"] + (2 * sp["head_dim"] if own else 0)},
+                "qkv": (T(np.concatenate([L[n][0] for n in names])), T(np.concatenate([L[n][1] for n in names]))),
                 "o": (T(L["o"][0]), T(L["o"][1])),
                 # gate row i and up row i adjacent: GEGLU pairs neighbouring outputs
                 "gu": (T(_interleave(L["gate"][0], L["up"][0])), T(_interleave(L["gate"][1], L["up"][1]))),
@@ -124,7 +135,7 @@ class DeviceModel:
                 "bits": bits,
             }
             for n in ("in_norm", "q_norm", "k_norm", "post_attn_norm", "pre_ffn_norm", "post_ffn_norm"):
-                d[n] = T(L[n], torch.float32)
+                d[n] = T(L[n], torch.float32) if n in L else None  # a KV-shared layer has no k_norm
             key = (sp["rope_theta"], sp["rope_cutoff"])
             if key not in self._rope:
                 cos, sin = rope_tables(max_seq, sp["head_dim"], *key)
@@ -137,7 +148,13 @@ class DeviceModel:
         self.cos, self.sin = self.layers[0]["cos"], self.layers[0]["sin"]
         # the persistent one-launch decode step and the GEMM-argmax lm_head take
         # the benchmark format only (4-bit codes, f16 group-32 scales, tied table)
-        self.group32_f16 = group32 and self.embed_s.dtype == torch.float16 and self.embed_group == 32
+        # and layers of one shape that own their K/V with no window in reach
+        sp0 = self.layers[0]["spec"]
+        self.uniform = all(d["spec"]["own"] and (d["spec"]["hd"], d["spec"]["qd"], d["spec"]["F"]) ==
+                           (sp0["hd"], sp0["qd"], sp0["F"]) and (not d["spec"]["window"] or
+                                                                 max_seq <= d["spec"]["window"])
+                           for d in self.layers)
+        self.group32_f16 = group32 and self.embed_s.dtype == torch.float16 and self.embed_group == 32 and self.uniform
         # per-layer embeddings (the dict of synth.ple_weights or of a reference export), when the model has them
         self.ple = None
         P = model.get("ple")
@@ -157,17 +174,13 @@ class DeviceModel:
 
     @staticmethod
     def _check(cfg: dict, specs: list, max_seq: int) -> None:
-        sp0 = specs[0]
         for i, sp in enumerate(specs):
-            if (sp["head_dim"], sp["q_dim"], sp["inter"]) != (sp0["head_dim"], sp0["q_dim"], sp0["inter"]):
-                raise ValueError(f"layer {i} differs in head_dim / q_dim / FFN width from layer 0; the GPU runner "
-                                 "takes layers of one shape")
-            if sp["kv_source"] != i:
-                raise ValueError(f"layer {i} reads the K/V of layer {sp['kv_source']}; the GPU runner takes layers "
-                                 "that own their K/V")
-            if sp["sliding"] and cfg.get("sliding_window", 0) and max_seq > cfg["sliding_window"]:
-                raise ValueError(f"max_seq {max_seq} exceeds the sliding window {cfg['sliding_window']} of layer {i};"
-                                 " the GPU runner attends over the full causal context")
+            src = sp["kv_source"]
+            if src != i and (src > i or specs[src]["kv_source"] != src or specs[src]["head_dim"] != sp["head_dim"]):
+                raise ValueError(f"layer {i} reads the K/V of layer {src}, which must be an earlier layer of the same "
+                                 "head_dim that owns its K/V")
+            if sp["q_dim"] % sp["head_dim"] or sp["q_dim"] // sp["head_dim"] != cfg["n_heads"]:
+                raise ValueError(f"layer {i}: q_dim {sp['q_dim']} is not n_heads x head_dim")
 
     def embed(self, tokens_ptr: int, m: int, out32, out16, stream: int) -> None:
         """Scaled embedding rows of ``m`` tokens (``embed_00``, gemma4/reference.py:168)."""
@@ -204,24 +217,36 @@ class Runner:
             raise ValueError("per-layer embeddings run on the per-op GEMV decode path (fused=False, proj='gemv')")
         if (fused or proj == "gemm") and not dm.group32_f16:
             raise ValueError("the persistent decode step and the GEMM decode path take 4-bit weights with f16 "
-                             "group-32 scales and a tied lm_head; use fused=False, proj='gemv'")
+                             "group-32 scales, a tied lm_head and uniform layers that own their K/V; use "
+                             "fused=False, proj='gemv'")
         self.proj = proj
         self.fused = fused
         self.dm = dm
         cfg = dm.cfg
         self.B = batch
-        self.H, self.nh, self.hd = cfg["hidden"], cfg["n_heads"], cfg["head_dim"]
-        self.F = cfg["inter"]
-        self.qd = self.nh * self.hd
-        self.nqkv = self.qd + 2 * self.hd
+        specs = [L["spec"] for L in dm.layers]
+        # buffer sizes: the largest layer (layers may differ in head_dim, q and FFN width)
+        self.H, self.nh = cfg["hidden"], cfg["n_heads"]
+        self.hd = max(sp["hd"] for sp in specs)
+        self.F = max(sp["F"] for sp in specs)
+        self.qd = max(sp["qd"] for sp in specs)
+        self.nqkv = max(sp["nqkv"] for sp in specs)
         self.eps = float(cfg["eps"])
         self.max_seq = dm.max_seq
         dev = dm.device
         B, H, S = batch, self.H, self.max_seq
         self.cache_stride = S * self.hd
         nL = cfg["n_layers"]
-        self.kc = [torch.zeros((B, S, self.hd), dtype=torch.float32, device=dev) for _ in range(nL)]
-        self.vc = [torch.zeros((B, S, self.hd), dtype=torch.float32, device=dev) for _ in range(nL)]
+        # K/V caches [B, max_seq, head_dim] per layer that owns its K/V; a
+        # KV-shared layer holds its source layer's tensors
+        self.kc, self.vc = [], []
+        for li, sp in enumerate(specs):
+            if sp["own"]:
+                self.kc.append(torch.zeros((B, S, sp["hd"]), dtype=torch.float32, device=dev))
+                self.vc.append(torch.zeros((B, S, sp["hd"]), dtype=torch.float32, device=dev))
+            else:
+                self.kc.append(self.kc[sp["src"]])
+                self.vc.append(self.vc[sp["src"]])
         f32 = lambda *s: torch.zeros(s, dtype=torch.float32, device=dev)  # noqa: E731
         self.x, self.h = f32(B, H), f32(B, H)
         self.qkv, self.q = f32(B, self.nqkv), f32(B, self.qd)
@@ -244,7 +269,7 @@ class Runner:
         self.tok = torch.zeros(B, dtype=torch.int32, device=dev)
         self.keys = torch.zeros(B, dtype=torch.int64, device=dev)
         self.history = torch.zeros((B, S), dtype=torch.int32, device=dev)
-        ws = _lib.load().sb_attn_decode_workspace_size(B, self.nh, self.hd, S)
+        ws = max(_lib.load().sb_attn_decode_workspace_size(B, self.nh, sp["hd"], S) for sp in specs)
         self.attn_ws = torch.empty(max(1, ws // 4), dtype=torch.float32, device=dev)
         self.stream = torch.cuda.Stream(device=dev)
         if fused:
@@ -278,7 +303,7 @@ class Runner:
                       self.nh, self.hd, self.eps, None, self.q.data_ptr(), self.kc[li].data_ptr(),
                       self.vc[li].data_ptr(), None, None, self.cache_stride, s)
             _lib.call("sb_attn_decode_f16", self.q.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
-                      self.cache_stride, self.pos.data_ptr(), B, self.nh, self.hd, self.max_seq,
+                      self.cache_stride, self.pos.data_ptr(), B, self.nh, self.hd, self.max_seq, 0,
                       self.attn16.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws.numel() * 4, s)
             proj(L["o"], self.attn16, self.o16)
             _lib.call("sb_add_rmsnorm", self.x.data_ptr(), self.o16.data_ptr(), _F16, L["post_attn_norm"].data_ptr(),
@@ -307,20 +332,26 @@ class Runner:
         _lib.call("sb_add_rmsnorm", self.x.data_ptr(), None, _F32, None, L0[0]["in_norm"].data_ptr(),
                   self.x.data_ptr(), self.h.data_ptr(), None, B, H, self.eps, s)
         for li, L in enumerate(L0):
-            self._gemv(L, "qkv", self.h, self.qkv)
-            _lib.call("sb_qkv_prep", self.qkv.data_ptr(), _F32, self.nqkv, L["q_norm"].data_ptr(),
-                      L["k_norm"].data_ptr(), L["cos"].data_ptr(), L["sin"].data_ptr(), self.pos.data_ptr(), 0, B,
-                      self.nh, self.hd, self.eps, None, self.q.data_ptr(), self.kc[li].data_ptr(),
-                      self.vc[li].data_ptr(), None, None, self.cache_stride, s)
-            _lib.call("sb_attn_decode", self.q.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
-                      self.cache_stride, self.pos.data_ptr(), B, self.nh, self.hd, self.max_seq,
-                      self.attn.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws.numel() * 4, s)
-            self._gemv(L, "o", self.attn, self.o)
+            sp = L["spec"]
+            hd, qd, F, nqkv = sp["hd"], sp["qd"], sp["F"], sp["nqkv"]
+            qkv, q, attn = _rows(self.qkv, B, nqkv), _rows(self.q, B, qd), _rows(self.attn, B, qd)
+            gu, a = _rows(self.gu, B, 2 * F), _rows(self.a, B, F)
+            self._gemv(L, "qkv", self.h, qkv)
+            # a KV-shared layer prepares q only and attends over its source layer's cache
+            _lib.call("sb_qkv_prep", qkv.data_ptr(), _F32, nqkv, L["q_norm"].data_ptr(),
+                      L["k_norm"].data_ptr() if sp["own"] else None, L["cos"].data_ptr(), L["sin"].data_ptr(),
+                      self.pos.data_ptr(), 0, B, self.nh, hd, self.eps, None, q.data_ptr(),
+                      self.kc[li].data_ptr() if sp["own"] else None, self.vc[li].data_ptr() if sp["own"] else None,
+                      None, None, self.max_seq * hd, s)
+            _lib.call("sb_attn_decode", q.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
+                      self.max_seq * hd, self.pos.data_ptr(), B, self.nh, hd, self.max_seq, sp["window"],
+                      attn.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws.numel() * 4, s)
+            self._gemv(L, "o", attn, self.o)
             _lib.call("sb_add_rmsnorm", self.x.data_ptr(), self.o.data_ptr(), _F32, L["post_attn_norm"].data_ptr(),
                       L["pre_ffn_norm"].data_ptr(), self.x.data_ptr(), self.h.data_ptr(), None, B, H, self.eps, s)
-            self._gemv(L, "gu", self.h, self.gu)
-            _lib.call("sb_geglu", self.gu.data_ptr(), _F32, B, self.F, self.a.data_ptr(), None, s)
-            self._gemv(L, "down", self.a, self.d)
+            self._gemv(L, "gu", self.h, gu)
+            _lib.call("sb_geglu", gu.data_ptr(), _F32, B, F, a.data_ptr(), None, s)
+            self._gemv(L, "down", a, self.d)
             nxt = L0[li + 1]["in_norm"] if li + 1 < len(L0) else dm.final_norm
             _lib.call("sb_add_rmsnorm", self.x.data_ptr(), self.d.data_ptr(), _F32, L["post_ffn_norm"].data_ptr(),
                       nxt.data_ptr(), self.x.data_ptr(), self.h.data_ptr(), None, B, H, self.eps, s)
@@ -430,28 +461,49 @@ class Runner:
         torch.cuda.current_stream().wait_stream(self.stream)
         return int(self.tok[0].item())
 
+    def _attn_route(self, sp, S) -> str:
+        """Prefill attention of a layer: the fused tcgen05 kernel, or -- for
+        head_dim 512 or a sliding window that masks keys at this length -- the
+        reference's QK^T -> masked softmax -> PV GEMM chain
+        (gemma4_150/prefill_gpu.py:259-313)."""
+        return "fused" if sp["hd"] <= 256 and (not sp["window"] or S <= sp["window"]) else "gemm"
+
     def _prefill_buffers(self, S):
         if self._pf is not None and self._pf["S"] >= S:
             return self._pf
         dev = self.dm.device
-        H, F, nh, hd = self.H, self.F, self.nh, self.hd
+        H, F, nh = self.H, self.F, self.nh
+        specs = [L["spec"] for L in self.dm.layers]
         f16 = lambda *s: torch.empty(s, dtype=torch.float16, device=dev)  # noqa: E731
         f32 = lambda *s: torch.empty(s, dtype=torch.float32, device=dev)  # noqa: E731
+        # per-layer widths vary: activations live in flat buffers of the widest layer
         pf = {"S": S,
               "tok": torch.empty(S, dtype=torch.int32, device=dev),
               "tok_host": torch.empty(S, dtype=torch.int32, pin_memory=True),
               "hid": f32(S, H), "h16": f16(S, H), "hlast": f32(S, H),
-              "qkv16": f16(S, self.nqkv), "q16": f16(S, nh, hd), "k16": f16(self.max_seq, hd),
-              "v16": f16(self.max_seq, hd), "attn16": f16(S, nh * hd), "o16": f16(S, H), "a16": f16(S, F),
-              "d16": f16(S, H)}
-        ws = max(kern.gemm_q4_workspace_size(S, n, k) for n, k in
-                 ((self.nqkv, H), (H, self.qd), (2 * F, H), (H, F)))
+              "qkv16": f16(S * self.nqkv), "q16": f16(S * self.qd), "attn16": f16(S * self.qd), "o16": f16(S, H),
+              "a16": f16(S * F), "d16": f16(S, H)}
+        # f16 K/V for the attention: one scratch pair per head_dim, and a pair of
+        # its own for every layer whose K/V a later (KV-shared) layer reads
+        sources = {sp["src"] for sp in specs if not sp["own"]}
+        pf["kv16"] = {}
+        for li, sp in enumerate(specs):
+            if sp["own"]:
+                key = li if li in sources else ("hd", sp["hd"])
+                if key not in pf["kv16"]:
+                    pf["kv16"][key] = (f16(self.max_seq, sp["hd"]), f16(self.max_seq, sp["hd"]))
+        ws = max(kern.gemm_q4_workspace_size(S, n, k) for sp in specs for n, k in
+                 ((sp["nqkv"], H), (H, sp["qd"]), (2 * sp["F"], H), (H, sp["F"])))
         pf["ws"] = torch.empty(max(1, ws // 4), dtype=torch.float32, device=dev)
         if self.dm.ple is not None:
             pd, nL = self.dm.ple["d"], len(self.dm.layers)
             pf["ple_x16"], pf["ple_ctx"], pf["ple_in"] = f16(S, H), f32(S, nL * pd), f32(S, nL, pd)
-        aws = _lib.load().sb_attn_prefill_workspace_size(S, nh, hd)
+        aws = max([_lib.load().sb_attn_prefill_workspace_size(S, nh, sp["hd"]) for sp in specs
+                   if self._attn_route(sp, S) == "fused"] + [0])
         pf["attn_ws"] = torch.empty(max(4, aws // 4), dtype=torch.float32, device=dev)
+        if any(self._attn_route(sp, S) == "gemm" for sp in specs):
+            ld = (S + 7) // 8 * 8
+            pf["scores"], pf["p16"] = f32(S * nh * ld), f16(S * nh * ld)
         self._pf = pf
         self._pgraphs.clear()  # captured prefills point at the old buffers
         return pf
@@ -501,17 +553,22 @@ class Runner:
 
     def prefill_launches(self, S: int) -> int:
         """Kernels of this library launched by one prefill of length S."""
-        H, F = self.H, self.F
+        H = self.H
         split = lambda n, k: 1 if kern.gemm_q4_workspace_size(S, n, k) else 0  # noqa: E731
-        per_layer = (4 + split(self.nqkv, H) + split(H, self.qd) + split(2 * F, H) + split(H, F)  # 4 projections
-                     + 1 + 1 + 2)  # prep; attention; two add+norms (GEGLU is in the gate|up GEMM)
-        if _lib.load().sb_attn_prefill_workspace_size(S, self.nh, self.hd):
-            per_layer += 1  # the attention merge kernel
+        total = 0
+        for L in self.dm.layers:
+            sp = L["spec"]
+            total += (4 + split(sp["nqkv"], H) + split(H, sp["qd"]) + split(2 * sp["F"], H) + split(H, sp["F"])
+                      + 1 + 2)  # 4 projections (+ split-K finalizes); prep; two add+norms (GEGLU in the GEMM)
+            if self._attn_route(sp, S) == "fused":
+                total += 1 + (1 if _lib.load().sb_attn_prefill_workspace_size(S, self.nh, sp["hd"]) else 0)
+            else:
+                total += 3  # scores GEMM, masked softmax, P.V GEMM
         ple = 0
         if self.dm.ple is not None:  # input: cast, GEMM, combine; per layer 3 launches (GEMVs) or 5 (GEMMs)
             gemv = 2 if S <= kern.PLE_FUSED_TAIL_ROWS else 3
             ple = 3 + len(self.dm.layers) * (gemv if S <= kern.PLE_GEMV_ROWS else 5)
-        return 2 + len(self.dm.layers) * per_layer + 2 + ple
+        return 2 + total + 2 + ple
 
     def prefill_timed_gemms(self, tokens, seq: int = 0):
         """Run one prefill eagerly with CUDA events around every fused projection
@@ -527,7 +584,7 @@ class Runner:
 
     def _prefill_ops(self, pf, S, seq, s, rec=None):
         dm, Ls = self.dm, self.dm.layers
-        H, nh, hd, F = self.H, self.nh, self.hd, self.F
+        H, nh = self.H, self.nh
         ws = pf["ws"]
 
         def proj(name, A, L, key, C, K, geglu=False):
@@ -554,24 +611,37 @@ class Runner:
                       kern.group_of(P["table_scale"], nL * pd), P["scale"], self.eps, pf["ple_in"].data_ptr(), S, s)
         _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), None, _F32, None, Ls[0]["in_norm"].data_ptr(),
                   pf["hid"].data_ptr(), None, pf["h16"].data_ptr(), S, H, self.eps, s)
-        kc_off = seq * self.cache_stride * 4
         for li, L in enumerate(Ls):
-            proj("qkv", pf["h16"][:S], L, "qkv", pf["qkv16"][:S], H)
-            _lib.call("sb_qkv_prep", pf["qkv16"].data_ptr(), _F16, self.nqkv, L["q_norm"].data_ptr(),
-                      L["k_norm"].data_ptr(), L["cos"].data_ptr(), L["sin"].data_ptr(), None, 0, S, nh, hd, self.eps,
-                      pf["q16"].data_ptr(), None, self.kc[li].data_ptr() + kc_off, self.vc[li].data_ptr() + kc_off,
-                      pf["k16"].data_ptr(), pf["v16"].data_ptr(), self.cache_stride, s)
-            # causal attention over the prompt: one fused kernel
-            _lib.call("sb_attn_prefill_ws", pf["q16"].data_ptr(), pf["k16"].data_ptr(), pf["v16"].data_ptr(),
-                      pf["attn16"].data_ptr(), S, nh, hd, pf["attn_ws"].data_ptr(),
-                      pf["attn_ws"].numel() * 4, s)
-            proj("o", pf["attn16"][:S], L, "o", pf["o16"][:S], self.qd)
+            sp = L["spec"]
+            lhd, qd, Fl, nqkv = sp["hd"], sp["qd"], sp["F"], sp["nqkv"]
+            qkv16, q16, attn16 = _rows(pf["qkv16"], S, nqkv), _rows(pf["q16"], S, qd), _rows(pf["attn16"], S, qd)
+            k16, v16 = pf["kv16"].get(sp["src"], pf["kv16"].get(("hd", lhd)))
+            proj("qkv", pf["h16"][:S], L, "qkv", qkv16, H)
+            kc_off = seq * self.max_seq * lhd * 4
+            if sp["own"]:
+                _lib.call("sb_qkv_prep", qkv16.data_ptr(), _F16, nqkv, L["q_norm"].data_ptr(), L["k_norm"].data_ptr(),
+                          L["cos"].data_ptr(), L["sin"].data_ptr(), None, 0, S, nh, lhd, self.eps, q16.data_ptr(), None,
+                          self.kc[li].data_ptr() + kc_off, self.vc[li].data_ptr() + kc_off, k16.data_ptr(),
+                          v16.data_ptr(), self.max_seq * lhd, s)
+            else:  # KV sharing: q only; K/V are the source layer's (its f16 copies kept for this)
+                _lib.call("sb_qkv_prep", qkv16.data_ptr(), _F16, nqkv, L["q_norm"].data_ptr(), None,
+                          L["cos"].data_ptr(), L["sin"].data_ptr(), None, 0, S, nh, lhd, self.eps, q16.data_ptr(), None,
+                          None, None, None, None, self.max_seq * lhd, s)
+            if self._attn_route(sp, S) == "fused":  # causal attention over the prompt: one fused kernel
+                _lib.call("sb_attn_prefill_ws", q16.data_ptr(), k16.data_ptr(), v16.data_ptr(), attn16.data_ptr(), S,
+                          nh, lhd, pf["attn_ws"].data_ptr(), pf["attn_ws"].numel() * 4, s)
+            else:
+                ld = (S + 7) // 8 * 8
+                kern.attn_prefill_gemm(q16.view(S, nh, lhd), k16, v16, attn16, S, window=sp["window"],
+                                       scores=_rows(pf["scores"], S * nh, ld), p16=_rows(pf["p16"], S * nh, ld))
+            proj("o", attn16, L, "o", pf["o16"][:S], qd)
             _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), pf["o16"].data_ptr(), _F16,
                       L["post_attn_norm"].data_ptr(), L["pre_ffn_norm"].data_ptr(), pf["hid"].data_ptr(), None,
                       pf["h16"].data_ptr(), S, H, self.eps, s)
             # gate|up GEMM with GEGLU in its epilogue: writes a = gelu(gate) * up
-            proj("gate|up", pf["h16"][:S], L, "gu", pf["a16"][:S], H, geglu=True)
-            proj("down", pf["a16"][:S], L, "down", pf["d16"][:S], F)
+            a16 = _rows(pf["a16"], S, Fl)
+            proj("gate|up", pf["h16"][:S], L, "gu", a16, H, geglu=True)
+            proj("down", a16, L, "down", pf["d16"][:S], Fl)
             last = li + 1 == len(Ls)
             nxt = Ls[li + 1]["in_norm"] if not last else dm.final_norm
             _lib.call("sb_add_rmsnorm", pf["hid"].data_ptr(), pf["d16"].data_ptr(), _F16,

@@ -337,7 +337,7 @@ def _safetensors(path, tensors):
 
 
 def export_checkpoint(model_dir, H=256, nL=3, nH=2, hd=64, inter=512, vocab=768, d=256, seed=5150,
-                      ffn_gain=30.0):
+                      ffn_gain=30.0, layer_types=None, hd_full=None, inters=None, kv_shared=0, window=512):
     """A synthetic QAT checkpoint with the reference checkpoint's tensor names,
     dtypes and bit widths (gemma4_150/loader.py:23-32, 62-73;
     gemma4/qat_loader.py:53-62): 4-bit attention and MLP weights with per-row
@@ -346,7 +346,11 @@ def export_checkpoint(model_dir, H=256, nL=3, nH=2, hd=64, inter=512, vocab=768,
     tied head of the weight-only reference and the exported head agree), the
     4-bit per-layer table with one scale per d values, int8 PLE linears, bf16
     norms and per-layer projection, scalar SRQ activation scales.  vocab is a
-    multiple of 6 so export.py's [24, -1, 4] lm_head re-layout divides evenly."""
+    multiple of 6 so export.py's [24, -1, 4] lm_head re-layout divides evenly.
+    ``layer_types`` (sliding/full per layer), ``hd_full`` (head_dim of the full
+    layers), ``inters`` (FFN width per layer), ``kv_shared`` (the last layers
+    reading an earlier layer's K/V) and ``window`` give the checkpoint the real
+    model's mixed architecture (gemma4/loader.py:104-122)."""
     import json
     from slang_b200.synth import f32_to_bf16_bits, q8_weight
     rng = np.random.default_rng(seed)
@@ -385,16 +389,26 @@ def export_checkpoint(model_dir, H=256, nL=3, nH=2, hd=64, inter=512, vocab=768,
     t[LMP + "per_layer_model_projection.weight"] = bf16(rng.normal(0, 0.02, (nL * d, H)))
     t[LMP + "norm.weight"] = norm(H)
     t[LMP + "per_layer_projection_norm.weight"] = norm(d)
+    types = layer_types or ["sliding_attention"] * nL
+    first_shared = nL - kv_shared
     for L in range(nL):
         p = f"{LMP}layers.{L}."
-        for n, size, gain in (("input_layernorm", H, 1.0), ("self_attn.q_norm", hd, 0.1), ("self_attn.k_norm", hd, 0.1),
+        lhd = hd_full if (hd_full and types[L] == "full_attention") else hd
+        F = inters[L] if inters else inter
+        own = L < first_shared
+        for n, size, gain in (("input_layernorm", H, 1.0), ("self_attn.q_norm", lhd, 0.1),
+                              ("self_attn.k_norm", lhd, 0.1),
                               ("post_attention_layernorm", H, 1.0), ("pre_feedforward_layernorm", H, 1.0),
                               ("post_feedforward_layernorm", H, ffn_gain), ("post_per_layer_input_norm", H, 1.0)):
+            if n == "self_attn.k_norm" and not own:
+                continue
             t[p + n + ".weight"] = norm(size, gain)
         t[p + "layer_scalar"] = bf16(rng.uniform(0.7, 1.3, 1))
-        for m, n_out, n_in in (("self_attn.q_proj", nH * hd, H), ("self_attn.k_proj", hd, H),
-                               ("self_attn.v_proj", hd, H), ("self_attn.o_proj", H, nH * hd),
-                               ("mlp.gate_proj", inter, H), ("mlp.up_proj", inter, H), ("mlp.down_proj", H, inter)):
+        for m, n_out, n_in in (("self_attn.q_proj", nH * lhd, H), ("self_attn.k_proj", lhd, H),
+                               ("self_attn.v_proj", lhd, H), ("self_attn.o_proj", H, nH * lhd),
+                               ("mlp.gate_proj", F, H), ("mlp.up_proj", F, H), ("mlp.down_proj", H, F)):
+            if m in ("self_attn.k_proj", "self_attn.v_proj") and not own:
+                continue
             linear(p + m, n_out, n_in, 4)
         for m, n_out, n_in in (("per_layer_input_gate", d, H), ("per_layer_projection", H, d)):
             c, sc = q8_weight(rng, n_out, n_in, 0.5 / (74.0 * np.sqrt(n_in)), 1.5 / (74.0 * np.sqrt(n_in)))
@@ -406,16 +420,21 @@ def export_checkpoint(model_dir, H=256, nL=3, nH=2, hd=64, inter=512, vocab=768,
     _safetensors(os.path.join(model_dir, "model.safetensors"), t)
     cfg = {"text_config": {
         "hidden_size": H, "num_hidden_layers": nL, "num_attention_heads": nH, "num_key_value_heads": 1,
-        "vocab_size": vocab, "rms_norm_eps": 1e-6, "sliding_window": 512, "final_logit_softcapping": 30.0,
-        "hidden_size_per_layer_input": d, "bos_token_id": 2, "eos_token_id": 1, "num_kv_shared_layers": 0,
-        "layer_types": ["sliding_attention"] * nL,
+        "vocab_size": vocab, "rms_norm_eps": 1e-6, "sliding_window": window, "final_logit_softcapping": 30.0,
+        "hidden_size_per_layer_input": d, "bos_token_id": 2, "eos_token_id": 1, "num_kv_shared_layers": kv_shared,
+        "layer_types": types,
         "rope_parameters": {"sliding_attention": {"rope_theta": 10000.0},
                             "full_attention": {"rope_theta": 1000000.0, "partial_rotary_factor": 0.25}}}}
     with open(os.path.join(model_dir, "config.json"), "w") as f:
         json.dump(cfg, f)
 
 
-def export_case(prompt_len=10, steps=16):
+ARCH = dict(nL=6, hd=128, hd_full=512, inters=[256, 256, 256, 512, 512, 512], kv_shared=2, window=16, vocab=384,
+            layer_types=["sliding_attention", "sliding_attention", "full_attention", "sliding_attention",
+                         "sliding_attention", "full_attention"])
+
+
+def export_case(prompt_len=10, steps=16, out_dir=EXPORT_DIR, ckpt=None, seed=5151):
     """Run the reference's ``gemma4_150.export.export`` on the synthetic
     checkpoint (its manifest.json + weights.bin are the fixture) and the
     reference's weight-only ``QATReference`` (ple=True) on the same checkpoint
@@ -428,22 +447,22 @@ def export_case(prompt_len=10, steps=16):
     from gemma4_150.export import export
     tmp = tempfile.mkdtemp(prefix="slang_export_")
     try:
-        export_checkpoint(tmp)
-        out_dir = export(tmp)
-        os.makedirs(EXPORT_DIR, exist_ok=True)
+        export_checkpoint(tmp, **(ckpt or {}))
+        written = export(tmp)
+        os.makedirs(out_dir, exist_ok=True)
         for name in ("manifest.json", "weights.bin"):
-            shutil.copy(os.path.join(out_dir, name), os.path.join(EXPORT_DIR, name))
+            shutil.copy(os.path.join(written, name), os.path.join(out_dir, name))
         qat = QATIndex(tmp)
         config = Gemma4Config(os.path.join(tmp, "config.json"), qat.idx)
         ref = QATReference(config, qat, max_seq=prompt_len + steps + 1, ple=True)
         holder = SimpleNamespace(ref=ref)
-        prompt = synth.prompt_tokens(prompt_len, config.vocab_size, seed=5151)
+        prompt = synth.prompt_tokens(prompt_len, config.vocab_size, seed=seed)
         toks, margins, top = _RefModel.generate(holder, prompt, steps)
         out = {"prompt": np.array(prompt, np.int64), "tokens": toks, "margins": margins, "top": top,
                "top8_idx": holder.top8[0], "top8_val": holder.top8[1]}
-        np.savez_compressed(os.path.join(EXPORT_DIR, "golden_export.npz"), **out)
-        print(f"export case: {len(set(toks.tolist()))} distinct tokens in {steps}; margins min "
-              f"{margins.min():.4f}; weights.bin {os.path.getsize(os.path.join(EXPORT_DIR, 'weights.bin'))} B")
+        np.savez_compressed(os.path.join(out_dir, "golden_export.npz"), **out)
+        print(f"export case {os.path.basename(out_dir)}: {len(set(toks.tolist()))} distinct tokens in {steps}; "
+              f"margins min {margins.min():.4f}; weights.bin {os.path.getsize(os.path.join(out_dir, 'weights.bin'))} B")
     finally:
         shutil.rmtree(tmp, ignore_errors=True)
 
@@ -473,6 +492,11 @@ def main():
         print("wrote golden_small.npz", len(out))
     if want("export"):
         export_case()
+    if want("export_arch"):
+        # the real model's mixed layers: sliding (head_dim 128, 16-key window) and
+        # full (head_dim 512, partial RoPE) attention, FFN width doubling from
+        # layer 3, the last two layers reading layers 3 and 2's K/V
+        export_case(prompt_len=24, steps=16, out_dir=os.path.join(HERE, "export_arch"), ckpt=ARCH, seed=5152)
     if want("ple"):
         out = {}
         ple_cases(out)

@@ -89,7 +89,7 @@ def test_attn_prefill_matches_three_kernel_chain(cuda):
     s = kern._stream()
     _lib.call("sb_gemm_f16_f32out", q.data_ptr(), k.data_ptr(), scores.data_ptr(), S * nh, S, HD, 1.0, 1, HD, HD,
               ldp, s)
-    _lib.call("sb_softmax_causal", scores.data_ptr(), ldp, S * nh, nh, 0, S, p16.data_ptr(), ldp, s)
+    _lib.call("sb_softmax_causal", scores.data_ptr(), ldp, S * nh, nh, 0, S, 0, p16.data_ptr(), ldp, s)
     _lib.call("sb_gemm_f16", p16.data_ptr(), v.data_ptr(), chain.data_ptr(), S * nh, HD, S, 1.0, 0, ldp, HD, HD, s)
     kern.device_status()
     assert_close(fused.float().reshape(S * nh, HD).cpu().numpy(), chain.float().cpu().numpy(),

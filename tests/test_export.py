@@ -63,3 +63,27 @@ def test_export_dequant_matches_reference_row_scale_rule():
     w = q4.dequant_f32(packed, scale, 4)
     codes = q4.unpack_codes(packed, 4).astype(np.float32) - 8
     np.testing.assert_array_equal(w, codes * scale)
+
+
+ARCH = os.path.join(os.path.dirname(__file__), "golden", "export_arch")
+
+
+def test_mixed_architecture_export_layout_and_oracle():
+    """The real model's mixed layers (export_arch): sliding head_dim-128 layers
+    with a 16-key window, full head_dim-512 layers with partial RoPE, FFN width
+    doubling from layer 3, layers 4 and 5 reading the K/V of layers 3 and 2.
+    The reader recovers the per-layer structure (no k/v weights for the shared
+    layers) and the oracle on it reproduces the reference's tokens."""
+    m = manifest.read(ARCH)
+    specs = m["config"]["layer_specs"]
+    assert [sp["head_dim"] for sp in specs] == [128, 128, 512, 128, 128, 512]
+    assert [sp["inter"] for sp in specs] == [256, 256, 256, 512, 512, 512]
+    assert [sp["kv_source"] for sp in specs] == [0, 1, 2, 3, 3, 2]
+    assert m["config"]["sliding_window"] == 16 and specs[2]["rope_cutoff"] == 64
+    assert "k" not in m["layers"][4] and "k_norm" not in m["layers"][5]
+    assert m["layers"][2]["q"][0].shape == (2 * 512, 256 // 2)
+    g = np.load(os.path.join(ARCH, "golden_export.npz"))
+    assert len(set(g["tokens"].tolist())) >= 8, "the reference's trajectory should move"
+    toks, margins = odec.OracleDecoder(m, 48).generate([int(t) for t in g["prompt"]], len(g["tokens"]))
+    assert first_divergence(toks, g["tokens"], g["margins"], 1e-4, "oracle on the mixed export") is None
+    np.testing.assert_allclose(margins, g["margins"], atol=1e-4)

@@ -85,12 +85,15 @@ def test_add_rmsnorm_in_place(cuda):
     assert rel(X.cpu().numpy(), x + odec.rms_norm(y.astype(np.float32), w, EPS)) < 1e-5
 
 
-@pytest.mark.parametrize("hd", [64, 128, 256])
+@pytest.mark.parametrize("hd", [64, 128, 256, 512])
 @pytest.mark.parametrize("decode", [False, True])
-def test_qkv_prep_vs_oracle(cuda, hd, decode):
-    rng = np.random.default_rng(hd + decode)
+@pytest.mark.parametrize("q_only", [False, True])
+def test_qkv_prep_vs_oracle(cuda, hd, decode, q_only):
+    """q/k norm + RoPE + cache store; ``q_only`` is a KV-shared layer (no caches:
+    only the q heads, rows of n_heads * head_dim)."""
+    rng = np.random.default_rng(hd + decode + 7 * q_only)
     nh, S, max_seq = 8, 37, 64
-    ld = (nh + 2) * hd
+    ld = (nh + (0 if q_only else 2)) * hd
     cos, sin = odec.rope_tables(max_seq, hd, 10000.0, hd // 4)
     qn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
     kn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
@@ -110,10 +113,10 @@ def test_qkv_prep_vs_oracle(cuda, hd, decode):
     q16 = torch.empty((S, nh, hd), dtype=torch.float16, device=cuda)
     q32 = torch.empty((S, nh, hd), device=cuda)
     P, QKV, QN, KN, C, SN = (T(a, cuda) for a in (pos, qkv, qn, kn, cos, sin))
+    caches = (None, None, None, None) if q_only else (kc.data_ptr(), vc.data_ptr(), k16.data_ptr(), v16.data_ptr())
     _lib.call("sb_qkv_prep", QKV.data_ptr(), _lib.SB_F32 if decode else _lib.SB_F16, ld, QN.data_ptr(),
-              KN.data_ptr(), C.data_ptr(), SN.data_ptr(), P.data_ptr() if decode else None, start, S, nh, hd, EPS,
-              q16.data_ptr(), q32.data_ptr(),
-              kc.data_ptr(), vc.data_ptr(), k16.data_ptr(), v16.data_ptr(), max_seq * hd, kern._stream())
+              None if q_only else KN.data_ptr(), C.data_ptr(), SN.data_ptr(), P.data_ptr() if decode else None, start,
+              S, nh, hd, EPS, q16.data_ptr(), q32.data_ptr(), *caches, max_seq * hd, kern._stream())
     kern.device_status()
     q32n, q16n = q32.cpu().numpy(), q16.cpu().numpy()
     kcn, vcn = kc.cpu().numpy(), vc.cpu().numpy()
@@ -126,21 +129,71 @@ def test_qkv_prep_vs_oracle(cuda, hd, decode):
         b = s if decode else 0
         assert rel(q32n[s], q) < 1e-5
         assert_f16_within_ulp(q16n[s], q)
+        if q_only:
+            continue
         assert rel(kcn[b, p], k) < 1e-5
         assert rel(vcn[b, p], v) < 1e-5
+    if q_only:
+        assert not kcn.any() and not vcn.any(), "a q-only prep must not touch the caches"
 
 
-def _attn_decode_ref(q, kc, vc, pos):
-    """softmax(q K^T) V over keys 0..pos of each sequence, attention scaling 1.0
-    (the oracle's decode attention, oracle/decoder.py OracleDecoder.layer)."""
+def _attn_decode_ref(q, kc, vc, pos, window=0):
+    """softmax(q K^T) V over keys 0..pos of each sequence (the last ``window``
+    of them when set), attention scaling 1.0 (the oracle's decode attention,
+    oracle/decoder.py OracleDecoder.layer)."""
     out = np.empty_like(q)
     for b in range(q.shape[0]):
-        s = q[b].astype(np.float64) @ kc[b, :pos[b] + 1].astype(np.float64).T
+        lo = max(0, int(pos[b]) + 1 - window) if window else 0
+        s = q[b].astype(np.float64) @ kc[b, lo:pos[b] + 1].astype(np.float64).T
         s -= s.max(axis=-1, keepdims=True)
         p = np.exp(s)
         p /= p.sum(axis=-1, keepdims=True)
-        out[b] = (p @ vc[b, :pos[b] + 1].astype(np.float64)).astype(np.float32)
+        out[b] = (p @ vc[b, lo:pos[b] + 1].astype(np.float64)).astype(np.float32)
     return out
+
+
+# head_dim 512 (the checkpoint's full-attention layers) and sliding windows that
+# start inside a split, on a split boundary, or cover everything
+@pytest.mark.parametrize("m,nh,hd,max_seq,window", [(3, 8, 512, 300, 0), (4, 8, 256, 700, 512), (5, 2, 64, 200, 40),
+                                                    (3, 8, 512, 900, 64), (6, 4, 128, 300, 1000)])
+def test_attn_decode_window_and_wide_heads(cuda, m, nh, hd, max_seq, window):
+    rng = np.random.default_rng(m + nh + hd + max_seq + window)
+    q = rng.standard_normal((m, nh, hd), dtype=np.float32) * np.float32(0.1)
+    kc = rng.standard_normal((m, max_seq, hd), dtype=np.float32)
+    vc = rng.standard_normal((m, max_seq, hd), dtype=np.float32)
+    pos = np.minimum(np.array([0, window, max_seq - 1, 32 * 5 + 7, window + 33, max_seq // 3][:m]), max_seq - 1)
+    pos = pos.astype(np.int32)
+    Q, KC, VC, P = T(q, cuda), T(kc, cuda), T(vc, cuda), T(pos, cuda)
+    got = kern.attn_decode(Q, KC, VC, P, window=window).cpu().numpy()
+    kern.device_status()
+    ref = _attn_decode_ref(q, kc, vc, pos, window)
+    assert np.abs(got - ref).max() <= 2e-5 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("S,nh,hd,window", [(200, 8, 512, 0), (300, 2, 64, 64), (130, 4, 256, 17), (96, 8, 512, 40)])
+def test_attn_prefill_gemm_chain_window_and_wide_heads(cuda, S, nh, hd, window):
+    """The GEMM -> windowed causal softmax -> GEMM prefill attention (used for
+    sliding-window and head_dim-512 layers) vs float64 with the same mask."""
+    rng = np.random.default_rng(S + nh + hd + window)
+    q = (rng.standard_normal((S, nh, hd)) * 0.1).astype(np.float16)
+    k = rng.standard_normal((S, hd)).astype(np.float16)
+    v = rng.standard_normal((S, hd)).astype(np.float16)
+    out = torch.empty((S, nh * hd), dtype=torch.float16, device=cuda)
+    kern.attn_prefill_gemm(T(q, cuda), T(k, cuda), T(v, cuda), out, S, window=window)
+    kern.device_status()
+    got = out.float().cpu().numpy().reshape(S, nh, hd)
+    sc = np.einsum("shd,td->hst", q.astype(np.float64), k.astype(np.float64))
+    i = np.arange(S)
+    mask = i[None, :] > i[:, None]
+    if window:
+        mask |= i[None, :] < i[:, None] + 1 - window
+    sc[:, mask] = -np.inf
+    sc -= sc.max(axis=-1, keepdims=True)
+    p = np.exp(sc)
+    p /= p.sum(axis=-1, keepdims=True)
+    ref = np.einsum("hst,td->shd", p, v.astype(np.float64))
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err < 1e-2, f"max rel err {err:.3e}"
 
 
 # (sequences, heads, head_dim, max_seq): the last two make the kernel walk
@@ -162,9 +215,9 @@ def test_attn_decode_vs_oracle(cuda, m, nh, hd, max_seq):
     out16 = torch.empty((m, nh, hd), dtype=torch.float16, device=cuda)
     nbytes = ws.numel() * 4
     _lib.call("sb_attn_decode", Q.data_ptr(), KC.data_ptr(), VC.data_ptr(), max_seq * hd, P.data_ptr(), m, nh, hd,
-              max_seq, out.data_ptr(), ws.data_ptr(), nbytes, kern._stream())
+              max_seq, 0, out.data_ptr(), ws.data_ptr(), nbytes, kern._stream())
     _lib.call("sb_attn_decode_f16", Q.data_ptr(), KC.data_ptr(), VC.data_ptr(), max_seq * hd, P.data_ptr(), m, nh, hd,
-              max_seq, out16.data_ptr(), ws.data_ptr(), nbytes, kern._stream())
+              max_seq, 0, out16.data_ptr(), ws.data_ptr(), nbytes, kern._stream())
     kern.device_status()
     ref = _attn_decode_ref(q, kc, vc, pos)
     got = out.cpu().numpy()

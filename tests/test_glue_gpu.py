@@ -124,13 +124,13 @@ def test_qkv_prep_vs_oracle(cuda, hd, decode, q_only):
         row = qkv[s].astype(np.float32)
         p = int(pos[s])
         q = odec.apply_rope(odec.rms_norm(row[:nh * hd].reshape(nh, hd), qn, EPS), cos[p], sin[p])
-        k = odec.apply_rope(odec.rms_norm(row[nh * hd:(nh + 1) * hd].reshape(1, hd), kn, EPS), cos[p], sin[p])[0]
-        v = odec.rms_norm(row[(nh + 1) * hd:], None, EPS)
         b = s if decode else 0
         assert rel(q32n[s], q) < 1e-5
         assert_f16_within_ulp(q16n[s], q)
         if q_only:
             continue
+        k = odec.apply_rope(odec.rms_norm(row[nh * hd:(nh + 1) * hd].reshape(1, hd), kn, EPS), cos[p], sin[p])[0]
+        v = odec.rms_norm(row[(nh + 1) * hd:], None, EPS)
         assert rel(kcn[b, p], k) < 1e-5
         assert rel(vcn[b, p], v) < 1e-5
     if q_only:

@@ -275,6 +275,28 @@ int sb_gemm_q4_argmax(const void* a, const void* w, const void* scales, int scal
 int sb_gemm_q4_noalloc(const void* a, const void* w, const void* scales, int scale_dtype, int group,
                        void* c, int m, int n, int k, float alpha, int lda, int ldc, void* stream);
 
+/*
+ * A quantised linear with static range quantisation (SRQ) of its activations,
+ * the reference's production decode arithmetic (ReferenceSRQ._qlin,
+ * gemma4_150/reference.py:96-101; kernels qkv_70, oproj_73, gateup_74/95,
+ * down_75/96 of gemma4_150/kernels_dsl.py):
+ *   y = srq(W @ srq(x, in_scale), out)      srq(v, s) = clip(round(v / s), -128, 127) * s
+ * with out = out_scales[row] when out_scales is given (rows of several linears
+ * concatenated, e.g. q|k|v, or gate|up interleaved), else out_scale; a scale of
+ * 0 skips that side's srq.  The input codes are exact integers, so the dot
+ * sum (q - zp) * code -- the reference's zero-point fold of sum(a) -- is
+ * computed exactly in 32-bit integers; W as in sb_gemv_q4 (bits 4) /
+ * sb_gemv_q2 (bits 2), with its group or per-row scales.
+ */
+int sb_gemv_srq(const void* w, int bits, const void* scales, int scale_dtype, int group, const void* x, int x_dtype,
+                float in_scale, float out_scale, const float* out_scales, float* y, int ldy, int m, int n, int k,
+                void* stream);
+
+/* out[i] = srq(x[i], scale) elementwise (f16 or f32 in and out; scale > 0):
+ * the activation-side quantisations of the reference's SRQ forward, e.g. the
+ * attention output before the o projection (gemma4_150/reference.py:176). */
+int sb_srq(const void* x, int x_dtype, size_t n, float scale, void* out, int out_dtype, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Decoder glue around the matmuls (the Gemma-4-E2B-shaped model: hidden H,
  * nh query heads and one KV head of head_dim, GEGLU FFN).  Activations of the

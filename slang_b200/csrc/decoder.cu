@@ -8,6 +8,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "q4_dot.cuh"
 
 namespace {
 
@@ -440,6 +441,20 @@ __global__ void softmax_causal_kernel(const float* __restrict__ scores, int ld_s
     prow[t] = t >= first && t <= last ? __float2half_rn(expf(srow[t] - m) / l) : __float2half_rn(0.f);
 }
 
+// ---------------------------------------------------------------- SRQ
+// out[i] = srq(x[i], s) = clip(round(x / s), -128, 127) * s (gemma4_150/reference.py:30-31),
+// read and written as f32 or f16 (f16 output rounds the quantised value).
+__global__ void srq_kernel(const void* __restrict__ x, int x_f16, size_t n, float s, void* out, int out_f16) {
+  sbd::griddep_launch_dependents();
+  sbd::griddep_wait();
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const float v = static_cast<float>(sbd::srq_code(load_act(x, x_f16, i), s)) * s;
+    if (out_f16) static_cast<__half*>(out)[i] = __float2half_rn(v);
+    else static_cast<float*>(out)[i] = v;
+  }
+}
+
 // ---------------------------------------------------------------- GEGLU
 // out[r, i] = gelu_tanh(gu[r, 2i]) * gu[r, 2i + 1]  (gate and up rows interleaved)
 __global__ void geglu_kernel(const void* __restrict__ gu, int gu_f16, int f, int rows, float* out32, __half* out16) {
@@ -849,6 +864,18 @@ extern "C" int sb_softmax_causal(const float* scores, int ld_s, int rows, int n_
                                  scores, ld_s, n_heads, start_pos, n_keys, window, static_cast<__half*>(p16), ld_p);
   if (e != cudaSuccess) return sb::cuda_fail(e, "softmax_causal_kernel");
   return sb::launch_status("softmax_causal_kernel");
+}
+
+extern "C" int sb_srq(const void* x, int x_dtype, size_t n, float scale, void* out, int out_dtype, void* stream) {
+  SB_CHECK_ARG((x_dtype == SB_F16 || x_dtype == SB_F32) && (out_dtype == SB_F16 || out_dtype == SB_F32),
+               "sb_srq: bad dtype");
+  SB_CHECK_ARG(scale > 0.f, "sb_srq: scale must be > 0");
+  if (n == 0) return SB_OK;
+  SB_CHECK_ARG(x && out, "sb_srq: null pointer");
+  cudaError_t e = sb::launch_pdl(srq_kernel, dim3(grid_for(n, kT)), dim3(kT), 0, static_cast<cudaStream_t>(stream), x,
+                                 static_cast<int>(x_dtype == SB_F16), n, scale, out, static_cast<int>(out_dtype == SB_F16));
+  if (e != cudaSuccess) return sb::cuda_fail(e, "srq_kernel");
+  return sb::launch_status("srq_kernel");
 }
 
 extern "C" int sb_geglu(const void* gu, int dtype, int m, int f, float* out32, void* out16, void* stream) {

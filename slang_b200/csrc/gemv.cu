@@ -65,7 +65,18 @@ struct GemvParams {
   const unsigned long long* peer_mailboxes;  // device array of `world` mailbox addresses
   const uint32_t* peer_epoch;                // this rank's step counter (its parity picks the key slots)
   int world, peer_row0;                      // peer_row0: first batch row of this launch
+  // static range quantisation (SRQ) of the linear, gemma4_150/reference.py:96-101:
+  // y = srq(W @ srq(x, srq_in), out) with out = srq_out_rows[row] when given,
+  // else srq_out; a scale of 0 skips that srq
+  float srq_in, srq_out;
+  const float* srq_out_rows;
 };
+
+// The output side of an SRQ linear: srq(y, s) = clip(round(y / s), -128, 127) * s.
+__device__ __forceinline__ float srq_out(const GemvParams& p, int row, float v) {
+  const float s = p.srq_out_rows ? p.srq_out_rows[row] : p.srq_out;
+  return s != 0.f ? static_cast<float>(sbd::srq_code(v, s)) * s : v;
+}
 
 struct GemvSmem {
   uint8_t w[kRing][kStageW];
@@ -117,7 +128,10 @@ __device__ __forceinline__ void load_x_groups(const GemvParams& p, const int (&g
           }
         }
       }
-      sbd::quantise_group(v, xg[m][u]);
+      if (p.srq_in != 0.f)
+        sbd::srq_group(v, p.srq_in, xg[m][u]);
+      else
+        sbd::quantise_group(v, xg[m][u]);
     }
   }
 }
@@ -281,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
       const int row = r0 + rr;
       if (m >= p.m) continue;
       if (EPI == EPI_STORE) {
-        p.y[static_cast<size_t>(m) * p.ldy + row] = v;
+        p.y[static_cast<size_t>(m) * p.ldy + row] = srq_out(p, row, v);
       } else {
         if (p.logits) p.logits[static_cast<size_t>(m) * p.n + row] = v;
         if (v != v) v = -INFINITY;
@@ -431,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
           if (m >= p.m) continue;
           float v = acc[m];
           if (EPI == EPI_STORE) {
-            p.y[static_cast<size_t>(m) * p.ldy + row] = v;
+            p.y[static_cast<size_t>(m) * p.ldy + row] = srq_out(p, row, v);
           } else {
             if (p.logits) p.logits[static_cast<size_t>(m) * p.n + row] = v;
             if (v != v) v = -INFINITY;
@@ -700,7 +714,8 @@ int zero_keys(unsigned long long* keys, int m, cudaStream_t s) {
 }  // namespace sb
 
 static int gemv_impl(const char* fn, int bits, const void* w, const void* scales, int scale_dtype, int group,
-                     const void* x, int x_dtype, float* y, int ldy, int m, int n, int k, void* stream) {
+                     const void* x, int x_dtype, float* y, int ldy, int m, int n, int k, void* stream,
+                     float srq_in = 0.f, float srq_out_s = 0.f, const float* srq_out_rows = nullptr) {
   int rc = check_common(fn, w, scales, scale_dtype, group, x, x_dtype, m, n, k, bits);
   if (rc != SB_OK) return rc;
   SB_CHECK_ARG(ldy >= n, "%s: ldy=%d < n=%d", fn, ldy, n);
@@ -717,6 +732,9 @@ static int gemv_impl(const char* fn, int bits, const void* w, const void* scales
   p.group = group;
   p.ldy = ldy;
   p.bits = bits;
+  p.srq_in = srq_in;
+  p.srq_out = srq_out_s;
+  p.srq_out_rows = srq_out_rows;
   return run(p, EPI_STORE, x_dtype == SB_F32, scale_dtype == SB_SCALE_F16, static_cast<cudaStream_t>(stream));
 }
 
@@ -728,6 +746,16 @@ extern "C" int sb_gemv_q4(const void* w, const void* scales, int scale_dtype, in
 extern "C" int sb_gemv_q2(const void* w, const void* scales, int scale_dtype, int group, const void* x,
                           int x_dtype, float* y, int ldy, int m, int n, int k, void* stream) {
   return gemv_impl("sb_gemv_q2", 2, w, scales, scale_dtype, group, x, x_dtype, y, ldy, m, n, k, stream);
+}
+
+extern "C" int sb_gemv_srq(const void* w, int bits, const void* scales, int scale_dtype, int group, const void* x,
+                           int x_dtype, float in_scale, float out_scale, const float* out_scales, float* y, int ldy,
+                           int m, int n, int k, void* stream) {
+  SB_CHECK_ARG(bits == 2 || bits == 4, "sb_gemv_srq: bits=%d must be 2 or 4", bits);
+  SB_CHECK_ARG(in_scale >= 0.f && out_scale >= 0.f && in_scale == in_scale && out_scale == out_scale,
+               "sb_gemv_srq: scales must be >= 0 (0 = no quantisation on that side)");
+  return gemv_impl("sb_gemv_srq", bits, w, scales, scale_dtype, group, x, x_dtype, y, ldy, m, n, k, stream, in_scale,
+                   out_scale, out_scales);
 }
 
 static int lmhead_impl(const char* fn, int bits, const void* emb, const void* scales, int scale_dtype, int group,

@@ -20,20 +20,17 @@ struct XGroup {
   float sx;
 };
 
-__device__ __forceinline__ void quantise_group(const float (&v)[32], XGroup& g) {
-  float mx = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(v[i]));
-  const float inv = mx > 0.f ? 32767.f / mx : 0.f;
-  g.sx = mx / 32767.f;
+// Pack 32 integer activations (|x_int| < 2^15) and their scale into g.
+__device__ __forceinline__ void pack_group(const int (&xi)[32], float sx, XGroup& g) {
+  g.sx = sx;
   int sum = 0;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     uint32_t he = 0, ho = 0, le = 0, lo = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int xe = __float2int_rn(v[8 * j + 2 * i] * inv);
-      const int xo = __float2int_rn(v[8 * j + 2 * i + 1] * inv);
+      const int xe = xi[8 * j + 2 * i];
+      const int xo = xi[8 * j + 2 * i + 1];
       sum += xe + xo;
       he |= (static_cast<uint32_t>(xe >> 8) & 0xFFu) << (8 * i);
       ho |= (static_cast<uint32_t>(xo >> 8) & 0xFFu) << (8 * i);
@@ -46,6 +43,25 @@ __device__ __forceinline__ void quantise_group(const float (&v)[32], XGroup& g) 
     g.lo[j] = lo;
   }
   g.bias = -8 * sum;
+}
+
+// x_int = rint(x * 32767 / max|x|), scale max|x| / 32767.
+__device__ __forceinline__ void quantise_group(const float (&v)[32], XGroup& g) {
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(v[i]));
+  const float inv = mx > 0.f ? 32767.f / mx : 0.f;
+  int xi[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) xi[i] = __float2int_rn(v[i] * inv);
+  pack_group(xi, mx / 32767.f, g);
+}
+
+// Static range quantisation of an activation (the reference's
+// srq(x, s) = clip(round(x / s), -128, 127) * s, gemma4_150/reference.py:30-31):
+// the integer code of x.  Division and round-half-to-even as numpy's f32 ops.
+__device__ __forceinline__ int srq_code(float x, float s) {
+  return max(-128, min(127, __float2int_rn(__fdiv_rn(x, s))));
 }
 
 // Exact integer dot of 32 int4 codes (minus 8) with the group's x_int, in four
@@ -76,12 +92,8 @@ struct XGroup2 {
   float sx;
 };
 
-__device__ __forceinline__ void quantise_group(const float (&v)[32], XGroup2& g) {
-  float mx = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(v[i]));
-  const float inv = mx > 0.f ? 32767.f / mx : 0.f;
-  g.sx = mx / 32767.f;
+__device__ __forceinline__ void pack_group(const int (&xi)[32], float sx, XGroup2& g) {
+  g.sx = sx;
   int sum = 0;
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
@@ -90,16 +102,27 @@ __device__ __forceinline__ void quantise_group(const float (&v)[32], XGroup2& g)
       uint32_t hi = 0, lo = 0;
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
-        const int xi = __float2int_rn(v[16 * j + 4 * b + k] * inv);
-        sum += xi;
-        hi |= (static_cast<uint32_t>(xi >> 8) & 0xFFu) << (8 * b);
-        lo |= (static_cast<uint32_t>(xi) & 0xFFu) << (8 * b);
+        const int x = xi[16 * j + 4 * b + k];
+        sum += x;
+        hi |= (static_cast<uint32_t>(x >> 8) & 0xFFu) << (8 * b);
+        lo |= (static_cast<uint32_t>(x) & 0xFFu) << (8 * b);
       }
       g.hi[4 * j + k] = hi;
       g.lo[4 * j + k] = lo;
     }
   }
   g.bias = -2 * sum;
+}
+
+__device__ __forceinline__ void quantise_group(const float (&v)[32], XGroup2& g) {
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(v[i]));
+  const float inv = mx > 0.f ? 32767.f / mx : 0.f;
+  int xi[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) xi[i] = __float2int_rn(v[i] * inv);
+  pack_group(xi, mx / 32767.f, g);
 }
 
 // Exact integer dot of 32 2-bit codes (minus 2) with the group's x_int.
@@ -119,6 +142,17 @@ __device__ __forceinline__ int dot_group(const uint2 q, const XGroup2& g) {
     }
   }
   return (h0 + h1) * 256 + l0 + l1;
+}
+
+// The SRQ input of a quantised linear: x_int = srq code, scale s -- the dot is
+// then exactly sum (q - zp) * code, the reference's sum-a zero-point fold
+// (gemma4_150/kernels_dsl.py:396-397) done in integers.
+template <typename XG>
+__device__ __forceinline__ void srq_group(const float (&v)[32], float s, XG& g) {
+  int xi[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) xi[i] = srq_code(v[i], s);
+  pack_group(xi, s, g);
 }
 
 // The group types and weight chunk of one 32-value group by code width.

@@ -84,6 +84,41 @@ def gemv_q4(w: torch.Tensor, scales: torch.Tensor, x: torch.Tensor,
     return y
 
 
+def gemv_srq(w: torch.Tensor, scales: torch.Tensor, x: torch.Tensor, in_scale: float, out_scale=0.0,
+             y: torch.Tensor | None = None, bits: int = 4) -> torch.Tensor:
+    """SRQ linear ``y = srq(W @ srq(x, in_scale), out)`` (``ReferenceSRQ._qlin``,
+    gemma4_150/reference.py:96-101); ``out_scale`` a float or a per-row f32
+    tensor [n] (concatenated linears)."""
+    _need(w, "w", (torch.uint8,))
+    _need(scales, "scales", (torch.float16, torch.float32))
+    _need(x, "x", (torch.float16, torch.float32))
+    n, k = w.shape[0], w.shape[1] * 8 // bits
+    x2 = x.reshape(-1, k)
+    m = x2.shape[0]
+    if y is None:
+        y = torch.empty((m, n), dtype=torch.float32, device=w.device)
+    _need(y, "y", (torch.float32,))
+    rows = None
+    if isinstance(out_scale, torch.Tensor):
+        _need(out_scale, "out_scale", (torch.float32,))
+        if out_scale.numel() != n:
+            raise ValueError("per-row out_scale must hold one scale per output row")
+        rows, out_scale = out_scale, 0.0
+    _lib.call("sb_gemv_srq", _ptr(w), bits, _ptr(scales), _DT[scales.dtype], group_of(scales, k), _ptr(x2),
+              _DT[x.dtype], float(in_scale), float(out_scale), _ptr(rows), _ptr(y), y.shape[-1], m, n, k, _stream())
+    return y
+
+
+def srq(x: torch.Tensor, scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Elementwise ``clip(round(x / scale), -128, 127) * scale`` (gemma4_150/reference.py:30-31)."""
+    _need(x, "x", (torch.float16, torch.float32))
+    if out is None:
+        out = torch.empty_like(x)
+    _need(out, "out", (torch.float16, torch.float32))
+    _lib.call("sb_srq", _ptr(x), _DT[x.dtype], x.numel(), float(scale), _ptr(out), _DT[out.dtype], _stream())
+    return out
+
+
 def lmhead_argmax(emb: torch.Tensor, scales: torch.Tensor, h: torch.Tensor, row_offset: int = 0,
                   keys: torch.Tensor | None = None, tokens: torch.Tensor | None = None,
                   logits: torch.Tensor | None = None, want_tokens: bool = True, bits: int = 4):

@@ -19,8 +19,10 @@ structure lives in manifest["layers"].  ``read`` loads two dialects of it:
   ``L{i}.{plegate,pleproj}_codes``/``_rowscale`` as +128-biased int8), and per
   layer ``head_dim``, ``q_dim``, ``intermediate``, ``sliding``, ``kv_source``,
   ``rope_theta``, ``rope_cutoff``.  The SRQ activation scales
-  (``layers[i].scales``, the GELU tables) are not used: the path is weight-only,
-  the reference's ``s == 0`` branch (gemma4_150/reference.py:30-31);
+  (``layers[i].scales``) are returned per layer as ``srq`` for the SRQ
+  linears (``sb_gemv_srq``); the model runs weight-only, the reference's
+  ``s == 0`` branch (gemma4_150/reference.py:30-31), and the GELU tables of
+  the SRQ kernels are not read;
 * this build's group-scale extension, written by ``write``: the same names for
   the packed weights and norms, plus per-group f16 scale tensors
   ``L{i}.{name}_gscale`` of shape ``[n_out, n_in/group]`` (``config.group``)
@@ -182,6 +184,9 @@ def _read_export(man: dict, get) -> dict:
         o_w12 = get(f"L{i}.o_w12")
         L.update(in_norm=get(f"L{i}.in_norm"), q_norm=get(f"L{i}.q_norm"), post_attn_norm=o_w12[:H],
                  pre_ffn_norm=o_w12[H:], post_ffn_norm=get(f"L{i}.down_nw"))
+        # the SRQ activation scales of each linear (qkv_in, q_out, k_out, v_out, o_in, o_out, gate_in, ...),
+        # for the SRQ arithmetic (gemma4_150/reference.py:96-101); the weight-only path ignores them
+        L["srq"] = {k: float(v) for k, v in man["layers"][i].get("scales", {}).items()}
         model["layers"].append(L)
     if "ple_q" in man["tensors"]:
         d = int(c["ple_d"])

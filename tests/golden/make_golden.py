@@ -354,6 +354,7 @@ def export_checkpoint(model_dir, H=256, nL=3, nH=2, hd=64, inter=512, vocab=768,
     import json
     from slang_b200.synth import f32_to_bf16_bits, q8_weight
     rng = np.random.default_rng(seed)
+    srq_rng = np.random.default_rng(seed + 7)  # SRQ scales: a stream of their own, so weights do not move
     LMP = "model.language_model."
     t = {}
 
@@ -372,11 +373,22 @@ def export_checkpoint(model_dir, H=256, nL=3, nH=2, hd=64, inter=512, vocab=768,
             packed |= (c[:, j::per] << (bits * j)).astype(np.uint8)
         return packed
 
+    shared_in = {}
+
+    def act_scales(name):
+        # linears fed the same activation (q/k/v; gate/up) share its input scale,
+        # as export.py's qkv_in / the reference's MLP input quantisation assume
+        a, b = srq_rng.uniform(0.02, 0.08, 2).astype(np.float32)
+        key = name.rsplit(".", 1)[0] + (".qkv" if "self_attn" in name and "o_proj" not in name else
+                                        ".gateup" if ("gate_proj" in name or "up_proj" in name) else name)
+        a = shared_in.setdefault(key, a)
+        t[name + ".input_activation_scale"] = ("F32", np.array(a, np.float32))
+        t[name + ".output_activation_scale"] = ("F32", np.array(b, np.float32))
+
     def linear(name, n_out, n_in, bits, lo=0.01, hi=0.03):
         t[name + ".weight"] = ("U8", codes(n_out, n_in, bits))
         t[name + ".weight_scale"] = ("F32", rng.uniform(lo, hi, (n_out, 1)).astype(np.float32))
-        t[name + ".input_activation_scale"] = ("F32", np.array(0.05, np.float32))
-        t[name + ".output_activation_scale"] = ("F32", np.array(0.05, np.float32))
+        act_scales(name)
 
     emb = codes(vocab, H, 2)
     emb_scale = rng.uniform(0.02, 0.06, (vocab, 1)).astype(np.float32)
@@ -414,8 +426,7 @@ def export_checkpoint(model_dir, H=256, nL=3, nH=2, hd=64, inter=512, vocab=768,
             c, sc = q8_weight(rng, n_out, n_in, 0.5 / (74.0 * np.sqrt(n_in)), 1.5 / (74.0 * np.sqrt(n_in)))
             t[p + m + ".weight"] = ("I8", (c.astype(np.int16) - 128).astype(np.int8))
             t[p + m + ".weight_scale"] = ("F32", sc.reshape(-1, 1))
-            t[p + m + ".input_activation_scale"] = ("F32", np.array(0.05, np.float32))
-            t[p + m + ".output_activation_scale"] = ("F32", np.array(0.05, np.float32))
+            act_scales(p + m)
     os.makedirs(model_dir, exist_ok=True)
     _safetensors(os.path.join(model_dir, "model.safetensors"), t)
     cfg = {"text_config": {
@@ -427,6 +438,45 @@ def export_checkpoint(model_dir, H=256, nL=3, nH=2, hd=64, inter=512, vocab=768,
                             "full_attention": {"rope_theta": 1000000.0, "partial_rotary_factor": 0.25}}}}
     with open(os.path.join(model_dir, "config.json"), "w") as f:
         json.dump(cfg, f)
+
+
+def srq_case():
+    """The reference's ``srq`` on known answers (halves, clipping) and its
+    ``ReferenceSRQ._qlin`` on linears of the export_small checkpoint (same
+    seeds, so the committed manifest holds the same weights and scales),
+    inputs drawn to cover the clip range and the round-half boundaries."""
+    import shutil
+    import tempfile
+    from gemma4_150.loader import Ckpt
+    from gemma4_150.reference import ReferenceSRQ, srq
+    out = {}
+    s = np.float32(0.05)
+    kat = np.array([0.0, 0.025, 0.075, -0.025, -0.075, 1.0, 6.35, 6.4, -6.4, -6.45, 100.0, -100.0, 0.0249, 0.0251],
+                   np.float32)
+    out["srq_kat_x"], out["srq_kat_s"], out["srq_kat_y"] = kat, np.float32(s), srq(kat, float(s))
+    tmp = tempfile.mkdtemp(prefix="slang_srq_")
+    try:
+        export_checkpoint(tmp)
+        ref = ReferenceSRQ.__new__(ReferenceSRQ)
+        ref.c = Ckpt(tmp)
+        rng = np.random.default_rng(9090)
+        cases = [(0, "self_attn.q_proj"), (0, "self_attn.k_proj"), (1, "self_attn.o_proj"), (1, "mlp.gate_proj"),
+                 (2, "mlp.up_proj"), (2, "mlp.down_proj")]
+        for i, (L, mod) in enumerate(cases):
+            lin = ref.c.linear(L, mod)
+            n_in, s_in = lin["n_in"], lin["in_scale"]
+            xs = [rng.standard_normal(n_in).astype(np.float32) * np.float32(s_in * 40),
+                  # values near round-half points of x / s_in, and beyond the clip range
+                  ((rng.integers(-140, 140, n_in) + 0.5) * s_in).astype(np.float32)]
+            for j, x in enumerate(xs):
+                y, _ = ref._qlin(x, L, mod)
+                out[f"qlin{i}_{j}_x"], out[f"qlin{i}_{j}_y"] = x, y.astype(np.float32)
+            out[f"qlin{i}_layer"], out[f"qlin{i}_mod"] = np.int64(L), np.array(mod)
+            out[f"qlin{i}_in"], out[f"qlin{i}_out"] = np.float32(s_in), np.float32(lin["out_scale"])
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    np.savez_compressed(os.path.join(HERE, "golden_srq.npz"), **out)
+    print("wrote golden_srq.npz", len(out))
 
 
 ARCH = dict(nL=6, hd=128, hd_full=512, inters=[256, 256, 256, 512, 512, 512], kv_shared=2, window=16, vocab=384,
@@ -492,6 +542,8 @@ def main():
         print("wrote golden_small.npz", len(out))
     if want("export"):
         export_case()
+    if want("srq"):
+        srq_case()
     if want("export_arch"):
         # the real model's mixed layers: sliding (head_dim 128, 16-key window) and
         # full (head_dim 512, partial RoPE) attention, FFN width doubling from

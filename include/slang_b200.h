@@ -276,6 +276,22 @@ int sb_gemm_q4_noalloc(const void* a, const void* w, const void* scales, int sca
                        void* c, int m, int n, int k, float alpha, int lda, int ldc, void* stream);
 
 /*
+ * Decode GEMV with the residual add + RMSNorm as a last-arriver tail (the
+ * reference's oproj_73 / down_75, gemma4_150/kernels_dsl.py:928-996, 398-429):
+ *   y = W @ x (as sb_gemv_q4 / sb_gemv_q2 by bits; y [m][n], row stride n),
+ *   hidden[r] = hidden[r] + rmsnorm(y[r]) * w_add,
+ *   h[r] = rmsnorm(hidden[r]) * w_next  -> h_out (f32) and/or h16_out (f16), when w_next != NULL.
+ * The CTA that completes `counter` (a caller-owned u32, zero before the first
+ * call) runs the tail over all rows and re-arms it; no CTA waits on another.
+ * After a call that reported SB_ERR_TIMEOUT, zero the counter again.
+ * n % 4 == 0, n <= 8192; y, hidden, w_add, w_next, h_out 16-byte aligned.
+ */
+int sb_gemv_norm_add(const void* w, int bits, const void* scales, int scale_dtype, int group, const void* x,
+                     int x_dtype, float* y, int m, int n, int k, float* hidden, const float* w_add,
+                     const float* w_next, float* h_out, void* h16_out, float eps, unsigned int* counter,
+                     void* stream);
+
+/*
  * A quantised linear with static range quantisation (SRQ) of its activations,
  * the reference's production decode arithmetic (ReferenceSRQ._qlin,
  * gemma4_150/reference.py:96-101; kernels qkv_70, oproj_73, gateup_74/95,

@@ -64,6 +64,7 @@ SIGNATURES = {
     "sb_gemv_f16": ([_vp, _f, _vp, _i, _vp, _i, _i, _i, _i, _vp], _i),
     "sb_gemv_srq": ([_vp, _i, _vp, _i, _i, _vp, _i, _f, _f, _vp, _vp, _i, _i, _i, _i, _vp], _i),
     "sb_srq": ([_vp, _i, _sz, _f, _vp, _i, _vp], _i),
+    "sb_gemv_norm_add": ([_vp, _i, _vp, _i, _i, _vp, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp], _i),
     "sb_ple_norm_add": ([_vp, _vp, _vp, _f, _vp, _vp, _vp, _i, _i, _f, _vp], _i),
     "sb_ple_gather": ([_vp, _vp, _vp, _i, _i, _i, _f, _vp, _i, _vp], _i),
     "sb_ple_combine": ([_vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _f, _f, _vp, _i, _vp], _i),

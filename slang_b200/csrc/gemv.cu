@@ -35,6 +35,7 @@
 #include <atomic>
 
 #include "common.cuh"
+#include "norm_tail.cuh"
 #include "q4_dot.cuh"
 
 namespace {
@@ -70,6 +71,9 @@ struct GemvParams {
   // else srq_out; a scale of 0 skips that srq
   float srq_in, srq_out;
   const float* srq_out_rows;
+  // optional last-arriver residual add + RMSNorm over the launch's rows of y
+  // (tail.counter != null; EPI_STORE only)
+  sbd::NormTail tail;
 };
 
 // The output side of an SRQ linear: srq(y, s) = clip(round(y / s), -128, 127) * s.
@@ -327,6 +331,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
     __syncthreads();
     publish_keys<M>(p, sm, tid);
   }
+  if (EPI == EPI_STORE && p.tail.counter) sbd::last_arriver_tail(p.y, p.ldy, p.m, p.n, p.tail);
 }
 
 // The GEMV for rows a half-warp covers whole (ks = 1: K <= 16 * GPL * 32),
@@ -498,6 +503,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
         }
     }
   }
+  if (EPI == EPI_STORE && p.tail.counter) sbd::last_arriver_tail(p.y, p.ldy, p.m, p.n, p.tail);
 }
 
 __global__ void keys_to_tokens_kernel(const unsigned long long* keys, int32_t* tokens, int m) {
@@ -642,7 +648,15 @@ int run(GemvParams p, int epi, bool xf32, bool sf16, cudaStream_t s) {
     GemvParams q = p;
     q.m = mt;
     q.x = static_cast<const char*>(p.x) + done * x_row;
-    if (epi == EPI_STORE) q.y = p.y + static_cast<size_t>(done) * p.ldy;
+    if (epi == EPI_STORE) {
+      q.y = p.y + static_cast<size_t>(done) * p.ldy;
+      if (p.tail.counter) {  // the tail of this launch covers its own rows
+        const size_t o = static_cast<size_t>(done) * p.n;
+        q.tail.hidden = p.tail.hidden + o;
+        if (p.tail.h_out) q.tail.h_out = p.tail.h_out + o;
+        if (p.tail.h16) q.tail.h16 = p.tail.h16 + o;
+      }
+    }
     else {
       if (p.keys) q.keys = p.keys + done;
       q.peer_row0 = p.peer_row0 + done;
@@ -746,6 +760,35 @@ extern "C" int sb_gemv_q4(const void* w, const void* scales, int scale_dtype, in
 extern "C" int sb_gemv_q2(const void* w, const void* scales, int scale_dtype, int group, const void* x,
                           int x_dtype, float* y, int ldy, int m, int n, int k, void* stream) {
   return gemv_impl("sb_gemv_q2", 2, w, scales, scale_dtype, group, x, x_dtype, y, ldy, m, n, k, stream);
+}
+
+extern "C" int sb_gemv_norm_add(const void* w, int bits, const void* scales, int scale_dtype, int group,
+                                const void* x, int x_dtype, float* y, int m, int n, int k, float* hidden,
+                                const float* w_add, const float* w_next, float* h_out, void* h16_out, float eps,
+                                unsigned int* counter, void* stream) {
+  SB_CHECK_ARG(bits == 2 || bits == 4, "sb_gemv_norm_add: bits=%d must be 2 or 4", bits);
+  SB_CHECK_ARG(n % 4 == 0 && n <= 4 * sbd::kTailV4 * kThreads, "sb_gemv_norm_add: n=%d must be a multiple of 4 up to %d",
+               n, 4 * sbd::kTailV4 * kThreads);
+  SB_CHECK_ARG(hidden && w_add && counter && (!w_next || h_out || h16_out), "sb_gemv_norm_add: null pointer");
+  SB_CHECK_ARG(sb::aligned(y, 16) && sb::aligned(hidden, 16) && sb::aligned(w_add, 16) &&
+                   (!w_next || sb::aligned(w_next, 16)) && (!h_out || sb::aligned(h_out, 16)),
+               "sb_gemv_norm_add: y, hidden, w_add, w_next and h_out need 16-byte alignment");
+  int rc = check_common("sb_gemv_norm_add", w, scales, scale_dtype, group, x, x_dtype, m, n, k, bits);
+  if (rc != SB_OK) return rc;
+  if (n == 0) return SB_OK;
+  GemvParams p{};
+  p.w = static_cast<const uint8_t*>(w);
+  p.scales = scales;
+  p.x = x;
+  p.y = y;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.group = group;
+  p.ldy = n;
+  p.bits = bits;
+  p.tail = sbd::NormTail{hidden, w_add, w_next, h_out, static_cast<__half*>(h16_out), counter, 1.f, eps};
+  return run(p, EPI_STORE, x_dtype == SB_F32, scale_dtype == SB_SCALE_F16, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int sb_gemv_srq(const void* w, int bits, const void* scales, int scale_dtype, int group, const void* x,

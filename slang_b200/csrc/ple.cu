@@ -15,6 +15,7 @@
 // GEMV decodes a weight byte with the exact magic-number conversion
 // (2^23 + b as an f32 bit pattern, minus 2^23 + 128).
 #include "common.cuh"
+#include "norm_tail.cuh"
 
 namespace {
 
@@ -93,72 +94,6 @@ struct FmtF16 {
   }
 };
 
-// The PLE norm-add tail run by the last CTA of a projection GEMV (counter != null):
-// hidden[r] = (hidden[r] + rmsnorm(y[r]) * w_post) * scalar, then optionally
-// h = rmsnorm(hidden[r]) * w_next.  hidden, h_out, h16 have row stride n.
-struct PleTail {
-  float* hidden;
-  const float* w_post;
-  const float* w_next;
-  float* h_out;
-  __half* h16;
-  unsigned int* counter;
-  float scalar, eps;
-};
-
-// Run by every thread of the last-arriving CTA, after a fence: the other CTAs'
-// rows of y are read through L2 (ld.global.cg), never from a stale L1 line.
-// A thread holds up to kTailV4 float4s of a row (n <= 4 * kTailV4 * blockDim,
-// n % 4 == 0) and issues each phase's loads together: one L2 round trip per phase.
-constexpr int kTailV4 = 8;
-__device__ void ple_tail_rows(const float* y, int ldy, int m, int n, const PleTail& t) {
-  __shared__ float red[32];
-  const int n4 = n >> 2, nt = blockDim.x;
-  for (int r = 0; r < m; ++r) {
-    const float4* pr = reinterpret_cast<const float4*>(y + static_cast<int64_t>(r) * ldy);
-    float4* hr = reinterpret_cast<float4*>(t.hidden + static_cast<int64_t>(r) * n);
-    float4 v[kTailV4], xv[kTailV4];
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < kTailV4; ++j) {
-      const int i = threadIdx.x + j * nt;
-      v[j] = i < n4 ? __ldcg(pr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-      xv[j] = i < n4 ? hr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int j = 0; j < kTailV4; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
-    const float d = sqrtf(block_sum(ss, red) / n + t.eps);
-    float ss2 = 0.f;
-#pragma unroll
-    for (int j = 0; j < kTailV4; ++j) {
-      const int i = threadIdx.x + j * nt;
-      if (i < n4) {
-        const float4 wp = reinterpret_cast<const float4*>(t.w_post)[i];
-        v[j] = make_float4((xv[j].x + v[j].x / d * wp.x) * t.scalar, (xv[j].y + v[j].y / d * wp.y) * t.scalar,
-                           (xv[j].z + v[j].z / d * wp.z) * t.scalar, (xv[j].w + v[j].w / d * wp.w) * t.scalar);
-        hr[i] = v[j];
-        ss2 += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
-      }
-    }
-    if (!t.w_next) continue;
-    const float d2 = sqrtf(block_sum(ss2, red) / n + t.eps);
-#pragma unroll
-    for (int j = 0; j < kTailV4; ++j) {
-      const int i = threadIdx.x + j * nt;
-      if (i < n4) {
-        const float4 wn = reinterpret_cast<const float4*>(t.w_next)[i];
-        const float4 h = make_float4(v[j].x / d2 * wn.x, v[j].y / d2 * wn.y, v[j].z / d2 * wn.z, v[j].w / d2 * wn.w);
-        if (t.h_out) reinterpret_cast<float4*>(t.h_out + static_cast<int64_t>(r) * n)[i] = h;
-        if (t.h16) {
-          __half* o16 = t.h16 + static_cast<int64_t>(r) * n + 4 * i;
-          o16[0] = __float2half_rn(h.x), o16[1] = __float2half_rn(h.y);
-          o16[2] = __float2half_rn(h.z), o16[3] = __float2half_rn(h.w);
-        }
-      }
-    }
-  }
-}
-
 // y[r, o] = epi(sum_k W[o, k] * x[r, k] * scale(o)),  scale(o) = row_scale[o] * alpha
 // (row_scale may be null), epi(v) = v, or gelu_tanh(v) * ple[r * ld_ple + o].
 // A group of G lanes owns one output row; each lane issues all of its (up to
@@ -170,7 +105,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_rows_kernel(const uint8_t* _
                                                              const float* __restrict__ row_scale, float alpha,
                                                              const float* __restrict__ x, int ldx, int m, int n,
                                                              int k, const float* __restrict__ ple, int ld_ple,
-                                                             float* __restrict__ y, int ldy, PleTail tail) {
+                                                             float* __restrict__ y, int ldy, sbd::NormTail tail) {
   sbd::griddep_launch_dependents();
   constexpr int kRowsPerWarp = 32 / G;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -241,7 +176,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_rows_kernel(const uint8_t* _
     __syncthreads();
     if (s_last) {
       __threadfence();
-      ple_tail_rows(y, ldy, m, n, tail);
+      sbd::norm_tail_rows(y, ldy, m, n, tail);
       if (threadIdx.x == 0) *tail.counter = 0u;
     }
   }
@@ -424,7 +359,7 @@ int grid_for(int64_t total) {
 template <class Fmt, int G>
 cudaError_t launch_gemv_m(int mm, dim3 grid, dim3 block, cudaStream_t st, const uint8_t* w, int64_t w_ld,
                           const float* row_scale, float alpha, const float* x, int ldx, int n, int k, const float* ple,
-                          int ld_ple, float* y, int ldy, const PleTail& tail) {
+                          int ld_ple, float* y, int ldy, const sbd::NormTail& tail) {
 #define SB_GEMV(MM)                                                                                                  \
   return sb::launch_pdl(gemv_rows_kernel<Fmt, G, MM>, grid, block, 0, st, w, w_ld, row_scale, alpha, x, ldx, mm, n, k, \
                         ple, ld_ple, y, ldy, tail)
@@ -438,7 +373,7 @@ cudaError_t launch_gemv_m(int mm, dim3 grid, dim3 block, cudaStream_t st, const 
 template <class Fmt>
 cudaError_t launch_gemv_rows(const uint8_t* w, int64_t w_ld, const float* row_scale, float alpha, const float* x,
                              int ldx, int m, int n, int k, const float* ple, int ld_ple, float* y, int ldy,
-                             cudaStream_t st, const PleTail& tail = PleTail{}) {
+                             cudaStream_t st, const sbd::NormTail& tail = sbd::NormTail{}) {
   const int nch = k / Fmt::kVals;
   const int G = nch >= 32 ? 32 : nch >= 16 ? 16 : nch >= 8 ? 8 : 4;
   // warps per CTA: 8, fewer when a short matrix would otherwise leave SMs idle
@@ -580,17 +515,17 @@ extern "C" int sb_ple_proj_norm_add(const void* codes, const float* row_scale, c
                                     const float* w_next, float* h_out, void* h16_out, float eps, unsigned int* counter,
                                     void* stream) {
   SB_CHECK_ARG(m >= 0 && m <= kMaxM, "sb_ple_proj_norm_add: m=%d must be in 0..%d (one launch)", m, kMaxM);
-  SB_CHECK_ARG(n > 0 && n % 4 == 0 && n <= 4 * kTailV4 * kWarps * 32 && k >= 64 && k % 16 == 0 && ldg >= k &&
+  SB_CHECK_ARG(n > 0 && n % 4 == 0 && n <= 4 * sbd::kTailV4 * kWarps * 32 && k >= 64 && k % 16 == 0 && ldg >= k &&
                    ldg % 4 == 0,
                "sb_ple_proj_norm_add: n=%d must be a multiple of 4 up to %d, k=%d a multiple of 16 and >= 64", n,
-               4 * kTailV4 * kWarps * 32, k);
+               4 * sbd::kTailV4 * kWarps * 32, k);
   if (m == 0) return SB_OK;
   SB_CHECK_ARG(codes && row_scale && g && proj && hidden && w_post && counter && (!w_next || h_out || h16_out),
                "sb_ple_proj_norm_add: null pointer");
   if (!sb::aligned(codes, 16) || !sb::aligned(g, 16) || !sb::aligned(proj, 16) || !sb::aligned(hidden, 16) ||
       !sb::aligned(w_post, 16) || (w_next && !sb::aligned(w_next, 16)) || (h_out && !sb::aligned(h_out, 16)))
     return sb::fail(SB_ERR_ALIGN, "sb_ple_proj_norm_add: operands need 16-byte alignment");
-  PleTail t{hidden, w_post, w_next, h_out, static_cast<__half*>(h16_out), counter, layer_scalar, eps};
+  sbd::NormTail t{hidden, w_post, w_next, h_out, static_cast<__half*>(h16_out), counter, layer_scalar, eps};
   cudaError_t e = launch_gemv_rows<FmtQ8>(static_cast<const uint8_t*>(codes), k, row_scale, 1.f, g, ldg, m, n, k,
                                           nullptr, 0, proj, n, static_cast<cudaStream_t>(stream), t);
   if (e != cudaSuccess) return sb::cuda_fail(e, "gemv_rows_kernel<q8> + PLE tail");

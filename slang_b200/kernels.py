@@ -109,6 +109,33 @@ def gemv_srq(w: torch.Tensor, scales: torch.Tensor, x: torch.Tensor, in_scale: f
     return y
 
 
+def gemv_norm_add(w: torch.Tensor, scales: torch.Tensor, x: torch.Tensor, hidden: torch.Tensor, w_add: torch.Tensor,
+                  eps: float, w_next: torch.Tensor | None = None, h_out: torch.Tensor | None = None,
+                  h16_out: torch.Tensor | None = None, y: torch.Tensor | None = None,
+                  counter: torch.Tensor | None = None, bits: int = 4) -> torch.Tensor:
+    """Decode GEMV ``y = W @ x`` whose last-arriving CTA then runs
+    ``hidden += rmsnorm(y) * w_add`` and ``h = rmsnorm(hidden) * w_next`` (the
+    reference's oproj_73 / down_75 tails); returns y."""
+    _need(w, "w", (torch.uint8,))
+    _need(scales, "scales", (torch.float16, torch.float32))
+    _need(x, "x", (torch.float16, torch.float32))
+    for t, name in ((hidden, "hidden"), (w_add, "w_add")):
+        _need(t, name, (torch.float32,))
+    n, k = w.shape[0], w.shape[1] * 8 // bits
+    x2 = x.reshape(-1, k)
+    m = x2.shape[0]
+    if hidden.numel() != m * n:
+        raise ValueError("hidden must hold m x n values")
+    if y is None:
+        y = torch.empty((m, n), dtype=torch.float32, device=w.device)
+    if counter is None:
+        counter = _counter(w.device)
+    _lib.call("sb_gemv_norm_add", _ptr(w), bits, _ptr(scales), _DT[scales.dtype], group_of(scales, k), _ptr(x2),
+              _DT[x.dtype], _ptr(y), m, n, k, _ptr(hidden), _ptr(w_add), _ptr(w_next), _ptr(h_out), _ptr(h16_out),
+              float(eps), _ptr(counter), _stream())
+    return y
+
+
 def srq(x: torch.Tensor, scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
     """Elementwise ``clip(round(x / scale), -128, 127) * scale`` (gemma4_150/reference.py:30-31)."""
     _need(x, "x", (torch.float16, torch.float32))

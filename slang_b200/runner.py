@@ -204,7 +204,12 @@ class Runner:
 
     MAX_BATCH = 1024
 
-    def __init__(self, dm: DeviceModel, batch: int = 1, fused: bool = False, proj: str = "auto"):
+    # the o and down GEMVs of the GEMV decode path carry the residual add + RMSNorm
+    # as a last-arriver tail (sb_gemv_norm_add) instead of a separate kernel
+    NORM_TAILS = False
+
+    def __init__(self, dm: DeviceModel, batch: int = 1, fused: bool = False, proj: str = "auto",
+                 norm_tails: bool | None = None):
         if proj == "auto":
             proj = "gemv" if batch <= 8 else "gemm"
         if proj not in ("gemv", "gemm"):
@@ -221,6 +226,7 @@ class Runner:
                              "fused=False, proj='gemv'")
         self.proj = proj
         self.fused = fused
+        self.norm_tails = self.NORM_TAILS if norm_tails is None else bool(norm_tails)
         self.dm = dm
         cfg = dm.cfg
         self.B = batch
@@ -264,6 +270,7 @@ class Runner:
             ws = max(kern.gemm_q4_workspace_size(B, n, k) for n, k in
                      ((self.nqkv, H), (H, self.qd), (2 * self.F, H), (H, self.F)))
             self.gemm_ws = torch.empty(max(1, ws // 4), dtype=torch.float32, device=dev) if ws else None
+        self.tail_counter = torch.zeros(1, dtype=torch.int32, device=dev)  # last-arriver count, self re-arming
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
         self.cur = torch.zeros(B, dtype=torch.int32, device=dev)
         self.tok = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -346,15 +353,26 @@ class Runner:
             _lib.call("sb_attn_decode", q.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
                       self.max_seq * hd, self.pos.data_ptr(), B, self.nh, hd, self.max_seq, sp["window"],
                       attn.data_ptr(), self.attn_ws.data_ptr(), self.attn_ws.numel() * 4, s)
-            self._gemv(L, "o", attn, self.o)
-            _lib.call("sb_add_rmsnorm", self.x.data_ptr(), self.o.data_ptr(), _F32, L["post_attn_norm"].data_ptr(),
-                      L["pre_ffn_norm"].data_ptr(), self.x.data_ptr(), self.h.data_ptr(), None, B, H, self.eps, s)
+            nxt = L0[li + 1]["in_norm"] if li + 1 < len(L0) else dm.final_norm
+            if self.norm_tails:
+                kern.gemv_norm_add(L["o"][0], L["o"][1], attn, self.x, L["post_attn_norm"], self.eps,
+                                   w_next=L["pre_ffn_norm"], h_out=self.h, y=self.o, counter=self.tail_counter,
+                                   bits=L["bits"]["o"])
+            else:
+                self._gemv(L, "o", attn, self.o)
+                _lib.call("sb_add_rmsnorm", self.x.data_ptr(), self.o.data_ptr(), _F32,
+                          L["post_attn_norm"].data_ptr(), L["pre_ffn_norm"].data_ptr(), self.x.data_ptr(),
+                          self.h.data_ptr(), None, B, H, self.eps, s)
             self._gemv(L, "gu", self.h, gu)
             _lib.call("sb_geglu", gu.data_ptr(), _F32, B, F, a.data_ptr(), None, s)
-            self._gemv(L, "down", a, self.d)
-            nxt = L0[li + 1]["in_norm"] if li + 1 < len(L0) else dm.final_norm
-            _lib.call("sb_add_rmsnorm", self.x.data_ptr(), self.d.data_ptr(), _F32, L["post_ffn_norm"].data_ptr(),
-                      nxt.data_ptr(), self.x.data_ptr(), self.h.data_ptr(), None, B, H, self.eps, s)
+            if self.norm_tails:
+                kern.gemv_norm_add(L["down"][0], L["down"][1], a, self.x, L["post_ffn_norm"], self.eps, w_next=nxt,
+                                   h_out=self.h, y=self.d, counter=self.tail_counter, bits=L["bits"]["down"])
+            else:
+                self._gemv(L, "down", a, self.d)
+                _lib.call("sb_add_rmsnorm", self.x.data_ptr(), self.d.data_ptr(), _F32,
+                          L["post_ffn_norm"].data_ptr(), nxt.data_ptr(), self.x.data_ptr(), self.h.data_ptr(), None,
+                          B, H, self.eps, s)
             if P is not None:  # PLE block, then the next norm from its output (gemma4/reference.py:154-163)
                 Lp = L["ple"]
                 kern.gemv_q8(Lp["gate"][0], Lp["gate"][1], self.x, out=self.ple_g, ple=self.ple_in[:, li])
@@ -406,7 +424,7 @@ class Runner:
             per_layer = (4 + split(self.nqkv, H) + split(H, self.qd) + split(2 * F, H) + split(H, F)
                          + 1 + 2 + 2)  # prep, attention (2), add+norm (2)
             return 2 + nL * per_layer + 2 + 1  # embed + norm, layers, argmax GEMM + tokens, advance
-        per_layer = 4 + 1 + 2 + 2 + 1  # 4 GEMVs, prep, attention (2), add+norm (2), geglu
+        per_layer = 4 + 1 + 2 + (0 if self.norm_tails else 2) + 1  # 4 GEMVs, prep, attention (2), add+norm (2), geglu
         per_ple = 2 if self.B <= kern.PLE_FUSED_TAIL_ROWS else 3  # per layer: gate GEMV, projection GEMV (+ fused tail)
         ple = 0 if self.dm.ple is None else 2 + per_ple * nL  # + PLE input (GEMV + combine)
         return 2 + nL * per_layer + 2 + 1 + ple  # embed + first norm, layers, lm_head (gemv + tokens), advance

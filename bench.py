@@ -881,6 +881,15 @@ def main():
     with torch.cuda.stream(stream):
         dms_ops = timed_graph(torch, r.graph, DECODE_STEPS, args.warmup, stream)
     dms_ops = max_over_ranks(dms_ops)
+    # the same per-op step with the o / down residual norms as last-arriver GEMV tails
+    rt = runner.Runner(dm, 1, norm_tails=True)
+    rt.prefill(prompt)
+    rt.capture()
+    with torch.cuda.stream(rt.stream):
+        dms_tails = max_over_ranks(timed_graph(torch, rt.graph, DECODE_STEPS, args.warmup, rt.stream))
+    tails_launches = rt.kernel_launches_per_step()
+    rt.graph = None
+    del rt
     ctx = PROMPT + args.warmup + DECODE_STEPS // 2
     w_bytes = sum(t.numel() * t.element_size() for L in dm.layers for key in ("qkv", "o", "gu", "down") for t in L[key])
     lm_bytes = dm.embed_q.numel() + dm.embed_s.numel() * 2
@@ -940,7 +949,9 @@ def main():
                        "kernel": "decode_step_kernel (persistent, one cooperative launch per token)",
                        "gpu_launches_per_token": rf.kernel_launches_per_step(),
                        "per_op_graph": {"value": world * 1e3 / dms_ops, "ms_per_token": dms_ops,
-                                        "gpu_launches_per_token": r.kernel_launches_per_step()}},
+                                        "gpu_launches_per_token": r.kernel_launches_per_step()},
+                       "per_op_graph_norm_tails": {"value": world * 1e3 / dms_tails, "ms_per_token": dms_tails,
+                                                   "gpu_launches_per_token": tails_launches}},
             "config5": {"metric": "batched decode tok/s (all replicas) by batch and projection path; gate|up "
                                   "per-call time GEMV vs tcgen05 GEMM", "scaling": "weak (replicas)", **c5},
             "lmhead": {"metric": "q4 GEMV HBM GB/s (lm_head 262144x1536 + argmax)", "value": lm_alg / (lms / 1e3) / 1e9,

@@ -48,7 +48,11 @@ constexpr int kStageS = 3 * 1024;               // max scale bytes per stage
 constexpr int kCtasPerSm = 2;                   // two CTAs share an SM (registers <= 113)
 constexpr int kRedMax = 128;                    // partial-sum slots per stage (rows x ks x M)
 
-enum { EPI_STORE = 0, EPI_ARGMAX = 1 };
+// epilogues: store y; running argmax keys; store srq(y) of an SRQ linear (whose
+// input is srq-coded too); store y and run the last-arriver norm-add tail.
+// The SRQ and tail forms are separate instantiations, so the plain store keeps
+// its registers.
+enum { EPI_STORE = 0, EPI_ARGMAX = 1, EPI_SRQ = 2, EPI_TAIL = 3 };
 
 struct GemvParams {
   const uint8_t* w;
@@ -97,7 +101,7 @@ using sbd::make_key;
 
 // This lane's groups of x (rows m < M of the batch, groups gidx[u]) quantised
 // to 16-bit integers, kept in registers for the whole launch.
-template <int M, int GPL, typename XG>
+template <int M, int GPL, typename XG, bool SRQ>
 __device__ __forceinline__ void load_x_groups(const GemvParams& p, const int (&gidx)[GPL], const bool (&gval)[GPL],
                                               XG (&xg)[M][GPL]) {
 #pragma unroll
@@ -132,10 +136,13 @@ __device__ __forceinline__ void load_x_groups(const GemvParams& p, const int (&g
           }
         }
       }
-      if (p.srq_in != 0.f)
-        sbd::srq_group(v, p.srq_in, xg[m][u]);
-      else
-        sbd::quantise_group(v, xg[m][u]);
+      if constexpr (SRQ) {
+        if (p.srq_in != 0.f) {
+          sbd::srq_group(v, p.srq_in, xg[m][u]);
+          continue;
+        }
+      }
+      sbd::quantise_group(v, xg[m][u]);
     }
   }
 }
@@ -225,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
   sbd::griddep_wait();
   // this lane's groups of x, quantised once (kept in registers)
   XG xg[M][GPL];
-  load_x_groups<M, GPL, XG>(p, gidx, gval, xg);
+  load_x_groups<M, GPL, XG, EPI == EPI_SRQ>(p, gidx, gval, xg);
 
   float best_v[M];
   long long best_i[M];
@@ -298,8 +305,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
       for (int q = 0; q < ks; ++q) v += red[(rr * ks + q) * M + m];
       const int row = r0 + rr;
       if (m >= p.m) continue;
-      if (EPI == EPI_STORE) {
-        p.y[static_cast<size_t>(m) * p.ldy + row] = srq_out(p, row, v);
+      if (EPI != EPI_ARGMAX) {
+        p.y[static_cast<size_t>(m) * p.ldy + row] = EPI == EPI_SRQ ? srq_out(p, row, v) : v;
       } else {
         if (p.logits) p.logits[static_cast<size_t>(m) * p.n + row] = v;
         if (v != v) v = -INFINITY;
@@ -331,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_kernel(const Gem
     __syncthreads();
     publish_keys<M>(p, sm, tid);
   }
-  if (EPI == EPI_STORE && p.tail.counter) sbd::last_arriver_tail(p.y, p.ldy, p.m, p.n, p.tail);
+  if constexpr (EPI == EPI_TAIL) sbd::last_arriver_tail(p.y, p.ldy, p.m, p.n, p.tail);
 }
 
 // The GEMV for rows a half-warp covers whole (ks = 1: K <= 16 * GPL * 32),
@@ -398,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
   // x is the previous kernel's output: wait for it (weights are already streaming)
   sbd::griddep_wait();
   XG xg[M][GPL];
-  load_x_groups<M, GPL, XG>(p, gidx, gval, xg);
+  load_x_groups<M, GPL, XG, EPI == EPI_SRQ>(p, gidx, gval, xg);
 
   float best_v[M];
   long long best_i[M];
@@ -449,8 +456,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
         for (int m = 0; m < M; ++m) {
           if (m >= p.m) continue;
           float v = acc[m];
-          if (EPI == EPI_STORE) {
-            p.y[static_cast<size_t>(m) * p.ldy + row] = srq_out(p, row, v);
+          if (EPI != EPI_ARGMAX) {
+            p.y[static_cast<size_t>(m) * p.ldy + row] = EPI == EPI_SRQ ? srq_out(p, row, v) : v;
           } else {
             if (p.logits) p.logits[static_cast<size_t>(m) * p.n + row] = v;
             if (v != v) v = -INFINITY;
@@ -503,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
         }
     }
   }
-  if (EPI == EPI_STORE && p.tail.counter) sbd::last_arriver_tail(p.y, p.ldy, p.m, p.n, p.tail);
+  if constexpr (EPI == EPI_TAIL) sbd::last_arriver_tail(p.y, p.ldy, p.m, p.n, p.tail);
 }
 
 __global__ void keys_to_tokens_kernel(const unsigned long long* keys, int32_t* tokens, int m) {
@@ -623,6 +630,15 @@ int launch_m(const GemvParams& p, const Plan& pl, bool sf16, int sms, cudaStream
   }
 }
 
+template <int EPI>
+int launch_bits(int bits, int mt, const GemvParams& q, const Plan& pl, bool sf16, int sms, cudaStream_t s) {
+  if (bits == 2)
+    return mt == 1 ? launch_m<1, EPI, 2>(q, pl, sf16, sms, s)
+                   : mt == 2 ? launch_m<2, EPI, 2>(q, pl, sf16, sms, s) : launch_m<4, EPI, 2>(q, pl, sf16, sms, s);
+  return mt == 1 ? launch_m<1, EPI, 4>(q, pl, sf16, sms, s)
+                 : mt == 2 ? launch_m<2, EPI, 4>(q, pl, sf16, sms, s) : launch_m<4, EPI, 4>(q, pl, sf16, sms, s);
+}
+
 int run(GemvParams p, int epi, bool xf32, bool sf16, cudaStream_t s) {
   const int sms = sb::num_sms();
   const int x_elt = xf32 ? 4 : 2;
@@ -648,7 +664,7 @@ int run(GemvParams p, int epi, bool xf32, bool sf16, cudaStream_t s) {
     GemvParams q = p;
     q.m = mt;
     q.x = static_cast<const char*>(p.x) + done * x_row;
-    if (epi == EPI_STORE) {
+    if (epi != EPI_ARGMAX) {
       q.y = p.y + static_cast<size_t>(done) * p.ldy;
       if (p.tail.counter) {  // the tail of this launch covers its own rows
         const size_t o = static_cast<size_t>(done) * p.n;
@@ -673,24 +689,11 @@ int run(GemvParams p, int epi, bool xf32, bool sf16, cudaStream_t s) {
     q.scale_bulk = (srow * pl.rs) % 16 == 0 && (srow * last) % 16 == 0 &&
                    srow * pl.rs <= static_cast<size_t>(kStageS) && sb::aligned(p.scales, 16);
     int rc;
-    if (p.bits == 2) {
-      if (epi == EPI_STORE) {
-        rc = mt == 1 ? launch_m<1, EPI_STORE, 2>(q, pl, sf16, sms, s)
-                     : mt == 2 ? launch_m<2, EPI_STORE, 2>(q, pl, sf16, sms, s)
-                               : launch_m<4, EPI_STORE, 2>(q, pl, sf16, sms, s);
-      } else {
-        rc = mt == 1 ? launch_m<1, EPI_ARGMAX, 2>(q, pl, sf16, sms, s)
-                     : mt == 2 ? launch_m<2, EPI_ARGMAX, 2>(q, pl, sf16, sms, s)
-                               : launch_m<4, EPI_ARGMAX, 2>(q, pl, sf16, sms, s);
-      }
-    } else if (epi == EPI_STORE) {
-      rc = mt == 1 ? launch_m<1, EPI_STORE, 4>(q, pl, sf16, sms, s)
-                   : mt == 2 ? launch_m<2, EPI_STORE, 4>(q, pl, sf16, sms, s)
-                             : launch_m<4, EPI_STORE, 4>(q, pl, sf16, sms, s);
-    } else {
-      rc = mt == 1 ? launch_m<1, EPI_ARGMAX, 4>(q, pl, sf16, sms, s)
-                   : mt == 2 ? launch_m<2, EPI_ARGMAX, 4>(q, pl, sf16, sms, s)
-                             : launch_m<4, EPI_ARGMAX, 4>(q, pl, sf16, sms, s);
+    switch (epi) {
+      case EPI_STORE: rc = launch_bits<EPI_STORE>(p.bits, mt, q, pl, sf16, sms, s); break;
+      case EPI_ARGMAX: rc = launch_bits<EPI_ARGMAX>(p.bits, mt, q, pl, sf16, sms, s); break;
+      case EPI_SRQ: rc = launch_bits<EPI_SRQ>(p.bits, mt, q, pl, sf16, sms, s); break;
+      default: rc = launch_bits<EPI_TAIL>(p.bits, mt, q, pl, sf16, sms, s); break;
     }
     if (rc != SB_OK) return rc;
     done += mt;
@@ -749,7 +752,9 @@ static int gemv_impl(const char* fn, int bits, const void* w, const void* scales
   p.srq_in = srq_in;
   p.srq_out = srq_out_s;
   p.srq_out_rows = srq_out_rows;
-  return run(p, EPI_STORE, x_dtype == SB_F32, scale_dtype == SB_SCALE_F16, static_cast<cudaStream_t>(stream));
+  const bool srq = srq_in != 0.f || srq_out_s != 0.f || srq_out_rows;
+  return run(p, srq ? EPI_SRQ : EPI_STORE, x_dtype == SB_F32, scale_dtype == SB_SCALE_F16,
+             static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int sb_gemv_q4(const void* w, const void* scales, int scale_dtype, int group, const void* x,
@@ -788,7 +793,7 @@ extern "C" int sb_gemv_norm_add(const void* w, int bits, const void* scales, int
   p.ldy = n;
   p.bits = bits;
   p.tail = sbd::NormTail{hidden, w_add, w_next, h_out, static_cast<__half*>(h16_out), counter, 1.f, eps};
-  return run(p, EPI_STORE, x_dtype == SB_F32, scale_dtype == SB_SCALE_F16, static_cast<cudaStream_t>(stream));
+  return run(p, EPI_TAIL, x_dtype == SB_F32, scale_dtype == SB_SCALE_F16, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int sb_gemv_srq(const void* w, int bits, const void* scales, int scale_dtype, int group, const void* x,

@@ -138,13 +138,16 @@ int sb_keys_to_tokens(const uint64_t* keys, int32_t* tokens, int m, void* stream
  * sb_peer_buffer_create (zeroed; ipc_handle receives a 64-byte CUDA IPC
  * handle), shares the handle, and maps the other ranks' mailboxes with
  * sb_peer_buffer_open.  sb_lmhead_argmax_peer then runs this rank's shard
- * GEMV (rows row_offset .. row_offset + v) with every CTA's keys going to
- * every rank's mailbox by system-scope atomic MAX over NVLink, and one small
- * kernel that counts this rank in at every mailbox, waits (bounded; timeout
- * -> SB_ERR_TIMEOUT in sb_device_status) for all `world` ranks, and writes the
- * combined keys / tokens (m <= 64 rows).  peer_mailboxes: device array of the
- * `world` mailbox addresses as this process maps them (its own at `rank`).
- * Every rank must make the same sequence of calls.
+ * GEMV (rows row_offset .. row_offset + v, v >= 1) as one launch: its CTAs fold
+ * their argmax keys into this rank's mailbox, and the last CTA to finish sends
+ * each row's key to every rank's mailbox (system-scope MAX over NVLink), counts
+ * this rank in at every mailbox, waits (bounded by sb_peer_set_wait_limit_ns;
+ * timeout -> SB_ERR_TIMEOUT in sb_device_status and keys of 0) for all `world`
+ * ranks, and writes the combined keys / tokens (m <= 64 rows).  A timed-out
+ * exchange leaves the mailboxes unusable: create them again.
+ * peer_mailboxes: device array of the `world` mailbox addresses as this
+ * process maps them (its own at `rank`).  Every rank must make the same
+ * sequence of calls.
  */
 size_t sb_peer_mailbox_size(void);
 int sb_peer_buffer_create(size_t bytes, void** dev_ptr, void* ipc_handle);

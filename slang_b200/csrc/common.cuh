@@ -265,13 +265,17 @@ __device__ __forceinline__ unsigned long long make_key(float v, long long idx) {
 }
 
 // ---- peer mailbox of the vocabulary-sharded lm_head (one per rank, mapped by
-// every rank): a step counter, two per-parity arrival counts and two
-// per-parity slot arrays of argmax keys.
+// every rank): a step counter, this rank's CTA count for the running launch,
+// two per-parity arrival counts, two per-parity slot arrays of combined argmax
+// keys (written by every rank) and this rank's own keys (its CTAs fold theirs
+// in before the last one sends them out).
 constexpr int kMailEpoch = 0;
+constexpr int kMailCtas = 4;       // uint32_t
 constexpr int kMailCount = 64;     // uint32_t[2]
 constexpr int kMailKeys = 128;     // unsigned long long[2][kMailMaxRows]
 constexpr int kMailMaxRows = 64;
-constexpr int kMailBytes = kMailKeys + 2 * kMailMaxRows * 8;
+constexpr int kMailLocal = kMailKeys + 2 * kMailMaxRows * 8;  // unsigned long long[kMailMaxRows]
+constexpr int kMailBytes = kMailLocal + kMailMaxRows * 8;
 
 // ---- thread-block clusters and distributed shared memory
 __device__ __forceinline__ uint32_t cluster_ctarank() {

@@ -68,8 +68,11 @@ struct GemvParams {
   // vocabulary shards over peer memory: each CTA's key goes to every rank's
   // mailbox (atomic MAX through NVLink) instead of `keys`
   const unsigned long long* peer_mailboxes;  // device array of `world` mailbox addresses
-  const uint32_t* peer_epoch;                // this rank's step counter (its parity picks the key slots)
+  uint8_t* peer_own;                         // this rank's mailbox
+  int32_t* tokens;                           // peer exchange: the combined tokens
   int world, peer_row0;                      // peer_row0: first batch row of this launch
+  int peer_rows, peer_finish;                // rows of the step; 1 in the launch that holds the last rows
+  uint64_t peer_wait_ns;                     // bound of the wait for the other ranks
   // static range quantisation (SRQ) of the linear, gemma4_150/reference.py:96-101:
   // y = srq(W @ srq(x, srq_in), out) with out = srq_out_rows[row] when given,
   // else srq_out; a scale of 0 skips that srq
@@ -150,23 +153,99 @@ __device__ __forceinline__ void load_x_groups(const GemvParams& p, const int (&g
 // Combine the per-warp argmax keys (sm.best[warp][m], warps 0..7) and publish
 // one key per batch row: atomic MAX into p.keys, or into every rank's mailbox.
 // Called by the 256 consumer threads after a barrier over them.
+// The vocabulary-sharded lm_head's exchange, at the end of this rank's shard
+// GEMV (every thread of every CTA calls it).  Each CTA folds its keys into this
+// rank's own mailbox (device-scope atomic MAX) and counts itself in; the CTA
+// that completes the count re-arms it and, in the launch holding the step's
+// last rows, exchanges every row's key with the other ranks:
+//   1. clear this mailbox's other-parity slots and count (no rank writes them
+//      before every rank has counted in for this step);
+//   2. fold this rank's keys into every rank's parity-q slots (system-scope
+//      reduction over NVLink), then a system fence;
+//   3. count in at every rank (system-scope add);
+//   4. wait, bounded, until all `world` ranks have counted in here;
+//   5. read the combined keys, write keys and tokens, clear this rank's own
+//      keys and advance the step counter.
+// Slots alternate by step parity q: a rank writes step e + 1's keys only after
+// every rank has counted in for step e, which each rank does only after
+// clearing those slots, so two slot sets suffice and no host sync is needed.
 template <int M>
-__device__ __forceinline__ void publish_keys(const GemvParams& p, GemvSmem& sm, int tid) {
+__device__ __forceinline__ void peer_publish(const GemvParams& p, GemvSmem& sm, int tid) {
+  uint8_t* own = p.peer_own;
+  unsigned long long* local = reinterpret_cast<unsigned long long*>(own + sbd::kMailLocal);
   if (tid < M && tid < p.m) {
     unsigned long long key = 0;
     for (int wi = 0; wi < kConsumers / 32; ++wi) key = sm.best[wi][tid] > key ? sm.best[wi][tid] : key;
-    if (key) {
-      if (p.peer_mailboxes) {
-        const uint32_t q = *p.peer_epoch & 1u;
-        for (int pe = 0; pe < p.world; ++pe)
-          atomicMax_system(reinterpret_cast<unsigned long long*>(p.peer_mailboxes[pe] + sbd::kMailKeys) +
-                               q * sbd::kMailMaxRows + p.peer_row0 + tid,
-                           key);
-        __threadfence_system();  // performed at every peer before this CTA exits
-      } else {
-        atomicMax(p.keys + tid, key);
-      }
+    if (key) atomicMax(local + p.peer_row0 + tid, key);
+  }
+  __shared__ unsigned int s_last;
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(reinterpret_cast<unsigned int*>(own + sbd::kMailCtas), 1u) == gridDim.x - 1 ? 1u : 0u;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  if (tid == 0) *reinterpret_cast<volatile unsigned int*>(own + sbd::kMailCtas) = 0u;  // re-arm for the next launch
+  if (!p.peer_finish || tid >= 32) return;
+  __threadfence();
+  const int lane = tid, rows = p.peer_rows;
+  uint32_t* epoch = reinterpret_cast<uint32_t*>(own + sbd::kMailEpoch);
+  uint32_t* count = reinterpret_cast<uint32_t*>(own + sbd::kMailCount);
+  unsigned long long* slots = reinterpret_cast<unsigned long long*>(own + sbd::kMailKeys);
+  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(epoch), q = e & 1u;
+  for (int i = lane; i < rows; i += 32) slots[(q ^ 1u) * sbd::kMailMaxRows + i] = 0ull;
+  if (lane == 0) count[q ^ 1u] = 0u;
+  unsigned long long mine[2];
+  for (int j = 0; j < 2; ++j) mine[j] = lane + 32 * j < rows ? __ldcg(local + lane + 32 * j) : 0ull;
+  __threadfence_system();
+  for (int pe = 0; pe < p.world; ++pe) {
+    unsigned long long* dst =
+        reinterpret_cast<unsigned long long*>(p.peer_mailboxes[pe] + sbd::kMailKeys) + q * sbd::kMailMaxRows;
+    for (int j = 0; j < 2; ++j)
+      if (lane + 32 * j < rows && mine[j])
+        asm volatile("red.relaxed.sys.global.max.u64 [%0], %1;" ::"l"(dst + lane + 32 * j), "l"(mine[j]) : "memory");
+  }
+  __threadfence_system();
+  __syncwarp();
+  if (lane < p.world)
+    asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(
+                     reinterpret_cast<uint32_t*>(p.peer_mailboxes[lane] + sbd::kMailCount) + q)
+                 : "memory");
+  int done = 0;
+  if (lane == 0) {
+    const uint64_t t0 = sbd::global_ns();
+    while (!done) {
+      uint32_t c;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(c) : "l"(count + q) : "memory");
+      if (c >= static_cast<uint32_t>(p.world)) done = 1;
+      else if (sbd::global_ns() - t0 > p.peer_wait_ns) break;
     }
+    if (!done && p.err) atomicExch(p.err, SB_ERR_TIMEOUT);
+  }
+  done = __shfl_sync(0xFFFFFFFFu, done, 0);
+  for (int i = lane; i < rows; i += 32) {
+    unsigned long long k;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(k) : "l"(slots + q * sbd::kMailMaxRows + i) : "memory");
+    if (!done) k = 0ull;
+    if (p.keys) p.keys[i] = k;
+    if (p.tokens) p.tokens[i] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
+    local[i] = 0ull;
+  }
+  __syncwarp();
+  if (lane == 0) *epoch = e + 1u;
+}
+
+template <int M>
+__device__ __forceinline__ void publish_keys(const GemvParams& p, GemvSmem& sm, int tid) {
+  if (p.peer_mailboxes) {
+    peer_publish<M>(p, sm, tid);
+    return;
+  }
+  if (tid < M && tid < p.m) {
+    unsigned long long key = 0;
+    for (int wi = 0; wi < kConsumers / 32; ++wi) key = sm.best[wi][tid] > key ? sm.best[wi][tid] : key;
+    if (key) atomicMax(p.keys + tid, key);
   }
 }
 
@@ -674,8 +753,9 @@ int run(GemvParams p, int epi, bool xf32, bool sf16, cudaStream_t s) {
       }
     }
     else {
-      if (p.keys) q.keys = p.keys + done;
+      if (p.keys && !p.peer_mailboxes) q.keys = p.keys + done;
       q.peer_row0 = p.peer_row0 + done;
+      q.peer_finish = done + mt == m_total ? 1 : 0;
       if (p.logits) q.logits = p.logits + static_cast<size_t>(done) * p.n;
     }
     q.ks = pl.ks;
@@ -858,51 +938,7 @@ extern "C" int sb_lmhead_argmax_q2(const void* emb, const void* scales, int scal
 
 namespace {
 
-// The exchange step of the vocabulary-sharded lm_head over peer memory (one
-// CTA per rank, after that rank's shard GEMV has added its keys to every
-// mailbox): clear the other parity's slots and count, tell every rank this
-// rank is done (system-scope atomic add after a system fence), wait (bounded)
-// until all `world` ranks are done, read the combined keys, advance the step.
-// Slots alternate by step parity: a rank writes step e + 1's keys only after
-// every rank has passed its step-e count, i.e. after this rank cleared them.
-__global__ void peer_combine_kernel(uint8_t* own, const unsigned long long* peers, int world, int m,
-                                    unsigned long long* keys_out, int32_t* tokens, int* err, uint64_t wait_ns) {
-  __shared__ int ok;
-  uint32_t* epoch = reinterpret_cast<uint32_t*>(own + sbd::kMailEpoch);
-  uint32_t* count = reinterpret_cast<uint32_t*>(own + sbd::kMailCount);
-  unsigned long long* slots = reinterpret_cast<unsigned long long*>(own + sbd::kMailKeys);
-  const uint32_t e = *epoch, q = e & 1u;
-  for (int i = threadIdx.x; i < m; i += blockDim.x) slots[(q ^ 1u) * sbd::kMailMaxRows + i] = 0ull;
-  if (threadIdx.x == 0) count[q ^ 1u] = 0u;
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int pe = 0; pe < world; ++pe) atomicAdd_system(reinterpret_cast<uint32_t*>(peers[pe] + sbd::kMailCount) + q, 1u);
-    // every rank's keys have landed once every rank has counted in
-    const uint64_t t0 = sbd::global_ns();
-    int done = 0;
-    while (!done) {
-      uint32_t c;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(c) : "l"(count + q) : "memory");
-      if (c >= static_cast<uint32_t>(world)) done = 1;
-      else if (sbd::global_ns() - t0 > wait_ns) break;
-    }
-    ok = done;
-    if (!done && err) atomicExch(err, SB_ERR_TIMEOUT);
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < m; i += blockDim.x) {
-    unsigned long long k;
-    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(k) : "l"(slots + q * sbd::kMailMaxRows + i) : "memory");
-    if (!ok) k = 0ull;
-    if (keys_out) keys_out[i] = k;
-    if (tokens) tokens[i] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) *epoch = e + 1u;
-}
-
-// How long a rank waits in peer_combine_kernel for the others to count in.
+// How long the sharded lm_head's exchange waits for the other ranks to count in.
 std::atomic<uint64_t> g_peer_wait_ns{sbd::kWaitLimitNs};
 
 }  // namespace
@@ -956,31 +992,27 @@ extern "C" int sb_lmhead_argmax_peer(const void* emb, const void* scales, int sc
   int rc = check_common("sb_lmhead_argmax_peer", emb, scales, scale_dtype, group, h, h_dtype, m, v, k);
   if (rc != SB_OK) return rc;
   SB_CHECK_ARG(m <= sbd::kMailMaxRows, "sb_lmhead_argmax_peer: m=%d > %d", m, sbd::kMailMaxRows);
-  SB_CHECK_ARG(world >= 1 && peer_mailboxes && own_mailbox, "sb_lmhead_argmax_peer: bad peer arguments");
+  SB_CHECK_ARG(v >= 1, "sb_lmhead_argmax_peer: every rank needs a non-empty shard (v=%d)", v);
+  SB_CHECK_ARG(world >= 1 && world <= 32 && peer_mailboxes && own_mailbox, "sb_lmhead_argmax_peer: bad peer arguments");
   SB_CHECK_ARG(row_offset >= 0 && row_offset + v <= 0xFFFFFFFFLL, "sb_lmhead_argmax_peer: row indices must fit in 32 bits");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (v > 0) {
-    GemvParams p{};
-    p.w = static_cast<const uint8_t*>(emb);
-    p.scales = scales;
-    p.x = h;
-    p.m = m;
-    p.n = v;
-    p.k = k;
-    p.group = group;
-    p.row_offset = row_offset;
-    p.bits = 4;
-    p.peer_mailboxes = reinterpret_cast<const unsigned long long*>(peer_mailboxes);
-    p.peer_epoch = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(own_mailbox) + sbd::kMailEpoch);
-    p.world = world;
-    rc = run(p, EPI_ARGMAX, h_dtype == SB_F32, scale_dtype == SB_SCALE_F16, s);
-    if (rc != SB_OK) return rc;
-  }
-  peer_combine_kernel<<<1, 128, 0, s>>>(static_cast<uint8_t*>(own_mailbox),
-                                        reinterpret_cast<const unsigned long long*>(peer_mailboxes), world, m,
-                                        reinterpret_cast<unsigned long long*>(keys), tokens, sb::device_error_word(),
-                                        g_peer_wait_ns.load());
-  return sb::launch_status("peer_combine_kernel");
+  GemvParams p{};
+  p.w = static_cast<const uint8_t*>(emb);
+  p.scales = scales;
+  p.x = h;
+  p.m = m;
+  p.n = v;
+  p.k = k;
+  p.group = group;
+  p.row_offset = row_offset;
+  p.bits = 4;
+  p.keys = reinterpret_cast<unsigned long long*>(keys);
+  p.tokens = tokens;
+  p.peer_mailboxes = reinterpret_cast<const unsigned long long*>(peer_mailboxes);
+  p.peer_own = static_cast<uint8_t*>(own_mailbox);
+  p.world = world;
+  p.peer_rows = m;
+  p.peer_wait_ns = g_peer_wait_ns.load();
+  return run(p, EPI_ARGMAX, h_dtype == SB_F32, scale_dtype == SB_SCALE_F16, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int sb_keys_to_tokens(const uint64_t* keys, int32_t* tokens, int m, void* stream) {

@@ -63,12 +63,13 @@ class PeerLMHead(ShardedLMHead):
     NVLink instead of an NCCL call.
 
     Every rank owns a small mailbox (``sb_peer_buffer_create``) that every
-    other rank maps (CUDA IPC).  The shard GEMV's CTAs put their argmax keys
-    into every rank's mailbox with system-scope atomic MAX over NVLink, then
-    one small kernel per rank counts in at every mailbox and waits (bounded)
-    until all ranks have, and reads the combined keys -- two launches, no host
-    synchronisation, capturable in a CUDA graph.  The exchange is a function of
-    the call sequence: every rank must call once per step.
+    other rank maps (CUDA IPC).  The shard GEMV's CTAs fold their argmax keys
+    into this rank's mailbox; the last CTA to finish sends each row's key to
+    every rank's mailbox with a system-scope MAX over NVLink, counts in at
+    every mailbox, waits (bounded) until all ranks have, and reads the combined
+    keys -- one launch, no host synchronisation, capturable in a CUDA graph.
+    The exchange is a function of the call sequence: every rank must call once
+    per step.
     """
 
     def __init__(self, emb: torch.Tensor, scales: torch.Tensor, rank: int = 0, world: int = 1, group=None,

@@ -65,7 +65,7 @@ def parse():
     ap.add_argument("--kernel", default="",
                     choices=["", "gemm_q4", "gemm_q4_geglu", "gemm_f16", "gemv", "lmhead", "attn", "attn_decode", "gemv_q8",
                              "gemv_bf16", "ple_block", "prefill",
-                             "decode", "decode_fused", "decode_batch", "decode_trace"],
+                             "decode", "decode_fused", "decode_batch", "decode_trace", "gemm_trace"],
                     help="run one kernel --iters times on a single shape and exit (for ncu captures)")
     ap.add_argument("--shape", default="6144,1536", help="N,K of the weight for --kernel")
     ap.add_argument("--m", type=int, default=1024, help="rows of the activation for --kernel")
@@ -180,12 +180,121 @@ def run_decode_trace(args):
                                              for m, v in stats[ph].items()))
 
 
+def run_gemm_trace(args):
+    """Where the time of one fused int4 GEMM launch goes, from the pair kernel's
+    own %globaltimer stamps (sb_gemm_q4_trace): the four matrices of a layer at
+    M = --m tokens, each as two back-to-back launches replayed from one CUDA
+    graph (the form the prefill runs them in).  Prints, per matrix, the span of
+    the second launch, its gap to the first, the CTAs per SM, and the mean (max)
+    over CTAs of each phase: set-up, scales, first packed stage, first MMA,
+    MMA loop, accumulator drain, epilogue, split reduction and teardown."""
+    import numpy as np
+    import torch
+
+    from slang_b200 import _lib
+    from slang_b200 import kernels as kern
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    M = args.m
+    slots = 16
+    cap = 8192  # CTAs per traced launch
+
+    def graph_us(A, w, sc, C, ws, geglu, reps=20):
+        st = torch.cuda.Stream()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            for _ in range(reps):
+                kern.gemm_q4(A, w, sc, C, workspace=ws, geglu=geglu)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    # one wave of tiles (a weight-row pair per CTA pair, 256 tokens) over K:
+    # the slope is the k-block rate of the MMA loop, the intercept the fixed
+    # cost of a tile (set-up, pipeline fill, epilogue, teardown, launch gap)
+    pairs = torch.cuda.get_device_properties(dev).multi_processor_count // 2
+    pts = []
+    for k in (512, 1024, 1536, 3072):
+        n = pairs * 256
+        A = (torch.randn((256, k), device=dev, generator=g) * 0.5).half()
+        w = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g)
+        sc = (torch.rand((n, k // 32), device=dev, generator=g) * 0.01 + 0.001).half()
+        C = torch.empty((256, n), dtype=torch.float16, device=dev)
+        for _ in range(3):
+            kern.gemm_q4(A, w, sc, C)
+        pts.append((k // 64, graph_us(A, w, sc, C, None, False)))
+    kb = np.array([p[0] for p in pts], dtype=np.float64)
+    us = np.array([p[1] for p in pts])
+    slope, icpt = np.polyfit(kb, us, 1)
+    print(f"one wave ({pairs} CTA pairs x one 256 x 256 tile), us per launch in a CUDA graph: "
+          + ", ".join(f"K={int(k) * 64}: {u:.2f}" for k, u in zip(kb, us))
+          + f" -> {slope:.3f} us per 64-deep k-block + {icpt:.2f} us per tile")
+    lib = _lib.load()
+    for name, n, k, geglu in (("q|k|v", 2560, 1536, False), ("o", 1536, 2048, False),
+                              ("gate|up+GEGLU", 12288, 1536, True), ("down", 1536, 6144, False)):
+        A = (torch.randn((M, k), device=dev, generator=g) * 0.5).half()
+        w = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g)
+        sc = (torch.rand((n, k // 32), device=dev, generator=g) * 0.01 + 0.001).half()
+        C = torch.empty((M, n // 2 if geglu else n), dtype=torch.float16, device=dev)
+        ws = kern._workspace(dev, kern.gemm_q4_workspace_size(M, n, k))
+        for _ in range(3):
+            kern.gemm_q4(A, w, sc, C, workspace=ws, geglu=geglu)
+        bufs = [torch.zeros(cap * slots, dtype=torch.int64, device=dev) for _ in range(2)]
+        torch.cuda.synchronize()
+        st = torch.cuda.Stream()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            for b in bufs:
+                _lib.call("sb_gemm_q4_trace", b.data_ptr(), b.numel() * 8)
+                kern.gemm_q4(A, w, sc, C, workspace=ws, geglu=geglu)
+        _lib.call("sb_gemm_q4_trace", None, 0)
+        graph.replay()
+        for b in bufs:
+            b.zero_()
+        torch.cuda.synchronize()
+        graph.replay()
+        torch.cuda.synchronize()
+        tr = [b.view(cap, slots).cpu().numpy() for b in bufs]
+        live = [t[t[:, 1] > 0] for t in tr]
+        t0 = live[0][:, 1].min()
+        x = live[1].astype(np.int64)
+        span = x[:, 11].max() - x[:, 1].min()
+        gap = x[:, 1].min() - live[0][:, 11].max()
+        per_sm = np.bincount(x[:, 0].astype(np.int64)).max()
+        lead = x[:, 6] > 0
+
+        def ph(a, b, mask=None):
+            d = (x[:, b] - x[:, a]) if mask is None else (x[mask, b] - x[mask, a])
+            return f"{d.mean() / 1e3:.2f} ({d.max() / 1e3:.2f})"
+
+        red = x[:, 10] > 0
+        print(f"{name:14s} [{M}x{n}x{k}] {len(x)} CTAs, <= {per_sm} per SM: launch span {span / 1e3:.2f} us, "
+              f"first entry {gap / 1e3:+.2f} us after the previous launch's last exit "
+              f"(previous span {(live[0][:, 11].max() - t0) / 1e3:.2f} us)")
+        print(f"    setup {ph(1, 2)}  act-go {ph(1, 3)}  scales {ph(2, 4)}  pack0 {ph(2, 5)}  "
+              f"mma0 {ph(1, 6, lead)}  mma-loop {ph(6, 7, lead)}  accum {ph(7, 8, lead)}  epilogue {ph(8, 9)}  "
+              + (f"reduce {ph(9, 10, red)}  teardown {ph(10, 11, red)}" if red.any() else f"teardown {ph(9, 11)}"))
+        ent = np.sort(x[:, 1] - x[:, 1].min())
+        ex = np.sort(x[:, 11] - x[:, 1].min())
+        print(f"    CTA entries (us): first {ent[0] / 1e3:.2f}, median {np.median(ent) / 1e3:.2f}, last {ent[-1] / 1e3:.2f};"
+              f"  exits: first {ex[0] / 1e3:.2f}, median {np.median(ex) / 1e3:.2f}, last {ex[-1] / 1e3:.2f};"
+              f"  {graph_us(A, w, sc, C, ws, geglu):.2f} us per launch in a CUDA graph of 20")
+
+
 def run_kernel_case(args):
     """One kernel on one shape, --iters launches after one warm-up (ncu target)."""
     import torch
 
     if args.kernel == "decode_trace":
         return run_decode_trace(args)
+    if args.kernel == "gemm_trace":
+        return run_gemm_trace(args)
     if args.kernel in ("prefill", "decode", "decode_fused", "decode_batch"):
         return run_model_case(args)
     from slang_b200 import kernels as kern

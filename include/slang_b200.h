@@ -225,6 +225,9 @@ int sb_gemm_q4_geglu(const void* a, const void* w, const void* scales, int scale
                      void* out, int m, int n, int k, float alpha, int lda, int ldo, void* workspace,
                      size_t workspace_bytes, void* stream);
 size_t sb_gemm_q4_workspace_size(int m, int n, int k);
+/* Kernels one sb_gemm_q4 call launches for this shape (group-32 f16 scales,
+ * workspace as sized above): 1, or 2 when a split-K finalize follows. */
+int sb_gemm_q4_kernels(int m, int n, int k);
 
 /*
  * sb_gemm_q4 / sb_gemm_q4_geglu over 2-bit codes (the checkpoint's 2-bit MLP
@@ -255,6 +258,17 @@ int sb_gemm_q2_geglu(const void* a, const void* w, const void* scales, int scale
  */
 int sb_gemm_q4_argmax(const void* a, const void* w, const void* scales, int scale_dtype, int group, int m, int n,
                       int k, float alpha, int lda, int64_t row_offset, uint64_t* keys, int32_t* tokens, void* stream);
+
+/*
+ * Profiling hook of the fused int4 / 2-bit GEMM's CTA-pair kernel: while `buf`
+ * is set (NULL turns it off), every launch whose grid fits in `bytes` writes
+ * 16 u64 per CTA at buf[16 * b] (b = the CTA's linear grid index): [0] its SM,
+ * then %globaltimer stamps -- [1] entry, [2] set-up done, [3] activations
+ * readable, [4] scales loaded, [5] first packed stage, [6] first MMA, [7] last
+ * MMA issued, [8] accumulator final, [9] epilogue issued, [10] split-K
+ * reduction done, [11] exit.  For measurement only; buf must stay valid.
+ */
+int sb_gemm_q4_trace(uint64_t* buf, size_t bytes);
 
 /*
  * sb_gemm_q4 without a caller workspace; it allocates nothing.  No counterpart

@@ -98,7 +98,32 @@ struct GemmParams {
   int bits;            // packed-weight code width: 4 (two per byte) or 2 (four per byte)
   float alpha;
   long long plane;     // f16 kernel, f32 C: elements between the output planes of K splits (blockIdx.z)
+  unsigned long long* trace;  // pair kernel, profiling only: kTraceSlots %globaltimer stamps per CTA, or null
 };
+
+// Profiling stamps of the pair kernel (sb_gemm_q4_trace): slot i of CTA b is
+// trace[b * kTraceSlots + i], b the CTA's linear index in the grid.
+enum {
+  TS_SMID = 0,       // the SM the CTA ran on
+  TS_ENTRY = 1,      // first instruction
+  TS_SETUP = 2,      // barriers initialised, TMEM allocated (after the cluster barrier)
+  TS_ACT_GO = 3,     // activation producer: the previous kernel's output may be read
+  TS_SCALES = 4,     // dequant warps: the tile's scales are in shared memory
+  TS_PACK0 = 5,      // dequant warp 2: first packed stage landed
+  TS_MMA0 = 6,       // MMA issuer: first k-block ready
+  TS_MMA_END = 7,    // MMA issuer: last MMA issued
+  TS_ACCUM = 8,      // epilogue warp 2: accumulator final
+  TS_EPI_END = 9,    // epilogue warp 2: its stores (or partial stash) issued
+  TS_REDUCED = 10,   // epilogue warp 2: cluster split reduction done
+  TS_EXIT = 11,      // TMEM released
+  kTraceSlots = 16
+};
+__device__ __forceinline__ void gemm_stamp(const GemmParams& p, int slot) {
+  if (p.trace) {
+    const size_t b = blockIdx.x + static_cast<size_t>(gridDim.x) * (blockIdx.y + static_cast<size_t>(gridDim.y) * blockIdx.z);
+    p.trace[b * kTraceSlots + slot] = sbd::global_ns();
+  }
+}
 
 struct Bars {
   uint64_t full[8];
@@ -765,6 +790,13 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
   volatile int* abort = &bars->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0 && p.trace) {
+    gemm_stamp(p, TS_ENTRY);
+    uint32_t sm;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+    const size_t b = blockIdx.x + static_cast<size_t>(gridDim.x) * (blockIdx.y + static_cast<size_t>(gridDim.y) * blockIdx.z);
+    p.trace[b * kTraceSlots + TS_SMID] = sm;
+  }
   // cluster (2, 1, csplit): rank = pair position + 2 * split
   const int rank = static_cast<int>(sbd::cluster_ctarank());
   const int lead_rank = rank & ~1;
@@ -805,6 +837,7 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
   sbd::cluster_sync_all();
   sbd::tc_fence_after();
   const uint32_t tmem = bars->tmem_slot;
+  if (threadIdx.x == 0) gemm_stamp(p, TS_SETUP);
 
   // the next kernel in the stream may start its prologue; this kernel's own
   // reads of the previous kernel's output (the activations) wait below
@@ -814,6 +847,7 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
     // ------------------------------------------------------------ activation TMA producer (both CTAs)
     if (lane == 0) {
       sbd::griddep_wait();
+      gemm_stamp(p, TS_ACT_GO);
       int issued = 0;
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % S;
@@ -863,6 +897,7 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
       const uint64_t bdesc0 = sbd::umma_desc(sbd::smem_u32(smem), 16, 1024, sbd::kLayoutSwizzle128B);
       const uint32_t a0 = tmem + 256;
       bool ok = nkb > 0 && sbd::mbar_wait_cluster(&bars->ready[0], 0, abort, p.err);
+      gemm_stamp(p, TS_MMA0);
       for (int base = 0; ok && base < nkb; base += S) {
         const uint32_t ph = (base / S) & 1;
 #pragma unroll
@@ -886,6 +921,7 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
           }
         }
       }
+      gemm_stamp(p, TS_MMA_END);
       sbd::umma_commit_pair(&bars->accum, pair_mask);
     }
   } else {
@@ -899,6 +935,7 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
     uint8_t* sct = smem + P_OFF_SCALE;
     load_scale_tile(p, sct, w0, g_lo, gs, dt, Q_DQ_WARPS * 32);
     sbd::named_bar_sync(1, Q_DQ_WARPS * 32);
+    if (dt == 0) gemm_stamp(p, TS_SCALES);
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t ready_lead = sbd::mapa_shared(sbd::smem_u32(&bars->ready[0]), lead_rank);
     const int kstep = Q_DQ_GROUPS * BK;
@@ -908,6 +945,7 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
       const int s = kb % S, slot = s;
       if (gstep == 0) gi = ((kb0 + kb) * BK + khalf * 32) / p.group - g_lo;
       bool ok = sbd::mbar_wait(&bars->pfull[s], (kb / S) & 1, abort, p.err);
+      if (dt == 0 && kb == 0) gemm_stamp(p, TS_PACK0);
       if (ok) ok = sbd::mbar_wait_cluster(&bars->empty[s], ((kb / S) & 1) ^ 1, abort, p.err);
       if (!__all_sync(0xFFFFFFFFu, ok)) break;
       sbd::tc_fence_after();
@@ -928,11 +966,13 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
     }
     // ------------------------------------------------------------ epilogue (this CTA's 128 rows)
     const bool ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait_cluster(&bars->accum, 0, abort, p.err));
+    if (dt == 0) gemm_stamp(p, TS_ACCUM);
     if (ok) {
       sbd::tc_fence_after();
       if (p.csplit > 1) stash_partial(smem, lane_addr, dw, r, NT);
       else epilogue_direct(p, lane_addr, dw, r, lane, w0, t0, blockIdx.z, NT);
     }
+    if (dt == 0) gemm_stamp(p, TS_EPI_END);
   }
 
   if (p.csplit > 1) {
@@ -941,6 +981,7 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
     if (warp >= 2 && warp < Q_WARPS)
       reduce_splits(p, smem, warp - 2, lane, w0, t0, rank >> 1, p.csplit, rank & 1, 2, NT);
     sbd::cluster_sync_all();
+    if (threadIdx.x == 64) gemm_stamp(p, TS_REDUCED);
   }
 
   // both CTAs are done with TMEM (the pair's MMAs completed before `accum`)
@@ -949,6 +990,7 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
   if (warp == 1) {
     sbd::tc_fence_after();
     sbd::tmem_dealloc_pair(tmem, Q_TMEM_COLS);
+    if (lane == 0) gemm_stamp(p, TS_EXIT);
   }
 }
 
@@ -1158,6 +1200,11 @@ extern "C" size_t sb_gemm_q4_workspace_size(int m, int n, int k) {
   return q4_workspace(m, n, k, 32, 2);
 }
 
+extern "C" int sb_gemm_q4_kernels(int m, int n, int k) {
+  if (m <= 0 || n <= 0 || k <= 0 || k % BK) return 0;
+  return q4_splits(m, n, k, 32, 2) > q4_max_cluster_splits(n) ? 2 : 1;
+}
+
 static int gemm_f16_impl(const void* a, const void* b, void* c, int c_f32, int m, int n, int k, float alpha, int tr,
                          int lda, int ldb, int ldc, void* stream, int splits = 1) {
   SB_CHECK_ARG(m >= 0 && n >= 0 && k >= 0, "sb_gemm_f16: negative shape");
@@ -1233,6 +1280,10 @@ static cudaError_t launch_pair(cudaLaunchConfig_t& cfg, const CUtensorMap& tact,
   }
   return cudaLaunchKernelEx(&cfg, gemm_q4_pair_kernel<BITS, NT>, tact, tw, p);
 }
+
+// Profiling buffer of sb_gemm_q4_trace (null: off) and its size in stamps.
+static unsigned long long* g_trace = nullptr;
+static size_t g_trace_slots = 0;
 
 static int gemm_q4_impl(const void* a, const void* w, const void* scales, int scale_dtype, int group, void* c, int m,
                         int n, int k, float alpha, int lda, int ldc, void* workspace, size_t workspace_bytes,
@@ -1317,6 +1368,7 @@ static int gemm_q4_impl(const void* a, const void* w, const void* scales, int sc
   if (in_cluster) p.csplit = splits;
   else if (splits > 1) p.ws = static_cast<float*>(workspace);
   const dim3 grid(gx, ttiles, splits);
+  if (pair && g_trace && static_cast<size_t>(grid.x) * grid.y * grid.z * kTraceSlots <= g_trace_slots) p.trace = g_trace;
   if (pair || in_cluster) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
@@ -1358,6 +1410,13 @@ static int gemm_q4_impl(const void* a, const void* w, const void* scales, int sc
   }
   if (rc != SB_OK || in_cluster || splits == 1) return rc;
   return finalize(p, splits, s);
+}
+
+extern "C" int sb_gemm_q4_trace(uint64_t* buf, size_t bytes) {
+  SB_CHECK_ARG(!buf || sb::aligned(buf, 8), "sb_gemm_q4_trace: buffer must be 8-byte aligned");
+  g_trace = buf ? reinterpret_cast<unsigned long long*>(buf) : nullptr;
+  g_trace_slots = buf ? bytes / sizeof(uint64_t) : 0;
+  return SB_OK;
 }
 
 extern "C" int sb_gemm_q4(const void* a, const void* w, const void* scales, int scale_dtype, int group, void* c, int m,

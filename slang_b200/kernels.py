@@ -333,6 +333,11 @@ def gemm_q4_workspace_size(M: int, N: int, K: int) -> int:
     return int(_lib.load().sb_gemm_q4_workspace_size(M, N, K))
 
 
+def gemm_q4_kernels(M: int, N: int, K: int) -> int:
+    """Kernels one gemm_q4 call of this shape launches (1, or 2 with a split-K finalize)."""
+    return int(_lib.load().sb_gemm_q4_kernels(M, N, K))
+
+
 _WS: dict = {}
 
 

@@ -420,7 +420,7 @@ class Runner:
         nL = len(self.dm.layers)
         if self.proj == "gemm":
             B, H, F = self.B, self.H, self.F
-            split = lambda n, k: 1 if kern.gemm_q4_workspace_size(B, n, k) else 0  # noqa: E731
+            split = lambda n, k: kern.gemm_q4_kernels(B, n, k) - 1  # noqa: E731
             per_layer = (4 + split(self.nqkv, H) + split(H, self.qd) + split(2 * F, H) + split(H, F)
                          + 1 + 2 + 2)  # prep, attention (2), add+norm (2)
             return 2 + nL * per_layer + 2 + 1  # embed + norm, layers, argmax GEMM + tokens, advance
@@ -572,7 +572,7 @@ class Runner:
     def prefill_launches(self, S: int) -> int:
         """Kernels of this library launched by one prefill of length S."""
         H = self.H
-        split = lambda n, k: 1 if kern.gemm_q4_workspace_size(S, n, k) else 0  # noqa: E731
+        split = lambda n, k: kern.gemm_q4_kernels(S, n, k) - 1  # noqa: E731
         total = 0
         for L in self.dm.layers:
             sp = L["spec"]

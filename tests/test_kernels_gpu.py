@@ -326,6 +326,38 @@ def test_gemm_q4_workspace_only_beyond_cluster_splits(cuda):
     assert kern.gemm_q4_workspace_size(256, 256, 6144) > 0  # 16 splits
 
 
+def test_gemm_q4_kernels_per_call(cuda):
+    """sb_gemm_q4_kernels: a split-K finalize launch follows exactly when the
+    workspace holds partial planes."""
+    for M, N, K in ((1024, 12288, 1536), (1024, 1536, 2048), (256, 256, 6144), (8, 12288, 1536), (32, 512, 6144)):
+        assert kern.gemm_q4_kernels(M, N, K) == (2 if kern.gemm_q4_workspace_size(M, N, K) else 1)
+
+
+def test_gemm_q4_trace_stamps_are_ordered(cuda):
+    """The profiling hook: every CTA of a traced launch stamps its phases in order."""
+    rng = np.random.default_rng(3)
+    M, N, K = 512, 2560, 1536
+    packed, scales = synth.q4_weight(rng, N, K)
+    a = synth.activations(rng, M, K)
+    A, P, S = T(a, cuda), T(packed, cuda), T(scales, cuda)
+    buf = torch.zeros(4096 * 16, dtype=torch.int64, device=cuda)
+    _lib.call("sb_gemm_q4_trace", buf.data_ptr(), buf.numel() * 8)
+    try:
+        c = kern.gemm_q4(A, P, S)
+    finally:
+        _lib.call("sb_gemm_q4_trace", None, 0)
+    kern.device_status()
+    x = buf.view(4096, 16).cpu().numpy()
+    x = x[x[:, 1] > 0]
+    tiles = 2 * ((N + 255) // 256) * ((M + 255) // 256)  # CTAs of one K split
+    assert len(x) >= tiles and len(x) % tiles == 0
+    for row in x:
+        assert row[1] <= row[2] <= row[3] and row[2] <= row[4] <= row[8] <= row[9] <= row[11]
+        if row[6]:  # the pair's MMA-issuing CTA
+            assert row[3] <= row[6] <= row[7] <= row[8]
+    assert_close(c.cpu().numpy(), q4.gemm_f64(a, q4.dequant_f16(packed, scales, 4)))
+
+
 def test_no_device_timeouts(cuda):
     torch.cuda.synchronize()
     kern.device_status()

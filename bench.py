@@ -137,7 +137,7 @@ def run_decode_trace(args):
         with torch.cuda.stream(r.stream):
             r._fused_ops()
     torch.cuda.synchronize()
-    kt, ct = 1024, 160  # trace slots per CTA, traced CTAs (decode_mega.cu kTraceLen, kTraceCtas)
+    kt, ct = 2048, 160  # trace slots per CTA, traced CTAs (decode_mega.cu kTraceLen, kTraceCtas)
     sc = r.fused_scratch
     sc[64:64 + ct * kt * 8].zero_()
     sc[12:16].copy_(torch.tensor([1], dtype=torch.int32).view(torch.uint8))  # the trace switch (scratch u32 3)
@@ -152,7 +152,9 @@ def run_decode_trace(args):
     tmask = np.uint64((1 << 56) - 1)
     ctas = [c for c in range(ct) if tr[c, 0] > 0]
     t_min = min(int(tr[c, 1] & tmask) for c in ctas)
-    names = {2: "arrive", 3: "exit", 4: "input", 5: "stage0", 6: "gemv"}
+    names = {2: "arrive", 3: "exit", 4: "input", 5: "stage0", 11: "rows0", 12: "free0", 6: "gemv", 7: "att_q",
+             8: "att_k", 9: "att_s", 10: "att_pv"}
+    marks = [m for m in names.values() if m not in ("arrive", "exit")]
     phases = ["q|k|v", "attention", "merge", "o", "gate|up", "down"]
     stats: dict = {}
     for c in ctas:
@@ -166,7 +168,7 @@ def run_decode_trace(args):
                 rec = stats.setdefault(ph, {})
                 rec.setdefault("work", []).append(cur.get("arrive", t) - start)
                 rec.setdefault("wait", []).append(t - cur.get("arrive", t))
-                for m in ("input", "stage0", "gemv"):
+                for m in marks:
                     if m in cur:
                         rec.setdefault(m, []).append(cur[m] - start)
                 start, cur, k = t, {}, k + 1

@@ -11,13 +11,13 @@
 //                   streams them (packed rows + their f16 group scales) with
 //                   cp.async.bulk into a shared-memory ring.  Weights do not
 //                   depend on activations, so the stream runs ahead across the
-//                   phase barriers below.
-//   8 consumer warps  run the phases, separated by grid-wide barriers:
+//                   phase hand-offs below.
+//   8 consumer warps  run the phases, each waiting on its input words:
 //     qkv:    x = layer input (embedding, or residual + post-FFN RMSNorm of
 //             the previous down output), h = RMSNorm(x) * in_norm, GEMV rows.
 //             Also starts the bulk copy of this CTA's attention chunk (16 keys
 //             of K and V, q/k norm weights, this position's RoPE row) so it
-//             lands while the GEMV and the barrier run.
+//             lands while the GEMV and the hand-off run.
 //     attn:   per 16-key chunk (one chunk per CTA): q/k norm + RoPE (the CTA
 //             owning this position's chunk also writes k, v to the cache),
 //             scores, chunk softmax partials, P.V partials
@@ -27,18 +27,34 @@
 //             GEGLU of each interleaved (gate, up) row pair
 //     down:   GEMV rows of down over the GEGLU output
 //   and finally RMSNorm * final_norm, the lm_head rows with a running
-//   (max, lowest index) per CTA, one 64-bit atomicMax per CTA, and block 0
-//   decodes the token and advances pos / cur / history.
+//   (max, lowest index) per CTA, one 64-bit atomicMax per CTA, and the CTA
+//   that arrives last decodes the token and advances pos / cur / history.
 //
 // Latency, not bandwidth, bounds this kernel (a phase moves ~20 MB over 148
-// SMs), so every phase is written as few dependent global round trips as
-// possible: each thread issues all of its loads of a phase input before using
-// any, values produced inside the launch are read with ld.global.cg (L2, never
-// a stale L1 line), the next layer's norm vectors are prefetched into L2, and
-// the grid barrier is one 64-bit atomic per CTA on a monotonic counter.
+// SMs), so the phases hand their outputs over with no grid barrier at all.
+// Every value produced inside the launch is stored as one 64-bit word: the
+// f32 bits in the low half and, in the high half, the epoch of the (launch,
+// layer) that wrote it.  A 64-bit store is single-copy atomic, so a reader
+// that sees the current epoch in a word also sees its value: a phase waits for
+// its input by polling the input itself (ld.relaxed.gpu, every word of a
+// thread's slots in flight at once) until every word carries the current
+// epoch.  A transition then costs one L2 round trip once the slowest producer
+// has stored, instead of a barrier's atomic, its poll and the load after it.
+// Each CTA keeps its own copy of the residual stream in shared memory (all
+// CTAs compute it identically), so only GEMV outputs, attention partials and
+// the attention output cross between CTAs.
+//
+// Reuse of a buffer in the next layer is safe without a barrier because every
+// CTA owns rows of gate|up (inter >= CTAs is checked at launch): a CTA's reads
+// of any layer-L buffer precede, in its own program order and through data
+// dependence, its gate|up rows of layer L (or L + 1), which every later
+// producer of that buffer has consumed first.  The launch ends with one atomic
+// count: the CTA that completes it reads the argmax key, advances the
+// position and bumps the launch count the epochs derive from.  The next
+// layer's norm vectors are prefetched into L2.
 //
 // GEMV arithmetic is the exact int4 x int16 DP4A dot of q4_dot.cuh.  Every wait
-// (mbarrier or grid barrier) is bounded by %globaltimer; a timeout raises a
+// (mbarrier or input poll) is bounded by %globaltimer; a timeout raises a
 // sticky abort flag in the scratch header that every CTA polls, writes
 // SB_ERR_TIMEOUT to the device error word, and the kernel unwinds.
 #include <algorithm>
@@ -66,7 +82,7 @@ constexpr int kPasses = kMaxK / (8 * kCons);  // 8-value slots per thread for th
 constexpr int kMaxLayers = 48;
 constexpr int kRed = 128;
 constexpr int kSegOut = 512;          // rows of one CTA's gate|up slice kept for GEGLU
-constexpr unsigned int kTraceLen = 1024;  // per CTA: [0] count, then tagged timestamps
+constexpr unsigned int kTraceLen = 2048;  // per CTA: [0] count, then tagged timestamps
 constexpr int kTraceCtas = 160;           // trace slots (CTAs beyond this are not traced)
 static_assert(kCons == HD, "the P.V step maps one thread to one head dim");
 static_assert(CKA == 16, "the score reduction is written for 16-key chunks");
@@ -102,9 +118,11 @@ struct Params {
   int32_t* history;
   int hist_len;
   unsigned long long* keys;
-  float *xa, *xb, *qkv, *attn, *o, *a, *d, *part;
-  unsigned long long* ctr;    // grid barrier: arrivals since the scratch was zeroed
-  unsigned int* bar;          // [2] sticky abort flag, [3] trace switch
+  // values produced inside the launch, one (epoch << 32 | f32 bits) word each
+  uint64_t *qkv, *attn, *o, *a, *d, *part;
+  unsigned long long* ctr;    // end-of-step count: arrivals since the scratch was zeroed
+  unsigned long long* kmax;   // running argmax key of the step (reset by the last arriver)
+  unsigned int* bar;          // [2] sticky abort flag, [3] trace switch, [4] completed launches
   unsigned long long* trace;  // optional: per CTA, tagged %globaltimer stamps
   int* err;
 };
@@ -119,6 +137,14 @@ struct XQ {
   float sx[kMaxG];
 };
 
+// This CTA's rows [r0, r1) of an N x K matrix and the rows per ring stage.
+struct Seg {
+  int r0, r1, rs;
+  int kslog, sg;  // GEMV layout: log2 of the K slices per row, groups per slice
+};
+// the matrices a CTA streams: per layer q|k|v, o, gate|up, down; then the lm_head
+enum { M_QKV = 0, M_O = 1, M_GU = 2, M_DOWN = 3, M_HEAD = 4, kMats = 5 };
+
 struct Smem {
   uint8_t w[kRing][kStageW];
   uint8_t s[kRing][kStageS];
@@ -132,6 +158,8 @@ struct Smem {
   float ps[kMaxHeads][CKA];  // chunk softmax numerators
   float red[2][kRed];
   float seg_out[kSegOut];
+  float resid[kMaxH];        // this CTA's copy of the residual stream
+  Seg seg[kMats];            // this CTA's rows of each matrix (segment, gemv_layout)
   unsigned long long best[8];
   uint64_t full[kRing];
   uint64_t empty[kRing];
@@ -140,6 +168,8 @@ struct Smem {
   unsigned int trace_n;
   Params prm;  // the launch parameters, for the out-of-line phase functions
 };
+
+static_assert(sizeof(Smem) <= 227 * 1024, "one CTA's shared memory");
 
 // The CTA's shared memory.  Out-of-line functions take it (and the launch
 // parameters) from here rather than through a pointer argument, so their
@@ -150,13 +180,31 @@ __device__ __forceinline__ Smem& smem() {
 }
 
 // ---------------------------------------------------------------- small helpers
-__device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+// Epoch-tagged words (see the file comment): value bits low, epoch high.
+__device__ __forceinline__ uint64_t ll_pack(float v, uint32_t ep) {
+  return (static_cast<uint64_t>(ep) << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ float ll_val(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
+__device__ __forceinline__ bool ll_is(uint64_t w, uint32_t ep) { return static_cast<uint32_t>(w >> 32) == ep; }
+__device__ __forceinline__ void ll_st(uint64_t* p, float v, uint32_t ep) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(ll_pack(v, ep)) : "memory");
+}
+__device__ __forceinline__ void ll_st2(uint64_t* p, float a, float b, uint32_t ep) {
+  asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(ll_pack(a, ep)), "l"(ll_pack(b, ep))
+               : "memory");
+}
+__device__ __forceinline__ uint64_t ll_ld(const uint64_t* p) {
+  uint64_t w;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p));
+  return w;
+}
+// p 16-byte aligned; each 64-bit element is a single-copy-atomic access
+__device__ __forceinline__ void ll_ld2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p));
 }
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -234,7 +282,7 @@ __device__ bool ring_wait(uint64_t* bar, uint32_t parity, const Params& p, bool&
 
 // Trace stamp by thread 0 of a CTA: (tag << 56) | %globaltimer.
 enum { TR_ENTRY = 1, TR_ARRIVE = 2, TR_EXIT = 3, TR_INPUT = 4, TR_STAGE0 = 5, TR_GEMV = 6, TR_ATT_Q = 7,
-       TR_ATT_K = 8, TR_ATT_S = 9, TR_ATT_PV = 10 };
+       TR_ATT_K = 8, TR_ATT_S = 9, TR_ATT_PV = 10, TR_ROWS0 = 11, TR_FREE0 = 12 };
 // The count lives in shared memory (a global read per stamp would distort the
 // intervals being measured) and is written out as entry 0 at every stamp.
 __device__ void trace_stamp(const Params& p, unsigned int tag) {
@@ -250,63 +298,99 @@ __device__ void trace_stamp(const Params& p, unsigned int tag) {
   }
 }
 
-// Grid-wide barrier among the consumer warps of every CTA (the producer warp
-// never joins: it may be blocked on a ring slot the consumers will free only
-// after this barrier).  Each CTA adds 1 to a 64-bit counter that only grows
-// (every barrier adds exactly gridDim.x) and waits until it reaches the end of
-// its round.  Bounded spin; false (for every consumer thread of the CTA) when
-// any of them failed or the step was aborted.  A failing CTA raises the abort
-// flag instead of arriving, which releases the others within kAbortPollNs.
-__device__ __noinline__ bool grid_sync(bool& fail) {
-  Smem& sm = smem();
-  const Params& p = sm.prm;
+// End of a phase: the consumer threads of the CTA agree whether any of them
+// failed (a wait that ran out or saw the abort flag).  If so the CTA raises the
+// abort flag -- which ends every other CTA's waits within kAbortPollNs -- and
+// leaves; false for every consumer thread.  No other CTA is waited for here:
+// the next phase waits on its own input words.
+__device__ __forceinline__ bool phase_end(bool& fail) {
   if (cons_sync_or(fail)) {
-    if (threadIdx.x == 0) raise_abort(p);
+    if (threadIdx.x == 0) raise_abort(smem().prm);
     fail = true;
     return false;
   }
-  if (threadIdx.x == 0) {
-    trace_stamp(p, TR_ARRIVE);
-    bool ok = true;
-    __threadfence();
-    const unsigned long long old = atomicAdd(p.ctr, 1ull);
-    const unsigned long long target = (old / gridDim.x + 1) * gridDim.x;
-    if (ld_acquire64(p.ctr) < target) {
-      const uint64_t t0 = sbd::global_ns();
-      while (ld_acquire64(p.ctr) < target) {
-        const uint64_t dt = sbd::global_ns() - t0;
-        if (dt > kAbortPollNs && aborted(p)) {
-          ok = false;
-          break;
-        }
-        if (dt > sbd::kWaitLimitNs) {
-          raise_abort(p);
-          ok = false;
-          break;
-        }
-      }
-    }
-    sm.flag = ok;
-    trace_stamp(p, TR_EXIT);
+  return true;
+}
+
+// One more round of an input poll?  Starts the clock on the first miss; past
+// kAbortPollNs also checks the abort flag, past the wait limit raises it.
+// false (and `fail` set) when the wait must end.
+__device__ __forceinline__ bool poll_again(const Params& p, uint64_t& t0, bool& fail) {
+  if (fail) return false;
+  if (t0 == 0) {
+    t0 = sbd::global_ns();
+    return true;
   }
-  cons_sync();
-  if (sm.flag == 0) fail = true;
-  return !fail;
+  const uint64_t dt = sbd::global_ns() - t0;
+  if (dt > kAbortPollNs && aborted(p)) {
+    fail = true;
+    return false;
+  }
+  if (dt > sbd::kWaitLimitNs) {
+    raise_abort(p);
+    fail = true;
+    return false;
+  }
+  return true;
+}
+
+// Loads of a thread's slots of an epoch-tagged vector: slot s = tid + ps *
+// kCons holds values [8 s, 8 s + 8); beyond n a word reads as epoch ep, 0.f.
+template <int NP>
+__device__ __forceinline__ void ll_issue(uint64_t (&w)[NP][8], const uint64_t* src, int n, uint32_t ep) {
+#pragma unroll
+  for (int ps = 0; ps < NP; ++ps) {
+    const int s = threadIdx.x + ps * kCons;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (8 * s < n) ll_ld2(src + 8 * s + 2 * q, w[ps][2 * q], w[ps][2 * q + 1]);
+      else w[ps][2 * q] = w[ps][2 * q + 1] = static_cast<uint64_t>(ep) << 32;
+    }
+  }
+}
+template <int NP>
+__device__ __forceinline__ bool ll_take(const uint64_t (&w)[NP][8], float (&v)[NP][8], uint32_t ep) {
+  bool ok = true;
+#pragma unroll
+  for (int ps = 0; ps < NP; ++ps)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      ok &= ll_is(w[ps][i], ep);
+      v[ps][i] = ll_val(w[ps][i]);
+    }
+  return ok;
+}
+
+// v[ps][0..8) <- values [8 s, 8 s + 8) of the epoch-tagged vector src, s = tid
+// + ps * kCons, once every one of those words carries epoch ep (zeros beyond
+// n).  All of the thread's loads are in flight before any is tested.  (Two
+// polls in flight, staggered by half a round trip, measured slower: the extra
+// L2 traffic lengthens every other CTA's wait.)
+template <int NP>
+__device__ __forceinline__ void ll_slots(float (&v)[NP][8], const uint64_t* src, int n, uint32_t ep, bool& fail) {
+  const Params& p = smem().prm;
+  uint64_t t0 = 0;
+  for (;;) {
+    uint64_t w[NP][8];
+    ll_issue<NP>(w, src, n, ep);
+    if (ll_take<NP>(w, v, ep) || !poll_again(p, t0, fail)) return;
+  }
 }
 
 // ---------------------------------------------------------------- weight segments
-// This CTA's rows [r0, r1) of an N x K matrix and the rows per ring stage.
-struct Seg {
-  int r0, r1, rs;
-};
+// Rows are dealt in pairs (gate/up rows stay together), as evenly as the pair
+// count allows: CTA b gets pairs [b P / G, (b + 1) P / G).
+// Computed once per launch (sm.seg); the GEMV layout fields are set by gemv_layout.
 __device__ __forceinline__ Seg segment(int n, int k) {
-  int per = (n + gridDim.x - 1) / gridDim.x;
-  per = (per + 1) & ~1;  // even: gate/up rows stay paired
+  const long long pairs = (n + 1) / 2, g = gridDim.x, b = blockIdx.x;
   Seg s;
-  s.r0 = min(n, static_cast<int>(blockIdx.x) * per);
-  s.r1 = min(n, s.r0 + per);
+  s.r0 = min(n, static_cast<int>(2 * (b * pairs / g)));
+  s.r1 = min(n, static_cast<int>(2 * ((b + 1) * pairs / g)));
+  const int per = 2 * static_cast<int>((pairs + g - 1) / g);
   s.rs = max(1, min(per, kStageW / (k / 2)));
   s.rs = min(s.rs, kStageS / (k / 16));
+  s.kslog = 0;
+  s.sg = 0;
   return s;
 }
 
@@ -320,11 +404,18 @@ __device__ __forceinline__ int ks_for(int k, int gpl) {
   while (16 * gpl * ks < k / 32) ks *= 2;
   return ks;
 }
+__device__ __forceinline__ Seg gemv_layout(int n, int k) {
+  Seg s = segment(n, k);
+  const int ks = ks_for(k, gpl_for(k));
+  s.kslog = __ffs(ks) - 1;
+  s.sg = (k / 32 + ks - 1) / ks;
+  return s;
+}
 
 // producer: stream one matrix's slice through the ring
-__device__ bool produce(const Params& p, Smem& sm, const uint8_t* w, const __half* s, int n, int k, int& it,
+__device__ bool produce(const Params& p, Smem& sm, const uint8_t* w, const __half* s, int mat, int k, int& it,
                         bool& fail) {
-  const Seg sg = segment(n, k);
+  const Seg sg = sm.seg[mat];
   const int rb = k / 2, sb = k / 16;
   const uint64_t pol = sbd::l2_policy_evict_first();
   for (int r = sg.r0; r < sg.r1; r += sg.rs) {
@@ -349,22 +440,24 @@ struct Cursor {
   float best_v;       // lm_head: running max ...
   long long best_i;   // ... and its row
   bool fail;          // sticky failure (see ring_wait)
+  uint32_t ep;        // epoch of the current (launch, layer): tags the words this CTA stores
 };
 
 // consumers: GEMV of this CTA's rows of one matrix over the quantised input
-// sm.xq (K values).  epi: EPI_STORE (out[row]), EPI_SEGOUT (sm.seg_out) or
+// sm.xq (K values).  epi: EPI_STORE (out[row], an epoch-tagged word), EPI_SEGOUT (sm.seg_out) or
 // EPI_ARGMAX (running max / lowest row).  Each half-warp works on two rows at
 // a time (independent dot chains).  A failed ring wait leaves garbage in this
 // CTA's results; the next grid barrier turns it into an abort.
 template <int GPL>
-__device__ __noinline__ void gemv_phase_t(int n, int k, int epi, float* out, Cursor& cur) {
+__device__ __noinline__ void gemv_phase_t(int mat, int k, int epi, uint64_t* out, Cursor& cur) {
   Smem& sm = smem();
   const Params& p = sm.prm;
   const int tid = threadIdx.x, hw = tid >> 4, l16 = tid & 15;
-  const int ks = ks_for(k, GPL);
+  const Seg sg = sm.seg[mat];
+  const int ks = 1 << sg.kslog;
   const int G = k / 32;
-  const int SG = (G + ks - 1) / ks;
-  const int kslice = hw % ks, rlane = hw / ks, nrl = 16 / ks;
+  const int SG = sg.sg;
+  const int kslice = hw & (ks - 1), rlane = hw >> sg.kslog, nrl = 16 >> sg.kslog;
   const int gb = kslice * SG, ge = min(G, gb + SG);
   int it = cur.it;
   float best_v = cur.best_v;
@@ -389,11 +482,10 @@ __device__ __noinline__ void gemv_phase_t(int n, int k, int epi, float* out, Cur
     xg[u].sx = sm.xq.sx[g];
   }
   trace_stamp(p, TR_INPUT);
-  const Seg sg = segment(n, k);
   const int rb = k / 2;
   auto put = [&](int row, float v) {
     if (epi == EPI_STORE) {
-      out[row] = v;
+      ll_st(out + row, v, cur.ep);
     } else if (epi == EPI_SEGOUT) {
       sm.seg_out[row - sg.r0] = v;
     } else {
@@ -441,6 +533,7 @@ __device__ __noinline__ void gemv_phase_t(int n, int k, int epi, float* out, Cur
         }
       }
     }
+    if (r == sg.r0) trace_stamp(p, TR_ROWS0);
     __syncwarp();
     if ((tid & 31) == 0) sbd::mbar_arrive(&sm.empty[slot]);
     if (ks > 1) {
@@ -451,6 +544,7 @@ __device__ __noinline__ void gemv_phase_t(int n, int k, int epi, float* out, Cur
         put(r + e, v);
       }
     }
+    if (r == sg.r0) trace_stamp(p, TR_FREE0);
     ++it;
   }
   trace_stamp(p, TR_GEMV);
@@ -460,11 +554,11 @@ __device__ __noinline__ void gemv_phase_t(int n, int k, int epi, float* out, Cur
   cur.fail = fail;
 }
 
-__device__ __forceinline__ void gemv_phase(int n, int k, int epi, float* out, Cursor& cur) {
+__device__ __forceinline__ void gemv_phase(int mat, int k, int epi, uint64_t* out, Cursor& cur) {
   if (gpl_for(k) == 4)
-    gemv_phase_t<4>(n, k, epi, out, cur);
+    gemv_phase_t<4>(mat, k, epi, out, cur);
   else
-    gemv_phase_t<3>(n, k, epi, out, cur);
+    gemv_phase_t<3>(mat, k, epi, out, cur);
 }
 
 // ---------------------------------------------------------------- phase inputs
@@ -533,14 +627,15 @@ __device__ __forceinline__ float sumsq8(const float (&v)[8]) {
 }
 
 // sm.xq <- quantise(RMSNorm(v) * w) for a hidden-sized v held one slot per
-// thread (values [8 tid, 8 tid + 8)); optionally stores v to `keep`.
-__device__ void finish_norm(const Params& p, Smem& sm, int n, float (&v)[8], const float (&w)[8], float* keep) {
+// thread (values [8 tid, 8 tid + 8)); with `keep`, v also becomes this CTA's
+// residual stream (sm.resid).
+__device__ void finish_norm(const Params& p, Smem& sm, int n, float (&v)[8], const float (&w)[8], bool keep) {
   // one reciprocal, then multiplies: eight IEEE divides per thread cost more
   // than the rest of the prologue (differs from v / dnm by at most an ulp)
   const float inv = 1.f / sqrtf(cons_reduce<false>(sumsq8(v), sm) / n + p.eps);
   const int s = threadIdx.x;
   if (keep && 8 * s < n) {
-    float4* k4 = reinterpret_cast<float4*>(keep) + 2 * s;
+    float4* k4 = reinterpret_cast<float4*>(sm.resid) + 2 * s;
     k4[0] = make_float4(v[0], v[1], v[2], v[3]);
     k4[1] = make_float4(v[4], v[5], v[6], v[7]);
   }
@@ -550,33 +645,43 @@ __device__ void finish_norm(const Params& p, Smem& sm, int n, float (&v)[8], con
   cons_sync();
 }
 
-// sm.xq <- quantise(RMSNorm(x + RMSNorm(y) * w_res) * w_norm), all loads issued up front
-__device__ __noinline__ void residual_norm(int n, const float* x, const float* y, const float* w_res,
-                                          const float* w_norm, float* keep) {
+// Wait for the epoch-ep words of the hidden-sized y (another phase's output),
+// then resid += RMSNorm(y) * w_res and sm.xq <- quantise(RMSNorm(resid) *
+// w_norm) (keep: the sum becomes the residual; the final norm does not need it).
+__device__ __noinline__ void residual_norm(int n, const uint64_t* y, uint32_t ep, const float* w_res,
+                                          const float* w_norm, bool keep, bool& fail) {
   Smem& sm = smem();
   const Params& p = sm.prm;
   const int s = threadIdx.x;
   const bool in = 8 * s < n;
-  float v[8], yv[8], wr[8], wn[8];
-  ld8(v, x, s, in, true);
-  ld8(yv, y, s, in, true);
+  float v[8], yv[1][8], wr[8], wn[8];
   ld8(wr, w_res, s, in, false);
   ld8(wn, w_norm, s, in, false);
-  const float inv = 1.f / sqrtf(cons_reduce<false>(sumsq8(yv), sm) / n + p.eps);
+  trace_stamp(p, TR_ARRIVE);
+  ll_slots<1>(yv, y, n, ep, fail);
+  trace_stamp(p, TR_EXIT);
+  if (in) {
+    const float4* r4 = reinterpret_cast<const float4*>(sm.resid) + 2 * s;
+    const float4 r0 = r4[0], r1 = r4[1];
+    v[0] = r0.x; v[1] = r0.y; v[2] = r0.z; v[3] = r0.w;
+    v[4] = r1.x; v[5] = r1.y; v[6] = r1.z; v[7] = r1.w;
+  } else {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = v[i] + yv[i] * inv * wr[i];
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+  }
+  const float inv = 1.f / sqrtf(cons_reduce<false>(sumsq8(yv[0]), sm) / n + p.eps);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = v[i] + yv[0][i] * inv * wr[i];
   finish_norm(p, sm, n, v, wn, keep);
 }
 
-// sm.xq <- quantise(src[0, n)) (values written earlier in this launch)
-__device__ __noinline__ void load_input(int n, const float* src) {
+// sm.xq <- quantise(src[0, n)), once every word carries epoch ep
+__device__ __noinline__ void load_input(int n, const uint64_t* src, uint32_t ep, bool& fail) {
   Smem& sm = smem();
   float v[kPasses][8];
-#pragma unroll
-  for (int ps = 0; ps < kPasses; ++ps) {
-    const int s = threadIdx.x + ps * kCons;
-    ld8(v[ps], src, s, 8 * s < n, true);
-  }
+  trace_stamp(sm.prm, TR_ARRIVE);
+  ll_slots<kPasses>(v, src, n, ep, fail);
+  trace_stamp(sm.prm, TR_EXIT);
 #pragma unroll
   for (int ps = 0; ps < kPasses; ++ps)
     if (ps * 8 * kCons < n) quantise_slot(sm, threadIdx.x + ps * kCons, n, v[ps]);
@@ -630,15 +735,45 @@ __device__ void kv_issue(const Params& p, Smem& sm, const Layer& L, int c, int p
 
 // q heads (and k, v of this position when `own`): RMSNorm (weights for q, k;
 // none for v), RoPE on q and k; q to sm.vb, k / v to the cache and sm.kpos / vpos.
-__device__ void qkv_heads(const Params& p, Smem& sm, const Layer& L, int pos, bool own) {
-  const int nh = p.nh, qd = nh * HD;
+// A warp takes heads warp and warp + 8 and waits for both heads' epoch-ep
+// words of the q|k|v output with all of its loads in flight at once.
+__device__ void qkv_heads(const Params& p, Smem& sm, const Layer& L, int pos, bool own, uint32_t ep,
+                          bool& fail) {
+  const int nh = p.nh, qd = nh * HD, nhead = nh + (own ? 2 : 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int h = warp; h < nh + (own ? 2 : 0); h += kCons / 32) {
-    const int col = h < nh ? h * HD : (h == nh ? qd : qd + HD);
-    float v[8];
-    float ss = 0.f;
+  static_assert(kMaxHeads + 2 <= 2 * (kCons / 32), "two heads per warp");
+  float vv[2][8];
+  {
+    uint64_t t0 = 0;
+    for (;;) {
+      uint64_t w[2][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = __ldcg(p.qkv + col + lane + 32 * j);
+      for (int u = 0; u < 2; ++u) {
+        const int h = warp + u * (kCons / 32);
+        const int col = h < nh ? h * HD : (h == nh ? qd : qd + HD);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          w[u][j] = h < nhead ? ll_ld(p.qkv + col + lane + 32 * j) : static_cast<uint64_t>(ep) << 32;
+      }
+      bool ok = true;
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          ok &= ll_is(w[u][j], ep);
+          vv[u][j] = ll_val(w[u][j]);
+        }
+      if (__all_sync(0xFFFFFFFFu, ok)) break;
+      // warp-uniform exit: a lane whose wait ended (fail set) ends the warp's
+      if (!__all_sync(0xFFFFFFFFu, poll_again(p, t0, fail))) break;
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int h = warp + u * (kCons / 32);
+    if (h >= nhead) break;
+    float* v = vv[u];
+    float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
     const float inv = 1.f / sqrtf(warp_sum(ss) / HD + p.eps);
@@ -669,8 +804,9 @@ __device__ void qkv_heads(const Params& p, Smem& sm, const Layer& L, int pos, bo
   }
 }
 
-// Chunk c's scores, softmax partials (max, sum) and P.V partials from sm.kv.
-__device__ void attn_chunk(const Params& p, Smem& sm, int c, int pos) {
+// Chunk c's scores, softmax partials (max, sum) and P.V partials from sm.kv,
+// stored as epoch-ep words.
+__device__ void attn_chunk(const Params& p, Smem& sm, int c, int pos, uint32_t ep) {
   const int nh = p.nh;
   const int T = pos + 1, t0 = c * CKA, nt = min(CKA, T - t0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -723,11 +859,7 @@ __device__ void attn_chunk(const Params& p, Smem& sm, int c, int pos) {
       sm.ps[h][key] = p0;
       sm.ps[h][key + 8] = p1;
     }
-    if (lane == 0) {
-      float* pm = p.part + (static_cast<size_t>(c) * nh + h) * (HD + 2);
-      pm[HD] = m;
-      pm[HD + 1] = l;
-    }
+    if (lane == 0) ll_st2(p.part + (static_cast<size_t>(c) * nh + h) * (HD + 2) + HD, m, l, ep);
   }
   cons_sync();
   trace_stamp(p, TR_ATT_S);
@@ -750,7 +882,7 @@ __device__ void attn_chunk(const Params& p, Smem& sm, int c, int pos) {
     }
 #pragma unroll
     for (int h = 0; h < kMaxHeads; ++h)
-      if (h < nh) p.part[(static_cast<size_t>(c) * nh + h) * (HD + 2) + dcol] = acc[h];
+      if (h < nh) ll_st(p.part + (static_cast<size_t>(c) * nh + h) * (HD + 2) + dcol, acc[h], ep);
   }
   trace_stamp(p, TR_ATT_PV);
 }
@@ -758,8 +890,8 @@ __device__ void attn_chunk(const Params& p, Smem& sm, int c, int pos) {
 // The attention phase: this CTA's chunks c = blockIdx.x, + gridDim.x, ...
 // The first chunk's copy was started in the qkv phase (kv_issue with consts).
 // kvph counts completed waits on sm.kvbar, issued (thread 0) the copies started.
-__device__ void attention(const Params& p, Smem& sm, const Layer& L, int pos, int nc, uint32_t& kvph,
-                          uint32_t& issued, bool& fail) {
+__device__ void attention(const Params& p, Smem& sm, const Layer& L, int pos, int nc, uint32_t ep,
+                          uint32_t& kvph, uint32_t& issued, bool& fail) {
   const int cpos = pos / CKA;
   const bool own = cpos % static_cast<int>(gridDim.x) == static_cast<int>(blockIdx.x);
   for (int c = blockIdx.x; c < nc; c += gridDim.x) {
@@ -769,8 +901,10 @@ __device__ void attention(const Params& p, Smem& sm, const Layer& L, int pos, in
     }
     if (ring_wait(&sm.kvbar, kvph & 1, p, fail)) ++kvph;
     if (c == static_cast<int>(blockIdx.x)) {
-      qkv_heads(p, sm, L, pos, own);
+      trace_stamp(p, TR_ARRIVE);
+      qkv_heads(p, sm, L, pos, own, ep, fail);
       cons_sync();
+      trace_stamp(p, TR_EXIT);
       trace_stamp(p, TR_ATT_Q);
     }
     if (c == cpos) {
@@ -779,31 +913,62 @@ __device__ void attention(const Params& p, Smem& sm, const Layer& L, int pos, in
     }
     cons_sync();
     trace_stamp(p, TR_ATT_K);
-    attn_chunk(p, sm, c, pos);
+    attn_chunk(p, sm, c, pos, ep);
   }
 }
 
-// Merge of the chunk partials: work item (head, kMergeDims dims).
-__device__ void merge(const Params& p, Smem& sm, int nc) {
+// Merge of the chunk partials: work item (head, kMergeDims dims).  Waits on
+// the partials' epoch-ep words (batches of 8 loads in flight per thread) and
+// stores the attention output as epoch-ep words.  A CTA without a work item
+// stamps an empty wait so that every CTA's trace has the same phases.
+__device__ void merge(const Params& p, Smem& sm, int nc, uint32_t ep, bool& fail) {
   const int nh = p.nh, tid = threadIdx.x;
   constexpr int NG = kCons / kMergeDims;  // chunk groups summed in parallel
+  constexpr int B = 8;                    // loads in flight per thread and poll
   const int items = nh * (HD / kMergeDims);
   const size_t cst = static_cast<size_t>(nh) * (HD + 2);
   float* ms = &sm.kv[0][0][0];      // the K/V chunk buffer is free until the next layer
   float* fv = ms;                   // [nc] chunk max, then weight
   float* lv = ms + kMaxChunks;      // [nc] chunk sum
   float* rv = ms + 2 * kMaxChunks;  // [NG][kMergeDims]
+  if (static_cast<int>(blockIdx.x) >= items) {
+    trace_stamp(p, TR_ARRIVE);
+    trace_stamp(p, TR_EXIT);
+  }
   for (int item = blockIdx.x; item < items; item += gridDim.x) {
     const int h = item / (HD / kMergeDims), d0 = (item % (HD / kMergeDims)) * kMergeDims;
-    const float* base = p.part + static_cast<size_t>(h) * (HD + 2);
+    const uint64_t* base = p.part + static_cast<size_t>(h) * (HD + 2);
+    if (item == static_cast<int>(blockIdx.x)) trace_stamp(p, TR_ARRIVE);
     float mx = -INFINITY;
-    for (int c = tid; c < nc; c += kCons) {
-      const float m = __ldcg(base + c * cst + HD);
-      fv[c] = m;
-      lv[c] = __ldcg(base + c * cst + HD + 1);
-      mx = fmaxf(mx, m);
+    for (int c0 = tid; c0 < nc; c0 += B * kCons) {
+      uint64_t t0 = 0;
+      for (;;) {
+        uint64_t wm[B], wl[B];
+#pragma unroll
+        for (int i = 0; i < B; ++i) {
+          const int c = c0 + i * kCons;
+          if (c < nc) ll_ld2(base + c * cst + HD, wm[i], wl[i]);
+          else wm[i] = wl[i] = static_cast<uint64_t>(ep) << 32;
+        }
+        bool ok = true;
+#pragma unroll
+        for (int i = 0; i < B; ++i) ok &= ll_is(wm[i], ep) && ll_is(wl[i], ep);
+        if (ok || !poll_again(p, t0, fail)) {
+#pragma unroll
+          for (int i = 0; i < B; ++i) {
+            const int c = c0 + i * kCons;
+            if (c < nc) {
+              fv[c] = ll_val(wm[i]);
+              lv[c] = ll_val(wl[i]);
+              mx = fmaxf(mx, ll_val(wm[i]));
+            }
+          }
+          break;
+        }
+      }
     }
     mx = cons_reduce<true>(mx, sm);
+    if (item == static_cast<int>(blockIdx.x)) trace_stamp(p, TR_EXIT);
     float ls = 0.f;
     for (int c = tid; c < nc; c += kCons) {
       const float f = expf(fv[c] - mx);
@@ -813,14 +978,34 @@ __device__ void merge(const Params& p, Smem& sm, int nc) {
     ls = cons_reduce<false>(ls, sm);  // its barriers also publish fv
     const int dd = tid % kMergeDims, g = tid / kMergeDims;
     float acc = 0.f;
-#pragma unroll 4
-    for (int c = g; c < nc; c += NG) acc = fmaf(fv[c], __ldcg(base + c * cst + d0 + dd), acc);
+    for (int c0 = g; c0 < nc; c0 += B * NG) {
+      uint64_t t0 = 0;
+      for (;;) {
+        uint64_t w[B];
+#pragma unroll
+        for (int i = 0; i < B; ++i) {
+          const int c = c0 + i * NG;
+          w[i] = c < nc ? ll_ld(base + c * cst + d0 + dd) : static_cast<uint64_t>(ep) << 32;
+        }
+        bool ok = true;
+#pragma unroll
+        for (int i = 0; i < B; ++i) ok &= ll_is(w[i], ep);
+        if (ok || !poll_again(p, t0, fail)) {
+#pragma unroll
+          for (int i = 0; i < B; ++i) {
+            const int c = c0 + i * NG;
+            if (c < nc) acc = fmaf(fv[c], ll_val(w[i]), acc);
+          }
+          break;
+        }
+      }
+    }
     rv[g * kMergeDims + dd] = acc;
     cons_sync();
     if (tid < kMergeDims) {
       float o = 0.f;
       for (int q = 0; q < NG; ++q) o += rv[q * kMergeDims + tid];
-      p.attn[h * HD + d0 + tid] = o / ls;
+      ll_st(p.attn + h * HD + d0 + tid, o / ls, ep);
     }
     cons_sync();
   }
@@ -853,6 +1038,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(Params p) {
     sbd::fence_mbar_init();
     sbd::fence_proxy_async_smem();
   }
+  if (tid >= 32 && tid < 32 + kMats) {
+    // this CTA's rows and GEMV layout of each matrix, once per launch
+    const int m = tid - 32;
+    const int n = m == M_QKV ? nqkv : m == M_GU ? 2 * F : m == M_HEAD ? p.V : H;
+    const int k = m == M_O ? qd : m == M_DOWN ? F : H;
+    sm.seg[m] = gemv_layout(n, k);
+  }
   __syncthreads();
 
   if (tid >= kCons) {
@@ -862,12 +1054,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(Params p) {
       bool ok = true, pfail = false;
       for (int li = 0; li < p.n_layers && ok; ++li) {
         const Layer& L = sm.layers[li];
-        ok = produce(p, sm, L.w[0], L.s[0], nqkv, H, it, pfail) &&
-             produce(p, sm, L.w[1], L.s[1], H, qd, it, pfail) &&
-             produce(p, sm, L.w[2], L.s[2], 2 * F, H, it, pfail) &&
-             produce(p, sm, L.w[3], L.s[3], H, F, it, pfail);
+        ok = produce(p, sm, L.w[0], L.s[0], M_QKV, H, it, pfail) &&
+             produce(p, sm, L.w[1], L.s[1], M_O, qd, it, pfail) &&
+             produce(p, sm, L.w[2], L.s[2], M_GU, H, it, pfail) &&
+             produce(p, sm, L.w[3], L.s[3], M_DOWN, F, it, pfail);
       }
-      if (ok) ok = produce(p, sm, p.emb, p.emb_s, p.V, H, it, pfail);
+      if (ok) ok = produce(p, sm, p.emb, p.emb_s, M_HEAD, H, it, pfail);
       if (!ok) {
         // let copies in flight land before the CTA releases its shared memory
         const uint64_t t0 = sbd::global_ns();
@@ -880,20 +1072,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(Params p) {
   }
 
   // -------------------------------------------------------------- consumer warps
-  if (blockIdx.x == 0 && tid == 0) *p.keys = 0ull;  // ordered before the lm_head by the barriers
   trace_stamp(p, TR_ENTRY);
   const int pos = p.pos[0];
   const int nc = pos / CKA + 1;  // attention chunks
-  Cursor cur{0, -INFINITY, 0x7FFFFFFF, false};
+  // epochs of this launch: e0 + li tags layer li's words; launches completed
+  // so far count up from the zeroed scratch (2^26 launches before a repeat)
+  const uint32_t e0 = (__ldcg(p.bar + 4) & 0x3FFFFFFu) * 64u + 1u;
+  Cursor cur{0, -INFINITY, 0x7FFFFFFF, false, e0};
   // an abort left by an earlier launch stays until the caller zeroes the scratch
   cur.fail = tid == 0 && aborted(p);
   bool& fail = cur.fail;
   uint32_t kvph = 0, kv_issued = 0;
-  const bool lead = blockIdx.x == 0;
   const bool has_chunk = static_cast<int>(blockIdx.x) < nc;
   bool ok = true;
   for (int li = 0; li < p.n_layers && ok; ++li) {
     const Layer& L = sm.layers[li];
+    const uint32_t ep = e0 + li;
     // ---- qkv: start this layer's K/V chunk copy, layer input, RMSNorm, GEMV
     if (has_chunk && tid == 0 && !fail) kv_issue(p, sm, L, blockIdx.x, pos, true, kv_issued);
     prefetch_norms(p, li + 1);
@@ -910,36 +1104,42 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(Params p) {
         const int q = static_cast<int>((wd >> (4 * i)) & 15u) - 8;
         v[i] = in ? __fmul_rn(__fmul_rn(static_cast<float>(q), sc), p.embed_scale) : 0.f;
       }
-      finish_norm(p, sm, H, v, wn, lead ? p.xa : nullptr);
+      finish_norm(p, sm, H, v, wn, true);
     } else {
-      residual_norm(H, p.xb, p.d, sm.layers[li - 1].post_ffn, L.in_norm, lead ? p.xa : nullptr);
+      // x += RMSNorm(down of the previous layer) * its post-FFN norm
+      residual_norm(H, p.d, ep - 1, sm.layers[li - 1].post_ffn, L.in_norm, true, fail);
     }
-    gemv_phase(nqkv, H, EPI_STORE, p.qkv, cur);
-    if (!(ok = grid_sync(fail))) break;
+    cur.ep = ep;
+    gemv_phase(M_QKV, H, EPI_STORE, p.qkv, cur);
+    if (!(ok = phase_end(fail))) break;
     // ---- attention partials
-    attention(p, sm, L, pos, nc, kvph, kv_issued, fail);
-    if (!(ok = grid_sync(fail))) break;
+    if (!has_chunk) {
+      trace_stamp(p, TR_ARRIVE);
+      trace_stamp(p, TR_EXIT);
+    }
+    attention(p, sm, L, pos, nc, ep, kvph, kv_issued, fail);
+    if (!(ok = phase_end(fail))) break;
     // ---- merge
-    merge(p, sm, nc);
-    if (!(ok = grid_sync(fail))) break;
+    merge(p, sm, nc, ep, fail);
+    if (!(ok = phase_end(fail))) break;
     // ---- o projection
-    load_input(qd, p.attn);
-    gemv_phase(H, qd, EPI_STORE, p.o, cur);
-    if (!(ok = grid_sync(fail))) break;
+    load_input(qd, p.attn, ep, fail);
+    gemv_phase(M_O, qd, EPI_STORE, p.o, cur);
+    if (!(ok = phase_end(fail))) break;
     // ---- gate|up with GEGLU
-    residual_norm(H, p.xa, p.o, L.post_attn, L.pre_ffn, lead ? p.xb : nullptr);
-    gemv_phase(2 * F, H, EPI_SEGOUT, nullptr, cur);
+    residual_norm(H, p.o, ep, L.post_attn, L.pre_ffn, true, fail);
+    gemv_phase(M_GU, H, EPI_SEGOUT, nullptr, cur);
     cons_sync();
     {
-      const Seg sg = segment(2 * F, H);
+      const Seg sg = sm.seg[M_GU];
       for (int i = tid; i < (sg.r1 - sg.r0) / 2; i += kCons)
-        p.a[sg.r0 / 2 + i] = gelu_tanh(sm.seg_out[2 * i]) * sm.seg_out[2 * i + 1];
+        ll_st(p.a + sg.r0 / 2 + i, gelu_tanh(sm.seg_out[2 * i]) * sm.seg_out[2 * i + 1], ep);
     }
-    if (!(ok = grid_sync(fail))) break;
+    if (!(ok = phase_end(fail))) break;
     // ---- down projection
-    load_input(F, p.a);
-    gemv_phase(H, F, EPI_STORE, p.d, cur);
-    ok = grid_sync(fail);
+    load_input(F, p.a, ep, fail);
+    gemv_phase(M_DOWN, F, EPI_STORE, p.d, cur);
+    ok = phase_end(fail);
   }
   if (!ok) {
     // a CTA that leaves early must still let its K/V copy land
@@ -951,8 +1151,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(Params p) {
     return;
   }
   // ---- final norm + tied lm_head with argmax
-  residual_norm(H, p.xb, p.d, sm.layers[p.n_layers - 1].post_ffn, p.final_norm, nullptr);
-  gemv_phase(p.V, H, EPI_ARGMAX, nullptr, cur);
+  residual_norm(H, p.d, e0 + p.n_layers - 1, sm.layers[p.n_layers - 1].post_ffn, p.final_norm, false, fail);
+  gemv_phase(M_HEAD, H, EPI_ARGMAX, nullptr, cur);
   {
     const int lane = tid & 31, warp = tid >> 5;
     unsigned long long key = 0ull;
@@ -969,22 +1169,30 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(Params p) {
       key = o > key ? o : key;
     }
     if (lane == 0) sm.best[warp] = key;
-    cons_sync();
-    if (tid == 0) {
-      unsigned long long k2 = 0;
-      for (int w = 0; w < kCons / 32; ++w) k2 = sm.best[w] > k2 ? sm.best[w] : k2;
-      if (k2) atomicMax(p.keys, k2);
-    }
   }
-  if (!grid_sync(fail)) return;
-  if (lead && tid == 0) {
-    const unsigned long long k2 = __ldcg(p.keys);
-    const int32_t t = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(k2 & 0xFFFFFFFFull));
-    const int np = pos + 1;
-    p.tok[0] = t;
-    p.cur[0] = t;
-    p.pos[0] = np;
-    if (p.history && np < p.hist_len) p.history[np] = t;
+  if (!phase_end(fail)) return;
+  if (tid == 0) {
+    // the step's argmax key; the CTA whose count completes the step decodes
+    // the token (every other CTA's atomicMax is ordered before its count)
+    trace_stamp(p, TR_ARRIVE);
+    unsigned long long k2 = 0;
+    for (int w = 0; w < kCons / 32; ++w) k2 = sm.best[w] > k2 ? sm.best[w] : k2;
+    if (k2) atomicMax(p.kmax, k2);
+    __threadfence();
+    const unsigned long long old = atomicAdd(p.ctr, 1ull);
+    trace_stamp(p, TR_EXIT);
+    if ((old + 1) % gridDim.x == 0) {
+      __threadfence();
+      const unsigned long long kf = atomicExch(p.kmax, 0ull);  // read, and clear for the next step
+      *p.keys = kf;
+      const int32_t t = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(kf & 0xFFFFFFFFull));
+      const int np = pos + 1;
+      p.tok[0] = t;
+      p.cur[0] = t;
+      p.pos[0] = np;
+      if (p.history && np < p.hist_len) p.history[np] = t;
+      atomicAdd(p.bar + 4, 1u);  // the next launch's epochs
+    }
   }
 }
 
@@ -1011,8 +1219,9 @@ extern "C" size_t sb_decode_step_fused_scratch_size(int hidden, int n_heads, int
   if (head_dim != HD || n_heads < 1 || n_heads > kMaxHeads || max_seq < 1 || max_seq > CKA * kMaxChunks) return 0;
   const size_t qd = static_cast<size_t>(n_heads) * HD;
   const size_t chunks = (static_cast<size_t>(max_seq) + CKA - 1) / CKA;
-  const size_t floats = 2 * hidden + (qd + 2 * HD) + qd + hidden + inter + hidden + chunks * n_heads * (HD + 2);
-  return kHeaderBytes + floats * sizeof(float);
+  // epoch-tagged 64-bit words: q|k|v, attention out, o, GEGLU out, down, chunk partials
+  const size_t words = (qd + 2 * HD) + qd + hidden + inter + hidden + chunks * n_heads * (HD + 2);
+  return kHeaderBytes + words * sizeof(uint64_t);
 }
 
 extern "C" int sb_decode_step_fused(const void* layers_dev, int n_layers, const void* emb, const void* emb_scales,
@@ -1037,9 +1246,11 @@ extern "C" int sb_decode_step_fused(const void* layers_dev, int n_layers, const 
   const int smem = static_cast<int>(sizeof(Smem));
   const int grid = grid_size(smem);
   if (grid < 1) return sb::fail(SB_ERR_CUDA, "sb_decode_step_fused: cannot place one CTA per SM");
-  // each CTA's gate|up slice must fit the GEGLU staging buffer
-  const int per = ((2 * inter + grid - 1) / grid + 1) & ~1;
+  // each CTA's gate|up slice must fit the GEGLU staging buffer, and every CTA
+  // must own gate|up rows (what makes buffer reuse across layers safe)
+  const int per = 2 * ((inter + grid - 1) / grid);
   SB_CHECK_ARG(per <= kSegOut, "sb_decode_step_fused: inter=%d too large for %d SMs", inter, grid);
+  SB_CHECK_ARG(inter >= grid, "sb_decode_step_fused: inter=%d must be at least the CTA count %d", inter, grid);
   Params p{};
   p.layers = static_cast<const Layer*>(layers_dev);
   p.n_layers = n_layers;
@@ -1063,16 +1274,15 @@ extern "C" int sb_decode_step_fused(const void* layers_dev, int n_layers, const 
   p.keys = reinterpret_cast<unsigned long long*>(keys);
   p.err = sb::device_error_word();
   char* base = static_cast<char*>(scratch);
+  // header: u64 step count at byte 0, u32 abort flag at 8, trace switch at 12
+  // (set by the caller), completed launches at 16, u64 running argmax key at 24
   p.ctr = reinterpret_cast<unsigned long long*>(base);
   p.bar = reinterpret_cast<unsigned int*>(base);
-  // the trace region is used only when the u32 at byte 12 (set by the caller) is non-zero
+  p.kmax = reinterpret_cast<unsigned long long*>(base + 24);
+  // the trace region is used only when the u32 at byte 12 is non-zero
   p.trace = reinterpret_cast<unsigned long long*>(base + 64);
-  float* f = reinterpret_cast<float*>(base + kHeaderBytes);
+  uint64_t* f = reinterpret_cast<uint64_t*>(base + kHeaderBytes);
   const size_t qd = static_cast<size_t>(n_heads) * HD;
-  p.xa = f;
-  f += hidden;
-  p.xb = f;
-  f += hidden;
   p.qkv = f;
   f += qd + 2 * HD;
   p.attn = f;

@@ -155,7 +155,7 @@ struct Smem {
   float qn[HD], kn[HD];      // q / k norm weights
   float cs[HD / 2], sn[HD / 2];  // RoPE row of this position
   float kpos[HD], vpos[HD];  // k and v of this position
-  float ps[kMaxHeads][CKA];  // chunk softmax numerators
+  float ps[CKA][kMaxHeads];  // chunk softmax numerators, key-major (a key's heads in two float4)
   float red[2][kRed];
   float seg_out[kSegOut];
   float resid[kMaxH];        // this CTA's copy of the residual stream
@@ -856,8 +856,8 @@ __device__ void attn_chunk(const Params& p, Smem& sm, int c, int pos, uint32_t e
     const float p1 = v1 ? expf(sc[1] - m) : 0.f;
     const float l = warp_sum((lane & 3) ? 0.f : p0 + p1);
     if (!(lane & 3)) {
-      sm.ps[h][key] = p0;
-      sm.ps[h][key + 8] = p1;
+      sm.ps[key][h] = p0;
+      sm.ps[key + 8][h] = p1;
     }
     if (lane == 0) ll_st2(p.part + (static_cast<size_t>(c) * nh + h) * (HD + 2) + HD, m, l, ep);
   }
@@ -869,16 +869,21 @@ __device__ void attn_chunk(const Params& p, Smem& sm, int c, int pos, uint32_t e
     float acc[kMaxHeads];
 #pragma unroll
     for (int h = 0; h < kMaxHeads; ++h) acc[h] = 0.f;
-    // rolled: this code runs once per layer, and straight-line code costs
-    // instruction fetches from L2 every time
+    // two keys per iteration, each key's eight numerators in two broadcast
+    // float4 loads; kept rolled (this code runs once per layer, and straight-
+    // line code costs instruction fetches from L2 every time).  A key past nt
+    // has numerator 0 and its V row is not read.
+    static_assert(kMaxHeads == 8, "a key's numerators are two float4");
 #pragma unroll 1
-    for (int t = 0; t < CKA; ++t) {
-      if (t < nt) {
-        const float vv = sm.kv[1][t][dcol];
+    for (int t = 0; t < nt; t += 2) {
+      const float v0 = sm.kv[1][t][dcol];
+      const float v1 = t + 1 < nt ? sm.kv[1][t + 1][dcol] : 0.f;
+      const float4* p4 = reinterpret_cast<const float4*>(&sm.ps[t][0]);
+      const float4 a0 = p4[0], a1 = p4[1], b0 = p4[2], b1 = p4[3];
+      const float pa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float pb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-        for (int h = 0; h < kMaxHeads; ++h)
-          if (h < nh) acc[h] = fmaf(sm.ps[h][t], vv, acc[h]);
-      }
+      for (int h = 0; h < kMaxHeads; ++h) acc[h] = fmaf(pb[h], v1, fmaf(pa[h], v0, acc[h]));
     }
 #pragma unroll
     for (int h = 0; h < kMaxHeads; ++h)

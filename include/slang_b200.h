@@ -459,8 +459,11 @@ typedef struct sb_decode_layer {
  * Requirements: head_dim 256, n_heads <= 8, hidden, inter, n_heads*256 <= 6144
  * and multiples of 32, f16 group-32 scales.  layers_dev: device array of
  * n_layers sb_decode_layer.  scratch: >= sb_decode_step_fused_scratch_size()
- * bytes, zero-filled before the first call (later calls leave it reusable);
- * keys receives the lm_head key as in sb_lmhead_argmax.
+ * bytes, zero-filled before the first call (later calls leave it reusable; it
+ * holds the step count that tags the phase outputs, so steps sharing one
+ * scratch must not overlap on the GPU, and after SB_ERR_TIMEOUT it is zeroed
+ * again); inter >= the SM count; keys receives the lm_head key as in
+ * sb_lmhead_argmax.
  */
 int sb_decode_step_fused(const void* layers_dev, int n_layers, const void* emb, const void* emb_scales,
                          const float* final_norm, const float* cos_t, const float* sin_t, int hidden,

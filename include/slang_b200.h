@@ -271,6 +271,18 @@ int sb_gemm_q4_argmax(const void* a, const void* w, const void* scales, int scal
 int sb_gemm_q4_trace(uint64_t* buf, size_t bytes);
 
 /*
+ * Profiling hook of the fused prefill attention kernel (no reference
+ * counterpart): while `buf` is set (NULL turns it off), every launch whose grid
+ * fits in `bytes` writes 24 u64 per CTA at buf[24 * b] (b = the CTA's linear
+ * grid index; CTAs past their tile's last chunk write nothing): [0] its SM,
+ * %globaltimer stamps [1] entry, [2] set-up done, [3] Q tile landed, [4] O
+ * final, [5] epilogue stores issued, [6] exit, [7] its key-block count, then
+ * per key block j < 8: [8 + j] scores readable, [16 + j] P written.  For
+ * measurement only; buf must stay valid.
+ */
+int sb_attn_prefill_trace(uint64_t* buf, size_t bytes);
+
+/*
  * sb_gemm_q4 without a caller workspace; it allocates nothing.  No counterpart
  * in the reference: it is for callers that cannot allocate device memory --
  * a host reaching the GPU only through this C ABI, with no CUDA allocator of

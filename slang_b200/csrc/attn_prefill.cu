@@ -99,7 +99,27 @@ struct Params {
   int s_len;  // S (keys = queries' tokens)
   int kpc;    // key blocks per chunk (a CTA's share of a tile's key range)
   int maxc;   // chunks of the longest tile (grid.y)
+  unsigned long long* trace;  // profiling only: kAttnTraceSlots %globaltimer stamps per CTA, or null
 };
+
+// Profiling stamps (sb_attn_prefill_trace): slot i of CTA b (linear grid index)
+// is trace[b * kAttnTraceSlots + i].
+enum {
+  AT_SMID = 0,      // the SM the CTA ran on
+  AT_ENTRY = 1,     // first instruction
+  AT_SETUP = 2,     // barriers initialised, TMEM allocated
+  AT_QFULL = 3,     // MMA issuer: the Q tile landed
+  AT_OFINAL = 4,    // softmax warp 2: O final (the last P.V done)
+  AT_EPI_END = 5,   // softmax warp 2: output or partial stores issued
+  AT_EXIT = 6,      // TMEM released
+  AT_NB = 7,        // key blocks of this CTA (a count, not a time)
+  AT_S0 = 8,        // softmax warp 2: S_j readable (j = 0..7 at slots 8..15)
+  AT_P0 = 16,       // softmax warp 2: P_j written (slots 16..23)
+  kAttnTraceSlots = 24
+};
+__device__ __forceinline__ void attn_stamp(const Params& p, int slot) {
+  if (p.trace) p.trace[(blockIdx.x + static_cast<size_t>(gridDim.x) * blockIdx.y) * kAttnTraceSlots + slot] = sbd::global_ns();
+}
 
 // Key blocks that query tile `tile` sees.
 __host__ __device__ __forceinline__ int tile_key_blocks(int tile, int rows, int nh, int s_len) {
@@ -147,6 +167,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   if (static_cast<int>(blockIdx.y) >= nchunks) return;  // the whole CTA, before any barrier
   const int kb_lo = blockIdx.y * p.kpc;
   const int nb = min(p.kpc, nb_all - kb_lo);  // key blocks of this chunk: kb_lo + [0, nb)
+  if (threadIdx.x == 0 && p.trace) {
+    attn_stamp(p, AT_ENTRY);
+    uint32_t sm;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+    const size_t b = blockIdx.x + static_cast<size_t>(gridDim.x) * blockIdx.y;
+    p.trace[b * kAttnTraceSlots + AT_SMID] = sm;
+    p.trace[b * kAttnTraceSlots + AT_NB] = static_cast<unsigned long long>(nb);
+  }
 
   if (threadIdx.x == 0) {
     sbd::mbar_init(&bars->q_full, 1);
@@ -180,6 +208,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   sbd::tc_fence_after();
   const uint32_t tmem = bars->tmem_slot;
   bool mma_issued = false;
+  if (threadIdx.x == 0) attn_stamp(p, AT_SETUP);
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -221,6 +250,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       constexpr uint32_t idesc_o = sbd::umma_idesc_f16(QR, HD, 0, 1);
       const uint32_t qbase = sbd::smem_u32(smem);
       bool ok = sbd::mbar_wait(&bars->q_full, 0, abort, p.err);
+      attn_stamp(p, AT_QFULL);
       for (int j = 0; j <= nb && ok; ++j) {
         if (j < nb) {
           // S_j = Q K_j^T
@@ -284,6 +314,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       if (!ok) break;
       sbd::tc_fence_after();
       uint32_t sv[2][32];
+      if (threadIdx.x == 64 && j < 8) attn_stamp(p, AT_S0 + j);
       sbd::tmem_ld_32x32b_x32(lane_base + TM_S + st * KB, sv[0]);
       sbd::tmem_ld_32x32b_x32(lane_base + TM_S + st * KB + 32, sv[1]);
       sbd::tmem_wait_ld();
@@ -357,33 +388,54 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       sbd::tc_fence_before();
       __syncwarp();
       if (lane == 0) sbd::mbar_arrive(&bars->p_full[st]);
+      if (threadIdx.x == 64 && j < 8) attn_stamp(p, AT_P0 + j);
     }
     // ------------------------------------------------------------ epilogue: O / l -> f16
     if (ok) ok = __all_sync(0xFFFFFFFFu, sbd::mbar_wait(&bars->o_final, 0, abort, p.err));
+    if (threadIdx.x == 64) attn_stamp(p, AT_OFINAL);
     // the row sum is the two halves' parts (every softmax warp meets this barrier)
     float* lx = reinterpret_cast<float*>(smem + C::OFF_L);
     lx[half * QR + row] = l;
     sbd::named_bar_sync(1, 8 * 32);
     const float l_row = lx[row] + lx[QR + row];
-    if (ok && nchunks > 1) {
-      // a share of a split tile: unnormalised O with its running max and sum
+    if (nchunks > 1) {
+      // A share of a split tile: unnormalised O with its running max and sum.
+      // The tile's 128 partial rows are one contiguous block of the
+      // workspace, so they are laid out in shared memory (the Q / K / V
+      // buffers are idle now: every MMA completed before o_final) and written
+      // with one bulk copy -- stores of a thread's own row from registers
+      // would scatter across 32 rows per instruction.
+      constexpr int PS = part_stride<HD>();
+      static_assert(QR * PS * 4 <= OFF_V + 2 * KV_BYTES, "the partial tile must fit the Q / K / V buffers");
+      float* stile = reinterpret_cast<float*>(smem);
       sbd::tc_fence_after();
-      float* dst = p.part + ((static_cast<size_t>(tile) * p.maxc + blockIdx.y) * QR + row) * part_stride<HD>();
-      for (int cc = 0; cc < HD / 64; ++cc) {
-        const int col = half * (HD / 2) + cc * 32;
-        uint32_t ov[32];
-        sbd::tmem_ld_32x32b_x32(lane_base + TM_O + col, ov);
+      // two 32-column TMEM loads in flight per wait
+      for (int cc = 0; cc < HD / 64; cc += 2) {
+        uint32_t ov[2][32];
+        sbd::tmem_ld_32x32b_x32(lane_base + TM_O + half * (HD / 2) + cc * 32, ov[0]);
+        if (cc + 1 < HD / 64) sbd::tmem_ld_32x32b_x32(lane_base + TM_O + half * (HD / 2) + cc * 32 + 32, ov[1]);
         sbd::tmem_wait_ld();
-        if (!row_ok) continue;
 #pragma unroll
-        for (int e = 0; e < 32; e += 4)
-          *reinterpret_cast<float4*>(dst + col + e) =
-              make_float4(__uint_as_float(ov[e]), __uint_as_float(ov[e + 1]), __uint_as_float(ov[e + 2]),
-                          __uint_as_float(ov[e + 3]));
+        for (int u = 0; u < 2; ++u) {
+          if (cc + u >= HD / 64) break;
+          const int col = half * (HD / 2) + (cc + u) * 32;
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(stile + row * PS + col + e) =
+                make_float4(__uint_as_float(ov[u][e]), __uint_as_float(ov[u][e + 1]), __uint_as_float(ov[u][e + 2]),
+                            __uint_as_float(ov[u][e + 3]));
+        }
       }
-      if (row_ok && half == 0) {
-        dst[HD] = m_used;
-        dst[HD + 1] = l_row;
+      if (half == 0)
+        *reinterpret_cast<float4*>(stile + row * PS + HD) = make_float4(m_used, l_row, 0.f, 0.f);
+      sbd::fence_proxy_async_smem();  // these generic-proxy writes feed the bulk copy
+      // each lane quadrant's 32 rows (its two warps) go out as soon as both wrote them
+      sbd::named_bar_sync(2 + quad, 2 * 32);
+      if (half == 0 && lane == 0 && ok) {
+        const size_t rq = static_cast<size_t>(quad) * 32 * PS;
+        float* dst = p.part + (static_cast<size_t>(tile) * p.maxc + blockIdx.y) * QR * PS + rq;
+        sbd::bulk_store(dst, stile + rq, 32 * PS * 4);
+        sbd::bulk_store_wait_read();  // before the CTA's shared memory is released
       }
     } else if (ok) {
       sbd::tc_fence_after();
@@ -408,6 +460,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         }
       }
     }
+    if (threadIdx.x == 64) attn_stamp(p, AT_EPI_END);
   }
 
   sbd::tc_fence_before();
@@ -415,6 +468,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   if (warp == 1) {
     sbd::tc_fence_after();
     sbd::tmem_dealloc(tmem, TM_COLS);
+    if (lane == 0) attn_stamp(p, AT_EXIT);
   }
 }
 
@@ -485,6 +539,10 @@ int choose_kpc(int rows, int nh, int s_len, int* maxc) {
   return kpc;
 }
 
+// Profiling buffer of sb_attn_prefill_trace (null: off) and its size in stamps.
+static unsigned long long* g_attn_trace = nullptr;
+static size_t g_attn_trace_slots = 0;
+
 template <int HD>
 int launch_attn(const void* q16, const void* k16, const void* v16, void* out16, int s_len, int n_heads, float* part,
                 size_t part_bytes, cudaStream_t stream) {
@@ -523,6 +581,7 @@ int launch_attn(const void* q16, const void* k16, const void* v16, void* out16, 
     }
   }
   p.maxc = maxc;
+  if (g_attn_trace && static_cast<size_t>(tiles) * maxc * kAttnTraceSlots <= g_attn_trace_slots) p.trace = g_attn_trace;
   cudaError_t e = sb::launch_pdl(attn_prefill_kernel<HD>, dim3(tiles, maxc), dim3(WARPS * 32), C::SMEM, stream, tq,
                                  tk, tv, p);
   if (e != cudaSuccess) return sb::cuda_fail(e, "attn_prefill_kernel");
@@ -554,6 +613,13 @@ static int attn_prefill_impl(const void* q16, const void* k16, const void* v16, 
     case 128: return launch_attn<128>(q16, k16, v16, out16, s_len, n_heads, part, workspace_bytes, s);
     default: return launch_attn<256>(q16, k16, v16, out16, s_len, n_heads, part, workspace_bytes, s);
   }
+}
+
+extern "C" int sb_attn_prefill_trace(uint64_t* buf, size_t bytes) {
+  SB_CHECK_ARG(!buf || sb::aligned(buf, 8), "sb_attn_prefill_trace: buffer must be 8-byte aligned");
+  g_attn_trace = buf ? reinterpret_cast<unsigned long long*>(buf) : nullptr;
+  g_attn_trace_slots = buf ? bytes / sizeof(uint64_t) : 0;
+  return SB_OK;
 }
 
 extern "C" int sb_attn_prefill(const void* q16, const void* k16, const void* v16, void* out16, int s_len,

@@ -134,6 +134,19 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 }
 // L2 policy for data read exactly once per step (weight streams): evicted
 // first, so activations, norm weights and KV caches stay resident in L2.
+// Bulk store shared -> global (both 16-byte aligned, bytes % 16 == 0) in this
+// thread's bulk group; bulk_store_wait_read() returns once the source may be
+// overwritten (the writes themselves land by the kernel's end).
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)),
+               "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));

@@ -508,24 +508,37 @@ __device__ __forceinline__ void epilogue_direct(const GemmParams& p, uint32_t la
     } else if (p.geglu) {
       // lanes 2i, 2i + 1 hold gate and up of output feature feat / 2, rounded
       // to f16 as the GEMM output would be; the even lane forms gelu(gate) * up
-      // for tokens col .. col + 15, the odd lane for col + 16 .. col + 31
+      // for tokens col .. col + 15, the odd lane for col + 16 .. col + 31.  A
+      // lane rounds its two values (tokens j, 16 + j) with one packed
+      // conversion and swaps the pair with its partner in one shuffle.
       const bool odd = lane & 1;
+      const bool a1 = p.alpha == 1.f;
       __half* dst = static_cast<__half*>(p.c) + static_cast<size_t>(t0 + col + (odd ? 16 : 0)) * p.ldc + (feat >> 1);
       const int jt = t0 + col + (odd ? 16 : 0);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const float lo = __half2float(__float2half_rn(p.alpha * __uint_as_float(v[j])));
-        const float hi = __half2float(__float2half_rn(p.alpha * __uint_as_float(v[16 + j])));
-        const float other = __shfl_xor_sync(0xFFFFFFFFu, odd ? lo : hi, 1);
-        const float g = odd ? other : lo, u = odd ? hi : other;
+        const float x0 = __uint_as_float(v[j]), x1 = __uint_as_float(v[16 + j]);
+        const __half2 h = a1 ? __floats2half2_rn(x0, x1) : __floats2half2_rn(p.alpha * x0, p.alpha * x1);
+        const uint32_t hu = *reinterpret_cast<const uint32_t*>(&h);
+        const uint32_t ou = __shfl_xor_sync(0xFFFFFFFFu, hu, 1);
+        const __half2 o2 = *reinterpret_cast<const __half2*>(&ou);
+        const float g = odd ? __high2float(o2) : __low2float(h);
+        const float u = odd ? __high2float(h) : __low2float(o2);
         if (feat_ok && jt + j < p.m) dst[static_cast<size_t>(j) * p.ldc] = __float2half_rn(sbd::gelu_tanh(g) * u);
       }
     } else {
       if (!feat_ok) continue;
       __half* dst = static_cast<__half*>(p.c) + static_cast<size_t>(t0 + col) * p.ldc + feat;
+      if (p.alpha == 1.f) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (t0 + col + j < p.m) dst[static_cast<size_t>(j) * p.ldc] = __float2half_rn(p.alpha * __uint_as_float(v[j]));
+        for (int j = 0; j < 32; ++j)
+          if (t0 + col + j < p.m) dst[static_cast<size_t>(j) * p.ldc] = __float2half_rn(__uint_as_float(v[j]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (t0 + col + j < p.m)
+            dst[static_cast<size_t>(j) * p.ldc] = __float2half_rn(p.alpha * __uint_as_float(v[j]));
+      }
     }
   }
 }

@@ -65,7 +65,7 @@ def parse():
     ap.add_argument("--kernel", default="",
                     choices=["", "gemm_q4", "gemm_q4_geglu", "gemm_f16", "gemv", "lmhead", "attn", "attn_decode", "gemv_q8",
                              "gemv_bf16", "ple_block", "prefill",
-                             "decode", "decode_fused", "decode_batch", "decode_trace", "gemm_trace"],
+                             "decode", "decode_fused", "decode_batch", "decode_trace", "gemm_trace", "attn_trace"],
                     help="run one kernel --iters times on a single shape and exit (for ncu captures)")
     ap.add_argument("--shape", default="6144,1536", help="N,K of the weight for --kernel")
     ap.add_argument("--m", type=int, default=1024, help="rows of the activation for --kernel")
@@ -180,6 +180,81 @@ def run_decode_trace(args):
         if ph in stats:
             print(f"  {ph:9s} " + "  ".join(f"{m} {np.mean(v) / 1e3:.2f} ({np.max(v) / 1e3:.2f})"
                                              for m, v in stats[ph].items()))
+
+
+def run_attn_trace(args):
+    """Where the time of the fused causal prefill attention goes, from its own
+    %globaltimer stamps (sb_attn_prefill_trace): --m tokens, 8 query heads of
+    256 on one K/V head.  Prints the split (kernel + merge) and unsplit times
+    from CUDA graphs of back-to-back launches, then for one traced launch the
+    start of each phase over CTAs (entry, set-up, Q landed, first scores, first
+    P written, O final, epilogue end, exit), the per-key-block softmax time and
+    gap, and the exit time by a CTA's key-block count."""
+    import numpy as np
+    import torch
+
+    from slang_b200 import _lib
+    from slang_b200 import kernels as kern
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    S, nh, hd = args.m, 8, 256
+    q = (torch.randn((S, nh, hd), device=dev, generator=g) * 0.2).half()
+    k = (torch.randn((S, hd), device=dev, generator=g) * 0.2).half()
+    v = torch.randn((S, hd), device=dev, generator=g).half()
+    out = torch.empty((S, nh, hd), dtype=torch.float16, device=dev)
+
+    def graph_us(fn, reps=20):
+        st = torch.cuda.Stream()
+        fn()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=st):
+            for _ in range(reps):
+                fn()
+        gr.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    print(f"attention S={S}, {nh} heads x {hd}: split (kernel + merge) "
+          f"{graph_us(lambda: kern.attn_prefill(q, k, v, out)):.2f} us, unsplit "
+          f"{graph_us(lambda: kern.attn_prefill(q, k, v, out, split=False)):.2f} us per launch in a CUDA graph of 20")
+    slots = 24  # attn_prefill.cu kAttnTraceSlots
+    tiles = (S * nh + 127) // 128
+    tr = torch.zeros(tiles * 8 * slots, dtype=torch.int64, device=dev)
+    lib = _lib.load()
+    lib.sb_attn_prefill_trace(tr.data_ptr(), tr.numel() * 8)
+    kern.attn_prefill(q, k, v, out)
+    torch.cuda.synchronize()
+    lib.sb_attn_prefill_trace(None, 0)
+    t = tr.view(-1, slots).cpu().numpy().astype(np.float64)
+    rows = t[t[:, 1] > 0]
+    e0 = rows[:, 1].min()
+    print(f"one traced launch: {len(rows)} CTAs; phase start over CTAs, us after the first entry: min / median / max")
+    for nm, c in (("entry", 1), ("set-up", 2), ("Q landed", 3), ("first scores", 8), ("first P", 16),
+                  ("O final", 4), ("epilogue end", 5), ("exit", 6)):
+        x = (rows[:, c][rows[:, c] > 0] - e0) / 1e3
+        print(f"  {nm:13s} {x.min():7.2f} {np.median(x):7.2f} {x.max():7.2f}")
+    nb = rows[:, 7].astype(int)
+    soft, gap = [], []
+    for r, n in zip(rows, nb):
+        for j in range(min(n, 8)):
+            if r[8 + j] > 0 and r[16 + j] > 0:
+                soft.append((r[16 + j] - r[8 + j]) / 1e3)
+            if j + 1 < min(n, 8) and r[8 + j + 1] > 0:
+                gap.append((r[8 + j + 1] - r[16 + j]) / 1e3)
+    print(f"  per key block: softmax {np.median(soft):.2f} us, P_j -> scores j+1 {np.median(gap):.2f} us; "
+          f"O final -> epilogue end {np.median((rows[:, 5] - rows[:, 4]) / 1e3):.2f} us (medians; the timer ticks 0.256 us)")
+    for n in sorted(set(nb.tolist())):
+        sel = rows[nb == n]
+        x = (sel[:, 6] - e0) / 1e3
+        print(f"  {n} key blocks: {len(sel)} CTAs, exit median {np.median(x):.2f} max {x.max():.2f} us")
+    kern.device_status()
 
 
 def run_gemm_trace(args):
@@ -297,6 +372,8 @@ def run_kernel_case(args):
         return run_decode_trace(args)
     if args.kernel == "gemm_trace":
         return run_gemm_trace(args)
+    if args.kernel == "attn_trace":
+        return run_attn_trace(args)
     if args.kernel in ("prefill", "decode", "decode_fused", "decode_batch"):
         return run_model_case(args)
     from slang_b200 import kernels as kern

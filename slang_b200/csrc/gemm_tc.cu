@@ -99,6 +99,10 @@ struct GemmParams {
   float alpha;
   long long plane;     // f16 kernel, f32 C: elements between the output planes of K splits (blockIdx.z)
   unsigned long long* trace;  // pair kernel, profiling only: kTraceSlots %globaltimer stamps per CTA, or null
+  // persistent pair kernel: `pt_pairs` CTA pairs take contiguous runs of the
+  // `pt_wtp` weight-row pairs x `pt_ttiles` token tiles (tile = wp * ttiles + tt)
+  int pt_pairs, pt_wtp, pt_ttiles;
+  int pt_kbc;  // k-blocks per scale tile (scale reload points at multiples of it)
 };
 
 // Profiling stamps of the pair kernel (sb_gemm_q4_trace): slot i of CTA b is
@@ -116,6 +120,10 @@ enum {
   TS_EPI_END = 9,    // epilogue warp 2: its stores (or partial stash) issued
   TS_REDUCED = 10,   // epilogue warp 2: cluster split reduction done
   TS_EXIT = 11,      // TMEM released
+  TS_PT_ISSUED0 = 12,  // persistent kernel: MMA issuer, the first tile's MMAs all issued
+  TS_PT_FREED0 = 13,   // persistent kernel: epilogue warp 2, first tile's accumulator released
+  TS_PT_MMA1 = 14,     // persistent kernel: MMA issuer, the second tile's first MMA
+  TS_PT_ACCUM1 = 15,   // persistent kernel: epilogue warp 2, the second tile's accumulator final
   kTraceSlots = 16
 };
 __device__ __forceinline__ void gemm_stamp(const GemmParams& p, int slot) {
@@ -1007,6 +1015,331 @@ __global__ void __launch_bounds__(P_WARPS * 32, 1)
   }
 }
 
+// ---- persistent form of the pair kernel (gemm_q4_persist_kernel)
+// For a matrix with more 256 x 256 tiles than the device holds CTA pairs, one
+// launch runs one pair per pair slot, and pair p takes the contiguous tiles
+// [T p / P, T (p + 1) / P) (tile = weight-row pair wp * token tiles + tt).  The
+// rings of the pair kernel run on from tile to tile, and a tile's epilogue
+// overlaps the next tile's MMAs: at a tile boundary the dequant warps load the
+// next tile's scales and dequantise its first P_STAGES k-blocks (into A slots
+// the finishing MMAs free), then read the finished accumulator into registers,
+// release it (the MMA issuer starts the next tile on `accfree`, its first
+// stages already full) and only then form and store the outputs.  The MMA
+// issuer keeps its ring position incrementally: between two MMAs it runs only
+// what the next MMA needs.
+struct PtBars {
+  PairBars pb;
+  uint64_t accfree;  // even CTA: both CTAs' epilogue warps have read the accumulator
+};
+static_assert(sizeof(PtBars) <= 512, "persistent barrier block");
+
+// 32 token columns c0 .. c0 + 31 of output feature `feat` (this lane's weight
+// row) -> C, from h[j] = (f16(alpha * sum_j), f16(alpha * sum_{16 + j})): the
+// values epilogue_direct forms (the outputs, or for GEGLU the rounded gate / up
+// that lanes 2i, 2i + 1 hold for output feature feat / 2; the even lane writes
+// gelu(gate) * up for columns c0 .. c0 + 15, the odd lane for c0 + 16 .. + 31).
+__device__ __forceinline__ void pt_store_cols(const GemmParams& p, const uint32_t (&h)[16], int feat, int lane,
+                                              int c0) {
+  const bool feat_ok = feat < p.n;
+  if (p.geglu) {
+    const bool odd = lane & 1;
+    __half* dst = static_cast<__half*>(p.c) + static_cast<size_t>(c0 + (odd ? 16 : 0)) * p.ldc + (feat >> 1);
+    const int jt = c0 + (odd ? 16 : 0);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t ou = __shfl_xor_sync(0xFFFFFFFFu, h[j], 1);
+      const __half2 mine = *reinterpret_cast<const __half2*>(&h[j]);
+      const __half2 o2 = *reinterpret_cast<const __half2*>(&ou);
+      const float g = odd ? __high2float(o2) : __low2float(mine);
+      const float u = odd ? __high2float(mine) : __low2float(o2);
+      if (feat_ok && jt + j < p.m) dst[static_cast<size_t>(j) * p.ldc] = __float2half_rn(sbd::gelu_tanh(g) * u);
+    }
+  } else if (feat_ok) {
+    __half* dst = static_cast<__half*>(p.c) + static_cast<size_t>(c0) * p.ldc + feat;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const __half2 hh = *reinterpret_cast<const __half2*>(&h[j]);
+      if (c0 + j < p.m) dst[static_cast<size_t>(j) * p.ldc] = __low2half(hh);
+      if (c0 + 16 + j < p.m) dst[static_cast<size_t>(16 + j) * p.ldc] = __high2half(hh);
+    }
+  }
+}
+
+// f16(alpha * v[j]), f16(alpha * v[16 + j]) packed for pt_store_cols
+__device__ __forceinline__ void pt_round(const GemmParams& p, const uint32_t (&v)[32], uint32_t (&h)[16]) {
+  const bool a1 = p.alpha == 1.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float x0 = __uint_as_float(v[j]), x1 = __uint_as_float(v[16 + j]);
+    const __half2 hh = a1 ? __floats2half2_rn(x0, x1) : __floats2half2_rn(p.alpha * x0, p.alpha * x1);
+    h[j] = *reinterpret_cast<const uint32_t*>(&hh);
+  }
+}
+
+// One tile's epilogue in the persistent kernel (the ti-th tile of this pair;
+// feat / tok: this thread's weight row and first token column): wait for the
+// accumulator, read this warp's 64 columns into registers (rounded to f16 as
+// stored), release the accumulator to the MMA issuer, then form and store the
+// outputs.  Returns the thread's ok flag (false after a failed wait).
+__device__ __forceinline__ bool pt_epilogue(const GemmParams& p, PairBars* bars, PtBars* pbars, uint32_t lane_addr,
+                                         int feat, int tok, int ti, bool lead, int dt, int lane, bool ok) {
+  volatile int* abort = &bars->abort;
+  if (ok) ok = sbd::mbar_wait_cluster(&bars->accum, ti & 1, abort, p.err);
+  ok = __all_sync(0xFFFFFFFFu, ok);
+  if (dt == 0 && ti <= 1) gemm_stamp(p, ti == 0 ? TS_ACCUM : TS_PT_ACCUM1);
+  sbd::tc_fence_after();
+  uint32_t h[2][16];  // the outputs rounded to f16 (as stored), so the registers held are halved
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    uint32_t a[32];
+    sbd::tmem_ld_32x32b_x32(lane_addr + 32 * u, a);
+    sbd::tmem_wait_ld();
+    pt_round(p, a, h[u]);
+  }
+  sbd::tc_fence_before();
+  sbd::named_bar_sync(1, Q_DQ_WARPS * 32);
+  if (dt == 0) {
+    if (lead) sbd::mbar_arrive(&pbars->accfree);
+    else sbd::mbar_arrive_remote_cta(sbd::mapa_shared(sbd::smem_u32(&pbars->accfree), 0));
+    if (ti == 0) gemm_stamp(p, TS_PT_FREED0);
+  }
+  if (ok) {
+    pt_store_cols(p, h[0], feat, lane, tok);
+    pt_store_cols(p, h[1], feat, lane, tok + 32);
+  }
+  if (dt == 0 && ti == 0) gemm_stamp(p, TS_EPI_END);
+  return ok;
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(P_WARPS * 32, 1)
+    gemm_q4_persist_kernel(const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ CUtensorMap tmW,
+                           const GemmParams p) {
+  constexpr int S = P_STAGES, NT = QT;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  PtBars* pbars = reinterpret_cast<PtBars*>(smem + P_OFF_BAR);
+  PairBars* bars = &pbars->pb;
+  volatile int* abort = &bars->abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = static_cast<int>(sbd::cluster_ctarank());  // cluster (2, 1, 1): 0 = even CTA
+  const bool lead = rank == 0;
+  constexpr uint16_t pair_mask = 3;
+  const int KB = p.kb_total;
+  const int tiles = p.pt_wtp * p.pt_ttiles;
+  const int t_first = static_cast<int>(static_cast<long long>(tiles) * blockIdx.y / p.pt_pairs);
+  const int t_end = static_cast<int>(static_cast<long long>(tiles) * (blockIdx.y + 1) / p.pt_pairs);
+  auto rows_of = [&](int t) { return (2 * (t / p.pt_ttiles) + rank) * QW; };  // this CTA's 128 weight rows
+  auto toks_of = [&](int t) { return (t % p.pt_ttiles) * NT; };              // the pair's 256 tokens
+  if (threadIdx.x == 0 && p.trace) {
+    gemm_stamp(p, TS_ENTRY);
+    uint32_t sm;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+    p.trace[(blockIdx.x + static_cast<size_t>(gridDim.x) * blockIdx.y) * kTraceSlots + TS_SMID] = sm;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      sbd::mbar_init(&bars->ready[i], 1 + 8 + 8);
+      sbd::mbar_init(&bars->empty[i], 1);
+      sbd::mbar_init(&bars->pfull[i], 1);
+      sbd::mbar_init(&bars->pempty[i], 8);
+    }
+    sbd::mbar_init(&bars->accum, 1);
+    sbd::mbar_init(&pbars->accfree, 2);
+    bars->abort = 0;
+    sbd::fence_mbar_init();
+    sbd::fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    sbd::prefetch_tmap(&tmAct);
+    sbd::prefetch_tmap(&tmW);
+  }
+  if (warp == 1) {
+    sbd::tmem_alloc_pair(&bars->tmem_slot, Q_TMEM_COLS);
+    sbd::tmem_relinquish_pair();
+  }
+  sbd::tc_fence_before();
+  sbd::cluster_sync_all();
+  sbd::tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+  if (threadIdx.x == 0) gemm_stamp(p, TS_SETUP);
+  sbd::griddep_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ activation TMA producer (both CTAs)
+    if (lane == 0) {
+      sbd::griddep_wait();
+      gemm_stamp(p, TS_ACT_GO);
+      int it = 0;
+      bool ok = true;
+      for (int t = t_first; ok && t < t_end; ++t) {
+        const int th = toks_of(t) + rank * (NT / 2);
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it & (S - 1);
+          if (!sbd::mbar_wait_cluster(&bars->empty[s], ((it / S) & 1) ^ 1, abort, p.err)) {
+            ok = false;
+            break;
+          }
+          if (lead) sbd::mbar_arrive_expect_tx(&bars->ready[s], NT * BK * 2);
+          sbd::tma_load_2d_pair(&tmAct, sbd::mapa_shared(sbd::smem_u32(&bars->ready[s]), 0),
+                                smem + s * P_ACT_BYTES, kb * BK, th);
+        }
+      }
+      if (*abort && lead)
+        for (int i = max(0, it - S); i < it; ++i) drain_wait(&bars->ready[i & (S - 1)], (i / S) & 1);
+    }
+  } else if (warp == P_WLOAD) {
+    // ------------------------------------------------------------ packed-weight TMA producer (both CTAs)
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int t = t_first; ok && t < t_end; ++t) {
+        const int w0 = rows_of(t);
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it & (S - 1);
+          if (!sbd::mbar_wait(&bars->pempty[s], ((it / S) & 1) ^ 1, abort, p.err)) {
+            ok = false;
+            break;
+          }
+          sbd::mbar_arrive_expect_tx(&bars->pfull[s], QW * BK * BITS / 8);
+          sbd::tma_load_2d(&tmW, &bars->pfull[s], smem + P_OFF_PACK + s * Q_PACK_BYTES, kb * BK * BITS / 8, w0);
+        }
+      }
+      if (*abort)
+        for (int i = max(0, it - S); i < it; ++i) drain_wait(&bars->pfull[i & (S - 1)], (i / S) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (lane == 0 && lead) {
+      constexpr uint32_t idesc = sbd::umma_idesc_f16(2 * QW, NT, 0, 0);
+      constexpr int kStepDesc = (UMMA_K * 2) >> 4;  // 32 bytes along K, in descriptor units
+      const uint64_t bdesc0 = sbd::umma_desc(sbd::smem_u32(smem), 16, 1024, sbd::kLayoutSwizzle128B);
+      const uint32_t a0 = tmem + 256;
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = t_first, ti = 0; t < t_end; ++t, ++ti) {
+        // the accumulator is free once both CTAs' epilogue warps have read the previous tile's
+        if (ok && ti > 0) ok = sbd::mbar_wait_cluster(&pbars->accfree, (ti - 1) & 1, abort, p.err);
+        sbd::tc_fence_after();
+        if (ok) ok = sbd::mbar_wait_cluster(&bars->ready[s], ph, abort, p.err);
+        if (ti <= 1) gemm_stamp(p, ti == 0 ? TS_MMA0 : TS_PT_MMA1);
+        uint32_t acc = 0u;
+        for (int n = KB; ok && n > 0; --n) {
+          sbd::tc_fence_after();
+          const uint64_t bd = bdesc0 + static_cast<uint64_t>((s * P_ACT_BYTES) >> 4);
+          const uint32_t ad = a0 + s * 32;
+          const int s1 = (s + 1) & (S - 1);
+          const uint32_t ph1 = s1 == 0 ? ph ^ 1u : ph;
+          sbd::umma_f16_ts_pair(tmem, ad, bd, idesc, acc);
+          sbd::umma_f16_ts_pair(tmem, ad + 8, bd + kStepDesc, idesc, 1u);
+          sbd::umma_f16_ts_pair(tmem, ad + 16, bd + 2 * kStepDesc, idesc, 1u);
+          const bool next_ready = n == 1 || sbd::mbar_test_wait_cluster(&bars->ready[s1], ph1);
+          sbd::umma_f16_ts_pair(tmem, ad + 24, bd + 3 * kStepDesc, idesc, 1u);
+          sbd::umma_commit_pair(&bars->empty[s], pair_mask);
+          acc = 1u;
+          s = s1;
+          ph = ph1;
+          if (n > 1 && !next_ready && !sbd::mbar_wait_cluster(&bars->ready[s], ph, abort, p.err)) ok = false;
+        }
+        // (also after a failure: the epilogue warps' wait on `accum` then ends
+        // at once or on their own abort check)
+        sbd::umma_commit_pair(&bars->accum, pair_mask);
+        if (ti == 0) gemm_stamp(p, TS_PT_ISSUED0);
+      }
+      gemm_stamp(p, TS_MMA_END);
+    }
+  } else {
+    // ------------------------------------------------------------ dequant producers + epilogue (warps 2..17, both CTAs)
+    // Every one of these 512 threads walks the same tiles, scale tiles and
+    // epilogues and meets every named barrier, failures included (a failed
+    // wait only skips work), so no barrier waits on a thread that left.
+    constexpr int kDq = Q_DQ_WARPS * 32;
+    const int dw = warp - 2;
+    const int grp = dw >> 3;
+    const int quad = warp & 3;
+    const int khalf = (dw & 7) >> 2;
+    const int r = quad * 32 + lane;
+    const int dt = threadIdx.x - 64;
+    uint8_t* sct = smem + P_OFF_SCALE;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t ready_lead = sbd::mapa_shared(sbd::smem_u32(&bars->ready[0]), 0);
+    const int col0 = (dw >> 2) * 64;  // this warp's 64 token columns of its lane quadrant
+    // a group's scale index advances by gstep per k-block it takes (0: recomputed)
+    const int gstep = (Q_DQ_GROUPS * BK) % p.group == 0 ? Q_DQ_GROUPS * BK / p.group : 0;
+    bool ok = true;
+    auto epilogue = [&](int t, int ti) {
+      ok = pt_epilogue(p, bars, pbars, lane_addr + col0, rows_of(t) + r, toks_of(t) + col0, ti, lead, dt, lane, ok);
+    };
+    int it0 = 0;  // ring position of the tile's first k-block
+    for (int t = t_first, ti = 0; t < t_end; ++t, ++ti) {
+      const int w0 = rows_of(t);
+      // k-blocks of this tile dequantised before the previous tile's epilogue
+      // (the first scale tile covers them: pt_kbc >= P_STAGES or the whole tile)
+      const int E = min(S, KB);
+      bool epi = ti == 0;
+      for (int c_lo = 0; c_lo < KB;) {
+        // one scale tile: k-blocks [c_lo, the next multiple of pt_kbc or the tile end)
+        const int c_hi = min(KB, (c_lo / p.pt_kbc + 1) * p.pt_kbc);
+        const int g_lo = (c_lo * BK) / p.group;
+        const int g_hi = (c_hi * BK + p.group - 1) / p.group;
+        sbd::named_bar_sync(1, kDq);  // every dequant warp is done with the previous scale tile
+        load_scale_tile(p, sct, w0, g_lo, g_hi - g_lo, dt, kDq);
+        sbd::named_bar_sync(1, kDq);
+        int kb = c_lo + ((grp - (it0 + c_lo)) & 1);  // this group's first k-block here
+        int gi = (kb * BK + khalf * 32) / p.group - g_lo;
+        for (; kb < c_hi; kb += Q_DQ_GROUPS) {
+          if (!epi && kb >= E) {
+            epilogue(t - 1, ti - 1);
+            epi = true;
+          }
+          const int itk = it0 + kb;
+          const int s = itk & (S - 1);
+          const uint32_t ph = (itk / S) & 1;
+          if (gstep == 0) gi = (kb * BK + khalf * 32) / p.group - g_lo;
+          if (ok) ok = sbd::mbar_wait(&bars->pfull[s], ph, abort, p.err);
+          if (ok) ok = sbd::mbar_wait_cluster(&bars->empty[s], ph ^ 1, abort, p.err);
+          ok = __all_sync(0xFFFFFFFFu, ok);
+          if (ok) {
+            sbd::tc_fence_after();
+            constexpr int rowb = 8 * BITS, halfb = 4 * BITS;  // packed bytes of a row's k-block and of its half
+            const uint8_t* q = smem + P_OFF_PACK + s * Q_PACK_BYTES + r * rowb + khalf * halfb;
+            uint32_t o[16];
+            dq_group<BITS>(p, sct, gi, r, q, o);
+            sbd::tmem_st_32x32b_x16(lane_addr + 256 + s * 32 + khalf * 16, o);
+            sbd::tmem_wait_st();
+            sbd::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              sbd::mbar_arrive(&bars->pempty[s]);
+              if (lead) sbd::mbar_arrive(&bars->ready[s]);
+              else sbd::mbar_arrive_remote_cta(ready_lead + s * sizeof(uint64_t));
+            }
+          }
+          gi += gstep;
+        }
+        if (!epi && c_hi >= E) {  // a group with no k-block at or past E in this scale tile
+          epilogue(t - 1, ti - 1);
+          epi = true;
+        }
+        c_lo = c_hi;
+      }
+      it0 += KB;
+    }
+    if (t_end > t_first) epilogue(t_end - 1, t_end - 1 - t_first);
+  }
+
+  // both CTAs are done with TMEM (the pair's MMAs completed before `accum`)
+  sbd::tc_fence_before();
+  sbd::cluster_sync_all();
+  if (warp == 1) {
+    sbd::tc_fence_after();
+    sbd::tmem_dealloc_pair(tmem, Q_TMEM_COLS);
+    if (lane == 0) gemm_stamp(p, TS_EXIT);
+  }
+}
+
 __global__ void splitk_finalize_kernel(const float* __restrict__ ws, __half* __restrict__ c, int m, int n, int ldc,
                                        int splits, float alpha, int geglu) {
   sbd::griddep_launch_dependents();
@@ -1294,6 +1627,21 @@ static cudaError_t launch_pair(cudaLaunchConfig_t& cfg, const CUtensorMap& tact,
   return cudaLaunchKernelEx(&cfg, gemm_q4_pair_kernel<BITS, NT>, tact, tw, p);
 }
 
+template <int BITS>
+static cudaError_t launch_persist(cudaLaunchConfig_t& cfg, const CUtensorMap& tact, const CUtensorMap& tw,
+                                  const GemmParams& p) {
+  static bool done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !done[dev]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(gemm_q4_persist_kernel<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) done[dev] = true;
+  }
+  return cudaLaunchKernelEx(&cfg, gemm_q4_persist_kernel<BITS>, tact, tw, p);
+}
+
 // Profiling buffer of sb_gemm_q4_trace (null: off) and its size in stamps.
 static unsigned long long* g_trace = nullptr;
 static size_t g_trace_slots = 0;
@@ -1358,6 +1706,40 @@ static int gemm_q4_impl(const void* a, const void* w, const void* scales, int sc
       return sb::fail(SB_ERR_ARG, "sb_gemm_q4_argmax: k=%d has too many scale groups for one split", k);
     rc = sb::zero_keys(reinterpret_cast<unsigned long long*>(keys), m, s);
     if (rc != SB_OK) return rc;
+  }
+  // More 256 x 256 tiles than the device holds CTA pairs: the persistent
+  // kernel (one launch wave; a tile's epilogue overlaps the next tile's MMAs)
+  const int pt_pairs = pair && nt == QT && !keys ? max_active_clusters(true, 1) : 0;
+  const int pt_tiles = ((n + 2 * QW - 1) / (2 * QW)) * ((m + QT - 1) / QT);
+  if (pt_pairs > 0 && pt_tiles > pt_pairs) {
+    int kbc = p.kb_total;  // k-blocks per scale tile
+    while (kbc > 1 && QW * q4_scale_groups(kbc, group) * esz > Q_SCALE_BYTES) --kbc;
+    const int gpk = group > BK ? group / BK : 1;  // scale tiles start on group boundaries
+    kbc = std::max(gpk, kbc / gpk * gpk);
+    if (kbc >= P_STAGES || kbc >= p.kb_total) {
+      p.pt_pairs = pt_pairs;
+      p.pt_wtp = (n + 2 * QW - 1) / (2 * QW);
+      p.pt_ttiles = (m + QT - 1) / QT;
+      p.pt_kbc = kbc;
+      if (g_trace && static_cast<size_t>(2) * pt_pairs * kTraceSlots <= g_trace_slots) p.trace = g_trace;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2, pt_pairs, 1);
+      cfg.blockDim = dim3(P_WARPS * 32);
+      cfg.dynamicSmemBytes = P_SMEM;
+      cfg.stream = s;
+      cudaLaunchAttribute attr[2];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 2;
+      const cudaError_t e = bits == 2 ? launch_persist<2>(cfg, tact, tw, p) : launch_persist<4>(cfg, tact, tw, p);
+      if (e != cudaSuccess) return sb::cuda_fail(e, "gemm_q4_persist_kernel (cluster launch)");
+      return sb::launch_status("gemm_q4_persist_kernel");
+    }
   }
   if (!pair) {
     static bool done[2][64] = {};

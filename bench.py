@@ -65,7 +65,7 @@ def parse():
     ap.add_argument("--kernel", default="",
                     choices=["", "gemm_q4", "gemm_q4_geglu", "gemm_f16", "gemv", "lmhead", "attn", "attn_decode", "gemv_q8",
                              "gemv_bf16", "ple_block", "prefill",
-                             "decode", "decode_fused", "decode_batch", "decode_trace", "gemm_trace", "attn_trace"],
+                             "decode", "decode_fused", "decode_batch", "decode_trace", "gemm_trace", "attn_trace", "gemv_trace"],
                     help="run one kernel --iters times on a single shape and exit (for ncu captures)")
     ap.add_argument("--shape", default="6144,1536", help="N,K of the weight for --kernel")
     ap.add_argument("--m", type=int, default=1024, help="rows of the activation for --kernel")
@@ -257,6 +257,90 @@ def run_attn_trace(args):
     kern.device_status()
 
 
+def run_gemv_trace(args):
+    """Where the time of the streaming GEMV goes when it runs back to back, from
+    its own %globaltimer stamps (sb_gemv_trace): the lm_head + argmax over a
+    --shape V,K int4 table (f16 group-32 scales, f32 hidden vector), as a CUDA
+    graph of 10 calls -- each the key-clearing kernel and the GEMV -- and the
+    peer-memory form at world size 1 (the mailbox exchange with this rank
+    only).  For launches 2..10 of one traced replay it prints the span of a
+    launch (first entry to last exit), the gap from the previous launch's last
+    exit, and each phase's start over CTAs relative to the launch's first
+    entry: median / max."""
+    import numpy as np
+    import torch
+
+    from slang_b200 import _lib, lmhead
+    from slang_b200 import kernels as kern
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    V, K = (int(x) for x in args.shape.split(","))
+    emb = torch.randint(0, 256, (V, K // 2), dtype=torch.uint8, device=dev, generator=g)
+    sc = (torch.randn((V, K // 32), device=dev, generator=g) * 0.02).abs().half()
+    h = torch.randn((1, K), device=dev, generator=g)
+    keys = torch.zeros(1, dtype=torch.int64, device=dev)
+    toks = torch.full((1,), -1, dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    slots, reps = 16, 10  # gemv.cu kGvTraceSlots
+    tr = torch.zeros(reps * 2 * 148 * 4 * slots, dtype=torch.int64, device=dev)
+    st = torch.cuda.Stream()
+    ph = lmhead.PeerLMHead(emb, sc, 0, 1, full_table=False)
+    forms = (("lm_head + argmax", lambda: kern.lmhead_argmax(emb, sc, h, keys=keys, want_tokens=False)),
+             ("peer exchange, world 1", lambda: ph(h, keys, toks)))
+    for name, fn in forms:
+        with torch.cuda.stream(st):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=st):
+                for _ in range(reps):
+                    fn()
+            us = timed_graph(torch, gr, 10, 3, st) * 1e3 / reps
+            del gr
+            tr.zero_()
+            lib.sb_gemv_trace(tr.data_ptr(), tr.numel() * 8)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=st):
+                for _ in range(reps):
+                    fn()
+            lib.sb_gemv_trace(None, 0)
+            gr.replay()
+            torch.cuda.synchronize()
+            del gr
+        t = tr.view(-1, slots).cpu().numpy().astype(np.float64)
+        used = t[t[:, 1] > 0]
+        grid = len(used) // reps
+        print(f"{name}: V={V} K={K}, {us:.2f} us per call in a CUDA graph of {reps}; "
+              f"traced: {grid} CTAs per launch, stages per CTA {int(used[:, 10].min())}-{int(used[:, 10].max())}")
+        launches = [used[i * grid:(i + 1) * grid] for i in range(reps)]
+        spans, gaps = [], []
+        cols = (("issued", 2), ("prev done", 3), ("x ready", 4), ("stage 0", 5), ("stage 0 done", 6),
+                ("rows done", 7), ("published", 8), ("exit", 9))
+        ph_rel = {c: [] for _, c in cols}
+        for i in range(1, reps):
+            L, P = launches[i], launches[i - 1]
+            e0 = L[:, 1].min()
+            spans.append((L[:, 9].max() - e0) / 1e3)
+            gaps.append((e0 - P[:, 9].max()) / 1e3)
+            for _, c in cols:
+                ph_rel[c].append((L[:, c] - e0) / 1e3)
+        spread = np.median([(x[:, 1].max() - x[:, 1].min()) / 1e3 for x in launches[1:]])
+        print(f"  span {np.median(spans):.2f} us, gap from the previous launch's last exit {np.median(gaps):.2f} us "
+              f"(medians over launches 2..{reps}); entries spread {spread:.2f} us")
+        for nm, c in cols:
+            x = np.concatenate(ph_rel[c])
+            print(f"  {nm:13s} {np.median(x):7.2f} {x.max():7.2f}")
+        last = [(i, r) for i, x in enumerate(launches) for r in x if r[11] == 1]
+        if last:
+            rel = lambda c: np.median([(r[c] - launches[i][:, 1].min()) / 1e3 for i, r in last])  # noqa: E731
+            print(f"  exchange CTA: rows done {rel(7):.2f} -> keys sent {rel(12):.2f} -> all received {rel(13):.2f} "
+                  f"-> exit {rel(9):.2f} us after the launch's first entry (medians)")
+    ph.close()
+    kern.device_status()
+
+
 def run_gemm_trace(args):
     """Where the time of one fused int4 GEMM launch goes, from the pair kernel's
     own %globaltimer stamps (sb_gemm_q4_trace): the four matrices of a layer at
@@ -374,6 +458,8 @@ def run_kernel_case(args):
         return run_gemm_trace(args)
     if args.kernel == "attn_trace":
         return run_attn_trace(args)
+    if args.kernel == "gemv_trace":
+        return run_gemv_trace(args)
     if args.kernel in ("prefill", "decode", "decode_fused", "decode_batch"):
         return run_model_case(args)
     from slang_b200 import kernels as kern

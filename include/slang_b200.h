@@ -283,6 +283,22 @@ int sb_gemm_q4_trace(uint64_t* buf, size_t bytes);
 int sb_attn_prefill_trace(uint64_t* buf, size_t bytes);
 
 /*
+ * Profiling hook of the streaming GEMV (sb_gemv_q4 / sb_lmhead_argmax /
+ * sb_lmhead_argmax_peer and the other entry points on the same kernel but the
+ * norm-add form; no reference counterpart): while `buf` is set (NULL turns it
+ * off; every call restarts at its beginning), each launch of the kernel --
+ * graph captures included -- takes the next 16 x grid u64 of `buf` while they
+ * last, CTA b's at [16 * b]: [0] its SM, %globaltimer stamps [1] entry, [2]
+ * first bulk copies issued, [3] previous kernel complete
+ * (griddepcontrol.wait), [4] x quantised, [5] first stage landed, [6] first
+ * stage done, [7] last stage done, [8] keys folded or rows stored, [9] exit,
+ * then [10] its stage count, [11] 1 in the CTA that completed the launch's
+ * count (peer form), with [12] keys sent to every rank and [13] every rank's
+ * keys received.  For measurement only; buf must stay valid.
+ */
+int sb_gemv_trace(uint64_t* buf, size_t bytes);
+
+/*
  * sb_gemm_q4 without a caller workspace; it allocates nothing.  No counterpart
  * in the reference: it is for callers that cannot allocate device memory --
  * a host reaching the GPU only through this C ABI, with no CUDA allocator of

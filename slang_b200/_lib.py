@@ -37,6 +37,7 @@ SIGNATURES = {
     "sb_gemm_q4_kernels": ([_i, _i, _i], _i),
     "sb_gemm_q4_trace": ([_vp, _sz], _i),
     "sb_attn_prefill_trace": ([_vp, _sz], _i),
+    "sb_gemv_trace": ([_vp, _sz], _i),
     "sb_gemm_q4_noalloc": ([_vp, _vp, _vp, _i, _i, _vp, _i, _i, _i, _f, _i, _i, _vp], _i),
     "sb_gemm_f16_f32out": ([_vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _i, _i, _vp], _i),
     "sb_embed_q4": ([_vp, _vp, _i, _i, _vp, _i, _i, _f, _vp, _vp, _vp], _i),

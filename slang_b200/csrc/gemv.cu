@@ -81,7 +81,31 @@ struct GemvParams {
   // optional last-arriver residual add + RMSNorm over the launch's rows of y
   // (tail.counter != null; EPI_STORE only)
   sbd::NormTail tail;
+  unsigned long long* trace;  // stream kernel, profiling only: kGvTraceSlots stamps per CTA, or null
 };
+
+// Profiling stamps of the stream kernel (sb_gemv_trace): slot i of CTA b is
+// trace[b * kGvTraceSlots + i]; %globaltimer ns unless noted.  Thread 0's view.
+enum {
+  GV_SMID = 0,        // the CTA's SM (not a time)
+  GV_ENTRY = 1,       // kernel entry
+  GV_ISSUED = 2,      // first stages' bulk copies issued
+  GV_DEP = 3,         // griddepcontrol.wait returned (the previous kernel is done)
+  GV_X = 4,           // x loaded and quantised
+  GV_STAGE0 = 5,      // first stage landed (warp 0)
+  GV_STAGE0_DONE = 6, // first stage's rows done (warp 0)
+  GV_ROWS_DONE = 7,   // warp 0's last stage done
+  GV_PUBLISHED = 8,   // keys folded (argmax) / rows stored
+  GV_EXIT = 9,        // leaving the kernel
+  GV_STAGES = 10,     // stages this CTA ran (not a time)
+  GV_LAST = 11,       // 1 when this CTA completed the launch's count (peer exchange; not a time)
+  GV_PEER_SENT = 12,  // last CTA: keys sent to every rank
+  GV_PEER_DONE = 13,  // last CTA: every rank's keys received
+  kGvTraceSlots = 16
+};
+__device__ __forceinline__ void gv_stamp(const GemvParams& p, int slot, unsigned long long v) {
+  if (p.trace) p.trace[static_cast<size_t>(blockIdx.x) * kGvTraceSlots + slot] = v;
+}
 
 // The output side of an SRQ linear: srq(y, s) = clip(round(y / s), -128, 127) * s.
 __device__ __forceinline__ float srq_out(const GemvParams& p, int row, float v) {
@@ -437,11 +461,19 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
   const int row_bytes = p.k * BITS / 8;
   const int gps = p.k / p.group;
   const int esz = SF16 ? 2 : 4;
+  constexpr bool TR = EPI != EPI_TAIL;  // profiling stamps (the norm-tail form has no registers to spare)
 
   sbd::griddep_launch_dependents();
   const int my_stages = p.n_stages > static_cast<int>(blockIdx.x)
                             ? (p.n_stages - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1
                             : 0;
+  if (TR && tid == 0 && p.trace) {
+    gv_stamp(p, GV_ENTRY, sbd::global_ns());
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    gv_stamp(p, GV_SMID, smid);
+    gv_stamp(p, GV_STAGES, static_cast<unsigned long long>(my_stages));
+  }
   const uint64_t pol = sbd::l2_policy_evict_first();  // weights are read once per step
   auto issue = [&](int i) {
     const int slot = i % kRing;
@@ -467,6 +499,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
     // weights do not depend on the previous kernel: start streaming now
     for (int i = 0; i < kRing && i < my_stages; ++i) issue(i);
     sm.issued = min(kRing, my_stages);
+    if (TR && p.trace) gv_stamp(p, GV_ISSUED, sbd::global_ns());
   }
   __syncthreads();
 
@@ -483,8 +516,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
   }
   // x is the previous kernel's output: wait for it (weights are already streaming)
   sbd::griddep_wait();
+  if (TR && tid == 0 && p.trace) gv_stamp(p, GV_DEP, sbd::global_ns());
   XG xg[M][GPL];
   load_x_groups<M, GPL, XG, EPI == EPI_SRQ>(p, gidx, gval, xg);
+  if (TR && tid == 0 && p.trace) gv_stamp(p, GV_X, sbd::global_ns());
 
   float best_v[M];
   long long best_i[M];
@@ -496,6 +531,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
   for (int i = 0; i < my_stages; ++i) {
     const int slot = i % kRing;
     if (!__all_sync(0xFFFFFFFFu, sbd::mbar_wait(&sm.full[slot], (i / kRing) & 1, abort, p.err))) break;
+    if (TR && i == 0 && tid == 0 && p.trace) gv_stamp(p, GV_STAGE0, sbd::global_ns());
     const int st = blockIdx.x + i * gridDim.x;
     const int r0 = st * p.rs;
     const int nr = min(p.rs, p.n - r0);
@@ -551,6 +587,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
     }
     // this warp is done with the slot; the last of the 8 warps refills it
     __syncwarp();
+    if (TR && i == 0 && tid == 0 && p.trace) gv_stamp(p, GV_STAGE0_DONE, sbd::global_ns());
     if (lane == 0) {
       __threadfence_block();  // this warp's reads of the slot are done before the release
       if (atomicAdd(&sm.released[slot], 1) == kConsumers / 32 - 1) {
@@ -565,6 +602,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
     }
   }
 
+  if (TR && tid == 0 && p.trace) gv_stamp(p, GV_ROWS_DONE, sbd::global_ns());
   if (EPI == EPI_ARGMAX) {
 #pragma unroll
     for (int m = 0; m < M; ++m) {
@@ -579,6 +617,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
     __syncthreads();
     publish_keys<M>(p, sm, tid);
   }
+  if (TR && tid == 0 && p.trace) gv_stamp(p, GV_PUBLISHED, sbd::global_ns());
   if (__syncthreads_or(*abort)) {
     // a copy never landed: let the latest one of each slot finish before the CTA exits (bounded)
     if (tid == 0) {
@@ -590,6 +629,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
     }
   }
   if constexpr (EPI == EPI_TAIL) sbd::last_arriver_tail(p.y, p.ldy, p.m, p.n, p.tail);
+  if (TR && tid == 0 && p.trace) gv_stamp(p, GV_EXIT, sbd::global_ns());
 }
 
 __global__ void keys_to_tokens_kernel(const unsigned long long* keys, int32_t* tokens, int m) {
@@ -648,10 +688,22 @@ Plan plan(int mtile, int n, int k, int bits, int scale_row_bytes, int sms) {
   return best;
 }
 
+// Profiling buffer of sb_gemv_trace (null: off), its size in stamps and the
+// stamps handed out so far: each traced launch (graph captures included) gets
+// the next grid x kGvTraceSlots stamps while they last.
+static unsigned long long* g_gv_trace = nullptr;
+static size_t g_gv_trace_slots = 0, g_gv_trace_used = 0;
+
 template <int M, int GPL, int EPI, int BITS>
-int launch_t(const GemvParams& p, bool sf16, int sms, cudaStream_t s) {
+int launch_t(GemvParams p, bool sf16, int sms, cudaStream_t s) {
   const int grid = std::min(p.n_stages, sms * kCtasPerSm);
   if (grid == 0) return SB_OK;
+  p.trace = nullptr;
+  if (g_gv_trace && p.ks == 1 && EPI != EPI_TAIL &&
+      g_gv_trace_used + static_cast<size_t>(grid) * kGvTraceSlots <= g_gv_trace_slots) {
+    p.trace = g_gv_trace + g_gv_trace_used;
+    g_gv_trace_used += static_cast<size_t>(grid) * kGvTraceSlots;
+  }
   const int smem = static_cast<int>(sizeof(GemvSmem));
   static bool done[64] = {false};
   int dev = 0;
@@ -835,6 +887,14 @@ static int gemv_impl(const char* fn, int bits, const void* w, const void* scales
   const bool srq = srq_in != 0.f || srq_out_s != 0.f || srq_out_rows;
   return run(p, srq ? EPI_SRQ : EPI_STORE, x_dtype == SB_F32, scale_dtype == SB_SCALE_F16,
              static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sb_gemv_trace(uint64_t* buf, size_t bytes) {
+  SB_CHECK_ARG(!buf || sb::aligned(buf, 8), "sb_gemv_trace: buffer must be 8-byte aligned");
+  g_gv_trace = buf ? reinterpret_cast<unsigned long long*>(buf) : nullptr;
+  g_gv_trace_slots = buf ? bytes / sizeof(uint64_t) : 0;
+  g_gv_trace_used = 0;
+  return SB_OK;
 }
 
 extern "C" int sb_gemv_q4(const void* w, const void* scales, int scale_dtype, int group, const void* x,

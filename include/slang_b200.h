@@ -139,15 +139,16 @@ int sb_keys_to_tokens(const uint64_t* keys, int32_t* tokens, int m, void* stream
  * handle), shares the handle, and maps the other ranks' mailboxes with
  * sb_peer_buffer_open.  sb_lmhead_argmax_peer then runs this rank's shard
  * GEMV (rows row_offset .. row_offset + v, v >= 1) as one launch: its CTAs fold
- * their argmax keys into this rank's mailbox, and the last CTA to finish sends
- * each row's key to every rank's mailbox (system-scope MAX over NVLink), counts
- * this rank in at every mailbox, waits (bounded by sb_peer_set_wait_limit_ns;
- * timeout -> SB_ERR_TIMEOUT in sb_device_status and keys of 0) for all `world`
- * ranks, and writes the combined keys / tokens (m <= 64 rows).  A timed-out
- * exchange leaves the mailboxes unusable: create them again.
+ * their argmax keys into this rank's mailbox, and the last CTA to finish writes
+ * each row's key, tagged with the step, into this rank's slot of every rank's
+ * mailbox (16-byte stores over NVLink), waits (bounded by
+ * sb_peer_set_wait_limit_ns; timeout -> SB_ERR_TIMEOUT in sb_device_status and
+ * keys of 0) until every rank's slots carry this step's tag, and writes the
+ * combined keys / tokens (m <= 64 rows, world <= 32).  A timed-out exchange
+ * leaves the mailboxes unusable: create them again.
  * peer_mailboxes: device array of the `world` mailbox addresses as this
- * process maps them (its own at `rank`).  Every rank must make the same
- * sequence of calls.
+ * process maps them, own_mailbox among them (its index is this rank; absent:
+ * SB_ERR_TIMEOUT at once).  Every rank must make the same sequence of calls.
  */
 size_t sb_peer_mailbox_size(void);
 int sb_peer_buffer_create(size_t bytes, void** dev_ptr, void* ipc_handle);
@@ -158,8 +159,8 @@ int sb_lmhead_argmax_peer(const void* emb, const void* scales, int scale_dtype, 
                           int m, int v, int k, int64_t row_offset, const uint64_t* peer_mailboxes, int world,
                           void* own_mailbox, uint64_t* keys, int32_t* tokens, void* stream);
 
-/* How long sb_lmhead_argmax_peer's exchange waits for the other ranks to count
- * in before it gives up with SB_ERR_TIMEOUT (in sb_device_status) and returns
+/* How long sb_lmhead_argmax_peer's exchange waits for the other ranks' keys
+ * before it gives up with SB_ERR_TIMEOUT (in sb_device_status) and returns
  * keys of 0: ns nanoseconds, 0 for the default (and maximum) of 2 s.  A rank
  * that never arrives then costs the others this long instead of a hang.
  * Applies to launches made after the call.  No counterpart in the reference

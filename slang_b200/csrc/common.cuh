@@ -279,16 +279,20 @@ __device__ __forceinline__ unsigned long long make_key(float v, long long idx) {
 
 // ---- peer mailbox of the vocabulary-sharded lm_head (one per rank, mapped by
 // every rank): a step counter, this rank's CTA count for the running launch,
-// two per-parity arrival counts, two per-parity slot arrays of combined argmax
-// keys (written by every rank) and this rank's own keys (its CTAs fold theirs
-// in before the last one sends them out).
-constexpr int kMailEpoch = 0;
+// this rank's own keys (its CTAs fold theirs in before the last one sends them
+// out) and, per step parity, one slot per (sending rank, row): two 64-bit words
+// {key high half, step tag} and {key low half, step tag}, written by the
+// sender over NVLink.  A 64-bit store is single-copy atomic, so a word whose
+// tag is the step's carries that step's half of the key: no fence or arrival
+// count is needed.
+constexpr int kMailEpoch = 0;      // uint32_t
 constexpr int kMailCtas = 4;       // uint32_t
-constexpr int kMailCount = 64;     // uint32_t[2]
-constexpr int kMailKeys = 128;     // unsigned long long[2][kMailMaxRows]
+constexpr int kMailLocal = 64;     // unsigned long long[kMailMaxRows]
 constexpr int kMailMaxRows = 64;
-constexpr int kMailLocal = kMailKeys + 2 * kMailMaxRows * 8;  // unsigned long long[kMailMaxRows]
-constexpr int kMailBytes = kMailLocal + kMailMaxRows * 8;
+constexpr int kMailMaxRanks = 32;
+constexpr int kMailSlots = 1024;   // unsigned long long[2][kMailMaxRanks][kMailMaxRows][2]
+constexpr int kMailBytes = kMailSlots + 2 * kMailMaxRanks * kMailMaxRows * 16;
+static_assert(kMailLocal + kMailMaxRows * 8 <= kMailSlots, "mailbox layout");
 
 // ---- thread-block clusters and distributed shared memory
 __device__ __forceinline__ uint32_t cluster_ctarank() {

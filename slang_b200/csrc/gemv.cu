@@ -30,6 +30,7 @@
 // sums are reduced with half-warp shuffles and, across K slices, through
 // shared memory in a fixed order (deterministic results).
 #include <algorithm>
+#include <cstddef>
 #include <cstring>
 
 #include <atomic>
@@ -64,6 +65,7 @@ struct GemvParams {
   int* err;
   int m, n, k, group, ldy, ks, rs, n_stages, scale_bulk, x_f32;
   int bits;  // code width: 4 (two per byte) or 2 (four per byte)
+  int x_stage;  // stream kernel: x quantised once per CTA into shared memory (else per warp)
   long long row_offset;
   // vocabulary shards over peer memory: each CTA's key goes to every rank's
   // mailbox (atomic MAX through NVLink) instead of `keys`
@@ -116,13 +118,17 @@ __device__ __forceinline__ float srq_out(const GemvParams& p, int row, float v) 
 struct GemvSmem {
   uint8_t w[kRing][kStageW];
   uint8_t s[kRing][kStageS];
-  float red[2][kRedMax];
   unsigned long long best[8][4];
   uint64_t full[kRing];
   int released[kRing];  // stream kernel: warps done with the slot's current stage
   int issued;           // stream kernel: stages issued so far
   int abort;
+  // gemv_q4_kernel: partial sums across K slices.  The stream kernel has no
+  // use for them and keeps its staged x here instead (x_stage), in a region
+  // sized at launch: kXqBytes per (batch row, group).
+  alignas(16) float red[2][kRedMax];
 };
+constexpr int kXqBytes = 72;  // one sbd::XGroup: he, ho, le, lo words, bias, sx
 
 using sbd::make_key;
 
@@ -174,6 +180,156 @@ __device__ __forceinline__ void load_x_groups(const GemvParams& p, const int (&g
   }
 }
 
+// load_x_groups for the stream kernel's 4-bit forms, where lanes l and l ^ 16
+// of a warp hold the same groups: each lane of the pair loads half of every
+// group (all loads issued before any is used) and the pair quantises it
+// together (quantise_group_pair).
+template <int M, int GPL>
+__device__ __forceinline__ void load_x_pairs(const GemvParams& p, const int (&gidx)[GPL], const bool (&gval)[GPL],
+                                             sbd::XGroup (&xg)[M][GPL], int h) {
+  float v[M][GPL][16];
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+#pragma unroll
+    for (int u = 0; u < GPL; ++u) {
+      const bool ok = gval[u] && m < p.m;
+      const size_t off = static_cast<size_t>(m) * p.k + gidx[u] * 32 + 16 * h;
+      if (p.x_f32) {
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + off);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float4 f = ok ? __ldg(src + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+          v[m][u][4 * j] = f.x;
+          v[m][u][4 * j + 1] = f.y;
+          v[m][u][4 * j + 2] = f.z;
+          v[m][u][4 * j + 3] = f.w;
+        }
+      } else {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x) + off);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const uint4 hv = ok ? __ldg(src + j) : make_uint4(0, 0, 0, 0);
+          const uint32_t w[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+            v[m][u][8 * j + 2 * e] = f.x;
+            v[m][u][8 * j + 2 * e + 1] = f.y;
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+#pragma unroll
+    for (int u = 0; u < GPL; ++u) sbd::quantise_group_pair(v[m][u], h, xg[m][u]);
+  }
+}
+
+// x quantised once per CTA for the stream kernel's 4-bit forms: thread pairs
+// (t, t ^ 1) take one (batch row, group) each, load half of its values, and
+// quantise it together (the pair's max and integer sum by one shuffle each)
+// into its kXqBytes record in shared memory; after a barrier every lane reads
+// the records of its own groups.  Same XGroups as quantise_group, for 1/8 of
+// the per-warp work of load_x_pairs.
+template <int M, int GPL>
+__device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xq, const int (&gidx)[GPL],
+                                        const bool (&gval)[GPL], sbd::XGroup (&xg)[M][GPL], int tid) {
+  const int G = p.k >> 5;
+  const int halves = 2 * M * G;
+  if ((tid & ~31) < halves) {  // warp-uniform: whole warps join the shuffles
+    const int h = tid & 1, gg = tid >> 1;
+    const bool act = tid < halves;
+    const int m = act ? gg / G : 0, g = act ? gg - m * G : 0;
+    const bool ld = act && m < p.m;
+    float v[16];
+    const size_t off = static_cast<size_t>(m) * p.k + g * 32 + 16 * h;
+    if (p.x_f32) {
+      const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + off);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 f = ld ? __ldg(src + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[4 * j] = f.x;
+        v[4 * j + 1] = f.y;
+        v[4 * j + 2] = f.z;
+        v[4 * j + 3] = f.w;
+      }
+    } else {
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x) + off);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint4 hv = ld ? __ldg(src + j) : make_uint4(0, 0, 0, 0);
+        const uint32_t w[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+          v[8 * j + 2 * e] = f.x;
+          v[8 * j + 2 * e + 1] = f.y;
+        }
+      }
+    }
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) mx = fmaxf(mx, fabsf(v[i]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
+    const float inv = mx > 0.f ? 32767.f / mx : 0.f;
+    uint32_t b[16], sum = 0u;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      b[i] = sbd::rint_bits(v[i], inv);
+      sum += b[i];
+    }
+    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+    if (act) {
+      uint32_t* rec = reinterpret_cast<uint32_t*>(xq + static_cast<size_t>(m * G + g) * kXqBytes);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        uint32_t he, ho, le, lo;
+        sbd::pack_word(b + 8 * j, he, ho, le, lo);
+        rec[2 * h + j] = he;
+        rec[4 + 2 * h + j] = ho;
+        rec[8 + 2 * h + j] = le;
+        rec[12 + 2 * h + j] = lo;
+      }
+      if (h == 0) {
+        rec[16] = static_cast<uint32_t>(-8 * static_cast<int>(sum - 32u * sbd::kRintBias));
+        rec[17] = __float_as_uint(mx / 32767.f);
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+#pragma unroll
+    for (int u = 0; u < GPL; ++u) {
+      uint32_t r[18];
+      if (gval[u]) {
+        const uint2* rec = reinterpret_cast<const uint2*>(xq + static_cast<size_t>(m * G + gidx[u]) * kXqBytes);
+#pragma unroll
+        for (int j = 0; j < 9; ++j) {
+          const uint2 w = rec[j];
+          r[2 * j] = w.x;
+          r[2 * j + 1] = w.y;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 18; ++j) r[j] = 0u;
+      }
+      sbd::XGroup& x = xg[m][u];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        x.he[j] = r[j];
+        x.ho[j] = r[4 + j];
+        x.le[j] = r[8 + j];
+        x.lo[j] = r[12 + j];
+      }
+      x.bias = static_cast<int>(r[16]);
+      x.sx = __uint_as_float(r[17]);
+    }
+  }
+}
+
 // Combine the per-warp argmax keys (sm.best[warp][m], warps 0..7) and publish
 // one key per batch row: atomic MAX into p.keys, or into every rank's mailbox.
 // Called by the 256 consumer threads after a barrier over them.
@@ -181,18 +337,17 @@ __device__ __forceinline__ void load_x_groups(const GemvParams& p, const int (&g
 // GEMV (every thread of every CTA calls it).  Each CTA folds its keys into this
 // rank's own mailbox (device-scope atomic MAX) and counts itself in; the CTA
 // that completes the count re-arms it and, in the launch holding the step's
-// last rows, exchanges every row's key with the other ranks:
-//   1. clear this mailbox's other-parity slots and count (no rank writes them
-//      before every rank has counted in for this step);
-//   2. fold this rank's keys into every rank's parity-q slots (system-scope
-//      reduction over NVLink), then a system fence;
-//   3. count in at every rank (system-scope add);
-//   4. wait, bounded, until all `world` ranks have counted in here;
-//   5. read the combined keys, write keys and tokens, clear this rank's own
-//      keys and advance the step counter.
-// Slots alternate by step parity q: a rank writes step e + 1's keys only after
-// every rank has counted in for step e, which each rank does only after
-// clearing those slots, so two slot sets suffice and no host sync is needed.
+// last rows, exchanges every row's key with the other ranks in one warp:
+//   1. send: each row's key as two tagged words (tag = step + 1) into slot
+//      [step parity][this rank][row] of every rank's mailbox (16-byte
+//      system-scope stores over NVLink);
+//   2. wait, bounded, until every rank's words of this step are in this
+//      mailbox's slots, and take the MAX per row;
+//   3. write keys and tokens, clear this rank's own keys, advance the step.
+// A rank sends step e + 1's words only after it has read every rank's words of
+// step e, which each rank sends only after its own step e - 1 has ended (the
+// launch's CTAs wait for the previous kernel first), so the parity-(e + 1)
+// slots it overwrites hold step e - 1's words, which every rank has read.
 template <int M>
 __device__ __forceinline__ void peer_publish(const GemvParams& p, GemvSmem& sm, int tid) {
   uint8_t* own = p.peer_own;
@@ -210,48 +365,75 @@ __device__ __forceinline__ void peer_publish(const GemvParams& p, GemvSmem& sm, 
   }
   __syncthreads();
   if (!s_last) return;
-  if (tid == 0) *reinterpret_cast<volatile unsigned int*>(own + sbd::kMailCtas) = 0u;  // re-arm for the next launch
+  if (tid == 0) {
+    *reinterpret_cast<volatile unsigned int*>(own + sbd::kMailCtas) = 0u;  // re-arm for the next launch
+    gv_stamp(p, GV_LAST, 1ull);
+  }
   if (!p.peer_finish || tid >= 32) return;
   __threadfence();
-  const int lane = tid, rows = p.peer_rows;
+  const int lane = tid, rows = p.peer_rows, world = p.world;
   uint32_t* epoch = reinterpret_cast<uint32_t*>(own + sbd::kMailEpoch);
-  uint32_t* count = reinterpret_cast<uint32_t*>(own + sbd::kMailCount);
-  unsigned long long* slots = reinterpret_cast<unsigned long long*>(own + sbd::kMailKeys);
   const uint32_t e = *reinterpret_cast<volatile uint32_t*>(epoch), q = e & 1u;
-  for (int i = lane; i < rows; i += 32) slots[(q ^ 1u) * sbd::kMailMaxRows + i] = 0ull;
-  if (lane == 0) count[q ^ 1u] = 0u;
-  unsigned long long mine[2];
-  for (int j = 0; j < 2; ++j) mine[j] = lane + 32 * j < rows ? __ldcg(local + lane + 32 * j) : 0ull;
-  __threadfence_system();
-  for (int pe = 0; pe < p.world; ++pe) {
-    unsigned long long* dst =
-        reinterpret_cast<unsigned long long*>(p.peer_mailboxes[pe] + sbd::kMailKeys) + q * sbd::kMailMaxRows;
-    for (int j = 0; j < 2; ++j)
-      if (lane + 32 * j < rows && mine[j])
-        asm volatile("red.relaxed.sys.global.max.u64 [%0], %1;" ::"l"(dst + lane + 32 * j), "l"(mine[j]) : "memory");
-  }
-  __threadfence_system();
-  __syncwarp();
-  if (lane < p.world)
-    asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(
-                     reinterpret_cast<uint32_t*>(p.peer_mailboxes[lane] + sbd::kMailCount) + q)
-                 : "memory");
-  int done = 0;
-  if (lane == 0) {
-    const uint64_t t0 = sbd::global_ns();
-    while (!done) {
-      uint32_t c;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(c) : "l"(count + q) : "memory");
-      if (c >= static_cast<uint32_t>(p.world)) done = 1;
-      else if (sbd::global_ns() - t0 > p.peer_wait_ns) break;
+  const unsigned long long tag = e + 1u;
+  // this rank's index: where its own mailbox sits in the peer array
+  const unsigned long long own_addr = reinterpret_cast<unsigned long long>(own);
+  const unsigned int at = __ballot_sync(0xFFFFFFFFu, lane < world && p.peer_mailboxes[lane] == own_addr);
+  const int rank = at ? __ffs(at) - 1 : -1;
+  auto slot = [&](unsigned long long base, int r, int i) {
+    return reinterpret_cast<unsigned long long*>(base + sbd::kMailSlots) +
+           2 * ((static_cast<int>(q) * sbd::kMailMaxRanks + r) * sbd::kMailMaxRows + i);
+  };
+  bool ok = rank >= 0;
+  if (ok) {
+    for (int idx = lane; idx < world * rows; idx += 32) {
+      const int pe = idx / rows, i = idx - pe * rows;
+      const unsigned long long key = __ldcg(local + i);
+      const unsigned long long w0 = (key & 0xFFFFFFFF00000000ull) | tag, w1 = (key << 32) | tag;
+      asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(slot(p.peer_mailboxes[pe], rank, i)),
+                   "l"(w0), "l"(w1)
+                   : "memory");
     }
-    if (!done && p.err) atomicExch(p.err, SB_ERR_TIMEOUT);
   }
-  done = __shfl_sync(0xFFFFFFFFu, done, 0);
-  for (int i = lane; i < rows; i += 32) {
-    unsigned long long k;
-    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(k) : "l"(slots + q * sbd::kMailMaxRows + i) : "memory");
-    if (!done) k = 0ull;
+  if (lane == 0) gv_stamp(p, GV_PEER_SENT, sbd::global_ns());
+  unsigned long long comb0 = 0ull, comb1 = 0ull;  // the combined keys of rows lane and lane + 32
+  const uint64_t t0 = sbd::global_ns();
+  for (int i = 0; i < rows; ++i) {
+    unsigned long long key = 0ull;
+    if (ok && lane < world) {
+      const unsigned long long* src = slot(own_addr, lane, i);
+      for (;;) {
+        unsigned long long w0, w1;
+        asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(src) : "memory");
+        if ((w0 & 0xFFFFFFFFull) == tag && (w1 & 0xFFFFFFFFull) == tag) {
+          key = (w0 & 0xFFFFFFFF00000000ull) | (w1 >> 32);
+          break;
+        }
+        if (sbd::global_ns() - t0 > p.peer_wait_ns) {
+          ok = false;
+          break;
+        }
+      }
+    }
+    ok = __all_sync(0xFFFFFFFFu, ok);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const unsigned long long o = __shfl_xor_sync(0xFFFFFFFFu, key, off);
+      key = o > key ? o : key;
+    }
+    if (lane == (i & 31)) {
+      if (i < 32)
+        comb0 = key;
+      else
+        comb1 = key;
+    }
+  }
+  if (!ok && lane == 0 && p.err) atomicExch(p.err, SB_ERR_TIMEOUT);
+  if (lane == 0) gv_stamp(p, GV_PEER_DONE, sbd::global_ns());
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int i = lane + 32 * j;
+    if (i >= rows) continue;
+    const unsigned long long k = ok ? (j ? comb1 : comb0) : 0ull;
     if (p.keys) p.keys[i] = k;
     if (p.tokens) p.tokens[i] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
     local[i] = 0ull;
@@ -518,7 +700,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
   sbd::griddep_wait();
   if (TR && tid == 0 && p.trace) gv_stamp(p, GV_DEP, sbd::global_ns());
   XG xg[M][GPL];
-  load_x_groups<M, GPL, XG, EPI == EPI_SRQ>(p, gidx, gval, xg);
+  if constexpr (BITS == 4 && EPI != EPI_SRQ) {
+    if (p.x_stage)
+      stage_x<M, GPL>(p, reinterpret_cast<uint8_t*>(sm.red), gidx, gval, xg, tid);
+    else
+      load_x_pairs<M, GPL>(p, gidx, gval, xg, lane >> 4);
+  } else
+    load_x_groups<M, GPL, XG, EPI == EPI_SRQ>(p, gidx, gval, xg);
   if (TR && tid == 0 && p.trace) gv_stamp(p, GV_X, sbd::global_ns());
 
   float best_v[M];
@@ -694,6 +882,30 @@ Plan plan(int mtile, int n, int k, int bits, int scale_row_bytes, int sms) {
 static unsigned long long* g_gv_trace = nullptr;
 static size_t g_gv_trace_slots = 0, g_gv_trace_used = 0;
 
+// Whether `kCtasPerSm` CTAs of `bytes` dynamic shared memory each fit one SM of
+// the current device (its shared memory per SM less the per-CTA reservation).
+bool fits_per_sm(int bytes) {
+  static int per_sm[64] = {0}, reserved[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return false;
+  if (!per_sm[dev]) {
+    int a = 0, r = 0;
+    if (cudaDeviceGetAttribute(&a, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&r, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess)
+      return false;
+    reserved[dev] = r;
+    per_sm[dev] = a;
+  }
+  return kCtasPerSm * (bytes + reserved[dev]) <= per_sm[dev];
+}
+
+// Dynamic shared memory of the stream kernel with x staged (x_stage): the
+// fixed part up to `red`, then one record per (batch row, group); every
+// stream-kernel shape has M x G <= 64 (16 lanes x GPL x M <= 64 groups).
+constexpr int kStreamFixed = static_cast<int>(offsetof(GemvSmem, red));
+constexpr int kStreamStagedMax = (kStreamFixed + 64 * kXqBytes + 15) & ~15;
+
 template <int M, int GPL, int EPI, int BITS>
 int launch_t(GemvParams p, bool sf16, int sms, cudaStream_t s) {
   const int grid = std::min(p.n_stages, sms * kCtasPerSm);
@@ -705,6 +917,18 @@ int launch_t(GemvParams p, bool sf16, int sms, cudaStream_t s) {
     g_gv_trace_used += static_cast<size_t>(grid) * kGvTraceSlots;
   }
   const int smem = static_cast<int>(sizeof(GemvSmem));
+  // the stream kernel's 4-bit forms quantise x once per CTA into the tail of
+  // their shared memory when two CTAs per SM still fit
+  int smem_stream = smem;
+  p.x_stage = 0;
+  if (p.ks == 1 && BITS == 4 && EPI != EPI_SRQ) {
+    const int xq = std::max(static_cast<int>(sizeof(GemvSmem::red)), M * (p.k >> 5) * kXqBytes);
+    const int need = (kStreamFixed + xq + 15) & ~15;
+    if (M * (p.k >> 5) <= 64 && fits_per_sm(need)) {
+      smem_stream = need;
+      p.x_stage = 1;
+    }
+  }
   static bool done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -718,12 +942,13 @@ int launch_t(GemvParams p, bool sf16, int sms, cudaStream_t s) {
       e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, true, EPI, BITS>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(gemv_q4_kernel<M, GPL, false, EPI, BITS>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    const int smem_stream_max = std::max(smem, kStreamStagedMax);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, true, EPI, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               smem);
+                               smem_stream_max);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, false, EPI, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               smem);
+                               smem_stream_max);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(gemv_q4_stream_kernel<M, GPL, true, EPI, BITS>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                100);
@@ -735,8 +960,10 @@ int launch_t(GemvParams p, bool sf16, int sms, cudaStream_t s) {
   }
   cudaError_t e;
   if (p.ks == 1) {
-    e = sf16 ? sb::launch_pdl(gemv_q4_stream_kernel<M, GPL, true, EPI, BITS>, dim3(grid), dim3(kThreads), smem, s, p)
-             : sb::launch_pdl(gemv_q4_stream_kernel<M, GPL, false, EPI, BITS>, dim3(grid), dim3(kThreads), smem, s, p);
+    e = sf16 ? sb::launch_pdl(gemv_q4_stream_kernel<M, GPL, true, EPI, BITS>, dim3(grid), dim3(kThreads), smem_stream,
+                              s, p)
+             : sb::launch_pdl(gemv_q4_stream_kernel<M, GPL, false, EPI, BITS>, dim3(grid), dim3(kThreads), smem_stream,
+                              s, p);
   } else {
     e = sf16 ? sb::launch_pdl(gemv_q4_kernel<M, GPL, true, EPI, BITS>, dim3(grid), dim3(kThreads), smem, s, p)
              : sb::launch_pdl(gemv_q4_kernel<M, GPL, false, EPI, BITS>, dim3(grid), dim3(kThreads), smem, s, p);
@@ -1053,7 +1280,7 @@ extern "C" int sb_lmhead_argmax_peer(const void* emb, const void* scales, int sc
   if (rc != SB_OK) return rc;
   SB_CHECK_ARG(m <= sbd::kMailMaxRows, "sb_lmhead_argmax_peer: m=%d > %d", m, sbd::kMailMaxRows);
   SB_CHECK_ARG(v >= 1, "sb_lmhead_argmax_peer: every rank needs a non-empty shard (v=%d)", v);
-  SB_CHECK_ARG(world >= 1 && world <= 32 && peer_mailboxes && own_mailbox, "sb_lmhead_argmax_peer: bad peer arguments");
+  SB_CHECK_ARG(world >= 1 && world <= sbd::kMailMaxRanks && peer_mailboxes && own_mailbox, "sb_lmhead_argmax_peer: bad peer arguments");
   SB_CHECK_ARG(row_offset >= 0 && row_offset + v <= 0xFFFFFFFFLL, "sb_lmhead_argmax_peer: row indices must fit in 32 bits");
   GemvParams p{};
   p.w = static_cast<const uint8_t*>(emb);

@@ -45,16 +45,89 @@ __device__ __forceinline__ void pack_group(const int (&xi)[32], float sx, XGroup
   g.bias = -8 * sum;
 }
 
+// rint(x * inv) for |x * inv| < 2^22 in the low 16 bits of the returned word
+// (the rest is 0x4B40 less any borrow): adding 1.5 * 2^23 to the product
+// rounds it to the nearest integer, ties to even, as cvt.rni does, and leaves
+// that integer in two's complement in the mantissa's low bits.  A NaN product
+// gives 0, as cvt does.  Two full-rate FP32 operations (never contracted into
+// one FMA) instead of a conversion on the quarter-rate pipe.
+constexpr uint32_t kRintBias = 0x4B400000u;  // bits of 1.5 * 2^23
+__device__ __forceinline__ uint32_t rint_bits(float x, float inv) {
+  const float f = __fmul_rn(x, inv);
+  const uint32_t b = __float_as_uint(__fadd_rn(f, 12582912.f));
+  return f == f ? b : kRintBias;
+}
+
+// Pack the rint_bits of values 8 j .. 8 j + 7 of a group (b[0..7]) into word j
+// of he / ho / le / lo: byte i of he (le) is the high (low) byte of value
+// 8 j + 2 i, of ho (lo) of value 8 j + 2 i + 1.
+__device__ __forceinline__ void pack_word(const uint32_t* b, uint32_t& he, uint32_t& ho, uint32_t& le,
+                                          uint32_t& lo) {
+  // [lo(a), lo(b), hi(a), hi(b)] of value pairs, then their low and high halves
+  const uint32_t e01 = __byte_perm(b[0], b[2], 0x5140), e23 = __byte_perm(b[4], b[6], 0x5140);
+  const uint32_t o01 = __byte_perm(b[1], b[3], 0x5140), o23 = __byte_perm(b[5], b[7], 0x5140);
+  le = __byte_perm(e01, e23, 0x5410);
+  he = __byte_perm(e01, e23, 0x7632);
+  lo = __byte_perm(o01, o23, 0x5410);
+  ho = __byte_perm(o01, o23, 0x7632);
+}
+
 // x_int = rint(x * 32767 / max|x|), scale max|x| / 32767.
 __device__ __forceinline__ void quantise_group(const float (&v)[32], XGroup& g) {
   float mx = 0.f;
 #pragma unroll
   for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(v[i]));
   const float inv = mx > 0.f ? 32767.f / mx : 0.f;
-  int xi[32];
+  uint32_t b[32], sum = 0u;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) xi[i] = __float2int_rn(v[i] * inv);
-  pack_group(xi, mx / 32767.f, g);
+  for (int i = 0; i < 32; ++i) {
+    b[i] = rint_bits(v[i], inv);
+    sum += b[i];
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) pack_word(b + 8 * j, g.he[j], g.ho[j], g.le[j], g.lo[j]);
+  g.bias = -8 * static_cast<int>(sum - 32u * kRintBias);  // the 32 biases cancel mod 2^32
+  g.sx = mx / 32767.f;
+}
+
+// The same group quantised by the two lanes of a warp that hold it (lane and
+// lane ^ 16): this lane has values 16 h .. 16 h + 15 (h = lane >> 4); the pair
+// combines its max, each packs words 2 h and 2 h + 1 of he / ho / le / lo, and
+// they swap them, so both lanes end with the group exactly as quantise_group
+// makes it, for half the work each.
+__device__ __forceinline__ void quantise_group_pair(const float (&v)[16], int h, XGroup& g) {
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) mx = fmaxf(mx, fabsf(v[i]));
+  mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
+  const float inv = mx > 0.f ? 32767.f / mx : 0.f;
+  uint32_t b[16], sum = 0u;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    b[i] = rint_bits(v[i], inv);
+    sum += b[i];
+  }
+  uint32_t w[2][4];  // [word][he, ho, le, lo]
+#pragma unroll
+  for (int j = 0; j < 2; ++j) pack_word(b + 8 * j, w[j][0], w[j][1], w[j][2], w[j][3]);
+  sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 16);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    uint32_t o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) o[t] = __shfl_xor_sync(0xFFFFFFFFu, w[j][t], 16);
+    // h = 0 packed words 0, 1 and receives 2, 3; h = 1 the reverse
+    g.he[j] = h ? o[0] : w[j][0];
+    g.ho[j] = h ? o[1] : w[j][1];
+    g.le[j] = h ? o[2] : w[j][2];
+    g.lo[j] = h ? o[3] : w[j][3];
+    g.he[2 + j] = h ? w[j][0] : o[0];
+    g.ho[2 + j] = h ? w[j][1] : o[1];
+    g.le[2 + j] = h ? w[j][2] : o[2];
+    g.lo[2 + j] = h ? w[j][3] : o[3];
+  }
+  g.bias = -8 * static_cast<int>(sum - 32u * kRintBias);
+  g.sx = mx / 32767.f;
 }
 
 // Static range quantisation of an activation (the reference's

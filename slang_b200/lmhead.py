@@ -64,10 +64,11 @@ class PeerLMHead(ShardedLMHead):
 
     Every rank owns a small mailbox (``sb_peer_buffer_create``) that every
     other rank maps (CUDA IPC).  The shard GEMV's CTAs fold their argmax keys
-    into this rank's mailbox; the last CTA to finish sends each row's key to
-    every rank's mailbox with a system-scope MAX over NVLink, counts in at
-    every mailbox, waits (bounded) until all ranks have, and reads the combined
-    keys -- one launch, no host synchronisation, capturable in a CUDA graph.
+    into this rank's mailbox; the last CTA to finish writes each row's key,
+    tagged with the step, into this rank's slot of every rank's mailbox over
+    NVLink, waits (bounded) until every rank's slots in its own mailbox carry
+    the step's tag, and takes the MAX -- one launch, no fence, no host
+    synchronisation, capturable in a CUDA graph.
     The exchange is a function of the call sequence: every rank must call once
     per step.
     """

@@ -1,7 +1,7 @@
 """GPU: a cross-GPU wait that runs out reports a timeout and leaves the GPU usable.
 
 The vocabulary-sharded lm_head's exchange in peer memory waits, bounded, until
-every rank has counted in at its mailbox.  Here a two-rank exchange is opened
+every rank's step-tagged keys are in its mailbox.  Here a two-rank exchange is opened
 on one GPU with only rank 0 calling: the second mailbox stands for a rank that
 never arrives (a flag nothing sets).  With the wait limit set to 50 ms the
 exchange kernel must return, ``sb_device_status`` must report SB_ERR_TIMEOUT

@@ -65,7 +65,8 @@ def parse():
     ap.add_argument("--kernel", default="",
                     choices=["", "gemm_q4", "gemm_q4_geglu", "gemm_f16", "gemv", "lmhead", "attn", "attn_decode", "gemv_q8",
                              "gemv_bf16", "ple_block", "prefill",
-                             "decode", "decode_fused", "decode_batch", "decode_trace", "gemm_trace", "attn_trace", "gemv_trace"],
+                             "decode", "decode_fused", "decode_batch", "decode_trace", "gemm_trace", "attn_trace", "gemv_trace",
+                             "lmhead_sharded"],
                     help="run one kernel --iters times on a single shape and exit (for ncu captures)")
     ap.add_argument("--shape", default="6144,1536", help="N,K of the weight for --kernel")
     ap.add_argument("--m", type=int, default=1024, help="rows of the activation for --kernel")
@@ -341,6 +342,49 @@ def run_gemv_trace(args):
     kern.device_status()
 
 
+def run_lmhead_sharded(args):
+    """The vocabulary-sharded lm_head alone (``sharded_lmhead``), one rank per
+    GPU under torchrun: the random int4 262144 x 1536 table replicated on every
+    rank, the shard GEMV timed alone, then the NCCL and peer-memory exchanges,
+    every token checked against the full-table argmax on every rank.  Rank 0
+    prints one JSON line."""
+    import types
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    from slang_b200 import kernels as kern
+    from slang_b200 import lmhead
+    for k, v in (("MASTER_ADDR", "127.0.0.1"), ("MASTER_PORT", "29591"), ("RANK", "0"), ("WORLD_SIZE", "1")):
+        os.environ.setdefault(k, v)  # one process without torchrun: a world of one
+    world = int(os.environ["WORLD_SIZE"])
+    rank = int(os.environ["RANK"])
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    def max_over_ranks(x):
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234)  # the same table on every rank
+    dm = types.SimpleNamespace(
+        device=dev, embed_q=torch.randint(0, 256, (VOCAB, HID // 2), dtype=torch.uint8, device=dev, generator=g),
+        embed_s=(torch.randn((VOCAB, HID // 32), device=dev, generator=g) * 0.02).abs().half())
+    h = torch.randn((1, HID), device=dev, generator=torch.Generator(device=dev).manual_seed(7 + rank))
+    lm_alg = VOCAB * HID // 2 + VOCAB * (HID // 32) * 2 + HID * 4
+    out = sharded_lmhead(torch, dist, kern, lmhead, dm, h, rank, world, args, max_over_ranks, lm_alg)
+    if rank == 0:
+        print(json.dumps(out))
+    torch.cuda.synchronize()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def run_gemm_trace(args):
     """Where the time of one fused int4 GEMM launch goes, from the pair kernel's
     own %globaltimer stamps (sb_gemm_q4_trace): the four matrices of a layer at
@@ -460,6 +504,8 @@ def run_kernel_case(args):
         return run_attn_trace(args)
     if args.kernel == "gemv_trace":
         return run_gemv_trace(args)
+    if args.kernel == "lmhead_sharded":
+        return run_lmhead_sharded(args)
     if args.kernel in ("prefill", "decode", "decode_fused", "decode_batch"):
         return run_model_case(args)
     from slang_b200 import kernels as kern

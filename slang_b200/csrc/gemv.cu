@@ -348,37 +348,57 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xq, const 
 // step e, which each rank sends only after its own step e - 1 has ended (the
 // launch's CTAs wait for the previous kernel first), so the parity-(e + 1)
 // slots it overwrites hold step e - 1's words, which every rank has read.
+// What the exchange needs besides the keys, read by warp 0 of every CTA right
+// after griddepcontrol.wait (the previous launch wrote the step counter), so
+// the CTA that turns out last does not wait for them: the step and this rank's
+// index (where its own mailbox sits in the peer array; -1 if absent).
+struct PeerPre {
+  uint32_t epoch;
+  int rank;
+  bool ready;
+};
+__device__ __forceinline__ PeerPre peer_preload(const GemvParams& p, int lane) {
+  PeerPre r;
+  r.epoch = *reinterpret_cast<const volatile uint32_t*>(p.peer_own + sbd::kMailEpoch);
+  const unsigned long long own_addr = reinterpret_cast<unsigned long long>(p.peer_own);
+  const unsigned int at = __ballot_sync(0xFFFFFFFFu, lane < p.world && p.peer_mailboxes[lane] == own_addr);
+  r.rank = at ? __ffs(at) - 1 : -1;
+  r.ready = true;
+  return r;
+}
+
 template <int M>
-__device__ __forceinline__ void peer_publish(const GemvParams& p, GemvSmem& sm, int tid) {
+__device__ __forceinline__ void peer_publish(const GemvParams& p, GemvSmem& sm, int tid, PeerPre pre) {
+  if (tid >= 32) return;  // warp 0 folds the CTA's keys, counts in, and (last CTA) exchanges
   uint8_t* own = p.peer_own;
   unsigned long long* local = reinterpret_cast<unsigned long long*>(own + sbd::kMailLocal);
-  if (tid < M && tid < p.m) {
+  const int lane = tid;
+  if (!pre.ready) pre = peer_preload(p, lane);
+  if (lane < M && lane < p.m) {
     unsigned long long key = 0;
-    for (int wi = 0; wi < kConsumers / 32; ++wi) key = sm.best[wi][tid] > key ? sm.best[wi][tid] : key;
-    if (key) atomicMax(local + p.peer_row0 + tid, key);
+    for (int wi = 0; wi < kConsumers / 32; ++wi) key = sm.best[wi][lane] > key ? sm.best[wi][lane] : key;
+    if (key) atomicMax(local + p.peer_row0 + lane, key);
   }
-  __shared__ unsigned int s_last;
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    s_last = atomicAdd(reinterpret_cast<unsigned int*>(own + sbd::kMailCtas), 1u) == gridDim.x - 1 ? 1u : 0u;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  if (tid == 0) {
+  __syncwarp();
+  // count in with release (the folds above come first) and acquire (the last
+  // CTA then sees every CTA's folds)
+  unsigned int old = 0;
+  if (lane == 0)
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                 : "=r"(old)
+                 : "l"(own + sbd::kMailCtas)
+                 : "memory");
+  const bool last = __shfl_sync(0xFFFFFFFFu, old, 0) == gridDim.x - 1;
+  if (!last) return;
+  if (lane == 0) {
     *reinterpret_cast<volatile unsigned int*>(own + sbd::kMailCtas) = 0u;  // re-arm for the next launch
     gv_stamp(p, GV_LAST, 1ull);
   }
-  if (!p.peer_finish || tid >= 32) return;
-  __threadfence();
-  const int lane = tid, rows = p.peer_rows, world = p.world;
-  uint32_t* epoch = reinterpret_cast<uint32_t*>(own + sbd::kMailEpoch);
-  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(epoch), q = e & 1u;
+  if (!p.peer_finish) return;
+  const int rows = p.peer_rows, world = p.world, rank = pre.rank;
+  const uint32_t e = pre.epoch, q = e & 1u;
   const unsigned long long tag = e + 1u;
-  // this rank's index: where its own mailbox sits in the peer array
   const unsigned long long own_addr = reinterpret_cast<unsigned long long>(own);
-  const unsigned int at = __ballot_sync(0xFFFFFFFFu, lane < world && p.peer_mailboxes[lane] == own_addr);
-  const int rank = at ? __ffs(at) - 1 : -1;
   auto slot = [&](unsigned long long base, int r, int i) {
     return reinterpret_cast<unsigned long long*>(base + sbd::kMailSlots) +
            2 * ((static_cast<int>(q) * sbd::kMailMaxRanks + r) * sbd::kMailMaxRows + i);
@@ -439,13 +459,13 @@ __device__ __forceinline__ void peer_publish(const GemvParams& p, GemvSmem& sm, 
     local[i] = 0ull;
   }
   __syncwarp();
-  if (lane == 0) *epoch = e + 1u;
+  if (lane == 0) *reinterpret_cast<volatile uint32_t*>(own + sbd::kMailEpoch) = e + 1u;
 }
 
 template <int M>
-__device__ __forceinline__ void publish_keys(const GemvParams& p, GemvSmem& sm, int tid) {
+__device__ __forceinline__ void publish_keys(const GemvParams& p, GemvSmem& sm, int tid, PeerPre pre = PeerPre{}) {
   if (p.peer_mailboxes) {
-    peer_publish<M>(p, sm, tid);
+    peer_publish<M>(p, sm, tid, pre);
     return;
   }
   if (tid < M && tid < p.m) {
@@ -699,6 +719,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
   // x is the previous kernel's output: wait for it (weights are already streaming)
   sbd::griddep_wait();
   if (TR && tid == 0 && p.trace) gv_stamp(p, GV_DEP, sbd::global_ns());
+  PeerPre pre{};
+  if constexpr (EPI == EPI_ARGMAX) {
+    if (p.peer_mailboxes && warp == 0) pre = peer_preload(p, lane);
+  }
   XG xg[M][GPL];
   if constexpr (BITS == 4 && EPI != EPI_SRQ) {
     if (p.x_stage)
@@ -803,7 +827,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q4_stream_kernel(co
       if (lane == 0) sm.best[warp][m] = key;
     }
     __syncthreads();
-    publish_keys<M>(p, sm, tid);
+    publish_keys<M>(p, sm, tid, pre);
   }
   if (TR && tid == 0 && p.trace) gv_stamp(p, GV_PUBLISHED, sbd::global_ns());
   if (__syncthreads_or(*abort)) {
